@@ -1,0 +1,384 @@
+"""Benchmark of the qdec hot path on B200 (one process per GPU; torchrun for N > 1).
+
+Workload (the isolated K-quant GEMV microbench): Q4_K weight matrices W_up 17408 x 5120
+and W_down 5120 x 17408 (256-weight super-blocks, f16 d ~ U(1e-3, 4e-3) and dmin ~ U(0, 1e-3), 6-bit
+scales and mins ~ U{0..63}, 4-bit codes ~ U{0..15}, seeded) times x ~ N(0, 1) f32 activations quantised to
+Q8_K on the device.  One step = for N in (1, 2, 4): quantise x_up (N x 5120), GEMV W_up, quantise x_down
+(N x 17408), GEMV W_down -- 12 kernel launches, 6 weight passes.  Three weight sets (301 MB) rotate so no
+step finds its weights in the 126 MB L2.  Metric: weight bytes streamed / second (the reference bench's
+definition, crates/cli/src/bench.rs:65-91), whole job over all ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qdec|reference]
+
+`--impl reference` times the reference's CPU path (its C restatement in oracle/, OpenMP over all host
+threads, the reference's row-parallel matvec) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen-3.8-in-rust_b200"))
+
+UP = (17408, 5120)
+DOWN = (5120, 17408)
+NS = (1, 2, 4)
+Q4K_BB = 144
+N_SETS = 3
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def synth_q4k(rows, cols, seed):
+    """Seeded Q4_K blocks with finite scales: d ~ U(1e-3, 4e-3), dmin ~ U(0, 1e-3), 6-bit scales/mins, 4-bit codes."""
+    rng = np.random.default_rng(seed)
+    nb = rows * (cols // 256)
+    blk = np.empty((nb, Q4K_BB), np.uint8)
+    d = rng.uniform(1e-3, 4e-3, nb).astype(np.float16).view(np.uint16)
+    dm = rng.uniform(0.0, 1e-3, nb).astype(np.float16).view(np.uint16)
+    blk[:, 0], blk[:, 1] = d & 0xFF, d >> 8
+    blk[:, 2], blk[:, 3] = dm & 0xFF, dm >> 8
+    sc = rng.integers(0, 64, (nb, 8), dtype=np.uint8)
+    mn = rng.integers(0, 64, (nb, 8), dtype=np.uint8)
+    q = np.zeros((nb, 12), np.uint8)  # pack as ggml's quantize_row_q4_K_ref does (inverse of get_scale_min_k4)
+    for j in range(8):
+        if j < 4:
+            q[:, j] = sc[:, j]
+            q[:, j + 4] = mn[:, j]
+        else:
+            q[:, j + 4] = (sc[:, j] & 0xF) | ((mn[:, j] & 0xF) << 4)
+            q[:, j - 4] |= (sc[:, j] >> 4) << 6
+            q[:, j] |= (mn[:, j] >> 4) << 6
+    blk[:, 4:16] = q
+    blk[:, 16:] = rng.integers(0, 256, (nb, 128), dtype=np.uint8)
+    return blk.reshape(-1)
+
+
+def algorithmic_bytes(rows, cols, n):
+    """Weights + Q8_K activations + f32 outputs of one GEMV launch."""
+    return rows * (cols // 256) * Q4K_BB + n * (cols // 256) * 292 + 4 * n * rows
+
+
+class ClockSampler:
+    """NVML samples of SM clock and throttle reasons while the timed region runs (nvidia-smi's data)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+            if not self.samples:  # region shorter than one sample period: take one now
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(backend):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path (oracle restatement, all host threads) on a bounded row sample per step."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    oracle.build()
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    # per step: the same 6 passes on a sample of rows, sized so the whole run stays within ~90 s of CPU time
+    frac_rows = {}
+    w = {}
+    for name, (rows, cols) in (("up", UP), ("down", DOWN)):
+        w[name] = synth_q4k(rows, cols, seed=1 + (name == "down"))
+    x = {n: np.random.default_rng(n).standard_normal((n, UP[1])).astype(np.float32) for n in NS}
+    xd = {n: np.random.default_rng(10 + n).standard_normal((n, DOWN[1])).astype(np.float32) for n in NS}
+
+    def step(sample_rows):
+        done = 0
+        for n in NS:
+            for name, (rows, cols), xx in (("up", UP, x[n]), ("down", DOWN, xd[n])):
+                r = sample_rows[name]
+                oracle.matmul(oracle.Q4_K, w[name][: r * (cols // 256) * Q4K_BB], r, cols, xx)
+                done += r * (cols // 256) * Q4K_BB
+        return done
+
+    # calibrate on a small sample
+    probe = {"up": 256, "down": 128}
+    t0 = time.perf_counter()
+    b = step(probe)
+    dt = max(time.perf_counter() - t0, 1e-6)
+    rate = b / dt
+    budget_s = 60.0
+    per_step_bytes = min(rate * budget_s / max(1, args.steps + args.warmup), float(sum(r * (c // 256) * Q4K_BB for r, c in (UP, DOWN)) * len(NS)))
+    scale = per_step_bytes / (sum(r * (c // 256) * Q4K_BB for r, c in (UP, DOWN)) * len(NS))
+    sample = {"up": max(8, int(UP[0] * scale) // 8 * 8), "down": max(8, int(DOWN[0] * scale) // 8 * 8)}
+    for _ in range(args.warmup):
+        step(sample)
+    t0 = time.perf_counter()
+    total = 0
+    for _ in range(args.steps):
+        total += step(sample)
+    el = time.perf_counter() - t0
+    gbs = total / el / 1e9
+    sample_desc = f"{sample['up']} of {UP[0]} rows of W_up and {sample['down']} of {DOWN[0]} rows of W_down per step, N in {list(NS)}"
+    line = {
+        "metric": "Q4_K GEMV weight GB/s (config 2: 17408x5120 + 5120x17408, N=1,2,4)", "value": round(gbs, 3),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8 (Q4_K) x i8 (Q8_K), f32 accumulate", "data": "synthetic",
+        "config": {"workload": "q4k_gemv_config2", "shapes": [list(UP), list(DOWN)], "n_cols": list(NS)},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample_desc},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample():
+    """The oracle (the reference's CPU arithmetic restated in C, OpenMP over the host cores) on a bounded
+    sample: the 6 passes of one step over the first 2048 / 512 rows, repeated for ~10 s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    oracle.build()
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    rows_up, rows_down = 2048, 512
+    wu = synth_q4k(rows_up, UP[1], seed=11)
+    wd = synth_q4k(rows_down, DOWN[1], seed=12)
+    xs = {n: (np.random.default_rng(n).standard_normal((n, UP[1])).astype(np.float32),
+              np.random.default_rng(n + 7).standard_normal((n, DOWN[1])).astype(np.float32)) for n in NS}
+    t0 = time.perf_counter()
+    total, reps = 0, 0
+    while time.perf_counter() - t0 < 10.0 or reps == 0:
+        for n in NS:
+            oracle.matmul(oracle.Q4_K, wu, rows_up, UP[1], xs[n][0])
+            oracle.matmul(oracle.Q4_K, wd, rows_down, DOWN[1], xs[n][1])
+            total += rows_up * (UP[1] // 256) * Q4K_BB + rows_down * (DOWN[1] // 256) * Q4K_BB
+        reps += 1
+    el = time.perf_counter() - t0
+    return {"value": round(total / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} x (6 passes: {rows_up} rows of W_up, {rows_down} rows of W_down, N=1,2,4), {el:.1f} s"}
+
+
+def run_qdec(args, world, rank, local):
+    import torch
+
+    import qdec
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    L = qdec.lib()
+    # weights: N_SETS rotating sets (more bytes than L2)
+    sets = []
+    for s in range(N_SETS):
+        wu = torch.from_numpy(synth_q4k(*UP, seed=100 * (rank + 1) + 2 * s)).to(dev)
+        wdn = torch.from_numpy(synth_q4k(*DOWN, seed=100 * (rank + 1) + 2 * s + 1)).to(dev)
+        sets.append((wu, wdn))
+    x_up = {n: torch.randn(n, UP[1], generator=torch.Generator().manual_seed(n), dtype=torch.float32).to(dev) for n in NS}
+    x_dn = {n: torch.randn(n, DOWN[1], generator=torch.Generator().manual_seed(10 + n), dtype=torch.float32).to(dev) for n in NS}
+    a_up = torch.empty(4 * qdec.act_row_bytes(qdec.Q4_K, UP[1]), dtype=torch.uint8, device=dev)
+    a_dn = torch.empty(4 * qdec.act_row_bytes(qdec.Q4_K, DOWN[1]), dtype=torch.uint8, device=dev)
+    y_up = torch.empty(4 * UP[0], dtype=torch.float32, device=dev)
+    y_dn = torch.empty(4 * DOWN[0], dtype=torch.float32, device=dev)
+    launches_per_step = 4 * len(NS)
+    ev_pairs = []
+
+    def step(i, record=False):
+        wu, wdn = sets[i % N_SETS]
+        for n in NS:
+            qdec.quantize_q8k(x_up[n].data_ptr(), UP[1], n, a_up.data_ptr(), sp)
+            if record and n == 4:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            qdec.gemv(qdec.Q4_K, wu.data_ptr(), UP[0], UP[1], a_up.data_ptr(), n, y_up.data_ptr(), sp)
+            if record and n == 4:
+                e1.record(stream)
+                ev_pairs.append((e0, e1))
+            qdec.quantize_q8k(x_dn[n].data_ptr(), DOWN[1], n, a_dn.data_ptr(), sp)
+            qdec.gemv(qdec.Q4_K, wdn.data_ptr(), DOWN[0], DOWN[1], a_dn.data_ptr(), n, y_dn.data_ptr(), sp)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    barrier()
+    torch.cuda.synchronize()
+    # the dominant kernel timed alone per launch (N = 4 on W_up), on the launching stream
+    for i in range(min(args.steps, 200)):
+        step(i, record=True)
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_pairs)
+    # end to end through the C ABI from pinned host buffers: H2D of x, qdec_matvec, D2H of y, every step
+    hx_up = {n: x_up[n].cpu().pin_memory() for n in NS}
+    hx_dn = {n: x_dn[n].cpu().pin_memory() for n in NS}
+    hy_up = torch.empty(4 * UP[0], dtype=torch.float32).pin_memory()
+    hy_dn = torch.empty(4 * DOWN[0], dtype=torch.float32).pin_memory()
+    dx_up = torch.empty(4 * UP[1], dtype=torch.float32, device=dev)
+    dx_dn = torch.empty(4 * DOWN[1], dtype=torch.float32, device=dev)
+    h2d = sum(4 * n * (UP[1] + DOWN[1]) for n in NS)
+    d2h = sum(4 * n * (UP[0] + DOWN[0]) for n in NS)
+
+    def e2e_step(i):
+        wu, wdn = sets[i % N_SETS]
+        for n in NS:
+            dx_up[: n * UP[1]].copy_(hx_up[n].view(-1), non_blocking=True)
+            qdec.matvec(qdec.Q4_K, wu.data_ptr(), UP[0], UP[1], dx_up.data_ptr(), n, y_up.data_ptr(), sp)
+            hy_up[: n * UP[0]].copy_(y_up[: n * UP[0]], non_blocking=True)
+            dx_dn[: n * DOWN[1]].copy_(hx_dn[n].view(-1), non_blocking=True)
+            qdec.matvec(qdec.Q4_K, wdn.data_ptr(), DOWN[0], DOWN[1], dx_dn.data_ptr(), n, y_dn.data_ptr(), sp)
+            hy_dn[: n * DOWN[0]].copy_(y_dn[: n * DOWN[0]], non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, e2e_ms, kern_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, kern_ms = t.tolist()
+    bytes_per_step = sum(r * (c // 256) * Q4K_BB for r, c in (UP, DOWN)) * len(NS)
+    value = world * bytes_per_step * args.steps / (ms / 1e3) / 1e9
+    e2e_value = world * bytes_per_step * args.steps / (e2e_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    alg = algorithmic_bytes(UP[0], UP[1], 4)
+    achieved = alg / (kern_ms / 1e3) / 1e9
+    if rank == 0:
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "q4k_gemv_traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch")
+        line = {
+            "metric": "Q4_K GEMV weight GB/s (config 2: 17408x5120 + 5120x17408, N=1,2,4)",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8 (Q4_K) x i8 (Q8_K), f32 accumulate", "data": "synthetic",
+            "config": {"workload": "q4k_gemv_config2", "shapes": [list(UP), list(DOWN)], "n_cols": list(NS),
+                       "l2": f"{N_SETS} rotating weight sets ({N_SETS * bytes_per_step // len(NS) / 1e6:.0f} MB) > 126 MB L2",
+                       "parallelism": f"replicas x{world}"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "kq_gemv_kernel<Q4_K, N=4> 17408x5120", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "alg_bytes_per_launch": alg, "launch_us": round(kern_ms * 1e3, 3)},
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample()
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["qdec", "reference"], default="qdec")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # the CPU arm needs no process group: rank 0 runs, the other ranks exit without work
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local = dist_setup("nccl")
+    run_qdec(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

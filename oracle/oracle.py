@@ -1,0 +1,258 @@
+"""ctypes binding of the CPU oracle (test infrastructure).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this module; the product
+(the `qdec` library) never does.  The library is built from oracle/*.c by oracle/Makefile into
+oracle/_build/liboracle.so.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+F32, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 2, 8, 12, 13, 14
+TYPE_IDS = {"F32": F32, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+LAYOUT = {F32: (1, 4), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+LIBM_CR, LIBM_GLIBC = 0, 1
+
+_lib = None
+
+
+def build():
+    """Compile the oracle (make -C oracle); a no-op when it is up to date."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I, F, S, U = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_uint32
+        sig = {
+            "oracle_set_libm": (None, [I]),
+            "oracle_get_libm": (I, []),
+            "oracle_set_threads": (None, [I]),
+            "oracle_f16_to_f32": (F, [ctypes.c_uint16]),
+            "oracle_f32_to_f16": (ctypes.c_uint16, [F]),
+            "oracle_expf": (F, [F]),
+            "oracle_dequantize": (I, [I, P, S, P, S]),
+            "oracle_quantize_q8k": (None, [P, I, P]),
+            "oracle_quantize_q8_0": (None, [P, I, P]),
+            "oracle_dot": (F, [I, P, P, I]),
+            "oracle_matmul_f32in": (None, [I, P, I, I, P, I, P]),
+            "oracle_matmul_act": (None, [I, P, I, I, P, S, I, P]),
+            "oracle_rmsnorm": (None, [P, P, I, F, P]),
+            "oracle_rmsnorm_gated": (None, [P, P, P, I, F, P]),
+            "oracle_swiglu": (None, [P, P, I, P]),
+            "oracle_softmax": (None, [P, I, P]),
+            "oracle_inv_freq": (None, [I, F, P]),
+            "oracle_cos_sin": (None, [U, P, I, P, P]),
+            "oracle_apply_rope": (None, [P, I, I, I, P, P]),
+            "oracle_conv1d_step": (None, [P, P, I, P, I, P, I]),
+            "oracle_l2norm": (None, [P, I, F]),
+            "oracle_gate_g": (F, [F, F, F]),
+            "oracle_gate_beta": (F, [F]),
+            "oracle_deltanet_step": (None, [P, P, P, I, I, F, F, P, P]),
+            "oracle_argmax": (U, [P, I]),
+            "oracle_crc32": (U, [P, S]),
+            "oracle_silu": (F, [F]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def set_libm(mode):
+    lib().oracle_set_libm(mode)
+
+
+def set_threads(n):
+    lib().oracle_set_threads(n)
+
+
+def row_bytes(t, cols):
+    be, bb = LAYOUT[t]
+    return cols // be * bb
+
+
+def act_bytes(t, cols):
+    if t in (Q4_K, Q5_K, Q6_K):
+        return cols // 256 * 292
+    if t in (Q8_0, Q4_0):
+        return cols // 32 * 34
+    return cols * 4
+
+
+def dequantize(t, raw, n):
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    out = np.empty(n, dtype=np.float32)
+    rc = lib().oracle_dequantize(t, _p(raw), raw.size, _p(out), n)
+    if rc != 0:
+        raise ValueError(f"dequantize: size mismatch for type {t}: {raw.size} bytes, {n} elements")
+    return out
+
+
+def quantize_q8k(x):
+    """Rows of f32 (last dim a multiple of 256) -> uint8 array of block_q8_K bytes, one row per input row."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    n = rows.shape[1]
+    out = np.empty((rows.shape[0], n // 256 * 292), dtype=np.uint8)
+    for r in range(rows.shape[0]):
+        lib().oracle_quantize_q8k(_p(rows[r]), n, _p(out[r]))
+    return out
+
+
+def quantize_q8_0(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    n = rows.shape[1]
+    out = np.empty((rows.shape[0], n // 32 * 34), dtype=np.uint8)
+    for r in range(rows.shape[0]):
+        lib().oracle_quantize_q8_0(_p(rows[r]), n, _p(out[r]))
+    return out
+
+
+def dot(t, wrow, act, cols):
+    wrow = np.ascontiguousarray(wrow, dtype=np.uint8)
+    act = np.ascontiguousarray(act)
+    return lib().oracle_dot(t, _p(wrow), _p(act), cols)
+
+
+def matmul(t, w, rows, cols, x):
+    """y[c, r] = w[r] . x[c] with x quantised into the form `t` consumes (matvec.rs:147-160)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
+    y = np.empty((x.shape[0], rows), dtype=np.float32)
+    lib().oracle_matmul_f32in(t, _p(w), rows, cols, _p(x), x.shape[0], _p(y))
+    return y
+
+
+def matmul_act(t, w, rows, cols, act):
+    """As `matmul` on pre-quantised activation rows (uint8 blocks, or f32 for F32 weights)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    act = np.ascontiguousarray(act)
+    ncols = act.shape[0]
+    stride = act.strides[0]
+    y = np.empty((ncols, rows), dtype=np.float32)
+    lib().oracle_matmul_act(t, _p(w), rows, cols, _p(act), stride, ncols, _p(y))
+    return y
+
+
+def rmsnorm(x, w, eps):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.empty_like(x)
+    rows = x.reshape(-1, x.shape[-1])
+    yr = y.reshape(-1, x.shape[-1])
+    for r in range(rows.shape[0]):
+        lib().oracle_rmsnorm(_p(rows[r]), _p(w), rows.shape[1], eps, _p(yr[r]))
+    return y
+
+
+def rmsnorm_gated(x, gate, w, eps):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    gate = np.ascontiguousarray(gate, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.empty_like(x)
+    xr, gr, yr = x.reshape(-1, x.shape[-1]), gate.reshape(-1, x.shape[-1]), y.reshape(-1, x.shape[-1])
+    for r in range(xr.shape[0]):
+        lib().oracle_rmsnorm_gated(_p(xr[r]), _p(gr[r]), _p(w), xr.shape[1], eps, _p(yr[r]))
+    return y
+
+
+def softmax(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oracle_softmax(_p(x), x.size, _p(y))
+    return y
+
+
+def silu(x):
+    return np.array([lib().oracle_silu(float(v)) for v in np.asarray(x, dtype=np.float32).ravel()], dtype=np.float32)
+
+
+def swiglu(g, u):
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    y = np.empty_like(g)
+    lib().oracle_swiglu(_p(g), _p(u), g.size, _p(y))
+    return y
+
+
+def inv_freq(rope_dim, theta):
+    out = np.empty(rope_dim // 2, dtype=np.float32)
+    lib().oracle_inv_freq(rope_dim, theta, _p(out))
+    return out
+
+
+def cos_sin(pos, inv_f):
+    inv_f = np.ascontiguousarray(inv_f, dtype=np.float32)
+    half = inv_f.size
+    c = np.empty(2 * half, dtype=np.float32)
+    s = np.empty(2 * half, dtype=np.float32)
+    lib().oracle_cos_sin(pos, _p(inv_f), half, _p(c), _p(s))
+    return c, s
+
+
+def apply_rope(x, head_dim, rope_dim, cos, sin):
+    x = np.array(x, dtype=np.float32, copy=True)
+    cos = np.ascontiguousarray(cos, dtype=np.float32)
+    sin = np.ascontiguousarray(sin, dtype=np.float32)
+    lib().oracle_apply_rope(_p(x), x.size, head_dim, rope_dim, _p(cos), _p(sin))
+    return x
+
+
+def conv1d_step(state, w, kernel, x_new):
+    state = np.array(state, dtype=np.float32, copy=True)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    x_new = np.ascontiguousarray(x_new, dtype=np.float32)
+    out = np.empty(x_new.size, dtype=np.float32)
+    lib().oracle_conv1d_step(_p(state), _p(w), kernel, _p(x_new), x_new.size, _p(out), 1)
+    return out, state
+
+
+def l2norm(x, eps=1e-6):
+    x = np.array(x, dtype=np.float32, copy=True)
+    lib().oracle_l2norm(_p(x), x.size, eps)
+    return x
+
+
+def gate_g(a, dt_bias, big_a):
+    return lib().oracle_gate_g(a, dt_bias, big_a)
+
+
+def gate_beta(b):
+    return lib().oracle_gate_beta(b)
+
+
+def deltanet_step(q, k, v, g, beta, s):
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    s = np.array(s, dtype=np.float32, copy=True)
+    out = np.empty(v.size, dtype=np.float32)
+    lib().oracle_deltanet_step(_p(q), _p(k), _p(v), q.size, v.size, g, beta, _p(s), _p(out))
+    return out, s
+
+
+def argmax(v):
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    return lib().oracle_argmax(_p(v), v.size)
+
+
+def crc32(b):
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    return lib().oracle_crc32(_p(b), b.size)

@@ -1,0 +1,148 @@
+// The kernel-level C ABI (include/qdec.h): argument checks in the reference's terms, error strings, and the
+// library-owned activation buffer of qdec_matvec.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/qdec.h"
+#include "capi_util.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace qdec {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(QDEC_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+void clear_error() { g_last_error.clear(); }
+
+bool supported_type(int t) {
+    return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K;
+}
+
+// Shape checks of the reference's assert!s (matvec.rs:73-77, :300, :338; kdot.rs:179-191).
+int check_gemv_shape(int type, int rows, int cols, int ncols) {
+    if (!supported_type(type)) return fail(QDEC_EINVAL, "unsupported weight type %d", type);
+    if (rows < 0 || cols <= 0 || ncols < 0) return fail(QDEC_EINVAL, "bad shape rows=%d cols=%d n_cols=%d", rows, cols, ncols);
+    const int be = block_elems(type);
+    if (cols % be) return fail(QDEC_EINVAL, "cols %d not a multiple of block size %d for type %d", cols, be, type);
+    if ((type == T_Q8_0 || type == T_Q4_0) && cols % 64)
+        return fail(QDEC_EINVAL, "cols %d: Q8_0/Q4_0 rows must hold an even number of 32-blocks", cols);
+    if (is_kquant(type)) {
+        const size_t smem = (size_t)4 * (cols / 256) * 324 + 64;
+        if (smem > 220 * 1024) return fail(QDEC_EINVAL, "cols %d too wide for the staged activations", cols);
+    }
+    return QDEC_OK;
+}
+
+// Library-owned activation buffer per device for qdec_matvec.
+struct ActPool {
+    std::mutex mu;
+    std::vector<void *> buf;
+    std::vector<size_t> cap;
+};
+static ActPool g_act;
+
+static int act_buffer(size_t bytes, void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(g_act.mu);
+    if ((int)g_act.buf.size() <= dev) g_act.buf.resize(dev + 1, nullptr), g_act.cap.resize(dev + 1, 0);
+    if (g_act.cap[dev] < bytes) {
+        if (g_act.buf[dev]) cudaFree(g_act.buf[dev]);
+        g_act.buf[dev] = nullptr;
+        g_act.cap[dev] = 0;
+        e = cudaMalloc(&g_act.buf[dev], bytes);
+        if (e != cudaSuccess) return fail(QDEC_ENOMEM, "activation buffer of %zu bytes: %s", bytes, cudaGetErrorString(e));
+        g_act.cap[dev] = bytes;
+    }
+    *out = g_act.buf[dev];
+    return QDEC_OK;
+}
+
+}  // namespace qdec
+
+using namespace qdec;
+
+extern "C" {
+
+const char *qdec_version(void) { return "qdec 0.1.0 sm_100a"; }
+
+const char *qdec_last_error(void) { return g_last_error.c_str(); }
+
+int qdec_quantize_q8k(const float *x_dev, int n, int rows, void *q8k_dev, void *stream) {
+    if (n <= 0 || n % 256 || rows < 0) return fail(QDEC_EINVAL, "qdec_quantize_q8k: length %d is not a multiple of 256", n);
+    if (!x_dev || !q8k_dev) return fail(QDEC_EINVAL, "qdec_quantize_q8k: null pointer");
+    cudaError_t e = launch_quantize_q8k(x_dev, n, rows, (uint8_t *)q8k_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_quantize_q8k");
+}
+
+int qdec_quantize_q8_0(const float *x_dev, int n, int rows, void *q8_dev, void *stream) {
+    if (n <= 0 || n % 32 || rows < 0) return fail(QDEC_EINVAL, "qdec_quantize_q8_0: length %d is not a multiple of 32", n);
+    if (!x_dev || !q8_dev) return fail(QDEC_EINVAL, "qdec_quantize_q8_0: null pointer");
+    cudaError_t e = launch_quantize_q8_0(x_dev, n, rows, (uint8_t *)q8_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_quantize_q8_0");
+}
+
+size_t qdec_act_row_bytes(int ggml_type, int cols) {
+    if (!supported_type(ggml_type) || cols <= 0 || cols % block_elems(ggml_type)) return 0;
+    return act_row_bytes(ggml_type, cols);
+}
+
+int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *act_dev, int n_cols, float *y_dev,
+              void *stream) {
+    int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
+    if (rc) return rc;
+    if (!w_dev || !act_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_gemv: null pointer");
+    cudaError_t e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, act_dev, n_cols, y_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv");
+}
+
+int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev,
+                void *stream) {
+    int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
+    if (rc) return rc;
+    if (!w_dev || !x_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_matvec: null pointer");
+    if (n_cols == 0) return QDEC_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (ggml_type == T_F32) {
+        cudaError_t e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, x_dev, n_cols, y_dev, s);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec");
+    }
+    void *act = nullptr;
+    rc = act_buffer(act_row_bytes(ggml_type, cols) * n_cols, &act);
+    if (rc) return rc;
+    cudaError_t e = is_kquant(ggml_type) ? launch_quantize_q8k(x_dev, cols, n_cols, (uint8_t *)act, s)
+                                         : launch_quantize_q8_0(x_dev, cols, n_cols, (uint8_t *)act, s);
+    if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec: quantise");
+    e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, act, n_cols, y_dev, s);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec: gemv");
+}
+
+int qdec_dequant_rows(int ggml_type, const void *w_dev, int rows, int cols, const int32_t *ids_dev, int n_ids,
+                      float *out_dev, void *stream) {
+    if (!supported_type(ggml_type) || cols <= 0 || cols % block_elems(ggml_type) || rows < 0 || n_ids < 0)
+        return fail(QDEC_EINVAL, "qdec_dequant_rows: bad type %d or shape %d x %d", ggml_type, rows, cols);
+    if (!w_dev || (!ids_dev && n_ids) || (!out_dev && n_ids)) return fail(QDEC_EINVAL, "qdec_dequant_rows: null pointer");
+    const size_t rb = (size_t)(cols / block_elems(ggml_type)) * block_bytes(ggml_type);
+    cudaError_t e = launch_dequant_rows(ggml_type, (const uint8_t *)w_dev, rb, cols, ids_dev, n_ids, out_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_dequant_rows");
+}
+
+}  // extern "C"

@@ -1,0 +1,28 @@
+// Kernel and launcher declarations shared by the qdec translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace qdec {
+
+__global__ void q8k_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
+__global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
+__global__ void dequant_rows_kernel(int type, const uint8_t* __restrict__ w, size_t row_bytes, int n,
+                                    const int32_t* __restrict__ ids, int nids, float* __restrict__ out);
+
+// Host launchers (return cudaError_t of the launch).
+cudaError_t launch_quantize_q8k(const float* x, int n, int rows, uint8_t* out, cudaStream_t s);
+cudaError_t launch_quantize_q8_0(const float* x, int n, int rows, uint8_t* out, cudaStream_t s);
+cudaError_t launch_dequant_rows(int type, const uint8_t* w, size_t row_bytes, int n, const int32_t* ids, int nids,
+                                float* out, cudaStream_t s);
+
+// y[c * rows + r] = W[r] . act_c for c in [0, ncols); act in the form the weight type consumes:
+// block_q8_K rows (K-quants), block_q8_0 rows (Q8_0, Q4_0) or f32 rows (F32), `ncols` rows back to back.
+cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
+                        cudaStream_t s);
+// Bytes of one activation row of `cols` values in the form `type` consumes.
+size_t act_row_bytes(int type, int cols);
+int num_sms();
+
+}  // namespace qdec

@@ -1,0 +1,162 @@
+// Activation quantisers and row dequantisation.
+//
+//  * q8k_quantize_kernel  -- ggml block_q8_K rows, bit-exact with crates/core/src/kernels/q8k.rs:76-114
+//  * q8_0_quantize_kernel -- ggml block_q8_0 rows, bit-exact with crates/core/src/kernels/q8.rs:81-103
+//  * dequant_rows_kernel  -- f32 rows from ggml blocks, bit-exact with crates/core/src/quant.rs:67-229
+//    (the embedding gather of crates/core/src/model.rs:364-368)
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace qdec {
+
+// One warp per 256-value block; lane i holds values 8i..8i+7.
+__global__ void q8k_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out) {
+    const int nb = n / QK_K;
+    const long long total = (long long)rows * nb;
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < total; b += nwarps) {
+        const long long r = b / nb, sb = b % nb;
+        const float* blk = x + r * (long long)n + sb * QK_K;
+        float v[8];
+        const float4 a0 = reinterpret_cast<const float4*>(blk)[2 * lane];
+        const float4 a1 = reinterpret_cast<const float4*>(blk)[2 * lane + 1];
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        // the first element with the largest |x| (strict > scan of q8k.rs:88-95)
+        float amax = 0.0f, mx = 0.0f;
+        int idx = 0x7fffffff;
+        for (int i = 0; i < 8; i++) {
+            float a = fabsf(v[i]);
+            if (a > amax) { amax = a; mx = v[i]; idx = lane * 8 + i; }
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+            float om = __shfl_xor_sync(0xffffffffu, mx, off);
+            int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+            if (oa > amax || (oa == amax && oi < idx)) { amax = oa; mx = om; idx = oi; }
+        }
+        uint8_t* o = out + b * Q8K_BLOCK_BYTES;
+        if (amax == 0.0f) {
+            // d = 0, codes 0, bsums 0 (q8k.rs:96-101); 292 bytes = 73 words
+            for (int w = lane; w < 73; w += 32) reinterpret_cast<uint32_t*>(o)[w] = 0u;
+            continue;
+        }
+        const float iscale = __fdiv_rn(-127.0f, mx);
+        int q[8];
+        for (int i = 0; i < 8; i++) {
+            int qi = __float2int_rn(__fmul_rn(iscale, v[i]));  // round_ties_even, then min(127)
+            q[i] = qi > 127 ? 127 : qi;
+        }
+        uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+        uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+        reinterpret_cast<uint32_t*>(o + 4)[2 * lane] = w0;
+        reinterpret_cast<uint32_t*>(o + 4)[2 * lane + 1] = w1;
+        int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);  // group g = lanes 2g, 2g+1
+        if ((lane & 1) == 0) reinterpret_cast<int16_t*>(o + 260)[lane >> 1] = (int16_t)s;
+        if (lane == 0) {
+            const float d = __fdiv_rn(1.0f, iscale);
+            *reinterpret_cast<float*>(o) = d;
+        }
+    }
+}
+
+// One warp per 32-value block; lane i holds value i.
+__global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out) {
+    const int nb = n / 32;
+    const long long total = (long long)rows * nb;
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < total; b += nwarps) {
+        const long long r = b / nb, blk = b % nb;
+        const float v = x[r * (long long)n + blk * 32 + lane];
+        float amax = fabsf(v);
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float dd = __fdiv_rn(amax, 127.0f);
+        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+        float qf = roundf(__fmul_rn(v, id));  // round half away from zero, then `as i8` (saturating)
+        int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
+        uint8_t* o = out + b * Q8_0_BLOCK_BYTES;
+        o[2 + lane] = (uint8_t)(int8_t)qi;
+        if (lane == 0) {
+            const uint16_t h = __half_as_ushort(__float2half_rn(dd));
+            o[0] = (uint8_t)(h & 0xff);
+            o[1] = (uint8_t)(h >> 8);
+        }
+    }
+}
+
+__device__ __forceinline__ float f16_at(const uint8_t* b, int off) {
+    return f16_bits_to_f32((uint16_t)(b[off] | (b[off + 1] << 8)));
+}
+
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Value e of a block, exactly as crates/core/src/quant.rs computes it.
+__device__ float dequant_value(int type, const uint8_t* b, int e) {
+    switch (type) {
+    case T_F32: return *reinterpret_cast<const float*>(b);  // F32: one element per 4-byte "block"
+    case T_Q4_0: {
+        const float d = f16_at(b, 0);
+        const int j = e & 15;
+        const int q = (e < 16) ? (b[2 + j] & 0x0F) : (b[2 + j] >> 4);
+        return __fmul_rn((float)(q - 8), d);
+    }
+    case T_Q8_0: return __fmul_rn((float)(int8_t)b[2 + e], f16_at(b, 0));
+    case T_Q4_K:
+    case T_Q5_K: {
+        const float d = f16_at(b, 0), mn = f16_at(b, 2);
+        const int g = e / 64, hi = (e / 32) & 1, l = e & 31;
+        int sc, m;
+        scale_min_k4(2 * g + hi, b + 4, sc, m);
+        const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(mn, (float)m);
+        int q;
+        if (type == T_Q4_K) {
+            const uint8_t byte = b[16 + g * 32 + l];
+            q = hi ? (byte >> 4) : (byte & 0xF);
+        } else {
+            const uint8_t byte = b[48 + g * 32 + l];
+            q = (hi ? (byte >> 4) : (byte & 0xF)) + ((b[16 + l] & (1u << (2 * g + hi))) ? 16 : 0);
+        }
+        return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    case T_Q6_K: {
+        const float d = f16_at(b, 208);
+        const int half = e / 128, r = e & 127, k = r / 32, l = r & 31;
+        const uint8_t* ql = b + half * 64;
+        const uint8_t* qh = b + 128 + half * 32;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192 + half * 8);
+        const int lo = (k == 0) ? (ql[l] & 0xF) : (k == 1) ? (ql[l + 32] & 0xF) : (k == 2) ? (ql[l] >> 4) : (ql[l + 32] >> 4);
+        const int q = (lo | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+        const int is = l / 16;
+        return __fmul_rn(__fmul_rn(d, (float)sc[is + 2 * k]), (float)q);
+    }
+    default: return 0.0f;
+    }
+}
+
+// out[i * n + e] = dequant(row ids[i])[e]; ids and the row count are on the device so a CUDA graph can gather
+// the token ids the previous kernel wrote.
+__global__ void dequant_rows_kernel(int type, const uint8_t* __restrict__ w, size_t row_bytes, int n,
+                                    const int32_t* __restrict__ ids, int nids, float* __restrict__ out) {
+    const int be = block_elems(type), bb = block_bytes(type);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)nids * n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / n), e = (int)(i % n);
+        const uint8_t* rb = w + (size_t)ids[row] * row_bytes;
+        out[i] = dequant_value(type, rb + (size_t)(e / be) * bb, e % be);
+    }
+}
+
+}  // namespace qdec

@@ -1,0 +1,166 @@
+"""GPU parity of the kernel-level C ABI against the CPU oracle and the reference's golden vectors.
+
+Bit-exact everywhere: the quantisers, the dequantiser and every GEMV path compute the reference's exact
+arithmetic (integer lanes, then f32 in the reference's order), so the expected result is the oracle's,
+bit for bit, not a tolerance band.
+"""
+import numpy as np
+import pytest
+
+import golden_io as G
+from helpers import bits_equal, hostile_rows, random_blocks, row_bytes, to_dev
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TYPES = [12, 13, 14, 8, 2, 0]
+
+
+@pytest.fixture(scope="module")
+def q():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import qdec
+
+    qdec.lib()
+    return qdec
+
+
+def gpu_q8k(q, x):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, x.shape[-1])
+    xd = to_dev(x)
+    out = torch.empty(x.shape[0] * (x.shape[1] // 256) * 292, dtype=torch.uint8, device="cuda")
+    q.quantize_q8k(xd.data_ptr(), x.shape[1], x.shape[0], out.data_ptr())
+    torch.cuda.synchronize()
+    return out.cpu().numpy().reshape(x.shape[0], -1)
+
+
+def gpu_q8_0(q, x):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, x.shape[-1])
+    xd = to_dev(x)
+    out = torch.empty(x.shape[0] * (x.shape[1] // 32) * 34, dtype=torch.uint8, device="cuda")
+    q.quantize_q8_0(xd.data_ptr(), x.shape[1], x.shape[0], out.data_ptr())
+    torch.cuda.synchronize()
+    return out.cpu().numpy().reshape(x.shape[0], -1)
+
+
+def test_q8k_quantiser_golden(q):
+    meta, a = G.load("q8k_quantize")
+    for c in meta["cases"]:
+        x = a[c["case"] + "__x"]
+        raw = a[c["case"] + "__raw"].reshape(x.shape[0], -1)
+        got = gpu_q8k(q, x)
+        for r in range(x.shape[0]):
+            assert np.array_equal(got[r], raw[r]), f"{c['case']} row {r} ({c['rows'][r]})"
+
+
+def test_q8k_quantiser_hostile_and_random(q, orc):
+    for width in (256, 5120, 17408):
+        x = np.concatenate([hostile_rows(width, 7), np.random.default_rng(3).standard_normal((5, width)).astype(np.float32)])
+        assert np.array_equal(gpu_q8k(q, x), orc.quantize_q8k(x)), width
+
+
+def test_q8_0_quantiser_golden_and_random(q, orc):
+    meta, a = G.load("q8_quantize")
+    for c in meta["cases"]:
+        x = a[c["case"] + "__x"]
+        raw = a[c["case"] + "__raw"].reshape(x.shape[0], -1)
+        assert np.array_equal(gpu_q8_0(q, x), raw), c["case"]
+    x = np.random.default_rng(5).standard_normal((7, 6144)).astype(np.float32) * 3
+    assert np.array_equal(gpu_q8_0(q, x), orc.quantize_q8_0(x))
+
+
+def run_gemv(q, t, w, rows, cols, x):
+    """qdec_matvec from f32 columns: quantise on the device, then the GEMV."""
+    wd = to_dev(w)
+    xd = to_dev(np.ascontiguousarray(x, np.float32))
+    n = x.shape[0]
+    y = torch.empty(n * rows, dtype=torch.float32, device="cuda")
+    q.matvec(t, wd.data_ptr(), rows, cols, xd.data_ptr(), n, y.data_ptr())
+    torch.cuda.synchronize()
+    return y.cpu().numpy().reshape(n, rows)
+
+
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("ncols", [1, 2, 3, 4, 5])
+def test_gemv_random_bit_exact(q, orc, t, ncols):
+    rows, cols = 261, 5120  # ragged row count: not a multiple of any tile
+    w = random_blocks(t, rows, cols, seed=100 + t)
+    x = np.random.default_rng(ncols).standard_normal((ncols, cols)).astype(np.float32)
+    got = run_gemv(q, t, w, rows, cols, x)
+    want = orc.matmul(t, w, rows, cols, x)
+    assert bits_equal(got, want), f"type {t} ncols {ncols}: max diff {np.abs(got - want).max()}"
+
+
+@pytest.mark.parametrize("name,t", [("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14), ("Q4_0", 2)])
+def test_gemv_real_weights_bit_exact(q, orc, name, t):
+    """64 rows of the real model's weights (reference fixtures/dequant) against hostile + random columns."""
+    meta, a = G.load("dequant")
+    info = meta["types"][name]["rows64"]
+    w = a[name + "__rows64_raw"]
+    cols = info["cols"]
+    x = hostile_rows(cols, 11)[:4] if t != 2 else np.random.default_rng(1).standard_normal((4, cols)).astype(np.float32)
+    x = np.nan_to_num(x, posinf=0, neginf=0)
+    got = run_gemv(q, t, w, 64, cols, x)
+    want = orc.matmul(t, w, 64, cols, x)
+    assert bits_equal(got, want), name
+
+
+@pytest.mark.parametrize("rows,cols", [(17408, 5120), (5120, 17408)])
+def test_gemv_config2_full_size_bit_exact(q, orc, rows, cols):
+    """The BASELINE config-2 shapes, Q4_K, N = 4: every output bit-identical to the oracle."""
+    t = 12
+    w = random_blocks(t, rows, cols, seed=rows)
+    x = np.random.default_rng(9).standard_normal((4, cols)).astype(np.float32)
+    got = run_gemv(q, t, w, rows, cols, x)
+    want = orc.matmul(t, w, rows, cols, x)
+    assert bits_equal(got, want)
+    # column independence: column c of the batched call == the single-column call (matmul_t.rs property)
+    got1 = run_gemv(q, t, w, rows, cols, x[2:3])
+    assert bits_equal(got1[0], got[2])
+
+
+def test_gemv_matches_golden_matvec(q):
+    """The reference's matvec fixtures: within the f64 budget, like crates/core/tests/kernels.rs."""
+    meta, a = G.load("matvec")
+    for c in meta["cases"]:
+        t, cols, rows = c["ggml_type_id"], c["width"], c["n_rows"]
+        if t in (2, 8) and cols % 64:
+            continue
+        w = a[c["case"] + "__w_raw"]
+        x = a[c["case"] + "__x_deq"][None, :]
+        y = run_gemv(q, t, w, rows, cols, x)[0]
+        if t in (12, 13, 14):
+            continue  # K-quant budgets are checked on the oracle; bit-equality with it is checked above
+        for r in range(rows):
+            assert abs(y[r] - c["ref_f64"][r]) <= G.budget(meta["budget_k"], cols, c["max_abs_term"][r]), c["case"]
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_dequant_rows_bit_exact(q, orc, t):
+    rows, cols = 50, 5120
+    w = random_blocks(t, rows, cols, seed=t + 1)
+    ids = np.array([3, 0, 49, 3, 17], np.int32)
+    wd, idd = to_dev(w), to_dev(ids)
+    out = torch.empty(len(ids) * cols, dtype=torch.float32, device="cuda")
+    q.dequant_rows(t, wd.data_ptr(), rows, cols, idd.data_ptr(), len(ids), out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(len(ids), cols)
+    rb = row_bytes(t, cols)
+    for i, r in enumerate(ids):
+        want = orc.dequantize(t, w[r * rb:(r + 1) * rb], cols)
+        assert bits_equal(got[i], want), (t, r)
+
+
+def test_dequant_golden_hostile(q):
+    meta, a = G.load("dequant")
+    for h in meta["hostile"]["hostile"]:
+        tid = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "F32": 0}[h["ggml_type"]]
+        base = h["raw_bin"][:-4]
+        raw, want, n = a[base + "__raw"], a[base + "__deq"], h["n_elements"]
+        ids = np.zeros(1, np.int32)
+        wd, idd = to_dev(raw), to_dev(ids)
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        q.dequant_rows(tid, wd.data_ptr(), 1, n, idd.data_ptr(), 1, out.data_ptr())
+        torch.cuda.synchronize()
+        assert bits_equal(out.cpu().numpy(), want), base
