@@ -76,6 +76,76 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
 int qdec_dequant_rows(int ggml_type, const void *w_dev, int rows, int cols, const int32_t *ids_dev, int n_ids,
                       float *out_dev, void *stream);
 
+
+/* ------------------------------------------------------------------------------------- model level */
+
+typedef struct qdec_model qdec_model;
+typedef struct qdec_state qdec_state;
+
+typedef struct qdec_opts {
+    int device;   /* CUDA device ordinal */
+    int max_pos;  /* positions the RoPE tables and KV caches of states cover (<= 0: 4096) */
+} qdec_opts;
+
+typedef struct qdec_model_info {
+    uint32_t n_layer, hidden, ffn, vocab, n_head, n_head_kv, head_dim, dn_n_k_heads, dn_n_v_heads, dn_head_dim_k,
+        dn_head_dim_v, n_full_attention, has_mtp;
+    uint64_t weight_bytes;  /* bytes resident on the device */
+    uint64_t decode_bytes;  /* weight bytes one plain token streams (layers + lm_head + norms + one embedding row) */
+    double load_secs;
+} qdec_model_info;
+
+/* Open a GGUF file and upload its tensors to the device: header, metadata and tensor index
+ * (crates/core/src/gguf.rs:483), the config contract (crates/core/src/config.rs:146), the weights.
+ * Replaces Model::load_with (crates/core/src/model.rs:184).  Malformed files give QDEC_EFORMAT with the
+ * reference's GgufError / ConfigError message. */
+int qdec_open(const char *gguf_path, const qdec_opts *opts, qdec_model **out);
+int qdec_close(qdec_model *m);
+int qdec_model_get_info(const qdec_model *m, qdec_model_info *info);
+/* Nonzero when `id` is a stop id: the GGUF EOS ids plus the architecture's (crates/core/src/arch.rs:79-90).
+ * Replaces Model::is_stop (crates/core/src/model.rs:492). */
+int qdec_is_stop(const qdec_model *m, uint32_t id);
+
+/* A decode state for one sequence: spec_k > 0 adds the speculative buffers for k drafts per round
+ * (Model::new_state / new_state_spec, crates/core/src/model.rs:334, spec.rs:184); max_pos bounds the
+ * sequence (State::reserve, model.rs:123); max_rows bounds the rows of one forward (prefill chunk, >= k + 1).
+ * A state is bound to one CUDA stream and is not thread-safe. */
+int qdec_state_new(qdec_model *m, int spec_k, int max_pos, int max_rows, qdec_state **out);
+int qdec_state_free(qdec_state *s);
+int qdec_state_pos(const qdec_state *s);
+
+/* Prefill `n` prompt ids; *first_out = argmax of the last row's logits (Model::prefill + logits_of +
+ * argmax, crates/core/src/model.rs:443, :423, :505). */
+int qdec_prefill(qdec_state *s, const uint32_t *ids, int n, uint32_t *first_out);
+/* One token in, the greedy next token out; logits (vocab floats) copied to `logits_out` when non-null
+ * (Model::forward_token, crates/core/src/model.rs:486). */
+int qdec_step(qdec_state *s, uint32_t id, uint32_t *next_out, float *logits_out);
+/* Speculative prefill: prefill, x_T, the MTP over the prompt rows and the first k drafts; *x_out = x_T
+ * (Model::spec_prefill, crates/core/src/spec.rs:229). */
+int qdec_spec_prefill(qdec_state *s, const uint32_t *ids, int n, uint32_t *x_out);
+/* One greedy speculative round from x_p: verify [x_p, d_1..d_k] in one batch, accept the longest matching
+ * prefix plus the model's next token, roll back the DeltaNet states and KV length, re-feed the MTP and draft
+ * the next round.  emitted_out receives *n_emitted (= m + 1 <= k + 1) ids; the last is the next x_p
+ * (Model::spec_round, crates/core/src/spec.rs:326). */
+int qdec_spec_round(qdec_state *s, uint32_t x_p, uint32_t *emitted_out, int *n_emitted);
+/* Replace the drafts of the next round (k ids) -- the forced drafts of the identity tests
+ * (Model::spec_set_drafts, crates/core/src/spec.rs:439); qdec_get_drafts reads the current ones. */
+int qdec_set_drafts(qdec_state *s, const uint32_t *drafts, int k);
+int qdec_get_drafts(const qdec_state *s, uint32_t *drafts_out, int k);
+/* Speculative counters: rounds, drafted, accepted, emitted (spec.rs:21-42 SpecStats). */
+int qdec_spec_counters(const qdec_state *s, uint64_t out4[4]);
+
+/* Parity hooks.  With capture on, every forward keeps the residual row after each layer; qdec_debug_hidden
+ * copies row `row` after layer `layer` (layer == n_layer: the post-final-norm row) to host `out` (hidden floats).
+ * qdec_debug_logits copies row `row` of the last forward's logits. */
+int qdec_set_capture(qdec_state *s, int on);
+int qdec_debug_hidden(qdec_state *s, int layer, int row, float *out);
+int qdec_debug_logits(qdec_state *s, int row, float *out);
+
+/* Write a synthetic Qwen3.8-style GGUF (preset "tiny", "27b" or "27b-L<n>") seeded with `seed`, with
+ * `threads` host threads (0 = all): the stand-in checkpoint of the benchmarks and parity tests. */
+int qdec_synth_gguf(const char *path, const char *preset, uint64_t seed, int threads);
+
 #ifdef __cplusplus
 }
 #endif

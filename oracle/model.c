@@ -1,0 +1,656 @@
+/*
+ * CPU ORACLE (test infrastructure; see oracle.h): the model-level restatement of the reference engine.
+ *
+ *   GGUF reader           crates/core/src/gguf.rs:483-600 (header, KV, tensor index, aligned data section)
+ *   config                crates/core/src/config.rs:146-260 (the keys this path needs)
+ *   forward_token         crates/core/src/model.rs:364-438, :486-490; layers/mod.rs:295-330
+ *   Gated DeltaNet        layers/gated_deltanet.rs:548-602 (token form)
+ *   gated GQA             layers/gqa_attention.rs:155-234 (token form)
+ *   MLP                   layers/mlp.rs:53-64
+ *   MTP head              layers/mtp.rs:95-137
+ *   speculative loop      spec.rs:229-433: verify of k+1 rows, greedy accept, snapshot/restore of the
+ *                         DeltaNet states + KV truncation, MTP re-feed, chained drafts
+ *
+ * The reference's batched forms (forward_batch_in, prefill, matmul_t) are bit-identical to its token form
+ * (its own tests/matmul_t.rs, spec_identity.rs); this oracle uses the token form throughout.  Weights are read
+ * through mmap of the GGUF file.
+ */
+#include <errno.h>
+#include <fcntl.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include "oracle.h"
+
+#define MAXT 2048
+
+typedef struct {
+    char *name;
+    int type;
+    uint64_t ne[4];
+    int nd;
+    uint64_t off, bytes;
+} OTensor;
+
+typedef struct {
+    int type, rows, cols;
+    const uint8_t *data;
+} OMat;
+
+typedef struct {
+    int attn;
+    const float *attn_norm, *post_norm;
+    OMat qkv, gate_z, alpha, beta, ssm_out;
+    const float *ssm_a, *dt_bias, *conv_w, *ssm_norm;
+    OMat q, k, v, o;
+    const float *q_norm, *k_norm;
+    OMat gate, up, down;
+} OLayer;
+
+typedef struct oracle_model {
+    int fd;
+    uint8_t *map;
+    size_t map_len;
+    uint64_t data_off;
+    int n_tensors;
+    OTensor *t;
+    /* config */
+    int n_layer, hidden, ffn, vocab, n_head, n_kv, hd, rope_dim, interval, conv_k, dk, n_k, n_v, dv, kd, vd, conv_dim;
+    float eps, theta, scaling;
+    uint32_t eos, stop2;
+    OLayer *layers;
+    OMat embed, lm_head;
+    const float *out_norm;
+    int has_mtp;
+    OLayer mtp_block;
+    OMat eh_proj;
+    const float *enorm, *hnorm, *head_norm;
+    char err[512];
+} OModel;
+
+typedef struct {
+    float *S, *conv;  /* DeltaNet */
+    float *K, *V;     /* attention: [max_pos][n_kv*hd] */
+} OLayerState;
+
+typedef struct oracle_state {
+    OModel *m;
+    int max_pos, pos;
+    OLayerState *ls;
+    float *mtpK, *mtpV;
+    int mtp_len;
+} OState;
+
+/* ------------------------------------------------------------------------------------------ GGUF */
+
+typedef struct {
+    const uint8_t *p, *end;
+    int ok;
+} Rd;
+
+static uint64_t rd_u(Rd *r, int n) {
+    if (r->p + n > r->end) { r->ok = 0; return 0; }
+    uint64_t v = 0;
+    memcpy(&v, r->p, n);
+    r->p += n;
+    return v;
+}
+static void rd_skip_value(Rd *r, uint32_t t);
+static void rd_skip_value(Rd *r, uint32_t t) {
+    static const int sz[] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    if (t == 8) { uint64_t n = rd_u(r, 8); if (r->p + n > r->end) { r->ok = 0; return; } r->p += n; return; }
+    if (t == 9) {
+        uint32_t et = (uint32_t)rd_u(r, 4);
+        uint64_t n = rd_u(r, 8);
+        for (uint64_t i = 0; i < n && r->ok; i++) rd_skip_value(r, et);
+        return;
+    }
+    if (t > 12) { r->ok = 0; return; }
+    r->p += sz[t];
+}
+
+typedef struct {
+    char key[128];
+    uint32_t type;
+    const uint8_t *val; /* pointer at the value */
+} OKv;
+
+static int kv_find(OKv *kv, int n, const char *key) {
+    for (int i = 0; i < n; i++)
+        if (!strcmp(kv[i].key, key)) return i;
+    return -1;
+}
+static int kv_u32(OKv *kv, int n, const char *key, uint32_t *out) {
+    int i = kv_find(kv, n, key);
+    if (i < 0 || kv[i].type != 4) return -1;
+    memcpy(out, kv[i].val, 4);
+    return 0;
+}
+static int kv_f32(OKv *kv, int n, const char *key, float *out) {
+    int i = kv_find(kv, n, key);
+    if (i < 0 || kv[i].type != 6) return -1;
+    memcpy(out, kv[i].val, 4);
+    return 0;
+}
+
+static OTensor *find_t(OModel *m, const char *name) {
+    for (int i = 0; i < m->n_tensors; i++)
+        if (!strcmp(m->t[i].name, name)) return &m->t[i];
+    return NULL;
+}
+
+static int get_mat(OModel *m, const char *name, int rows, int cols, OMat *out) {
+    OTensor *t = find_t(m, name);
+    if (!t || t->nd != 2 || (int)t->ne[0] != cols || (int)t->ne[1] != rows) {
+        snprintf(m->err, sizeof m->err, "tensor %s missing or not [%d, %d]", name, rows, cols);
+        return -1;
+    }
+    out->type = t->type;
+    out->rows = rows;
+    out->cols = cols;
+    out->data = m->map + m->data_off + t->off;
+    return 0;
+}
+static const float *get_vec(OModel *m, const char *name, int len) {
+    OTensor *t = find_t(m, name);
+    uint64_t n = 1;
+    if (!t) { snprintf(m->err, sizeof m->err, "tensor %s missing", name); return NULL; }
+    for (int d = 0; d < t->nd; d++) n *= t->ne[d];
+    if ((int)n != len || t->type != OT_F32) { snprintf(m->err, sizeof m->err, "tensor %s: %llu elements or not F32", name, (unsigned long long)n); return NULL; }
+    return (const float *)(m->map + m->data_off + t->off);
+}
+
+static int load_layer(OModel *m, int i, int attn, OLayer *L) {
+    char p[64], n[160];
+    snprintf(p, sizeof p, "blk.%d.", i);
+    memset(L, 0, sizeof *L);
+    L->attn = attn;
+#define V(field, suffix, len) do { snprintf(n, sizeof n, "%s%s", p, suffix); if (!(L->field = get_vec(m, n, len))) return -1; } while (0)
+#define M(field, suffix, r, c) do { snprintf(n, sizeof n, "%s%s", p, suffix); if (get_mat(m, n, r, c, &L->field)) return -1; } while (0)
+    V(attn_norm, "attn_norm.weight", m->hidden);
+    V(post_norm, "post_attention_norm.weight", m->hidden);
+    if (attn) {
+        M(q, "attn_q.weight", 2 * m->n_head * m->hd, m->hidden);
+        M(k, "attn_k.weight", m->n_kv * m->hd, m->hidden);
+        M(v, "attn_v.weight", m->n_kv * m->hd, m->hidden);
+        M(o, "attn_output.weight", m->hidden, m->n_head * m->hd);
+        V(q_norm, "attn_q_norm.weight", m->hd);
+        V(k_norm, "attn_k_norm.weight", m->hd);
+    } else {
+        M(qkv, "attn_qkv.weight", m->conv_dim, m->hidden);
+        M(gate_z, "attn_gate.weight", m->vd, m->hidden);
+        M(alpha, "ssm_alpha.weight", m->n_v, m->hidden);
+        M(beta, "ssm_beta.weight", m->n_v, m->hidden);
+        V(ssm_a, "ssm_a", m->n_v);
+        V(dt_bias, "ssm_dt.bias", m->n_v);
+        V(conv_w, "ssm_conv1d.weight", m->conv_dim * m->conv_k);
+        V(ssm_norm, "ssm_norm.weight", m->dv);
+        M(ssm_out, "ssm_out.weight", m->hidden, m->vd);
+    }
+    M(gate, "ffn_gate.weight", m->ffn, m->hidden);
+    M(up, "ffn_up.weight", m->ffn, m->hidden);
+    M(down, "ffn_down.weight", m->hidden, m->ffn);
+#undef V
+#undef M
+    return 0;
+}
+
+void oracle_model_close(OModel *m);
+
+OModel *oracle_model_open(const char *path, char *err, int errlen) {
+    OModel *m = (OModel *)calloc(1, sizeof *m);
+    OKv *kv = NULL;
+    m->fd = open(path, O_RDONLY);
+    if (m->fd < 0) { snprintf(err, errlen, "cannot open %s: %s", path, strerror(errno)); free(m); return NULL; }
+    struct stat st;
+    fstat(m->fd, &st);
+    m->map_len = (size_t)st.st_size;
+    m->map = (uint8_t *)mmap(NULL, m->map_len, PROT_READ, MAP_PRIVATE, m->fd, 0);
+    if (m->map == MAP_FAILED) { snprintf(err, errlen, "mmap failed"); close(m->fd); free(m); return NULL; }
+    Rd r = {m->map, m->map + m->map_len, 1};
+    uint32_t magic = (uint32_t)rd_u(&r, 4), ver = (uint32_t)rd_u(&r, 4);
+    if (magic != 0x46554747u || ver != 3) { snprintf(err, errlen, "not a GGUF v3 file"); goto fail; }
+    uint64_t nt = rd_u(&r, 8), nkv = rd_u(&r, 8);
+    kv = (OKv *)calloc(nkv ? nkv : 1, sizeof *kv);
+    for (uint64_t i = 0; i < nkv && r.ok; i++) {
+        uint64_t kl = rd_u(&r, 8);
+        if (kl >= sizeof kv[i].key || r.p + kl > r.end) { r.ok = 0; break; }
+        memcpy(kv[i].key, r.p, kl);
+        r.p += kl;
+        kv[i].type = (uint32_t)rd_u(&r, 4);
+        kv[i].val = r.p;
+        rd_skip_value(&r, kv[i].type);
+    }
+    m->n_tensors = (int)nt;
+    m->t = (OTensor *)calloc(nt ? nt : 1, sizeof *m->t);
+    for (uint64_t i = 0; i < nt && r.ok; i++) {
+        uint64_t nl = rd_u(&r, 8);
+        if (r.p + nl > r.end) { r.ok = 0; break; }
+        m->t[i].name = (char *)calloc(nl + 1, 1);
+        memcpy(m->t[i].name, r.p, nl);
+        r.p += nl;
+        m->t[i].nd = (int)rd_u(&r, 4);
+        uint64_t n = 1;
+        for (int d = 0; d < m->t[i].nd && d < 4; d++) n *= (m->t[i].ne[d] = rd_u(&r, 8));
+        m->t[i].type = (int)rd_u(&r, 4);
+        m->t[i].off = rd_u(&r, 8);
+        int be, bb;
+        if (!oracle_block_layout(m->t[i].type, &be, &bb)) { snprintf(err, errlen, "unsupported type of %s", m->t[i].name); goto fail; }
+        m->t[i].bytes = n / be * bb;
+    }
+    if (!r.ok) { snprintf(err, errlen, "header truncated"); goto fail; }
+    uint32_t align = 32;
+    kv_u32(kv, (int)nkv, "general.alignment", &align);
+    uint64_t hdr = (uint64_t)(r.p - m->map);
+    m->data_off = (hdr + align - 1) / align * align;
+    uint32_t u;
+#define U(field, key) do { if (kv_u32(kv, (int)nkv, key, &u)) { snprintf(err, errlen, "metadata key missing: %s", key); goto fail; } m->field = (int)u; } while (0)
+    uint32_t bc, nn;
+    if (kv_u32(kv, (int)nkv, "qwen35.block_count", &bc) || kv_u32(kv, (int)nkv, "qwen35.nextn_predict_layers", &nn)) {
+        snprintf(err, errlen, "metadata key missing: block_count");
+        goto fail;
+    }
+    m->n_layer = (int)(bc - nn);
+    U(hidden, "qwen35.embedding_length");
+    U(ffn, "qwen35.feed_forward_length");
+    U(n_head, "qwen35.attention.head_count");
+    U(n_kv, "qwen35.attention.head_count_kv");
+    U(hd, "qwen35.attention.key_length");
+    U(rope_dim, "qwen35.rope.dimension_count");
+    U(interval, "qwen35.full_attention_interval");
+    U(conv_k, "qwen35.ssm.conv_kernel");
+    U(dk, "qwen35.ssm.state_size");
+    U(n_k, "qwen35.ssm.group_count");
+    U(n_v, "qwen35.ssm.time_step_rank");
+    U(vd, "qwen35.ssm.inner_size");
+#undef U
+    if (kv_f32(kv, (int)nkv, "qwen35.attention.layer_norm_rms_epsilon", &m->eps) || kv_f32(kv, (int)nkv, "qwen35.rope.freq_base", &m->theta)) {
+        snprintf(err, errlen, "metadata key missing: eps / freq_base");
+        goto fail;
+    }
+    kv_u32(kv, (int)nkv, "tokenizer.ggml.eos_token_id", &m->eos);
+    m->stop2 = 248044; /* the architecture's extra stop id (crates/core/src/arch.rs:71) */
+    {
+        int ti = kv_find(kv, (int)nkv, "tokenizer.ggml.tokens");
+        if (ti < 0) { snprintf(err, errlen, "metadata key missing: tokenizer.ggml.tokens"); goto fail; }
+        uint64_t cnt;
+        memcpy(&cnt, kv[ti].val + 4, 8);
+        m->vocab = (int)cnt;
+    }
+    m->dv = m->vd / m->n_v;
+    m->kd = m->n_k * m->dk;
+    m->conv_dim = 2 * m->kd + m->vd;
+    m->scaling = powf((float)m->hd, -0.5f);
+    m->layers = (OLayer *)calloc(m->n_layer, sizeof *m->layers);
+    for (int i = 0; i < m->n_layer; i++) {
+        char nm[64];
+        snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", i);
+        int attn = find_t(m, nm) != NULL;
+        if (load_layer(m, i, attn, &m->layers[i])) { snprintf(err, errlen, "%s", m->err); goto fail; }
+    }
+    if (get_mat(m, "token_embd.weight", m->vocab, m->hidden, &m->embed) ||
+        get_mat(m, find_t(m, "output.weight") ? "output.weight" : "token_embd.weight", m->vocab, m->hidden, &m->lm_head) ||
+        !(m->out_norm = get_vec(m, "output_norm.weight", m->hidden))) {
+        snprintf(err, errlen, "%s", m->err);
+        goto fail;
+    }
+    if (nn > 0) {
+        char nm[96];
+        int mi = m->n_layer;
+        if (load_layer(m, mi, 1, &m->mtp_block)) { snprintf(err, errlen, "%s", m->err); goto fail; }
+        snprintf(nm, sizeof nm, "blk.%d.nextn.eh_proj.weight", mi);
+        if (get_mat(m, nm, m->hidden, 2 * m->hidden, &m->eh_proj)) { snprintf(err, errlen, "%s", m->err); goto fail; }
+        snprintf(nm, sizeof nm, "blk.%d.nextn.enorm.weight", mi);
+        m->enorm = get_vec(m, nm, m->hidden);
+        snprintf(nm, sizeof nm, "blk.%d.nextn.hnorm.weight", mi);
+        m->hnorm = get_vec(m, nm, m->hidden);
+        snprintf(nm, sizeof nm, "blk.%d.nextn.shared_head_norm.weight", mi);
+        m->head_norm = get_vec(m, nm, m->hidden);
+        if (!m->enorm || !m->hnorm || !m->head_norm) { snprintf(err, errlen, "%s", m->err); goto fail; }
+        m->has_mtp = 1;
+    }
+    free(kv);
+    return m;
+fail:
+    free(kv);
+    oracle_model_close(m);
+    return NULL;
+}
+
+void oracle_model_close(OModel *m) {
+    if (!m) return;
+    if (m->map && m->map != MAP_FAILED) munmap(m->map, m->map_len);
+    if (m->fd >= 0) close(m->fd);
+    for (int i = 0; i < m->n_tensors; i++) free(m->t[i].name);
+    free(m->t);
+    free(m->layers);
+    free(m);
+}
+
+int oracle_model_dims(OModel *m, int *out8) {
+    out8[0] = m->n_layer;
+    out8[1] = m->hidden;
+    out8[2] = m->vocab;
+    out8[3] = m->has_mtp;
+    out8[4] = (int)m->eos;
+    out8[5] = m->ffn;
+    out8[6] = m->n_head;
+    out8[7] = m->hd;
+    return 0;
+}
+
+/* ----------------------------------------------------------------------------------------- state */
+
+OState *oracle_state_new(OModel *m, int max_pos) {
+    OState *s = (OState *)calloc(1, sizeof *s);
+    s->m = m;
+    s->max_pos = max_pos;
+    s->ls = (OLayerState *)calloc(m->n_layer, sizeof *s->ls);
+    size_t kvd = (size_t)m->n_kv * m->hd;
+    for (int i = 0; i < m->n_layer; i++) {
+        if (m->layers[i].attn) {
+            s->ls[i].K = (float *)calloc((size_t)max_pos * kvd, 4);
+            s->ls[i].V = (float *)calloc((size_t)max_pos * kvd, 4);
+        } else {
+            s->ls[i].S = (float *)calloc((size_t)m->n_v * m->dk * m->dv, 4);
+            s->ls[i].conv = (float *)calloc((size_t)m->conv_dim * (m->conv_k - 1), 4);
+        }
+    }
+    if (m->has_mtp) {
+        s->mtpK = (float *)calloc((size_t)max_pos * kvd, 4);
+        s->mtpV = (float *)calloc((size_t)max_pos * kvd, 4);
+    }
+    return s;
+}
+
+void oracle_state_free(OState *s) {
+    if (!s) return;
+    for (int i = 0; i < s->m->n_layer; i++) {
+        free(s->ls[i].S);
+        free(s->ls[i].conv);
+        free(s->ls[i].K);
+        free(s->ls[i].V);
+    }
+    free(s->ls);
+    free(s->mtpK);
+    free(s->mtpV);
+    free(s);
+}
+
+/* snapshot / restore of the DeltaNet states (spec.rs:154-179); KV caches roll back by length */
+static float *snapshot(OState *s) {
+    OModel *m = s->m;
+    size_t per = (size_t)m->n_v * m->dk * m->dv + (size_t)m->conv_dim * (m->conv_k - 1), n = 0;
+    for (int i = 0; i < m->n_layer; i++) n += m->layers[i].attn ? 0 : per;
+    float *snap = (float *)malloc((n ? n : 1) * 4), *p = snap;
+    for (int i = 0; i < m->n_layer; i++) {
+        if (m->layers[i].attn) continue;
+        memcpy(p, s->ls[i].S, (size_t)m->n_v * m->dk * m->dv * 4);
+        p += (size_t)m->n_v * m->dk * m->dv;
+        memcpy(p, s->ls[i].conv, (size_t)m->conv_dim * (m->conv_k - 1) * 4);
+        p += (size_t)m->conv_dim * (m->conv_k - 1);
+    }
+    return snap;
+}
+static void restore(OState *s, const float *snap) {
+    OModel *m = s->m;
+    const float *p = snap;
+    for (int i = 0; i < m->n_layer; i++) {
+        if (m->layers[i].attn) continue;
+        memcpy(s->ls[i].S, p, (size_t)m->n_v * m->dk * m->dv * 4);
+        p += (size_t)m->n_v * m->dk * m->dv;
+        memcpy(s->ls[i].conv, p, (size_t)m->conv_dim * (m->conv_k - 1) * 4);
+        p += (size_t)m->conv_dim * (m->conv_k - 1);
+    }
+}
+
+/* ---------------------------------------------------------------------------------------- layers */
+
+static void matvec(const OMat *w, const float *x, float *y) { oracle_matmul_f32in(w->type, w->data, w->rows, w->cols, x, 1, y); }
+
+/* gated_deltanet.rs:548-602 */
+static void deltanet_token(OModel *m, const OLayer *L, OLayerState *st, const float *x, float *y) {
+    float *mixed = (float *)malloc((size_t)m->conv_dim * 4), *conved = (float *)malloc((size_t)m->conv_dim * 4);
+    float *z = (float *)malloc((size_t)m->vd * 4), *ga = (float *)malloc((size_t)m->n_v * 4), *gb = (float *)malloc((size_t)m->n_v * 4);
+    float *heads = (float *)malloc((size_t)m->vd * 4), *qn = (float *)malloc((size_t)m->dk * 4), *kn = (float *)malloc((size_t)m->dk * 4);
+    float *o = (float *)malloc((size_t)m->dv * 4);
+    matvec(&L->qkv, x, mixed);
+    matvec(&L->gate_z, x, z);
+    matvec(&L->alpha, x, ga);
+    matvec(&L->beta, x, gb);
+    oracle_conv1d_step(st->conv, L->conv_w, m->conv_k, mixed, m->conv_dim, conved, 1);
+    const float scale = 1.0f / sqrtf((float)m->dk);
+    for (int p = 0; p < m->n_v; p++) {
+        int kh = p % m->n_k;
+        memcpy(qn, conved + kh * m->dk, (size_t)m->dk * 4);
+        memcpy(kn, conved + m->kd + kh * m->dk, (size_t)m->dk * 4);
+        oracle_l2norm(qn, m->dk, 1e-6f);
+        oracle_l2norm(kn, m->dk, 1e-6f);
+        for (int i = 0; i < m->dk; i++) qn[i] *= scale;
+        float g = oracle_gate_g(ga[p], L->dt_bias[p], L->ssm_a[p]);
+        float beta = oracle_gate_beta(gb[p]);
+        oracle_deltanet_step(qn, kn, conved + 2 * m->kd + p * m->dv, m->dk, m->dv, g, beta, st->S + (size_t)p * m->dk * m->dv, o);
+        oracle_rmsnorm_gated(o, z + p * m->dv, L->ssm_norm, m->dv, m->eps, heads + p * m->dv);
+    }
+    matvec(&L->ssm_out, heads, y);
+    free(mixed); free(conved); free(z); free(ga); free(gb); free(heads); free(qn); free(kn); free(o);
+}
+
+/* gqa_attention.rs:155-234 */
+static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int pos, const float *x, float *y) {
+    const int nh = m->n_head, nkv = m->n_kv, hd = m->hd, rd = m->rope_dim, group = nh / nkv;
+    float *qg = (float *)malloc((size_t)2 * nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4), *v = (float *)malloc((size_t)nkv * hd * 4);
+    float *q = (float *)malloc((size_t)nh * hd * 4), *attn = (float *)malloc((size_t)nh * hd * 4), *tmp = (float *)malloc((size_t)hd * 4);
+    float *inv = (float *)malloc((size_t)rd / 2 * 4 + 4), *cs = (float *)malloc((size_t)rd * 4 + 4), *sn = (float *)malloc((size_t)rd * 4 + 4);
+    int len = pos + 1;
+    float *sc = (float *)malloc((size_t)len * 4), *pr = (float *)malloc((size_t)len * 4);
+    matvec(&L->q, x, qg);
+    matvec(&L->k, x, k);
+    matvec(&L->v, x, v);
+    oracle_inv_freq(rd, m->theta, inv);
+    oracle_cos_sin((uint32_t)pos, inv, rd / 2, cs, sn);
+    for (int h = 0; h < nh; h++) {
+        oracle_rmsnorm(qg + (size_t)h * 2 * hd, L->q_norm, hd, m->eps, tmp);
+        oracle_apply_rope(tmp, hd, hd, rd, cs, sn);
+        memcpy(q + (size_t)h * hd, tmp, (size_t)hd * 4);
+    }
+    for (int h = 0; h < nkv; h++) {
+        oracle_rmsnorm(k + (size_t)h * hd, L->k_norm, hd, m->eps, tmp);
+        oracle_apply_rope(tmp, hd, hd, rd, cs, sn);
+        memcpy(k + (size_t)h * hd, tmp, (size_t)hd * 4);
+    }
+    memcpy(K + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
+    memcpy(V + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+    for (int h = 0; h < nh; h++) {
+        int kvh = h / group;
+        const float *qh = q + (size_t)h * hd;
+        for (int t = 0; t < len; t++) {
+            const float *kt = K + ((size_t)t * nkv + kvh) * hd;
+            float s = 0.0f;
+            for (int d = 0; d < hd; d++) s += qh[d] * kt[d];
+            sc[t] = s * m->scaling;
+        }
+        oracle_softmax(sc, len, pr);
+        float *out = attn + (size_t)h * hd;
+        for (int d = 0; d < hd; d++) out[d] = 0.0f;
+        for (int t = 0; t < len; t++) {
+            const float *vt = V + ((size_t)t * nkv + kvh) * hd;
+            for (int d = 0; d < hd; d++) out[d] += pr[t] * vt[d];
+        }
+        for (int d = 0; d < hd; d++) out[d] *= oracle_sigmoid(qg[(size_t)h * 2 * hd + hd + d]);
+    }
+    matvec(&L->o, attn, y);
+    free(qg); free(k); free(v); free(q); free(attn); free(tmp); free(inv); free(cs); free(sn); free(sc); free(pr);
+}
+
+/* layers/mod.rs:295-330: h = x + mixer(norm(x)); y = h + mlp(norm(h)) */
+static void layer_token(OModel *m, const OLayer *L, OLayerState *st, float *K, float *V, int pos, const float *x, float *y) {
+    const int H = m->hidden;
+    float *normed = (float *)malloc((size_t)H * 4), *mixed = (float *)malloc((size_t)H * 4), *resid = (float *)malloc((size_t)H * 4);
+    float *g = (float *)malloc((size_t)m->ffn * 4), *u = (float *)malloc((size_t)m->ffn * 4), *hh = (float *)malloc((size_t)m->ffn * 4);
+    oracle_rmsnorm(x, L->attn_norm, H, m->eps, normed);
+    if (L->attn) attention_token(m, L, K, V, pos, normed, mixed);
+    else deltanet_token(m, L, st, normed, mixed);
+    for (int i = 0; i < H; i++) resid[i] = x[i] + mixed[i];
+    oracle_rmsnorm(resid, L->post_norm, H, m->eps, normed);
+    matvec(&L->gate, normed, g);
+    matvec(&L->up, normed, u);
+    oracle_swiglu(g, u, m->ffn, hh);
+    matvec(&L->down, hh, mixed);
+    for (int i = 0; i < H; i++) y[i] = resid[i] + mixed[i];
+    free(normed); free(mixed); free(resid); free(g); free(u); free(hh);
+}
+
+static void embed_row(OModel *m, uint32_t id, float *out) {
+    size_t rb = oracle_row_bytes(m->embed.type, m->hidden);
+    oracle_dequantize(m->embed.type, m->embed.data + (size_t)id * rb, rb, out, (size_t)m->hidden);
+}
+
+/* Model::forward_token (model.rs:486-490): logits [vocab]; optional capture [n_layer + 1][hidden] of the
+ * residual after each layer and the post-final-norm row; `normed_out` receives the post-final-norm row. */
+int oracle_forward_token(OState *s, uint32_t id, float *logits, float *capture, float *normed_out) {
+    OModel *m = s->m;
+    const int H = m->hidden;
+    if (id >= (uint32_t)m->vocab || s->pos >= s->max_pos) return -1;
+    float *x = (float *)malloc((size_t)H * 4), *y = (float *)malloc((size_t)H * 4), *nrm = (float *)malloc((size_t)H * 4);
+    embed_row(m, id, x);
+    for (int i = 0; i < m->n_layer; i++) {
+        layer_token(m, &m->layers[i], &s->ls[i], s->ls[i].K, s->ls[i].V, s->pos, x, y);
+        memcpy(x, y, (size_t)H * 4);
+        if (capture) memcpy(capture + (size_t)i * H, x, (size_t)H * 4);
+    }
+    oracle_rmsnorm(x, m->out_norm, H, m->eps, nrm);
+    if (capture) memcpy(capture + (size_t)m->n_layer * H, nrm, (size_t)H * 4);
+    if (normed_out) memcpy(normed_out, nrm, (size_t)H * 4);
+    if (logits) matvec(&m->lm_head, nrm, logits);
+    s->pos++;
+    free(x); free(y); free(nrm);
+    return 0;
+}
+
+/* One MTP row (layers/mtp.rs:95-137): hout = head_norm(block([enorm(embed(tok)) | hnorm(h)] @ eh_proj)),
+ * at MTP position s->mtp_len; returns the greedy draft from the shared lm_head when want_draft. */
+static uint32_t mtp_row(OState *s, uint32_t tok, const float *h, float *hout, int want_draft) {
+    OModel *m = s->m;
+    const int H = m->hidden;
+    float *e = (float *)malloc((size_t)H * 4), *cat = (float *)malloc((size_t)2 * H * 4), *u = (float *)malloc((size_t)H * 4);
+    float *yy = (float *)malloc((size_t)H * 4);
+    embed_row(m, tok, e);
+    oracle_rmsnorm(e, m->enorm, H, m->eps, cat);
+    oracle_rmsnorm(h, m->hnorm, H, m->eps, cat + H);
+    matvec(&m->eh_proj, cat, u);
+    layer_token(m, &m->mtp_block, NULL, s->mtpK, s->mtpV, s->mtp_len, u, yy);
+    oracle_rmsnorm(yy, m->head_norm, H, m->eps, hout);
+    s->mtp_len++;
+    uint32_t d = 0;
+    if (want_draft) {
+        float *lg = (float *)malloc((size_t)m->vocab * 4);
+        matvec(&m->lm_head, hout, lg);
+        d = oracle_argmax(lg, m->vocab);
+        free(lg);
+    }
+    free(e); free(cat); free(u); free(yy);
+    return d;
+}
+
+static int is_stop(OModel *m, uint32_t id) { return id == m->eos || id == m->stop2; }
+
+/* The plain greedy loop (crates/cli/src/run.rs:329-350): prefill the prompt, then one token per step;
+ * stops after a stop id when `stop` is set.  Returns the number of ids written. */
+int oracle_generate(OState *s, const uint32_t *prompt, int n, int n_out, int stop, uint32_t *out) {
+    OModel *m = s->m;
+    float *lg = (float *)malloc((size_t)m->vocab * 4);
+    for (int i = 0; i < n; i++)
+        if (oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, NULL)) { free(lg); return -1; }
+    int c = 0;
+    out[c++] = oracle_argmax(lg, m->vocab);
+    while (c < n_out && !(stop && is_stop(m, out[c - 1]))) {
+        if (oracle_forward_token(s, out[c - 1], lg, NULL, NULL)) break;
+        out[c++] = oracle_argmax(lg, m->vocab);
+    }
+    free(lg);
+    return c;
+}
+
+/* The --spec k loop (spec.rs:229-433, run.rs:353-383), greedy: spec_prefill, then rounds of verify
+ * [x_p, d_1..d_k] (token by token on the snapshot), accept, restore + replay of the kept rows, MTP re-feed,
+ * chained drafts.  forced_drafts (optional, n_forced_rounds x k) replaces the MTP drafts of the first rounds,
+ * as spec_set_drafts does in the reference's identity test.  stats4 = rounds, drafted, accepted, emitted. */
+int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, int k, int stop, const uint32_t *forced,
+                         int n_forced, uint32_t *out, uint64_t *stats4, uint32_t *drafts_log) {
+    OModel *m = s->m;
+    const int H = m->hidden, t = k + 1;
+    if (!m->has_mtp || k < 1 || k + 1 > MAXT) return -1;
+    float *lg = (float *)malloc((size_t)m->vocab * 4 * t);
+    float *normed = (float *)malloc((size_t)H * 4 * (n > t ? n : t));
+    float *hout = (float *)malloc((size_t)H * 4), *hprev = (float *)malloc((size_t)H * 4);
+    uint32_t *drafts = (uint32_t *)malloc(sizeof(uint32_t) * k), *emitted = (uint32_t *)malloc(sizeof(uint32_t) * t);
+    int c = 0, round = 0;
+    /* spec_prefill (spec.rs:229-285) */
+    int p = s->pos;
+    for (int i = 0; i < n; i++) oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, normed + (size_t)i * H);
+    uint32_t x_t = oracle_argmax(lg, m->vocab);
+    s->mtp_len = p;
+    for (int j = 0; j < n; j++) {
+        uint32_t x = (j + 1 < n) ? prompt[j + 1] : x_t;
+        uint32_t d = mtp_row(s, x, normed + (size_t)j * H, hout, j == n - 1);
+        if (j == n - 1) drafts[0] = d;
+    }
+    for (int i = 1; i < k; i++) { memcpy(hprev, hout, (size_t)H * 4); drafts[i] = mtp_row(s, drafts[i - 1], hprev, hout, 1); }
+    out[c++] = x_t;
+    uint32_t x_p = x_t;
+    while (c < n_out && !(stop && is_stop(m, out[c - 1]))) {
+        if (forced && round < n_forced) memcpy(drafts, forced + (size_t)round * k, sizeof(uint32_t) * k);
+        if (drafts_log) memcpy(drafts_log + (size_t)round * k, drafts, sizeof(uint32_t) * k);
+        p = s->pos;
+        if (p + t > s->max_pos) break;
+        float *snap = snapshot(s);
+        uint32_t batch[MAXT];
+        batch[0] = x_p;
+        for (int i = 0; i < k; i++) batch[i + 1] = drafts[i];
+        for (int i = 0; i < t; i++) oracle_forward_token(s, batch[i], lg + (size_t)i * m->vocab, NULL, normed + (size_t)i * H);
+        int mm = 0, ne = 0;
+        while (mm < k) {
+            uint32_t a = oracle_argmax(lg + (size_t)mm * m->vocab, m->vocab);
+            emitted[ne++] = a;
+            if (a != drafts[mm]) break;
+            mm++;
+        }
+        if (mm == k) emitted[ne++] = oracle_argmax(lg + (size_t)k * m->vocab, m->vocab);
+        int keep = mm + 1;
+        if (keep < t) {
+            /* restore and replay the kept rows (the replay reruns their recurrence on the same inputs, so the
+             * states are the verify's states after `keep` rows, bit for bit); the KV caches end at p + keep */
+            restore(s, snap);
+            s->pos = p;
+            for (int i = 0; i < keep; i++) oracle_forward_token(s, batch[i], NULL, NULL, NULL);
+        }
+        free(snap);
+        if (stats4) { stats4[0]++; stats4[1] += k; stats4[2] += mm; stats4[3] += keep; }
+        /* the MTP: truncate to p, re-feed the kept pairs (emitted_i, normed_i), draft, chain */
+        s->mtp_len = p;
+        for (int i = 0; i < keep; i++) mtp_row(s, emitted[i], normed + (size_t)i * H, hout, 0);
+        {
+            float *lg1 = (float *)malloc((size_t)m->vocab * 4);
+            matvec(&m->lm_head, hout, lg1);
+            drafts[0] = oracle_argmax(lg1, m->vocab);
+            free(lg1);
+        }
+        for (int i = 1; i < k; i++) { memcpy(hprev, hout, (size_t)H * 4); drafts[i] = mtp_row(s, drafts[i - 1], hprev, hout, 1); }
+        for (int i = 0; i < keep && c < n_out; i++) {
+            out[c++] = emitted[i];
+            if (stop && is_stop(m, emitted[i])) break;
+        }
+        x_p = emitted[keep - 1];
+        round++;
+    }
+    free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted);
+    return c;
+}
+
+int oracle_state_pos(OState *s) { return s->pos; }

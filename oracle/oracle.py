@@ -62,6 +62,18 @@ def lib():
             "oracle_crc32": (U, [P, S]),
             "oracle_silu": (F, [F]),
         }
+        U32P = ctypes.POINTER(ctypes.c_uint32)
+        sig.update({
+            "oracle_model_open": (P, [ctypes.c_char_p, ctypes.c_char_p, I]),
+            "oracle_model_close": (None, [P]),
+            "oracle_model_dims": (I, [P, ctypes.POINTER(ctypes.c_int)]),
+            "oracle_state_new": (P, [P, I]),
+            "oracle_state_free": (None, [P]),
+            "oracle_state_pos": (I, [P]),
+            "oracle_forward_token": (I, [P, ctypes.c_uint32, P, P, P]),
+            "oracle_generate": (I, [P, U32P, I, I, I, U32P]),
+            "oracle_spec_generate": (I, [P, U32P, I, I, I, I, U32P, I, U32P, ctypes.POINTER(ctypes.c_uint64), U32P]),
+        })
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
             fn.restype = res
@@ -256,3 +268,84 @@ def argmax(v):
 def crc32(b):
     b = np.ascontiguousarray(b, dtype=np.uint8)
     return lib().oracle_crc32(_p(b), b.size)
+
+
+class OracleModel:
+    """The reference's model seam restated on the CPU (oracle/model.c): forward_token, the plain greedy loop and
+    the greedy --spec k loop, over a GGUF read through mmap."""
+
+    def __init__(self, path):
+        err = ctypes.create_string_buffer(512)
+        self._h = lib().oracle_model_open(str(path).encode(), err, 512)
+        if not self._h:
+            raise ValueError(f"oracle: {err.value.decode()}")
+        dims = (ctypes.c_int * 8)()
+        lib().oracle_model_dims(self._h, dims)
+        self.n_layer, self.hidden, self.vocab, self.has_mtp, self.eos, self.ffn, self.n_head, self.head_dim = list(dims)
+
+    def close(self):
+        if self._h:
+            lib().oracle_model_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def state(self, max_pos=4096):
+        return OracleState(self, max_pos)
+
+
+class OracleState:
+    def __init__(self, model, max_pos):
+        self.model = model
+        self._h = lib().oracle_state_new(model._h, max_pos)
+
+    def __del__(self):
+        try:
+            lib().oracle_state_free(self._h)
+        except Exception:
+            pass
+
+    @property
+    def pos(self):
+        return lib().oracle_state_pos(self._h)
+
+    def forward_token(self, tok, capture=False):
+        """Returns (logits, captured per-layer residual rows [n_layer + 1][hidden] or None)."""
+        m = self.model
+        lg = np.empty(m.vocab, np.float32)
+        cap = np.empty((m.n_layer + 1, m.hidden), np.float32) if capture else None
+        rc = lib().oracle_forward_token(self._h, tok, _p(lg), _p(cap) if capture else None, None)
+        if rc != 0:
+            raise ValueError("oracle: forward_token failed (id out of range or sequence full)")
+        return lg, cap
+
+    def generate(self, prompt, n_out, stop=True):
+        out = (ctypes.c_uint32 * n_out)()
+        arr = (ctypes.c_uint32 * len(prompt))(*prompt)
+        c = lib().oracle_generate(self._h, arr, len(prompt), n_out, 1 if stop else 0, out)
+        if c < 0:
+            raise ValueError("oracle: generate failed")
+        return list(out[:c])
+
+    def spec_generate(self, prompt, n_out, k, stop=True, forced=None):
+        """Returns (ids, stats dict, drafts used per round)."""
+        out = (ctypes.c_uint32 * n_out)()
+        arr = (ctypes.c_uint32 * len(prompt))(*prompt)
+        st = (ctypes.c_uint64 * 4)()
+        n_forced = 0
+        fz = None
+        if forced is not None:
+            flat = [int(v) for r in forced for v in r]
+            n_forced = len(forced)
+            fz = (ctypes.c_uint32 * len(flat))(*flat)
+        log = (ctypes.c_uint32 * (k * (n_out + 2)))()
+        c = lib().oracle_spec_generate(self._h, arr, len(prompt), n_out, k, 1 if stop else 0, fz, n_forced, out, st, log)
+        if c < 0:
+            raise ValueError("oracle: spec_generate failed")
+        stats = dict(zip(("rounds", "drafted", "accepted", "emitted"), list(st)))
+        drafts = [list(log[i * k:(i + 1) * k]) for i in range(stats["rounds"])]
+        return list(out[:c]), stats, drafts

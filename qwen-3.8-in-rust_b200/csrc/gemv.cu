@@ -13,6 +13,7 @@
 // the reference's order.  Weight bytes stream with ld.global.nc.L1::no_allocate; the activation columns are
 // staged once per CTA into shared memory, transposed so lane l reads its 8 code words with two 16-byte loads.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -82,8 +83,130 @@ __device__ __forceinline__ float group_reduce4(float v) {
     return __shfl_sync(0xffffffffu, b, 0, 8);
 }
 
-template <int TYPE, int NC, int RPT>
-__global__ void __launch_bounds__(GEMV_THREADS, 1)
+// Raw bytes of one weight super-block that lane l needs (positions 4l..4l+3 of every 32-element chunk).
+template <int TYPE>
+struct KBlk;
+template <>
+struct KBlk<T_Q4_K> {
+    uint4 hdr;        // f16 d, f16 dmin, 12 bytes of packed 6-bit scales/mins
+    uint32_t cw[4];   // code bytes 16 + 32p + 4l .. +3: sub-block 2p (low nibbles) and 2p+1 (high)
+};
+template <>
+struct KBlk<T_Q5_K> {
+    uint4 hdr;
+    uint32_t cw[4];   // ql bytes 48 + 32p + 4l .. +3
+    uint32_t qh;      // qh bytes 16 + 4l .. +3: bit s = fifth bit of sub-block s
+};
+template <>
+struct KBlk<T_Q6_K> {
+    uint32_t ql[4];   // ql bytes 32i + 4l .. +3 (i = 2*half + (k & 1))
+    uint32_t qh[2];   // qh bytes 128 + 32*half + 4l .. +3
+    uint32_t sc[4];   // the 16 int8 scales
+    uint32_t d;       // f16 d (low half)
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_blk(const uint8_t* blk, int l, KBlk<TYPE>& b) {
+    if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        constexpr int QO = TYPE == T_Q4_K ? 16 : 48;
+        b.hdr = ld_nc_u128(blk);
+#pragma unroll
+        for (int p = 0; p < 4; p++) b.cw[p] = ld_nc_u32(blk + QO + 32 * p + 4 * l);
+        if constexpr (TYPE == T_Q5_K) b.qh = ld_nc_u32(blk + 16 + 4 * l);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) b.ql[i] = ld_u32_2aligned(blk + 32 * i + 4 * l);
+#pragma unroll
+        for (int h = 0; h < 2; h++) b.qh[h] = ld_u32_2aligned(blk + 128 + 32 * h + 4 * l);
+#pragma unroll
+        for (int i = 0; i < 4; i++) b.sc[i] = ld_u32_2aligned(blk + 192 + 4 * i);
+        b.d = ld_nc_u16(blk + 208);
+    }
+}
+
+// The f32 terms lane l adds for one (row, super-block): main[n] = (dx * dw) * f32(sumi[l]) and, for
+// Q4_K/Q5_K lanes l < 4, mins[n] = (-dx * dminw) * f32(prod[l]) (kdot.rs:37-76, :97-141).
+template <int TYPE, int NC>
+__device__ __forceinline__ void kblk_terms(const KBlk<TYPE>& b, int l, const uint32_t* __restrict__ xq_sb, int xq_stride,
+                                           const float* __restrict__ xd_sb, int xd_stride, const int* __restrict__ xs_sb,
+                                           int xs_stride, float (&tmain)[NC], float (&tmin)[NC]) {
+    if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        // get_scale_min_k4 for the 8 sub-blocks, one byte per sub-block (quant.rs:45-51)
+        const uint32_t sc03 = b.hdr.y & 0x3F3F3F3Fu;
+        const uint32_t m03 = b.hdr.z & 0x3F3F3F3Fu;
+        const uint32_t sc47 = (b.hdr.w & 0x0F0F0F0Fu) | ((b.hdr.y >> 2) & 0x30303030u);
+        const uint32_t m47 = ((b.hdr.w >> 4) & 0x0F0F0F0Fu) | ((b.hdr.z >> 2) & 0x30303030u);
+        const float dw = f16_bits_to_f32((uint16_t)(b.hdr.x & 0xffff));
+        const float dminw = f16_bits_to_f32((uint16_t)(b.hdr.x >> 16));
+        int sc[8];
+#pragma unroll
+        for (int s = 0; s < 4; s++) sc[s] = byte_of(sc03, s), sc[s + 4] = byte_of(sc47, s);
+        uint32_t code[8];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            code[2 * p] = b.cw[p] & 0x0F0F0F0Fu;
+            code[2 * p + 1] = (b.cw[p] >> 4) & 0x0F0F0F0Fu;
+        }
+        if constexpr (TYPE == T_Q5_K) {
+#pragma unroll
+            for (int s = 0; s < 8; s++) code[s] |= ((b.qh >> s) & 0x01010101u) << 4;
+        }
+        const int lm = l & 3;  // min lane l (l < 4): sub-blocks 2l, 2l+1
+        const int mA = (lm < 2) ? byte_of(m03, 2 * lm) : byte_of(m47, 2 * lm - 4);
+        const int mB = (lm < 2) ? byte_of(m03, 2 * lm + 1) : byte_of(m47, 2 * lm - 3);
+#pragma unroll
+        for (int n = 0; n < NC; n++) {
+            const uint4* xp = reinterpret_cast<const uint4*>(xq_sb + (size_t)n * xq_stride + l * 8);
+            const uint4 x0 = xp[0], x1 = xp[1];
+            const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int sumi = 0;
+#pragma unroll
+            for (int s = 0; s < 8; s++) sumi += sc[s] * __dp4a((int)code[s], (int)xw[s], 0);
+            const float dx = xd_sb[n * xd_stride];
+            tmain[n] = __fmul_rn(__fmul_rn(dx, dw), (float)sumi);
+            const int2 q8 = *reinterpret_cast<const int2*>(xs_sb + (size_t)n * xs_stride + 2 * lm);
+            tmin[n] = __fmul_rn(__fmul_rn(-dx, dminw), (float)(mA * q8.x + mB * q8.y));
+        }
+    } else {
+        const float dw = f16_bits_to_f32((uint16_t)(b.d & 0xffff));
+        uint32_t code[8];
+        int scl[8];
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t lo = (b.ql[2 * h + (k & 1)] >> (4 * (k >> 1))) & 0x0F0F0F0Fu;
+                const uint32_t hi = ((b.qh[h] >> (2 * k)) & 0x03030303u) << 4;
+                code[4 * h + k] = lo | hi;
+                const int si = h * 8 + 2 * k + (l >> 2);  // sc[2k + l/16] of half h
+                scl[4 * h + k] = (int)(int8_t)byte_of(b.sc[si >> 2], si & 3);
+            }
+        const int s0 = (int)(int8_t)byte_of(b.sc[(2 * l) >> 2], (2 * l) & 3);
+        const int s1 = (int)(int8_t)byte_of(b.sc[(2 * l + 1) >> 2], (2 * l + 1) & 3);
+#pragma unroll
+        for (int n = 0; n < NC; n++) {
+            const uint4* xp = reinterpret_cast<const uint4*>(xq_sb + (size_t)n * xq_stride + l * 8);
+            const uint4 x0 = xp[0], x1 = xp[1];
+            const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int sumi = 0;
+#pragma unroll
+            for (int c = 0; c < 8; c++) sumi += scl[c] * __dp4a((int)code[c], (int)xw[c], 0);
+            const int2 bs = *reinterpret_cast<const int2*>(xs_sb + (size_t)n * xs_stride + 2 * l);
+            sumi -= 32 * (bs.x * s0 + bs.y * s1);
+            tmain[n] = __fmul_rn(__fmul_rn(xd_sb[n * xd_stride], dw), (float)sumi);
+            tmin[n] = 0.0f;
+        }
+    }
+}
+
+// K-quant GEMV.  A warp owns R rows; its 32 lanes are 4 super-block slots x 8 lane groups: in round j the
+// lane (slot k, group l) takes super-block 4j + k of each of the R rows and computes the f32 terms of the
+// reference's lane l.  The per-lane f32 accumulators are then advanced in super-block order by shuffling the
+// 4 slots' terms in (the reference's sequential chain, kdot.rs:72-74), so every bit matches while 32 lanes
+// keep 4 x R super-blocks in flight; the next round's blocks are loaded before this round is computed.
+// Lane l's activation words are read from shared memory once per super-block and reused for the R rows.
+template <int TYPE, int NC, int R>
+__global__ void __launch_bounds__(GEMV_THREADS)
 kq_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8_t* __restrict__ act, float* __restrict__ y) {
     constexpr int BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
     constexpr int XS = TYPE == T_Q6_K ? 16 : 8;
@@ -94,134 +217,65 @@ kq_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8_t* _
     stage_q8k<XS>(act, NC, nb, xq, xd, xs);
     __syncthreads();
 
-    const int lane = threadIdx.x & 31, l = lane & 7, rg = lane >> 3, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, l = lane & 7, slot = lane >> 3;
     const size_t row_bytes = (size_t)nb * BB;
-    const int rows_per_cta = (GEMV_THREADS / 32) * 4 * RPT;
-    for (int tile = blockIdx.x; tile * rows_per_cta < rows; tile += gridDim.x) {
-        const int row0 = tile * rows_per_cta + warp * 4 * RPT + rg * RPT;
-        const uint8_t* wr[RPT];
-        bool ok[RPT];
+    const int warps_total = gridDim.x * (GEMV_THREADS / 32);
+    for (int grp = blockIdx.x * (GEMV_THREADS / 32) + (threadIdx.x >> 5); grp * R < rows; grp += warps_total) {
+        const int row0 = grp * R;
+        const uint8_t* wr[R];
 #pragma unroll
-        for (int r = 0; r < RPT; r++) {
-            ok[r] = row0 + r < rows;
-            wr[r] = w + (size_t)(ok[r] ? row0 + r : 0) * row_bytes;
-        }
-        float acc[RPT][NC], accm[RPT][NC];
+        for (int r = 0; r < R; r++) wr[r] = w + (size_t)min(row0 + r, rows - 1) * row_bytes;
+        float acc[R][NC], accm[R][NC];
 #pragma unroll
-        for (int r = 0; r < RPT; r++)
+        for (int r = 0; r < R; r++)
 #pragma unroll
             for (int n = 0; n < NC; n++) acc[r][n] = 0.0f, accm[r][n] = 0.0f;
 
-        for (int sb = 0; sb < nb; sb++) {
-            if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-                uint4 hdr[RPT];
-                uint32_t cw[RPT][4], qh[RPT];
+        KBlk<TYPE> cur[R], nxt[R];
+        if (slot < nb) {
 #pragma unroll
-                for (int r = 0; r < RPT; r++) {
-                    const uint8_t* blk = wr[r] + (size_t)sb * BB;
-                    hdr[r] = ld_nc_u128(blk);
-                    constexpr int QO = TYPE == T_Q4_K ? 16 : 48;
-#pragma unroll
-                    for (int p = 0; p < 4; p++) cw[r][p] = ld_nc_u32(blk + QO + 32 * p + 4 * l);
-                    if constexpr (TYPE == T_Q5_K) qh[r] = ld_nc_u32(blk + 16 + 4 * l);
-                }
-#pragma unroll
-                for (int r = 0; r < RPT; r++) {
-                    // get_scale_min_k4 for the 8 sub-blocks, packed one byte per sub-block (quant.rs:45-51)
-                    const uint32_t sc03 = hdr[r].y & 0x3F3F3F3Fu;
-                    const uint32_t m03 = hdr[r].z & 0x3F3F3F3Fu;
-                    const uint32_t sc47 = (hdr[r].w & 0x0F0F0F0Fu) | ((hdr[r].y >> 2) & 0x30303030u);
-                    const uint32_t m47 = ((hdr[r].w >> 4) & 0x0F0F0F0Fu) | ((hdr[r].z >> 2) & 0x30303030u);
-                    const float dw = f16_bits_to_f32((uint16_t)(hdr[r].x & 0xffff));
-                    const float dminw = f16_bits_to_f32((uint16_t)(hdr[r].x >> 16));
-                    int sc[8];
-#pragma unroll
-                    for (int s = 0; s < 4; s++) sc[s] = byte_of(sc03, s), sc[s + 4] = byte_of(sc47, s);
-                    uint32_t code[8];
-#pragma unroll
-                    for (int p = 0; p < 4; p++) {
-                        code[2 * p] = cw[r][p] & 0x0F0F0F0Fu;
-                        code[2 * p + 1] = (cw[r][p] >> 4) & 0x0F0F0F0Fu;
-                    }
-                    if constexpr (TYPE == T_Q5_K) {
-#pragma unroll
-                        for (int s = 0; s < 8; s++) code[s] |= ((qh[r] >> s) & 0x01010101u) << 4;
-                    }
-                    // min lane l (l < 4): sub-blocks 2l and 2l+1
-                    const int lm = l & 3;  // only lanes 0..3 use it
-                    const int mA = (lm < 2) ? byte_of(m03, 2 * lm) : byte_of(m47, 2 * lm - 4);
-                    const int mB = (lm < 2) ? byte_of(m03, 2 * lm + 1) : byte_of(m47, 2 * lm - 3);
-#pragma unroll
-                    for (int n = 0; n < NC; n++) {
-                        const uint4* xp = reinterpret_cast<const uint4*>(xq + ((size_t)(n * nb + sb) * 64 + l * 8));
-                        const uint4 x0 = xp[0], x1 = xp[1];
-                        const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        int sumi = 0;
-#pragma unroll
-                        for (int s = 0; s < 8; s++) sumi += sc[s] * __dp4a((int)code[s], (int)xw[s], 0);
-                        const float dx = xd[n * nb + sb];
-                        acc[r][n] = __fadd_rn(acc[r][n], __fmul_rn(__fmul_rn(dx, dw), (float)sumi));
-                        if (l < 4) {
-                            const int2 q8 = *reinterpret_cast<const int2*>(xs + (size_t)(n * nb + sb) * 8 + 2 * l);
-                            const int prod = mA * q8.x + mB * q8.y;
-                            accm[r][n] = __fadd_rn(accm[r][n], __fmul_rn(__fmul_rn(-dx, dminw), (float)prod));
-                        }
-                    }
-                }
-            } else {  // Q6_K: 128 ql, 64 qh, 16 int8 scales, f16 d (kdot.rs:97-141)
-                uint32_t qlw[RPT][4], qhw[RPT][2], scw[RPT][4];
-                uint16_t dbits[RPT];
-#pragma unroll
-                for (int r = 0; r < RPT; r++) {
-                    const uint8_t* blk = wr[r] + (size_t)sb * BB;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) qlw[r][i] = ld_u32_2aligned(blk + 32 * i + 4 * l);
-#pragma unroll
-                    for (int h = 0; h < 2; h++) qhw[r][h] = ld_u32_2aligned(blk + 128 + 32 * h + 4 * l);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) scw[r][i] = ld_u32_2aligned(blk + 192 + 4 * i);
-                    dbits[r] = ld_nc_u16(blk + 208);
-                }
-#pragma unroll
-                for (int r = 0; r < RPT; r++) {
-                    const float dw = f16_bits_to_f32(dbits[r]);
-                    uint32_t code[8];
-                    int scl[8];
-#pragma unroll
-                    for (int h = 0; h < 2; h++)
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const uint32_t lo = (qlw[r][2 * h + (k & 1)] >> (4 * (k >> 1))) & 0x0F0F0F0Fu;
-                            const uint32_t hi = ((qhw[r][h] >> (2 * k)) & 0x03030303u) << 4;
-                            code[4 * h + k] = lo | hi;
-                            const int si = h * 8 + 2 * k + (l >> 2);  // sc[2k + l/16] of half h
-                            scl[4 * h + k] = (int)(int8_t)byte_of(scw[r][si >> 2], si & 3);
-                        }
-                    const int s0 = (int)(int8_t)byte_of(scw[r][(2 * l) >> 2], (2 * l) & 3);
-                    const int s1 = (int)(int8_t)byte_of(scw[r][(2 * l + 1) >> 2], (2 * l + 1) & 3);
-#pragma unroll
-                    for (int n = 0; n < NC; n++) {
-                        const uint4* xp = reinterpret_cast<const uint4*>(xq + ((size_t)(n * nb + sb) * 64 + l * 8));
-                        const uint4 x0 = xp[0], x1 = xp[1];
-                        const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        int sumi = 0;
-#pragma unroll
-                        for (int c = 0; c < 8; c++) sumi += scl[c] * __dp4a((int)code[c], (int)xw[c], 0);
-                        const int2 bs = *reinterpret_cast<const int2*>(xs + (size_t)(n * nb + sb) * 16 + 2 * l);
-                        sumi -= 32 * (bs.x * s0 + bs.y * s1);
-                        const float dx = xd[n * nb + sb];
-                        acc[r][n] = __fadd_rn(acc[r][n], __fmul_rn(__fmul_rn(dx, dw), (float)sumi));
-                    }
-                }
-            }
+            for (int r = 0; r < R; r++) load_blk<TYPE>(wr[r] + (size_t)slot * BB, l, cur[r]);
         }
+        for (int base = 0; base < nb; base += 4) {
+            const int sb = base + slot;
+            if (sb + 4 < nb) {
 #pragma unroll
-        for (int r = 0; r < RPT; r++)
+                for (int r = 0; r < R; r++) load_blk<TYPE>(wr[r] + (size_t)(sb + 4) * BB, l, nxt[r]);
+            }
+            float tmain[R][NC], tmin[R][NC];
+            if (sb < nb) {
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    kblk_terms<TYPE, NC>(cur[r], l, xq + (size_t)sb * 64, nb * 64, xd + sb, nb, xs + (size_t)sb * XS, nb * XS,
+                                         tmain[r], tmin[r]);
+            } else {
+#pragma unroll
+                for (int r = 0; r < R; r++)
+#pragma unroll
+                    for (int n = 0; n < NC; n++) tmain[r][n] = 0.0f, tmin[r][n] = 0.0f;
+            }
+            const int kmax = min(4, nb - base);
+            for (int k = 0; k < kmax; k++) {
+#pragma unroll
+                for (int r = 0; r < R; r++)
+#pragma unroll
+                    for (int n = 0; n < NC; n++) {
+                        acc[r][n] = __fadd_rn(acc[r][n], __shfl_sync(0xffffffffu, tmain[r][n], k * 8 + l));
+                        if constexpr (TYPE != T_Q6_K)
+                            accm[r][n] = __fadd_rn(accm[r][n], __shfl_sync(0xffffffffu, tmin[r][n], k * 8 + l));
+                    }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) cur[r] = nxt[r];
+        }
+        // every slot now holds the same lane accumulators; slot 0 reduces in the reference's order
+#pragma unroll
+        for (int r = 0; r < R; r++)
 #pragma unroll
             for (int n = 0; n < NC; n++) {
                 float v = group_reduce8(acc[r][n]);
                 if constexpr (TYPE != T_Q6_K) v = __fadd_rn(v, group_reduce4(accm[r][n]));
-                if (l == 0 && ok[r]) y[(size_t)n * rows + row0 + r] = v;
+                if (lane == 0 && row0 + r < rows) y[(size_t)n * rows + row0 + r] = v;
             }
     }
 }
@@ -358,23 +412,39 @@ __global__ void f32_gemv_kernel(const float* __restrict__ w, int rows, int cols,
 
 int g_num_sms = 0;
 
-template <int TYPE, int NC>
-cudaError_t launch_kq(const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
-    const int nb = cols / QK_K;
+template <int TYPE, int NC, int R>
+cudaError_t launch_kq_r(const uint8_t* w, int rows, int nb, const void* act, float* y, cudaStream_t s) {
     constexpr int XS = TYPE == T_Q6_K ? 16 : 8;
-    constexpr int RPT = 1;
     const size_t smem = Q8KSmem<XS>::bytes(NC, nb);
-    auto kern = kq_gemv_kernel<TYPE, NC, RPT>;
+    auto kern = kq_gemv_kernel<TYPE, NC, R>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int rows_per_cta = (GEMV_THREADS / 32) * 4 * RPT;
-    const int tiles = (rows + rows_per_cta - 1) / rows_per_cta;
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, smem);
     if (e != cudaSuccess) return e;
-    const int grid = std::max(1, std::min(tiles, num_sms() * std::max(1, per_sm)));
+    const int warps = GEMV_THREADS / 32;
+    const int groups = (rows + R - 1) / R;
+    const int grid = std::max(1, std::min((groups + warps - 1) / warps, num_sms() * std::max(1, per_sm)));
     kern<<<grid, GEMV_THREADS, smem, s>>>(w, rows, nb, (const uint8_t*)act, y);
     return cudaGetLastError();
+}
+
+// Rows per warp: 4 when there are enough rows to give every SM a few dozen warps (activation reads from shared
+// memory then amortise over 4 rows), fewer for short matrices so the grid still covers the GPU.
+template <int TYPE, int NC>
+cudaError_t launch_kq(const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
+    const int nb = cols / QK_K;
+    const int sms = num_sms();
+    static const int forced_r = [] {
+        const char* e = getenv("QDEC_GEMV_ROWS_PER_WARP");  // tuning override: 1, 2 or 4
+        return e ? atoi(e) : 0;
+    }();
+    if (forced_r == 4) return launch_kq_r<TYPE, NC, 4>(w, rows, nb, act, y, s);
+    if (forced_r == 2) return launch_kq_r<TYPE, NC, 2>(w, rows, nb, act, y, s);
+    if (forced_r == 1) return launch_kq_r<TYPE, NC, 1>(w, rows, nb, act, y, s);
+    if (rows >= sms * 16 * 4) return launch_kq_r<TYPE, NC, 4>(w, rows, nb, act, y, s);
+    if (rows >= sms * 16 * 2) return launch_kq_r<TYPE, NC, 2>(w, rows, nb, act, y, s);
+    return launch_kq_r<TYPE, NC, 1>(w, rows, nb, act, y, s);
 }
 
 template <int TYPE, int NC>
@@ -406,6 +476,9 @@ cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, fl
 
 template <int NC>
 cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
+    static const bool no_tma = getenv("QDEC_GEMV_NO_TMA") != nullptr;  // tuning override: the register-path kernel
+    if (!no_tma && tma_gemv_supported(type, cols, NC) && ((uintptr_t)w & 15) == 0)
+        return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
     switch (type) {
     case T_Q4_K: return launch_kq<T_Q4_K, NC>(w, rows, cols, act, y, s);
     case T_Q5_K: return launch_kq<T_Q5_K, NC>(w, rows, cols, act, y, s);

@@ -24,5 +24,11 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
 // Bytes of one activation row of `cols` values in the form `type` consumes.
 size_t act_row_bytes(int type, int cols);
 int num_sms();
+// Bulk-copy pipelined K-quant GEMV (gemv_tma.cu) for Q4_K / Q5_K when its staging fits shared memory.
+bool tma_gemv_supported(int type, int cols, int ncols);
+cudaError_t launch_gemv_tma(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
+                            cudaStream_t s);
+// The device error word set by bounded waits that gave up (0 = none); optionally cleared.
+unsigned read_kernel_error(bool clear);
 
 }  // namespace qdec

@@ -1,0 +1,520 @@
+// Per-layer kernels of the decode step, each bit-exact with the reference's f32 order:
+//
+//   resid_norm_quant  h = a + b; y = rmsnorm(h, w); y -> Q8_K / Q8_0 rows   (layers/mod.rs:316-323,
+//                     kernels/rmsnorm.rs:14-76, q8k.rs:76-114, q8.rs:81-103)
+//   swiglu_quant      h = silu(g) * u; h -> Q8_K / Q8_0                     (layers/mlp.rs:53-64, act.rs:24)
+//   conv_step         causal depthwise conv + SiLU, t rows, deferred commit  (kernels/conv.rs:11-36)
+//   deltanet_heads    l2norm, gates, gated delta rule, gated RMSNorm per V head, t rows sequential, with the
+//                     state commit of the previous round's accepted rows    (layers/gated_deltanet.rs:261-370,
+//                     kernels/deltanet.rs:19-89, spec.rs:395-415)
+//   qk_norm_rope      per-head q/k RMSNorm, partial rotate-half RoPE, K/V cache append
+//                                                                           (layers/gqa_attention.rs:343-362)
+//   attention         scores over the cache, softmax, V sum, sigmoid gate   (layers/gqa_attention.rs:376-409,
+//                                                                            kernels/softmax.rs:22-50)
+//   argmax            first index of the maximum                            (model.rs:505-513)
+//
+// "Bit-exact" holds with the transcendentals of common.cuh (exp/log1p evaluated in double, rounded once).
+#include <algorithm>
+
+#include "common.cuh"
+#include "layers.cuh"
+
+namespace qdec {
+
+namespace {
+
+// The reference's 8-lane sum of squares over x[0..n) (rmsnorm.rs:55-69): lane k accumulates x[k], x[k+8], ...
+// left to right; then reduce8; then the n % 8 tail left to right.  `xs` is in shared memory; the 8 lanes run
+// on threads 0..7 of the block; the result is returned on every thread (via shared memory).
+__device__ float sum_squares_8lane_block(const float* xs, int n, float* red) {
+    const int n8 = n / 8 * 8;
+    if (threadIdx.x < 8) {
+        float acc = 0.0f;
+        for (int i = threadIdx.x; i < n8; i += 8) acc = __fadd_rn(acc, __fmul_rn(xs[i], xs[i]));
+        red[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float ss = reduce8(red);
+        for (int i = n8; i < n; i++) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
+        red[8] = ss;
+    }
+    __syncthreads();
+    const float r = red[8];
+    __syncthreads();
+    return r;
+}
+
+// 1 / sqrt(mean + eps) with mean = ss / n (rmsnorm.rs:49-53)
+__device__ __forceinline__ float inv_rms_of(float ss, int n, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// Quantise a row held in shared memory into Q8_K blocks (warp per block), bit-exact with q8k.rs:76-114.
+__device__ void quant_q8k_block_row(const float* xs, int n, uint8_t* out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int b = warp; b < n / 256; b += nw) {
+        const float* blk = xs + b * 256;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = blk[lane * 8 + i];
+        float amax = 0.0f, mx = 0.0f;
+        int idx = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float a = fabsf(v[i]);
+            if (a > amax) amax = a, mx = v[i], idx = lane * 8 + i;
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+            const float om = __shfl_xor_sync(0xffffffffu, mx, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+            if (oa > amax || (oa == amax && oi < idx)) amax = oa, mx = om, idx = oi;
+        }
+        uint8_t* o = out + (size_t)b * Q8K_BLOCK_BYTES;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+        if (amax == 0.0f) {
+            for (int w = lane; w < 73; w += 32) ow[w] = 0u;
+            continue;
+        }
+        const float iscale = __fdiv_rn(-127.0f, mx);
+        int q[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int qi = __float2int_rn(__fmul_rn(iscale, v[i]));
+            q[i] = qi > 127 ? 127 : qi;
+        }
+        ow[1 + 2 * lane] = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+        ow[2 + 2 * lane] = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+        int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        const int s_hi = __shfl_down_sync(0xffffffffu, s, 2);  // lane 4g: bsums[2g] (own), bsums[2g+1] (lane 4g+2)
+        if ((lane & 3) == 0) ow[65 + (lane >> 2)] = (uint32_t)(s & 0xffff) | ((uint32_t)(s_hi & 0xffff) << 16);
+        if (lane == 0) ow[0] = __float_as_uint(__fdiv_rn(1.0f, iscale));
+    }
+}
+
+// Quantise a row held in shared memory into Q8_0 blocks (warp per block), bit-exact with q8.rs:81-103.
+__device__ void quant_q8_0_block_row(const float* xs, int n, uint8_t* out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int b = warp; b < n / 32; b += nw) {
+        const float v = xs[b * 32 + lane];
+        float amax = fabsf(v);
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float dd = __fdiv_rn(amax, 127.0f);
+        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+        const float qf = roundf(__fmul_rn(v, id));
+        const int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
+        const int lo = __shfl_sync(0xffffffffu, qi, (2 * lane - 2) & 31);
+        const int hi = __shfl_sync(0xffffffffu, qi, (2 * lane - 1) & 31);
+        uint16_t* o = reinterpret_cast<uint16_t*>(out + (size_t)b * Q8_0_BLOCK_BYTES);
+        if (lane == 0) o[0] = __half_as_ushort(__float2half_rn(dd));
+        else if (lane <= 16) o[lane] = (uint16_t)((lo & 0xff) | ((hi & 0xff) << 8));
+    }
+}
+
+}  // namespace
+
+// One CTA per row.  h = a + b (b may be null: h = a), written to h_out when given; y = rmsnorm(h, w) written
+// to y_out when given; y quantised into q8k_out / q80_out rows when given.
+__global__ void resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ h_out,
+                                        const float* __restrict__ w, float eps, int n, float* __restrict__ y_out,
+                                        uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
+    extern __shared__ __align__(16) float sm[];
+    float* xs = sm;
+    float* red = sm + n;
+    const int row = blockIdx.x;
+    const float* ar = a + (size_t)row * n;
+    const float* br = b ? b + (size_t)row * n : nullptr;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float h = br ? __fadd_rn(ar[i], br[i]) : ar[i];
+        xs[i] = h;
+        if (h_out) h_out[(size_t)row * n + i] = h;
+    }
+    __syncthreads();
+    const float inv = inv_rms_of(sum_squares_8lane_block(xs, n, red), n, eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float y = __fmul_rn(__fmul_rn(xs[i], inv), w[i]);
+        xs[i] = y;
+        if (y_out) y_out[(size_t)row * n + i] = y;
+    }
+    __syncthreads();
+    if (q8k_out) quant_q8k_block_row(xs, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
+    if (q80_out) quant_q8_0_block_row(xs, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+}
+
+// One CTA per row: y[row * y_ld + i] = rmsnorm(x[row * x_ld ..], w)[i] (rmsnorm.rs:25-33).
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int x_ld, const float* __restrict__ w, float eps, int n,
+                                    float* __restrict__ y, int y_ld) {
+    extern __shared__ __align__(16) float sm[];
+    float* xs = sm;
+    float* red = sm + n;
+    const float* xr = x + (size_t)blockIdx.x * x_ld;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
+    __syncthreads();
+    const float inv = inv_rms_of(sum_squares_8lane_block(xs, n, red), n, eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) y[(size_t)blockIdx.x * y_ld + i] = __fmul_rn(__fmul_rn(xs[i], inv), w[i]);
+}
+
+// One CTA per row: h = silu(g) * u (act.rs:24), optionally written, then quantised.
+__global__ void swiglu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int n, float* __restrict__ h_out,
+                                    uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
+    extern __shared__ __align__(16) float sm[];
+    const int row = blockIdx.x;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float h = __fmul_rn(silu_f32(g[(size_t)row * n + i]), u[(size_t)row * n + i]);
+        sm[i] = h;
+        if (h_out) h_out[(size_t)row * n + i] = h;
+    }
+    __syncthreads();
+    if (q8k_out) quant_q8k_block_row(sm, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
+    if (q80_out) quant_q8_0_block_row(sm, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+}
+
+// Quantise rows already in global memory (one CTA per row) -- used for the mixer outputs.
+__global__ void quant_rows_kernel(const float* __restrict__ x, int n, uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
+    extern __shared__ __align__(16) float sm[];
+    const int row = blockIdx.x;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = x[(size_t)row * n + i];
+    __syncthreads();
+    if (q8k_out) quant_q8k_block_row(sm, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
+    if (q80_out) quant_q8_0_block_row(sm, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+}
+
+// Causal depthwise conv1d (+ SiLU) for t rows, one thread per channel (conv.rs:11-36).  The committed window
+// `state` (channels x (K-1)) first absorbs the `keep` pending inputs of the previous call (the accepted rows of
+// the previous round), then the t new rows are stepped from it; their inputs become the new pending rows.
+__global__ void conv_step_kernel(float* __restrict__ state, const float* __restrict__ w, int K, int channels,
+                                 const float* __restrict__ x, int t, float* __restrict__ out, float* __restrict__ pend_x,
+                                 const int* __restrict__ keep_prev, int max_t) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= channels) return;
+    float st[8];
+    for (int j = 0; j < K - 1; j++) st[j] = state[(size_t)c * (K - 1) + j];
+    const int keep = keep_prev ? *keep_prev : 0;
+    for (int i = 0; i < keep; i++) {  // commit: shift in the accepted inputs (conv.rs:30-33)
+        for (int j = 0; j < K - 2; j++) st[j] = st[j + 1];
+        if (K >= 2) st[K - 2] = pend_x[(size_t)i * channels + c];
+    }
+    for (int j = 0; j < K - 1; j++) state[(size_t)c * (K - 1) + j] = st[j];
+    const float* wc = w + (size_t)c * K;
+    for (int i = 0; i < t; i++) {
+        const float xn = x[(size_t)i * channels + c];
+        float acc = 0.0f;
+        for (int j = 0; j < K - 1; j++) acc = __fadd_rn(acc, __fmul_rn(wc[j], st[j]));
+        acc = __fadd_rn(acc, __fmul_rn(wc[K - 1], xn));
+        for (int j = 0; j < K - 2; j++) st[j] = st[j + 1];
+        if (K >= 2) st[K - 2] = xn;
+        out[(size_t)i * channels + c] = silu_f32(acc);
+        if (i < max_t) pend_x[(size_t)i * channels + c] = xn;
+    }
+}
+
+// One CTA per V head p, one thread per value column j (blockDim.x == dv, dk <= DK_MAX); the head's state column
+// S[:, j] lives in the thread's registers.  Steps:
+//   1. load S (the committed state of the previous call) and apply its `keep` pending rows: S *= decay_i;
+//      S += k_i (x) delta_i -- the same element operations, in the same order, as the reference's replay of the
+//      accepted rows from a snapshot (spec.rs:395-415), so the state is bit-identical; store S back.
+//   2. for each of the t new rows: l2norm q and k, scale q, gates, the delta rule, gated RMSNorm; record
+//      (decay, k, delta) as the pending rows.  The state after the t rows is not stored: the next call commits
+//      exactly the rows the accept step keeps.
+template <int DK>
+__global__ void __launch_bounds__(128) deltanet_heads_kernel(const DeltaArgs a) {
+    const int p = blockIdx.x, j = threadIdx.x;
+    const int dk = DK, dv = a.dv;
+    const int kh = p % a.n_k;
+    __shared__ float qs[DK], ks[DK], red[16], outs[256];
+    __shared__ float scal[4];
+    float S[DK];
+    float* Sg = a.S + (size_t)p * dk * dv;
+#pragma unroll
+    for (int k = 0; k < DK; k++) S[k] = Sg[(size_t)k * dv + j];
+    const int keep = a.keep_prev ? *a.keep_prev : 0;
+    for (int i = 0; i < keep; i++) {
+        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
+        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk;
+        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
+    }
+    if (keep > 0) {
+#pragma unroll
+        for (int k = 0; k < DK; k++) Sg[(size_t)k * dv + j] = S[k];
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
+    for (int i = 0; i < a.t; i++) {
+        const float* row = a.conved + (size_t)i * a.conv_dim;
+        for (int k = j; k < dk; k += blockDim.x) {
+            qs[k] = row[kh * dk + k];
+            ks[k] = row[a.kd + kh * dk + k];
+        }
+        __syncthreads();
+        // l2norm(q) on thread 0, l2norm(k) on thread 32 (deltanet.rs:19-27): sum left to right
+        if (j == 0 || j == 32) {
+            float* vec = j == 0 ? qs : ks;
+            float ss = 0.0f;
+            for (int k = 0; k < dk; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+            scal[j == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+        }
+        if (j == (int)blockDim.x - 1) {
+            const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)i * a.n_v + p], a.dt_bias[p])));
+            scal[2] = exp_f32(g);                                        // decay = exp(g)
+            scal[3] = sigmoid_f32(a.beta[(size_t)i * a.n_v + p]);        // beta = sigmoid(b)
+        }
+        __syncthreads();
+        for (int k = j; k < dk; k += blockDim.x) {
+            qs[k] = __fmul_rn(__fmul_rn(qs[k], scal[0]), scale);
+            ks[k] = __fmul_rn(ks[k], scal[1]);
+        }
+        __syncthreads();
+        const float decay = scal[2], beta = scal[3];
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
+        float kv = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+        const float v = row[2 * a.kd + p * dv + j];
+        const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
+        float o = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+        // pending row i of this call
+        if (i < a.max_t) {
+            if (j == 0) a.pend_decay[(size_t)i * a.n_v + p] = decay;
+            for (int k = j; k < dk; k += blockDim.x) a.pend_k[((size_t)i * a.n_v + p) * dk + k] = ks[k];
+            a.pend_delta[((size_t)i * a.n_v + p) * dv + j] = delta;
+        }
+        // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47)
+        outs[j] = o;
+        __syncthreads();
+        const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
+        const float z = a.z[(size_t)i * a.n_v * dv + p * dv + j];
+        a.heads[(size_t)i * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
+        __syncthreads();
+    }
+}
+
+// Per (row i, head): RMSNorm of q (heads 0..nh-1) or k (heads nh..nh+nkv-1) with the 8-lane order, then
+// rotate-half RoPE on the first rope_dim dims (rope.rs:31-45); q written to q_out with its gate copied to
+// gate_out; k and v appended to the cache at position pos0 + i (gqa_attention.rs:343-362).
+__global__ void qk_norm_rope_kernel(const QkArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int i = blockIdx.y, h = blockIdx.x;
+    const int hd = a.head_dim, rd = a.rope_dim, half = rd / 2;
+    const int pos = *a.pos + i;
+    float* xs = sm;
+    float* red = sm + hd;
+    const bool is_q = h < a.n_head;
+    const float* src = is_q ? a.qg + (size_t)i * 2 * a.n_head * hd + (size_t)h * 2 * hd
+                            : a.k + (size_t)i * a.n_kv * hd + (size_t)(h - a.n_head) * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) xs[d] = src[d];
+    __syncthreads();
+    const float inv = inv_rms_of(sum_squares_8lane_block(xs, hd, red), hd, a.eps);
+    const float* nw = is_q ? a.q_norm : a.k_norm;
+    const float* cs = a.cos + (size_t)pos * rd;
+    const float* sn = a.sin + (size_t)pos * rd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) xs[d] = __fmul_rn(__fmul_rn(xs[d], inv), nw[d]);
+    __syncthreads();
+    float* dst;
+    if (is_q) dst = a.q_out + (size_t)i * a.n_head * hd + (size_t)h * hd;
+    else dst = a.k_cache + ((size_t)pos * a.n_kv + (h - a.n_head)) * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float val = xs[d];
+        if (d < half) val = __fsub_rn(__fmul_rn(xs[d], cs[d]), __fmul_rn(xs[d + half], sn[d]));
+        else if (d < rd) val = __fadd_rn(__fmul_rn(xs[d], cs[d]), __fmul_rn(xs[d - half], sn[d]));
+        dst[d] = val;
+    }
+    if (is_q) {
+        for (int d = threadIdx.x; d < hd; d += blockDim.x)
+            a.gate_out[(size_t)i * a.n_head * hd + (size_t)h * hd + d] = src[hd + d];
+    } else {
+        const float* vsrc = a.v + (size_t)i * a.n_kv * hd + (size_t)(h - a.n_head) * hd;
+        float* vdst = a.v_cache + ((size_t)pos * a.n_kv + (h - a.n_head)) * hd;
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) vdst[d] = vsrc[d];
+    }
+}
+
+// One CTA per (row i, head h): scores s[t] = (sum_d q[d] k_t[d]) * scaling over the cache positions
+// 0..pos0+i (sum left to right over d), softmax (max, exp, 8-lane sum, divide), out[d] = sum_t p[t] v_t[d]
+// (left to right over t), times sigmoid(gate) (gqa_attention.rs:376-409).
+__global__ void attention_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const int i = blockIdx.y, h = blockIdx.x;
+    const int hd = a.head_dim, kvh = h / (a.n_head / a.n_kv);
+    const int len = *a.pos + i + 1;
+    float* qs = sm;
+    float* p = sm + hd;           // len scores / probabilities
+    float* red = p + a.max_len;   // 16 floats
+    const float* q = a.q + (size_t)i * a.n_head * hd + (size_t)h * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    __syncthreads();
+    for (int t = threadIdx.x; t < len; t += blockDim.x) {
+        const float* kt = a.k_cache + ((size_t)t * a.n_kv + kvh) * hd;
+        float s = 0.0f;
+        for (int d = 0; d < hd; d++) s = __fadd_rn(s, __fmul_rn(qs[d], kt[d]));
+        p[t] = __fmul_rn(s, a.scaling);
+    }
+    __syncthreads();
+    // softmax (softmax.rs:22-50): m = max; e = exp(x - m); 8-lane sum; divide
+    float m = -INFINITY;
+    for (int t = threadIdx.x; t < len; t += blockDim.x) m = fmaxf(m, p[t]);
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = red[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
+        red[15] = mm;
+    }
+    __syncthreads();
+    m = red[15];
+    __syncthreads();
+    for (int t = threadIdx.x; t < len; t += blockDim.x) p[t] = exp_f32(__fsub_rn(p[t], m));
+    __syncthreads();
+    const int n8 = len / 8 * 8;
+    if (threadIdx.x < 8) {
+        float acc = 0.0f;
+        for (int t = threadIdx.x; t < n8; t += 8) acc = __fadd_rn(acc, p[t]);
+        red[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = reduce8(red);
+        for (int t = n8; t < len; t++) s = __fadd_rn(s, p[t]);
+        red[8] = s;
+    }
+    __syncthreads();
+    const float ssum = red[8];
+    for (int t = threadIdx.x; t < len; t += blockDim.x) p[t] = __fdiv_rn(p[t], ssum);
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f;
+        const float* vcol = a.v_cache + (size_t)kvh * hd + d;
+        const size_t stride = (size_t)a.n_kv * hd;
+        for (int t = 0; t < len; t++) o = __fadd_rn(o, __fmul_rn(p[t], vcol[(size_t)t * stride]));
+        const float g = a.gate[(size_t)i * a.n_head * hd + (size_t)h * hd + d];
+        a.out[(size_t)i * a.n_head * hd + (size_t)h * hd + d] = __fmul_rn(o, sigmoid_f32(g));
+    }
+}
+
+// One CTA per row: out[row] = the first index of the maximum (model.rs:505-513: strict > scan from 0).
+__global__ void argmax_kernel(const float* __restrict__ x, int n, int32_t* __restrict__ out) {
+    const float* r = x + (size_t)blockIdx.x * n;
+    float best = r[0];
+    int bi = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = r[i];
+        if (v > best || (v == best && i < bi)) best = v, bi = i;
+    }
+    // the reference keeps index 0 unless a strictly greater value appears; r[0] seeds every thread
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > best || (ov == best && oi < bi)) best = ov, bi = oi;
+    }
+    __shared__ float bv[32];
+    __shared__ int bx[32];
+    if ((threadIdx.x & 31) == 0) bv[threadIdx.x >> 5] = best, bx[threadIdx.x >> 5] = bi;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (bv[w] > best || (bv[w] == best && bx[w] < bi)) best = bv[w], bi = bx[w];
+        out[blockIdx.x] = bi;
+    }
+}
+
+// ------------------------------------------------------------------------------------------- launchers
+
+cudaError_t launch_resid_norm_quant(const float* a, const float* b, float* h_out, const float* w, float eps, int n, int rows,
+                                    float* y_out, uint8_t* q8k_out, uint8_t* q80_out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const size_t smem = (size_t)(n + 16) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(resid_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    resid_norm_quant_kernel<<<rows, 512, smem, s>>>(a, b, h_out, w, eps, n, y_out, q8k_out, q80_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows(const float* x, int x_ld, const float* w, float eps, int n, int rows, float* y, int y_ld,
+                               cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const size_t smem = (size_t)(n + 16) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    rmsnorm_rows_kernel<<<rows, 512, smem, s>>>(x, x_ld, w, eps, n, y, y_ld);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_quant(const float* g, const float* u, int n, int rows, float* h_out, uint8_t* q8k_out,
+                                uint8_t* q80_out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const size_t smem = (size_t)n * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    swiglu_quant_kernel<<<rows, 512, smem, s>>>(g, u, n, h_out, q8k_out, q80_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_rows(const float* x, int n, int rows, uint8_t* q8k_out, uint8_t* q80_out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const size_t smem = (size_t)n * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(quant_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    quant_rows_kernel<<<rows, 512, smem, s>>>(x, n, q8k_out, q80_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, const float* x, int t, float* out,
+                             float* pend_x, const int* keep_prev, int max_t, cudaStream_t s) {
+    conv_step_kernel<<<(channels + 255) / 256, 256, 0, s>>>(state, w, K, channels, x, t, out, pend_x, keep_prev, max_t);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s) {
+    if (a.dv > 256 || a.dv % 32) return cudaErrorInvalidValue;
+    switch (a.dk) {
+    case 128: deltanet_heads_kernel<128><<<a.n_v, a.dv, 0, s>>>(a); break;
+    case 64: deltanet_heads_kernel<64><<<a.n_v, a.dv, 0, s>>>(a); break;
+    case 8: deltanet_heads_kernel<8><<<a.n_v, a.dv, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
+    const dim3 grid(a.n_head + a.n_kv, t);
+    const size_t smem = (size_t)(a.head_dim + 16) * sizeof(float);
+    qk_norm_rope_kernel<<<grid, 128, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
+    const dim3 grid(a.n_head, t);
+    const size_t smem = (size_t)(a.head_dim + a.max_len + 16) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attention_kernel<<<grid, 256, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    argmax_kernel<<<rows, 1024, 0, s>>>(x, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace qdec

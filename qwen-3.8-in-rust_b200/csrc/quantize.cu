@@ -78,13 +78,15 @@ __global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int row
         const float dd = __fdiv_rn(amax, 127.0f);
         const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
         float qf = roundf(__fmul_rn(v, id));  // round half away from zero, then `as i8` (saturating)
-        int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
-        uint8_t* o = out + b * Q8_0_BLOCK_BYTES;
-        o[2 + lane] = (uint8_t)(int8_t)qi;
+        const int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
+        // the 34-byte block as 17 half-words: lane 0 the f16 scale, lane j (1..16) codes 2j-2 and 2j-1
+        const int lo = __shfl_sync(0xffffffffu, qi, (2 * lane - 2) & 31);
+        const int hi = __shfl_sync(0xffffffffu, qi, (2 * lane - 1) & 31);
+        uint16_t* o = reinterpret_cast<uint16_t*>(out + b * Q8_0_BLOCK_BYTES);
         if (lane == 0) {
-            const uint16_t h = __half_as_ushort(__float2half_rn(dd));
-            o[0] = (uint8_t)(h & 0xff);
-            o[1] = (uint8_t)(h >> 8);
+            o[0] = __half_as_ushort(__float2half_rn(dd));
+        } else if (lane <= 16) {
+            o[lane] = (uint16_t)((lo & 0xff) | ((hi & 0xff) << 8));
         }
     }
 }

@@ -22,6 +22,17 @@ TYPE_NAMES = {F32: "F32", Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K"
 LAYOUT = {F32: (1, 4), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 
 
+class Opts(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("max_pos", ctypes.c_int)]
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in ("n_layer", "hidden", "ffn", "vocab", "n_head", "n_head_kv", "head_dim",
+                                               "dn_n_k_heads", "dn_n_v_heads", "dn_head_dim_k", "dn_head_dim_v",
+                                               "n_full_attention", "has_mtp")] + [
+        ("weight_bytes", ctypes.c_uint64), ("decode_bytes", ctypes.c_uint64), ("load_secs", ctypes.c_double)]
+
+
 class QdecError(RuntimeError):
     def __init__(self, code, msg):
         super().__init__(f"qdec error {code}: {msg}")
@@ -52,6 +63,31 @@ def lib():
             fn.argtypes = args
         L.qdec_act_row_bytes.restype = S
         L.qdec_act_row_bytes.argtypes = [I, I]
+        PP = ctypes.POINTER(ctypes.c_void_p)
+        U32P = ctypes.POINTER(ctypes.c_uint32)
+        for name, args in {
+            "qdec_open": [ctypes.c_char_p, ctypes.POINTER(Opts), PP],
+            "qdec_close": [P],
+            "qdec_model_get_info": [P, ctypes.POINTER(ModelInfo)],
+            "qdec_is_stop": [P, ctypes.c_uint32],
+            "qdec_state_new": [P, I, I, I, PP],
+            "qdec_state_free": [P],
+            "qdec_state_pos": [P],
+            "qdec_prefill": [P, U32P, I, U32P],
+            "qdec_step": [P, ctypes.c_uint32, U32P, P],
+            "qdec_spec_prefill": [P, U32P, I, U32P],
+            "qdec_spec_round": [P, ctypes.c_uint32, U32P, ctypes.POINTER(I)],
+            "qdec_set_drafts": [P, U32P, I],
+            "qdec_get_drafts": [P, U32P, I],
+            "qdec_spec_counters": [P, ctypes.POINTER(ctypes.c_uint64)],
+            "qdec_set_capture": [P, I],
+            "qdec_debug_hidden": [P, I, I, P],
+            "qdec_debug_logits": [P, I, P],
+            "qdec_synth_gguf": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, I],
+        }.items():
+            fn = getattr(L, name)
+            fn.restype = I
+            fn.argtypes = args
         _lib = L
     return _lib
 
@@ -97,3 +133,144 @@ def matvec(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream=0):
 def dequant_rows(t, w_ptr, rows, cols, ids_ptr, nids, out_ptr, stream=0):
     """Model::embed_token_into (crates/core/src/model.rs:364) for n device-resident ids."""
     _check(lib().qdec_dequant_rows(t, w_ptr, rows, cols, ids_ptr, nids, out_ptr, stream))
+
+
+def _u32(seq):
+    arr = (ctypes.c_uint32 * len(seq))(*[int(v) for v in seq])
+    return arr
+
+
+def synth_gguf(path, preset, seed, threads=0):
+    """Write a synthetic checkpoint ("tiny", "27b", "27b-L<n>"); the stand-in for the real GGUF."""
+    _check(lib().qdec_synth_gguf(str(path).encode(), preset.encode(), seed, threads))
+
+
+class Model:
+    """Model::load_with (crates/core/src/model.rs:184): the GGUF's weights resident on `device`."""
+
+    def __init__(self, path, device=0, max_pos=4096):
+        self._h = ctypes.c_void_p()
+        o = Opts(device, max_pos)
+        _check(lib().qdec_open(str(path).encode(), ctypes.byref(o), ctypes.byref(self._h)))
+        info = ModelInfo()
+        _check(lib().qdec_model_get_info(self._h, ctypes.byref(info)))
+        self.info = info
+        self.max_pos = max_pos
+
+    def close(self):
+        if self._h:
+            lib().qdec_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def is_stop(self, tok):
+        return bool(lib().qdec_is_stop(self._h, tok))
+
+    def new_state(self, spec_k=0, max_pos=None, max_rows=32):
+        """Model::new_state / new_state_spec (model.rs:334, spec.rs:184)."""
+        return State(self, spec_k, max_pos or self.max_pos, max_rows)
+
+
+class State:
+    def __init__(self, model, spec_k, max_pos, max_rows):
+        self.model = model
+        self.k = spec_k
+        self._h = ctypes.c_void_p()
+        _check(lib().qdec_state_new(model._h, spec_k, max_pos, max_rows, ctypes.byref(self._h)))
+
+    def free(self):
+        if self._h:
+            lib().qdec_state_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    @property
+    def pos(self):
+        return lib().qdec_state_pos(self._h)
+
+    def prefill(self, ids):
+        out = ctypes.c_uint32()
+        _check(lib().qdec_prefill(self._h, _u32(ids), len(ids), ctypes.byref(out)))
+        return out.value
+
+    def step(self, tok, want_logits=False):
+        out = ctypes.c_uint32()
+        if want_logits:
+            import numpy as np
+
+            lg = np.empty(self.model.info.vocab, np.float32)
+            _check(lib().qdec_step(self._h, tok, ctypes.byref(out), lg.ctypes.data_as(ctypes.c_void_p)))
+            return out.value, lg
+        _check(lib().qdec_step(self._h, tok, ctypes.byref(out), None))
+        return out.value
+
+    def spec_prefill(self, ids):
+        out = ctypes.c_uint32()
+        _check(lib().qdec_spec_prefill(self._h, _u32(ids), len(ids), ctypes.byref(out)))
+        return out.value
+
+    def spec_round(self, x_p):
+        buf = (ctypes.c_uint32 * (self.k + 1))()
+        n = ctypes.c_int()
+        _check(lib().qdec_spec_round(self._h, x_p, buf, ctypes.byref(n)))
+        return list(buf[: n.value])
+
+    def set_drafts(self, drafts):
+        _check(lib().qdec_set_drafts(self._h, _u32(drafts), len(drafts)))
+
+    def drafts(self):
+        buf = (ctypes.c_uint32 * self.k)()
+        _check(lib().qdec_get_drafts(self._h, buf, self.k))
+        return list(buf)
+
+    def counters(self):
+        buf = (ctypes.c_uint64 * 4)()
+        _check(lib().qdec_spec_counters(self._h, buf))
+        return dict(zip(("rounds", "drafted", "accepted", "emitted"), list(buf)))
+
+    def set_capture(self, on=True):
+        _check(lib().qdec_set_capture(self._h, 1 if on else 0))
+
+    def hidden(self, layer, row=0):
+        import numpy as np
+
+        out = np.empty(self.model.info.hidden, np.float32)
+        _check(lib().qdec_debug_hidden(self._h, layer, row, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def logits(self, row=0):
+        import numpy as np
+
+        out = np.empty(self.model.info.vocab, np.float32)
+        _check(lib().qdec_debug_logits(self._h, row, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+
+def generate(state, prompt, n_tokens, stop=True):
+    """The reference's plain greedy loop (crates/cli/src/run.rs:329-350): prefill, then one token per step."""
+    out = [state.prefill(prompt)]
+    while len(out) < n_tokens and not (stop and state.model.is_stop(out[-1])):
+        out.append(state.step(out[-1]))
+    return out
+
+
+def generate_spec(state, prompt, n_tokens, stop=True):
+    """The reference's --spec loop (crates/cli/src/run.rs:353-383): spec_prefill, then rounds."""
+    out = [state.spec_prefill(prompt)]
+    while len(out) < n_tokens and not (stop and state.model.is_stop(out[-1])):
+        em = state.spec_round(out[-1])
+        for t in em:
+            out.append(t)
+            if len(out) >= n_tokens or (stop and state.model.is_stop(t)):
+                break
+    return out[:n_tokens]

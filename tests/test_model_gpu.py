@@ -1,0 +1,147 @@
+"""GPU parity of the whole decode path (the tiny synthetic Qwen3.8-style checkpoint) against
+the CPU oracle: greedy ids, per-layer hidden states and logits, the --spec 3 loop (ids identical to plain decoding
+and to the oracle, MTP drafts identical), and forced drafts that exercise every acceptance count
+(the device of crates/core/tests/spec_identity.rs)."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+SEED = 20261201
+N_TOKENS = 32
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import qdec
+
+    path = tmp_path_factory.mktemp("tiny") / "tiny.gguf"
+    qdec.synth_gguf(path, "tiny", SEED)
+    return path
+
+
+@pytest.fixture(scope="module")
+def model(tiny):
+    import qdec
+
+    return qdec.Model(tiny, max_pos=512)
+
+
+@pytest.fixture(scope="module")
+def omodel(tiny, orc):
+    return orc.OracleModel(tiny)
+
+
+def prompt16():
+    return [int(v) for v in np.random.default_rng(SEED + 1).integers(0, 4096, 16)]
+
+
+def test_config_from_synthetic_gguf(model):
+    i = model.info
+    assert (i.n_layer, i.hidden, i.ffn, i.vocab, i.n_head, i.n_head_kv, i.head_dim) == (4, 256, 768, 4096, 4, 2, 64)
+    assert (i.dn_n_k_heads, i.dn_n_v_heads, i.dn_head_dim_k, i.dn_head_dim_v, i.n_full_attention, i.has_mtp) == (2, 4, 64, 64, 1, 1)
+
+
+def test_greedy_ids_match_oracle(model, omodel):
+    import qdec
+
+    p = prompt16()
+    want = omodel.state(512).generate(p, N_TOKENS, stop=False)
+    got = qdec.generate(model.new_state(), p, N_TOKENS, stop=False)
+    assert got == want
+
+
+def test_hidden_states_and_logits_bit_exact(model, omodel):
+    """Every layer's residual row and the logits of every prompt position, bit for bit."""
+    p = prompt16()
+    st = model.new_state(max_rows=1)
+    st.set_capture(True)
+    os_ = omodel.state(512)
+    for tok in p[:6]:
+        st.step(tok)
+        lg, cap = os_.forward_token(tok, capture=True)
+        for layer in range(model.info.n_layer + 1):
+            h = st.hidden(layer)
+            assert np.array_equal(h.view(np.uint32), cap[layer].view(np.uint32)), f"layer {layer} at position {os_.pos - 1}"
+        assert np.array_equal(st.logits(0).view(np.uint32), lg.view(np.uint32))
+
+
+def test_batched_prefill_equals_token_steps(model):
+    """Row i of a batched forward == forward_token on row i (crates/core/tests/matmul_t.rs, spec.md:31-34)."""
+    p = prompt16()
+    a = model.new_state(max_rows=32)
+    b = model.new_state(max_rows=1)
+    first_a = a.prefill(p)
+    first_b = None
+    for tok in p:
+        first_b = b.step(tok)
+    assert first_a == first_b
+    ga = [first_a] + [a.step(0) for _ in range(3)]
+    gb = [first_b] + [b.step(0) for _ in range(3)]
+    assert ga == gb
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4])
+def test_spec_ids_equal_plain_and_oracle(model, omodel, k):
+    import qdec
+
+    p = prompt16()
+    plain = qdec.generate(model.new_state(), p, N_TOKENS, stop=False)
+    st = model.new_state(spec_k=k)
+    got = qdec.generate_spec(st, p, N_TOKENS, stop=False)
+    assert got == plain
+    want, stats, _ = omodel.state(512).spec_generate(p, N_TOKENS, k, stop=False)
+    assert want == plain
+    c = st.counters()
+    assert c["rounds"] == stats["rounds"] and c["accepted"] == stats["accepted"]
+
+
+def test_mtp_drafts_match_oracle(model, omodel):
+    """The drafts the MTP head proposes each round, compared with the oracle's."""
+    k = 3
+    p = prompt16()
+    st = model.new_state(spec_k=k)
+    x = st.spec_prefill(p)
+    drafts = [st.drafts()]
+    seq = [x]
+    for _ in range(6):
+        em = st.spec_round(seq[-1])
+        seq += em
+        drafts.append(st.drafts())
+    _, stats, odrafts = omodel.state(512).spec_generate(p, len(seq), k, stop=False)
+    assert drafts[: len(odrafts)] == odrafts[: len(drafts)]
+
+
+def test_forced_drafts_every_acceptance_count(model, omodel):
+    """Drafts forced to the plain run's own next tokens with a deliberate miss at position j accept exactly j
+    drafts; ids stay identical to plain decoding and to the oracle under the same forced drafts."""
+    import qdec
+
+    k = 3
+    p = prompt16()
+    plain = qdec.generate(model.new_state(), p, N_TOKENS + 8, stop=False)
+    st = model.new_state(spec_k=k)
+    seq = [st.spec_prefill(p)]
+    forced = []
+    hist = [0] * (k + 1)
+    r = 0
+    while len(seq) < N_TOKENS:
+        pos = len(seq)  # the next plain token index the verify's row 0 predicts
+        want = plain[pos:pos + k]
+        miss = r % (k + 1)  # accept exactly `miss` drafts (k = all)
+        d = list(want)
+        if miss < k:
+            d[miss] = (d[miss] + 1) % 4096
+        forced.append(d)
+        st.set_drafts(d)
+        em = st.spec_round(seq[-1])
+        hist[len(em) - 1] += 1
+        seq += em
+        r += 1
+    assert seq[:N_TOKENS] == plain[:N_TOKENS]
+    assert all(h > 0 for h in hist), hist
+    want, stats, _ = omodel.state(512).spec_generate(p, len(seq), k, stop=False, forced=forced)
+    assert want[: len(seq)] == seq
