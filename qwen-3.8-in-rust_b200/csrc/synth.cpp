@@ -36,12 +36,25 @@ inline uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
 
 struct Rng {
     uint64_t s;
+    float spare = 0.f;
+    bool has_spare = false;
     explicit Rng(uint64_t seed, uint64_t a, uint64_t b) : s(mix64(seed ^ mix64(a * 0x100000001B3ull ^ mix64(b)))) {}
     uint64_t next() { return s = mix64(s); }
     double uniform() { return ((next() >> 11) + 0.5) * (1.0 / 9007199254740992.0); }  // (0, 1)
-    float normal() {  // Box-Muller, one value per call
-        const double u1 = uniform(), u2 = uniform();
-        return (float)(std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+    float normal() {  // Box-Muller in f32, two values per pair of uniforms
+        if (has_spare) {
+            has_spare = false;
+            return spare;
+        }
+        const uint64_t r = next();
+        const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = (float)((r >> 16) & 0xffffff) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1));
+        float sn, cs;
+        sincosf(6.2831853f * u2, &sn, &cs);
+        spare = rad * sn;
+        has_spare = true;
+        return rad * cs;
     }
 };
 
@@ -86,6 +99,7 @@ inline float f16_to_f32(uint16_t h) {
 }
 inline void put16(uint8_t *p, uint16_t v) { p[0] = v & 0xff; p[1] = v >> 8; }
 inline int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+inline long lroundf_fast(float v) { return (long)(v + (v >= 0.f ? 0.5f : -0.5f)); }
 
 // ------------------------------------------------------------------------------- block encoders
 
@@ -104,8 +118,8 @@ void enc_q4k_q5k(const float *x, uint8_t *b, bool q5) {
     const float d = f16_to_f32(dh), dmin = f16_to_f32(mh);
     int ls[8], lm[8];
     for (int s = 0; s < 8; s++) {
-        ls[s] = d > 0 ? clampi((int)std::lround(scale[s] / d), 0, 63) : 0;
-        lm[s] = dmin > 0 ? clampi((int)std::lround(mins[s] / dmin), 0, 63) : 0;
+        ls[s] = d > 0 ? clampi((int)lroundf_fast(scale[s] / d), 0, 63) : 0;
+        lm[s] = dmin > 0 ? clampi((int)lroundf_fast(mins[s] / dmin), 0, 63) : 0;
     }
     memset(b, 0, q5 ? 176 : 144);
     put16(b, dh);
@@ -124,7 +138,7 @@ void enc_q4k_q5k(const float *x, uint8_t *b, bool q5) {
     for (int s = 0; s < 8; s++) {
         const float ds = d * ls[s], off = dmin * lm[s];
         for (int j = 0; j < 32; j++) {
-            const int v = ds > 0 ? clampi((int)std::lround((x[s * 32 + j] + off) / ds), 0, levels) : 0;
+            const int v = ds > 0 ? clampi((int)lroundf_fast((x[s * 32 + j] + off) / ds), 0, levels) : 0;
             if (!q5) {
                 b[16 + (s / 2) * 32 + j] |= (uint8_t)((v & 0xF) << ((s & 1) * 4));
             } else {
@@ -147,11 +161,11 @@ void enc_q6k(const float *x, uint8_t *b) {
     const float d = f16_to_f32(dh);
     memset(b, 0, 210);
     int8_t isc[16];
-    for (int g = 0; g < 16; g++) isc[g] = (int8_t)(d > 0 ? clampi((int)std::lround(sc[g] / d), -128, 127) : 0);
+    for (int g = 0; g < 16; g++) isc[g] = (int8_t)(d > 0 ? clampi((int)lroundf_fast(sc[g] / d), -128, 127) : 0);
     for (int e = 0; e < 256; e++) {
         const int g = e / 16;
         const float ds = d * isc[g];
-        const int v = ds != 0 ? clampi((int)std::lround(x[e] / ds) + 32, 0, 63) : 32;
+        const int v = ds != 0 ? clampi((int)lroundf_fast(x[e] / ds) + 32, 0, 63) : 32;
         const int h = e / 128, r = e % 128, k = r / 32, l = r % 32;
         b[h * 64 + l + 32 * (k & 1)] |= (uint8_t)((v & 0xF) << (4 * (k >> 1)));
         b[128 + h * 32 + l] |= (uint8_t)(((v >> 4) & 3) << (2 * k));
@@ -165,7 +179,7 @@ void enc_q8_0(const float *x, uint8_t *b) {
     for (int j = 0; j < 32; j++) amax = std::max(amax, std::fabs(x[j]));
     const float d = amax / 127.f, id = d != 0 ? 1.f / d : 0.f;
     put16(b, f16_rn(d));
-    for (int j = 0; j < 32; j++) b[2 + j] = (uint8_t)(int8_t)clampi((int)std::lround(x[j] * id), -128, 127);
+    for (int j = 0; j < 32; j++) b[2 + j] = (uint8_t)(int8_t)clampi((int)lroundf_fast(x[j] * id), -128, 127);
 }
 
 void enc_q4_0(const float *x, uint8_t *b) {
