@@ -70,6 +70,17 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
 int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev,
                 void *stream);
 
+/* qdec_matvec for callers that cannot let a library allocate device memory: an application whose device memory
+ * belongs to another allocator, or a decode loop that must stay allocation-free while it runs.  Same arguments,
+ * same results as qdec_matvec, but the quantised columns live in a fixed array inside the library
+ * (qdec_matvec_noalloc_max_bytes() bytes, held on every device that loads the library until exit); sizes that
+ * do not fit are rejected with QDEC_EINVAL.  The first call on a device looks the array's address up, so make it
+ * before any stream capture.  All calls on a device share the array: calls that overlap on the GPU race.
+ * This entry point has no counterpart in the reference, whose CPU matvec quantises into caller-owned rows. */
+int qdec_matvec_noalloc(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols,
+                        float *y_dev, void *stream);
+size_t qdec_matvec_noalloc_max_bytes(void);
+
 /* out[i * cols + e] = dequantised element e of row ids[i] of `w_dev` (ids on the device, n_ids of them):
  * the embedding gather.  Replaces Model::embed_token_into (crates/core/src/model.rs:364-368) and
  * dequantize_into (crates/core/src/quant.rs:229). */

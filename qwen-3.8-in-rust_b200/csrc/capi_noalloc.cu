@@ -1,0 +1,85 @@
+// qdec_matvec_noalloc: qdec_matvec for callers that cannot allocate device memory.
+//
+// qdec_matvec quantises its f32 input columns into a device buffer that the library allocates (and grows) on
+// demand.  Some callers cannot let a library call cudaMalloc: an application whose device memory is owned by
+// another allocator (a framework's caching allocator that has reserved the GPU), or a decode loop that must
+// stay allocation-free once it is running (the rule the reference enforces for its own decode step).  This
+// entry point keeps the quantised columns in a fixed array in the library's own device memory instead, so it
+// allocates nothing.
+//
+// The array is a file-scope __device__ object of NOALLOC_SCRATCH_BYTES; every GPU that loads the library holds
+// one copy until the process exits.  Host code cannot use the array's name as a device address, so the first
+// call on each device looks the address up with cudaGetSymbolAddress (with that device current) and caches it;
+// make that first call before any stream capture.  All calls on a device share the one array and it keeps the
+// last call's contents: two calls whose kernels overlap on the GPU (different streams, or host threads) race on
+// it.  Nothing in it has to start at zero: every call overwrites the bytes it reads.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/qdec.h"
+#include "capi_util.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace qdec {
+
+namespace {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = 256 * 1024;
+__device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+std::mutex g_mu;
+void* g_addr[MAX_DEVICES] = {nullptr};
+
+// The device address of g_noalloc_scratch on the current device (looked up once per device).
+int scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= MAX_DEVICES) return fail(QDEC_EINVAL, "qdec_matvec_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec_noalloc: cudaGetSymbolAddress");
+        g_addr[dev] = p;
+    }
+    *out = g_addr[dev];
+    return QDEC_OK;
+}
+
+}  // namespace
+}  // namespace qdec
+
+using namespace qdec;
+
+extern "C" size_t qdec_matvec_noalloc_max_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int qdec_matvec_noalloc(int ggml_type, const void* w_dev, int rows, int cols, const float* x_dev, int n_cols,
+                                   float* y_dev, void* stream) {
+    int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
+    if (rc) return rc;
+    if (!w_dev || !x_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_matvec_noalloc: null pointer");
+    if (n_cols == 0) return QDEC_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (ggml_type == T_F32) {  // F32 weights take the f32 columns as they are: no scratch
+        cudaError_t e = launch_gemv(ggml_type, (const uint8_t*)w_dev, rows, cols, x_dev, n_cols, y_dev, s);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec_noalloc");
+    }
+    const size_t need = act_row_bytes(ggml_type, cols) * (size_t)n_cols;
+    if (need > NOALLOC_SCRATCH_BYTES)
+        return fail(QDEC_EINVAL,
+                    "qdec_matvec_noalloc: %d columns of %d values need %zu bytes of quantised activations; the fixed "
+                    "scratch holds %zu (use qdec_matvec, or fewer columns per call)",
+                    n_cols, cols, need, NOALLOC_SCRATCH_BYTES);
+    void* act = nullptr;
+    rc = scratch_address(&act);
+    if (rc) return rc;
+    cudaError_t e = is_kquant(ggml_type) ? launch_quantize_q8k(x_dev, cols, n_cols, (uint8_t*)act, s)
+                                         : launch_quantize_q8_0(x_dev, cols, n_cols, (uint8_t*)act, s);
+    if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec_noalloc: quantise");
+    e = launch_gemv(ggml_type, (const uint8_t*)w_dev, rows, cols, act, n_cols, y_dev, s);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec_noalloc: gemv");
+}

@@ -56,6 +56,7 @@ def lib():
             "qdec_quantize_q8_0": [P, I, I, P, P],
             "qdec_gemv": [I, P, I, I, P, I, P, P],
             "qdec_matvec": [I, P, I, I, P, I, P, P],
+            "qdec_matvec_noalloc": [I, P, I, I, P, I, P, P],
             "qdec_dequant_rows": [I, P, I, I, P, I, P, P],
         }.items():
             fn = getattr(L, name)
@@ -63,6 +64,8 @@ def lib():
             fn.argtypes = args
         L.qdec_act_row_bytes.restype = S
         L.qdec_act_row_bytes.argtypes = [I, I]
+        L.qdec_matvec_noalloc_max_bytes.restype = S
+        L.qdec_matvec_noalloc_max_bytes.argtypes = []
         PP = ctypes.POINTER(ctypes.c_void_p)
         U32P = ctypes.POINTER(ctypes.c_uint32)
         for name, args in {
@@ -128,6 +131,16 @@ def gemv(t, w_ptr, rows, cols, act_ptr, ncols, y_ptr, stream=0):
 def matvec(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream=0):
     """matvec_f32_in / matmul (crates/core/src/kernels/matvec.rs:541, :369) from f32 activation rows."""
     _check(lib().qdec_matvec(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream))
+
+
+def matvec_noalloc(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream=0):
+    """As `matvec`, allocating nothing: the quantised columns use a fixed array inside the library (for callers
+    that cannot let a library allocate device memory)."""
+    _check(lib().qdec_matvec_noalloc(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream))
+
+
+def matvec_noalloc_max_bytes():
+    return lib().qdec_matvec_noalloc_max_bytes()
 
 
 def dequant_rows(t, w_ptr, rows, cols, ids_ptr, nids, out_ptr, stream=0):
