@@ -358,14 +358,162 @@ def run_qdec(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------------
+# The --spec 3 decode workload: the full 27B architecture, synthetic Q4_K_M weights.
+
+SPEC_K = 3
+PROMPT_LEN = 128
+SPEC_SEED = 20261201
+
+
+def checkpoint_path(preset, seed):
+    d = os.environ.get("QDEC_BENCH_DIR") or ("/dev/shm" if os.path.isdir("/dev/shm") else "/tmp")
+    return os.path.join(d, f"qdec_{preset}_{seed}.gguf")
+
+
+def ensure_checkpoint(preset, seed):
+    import qdec
+
+    path = checkpoint_path(preset, seed)
+    if not os.path.exists(path):
+        tmp = path + f".part{os.getpid()}"
+        qdec.synth_gguf(tmp, preset, seed)
+        os.replace(tmp, path)
+    return path
+
+
+def spec_prompt(vocab, seed):
+    return [int(v) for v in np.random.default_rng(seed).integers(0, min(vocab, 248044), PROMPT_LEN)]
+
+
+def run_spec_qdec(args, world, rank, local):
+    import torch
+
+    import qdec
+
+    torch.cuda.set_device(local)
+    preset = args.preset
+    if rank == 0:
+        path = ensure_checkpoint(preset, SPEC_SEED)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    path = checkpoint_path(preset, SPEC_SEED)
+    k = SPEC_K
+    max_pos = PROMPT_LEN + (args.warmup + args.steps) * (k + 1) * 2 + 64
+    model = qdec.Model(path, device=local, max_pos=max_pos)
+    info = model.info
+    prompt = spec_prompt(info.vocab, SPEC_SEED + 1 + rank)
+    st = model.new_state(spec_k=k, max_rows=32)
+    stream = torch.cuda.ExternalStream(st.stream)
+    x = st.spec_prefill(prompt)
+    for _ in range(args.warmup):
+        x = st.spec_round(x)[-1]
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    torch.cuda.synchronize()
+    barrier()
+    c0 = st.counters()
+    l0 = st.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    emitted = 0
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            em = st.spec_round(x)
+            emitted += len(em)
+            x = em[-1]
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    c1 = st.counters()
+    launches = st.launches - l0
+    # forced drafts (drafts = the plain run's own next tokens, every draft accepted): the m = k regime
+    plain = model.new_state(spec_k=0, max_rows=32)
+    n_forced = min(args.steps, 64)
+    seq = qdec.generate(plain, prompt, 1 + n_forced * (k + 1) + k, stop=False)
+    plain.free()
+    fs = model.new_state(spec_k=k, max_rows=32)
+    fx = fs.spec_prefill(prompt)
+    fstream = torch.cuda.ExternalStream(fs.stream)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pos = 1
+    f0.record(fstream)
+    forced_tokens = 0
+    for _ in range(n_forced):
+        fs.set_drafts(seq[pos:pos + k])
+        em = fs.spec_round(fx)
+        forced_tokens += len(em)
+        pos += len(em)
+        fx = em[-1]
+    f1.record(fstream)
+    torch.cuda.synchronize()
+    forced_ms = f0.elapsed_time(f1)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, wall * 1e3, forced_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, wall_ms, forced_ms = t.tolist()
+        wall = wall_ms / 1e3
+        tt = torch.tensor([emitted, forced_tokens], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt)
+        emitted_all, forced_all = tt.tolist()
+    else:
+        emitted_all, forced_all = emitted, forced_tokens
+    if rank != 0:
+        return
+    rounds = args.steps
+    s_round = ms / 1e3 / rounds
+    peak, peak_kind = peaks()
+    verify_bytes = info.decode_bytes
+    round_bytes = verify_bytes + k * (info.mtp_bytes + info.lm_head_bytes)
+    line = {
+        "metric": "decode tok/s (greedy, --spec 3) Qwen3.8-27B Q4_K_M", "value": round(emitted_all / (ms / 1e3), 3),
+        "unit": "tok/s", "n_gpus": world, "steps": rounds, "warmup": args.warmup, "ms_per_step": round(ms / rounds, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "Q4_K_M weights x Q8_K activations, f32",
+        "data": "synthetic (seeded N(0,0.02) weights in the Q4_K_M recipe; seeded uniform prompt ids)",
+        "config": {"workload": f"{preset} --spec 3 (BASELINE config 4)", "prompt": PROMPT_LEN, "k": k,
+                   "global_batch": world, "parallelism": f"replicas x{world}",
+                   "l2": f"weights {info.weight_bytes / 1e9:.1f} GB >> 126 MB L2"},
+        "spec": {"s_per_round": round(s_round, 6), "accepted_per_round": (c1["accepted"] - c0["accepted"]) / rounds,
+                 "emitted_per_round": (c1["emitted"] - c0["emitted"]) / rounds,
+                 "forced_drafts_tok_s": round(forced_all / (forced_ms / 1e3), 3),
+                 "forced_s_per_round": round(forced_ms / 1e3 / n_forced, 6)},
+        "e2e": {"value": round(emitted_all / wall, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * (k + 1) + 4 * (k + 1) * 2,
+                "d2h_bytes_per_step": 4 * (k + 1) + 4 * k},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "the whole --spec 3 round", "achieved": round(round_bytes / s_round / 1e9, 1),
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(round_bytes / s_round / 1e9 / peak, 4),
+                     "traffic": None, "alg_bytes_per_round": round_bytes,
+                     "north_star_frac": round(17.8e9 / s_round / 1e9 / peak, 4)},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["qdec", "reference"], default="qdec")
+    ap.add_argument("--workload", choices=["gemv", "spec"], default="gemv")
+    ap.add_argument("--preset", default="27b", help="synthetic checkpoint of the spec workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 2000 if args.workload == "gemv" else 50
+    if args.warmup is None:
+        args.warmup = 20 if args.workload == "gemv" else 5
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -373,7 +521,10 @@ def main():
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
     world, rank, local = dist_setup("nccl")
-    run_qdec(args, world, rank, local)
+    if args.workload == "spec":
+        run_spec_qdec(args, world, rank, local)
+    else:
+        run_qdec(args, world, rank, local)
     if world > 1:
         import torch.distributed as dist
 

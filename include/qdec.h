@@ -34,6 +34,9 @@ extern "C" {
 #define QDEC_TYPE_Q4_K 12
 #define QDEC_TYPE_Q5_K 13
 #define QDEC_TYPE_Q6_K 14
+/* Q6_K in the engine's split device layout: the tensor's 208-byte blocks [ql | qh | scales], then every block's
+ * f16 d -- the same bytes as ggml's 210-byte blocks, 16-byte aligned for bulk copies (qdec_repack_q6k). */
+#define QDEC_TYPE_Q6_K_SPLIT 114
 
 /* Library version string, e.g. "qdec 0.1.0 sm_100a". */
 const char *qdec_version(void);
@@ -70,6 +73,14 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
 int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev,
                 void *stream);
 
+/* Tuning knob of the K-quant GEMV: lanes that share one weight row (1, 2, 4 or 8; 0 = chosen from the row
+ * count, the default).  Results do not depend on it; it exists for tests and sweeps. */
+int qdec_tune_gemv_lanes_per_row(int lpr);
+
+/* Repack rows x cols of ggml Q6_K (src) into the split layout (dst, the same number of bytes, a distinct
+ * buffer) that qdec_gemv reads as QDEC_TYPE_Q6_K_SPLIT.  No counterpart in the reference (a device layout). */
+int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void *stream);
+
 /* qdec_matvec for callers that cannot let a library allocate device memory: an application whose device memory
  * belongs to another allocator, or a decode loop that must stay allocation-free while it runs.  Same arguments,
  * same results as qdec_matvec, but the quantised columns live in a fixed array inside the library
@@ -103,6 +114,8 @@ typedef struct qdec_model_info {
         dn_head_dim_v, n_full_attention, has_mtp;
     uint64_t weight_bytes;  /* bytes resident on the device */
     uint64_t decode_bytes;  /* weight bytes one plain token streams (layers + lm_head + norms + one embedding row) */
+    uint64_t lm_head_bytes; /* output.weight */
+    uint64_t mtp_bytes;     /* the MTP block's weights (blk.{n_layer}) */
     double load_secs;
 } qdec_model_info;
 
@@ -143,6 +156,10 @@ int qdec_spec_round(qdec_state *s, uint32_t x_p, uint32_t *emitted_out, int *n_e
  * (Model::spec_set_drafts, crates/core/src/spec.rs:439); qdec_get_drafts reads the current ones. */
 int qdec_set_drafts(qdec_state *s, const uint32_t *drafts, int k);
 int qdec_get_drafts(const qdec_state *s, uint32_t *drafts_out, int k);
+/* The CUDA stream every kernel of this state runs on (to time it with events), and the number of kernels the
+ * state has launched so far (for launch accounting); no counterpart in the reference (CPU-only). */
+void *qdec_state_stream(const qdec_state *s);
+uint64_t qdec_state_launches(const qdec_state *s);
 /* Speculative counters: rounds, drafted, accepted, emitted (spec.rs:21-42 SpecStats). */
 int qdec_spec_counters(const qdec_state *s, uint64_t out4[4]);
 

@@ -32,7 +32,7 @@ int cuda_fail(cudaError_t e, const char *what) {
 void clear_error() { g_last_error.clear(); }
 
 bool supported_type(int t) {
-    return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K;
+    return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT;
 }
 
 // Shape checks of the reference's assert!s (matvec.rs:73-77, :300, :338; kdot.rs:179-191).
@@ -135,9 +135,23 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
     return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec: gemv");
 }
 
+int qdec_tune_gemv_lanes_per_row(int lpr) {
+    if (lpr != 0 && lpr != 1 && lpr != 2 && lpr != 4 && lpr != 8) return fail(QDEC_EINVAL, "lanes per row must be 0, 1, 2, 4 or 8");
+    set_gemv_lanes_per_row(lpr);
+    return QDEC_OK;
+}
+
+int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void *stream) {
+    if (!src_dev || !dst_dev || rows < 0 || cols <= 0 || cols % 256)
+        return fail(QDEC_EINVAL, "qdec_repack_q6k: bad argument (cols %d must be a multiple of 256)", cols);
+    if (src_dev == dst_dev) return fail(QDEC_EINVAL, "qdec_repack_q6k: source and destination must differ");
+    cudaError_t e = launch_repack_q6k((const uint8_t *)src_dev, (size_t)rows * (cols / 256), (uint8_t *)dst_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_repack_q6k");
+}
+
 int qdec_dequant_rows(int ggml_type, const void *w_dev, int rows, int cols, const int32_t *ids_dev, int n_ids,
                       float *out_dev, void *stream) {
-    if (!supported_type(ggml_type) || cols <= 0 || cols % block_elems(ggml_type) || rows < 0 || n_ids < 0)
+    if (!supported_type(ggml_type) || ggml_type == T_Q6_K_SPLIT || cols <= 0 || cols % block_elems(ggml_type) || rows < 0 || n_ids < 0)
         return fail(QDEC_EINVAL, "qdec_dequant_rows: bad type %d or shape %d x %d", ggml_type, rows, cols);
     if (!w_dev || (!ids_dev && n_ids) || (!out_dev && n_ids)) return fail(QDEC_EINVAL, "qdec_dequant_rows: null pointer");
     const size_t rb = (size_t)(cols / block_elems(ggml_type)) * block_bytes(ggml_type);

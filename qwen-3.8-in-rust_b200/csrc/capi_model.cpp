@@ -87,6 +87,8 @@ int qdec_model_get_info(const qdec_model* m, qdec_model_info* info) {
     info->has_mtp = m->m->has_mtp;
     info->weight_bytes = m->m->weight_bytes;
     info->decode_bytes = m->m->decode_bytes;
+    info->lm_head_bytes = m->m->lm_head.bytes;
+    info->mtp_bytes = m->m->mtp_bytes;
     info->load_secs = m->m->load_secs;
     return QDEC_OK;
 }
@@ -168,6 +170,10 @@ int qdec_spec_counters(const qdec_state* s, uint64_t out4[4]) {
     out4[3] = c.emitted;
     return QDEC_OK;
 }
+
+void* qdec_state_stream(const qdec_state* s) { return s ? (void*)s->s->stream : nullptr; }
+
+uint64_t qdec_state_launches(const qdec_state* s) { return s ? s->s->launches() : 0; }
 
 int qdec_set_capture(qdec_state* s, int on) {
     if (!s) return qdec::fail(QDEC_EINVAL, "qdec_set_capture: null state");

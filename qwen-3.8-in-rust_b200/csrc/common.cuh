@@ -12,6 +12,8 @@ namespace qdec {
 
 // ggml tensor type ids (GGUF), the same numbering as crates/core/src/gguf.rs GgmlType.
 enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+// Q6_K in the engine's split layout: 208-byte blocks [ql | qh | scales], then every block's f16 d (gemv_tma.cu).
+constexpr int T_Q6_K_SPLIT = 114;
 
 constexpr int QK_K = 256;
 constexpr int Q8K_BLOCK_BYTES = 292;  // f32 d, 256 x i8, 16 x i16 (ggml block_q8_K)
@@ -28,10 +30,11 @@ __host__ __device__ inline int block_bytes(int t) {
     case T_Q4_K: return 144;
     case T_Q5_K: return 176;
     case T_Q6_K: return 210;
+    case T_Q6_K_SPLIT: return 210;  // 208 in the block array + 2 in the scale array
     default: return 0;
     }
 }
-__host__ __device__ inline bool is_kquant(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
+__host__ __device__ inline bool is_kquant(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT; }
 
 // Exact f16 -> f32 (the `half` crate's to_f32; hardware conversion is exact).
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }

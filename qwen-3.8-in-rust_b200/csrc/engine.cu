@@ -104,6 +104,19 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         cudaStreamDestroy(s);
     }
     auto ptr = [&](const TensorInfo& t) { return m->blob_ + t.rel_offset; };
+    // Q6_K matrices are repacked in place into the split layout the bulk-copy GEMV reads (same bytes); the
+    // embedding table keeps the ggml layout because rows of it are dequantised directly
+    uint8_t* repack_tmp = nullptr;
+    uint64_t repack_cap = 0;
+    for (const TensorInfo& t : g.tensors())
+        if (t.type == T_Q6_K && t.name != "token_embd.weight") repack_cap = std::max(repack_cap, t.byte_size);
+    if (repack_cap) ck(cudaMalloc(&repack_tmp, repack_cap), "repack buffer");
+    auto repack = [&](const TensorInfo& t) {
+        uint8_t* p = m->blob_ + t.rel_offset;
+        ck(cudaMemcpy(repack_tmp, p, t.byte_size, cudaMemcpyDeviceToDevice), "repack copy");
+        ck(launch_repack_q6k(repack_tmp, t.byte_size / 210, p, 0), "repack");
+        ck(cudaDeviceSynchronize(), "repack");
+    };
     auto mat = [&](const std::string& name, uint64_t rows, uint64_t cols) {
         const TensorInfo& t = g.tensor(name);
         const auto sh = t.shape_numpy();
@@ -117,6 +130,10 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         d.cols = (int)cols;
         d.p = ptr(t);
         d.bytes = t.byte_size;
+        if (t.type == T_Q6_K && name != "token_embd.weight") {
+            repack(t);
+            d.type = T_Q6_K_SPLIT;
+        }
         return d;
     };
     auto vec = [&](const std::string& name, uint64_t len) -> const float* {
@@ -189,6 +206,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     ck(cudaMalloc(&m->rope_sin, sn.size() * 4), "rope table");
     ck(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
     ck(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    if (repack_tmp) cudaFree(repack_tmp);
     m->attn_scaling = powf((float)c.head_dim_k, -0.5f);  // (hd as f32).powf(-0.5) (gqa_attention.rs:186)
     uint64_t layer_total = 0;
     for (uint32_t i = 0; i < c.n_layer; i++) {
@@ -196,6 +214,10 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         if (g.layer_span(i, s0, e0)) layer_total += e0 - s0;
     }
     m->decode_bytes = layer_total + m->lm_head.bytes + 4ull * H + m->embed.bytes / c.vocab_size;
+    for (uint32_t mi : c.mtp_layers) {
+        uint64_t s0, e0;
+        if (g.layer_span(mi, s0, e0)) m->mtp_bytes += e0 - s0;
+    }
     m->load_secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     return m;
 }
@@ -312,7 +334,7 @@ void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y) {
 }
 
 void State::quant_for(int type, const float* x, int n, int rows) {
-    ck(launch_quant_rows(x, n, rows, is_kquant(type) ? q8k_ : nullptr, (type == T_Q8_0 || type == T_Q4_0) ? q80_ : nullptr, stream),
+    count_launch(); ck(launch_quant_rows(x, n, rows, is_kquant(type) ? q8k_ : nullptr, (type == T_Q8_0 || type == T_Q4_0) ? q80_ : nullptr, stream),
        "quantise");
 }
 
@@ -324,46 +346,46 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     const float eps = c.rms_norm_eps;
     if (L.attn) {
         const bool k8 = needs_q8k({L.q.type, L.k.type, L.v.type}), k0 = needs_q80({L.q.type, L.k.type, L.v.type});
-        ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
+        count_launch(); ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
                                    k0 ? q80_ : nullptr, stream), "attn_norm");
         gemv(L.q, normed_, t, qg_);
         gemv(L.k, normed_, t, kk_);
         gemv(L.v, normed_, t, vv_);
         QkArgs qa{qg_, kk_, vv_, L.q_norm, L.k_norm, m_.rope_cos, m_.rope_sin, pos_dev, qr_, gate_, kv->k, kv->v,
                   (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k, (int)c.rope_dim, eps};
-        ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
+        count_launch(); ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
         AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k, max_pos_,
                     m_.attn_scaling};
-        ck(launch_attention(aa, t, stream), "attention");
+        count_launch(); ck(launch_attention(aa, t, stream), "attention");
         quant_for(L.o.type, attn_, L.o.cols, t);
         gemv(L.o, attn_, t, mix_out_);
     } else {
         const DnState& d = dn_[li];
         const bool k8 = needs_q8k({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
         const bool k0 = needs_q80({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
-        ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
+        count_launch(); ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
                                    k0 ? q80_ : nullptr, stream), "attn_norm");
         gemv(L.qkv, normed_, t, qkv_);
         gemv(L.gate_z, normed_, t, z_);
         gemv(L.alpha, normed_, t, alpha_);
         gemv(L.beta, normed_, t, beta_);
-        ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, (int)c.dn_qkv_dim, qkv_, t, conved_, d.pend_x,
+        count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, (int)c.dn_qkv_dim, qkv_, t, conved_, d.pend_x,
                             commit_dn ? d_keep : nullptr, T_, stream), "conv");
         DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,
                      commit_dn ? d_keep : nullptr, t, T_, (int)c.dn_n_k_heads, (int)c.dn_n_v_heads, (int)c.dn_head_dim_k,
                      (int)c.dn_head_dim_v, (int)c.dn_k_dim, (int)c.dn_qkv_dim, eps};
-        ck(launch_deltanet_heads(da, stream), "deltanet");
+        count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
         quant_for(L.ssm_out.type, heads_, L.ssm_out.cols, t);
         gemv(L.ssm_out, heads_, t, mix_out_);
     }
     // h = x + mixer(x); then the MLP on post_attention_norm(h) (mlp.rs:53-64)
     const bool k8 = needs_q8k({L.ffn_gate.type, L.ffn_up.type}), k0 = needs_q80({L.ffn_gate.type, L.ffn_up.type});
-    ck(launch_resid_norm_quant(h_, mix_out_, h_, L.post_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr, k0 ? q80_ : nullptr, stream),
+    count_launch(); ck(launch_resid_norm_quant(h_, mix_out_, h_, L.post_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr, k0 ? q80_ : nullptr, stream),
        "post_attention_norm");
     gemv(L.ffn_gate, normed_, t, g_);
     gemv(L.ffn_up, normed_, t, u_);
     const int dt = L.ffn_down.type;
-    ck(launch_swiglu_quant(g_, u_, (int)c.intermediate_size, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
+    count_launch(); ck(launch_swiglu_quant(g_, u_, (int)c.intermediate_size, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
                            (dt == T_Q8_0 || dt == T_Q4_0) ? q80_ : nullptr, stream), "swiglu");
     gemv(L.ffn_down, g_, t, mlp_out_);
 }
@@ -371,7 +393,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
 void State::forward_rows(int t, bool want_logits_all) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
-    ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, h_, stream), "embed");
+    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, h_, stream), "embed");
     for (size_t li = 0; li < m_.layers.size(); li++) {
         layer_forward(m_.layers[li], (int)li, t, &kv_[li], d_pos, true);
         if (capture_) {
@@ -384,18 +406,18 @@ void State::forward_rows(int t, bool want_logits_all) {
     }
     // final norm (model.rs:430-438): the post-norm rows are what the lm_head and the MTP read
     const int ht = m_.lm_head.type;
-    ck(launch_resid_norm_quant(h_, mlp_out_, h_, m_.output_norm, c.rms_norm_eps, H, t, final_, is_kquant(ht) ? q8k_ : nullptr,
+    count_launch(); ck(launch_resid_norm_quant(h_, mlp_out_, h_, m_.output_norm, c.rms_norm_eps, H, t, final_, is_kquant(ht) ? q8k_ : nullptr,
                                (ht == T_Q8_0 || ht == T_Q4_0) ? q80_ : nullptr, stream), "output_norm");
     if (capture_ && !capture_h_.empty())
         ck(cudaMemcpyAsync(capture_h_[m_.layers.size()], final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "capture");
     if (want_logits_all) {
         gemv(m_.lm_head, final_, t, logits_);
-        ck(launch_argmax(logits_, (int)c.vocab_size, t, d_argmax, stream), "argmax");
+        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, t, d_argmax, stream), "argmax");
     } else {
         // only the last row's logits (prefill): quantise that row alone at row 0
         quant_for(ht, final_ + (size_t)(t - 1) * H, H, 1);
         gemv(m_.lm_head, final_ + (size_t)(t - 1) * H, 1, logits_);
-        ck(launch_argmax(logits_, (int)c.vocab_size, 1, d_argmax, stream), "argmax");
+        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, 1, d_argmax, stream), "argmax");
     }
 }
 
@@ -454,14 +476,14 @@ void State::mtp_rows(int t, const uint32_t* tokens, const float* hidden, bool hi
     const MtpW& M = m_.mtp;
     (void)hidden_is_hout;
     upload_ids(tokens, t);
-    ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, embed_, stream), "embed");
-    ck(launch_rmsnorm_rows(embed_, H, M.enorm, c.rms_norm_eps, H, t, cat_, 2 * H, stream), "enorm");
-    ck(launch_rmsnorm_rows(hidden, H, M.hnorm, c.rms_norm_eps, H, t, cat_ + H, 2 * H, stream), "hnorm");
+    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, embed_, stream), "embed");
+    count_launch(); ck(launch_rmsnorm_rows(embed_, H, M.enorm, c.rms_norm_eps, H, t, cat_, 2 * H, stream), "enorm");
+    count_launch(); ck(launch_rmsnorm_rows(hidden, H, M.hnorm, c.rms_norm_eps, H, t, cat_ + H, 2 * H, stream), "hnorm");
     quant_for(M.eh_proj.type, cat_, 2 * H, t);
     gemv(M.eh_proj, cat_, t, h_);  // u rows become the block's residual input
     set_dev_int(d_mtp_pos, mtp_len_, stream);
     layer_forward(M.block, 0, t, &mtp_kv_, d_mtp_pos, false);
-    ck(launch_resid_norm_quant(h_, mlp_out_, h_, M.head_norm, c.rms_norm_eps, H, t, mtp_hout_, nullptr, nullptr, stream), "head_norm");
+    count_launch(); ck(launch_resid_norm_quant(h_, mlp_out_, h_, M.head_norm, c.rms_norm_eps, H, t, mtp_hout_, nullptr, nullptr, stream), "head_norm");
     mtp_len_ += t;
 }
 
@@ -471,7 +493,7 @@ uint32_t State::mtp_draft_from_row(int row) {
     const int H = (int)c.hidden_size;
     quant_for(m_.lm_head.type, mtp_hout_ + (size_t)row * H, H, 1);
     gemv(m_.lm_head, mtp_hout_ + (size_t)row * H, 1, logits_ + (size_t)(T_ - 1) * c.vocab_size);
-    ck(launch_argmax(logits_ + (size_t)(T_ - 1) * c.vocab_size, (int)c.vocab_size, 1, d_argmax + (T_ - 1), stream), "argmax");
+    count_launch(); ck(launch_argmax(logits_ + (size_t)(T_ - 1) * c.vocab_size, (int)c.vocab_size, 1, d_argmax + (T_ - 1), stream), "argmax");
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax + (T_ - 1), 4, cudaMemcpyDeviceToHost, stream), "argmax");
     sync();

@@ -63,6 +63,7 @@ class Model {
     float attn_scaling = 0.f;
     uint64_t weight_bytes = 0;   // bytes resident on the device
     uint64_t decode_bytes = 0;   // weight bytes one plain token reads (model.rs:274)
+    uint64_t mtp_bytes = 0;      // the MTP block's bytes (blk.{n_layer})
     double load_secs = 0;
     bool is_stop(uint32_t id) const;
 
@@ -105,12 +106,15 @@ class State {
     int spec_k() const { return k_; }
     SpecCounters counters;
     cudaStream_t stream = nullptr;
+    uint64_t launches() const { return launches_; }
 
   private:
     const Model& m_;
     int k_, max_pos_, T_;
     int pos_ = 0, mtp_len_ = 0, prev_row_ = 0;
     bool capture_ = false;
+    uint64_t launches_ = 0;  // kernels this state has launched
+    void count_launch() { launches_++; }
     std::vector<uint32_t> drafts_;
     std::vector<void*> allocs_;
     void* dalloc(size_t bytes);

@@ -477,6 +477,10 @@ cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, fl
 template <int NC>
 cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
     static const bool no_tma = getenv("QDEC_GEMV_NO_TMA") != nullptr;  // tuning override: the register-path kernel
+    if (type == T_Q6_K_SPLIT) {  // only the bulk-copy kernel reads the split layout
+        if (!tma_gemv_supported(type, cols, NC) || ((uintptr_t)w & 15)) return cudaErrorInvalidValue;
+        return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
+    }
     if (!no_tma && tma_gemv_supported(type, cols, NC) && ((uintptr_t)w & 15) == 0)
         return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
     switch (type) {

@@ -28,6 +28,10 @@ int num_sms();
 bool tma_gemv_supported(int type, int cols, int ncols);
 cudaError_t launch_gemv_tma(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
                             cudaStream_t s);
+// ggml Q6_K blocks -> the split layout the bulk-copy GEMV reads (nblocks blocks; dst holds the same bytes).
+cudaError_t launch_repack_q6k(const uint8_t* src, size_t nblocks, uint8_t* dst, cudaStream_t s);
+// Force the bulk-copy GEMV's lanes per row (1, 2, 4, 8; 0 = chosen from the row count).
+void set_gemv_lanes_per_row(int lpr);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
 

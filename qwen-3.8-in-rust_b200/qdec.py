@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "libqdec.so")
 
 OK, EINVAL, ECUDA, ENOMEM, EIO, EFORMAT, ESTATE, ETIMEOUT = 0, -1, -2, -3, -4, -5, -6, -7
 F32, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 2, 8, 12, 13, 14
+Q6_K_SPLIT = 114
 TYPE_NAMES = {F32: "F32", Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
 LAYOUT = {F32: (1, 4), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 
@@ -30,7 +31,8 @@ class ModelInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in ("n_layer", "hidden", "ffn", "vocab", "n_head", "n_head_kv", "head_dim",
                                                "dn_n_k_heads", "dn_n_v_heads", "dn_head_dim_k", "dn_head_dim_v",
                                                "n_full_attention", "has_mtp")] + [
-        ("weight_bytes", ctypes.c_uint64), ("decode_bytes", ctypes.c_uint64), ("load_secs", ctypes.c_double)]
+        ("weight_bytes", ctypes.c_uint64), ("decode_bytes", ctypes.c_uint64), ("lm_head_bytes", ctypes.c_uint64),
+        ("mtp_bytes", ctypes.c_uint64), ("load_secs", ctypes.c_double)]
 
 
 class QdecError(RuntimeError):
@@ -58,6 +60,8 @@ def lib():
             "qdec_matvec": [I, P, I, I, P, I, P, P],
             "qdec_matvec_noalloc": [I, P, I, I, P, I, P, P],
             "qdec_dequant_rows": [I, P, I, I, P, I, P, P],
+            "qdec_repack_q6k": [P, I, I, P, P],
+            "qdec_tune_gemv_lanes_per_row": [I],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
@@ -91,6 +95,10 @@ def lib():
             fn = getattr(L, name)
             fn.restype = I
             fn.argtypes = args
+        L.qdec_state_stream.restype = P
+        L.qdec_state_stream.argtypes = [P]
+        L.qdec_state_launches.restype = ctypes.c_uint64
+        L.qdec_state_launches.argtypes = [P]
         _lib = L
     return _lib
 
@@ -141,6 +149,16 @@ def matvec_noalloc(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream=0):
 
 def matvec_noalloc_max_bytes():
     return lib().qdec_matvec_noalloc_max_bytes()
+
+
+def tune_gemv_lanes_per_row(lpr):
+    """Force the GEMV's lanes per row (1, 2, 4, 8; 0 = automatic). Results are identical for every value."""
+    _check(lib().qdec_tune_gemv_lanes_per_row(lpr))
+
+
+def repack_q6k(src_ptr, rows, cols, dst_ptr, stream=0):
+    """ggml Q6_K rows -> the engine's split device layout (QDEC_TYPE_Q6_K_SPLIT)."""
+    _check(lib().qdec_repack_q6k(src_ptr, rows, cols, dst_ptr, stream))
 
 
 def dequant_rows(t, w_ptr, rows, cols, ids_ptr, nids, out_ptr, stream=0):
@@ -210,6 +228,15 @@ class State:
     @property
     def pos(self):
         return lib().qdec_state_pos(self._h)
+
+    @property
+    def stream(self):
+        """The cudaStream_t (as an int) all of this state's kernels run on."""
+        return lib().qdec_state_stream(self._h) or 0
+
+    @property
+    def launches(self):
+        return lib().qdec_state_launches(self._h)
 
     def prefill(self, ids):
         out = ctypes.c_uint32()

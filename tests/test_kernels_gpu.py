@@ -164,3 +164,49 @@ def test_dequant_golden_hostile(q):
         q.dequant_rows(tid, wd.data_ptr(), 1, n, idd.data_ptr(), 1, out.data_ptr())
         torch.cuda.synchronize()
         assert bits_equal(out.cpu().numpy(), want), base
+
+
+def run_gemv_raw(q, t, wd, rows, cols, x):
+    xd = to_dev(np.ascontiguousarray(x, np.float32))
+    n = x.shape[0]
+    y = torch.empty(n * rows, dtype=torch.float32, device="cuda")
+    q.matvec(t, wd.data_ptr(), rows, cols, xd.data_ptr(), n, y.data_ptr())
+    torch.cuda.synchronize()
+    return y.cpu().numpy().reshape(n, rows)
+
+
+@pytest.mark.parametrize("lpr", [1, 2, 4, 8])
+@pytest.mark.parametrize("t", [12, 13])
+def test_gemv_every_lanes_per_row_bit_exact(q, orc, t, lpr):
+    """The bulk-copy GEMV gives the same bits whichever number of lanes shares a row."""
+    rows, cols = 333, 6144
+    w = random_blocks(t, rows, cols, seed=5 + t)
+    x = np.random.default_rng(lpr).standard_normal((4, cols)).astype(np.float32)
+    want = orc.matmul(t, w, rows, cols, x)
+    q.tune_gemv_lanes_per_row(lpr)
+    try:
+        for n in (1, 3, 4):
+            got = run_gemv_raw(q, t, to_dev(w), rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (t, lpr, n)
+    finally:
+        q.tune_gemv_lanes_per_row(0)
+
+
+@pytest.mark.parametrize("lpr", [0, 1, 2, 8])
+def test_gemv_q6k_split_layout_bit_exact(q, orc, lpr):
+    """Q6_K repacked into the split device layout (208-byte blocks + f16 scales) gives the ggml-layout bits."""
+    rows, cols = 515, 5120
+    w = random_blocks(14, rows, cols, seed=99)
+    src = to_dev(w)
+    dst = torch.empty_like(src)
+    q.repack_q6k(src.data_ptr(), rows, cols, dst.data_ptr())
+    torch.cuda.synchronize()
+    x = np.random.default_rng(3).standard_normal((4, cols)).astype(np.float32)
+    want = orc.matmul(14, w, rows, cols, x)
+    q.tune_gemv_lanes_per_row(lpr)
+    try:
+        for n in (1, 2, 4):
+            got = run_gemv_raw(q, q.Q6_K_SPLIT, dst, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (lpr, n)
+    finally:
+        q.tune_gemv_lanes_per_row(0)
