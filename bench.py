@@ -136,9 +136,54 @@ def dist_setup(backend):
     return world, rank, local
 
 
+def oracle_spec_sample(path, k, prompt_len, rounds):
+    """The reference's greedy --spec k loop restated on the CPU (oracle/model.c, OpenMP over all host threads) on
+    the 27B checkpoint: a short prompt, then `rounds` rounds; returns (tok/s over the rounds, stats, cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    oracle.build()
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    om = oracle.OracleModel(path)
+    st = om.state(max_pos=prompt_len + (k + 1) * (rounds + 2) + 8)
+    prompt = spec_prompt(om.vocab, SPEC_SEED + 1)[:prompt_len]
+    ids, stats, _ = st.spec_generate(prompt, 1 + rounds, k, stop=False)
+    secs = stats["round_seconds"]
+    emitted = len(ids) - 1
+    om.close()
+    return emitted / secs, secs / max(1, stats["rounds"]), stats, cores
+
+
+def run_reference_spec(args, world, rank):
+    if rank != 0:
+        return
+    path = ensure_checkpoint(args.preset, SPEC_SEED)
+    k = SPEC_K
+    # each step is one round; the CPU restatement needs tens of seconds per 27B round, so the run is capped
+    rounds = max(1, min(args.steps, 2))
+    tok_s, s_round, stats, cores = oracle_spec_sample(path, k, 4, rounds)
+    sample = (f"{stats['rounds']} --spec {k} rounds after a 4-token prompt on the {args.preset} checkpoint "
+              f"(of {args.steps} requested steps; {s_round:.1f} s/round)")
+    line = {
+        "metric": "decode tok/s (greedy, --spec 3) Qwen3.8-27B Q4_K_M", "value": round(tok_s, 5), "unit": "tok/s",
+        "n_gpus": world, "steps": stats["rounds"], "warmup": 0, "ms_per_step": round(s_round * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "Q4_K_M weights x Q8_K activations, f32", "data": "synthetic",
+        "config": {"workload": f"{args.preset} --spec 3 (BASELINE config 4)", "k": k},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(tok_s, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, world, rank):
     """The reference's CPU path (oracle restatement, all host threads) on a bounded row sample per step."""
     if rank != 0:
+        return
+    if args.workload == "spec":
+        run_reference_spec(args, world, rank)
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
@@ -497,6 +542,10 @@ def run_spec_qdec(args, world, rank, local):
                      "north_star_frac": round(17.8e9 / s_round / 1e9 / peak, 4)},
         "clocks": clk.summary(),
     }
+    if world == 1 and not args.no_cpu_baseline:
+        tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 1)
+        line["cpu_baseline"] = {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": f"1 --spec {k} round after a 2-token prompt ({s_rnd:.1f} s/round)"}
     print(json.dumps(line), flush=True)
 
 
@@ -506,7 +555,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["qdec", "reference"], default="qdec")
-    ap.add_argument("--workload", choices=["gemv", "spec"], default="gemv")
+    ap.add_argument("--workload", choices=["spec", "gemv"], default="spec")
     ap.add_argument("--preset", default="27b", help="synthetic checkpoint of the spec workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -74,8 +74,15 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
                 void *stream);
 
 /* Tuning knob of the K-quant GEMV: lanes that share one weight row (1, 2, 4 or 8; 0 = chosen from the row
- * count, the default).  Results do not depend on it; it exists for tests and sweeps. */
+ * count, the default).  A non-zero value selects the bulk-copy kernel.  Results do not depend on it; it exists
+ * for tests and sweeps. */
 int qdec_tune_gemv_lanes_per_row(int lpr);
+
+/* Tuning knob of the K-quant GEMV: the kernel (0 = automatic, 2 = register path with super-block slots, 4 =
+ * bulk-copy, 5 = register-streamed), and for the register-streamed kernel the reference lanes per thread
+ * (0 = automatic, 1, 2) and the super-blocks in flight per thread (0 = automatic, 4, 8).  Results do not depend
+ * on it; it exists for tests and sweeps.  No counterpart in the reference. */
+int qdec_tune_gemv(int impl, int lanes_per_thread, int depth);
 
 /* Repack rows x cols of ggml Q6_K (src) into the split layout (dst, the same number of bytes, a distinct
  * buffer) that qdec_gemv reads as QDEC_TYPE_Q6_K_SPLIT.  No counterpart in the reference (a device layout). */

@@ -21,6 +21,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -581,6 +582,16 @@ int oracle_generate(OState *s, const uint32_t *prompt, int n, int n_out, int sto
  * [x_p, d_1..d_k] (token by token on the snapshot), accept, restore + replay of the kept rows, MTP re-feed,
  * chained drafts.  forced_drafts (optional, n_forced_rounds x k) replaces the MTP drafts of the first rounds,
  * as spec_set_drafts does in the reference's identity test.  stats4 = rounds, drafted, accepted, emitted. */
+static double g_round_seconds = 0.0;  /* wall time the last oracle_spec_generate spent in its rounds */
+
+double oracle_last_round_seconds(void) { return g_round_seconds; }
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
 int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, int k, int stop, const uint32_t *forced,
                          int n_forced, uint32_t *out, uint64_t *stats4, uint32_t *drafts_log) {
     OModel *m = s->m;
@@ -604,6 +615,7 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
     for (int i = 1; i < k; i++) { memcpy(hprev, hout, (size_t)H * 4); drafts[i] = mtp_row(s, drafts[i - 1], hprev, hout, 1); }
     out[c++] = x_t;
     uint32_t x_p = x_t;
+    const double t_rounds = now_s();
     while (c < n_out && !(stop && is_stop(m, out[c - 1]))) {
         if (forced && round < n_forced) memcpy(drafts, forced + (size_t)round * k, sizeof(uint32_t) * k);
         if (drafts_log) memcpy(drafts_log + (size_t)round * k, drafts, sizeof(uint32_t) * k);
@@ -649,6 +661,7 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
         x_p = emitted[keep - 1];
         round++;
     }
+    g_round_seconds = now_s() - t_rounds;
     free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted);
     return c;
 }

@@ -70,6 +70,7 @@ def lib():
             "oracle_state_new": (P, [P, I]),
             "oracle_state_free": (None, [P]),
             "oracle_state_pos": (I, [P]),
+            "oracle_last_round_seconds": (ctypes.c_double, []),
             "oracle_forward_token": (I, [P, ctypes.c_uint32, P, P, P]),
             "oracle_generate": (I, [P, U32P, I, I, I, U32P]),
             "oracle_spec_generate": (I, [P, U32P, I, I, I, I, U32P, I, U32P, ctypes.POINTER(ctypes.c_uint64), U32P]),
@@ -347,5 +348,6 @@ class OracleState:
         if c < 0:
             raise ValueError("oracle: spec_generate failed")
         stats = dict(zip(("rounds", "drafted", "accepted", "emitted"), list(st)))
+        stats["round_seconds"] = lib().oracle_last_round_seconds()
         drafts = [list(log[i * k:(i + 1) * k]) for i in range(stats["rounds"])]
         return list(out[:c]), stats, drafts

@@ -138,6 +138,16 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
 int qdec_tune_gemv_lanes_per_row(int lpr) {
     if (lpr != 0 && lpr != 1 && lpr != 2 && lpr != 4 && lpr != 8) return fail(QDEC_EINVAL, "lanes per row must be 0, 1, 2, 4 or 8");
     set_gemv_lanes_per_row(lpr);
+    set_gemv_impl(lpr ? 4 : 0);
+    return QDEC_OK;
+}
+
+int qdec_tune_gemv(int impl, int lanes_per_thread, int depth) {
+    if (impl != 0 && impl != 2 && impl != 4 && impl != 5) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 4 or 5");
+    if (lanes_per_thread < 0 || lanes_per_thread > 2) return fail(QDEC_EINVAL, "lanes per thread must be 0, 1 or 2");
+    if (depth != 0 && depth != 4 && depth != 8) return fail(QDEC_EINVAL, "depth must be 0, 4 or 8");
+    set_gemv_impl(impl);
+    set_gemv_v5_tuning(lanes_per_thread, depth);
     return QDEC_OK;
 }
 

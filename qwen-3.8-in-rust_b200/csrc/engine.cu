@@ -330,7 +330,8 @@ static bool needs_q80(std::initializer_list<int> ts) {
 void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y) {
     const void* act = is_kquant(w.type) ? (const void*)q8k_ : (w.type == T_F32 ? (const void*)normed_f32 : (const void*)q80_);
     // activation rows are laid out back to back at the stride of this weight's width
-    ck(launch_gemv(w.type, w.p, w.rows, w.cols, act, rows, y, stream), "gemv");
+    // weights are written once at load, so the GEMV may stream them before its predecessor finishes
+    ck(launch_gemv(w.type, w.p, w.rows, w.cols, act, rows, y, stream, true), "gemv");
 }
 
 void State::quant_for(int type, const float* x, int n, int rows) {

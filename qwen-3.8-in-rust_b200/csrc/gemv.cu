@@ -474,14 +474,24 @@ cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, fl
     return cudaGetLastError();
 }
 
+int g_gemv_impl = [] {
+    const char* e = getenv("QDEC_GEMV_IMPL");  // tuning override: 2, 4 or 5
+    return e ? atoi(e) : 0;
+}();
+
 template <int NC>
-cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
-    static const bool no_tma = getenv("QDEC_GEMV_NO_TMA") != nullptr;  // tuning override: the register-path kernel
-    if (type == T_Q6_K_SPLIT) {  // only the bulk-copy kernel reads the split layout
-        if (!tma_gemv_supported(type, cols, NC) || ((uintptr_t)w & 15)) return cudaErrorInvalidValue;
+cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s, bool pdl) {
+    const int impl = g_gemv_impl;
+    const bool aligned = ((uintptr_t)w & 15) == 0;
+    if (type == T_Q6_K_SPLIT) {  // the split layout is read by the bulk-copy and register-streamed kernels
+        if (!aligned) return cudaErrorInvalidValue;
+        if (impl != 4 && v5_gemv_supported(type, cols, NC)) return launch_gemv_v5(type, w, rows, cols, act, NC, y, s, pdl);
+        if (!tma_gemv_supported(type, cols, NC)) return cudaErrorInvalidValue;
         return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
     }
-    if (!no_tma && tma_gemv_supported(type, cols, NC) && ((uintptr_t)w & 15) == 0)
+    if ((impl == 0 || impl == 5) && aligned && v5_gemv_supported(type, cols, NC))
+        return launch_gemv_v5(type, w, rows, cols, act, NC, y, s, pdl);
+    if ((impl == 0 || impl == 4) && tma_gemv_supported(type, cols, NC) && aligned)
         return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
     switch (type) {
     case T_Q4_K: return launch_kq<T_Q4_K, NC>(w, rows, cols, act, y, s);
@@ -512,7 +522,10 @@ size_t act_row_bytes(int type, int cols) {
     return (size_t)cols * 4;
 }
 
-cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y, cudaStream_t s) {
+void set_gemv_impl(int impl) { g_gemv_impl = impl; }
+
+cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y, cudaStream_t s,
+                        bool pdl) {
     if (rows <= 0) return cudaSuccess;
     // columns beyond 4 are processed in groups of at most 4 (each weight byte then read once per group)
     int c0 = 0;
@@ -522,10 +535,10 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
         float* yy = y + (size_t)c0 * rows;
         cudaError_t e;
         switch (nc) {
-        case 1: e = dispatch_type<1>(type, w, rows, cols, a, yy, s); break;
-        case 2: e = dispatch_type<2>(type, w, rows, cols, a, yy, s); break;
-        case 3: e = dispatch_type<3>(type, w, rows, cols, a, yy, s); break;
-        default: e = dispatch_type<4>(type, w, rows, cols, a, yy, s); break;
+        case 1: e = dispatch_type<1>(type, w, rows, cols, a, yy, s, pdl); break;
+        case 2: e = dispatch_type<2>(type, w, rows, cols, a, yy, s, pdl); break;
+        case 3: e = dispatch_type<3>(type, w, rows, cols, a, yy, s, pdl); break;
+        default: e = dispatch_type<4>(type, w, rows, cols, a, yy, s, pdl); break;
         }
         if (e != cudaSuccess) return e;
         c0 += nc;

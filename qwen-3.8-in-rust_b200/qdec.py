@@ -62,6 +62,7 @@ def lib():
             "qdec_dequant_rows": [I, P, I, I, P, I, P, P],
             "qdec_repack_q6k": [P, I, I, P, P],
             "qdec_tune_gemv_lanes_per_row": [I],
+            "qdec_tune_gemv": [I, I, I],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
@@ -154,6 +155,12 @@ def matvec_noalloc_max_bytes():
 def tune_gemv_lanes_per_row(lpr):
     """Force the GEMV's lanes per row (1, 2, 4, 8; 0 = automatic). Results are identical for every value."""
     _check(lib().qdec_tune_gemv_lanes_per_row(lpr))
+
+
+def tune_gemv(impl=0, lanes_per_thread=0, depth=0):
+    """Select the GEMV kernel (0 automatic, 2, 4, 5) and the register-streamed kernel's lanes per thread and
+    depth (0 = automatic). Results are identical for every value."""
+    _check(lib().qdec_tune_gemv(impl, lanes_per_thread, depth))
 
 
 def repack_q6k(src_ptr, rows, cols, dst_ptr, stream=0):

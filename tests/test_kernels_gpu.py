@@ -210,3 +210,41 @@ def test_gemv_q6k_split_layout_bit_exact(q, orc, lpr):
             assert bits_equal(got, want[:n]), (lpr, n)
     finally:
         q.tune_gemv_lanes_per_row(0)
+
+
+@pytest.mark.parametrize("t", [12, 13, 114])
+@pytest.mark.parametrize("gl,depth", [(1, 4), (1, 8), (2, 4), (2, 8)])
+def test_gemv_register_streamed_bit_exact(q, orc, t, gl, depth):
+    """The register-streamed GEMV at every lanes-per-thread / depth: the oracle's bits for 1..4 columns, on a
+    ragged row count and a width whose super-block count is not a multiple of the depth."""
+    rows, cols = 389, 5376  # 21 super-blocks
+    base = 14 if t == 114 else t
+    w = random_blocks(base, rows, cols, seed=7 + t)
+    x = np.random.default_rng(gl * 10 + depth).standard_normal((4, cols)).astype(np.float32)
+    want = orc.matmul(base, w, rows, cols, x)
+    wd = to_dev(w)
+    if t == 114:
+        dst = torch.empty_like(wd)
+        q.repack_q6k(wd.data_ptr(), rows, cols, dst.data_ptr())
+        wd = dst
+    q.tune_gemv(5, gl, depth)
+    try:
+        for n in (1, 2, 3, 4):
+            got = run_gemv_raw(q, t, wd, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (t, gl, depth, n)
+    finally:
+        q.tune_gemv(0, 0, 0)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 256), (5, 17408), (4099, 256)])
+def test_gemv_register_streamed_edge_shapes(q, orc, rows, cols):
+    """One row, one super-block per row, and the widest activation the kernel stages."""
+    w = random_blocks(12, rows, cols, seed=rows)
+    x = np.random.default_rng(2).standard_normal((4, cols)).astype(np.float32)
+    want = orc.matmul(12, w, rows, cols, x)
+    q.tune_gemv(5, 0, 0)
+    try:
+        got = run_gemv_raw(q, 12, to_dev(w), rows, cols, x)
+    finally:
+        q.tune_gemv(0, 0, 0)
+    assert bits_equal(got, want)
