@@ -37,6 +37,11 @@ extern "C" {
 /* Q6_K in the engine's split device layout: the tensor's 208-byte blocks [ql | qh | scales], then every block's
  * f16 d -- the same bytes as ggml's 210-byte blocks, 16-byte aligned for bulk copies (qdec_repack_q6k). */
 #define QDEC_TYPE_Q6_K_SPLIT 114
+/* The tile layout (qdec_repack_tiles): 8 rows x one super-block per tile block of 8 * (block bytes), arranged in
+ * the order the GEMV threads read them; the same bytes as the ggml layout.  rows must be a multiple of 8. */
+#define QDEC_TYPE_Q4_K_TILE 112
+#define QDEC_TYPE_Q5_K_TILE 113
+#define QDEC_TYPE_Q6_K_TILE 116
 
 /* Library version string, e.g. "qdec 0.1.0 sm_100a". */
 const char *qdec_version(void);
@@ -73,26 +78,28 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
 int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev,
                 void *stream);
 
-/* Tuning knob of the K-quant GEMV: lanes that share one weight row (1, 2, 4 or 8; 0 = chosen from the row
- * count, the default).  A non-zero value selects the bulk-copy kernel.  Results do not depend on it; it exists
- * for tests and sweeps. */
-int qdec_tune_gemv_lanes_per_row(int lpr);
-
-/* Tuning knob of the K-quant GEMV: the kernel (0 = automatic, 2 = register path with super-block slots, 4 =
- * bulk-copy, 5 = register-streamed), and for the register-streamed kernel the reference lanes per thread
- * (0 = automatic, 1, 2) and the super-blocks in flight per thread (0 = automatic, 4, 8).  Results do not depend
- * on it; it exists for tests and sweeps.  No counterpart in the reference. */
-int qdec_tune_gemv(int impl, int lanes_per_thread, int depth);
+/* Tuning knob of the K-quant GEMV (process-wide): the kernel (0 = automatic; 2 = the kernel that reads
+ * block_q8_K activations in the reference layout; 6 = the kernel that reads the library's activation image) and
+ * the image kernel's configuration (0 = automatic, 1..8: lanes per thread, rows per thread, super-blocks in
+ * flight, integer or FP32 scale multiply).  Results do not depend on it; it exists for tests and sweeps.
+ * No counterpart in the reference. */
+int qdec_tune_gemv(int impl, int config);
 
 /* Repack rows x cols of ggml Q6_K (src) into the split layout (dst, the same number of bytes, a distinct
  * buffer) that qdec_gemv reads as QDEC_TYPE_Q6_K_SPLIT.  No counterpart in the reference (a device layout). */
 int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void *stream);
 
+/* Repack rows x cols of ggml Q4_K / Q5_K / Q6_K (src) into the tile layout (dst: the same number of bytes, a
+ * distinct 16-byte aligned buffer) that qdec_gemv reads as QDEC_TYPE_Q4_K_TILE / _Q5_K_TILE / _Q6_K_TILE.
+ * No counterpart in the reference (a device layout). */
+int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, void *dst_dev, void *stream);
+
 /* qdec_matvec for callers that cannot let a library allocate device memory: an application whose device memory
  * belongs to another allocator, or a decode loop that must stay allocation-free while it runs.  Same arguments,
  * same results as qdec_matvec, but the quantised columns live in a fixed array inside the library
  * (qdec_matvec_noalloc_max_bytes() bytes, held on every device that loads the library until exit); sizes that
- * do not fit are rejected with QDEC_EINVAL.  The first call on a device looks the array's address up, so make it
+ * do not fit are rejected with QDEC_EINVAL.  K-quant columns take cols/256 * 320 bytes each there (the library's
+ * activation image), Q8_0/Q4_0 columns cols/32 * 34.  The first call on a device looks the array's address up, so make it
  * before any stream capture.  All calls on a device share the array: calls that overlap on the GPU race.
  * This entry point has no counterpart in the reference, whose CPU matvec quantises into caller-owned rows. */
 int qdec_matvec_noalloc(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols,

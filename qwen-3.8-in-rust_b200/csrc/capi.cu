@@ -32,7 +32,8 @@ int cuda_fail(cudaError_t e, const char *what) {
 void clear_error() { g_last_error.clear(); }
 
 bool supported_type(int t) {
-    return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT;
+    return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT ||
+           t == T_Q4_K_TILE || t == T_Q5_K_TILE || t == T_Q6_K_TILE;
 }
 
 // Shape checks of the reference's assert!s (matvec.rs:73-77, :300, :338; kdot.rs:179-191).
@@ -43,8 +44,10 @@ int check_gemv_shape(int type, int rows, int cols, int ncols) {
     if (cols % be) return fail(QDEC_EINVAL, "cols %d not a multiple of block size %d for type %d", cols, be, type);
     if ((type == T_Q8_0 || type == T_Q4_0) && cols % 64)
         return fail(QDEC_EINVAL, "cols %d: Q8_0/Q4_0 rows must hold an even number of 32-blocks", cols);
+    if (tile_base_type(type) != type && rows % 8)
+        return fail(QDEC_EINVAL, "rows %d: the tile layout holds a multiple of 8 rows", rows);
     if (is_kquant(type)) {
-        const size_t smem = (size_t)4 * (cols / 256) * 324 + 64;
+        const size_t smem = (size_t)4 * (cols / 256) * 324 + 64;  // the raw-activation kernel stages 4 columns
         if (smem > 220 * 1024) return fail(QDEC_EINVAL, "cols %d too wide for the staged activations", cols);
     }
     return QDEC_OK;
@@ -74,6 +77,39 @@ static int act_buffer(size_t bytes, void **out) {
     }
     *out = g_act.buf[dev];
     return QDEC_OK;
+}
+
+bool uses_image(int type, const void *w_dev) {
+    return gemv_impl() != 2 && v6_gemv_supported(type) && ((uintptr_t)w_dev & 15) == 0;
+}
+
+size_t image_bytes(int cols, int n_cols) { return (size_t)(cols / QK_K) * Q8K_IMG_BYTES * n_cols; }
+
+size_t matvec_scratch_bytes(int type, const void *w_dev, int cols, int n_cols) {
+    if (type == T_F32) return 0;
+    if (uses_image(type, w_dev)) return image_bytes(cols, n_cols);
+    return act_row_bytes(type, cols) * n_cols;
+}
+
+int matvec_run(int type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev, cudaStream_t s,
+               void *scratch, const char *who) {
+    const uint8_t *w = (const uint8_t *)w_dev;
+    cudaError_t e;
+    if (type == T_F32) {
+        e = launch_gemv(type, w, rows, cols, x_dev, n_cols, y_dev, s);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, who);
+    }
+    if (uses_image(type, w_dev)) {
+        e = launch_quantize_q8k_image(x_dev, cols, n_cols, (uint8_t *)scratch, s);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+        e = launch_gemv_img(type, w, rows, cols, scratch, n_cols, y_dev, s, false);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, who);
+    }
+    e = is_kquant(type) ? launch_quantize_q8k(x_dev, cols, n_cols, (uint8_t *)scratch, s)
+                        : launch_quantize_q8_0(x_dev, cols, n_cols, (uint8_t *)scratch, s);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    e = launch_gemv(type, w, rows, cols, scratch, n_cols, y_dev, s);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, who);
 }
 
 }  // namespace qdec
@@ -110,7 +146,18 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
     int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
     if (rc) return rc;
     if (!w_dev || !act_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_gemv: null pointer");
-    cudaError_t e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, act_dev, n_cols, y_dev, (cudaStream_t)stream);
+    if (n_cols == 0 || rows == 0) return QDEC_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (uses_image(ggml_type, w_dev)) {  // rearrange the block_q8_K rows into the image the kernel reads
+        void *img = nullptr;
+        rc = act_buffer(image_bytes(cols, n_cols), &img);
+        if (rc) return rc;
+        cudaError_t e = launch_q8k_raw_to_image((const uint8_t *)act_dev, (long long)n_cols * (cols / QK_K), (uint8_t *)img, s);
+        if (e != cudaSuccess) return cuda_fail(e, "qdec_gemv: activation image");
+        e = launch_gemv_img(ggml_type, (const uint8_t *)w_dev, rows, cols, img, n_cols, y_dev, s, false);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv");
+    }
+    cudaError_t e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, act_dev, n_cols, y_dev, s);
     return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv");
 }
 
@@ -120,34 +167,20 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
     if (rc) return rc;
     if (!w_dev || !x_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_matvec: null pointer");
     if (n_cols == 0) return QDEC_OK;
-    cudaStream_t s = (cudaStream_t)stream;
-    if (ggml_type == T_F32) {
-        cudaError_t e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, x_dev, n_cols, y_dev, s);
-        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec");
-    }
     void *act = nullptr;
-    rc = act_buffer(act_row_bytes(ggml_type, cols) * n_cols, &act);
-    if (rc) return rc;
-    cudaError_t e = is_kquant(ggml_type) ? launch_quantize_q8k(x_dev, cols, n_cols, (uint8_t *)act, s)
-                                         : launch_quantize_q8_0(x_dev, cols, n_cols, (uint8_t *)act, s);
-    if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec: quantise");
-    e = launch_gemv(ggml_type, (const uint8_t *)w_dev, rows, cols, act, n_cols, y_dev, s);
-    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec: gemv");
+    const size_t need = matvec_scratch_bytes(ggml_type, w_dev, cols, n_cols);
+    if (need) {
+        rc = act_buffer(need, &act);
+        if (rc) return rc;
+    }
+    return matvec_run(ggml_type, w_dev, rows, cols, x_dev, n_cols, y_dev, (cudaStream_t)stream, act, "qdec_matvec");
 }
 
-int qdec_tune_gemv_lanes_per_row(int lpr) {
-    if (lpr != 0 && lpr != 1 && lpr != 2 && lpr != 4 && lpr != 8) return fail(QDEC_EINVAL, "lanes per row must be 0, 1, 2, 4 or 8");
-    set_gemv_lanes_per_row(lpr);
-    set_gemv_impl(lpr ? 4 : 0);
-    return QDEC_OK;
-}
-
-int qdec_tune_gemv(int impl, int lanes_per_thread, int depth) {
-    if (impl != 0 && impl != 2 && impl != 4 && impl != 5) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 4 or 5");
-    if (lanes_per_thread < 0 || lanes_per_thread > 2) return fail(QDEC_EINVAL, "lanes per thread must be 0, 1 or 2");
-    if (depth != 0 && depth != 4 && depth != 8) return fail(QDEC_EINVAL, "depth must be 0, 4 or 8");
+int qdec_tune_gemv(int impl, int config) {
+    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2 or 6");
+    if (config < 0 || config > 14) return fail(QDEC_EINVAL, "gemv configuration must be 0..14");
     set_gemv_impl(impl);
-    set_gemv_v5_tuning(lanes_per_thread, depth);
+    set_gemv_v6_config(config);
     return QDEC_OK;
 }
 
@@ -159,9 +192,20 @@ int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void
     return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_repack_q6k");
 }
 
+int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, void *dst_dev, void *stream) {
+    if (ggml_type != T_Q4_K && ggml_type != T_Q5_K && ggml_type != T_Q6_K)
+        return fail(QDEC_EINVAL, "qdec_repack_tiles: type %d has no tile layout", ggml_type);
+    if (!src_dev || !dst_dev || rows < 0 || rows % 8 || cols <= 0 || cols % 256)
+        return fail(QDEC_EINVAL, "qdec_repack_tiles: bad argument (rows %d must be a multiple of 8, cols %d of 256)", rows, cols);
+    if (src_dev == dst_dev) return fail(QDEC_EINVAL, "qdec_repack_tiles: source and destination must differ");
+    if (((uintptr_t)dst_dev & 15) != 0) return fail(QDEC_EINVAL, "qdec_repack_tiles: destination must be 16-byte aligned");
+    cudaError_t e = launch_repack_tiles(ggml_type, (const uint8_t *)src_dev, rows, cols, (uint8_t *)dst_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_repack_tiles");
+}
+
 int qdec_dequant_rows(int ggml_type, const void *w_dev, int rows, int cols, const int32_t *ids_dev, int n_ids,
                       float *out_dev, void *stream) {
-    if (!supported_type(ggml_type) || ggml_type == T_Q6_K_SPLIT || cols <= 0 || cols % block_elems(ggml_type) || rows < 0 || n_ids < 0)
+    if (!supported_type(ggml_type) || ggml_type == T_Q6_K_SPLIT || tile_base_type(ggml_type) != ggml_type || cols <= 0 || cols % block_elems(ggml_type) || rows < 0 || n_ids < 0)
         return fail(QDEC_EINVAL, "qdec_dequant_rows: bad type %d or shape %d x %d", ggml_type, rows, cols);
     if (!w_dev || (!ids_dev && n_ids) || (!out_dev && n_ids)) return fail(QDEC_EINVAL, "qdec_dequant_rows: null pointer");
     const size_t rb = (size_t)(cols / block_elems(ggml_type)) * block_bytes(ggml_type);

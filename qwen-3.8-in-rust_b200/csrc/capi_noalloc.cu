@@ -64,11 +64,9 @@ extern "C" int qdec_matvec_noalloc(int ggml_type, const void* w_dev, int rows, i
     if (!w_dev || !x_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_matvec_noalloc: null pointer");
     if (n_cols == 0) return QDEC_OK;
     cudaStream_t s = (cudaStream_t)stream;
-    if (ggml_type == T_F32) {  // F32 weights take the f32 columns as they are: no scratch
-        cudaError_t e = launch_gemv(ggml_type, (const uint8_t*)w_dev, rows, cols, x_dev, n_cols, y_dev, s);
-        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec_noalloc");
-    }
-    const size_t need = act_row_bytes(ggml_type, cols) * (size_t)n_cols;
+    const size_t need = matvec_scratch_bytes(ggml_type, w_dev, cols, n_cols);
+    if (need == 0)  // F32 weights take the f32 columns as they are: no scratch
+        return matvec_run(ggml_type, w_dev, rows, cols, x_dev, n_cols, y_dev, s, nullptr, "qdec_matvec_noalloc");
     if (need > NOALLOC_SCRATCH_BYTES)
         return fail(QDEC_EINVAL,
                     "qdec_matvec_noalloc: %d columns of %d values need %zu bytes of quantised activations; the fixed "
@@ -77,9 +75,5 @@ extern "C" int qdec_matvec_noalloc(int ggml_type, const void* w_dev, int rows, i
     void* act = nullptr;
     rc = scratch_address(&act);
     if (rc) return rc;
-    cudaError_t e = is_kquant(ggml_type) ? launch_quantize_q8k(x_dev, cols, n_cols, (uint8_t*)act, s)
-                                         : launch_quantize_q8_0(x_dev, cols, n_cols, (uint8_t*)act, s);
-    if (e != cudaSuccess) return cuda_fail(e, "qdec_matvec_noalloc: quantise");
-    e = launch_gemv(ggml_type, (const uint8_t*)w_dev, rows, cols, act, n_cols, y_dev, s);
-    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_matvec_noalloc: gemv");
+    return matvec_run(ggml_type, w_dev, rows, cols, x_dev, n_cols, y_dev, s, act, "qdec_matvec_noalloc");
 }

@@ -12,17 +12,32 @@ namespace qdec {
 
 // ggml tensor type ids (GGUF), the same numbering as crates/core/src/gguf.rs GgmlType.
 enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
-// Q6_K in the engine's split layout: 208-byte blocks [ql | qh | scales], then every block's f16 d (gemv_tma.cu).
+// Q6_K in the split layout: 208-byte blocks [ql | qh | scales], then every block's f16 d (gemv_v6.cu).
 constexpr int T_Q6_K_SPLIT = 114;
+// K-quants in the tile layout of gemv_v6.cu (8 rows x one super-block per tile block; rows % 8 == 0).
+constexpr int T_Q4_K_TILE = 112, T_Q5_K_TILE = 113, T_Q6_K_TILE = 116;
+__host__ __device__ inline int tile_base_type(int t) {
+    return t == T_Q4_K_TILE ? T_Q4_K : t == T_Q5_K_TILE ? T_Q5_K : t == T_Q6_K_TILE ? T_Q6_K : t;
+}
 
 constexpr int QK_K = 256;
 constexpr int Q8K_BLOCK_BYTES = 292;  // f32 d, 256 x i8, 16 x i16 (ggml block_q8_K)
+
+// The engine's device image of one Q8_K block (the GEMV reads it; same values as block_q8_K, rearranged):
+//   [0, 256)   the 256 codes, lane-major: word g*8 + s = codes s*32 + 4g .. +3 (the reference's i32 lane g of
+//              sub-block s), so the reader of lane g loads 32 contiguous bytes
+//   [256, 260) f32 d
+//   [272, 304) 8 x (bsums[2g] | bsums[2g+1] << 16)           -- the Q6_K bsum pairs
+//   [304, 320) 4 x (q8s[2i] | q8s[2i+1] << 16), q8s[j] = bsums[2j] + bsums[2j+1]  -- the Q4_K/Q5_K min pairs
+constexpr int Q8K_IMG_BYTES = 320;
+constexpr int Q8K_IMG_D = 256, Q8K_IMG_BSP = 272, Q8K_IMG_Q8S = 304;
 constexpr int Q8_0_BLOCK_BYTES = 34;  // f16 d, 32 x i8 (ggml block_q8_0)
 
 __host__ __device__ inline int block_elems(int t) {
     return (t == T_F32) ? 1 : (t == T_Q4_0 || t == T_Q8_0) ? 32 : 256;
 }
 __host__ __device__ inline int block_bytes(int t) {
+    t = tile_base_type(t);
     switch (t) {
     case T_F32: return 4;
     case T_Q4_0: return 18;
@@ -34,7 +49,10 @@ __host__ __device__ inline int block_bytes(int t) {
     default: return 0;
     }
 }
-__host__ __device__ inline bool is_kquant(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT; }
+__host__ __device__ inline bool is_kquant(int t) {
+    t = tile_base_type(t);
+    return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT;
+}
 
 // Exact f16 -> f32 (the `half` crate's to_f32; hardware conversion is exact).
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
@@ -68,6 +86,54 @@ __device__ __forceinline__ uint4 ld_nc_u128(const void* p) {
                  : "l"(p));
     return v;
 }
+// One Q8_K block quantised by a warp and written as the device image (layout above); lane i holds values
+// 8i..8i+7.  Bit-exact with crates/core/src/kernels/q8k.rs:76-114 (the first element of largest |x| sets the
+// scale; iscale = -127 / max; q = min(127, round_ties_even(iscale * x)); d = 1 / iscale; bsums per 16).
+__device__ __forceinline__ void q8k_quantize_to_image(const float (&v)[8], uint8_t* __restrict__ img) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.0f, mx = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float a = fabsf(v[i]);
+        if (a > amax) amax = a, mx = v[i], idx = lane * 8 + i;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+        const float om = __shfl_xor_sync(0xffffffffu, mx, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) amax = oa, mx = om, idx = oi;
+    }
+    uint32_t* ow = reinterpret_cast<uint32_t*>(img);
+    if (amax == 0.0f) {  // d = 0, codes 0, sums 0 (q8k.rs:96-101)
+        for (int w = lane; w < Q8K_IMG_BYTES / 4; w += 32) ow[w] = 0u;
+        return;
+    }
+    const float iscale = __fdiv_rn(-127.0f, mx);
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int qi = __float2int_rn(__fmul_rn(iscale, v[i]));
+        q[i] = qi > 127 ? 127 : qi;
+    }
+    // lane i holds sub-block s = i / 4, positions (i % 4) * 8 .. +7 = reference lanes g = 2(i%4), 2(i%4)+1
+    const int s = lane >> 2, g = 2 * (lane & 3);
+    ow[g * 8 + s] = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    ow[(g + 1) * 8 + s] = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    int sum8 = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+    const int bsum = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);   // bsums[lane / 2]
+    const int bsum_hi = __shfl_down_sync(0xffffffffu, bsum, 2);      // at lane 4g': bsums[2g'+1]
+    const int q8s = (int)(int16_t)(bsum + bsum_hi);                    // at lane 4j: q8s[j]
+    const int q8s_hi = __shfl_down_sync(0xffffffffu, q8s, 4);         // at lane 8i: q8s[2i+1]
+    if ((lane & 3) == 0) ow[Q8K_IMG_BSP / 4 + (lane >> 2)] = (uint32_t)(bsum & 0xffff) | ((uint32_t)(bsum_hi & 0xffff) << 16);
+    if ((lane & 7) == 0) ow[Q8K_IMG_Q8S / 4 + (lane >> 3)] = (uint32_t)(q8s & 0xffff) | ((uint32_t)(q8s_hi & 0xffff) << 16);
+    if (lane == 0) {
+        ow[Q8K_IMG_D / 4] = __float_as_uint(__fdiv_rn(1.0f, iscale));
+        ow[Q8K_IMG_D / 4 + 1] = ow[Q8K_IMG_D / 4 + 2] = ow[Q8K_IMG_D / 4 + 3] = 0u;
+    }
+}
+
 __device__ __forceinline__ uint16_t ld_nc_u16(const void* p) {
     uint16_t v;
     asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));

@@ -42,6 +42,38 @@ __global__ void add_rows_kernel(const float* a, const float* b, float* out, size
         out[i] = __fadd_rn(a[i], b[i]);
 }
 
+// Greedy acceptance of a verify batch on the device (spec.rs:352-366): m = the longest prefix where the model's
+// argmax equals the draft (vids[1 + i] is draft i); the emitted ids are argmax[0..m] (m + 1 of them).  Then the
+// rollback bookkeeping of spec.rs:368-415: the DeltaNet layers will commit `keep` = m + 1 rows, the position
+// advances by keep, the MTP is truncated to the round's start p and re-fed the kept rows (MTP positions
+// p..p+k, rows past keep are scratch that later rows overwrite before anything reads them), then chained at
+// p + keep + i - 1 for draft i + 1.  emit = {keep, emitted ids...}.
+__global__ void spec_accept_kernel(const int32_t* __restrict__ argmax, const int32_t* __restrict__ vids, int k, int* pos,
+                                   int* keep_out, int* mpos, int32_t* mids, int* sel, int32_t* emit) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int m = 0;
+    while (m < k && argmax[m] == vids[1 + m]) m++;
+    const int keep = m + 1;
+    const int p = *pos;
+    emit[0] = keep;
+    for (int i = 0; i <= k; i++) {
+        const int32_t a = i < keep ? argmax[i] : argmax[keep - 1];
+        if (i < keep) emit[1 + i] = a;
+        mids[i] = a;  // MTP re-feed tokens (rows past keep: any valid id)
+    }
+    *keep_out = keep;
+    *pos = p + keep;
+    mpos[0] = p;
+    for (int i = 1; i < k; i++) mpos[i] = p + keep + i - 1;
+    *sel = keep - 1;
+}
+
+// dst[0..n) = src rows[*sel][0..n)
+__global__ void select_row_kernel(const float* __restrict__ src, const int* __restrict__ sel, int n, float* __restrict__ dst) {
+    const float* r = src + (size_t)(*sel) * n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = r[i];
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------ Model
@@ -104,18 +136,27 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         cudaStreamDestroy(s);
     }
     auto ptr = [&](const TensorInfo& t) { return m->blob_ + t.rel_offset; };
-    // Q6_K matrices are repacked in place into the split layout the bulk-copy GEMV reads (same bytes); the
-    // embedding table keeps the ggml layout because rows of it are dequantised directly
+    // K-quant matrices are repacked in place (same bytes) into the tile layout the GEMV streams (rows % 8 == 0),
+    // else Q6_K into the split layout; the embedding table keeps the ggml layout because rows of it are
+    // dequantised directly
     uint8_t* repack_tmp = nullptr;
     uint64_t repack_cap = 0;
     for (const TensorInfo& t : g.tensors())
-        if (t.type == T_Q6_K && t.name != "token_embd.weight") repack_cap = std::max(repack_cap, t.byte_size);
+        if (is_kquant(t.type) && t.name != "token_embd.weight") repack_cap = std::max(repack_cap, t.byte_size);
     if (repack_cap) ck(cudaMalloc(&repack_tmp, repack_cap), "repack buffer");
-    auto repack = [&](const TensorInfo& t) {
+    auto repack = [&](const TensorInfo& t, int rows, int cols) -> int {
         uint8_t* p = m->blob_ + t.rel_offset;
         ck(cudaMemcpy(repack_tmp, p, t.byte_size, cudaMemcpyDeviceToDevice), "repack copy");
-        ck(launch_repack_q6k(repack_tmp, t.byte_size / 210, p, 0), "repack");
+        int type = t.type;
+        if (rows % 8 == 0 && ((uintptr_t)p & 15) == 0) {
+            ck(launch_repack_tiles(t.type, repack_tmp, rows, cols, p, 0), "repack");
+            type = t.type == T_Q4_K ? T_Q4_K_TILE : t.type == T_Q5_K ? T_Q5_K_TILE : T_Q6_K_TILE;
+        } else if (t.type == T_Q6_K) {
+            ck(launch_repack_q6k(repack_tmp, t.byte_size / 210, p, 0), "repack");
+            type = T_Q6_K_SPLIT;
+        }
         ck(cudaDeviceSynchronize(), "repack");
+        return type;
     };
     auto mat = [&](const std::string& name, uint64_t rows, uint64_t cols) {
         const TensorInfo& t = g.tensor(name);
@@ -130,10 +171,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         d.cols = (int)cols;
         d.p = ptr(t);
         d.bytes = t.byte_size;
-        if (t.type == T_Q6_K && name != "token_embd.weight") {
-            repack(t);
-            d.type = T_Q6_K_SPLIT;
-        }
+        if (is_kquant(t.type) && name != "token_embd.weight") d.type = repack(t, (int)rows, (int)cols);
         return d;
     };
     auto vec = [&](const std::string& name, uint64_t len) -> const float* {
@@ -191,9 +229,11 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     // RoPE tables (rope.rs:10-29): inv_freq[i] = 1 / theta^(2i / rope_dim) in f32, angle = f32(pos) * inv_freq,
     // cos/sin in f32, each half duplicated -- computed on the host with the C library, like the reference
     const int rd = (int)c.rope_dim, half = rd / 2;
-    std::vector<float> inv(half), cs((size_t)opt.max_pos * rd), sn((size_t)opt.max_pos * rd);
+    // (ROPE_SLACK extra positions: the MTP rows of a speculative round run up to 2k past the sequence end)
+    const int npos = opt.max_pos + ROPE_SLACK;
+    std::vector<float> inv(half), cs((size_t)npos * rd), sn((size_t)npos * rd);
     for (int i = 0; i < half; i++) inv[i] = 1.0f / powf(c.rope_freq_base, (float)(2 * i) / (float)rd);
-    for (int pos = 0; pos < opt.max_pos; pos++) {
+    for (int pos = 0; pos < npos; pos++) {
         const float pf = (float)pos;
         for (int i = 0; i < half; i++) {
             const float a = pf * inv[i];
@@ -235,20 +275,24 @@ void* State::dalloc(size_t bytes) {
 State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(spec_k), max_pos_(max_pos) {
     const ModelConfig& c = m.cfg;
     if (max_pos > m.max_pos) throw std::invalid_argument("max_pos exceeds the model's RoPE table");
+    if (spec_k < 0 || 2 * spec_k + 2 > ROPE_SLACK) throw std::invalid_argument("spec_k out of range");
+    mtp_cap_ = max_pos + 2 * spec_k + 2;
     if (spec_k > 0 && !m.has_mtp) throw std::invalid_argument("the GGUF has no MTP block (no nextn tensors): speculative decoding needs one");
     T_ = std::max(max_rows, spec_k + 1);
     ck(cudaSetDevice(m.device), "cudaSetDevice");
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
     const size_t H = c.hidden_size, FF = c.intermediate_size, T = T_;
     size_t maxw = std::max<size_t>(std::max<size_t>(2 * H, FF), std::max<size_t>(c.dn_v_dim, (size_t)c.n_head * c.head_dim_k));
-    q8k_stride_ = maxw / 256 * 292 + 64;
+    q8k_stride_ = maxw / 256 * Q8K_IMG_BYTES;  // the Q8_K device image
     q80_stride_ = maxw / 32 * 34 + 64;
     d_ids = (int32_t*)dalloc(T * 4);
     d_argmax = (int32_t*)dalloc(T * 4);
     d_pos = (int*)dalloc(4);
     d_keep = (int*)dalloc(4);
     d_mtp_pos = (int*)dalloc(4);
+    amx_scratch_ = dalloc(argmax_scratch_bytes((int)c.vocab_size, (int)T));  // zero-filled by dalloc
     h_ = (float*)dalloc(T * H * 4);
+    h_alt_ = (float*)dalloc(T * H * 4);
     embed_ = (float*)dalloc(T * H * 4);
     normed_ = (float*)dalloc(T * maxw * 4);
     mix_out_ = (float*)dalloc(T * H * 4);
@@ -291,7 +335,13 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
         }
     }
     if (m.has_mtp) {
-        mtp_kv_ = {(float*)dalloc((size_t)max_pos * kvd * 4), (float*)dalloc((size_t)max_pos * kvd * 4)};
+        mtp_kv_ = {(float*)dalloc((size_t)mtp_cap_ * kvd * 4), (float*)dalloc((size_t)mtp_cap_ * kvd * 4)};
+        d_vids = (int32_t*)dalloc(T * 4);
+        d_mids = (int32_t*)dalloc(T * 4);
+        d_mpos = (int*)dalloc(T * 4);
+        d_sel = (int*)dalloc(4);
+        d_emit = (int32_t*)dalloc((T + 2) * 4);
+        ck(cudaMallocHost(&h_io_, 64 * 4), "pinned round buffer");
         cat_ = (float*)dalloc(T * 2 * H * 4);
         mtp_h_ = (float*)dalloc(T * H * 4);
         mtp_hout_ = (float*)dalloc(T * H * 4);
@@ -301,6 +351,8 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
 
 State::~State() {
     if (stream) cudaStreamSynchronize(stream);
+    if (round_exec_) cudaGraphExecDestroy(round_exec_);
+    if (h_io_) cudaFreeHost(h_io_);
     for (void* p : allocs_) cudaFree(p);
     for (float* p : capture_h_) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
@@ -328,10 +380,27 @@ static bool needs_q80(std::initializer_list<int> ts) {
 }
 
 void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y) {
-    const void* act = is_kquant(w.type) ? (const void*)q8k_ : (w.type == T_F32 ? (const void*)normed_f32 : (const void*)q80_);
     // activation rows are laid out back to back at the stride of this weight's width
-    // weights are written once at load, so the GEMV may stream them before its predecessor finishes
-    ck(launch_gemv(w.type, w.p, w.rows, w.cols, act, rows, y, stream, true), "gemv");
+    if (is_kquant(w.type)) {
+        // weights are written once at load, so the GEMV may stream them before its predecessor finishes
+        count_launch((rows + 3) / 4);
+        ck(launch_gemv_img(w.type, w.p, w.rows, w.cols, q8k_, rows, y, stream, true), "gemv");
+        return;
+    }
+    const void* act = w.type == T_F32 ? (const void*)normed_f32 : (const void*)q80_;
+    count_launch((rows + 3) / 4);
+    ck(launch_gemv(w.type, w.p, w.rows, w.cols, act, rows, y, stream), "gemv");
+}
+
+// h = h + delta (delta null: h as it is) into the other residual buffer, normed and quantised on the way.
+void State::resid_norm(const float* delta, const float* w, int t, float* y_out, bool k8, bool k0) {
+    const ModelConfig& c = m_.cfg;
+    const int H = (int)c.hidden_size;
+    count_launch();
+    ck(launch_resid_norm_quant(h_, delta, delta ? h_alt_ : nullptr, w, c.rms_norm_eps, H, t, y_out, k8 ? q8k_ : nullptr,
+                               k0 ? q80_ : nullptr, stream),
+       "rmsnorm");
+    if (delta) std::swap(h_, h_alt_);
 }
 
 void State::quant_for(int type, const float* x, int n, int rows) {
@@ -347,15 +416,15 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     const float eps = c.rms_norm_eps;
     if (L.attn) {
         const bool k8 = needs_q8k({L.q.type, L.k.type, L.v.type}), k0 = needs_q80({L.q.type, L.k.type, L.v.type});
-        count_launch(); ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
-                                   k0 ? q80_ : nullptr, stream), "attn_norm");
+        resid_norm(li == 0 ? nullptr : mlp_out_, L.attn_norm, t, normed_, k8, k0);
         gemv(L.q, normed_, t, qg_);
         gemv(L.k, normed_, t, kk_);
         gemv(L.v, normed_, t, vv_);
         QkArgs qa{qg_, kk_, vv_, L.q_norm, L.k_norm, m_.rope_cos, m_.rope_sin, pos_dev, qr_, gate_, kv->k, kv->v,
                   (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k, (int)c.rope_dim, eps};
         count_launch(); ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
-        AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k, max_pos_,
+        AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k,
+                    kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
                     m_.attn_scaling};
         count_launch(); ck(launch_attention(aa, t, stream), "attention");
         quant_for(L.o.type, attn_, L.o.cols, t);
@@ -364,8 +433,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         const DnState& d = dn_[li];
         const bool k8 = needs_q8k({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
         const bool k0 = needs_q80({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
-        count_launch(); ck(launch_resid_norm_quant(h_, li == 0 ? nullptr : mlp_out_, h_, L.attn_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr,
-                                   k0 ? q80_ : nullptr, stream), "attn_norm");
+        resid_norm(li == 0 ? nullptr : mlp_out_, L.attn_norm, t, normed_, k8, k0);
         gemv(L.qkv, normed_, t, qkv_);
         gemv(L.gate_z, normed_, t, z_);
         gemv(L.alpha, normed_, t, alpha_);
@@ -381,8 +449,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     }
     // h = x + mixer(x); then the MLP on post_attention_norm(h) (mlp.rs:53-64)
     const bool k8 = needs_q8k({L.ffn_gate.type, L.ffn_up.type}), k0 = needs_q80({L.ffn_gate.type, L.ffn_up.type});
-    count_launch(); ck(launch_resid_norm_quant(h_, mix_out_, h_, L.post_norm, eps, H, t, normed_, k8 ? q8k_ : nullptr, k0 ? q80_ : nullptr, stream),
-       "post_attention_norm");
+    resid_norm(mix_out_, L.post_norm, t, normed_, k8, k0);
     gemv(L.ffn_gate, normed_, t, g_);
     gemv(L.ffn_up, normed_, t, u_);
     const int dt = L.ffn_down.type;
@@ -391,10 +458,10 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     gemv(L.ffn_down, g_, t, mlp_out_);
 }
 
-void State::forward_rows(int t, bool want_logits_all) {
+void State::forward_rows(int t, const int32_t* ids_dev, bool want_logits_all) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
-    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, h_, stream), "embed");
+    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, ids_dev, t, h_, stream), "embed");
     for (size_t li = 0; li < m_.layers.size(); li++) {
         layer_forward(m_.layers[li], (int)li, t, &kv_[li], d_pos, true);
         if (capture_) {
@@ -407,18 +474,17 @@ void State::forward_rows(int t, bool want_logits_all) {
     }
     // final norm (model.rs:430-438): the post-norm rows are what the lm_head and the MTP read
     const int ht = m_.lm_head.type;
-    count_launch(); ck(launch_resid_norm_quant(h_, mlp_out_, h_, m_.output_norm, c.rms_norm_eps, H, t, final_, is_kquant(ht) ? q8k_ : nullptr,
-                               (ht == T_Q8_0 || ht == T_Q4_0) ? q80_ : nullptr, stream), "output_norm");
+    resid_norm(mlp_out_, m_.output_norm, t, final_, is_kquant(ht), ht == T_Q8_0 || ht == T_Q4_0);
     if (capture_ && !capture_h_.empty())
         ck(cudaMemcpyAsync(capture_h_[m_.layers.size()], final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "capture");
     if (want_logits_all) {
         gemv(m_.lm_head, final_, t, logits_);
-        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, t, d_argmax, stream), "argmax");
+        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, t, d_argmax, amx_scratch_, stream), "argmax");
     } else {
         // only the last row's logits (prefill): quantise that row alone at row 0
         quant_for(ht, final_ + (size_t)(t - 1) * H, H, 1);
         gemv(m_.lm_head, final_ + (size_t)(t - 1) * H, 1, logits_);
-        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, 1, d_argmax, stream), "argmax");
+        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, 1, d_argmax, amx_scratch_, stream), "argmax");
     }
 }
 
@@ -434,10 +500,11 @@ uint32_t State::prefill(const uint32_t* ids, int n) {
         const int t = std::min(T_, n - off);
         upload_ids(ids + off, t);
         set_dev_int(d_pos, pos_, stream);
-        forward_rows(t, false);
+        forward_rows(t, d_ids, false);
         set_dev_int(d_keep, t, stream);  // every row of a prefill chunk is kept
         pos_ += t;
     }
+    set_dev_int(d_pos, pos_, stream);
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
     sync();
@@ -448,9 +515,10 @@ uint32_t State::step(uint32_t id, float* logits) {
     if (pos_ + 1 > max_pos_) throw std::invalid_argument("step: the sequence would exceed max_pos");
     upload_ids(&id, 1);
     set_dev_int(d_pos, pos_, stream);
-    forward_rows(1, true);
+    forward_rows(1, d_ids, true);
     set_dev_int(d_keep, 1, stream);
     pos_ += 1;
+    set_dev_int(d_pos, pos_, stream);
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
     if (logits) ck(cudaMemcpyAsync(logits, logits_, (size_t)m_.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, stream), "logits");
@@ -468,50 +536,40 @@ void State::debug_hidden(int layer, int row, float* out) {
     ck(cudaMemcpy(out, capture_h_[layer] + (size_t)row * m_.cfg.hidden_size, m_.cfg.hidden_size * 4, cudaMemcpyDeviceToHost), "capture");
 }
 
-// The MTP block over t rows at MTP positions mtp_len_.. (layers/mtp.rs:95-130): row i is
-// [rmsnorm(embed(tokens[i]), enorm) | rmsnorm(hidden[i], hnorm)] -> eh_proj -> one attention decoder layer with
-// its own KV cache -> shared_head_norm, into mtp_hout_.
-void State::mtp_rows(int t, const uint32_t* tokens, const float* hidden, bool hidden_is_hout) {
+// The MTP block over t rows (layers/mtp.rs:95-130): row i is [rmsnorm(embed(ids[i]), enorm) |
+// rmsnorm(hidden[i], hnorm)] -> eh_proj -> one attention decoder layer with its own KV cache at MTP positions
+// *pos_dev + i -> shared_head_norm, into mtp_hout_.
+void State::mtp_rows(int t, const int32_t* ids_dev, const float* hidden, const int* pos_dev) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     const MtpW& M = m_.mtp;
-    (void)hidden_is_hout;
-    upload_ids(tokens, t);
-    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, d_ids, t, embed_, stream), "embed");
+    count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, ids_dev, t, embed_, stream), "embed");
     count_launch(); ck(launch_rmsnorm_rows(embed_, H, M.enorm, c.rms_norm_eps, H, t, cat_, 2 * H, stream), "enorm");
     count_launch(); ck(launch_rmsnorm_rows(hidden, H, M.hnorm, c.rms_norm_eps, H, t, cat_ + H, 2 * H, stream), "hnorm");
     quant_for(M.eh_proj.type, cat_, 2 * H, t);
     gemv(M.eh_proj, cat_, t, h_);  // u rows become the block's residual input
-    set_dev_int(d_mtp_pos, mtp_len_, stream);
-    layer_forward(M.block, 0, t, &mtp_kv_, d_mtp_pos, false);
-    count_launch(); ck(launch_resid_norm_quant(h_, mlp_out_, h_, M.head_norm, c.rms_norm_eps, H, t, mtp_hout_, nullptr, nullptr, stream), "head_norm");
-    mtp_len_ += t;
+    layer_forward(M.block, 0, t, &mtp_kv_, pos_dev, false);
+    resid_norm(mlp_out_, M.head_norm, t, mtp_hout_, false, false);
 }
 
-// The draft of MTP row `row`: the shared lm_head on mtp_hout_[row], greedy (spec.rs:205-215, mtp.rs:132-137).
-uint32_t State::mtp_draft_from_row(int row) {
+// The draft of the MTP row held in mtp_h_: the shared lm_head, greedy (spec.rs:205-215, mtp.rs:132-137).
+void State::enqueue_draft(int32_t* out_dev) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
-    quant_for(m_.lm_head.type, mtp_hout_ + (size_t)row * H, H, 1);
-    gemv(m_.lm_head, mtp_hout_ + (size_t)row * H, 1, logits_ + (size_t)(T_ - 1) * c.vocab_size);
-    count_launch(); ck(launch_argmax(logits_ + (size_t)(T_ - 1) * c.vocab_size, (int)c.vocab_size, 1, d_argmax + (T_ - 1), stream), "argmax");
-    int32_t a = 0;
-    ck(cudaMemcpyAsync(&a, d_argmax + (T_ - 1), 4, cudaMemcpyDeviceToHost, stream), "argmax");
-    sync();
-    return (uint32_t)a;
+    float* lg = logits_ + (size_t)(T_ - 1) * c.vocab_size;
+    quant_for(m_.lm_head.type, mtp_h_, H, 1);
+    gemv(m_.lm_head, mtp_h_, 1, lg);
+    count_launch(); ck(launch_argmax(lg, (int)c.vocab_size, 1, out_dev, amx_scratch_, stream), "argmax");
 }
 
-// Drafts from..k-1 by chaining single MTP rows from the previous row's hidden (spec.rs:205-222).
-void State::chain_drafts(int from) {
+// Drafts from..k-1 by chaining single MTP rows (spec.rs:205-222): draft i comes from the MTP row of token
+// draft i-1 (d_vids[i]) and the previous MTP row's post-norm hidden (mtp_h_), at MTP position d_mpos[i].
+void State::enqueue_chain(int from) {
     const int H = (int)m_.cfg.hidden_size;
     for (int i = from; i < k_; i++) {
-        const uint32_t last = drafts_[i - 1];
-        // hprev = the previous MTP row's post-norm hidden, which the last call left in mtp_hout_[prev]; copy it
-        // aside since this row's output overwrites mtp_hout_
-        ck(cudaMemcpyAsync(mtp_h_, mtp_hout_ + (size_t)prev_row_ * H, (size_t)H * 4, cudaMemcpyDeviceToDevice, stream), "hprev");
-        mtp_rows(1, &last, mtp_h_, true);
-        prev_row_ = 0;
-        drafts_.push_back(mtp_draft_from_row(0));
+        mtp_rows(1, d_vids + i, mtp_h_, d_mpos + i);
+        ck(cudaMemcpyAsync(mtp_h_, mtp_hout_, (size_t)H * 4, cudaMemcpyDeviceToDevice, stream), "hprev");
+        enqueue_draft(d_vids + 1 + i);
     }
 }
 
@@ -520,6 +578,8 @@ uint32_t State::spec_prefill(const uint32_t* ids, int n) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     const int p = pos_;
+    if (n <= 0) throw std::invalid_argument("spec_prefill: empty prompt");
+    if (p + n > max_pos_) throw std::invalid_argument("spec_prefill: the sequence would exceed max_pos");
     if (mtp_len_ < p) throw std::logic_error("spec_prefill: the MTP has fewer rows than consumed positions");
     // the prompt's post-final-norm rows, kept for the MTP rows (x_{j+1}, h_j)
     float* normed_all = nullptr;
@@ -530,7 +590,7 @@ uint32_t State::spec_prefill(const uint32_t* ids, int n) {
             const int t = std::min(T_, n - off);
             upload_ids(ids + off, t);
             set_dev_int(d_pos, pos_, stream);
-            forward_rows(t, false);
+            forward_rows(t, d_ids, false);
             set_dev_int(d_keep, t, stream);
             pos_ += t;
             ck(cudaMemcpyAsync(normed_all + (size_t)off * H, final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "rows");
@@ -539,78 +599,122 @@ uint32_t State::spec_prefill(const uint32_t* ids, int n) {
         ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
         sync();
         x_t = (uint32_t)a;
-        mtp_len_ = p;
-        std::vector<uint32_t> xs(n);
-        for (int j = 0; j < n; j++) xs[j] = (j + 1 < n) ? ids[j + 1] : x_t;
+        // MTP rows (x_{j+1}, h_j) at MTP positions p + j (spec.rs:241-262), chunks of T_ rows
+        std::vector<int32_t> xs(n), mp(T_);
+        for (int j = 0; j < n; j++) xs[j] = (int32_t)((j + 1 < n) ? ids[j + 1] : x_t);
         for (int off = 0; off < n; off += T_) {
             const int t = std::min(T_, n - off);
-            mtp_rows(t, xs.data() + off, normed_all + (size_t)off * H, false);
-            prev_row_ = t - 1;
+            mp[0] = p + off;
+            ck(cudaMemcpy(d_mids, xs.data() + off, (size_t)t * 4, cudaMemcpyHostToDevice), "mtp ids");
+            ck(cudaMemcpy(d_mpos, mp.data(), 4, cudaMemcpyHostToDevice), "mtp pos");
+            mtp_rows(t, d_mids, normed_all + (size_t)off * H, d_mpos);
+            if (off + t == n) ck(cudaMemcpyAsync(mtp_h_, mtp_hout_ + (size_t)(t - 1) * H, (size_t)H * 4, cudaMemcpyDeviceToDevice, stream), "hlast");
+            sync();
         }
+        // the first draft from the last prompt row, then the chain at p + n, p + n + 1, ...
+        enqueue_draft(d_vids + 1);
+        for (int i = 1; i < k_; i++) mp[i] = p + n + i - 1;
+        ck(cudaMemcpyAsync(d_mpos, mp.data(), (size_t)T_ * 4, cudaMemcpyHostToDevice, stream), "mtp pos");
+        enqueue_chain(1);
+        set_dev_int(d_pos, pos_, stream);  // the device position the next round starts from
+        sync();
     } catch (...) {
         cudaStreamSynchronize(stream);
         cudaFree(normed_all);
         throw;
     }
-    cudaStreamSynchronize(stream);
     cudaFree(normed_all);
-    drafts_.clear();
-    drafts_.push_back(mtp_draft_from_row(prev_row_));
-    chain_drafts(1);
+    mtp_len_ = p + n + k_ - 1;
+    drafts_ready_ = true;
     return x_t;
+}
+
+void State::enqueue_round() {
+    const ModelConfig& c = m_.cfg;
+    const int H = (int)c.hidden_size;
+    const int t = k_ + 1;
+    ck(cudaMemcpyAsync(d_vids, h_io_, 4, cudaMemcpyHostToDevice, stream), "x_p");
+    forward_rows(t, d_vids, true);  // the verify batch: x_p, d_1..d_k
+    count_launch();
+    spec_accept_kernel<<<1, 32, 0, stream>>>(d_argmax, d_vids, k_, d_pos, d_keep, d_mpos, d_mids, d_sel, d_emit);
+    ck(cudaGetLastError(), "accept");
+    // the MTP re-feed: all t rows (rows past keep are scratch; their cache slots are rewritten before any read)
+    mtp_rows(t, d_mids, final_, d_mpos);
+    count_launch();
+    select_row_kernel<<<8, 256, 0, stream>>>(mtp_hout_, d_sel, H, mtp_h_);
+    ck(cudaGetLastError(), "select row");
+    enqueue_draft(d_vids + 1);
+    enqueue_chain(1);
+    ck(cudaMemcpyAsync(h_io_ + 16, d_emit, (size_t)(k_ + 2) * 4, cudaMemcpyDeviceToHost, stream), "emitted");
 }
 
 int State::spec_round(uint32_t x_p, uint32_t* out) {
     if (k_ <= 0) throw std::invalid_argument("spec_round: state without spec buffers");
-    if ((int)drafts_.size() != k_) throw std::logic_error("spec_round: drafts missing (call spec_prefill first)");
+    if (!drafts_ready_) throw std::logic_error("spec_round: drafts missing (call spec_prefill first)");
     const int t = k_ + 1;
     const int p = pos_;
     if (p + t > max_pos_) throw std::invalid_argument("spec_round: the sequence would exceed max_pos");
     if (mtp_len_ != p + k_ - 1) throw std::logic_error("spec_round: MTP rows out of step with the position");
-    std::vector<uint32_t> batch(t);
-    batch[0] = x_p;
-    for (int i = 0; i < k_; i++) batch[i + 1] = drafts_[i];
-    upload_ids(batch.data(), t);
-    set_dev_int(d_pos, p, stream);
-    forward_rows(t, true);  // the verify batch
-    std::vector<int32_t> am(t);
-    ck(cudaMemcpyAsync(am.data(), d_argmax, (size_t)t * 4, cudaMemcpyDeviceToHost, stream), "argmax");
-    sync();
-    // greedy accept (spec.rs:352-366): the longest prefix where the model's argmax equals the draft
-    int m = 0;
-    std::vector<uint32_t> emitted;
-    while (m < k_) {
-        const uint32_t a = (uint32_t)am[m];
-        emitted.push_back(a);
-        if (a != drafts_[m]) break;
-        m++;
+    if (x_p >= m_.cfg.vocab_size) throw std::invalid_argument("spec_round: token id outside the vocabulary");
+    h_io_[0] = (int32_t)x_p;
+    if (capture_) {
+        enqueue_round();  // debugging captures allocate and copy per layer: run the round eagerly
+    } else {
+        if (!round_exec_) {
+            const uint64_t before = launches_;
+            cudaGraph_t g = nullptr;
+            ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "round capture");
+            try {
+                enqueue_round();
+            } catch (...) {
+                cudaStreamEndCapture(stream, &g);
+                if (g) cudaGraphDestroy(g);
+                throw;
+            }
+            ck(cudaStreamEndCapture(stream, &g), "round capture");
+            cudaError_t e = cudaGraphInstantiate(&round_exec_, g, 0);
+            cudaGraphDestroy(g);
+            ck(e, "round graph");
+            round_launches_ = launches_ - before;
+            launches_ = before;
+        }
+        ck(cudaGraphLaunch(round_exec_, stream), "round");
+        launches_ += round_launches_;
     }
-    if (m == k_) emitted.push_back((uint32_t)am[k_]);
-    const int keep = m + 1;
-    // roll back: the DeltaNet layers will commit `keep` rows; the KV caches end at p + keep
-    set_dev_int(d_keep, keep, stream);
+    sync();
+    const int keep = h_io_[16];
+    if (keep < 1 || keep > t) throw std::runtime_error("spec_round: device acceptance returned an invalid count");
+    for (int i = 0; i < keep; i++) out[i] = (uint32_t)h_io_[17 + i];
     pos_ = p + keep;
+    mtp_len_ = p + keep + k_ - 1;
     counters.rounds++;
     counters.drafted += k_;
-    counters.accepted += m;
+    counters.accepted += keep - 1;
     counters.emitted += keep;
-    counters.hist[m]++;
-    // the MTP: forget its draft rows, feed the accepted pairs (emitted_i, normed_i), draft the next round
-    mtp_len_ = p;
-    mtp_rows(keep, emitted.data(), final_, false);
-    prev_row_ = keep - 1;
-    drafts_.clear();
-    drafts_.push_back(mtp_draft_from_row(prev_row_));
-    chain_drafts(1);
-    for (int i = 0; i < keep; i++) out[i] = emitted[i];
+    counters.hist[keep - 1]++;
     return keep;
 }
 
 void State::set_drafts(const uint32_t* d, int k) {
     if (k != k_) throw std::invalid_argument("set_drafts: wrong number of drafts");
-    for (int i = 0; i < k; i++)
+    if (!drafts_ready_) throw std::logic_error("set_drafts: no round pending (call spec_prefill first)");
+    std::vector<int32_t> v(k);
+    for (int i = 0; i < k; i++) {
         if (d[i] >= m_.cfg.vocab_size) throw std::invalid_argument("set_drafts: draft outside the vocabulary");
-    drafts_.assign(d, d + k);
+        v[i] = (int32_t)d[i];
+    }
+    ck(cudaStreamSynchronize(stream), "sync");
+    ck(cudaMemcpy(d_vids + 1, v.data(), (size_t)k * 4, cudaMemcpyHostToDevice), "drafts");
+}
+
+std::vector<uint32_t> State::drafts() const {
+    std::vector<uint32_t> out;
+    if (!drafts_ready_ || k_ <= 0) return out;
+    std::vector<int32_t> v(k_);
+    ck(cudaStreamSynchronize(stream), "sync");
+    ck(cudaMemcpy(v.data(), d_vids + 1, (size_t)k_ * 4, cudaMemcpyDeviceToHost), "drafts");
+    for (int x : v) out.push_back((uint32_t)x);
+    return out;
 }
 
 }  // namespace qdec

@@ -41,6 +41,10 @@ struct MtpW {  // layers/mtp.rs:1-90
     const float *enorm = nullptr, *hnorm = nullptr, *head_norm = nullptr;
 };
 
+// RoPE positions past max_pos that the tables cover: a speculative round's MTP rows run up to 2k + 1 past the
+// sequence position (its scratch re-feed rows and chained drafts).
+constexpr int ROPE_SLACK = 64;
+
 struct LoadOptions {
     int device = 0;
     int max_pos = 4096;  // RoPE table length
@@ -93,7 +97,7 @@ class State {
     int spec_round(uint32_t x_p, uint32_t* out);
     // forced drafts for the next round (spec.rs:439-452, used by the identity tests)
     void set_drafts(const uint32_t* d, int k);
-    const std::vector<uint32_t>& drafts() const { return drafts_; }
+    std::vector<uint32_t> drafts() const;
 
     // debugging / parity: the residual stream after layer `layer` of the last forward's row `row`
     // (layer = n_layer: the post-final-norm row the lm_head read)
@@ -110,19 +114,27 @@ class State {
 
   private:
     const Model& m_;
-    int k_, max_pos_, T_;
-    int pos_ = 0, mtp_len_ = 0, prev_row_ = 0;
+    int k_, max_pos_, T_, mtp_cap_ = 0;
+    int pos_ = 0, mtp_len_ = 0;
     bool capture_ = false;
+    bool drafts_ready_ = false;
     uint64_t launches_ = 0;  // kernels this state has launched
-    void count_launch() { launches_++; }
-    std::vector<uint32_t> drafts_;
+    void count_launch(uint64_t n = 1) { launches_ += n; }
+    // the speculative round as one CUDA graph (captured on first use)
+    cudaGraphExec_t round_exec_ = nullptr;
+    uint64_t round_launches_ = 0;
+    int32_t* h_io_ = nullptr;  // pinned: [0] x_p in; [16..] {keep, emitted ids} out
     std::vector<void*> allocs_;
     void* dalloc(size_t bytes);
 
     // device buffers
     int32_t *d_ids = nullptr, *d_argmax = nullptr;
+    // speculative round: verify ids (x_p, drafts), MTP re-feed ids, MTP positions, selected row, emitted ids
+    int32_t *d_vids = nullptr, *d_mids = nullptr, *d_emit = nullptr;
+    int *d_mpos = nullptr, *d_sel = nullptr;
     int *d_pos = nullptr, *d_keep = nullptr, *d_mtp_pos = nullptr;
-    float *h_ = nullptr, *embed_ = nullptr, *normed_ = nullptr, *mix_out_ = nullptr, *mlp_out_ = nullptr;
+    void* amx_scratch_ = nullptr;  // argmax partials and counters
+    float *h_ = nullptr, *h_alt_ = nullptr, *embed_ = nullptr, *normed_ = nullptr, *mix_out_ = nullptr, *mlp_out_ = nullptr;
     uint8_t *q8k_ = nullptr, *q80_ = nullptr;
     float *qkv_ = nullptr, *conved_ = nullptr, *z_ = nullptr, *alpha_ = nullptr, *beta_ = nullptr, *heads_ = nullptr;
     float *qg_ = nullptr, *kk_ = nullptr, *vv_ = nullptr, *qr_ = nullptr, *gate_ = nullptr, *attn_ = nullptr;
@@ -138,13 +150,19 @@ class State {
 
     void upload_ids(const uint32_t* ids, int n);
     void gemv(const DevMat& w, const float* normed_f32, int rows, float* y);
+    void resid_norm(const float* delta, const float* w, int t, float* y_out, bool k8, bool k0);
     void quant_for(int type, const float* x, int n, int rows);
     void layer_forward(const LayerW& L, int li, int t, KvState* kv, const int* pos_dev, bool commit_dn);
-    // the t-row forward of the main stack from the ids in d_ids; returns nothing, logits in logits_
-    void forward_rows(int t, bool want_logits_all);
-    void mtp_rows(int t, const uint32_t* tokens_host, const float* hidden_rows, bool hidden_is_hout);
-    uint32_t mtp_draft_from_row(int row);
-    void chain_drafts(int from);
+    // the t-row forward of the main stack from device ids; logits in logits_, argmax in d_argmax
+    void forward_rows(int t, const int32_t* ids_dev, bool want_logits_all);
+    // the MTP block over t rows (tokens ids_dev, hidden rows, MTP position of row 0 at *pos_dev) into mtp_hout_
+    void mtp_rows(int t, const int32_t* ids_dev, const float* hidden_rows, const int* pos_dev);
+    // greedy draft from mtp_h_ (one row) through the shared lm_head into *out_dev
+    void enqueue_draft(int32_t* out_dev);
+    // drafts from..k-1, each an MTP row chained from the previous one (positions d_mpos[i])
+    void enqueue_chain(int from);
+    // the whole speculative round on the stream: verify, accept, rollback bookkeeping, MTP re-feed, drafts
+    void enqueue_round();
     void sync();
 };
 

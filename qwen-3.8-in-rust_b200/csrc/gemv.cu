@@ -381,32 +381,53 @@ q80_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nblk, const uint8_t
 
 // ---------------------------------------------------------------------------- F32 x f32
 
-// One CTA per row; thread j computes the 32-element partial of block j (left to right), then thread 0
-// chains the partials in order and adds the tail partial (dot.rs:180-198), per column.
+// One warp per row (4 warps per CTA): lane j computes the 32-element partials of blocks j, j+32, ... (left to
+// right inside a block) into shared memory, then lane n < NC chains column n's block partials in order and adds
+// the tail partial (dot.rs:180-198).
 template <int NC>
-__global__ void f32_gemv_kernel(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x, float* __restrict__ y) {
+__global__ void __launch_bounds__(128) f32_gemv_kernel(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x,
+                                                       float* __restrict__ y) {
     extern __shared__ __align__(16) uint8_t smem[];
-    float* part = reinterpret_cast<float*>(smem);
-    const int nfull = cols / 32;
-    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
-        const float* wr = w + (size_t)row * cols;
-        for (int j = threadIdx.x; j <= nfull; j += blockDim.x) {
-            const int lo = j * 32, hi = min(cols, lo + 32);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nfull = cols / 32, nparts = nfull + (cols % 32 ? 1 : 0);
+    float* part = reinterpret_cast<float*>(smem) + (size_t)warp * NC * (nfull + 1);
+    const int row = blockIdx.x * 4 + warp;
+    if (row >= rows) return;
+    const float* wr = w + (size_t)row * cols;
+    const bool vec = (cols % 4) == 0;
+    for (int j = lane; j < nparts; j += 32) {
+        const int lo = j * 32, hi = min(cols, lo + 32);
+        float p[NC];
 #pragma unroll
-            for (int n = 0; n < NC; n++) {
-                float p = 0.0f;
-                for (int i = lo; i < hi; i++) p = __fadd_rn(p, __fmul_rn(wr[i], x[(size_t)n * cols + i]));
-                part[n * (nfull + 1) + j] = p;
+        for (int n = 0; n < NC; n++) p[n] = 0.0f;
+        if (vec && hi - lo == 32) {
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + lo) + q);
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const float4 xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)n * cols + lo) + q);
+                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.x, xv.x));
+                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.y, xv.y));
+                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.z, xv.z));
+                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.w, xv.w));
+                }
             }
+        } else {
+            for (int i = lo; i < hi; i++)
+#pragma unroll
+                for (int n = 0; n < NC; n++) p[n] = __fadd_rn(p[n], __fmul_rn(wr[i], x[(size_t)n * cols + i]));
         }
-        __syncthreads();
-        if (threadIdx.x < NC) {
-            const int n = threadIdx.x;
-            float acc = 0.0f;
-            for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, part[n * (nfull + 1) + j]);
-            y[(size_t)n * rows + row] = __fadd_rn(acc, part[n * (nfull + 1) + nfull]);
-        }
-        __syncthreads();
+#pragma unroll
+        for (int n = 0; n < NC; n++) part[n * (nfull + 1) + j] = p[n];
+    }
+    __syncwarp();
+    if (lane < NC) {
+        const float* pp = part + lane * (nfull + 1);
+        float acc = 0.0f;
+        for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, pp[j]);
+        acc = __fadd_rn(acc, nparts > nfull ? pp[nfull] : 0.0f);  // the tail partial, +0 when empty (dot.rs:194-197)
+        y[(size_t)lane * rows + row] = acc;
     }
 }
 
@@ -452,47 +473,41 @@ cudaError_t launch_q80(const uint8_t* w, int rows, int cols, const void* act, fl
     const int nblk = cols / 32;
     const size_t smem = (size_t)NC * nblk * 36;
     auto kern = q80_gemv_kernel<TYPE, NC>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, smem);
-    if (e != cudaSuccess) return e;
+    static int per_sm = 0;  // per instantiation, at the largest shared-memory size: set once (graph capture safe)
+    if (per_sm == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, 48 * 1024);
+        if (e != cudaSuccess) return e;
+        per_sm = std::max(1, per_sm);
+    }
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
     const int warps = GEMV_THREADS / 32;
-    const int grid = std::max(1, std::min((rows + warps - 1) / warps, num_sms() * std::max(1, per_sm)));
+    const int grid = std::max(1, std::min((rows + warps - 1) / warps, num_sms() * per_sm));
     kern<<<grid, GEMV_THREADS, smem, s>>>(w, rows, nblk, (const uint8_t*)act, y);
     return cudaGetLastError();
 }
 
 template <int NC>
 cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
-    const size_t smem = (size_t)NC * (cols / 32 + 1) * 4;
+    const size_t smem = (size_t)4 * NC * (cols / 32 + 1) * 4;
     auto kern = f32_gemv_kernel<NC>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    const int grid = std::max(1, std::min(rows, num_sms() * 8));
-    kern<<<grid, 256, smem, s>>>((const float*)w, rows, cols, (const float*)act, y);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<(rows + 3) / 4, 128, smem, s>>>((const float*)w, rows, cols, (const float*)act, y);
     return cudaGetLastError();
 }
 
 int g_gemv_impl = [] {
-    const char* e = getenv("QDEC_GEMV_IMPL");  // tuning override: 2, 4 or 5
+    const char* e = getenv("QDEC_GEMV_IMPL");  // tuning override: 2 (raw-Q8_K register path)
     return e ? atoi(e) : 0;
 }();
 
+// Raw-activation dispatch: block_q8_K / block_q8_0 / f32 columns in the reference's layouts.
 template <int NC>
-cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s, bool pdl) {
-    const int impl = g_gemv_impl;
-    const bool aligned = ((uintptr_t)w & 15) == 0;
-    if (type == T_Q6_K_SPLIT) {  // the split layout is read by the bulk-copy and register-streamed kernels
-        if (!aligned) return cudaErrorInvalidValue;
-        if (impl != 4 && v5_gemv_supported(type, cols, NC)) return launch_gemv_v5(type, w, rows, cols, act, NC, y, s, pdl);
-        if (!tma_gemv_supported(type, cols, NC)) return cudaErrorInvalidValue;
-        return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
-    }
-    if ((impl == 0 || impl == 5) && aligned && v5_gemv_supported(type, cols, NC))
-        return launch_gemv_v5(type, w, rows, cols, act, NC, y, s, pdl);
-    if ((impl == 0 || impl == 4) && tma_gemv_supported(type, cols, NC) && aligned)
-        return launch_gemv_tma(type, w, rows, cols, act, NC, y, s);
+cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
     switch (type) {
     case T_Q4_K: return launch_kq<T_Q4_K, NC>(w, rows, cols, act, y, s);
     case T_Q5_K: return launch_kq<T_Q5_K, NC>(w, rows, cols, act, y, s);
@@ -523,9 +538,9 @@ size_t act_row_bytes(int type, int cols) {
 }
 
 void set_gemv_impl(int impl) { g_gemv_impl = impl; }
+int gemv_impl() { return g_gemv_impl; }
 
-cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y, cudaStream_t s,
-                        bool pdl) {
+cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     // columns beyond 4 are processed in groups of at most 4 (each weight byte then read once per group)
     int c0 = 0;
@@ -535,10 +550,10 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
         float* yy = y + (size_t)c0 * rows;
         cudaError_t e;
         switch (nc) {
-        case 1: e = dispatch_type<1>(type, w, rows, cols, a, yy, s, pdl); break;
-        case 2: e = dispatch_type<2>(type, w, rows, cols, a, yy, s, pdl); break;
-        case 3: e = dispatch_type<3>(type, w, rows, cols, a, yy, s, pdl); break;
-        default: e = dispatch_type<4>(type, w, rows, cols, a, yy, s, pdl); break;
+        case 1: e = dispatch_type<1>(type, w, rows, cols, a, yy, s); break;
+        case 2: e = dispatch_type<2>(type, w, rows, cols, a, yy, s); break;
+        case 3: e = dispatch_type<3>(type, w, rows, cols, a, yy, s); break;
+        default: e = dispatch_type<4>(type, w, rows, cols, a, yy, s); break;
         }
         if (e != cudaSuccess) return e;
         c0 += nc;
@@ -553,6 +568,24 @@ cudaError_t launch_quantize_q8k(const float* x, int n, int rows, uint8_t* out, c
     const long long want = (blocks * 32 + threads - 1) / threads;
     const int grid = (int)std::min<long long>(want, (long long)num_sms() * 16);
     q8k_quantize_kernel<<<grid, threads, 0, s>>>(x, n, rows, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8k_image(const float* x, int n, int rows, uint8_t* img, cudaStream_t s) {
+    const long long blocks = (long long)rows * (n / QK_K);
+    if (blocks == 0) return cudaSuccess;
+    const int threads = 256;
+    const long long want = (blocks * 32 + threads - 1) / threads;
+    const int grid = (int)std::min<long long>(want, (long long)num_sms() * 16);
+    q8k_image_kernel<<<grid, threads, 0, s>>>(x, n, rows, img);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q8k_raw_to_image(const uint8_t* raw, long long nblocks, uint8_t* img, cudaStream_t s) {
+    if (nblocks == 0) return cudaSuccess;
+    const int threads = 256;
+    const int grid = (int)std::min<long long>((nblocks * 32 + threads - 1) / threads, (long long)num_sms() * 16);
+    q8k_raw_to_image_kernel<<<grid, threads, 0, s>>>(raw, nblocks, img);
     return cudaGetLastError();
 }
 

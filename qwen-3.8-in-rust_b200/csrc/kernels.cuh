@@ -7,6 +7,8 @@
 namespace qdec {
 
 __global__ void q8k_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
+__global__ void q8k_image_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ img);
+__global__ void q8k_raw_to_image_kernel(const uint8_t* __restrict__ raw, long long nblocks, uint8_t* __restrict__ img);
 __global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
 __global__ void dequant_rows_kernel(int type, const uint8_t* __restrict__ w, size_t row_bytes, int n,
                                     const int32_t* __restrict__ ids, int nids, float* __restrict__ out);
@@ -19,29 +21,31 @@ cudaError_t launch_dequant_rows(int type, const uint8_t* w, size_t row_bytes, in
 
 // y[c * rows + r] = W[r] . act_c for c in [0, ncols); act in the form the weight type consumes:
 // block_q8_K rows (K-quants), block_q8_0 rows (Q8_0, Q4_0) or f32 rows (F32), `ncols` rows back to back.
-// `pdl`: launch as a programmatic dependent of the previous kernel in the stream; the GEMV then streams its
-// first weight bytes before that kernel finishes, so the weights must not be written by it.
 cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
-                        cudaStream_t s, bool pdl = false);
-// Bytes of one activation row of `cols` values in the form `type` consumes.
+                        cudaStream_t s);
+// Bytes of one activation row of `cols` values in the form `type` consumes (reference layouts).
 size_t act_row_bytes(int type, int cols);
 int num_sms();
-// Bulk-copy pipelined K-quant GEMV (gemv_tma.cu) for Q4_K / Q5_K when its staging fits shared memory.
-bool tma_gemv_supported(int type, int cols, int ncols);
-cudaError_t launch_gemv_tma(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
-                            cudaStream_t s);
-// Register-streamed K-quant GEMV (gemv_v5.cu) for Q4_K / Q5_K / Q6_K split.
-bool v5_gemv_supported(int type, int cols, int ncols);
-cudaError_t launch_gemv_v5(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
-                           cudaStream_t s, bool pdl);
-// Tuning: GEMV implementation (0 = automatic, 2 = register path with super-block slots, 4 = bulk-copy,
-// 5 = register-streamed) and the register-streamed kernel's lanes per thread (0, 1, 2) and depth (0, 4, 8).
+
+// The engine's Q8_K device image (common.cuh): quantise f32 rows into it, or rearrange block_q8_K rows.
+cudaError_t launch_quantize_q8k_image(const float* x, int n, int rows, uint8_t* img, cudaStream_t s);
+cudaError_t launch_q8k_raw_to_image(const uint8_t* raw, long long nblocks, uint8_t* img, cudaStream_t s);
+// K-quant GEMV over the Q8_K device image (gemv_v6.cu): Q4_K, Q5_K and Q6_K in the split layout, weights
+// 16-byte aligned.  `img` holds `ncols` rows of cols/256 image blocks back to back.
+// `pdl`: launch as a programmatic dependent of the previous kernel in the stream; the GEMV then streams its
+// first weight bytes before that kernel finishes, so the weights must not be written by it.
+bool v6_gemv_supported(int type);
+cudaError_t launch_gemv_img(int type, const uint8_t* w, int rows, int cols, const void* img, int ncols, float* y,
+                            cudaStream_t s, bool pdl);
+// Tuning: the K-quant GEMV implementation (0 = automatic, 2 = the raw-Q8_K register path, 6 = the image kernel)
+// and the image kernel's configuration (0 = automatic, 1..8).
 void set_gemv_impl(int impl);
-void set_gemv_v5_tuning(int gl, int depth);
-// ggml Q6_K blocks -> the split layout the bulk-copy GEMV reads (nblocks blocks; dst holds the same bytes).
+int gemv_impl();
+void set_gemv_v6_config(int cfg);
+// ggml Q6_K blocks -> the split layout the image kernel reads (nblocks blocks; dst holds the same bytes).
 cudaError_t launch_repack_q6k(const uint8_t* src, size_t nblocks, uint8_t* dst, cudaStream_t s);
-// Force the bulk-copy GEMV's lanes per row (1, 2, 4, 8; 0 = chosen from the row count).
-void set_gemv_lanes_per_row(int lpr);
+// ggml Q4_K / Q5_K / Q6_K rows (rows % 8 == 0) -> the tile layout (gemv_v6.cu); dst holds the same bytes.
+cudaError_t launch_repack_tiles(int ggml_type, const uint8_t* src, int rows, int cols, uint8_t* dst, cudaStream_t s);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
 

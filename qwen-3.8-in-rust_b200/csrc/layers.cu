@@ -30,6 +30,7 @@ __device__ float sum_squares_8lane_block(const float* xs, int n, float* red) {
     const int n8 = n / 8 * 8;
     if (threadIdx.x < 8) {
         float acc = 0.0f;
+#pragma unroll 8
         for (int i = threadIdx.x; i < n8; i += 8) acc = __fadd_rn(acc, __fmul_rn(xs[i], xs[i]));
         red[threadIdx.x] = acc;
     }
@@ -50,97 +51,71 @@ __device__ __forceinline__ float inv_rms_of(float ss, int n, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
 
-// Quantise a row held in shared memory into Q8_K blocks (warp per block), bit-exact with q8k.rs:76-114.
-__device__ void quant_q8k_block_row(const float* xs, int n, uint8_t* out) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int b = warp; b < n / 256; b += nw) {
-        const float* blk = xs + b * 256;
+// Quantise the 256 values of one chunk held in shared memory: warp 0 writes the Q8_K image block
+// (q8k.rs:76-114), warps 0..7 the eight Q8_0 blocks (q8.rs:81-103).  Block of 256 threads.
+__device__ void quant_chunk(const float* xs, uint8_t* img_blk, uint8_t* q80_blk) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (img_blk && warp == 0) {
         float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = blk[lane * 8 + i];
-        float amax = 0.0f, mx = 0.0f;
-        int idx = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float a = fabsf(v[i]);
-            if (a > amax) amax = a, mx = v[i], idx = lane * 8 + i;
-        }
-        for (int off = 16; off > 0; off >>= 1) {
-            const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-            const float om = __shfl_xor_sync(0xffffffffu, mx, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-            if (oa > amax || (oa == amax && oi < idx)) amax = oa, mx = om, idx = oi;
-        }
-        uint8_t* o = out + (size_t)b * Q8K_BLOCK_BYTES;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(o);
-        if (amax == 0.0f) {
-            for (int w = lane; w < 73; w += 32) ow[w] = 0u;
-            continue;
-        }
-        const float iscale = __fdiv_rn(-127.0f, mx);
-        int q[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int qi = __float2int_rn(__fmul_rn(iscale, v[i]));
-            q[i] = qi > 127 ? 127 : qi;
-        }
-        ow[1 + 2 * lane] = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
-        ow[2 + 2 * lane] = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-        int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        const int s_hi = __shfl_down_sync(0xffffffffu, s, 2);  // lane 4g: bsums[2g] (own), bsums[2g+1] (lane 4g+2)
-        if ((lane & 3) == 0) ow[65 + (lane >> 2)] = (uint32_t)(s & 0xffff) | ((uint32_t)(s_hi & 0xffff) << 16);
-        if (lane == 0) ow[0] = __float_as_uint(__fdiv_rn(1.0f, iscale));
+        for (int i = 0; i < 8; i++) v[i] = xs[lane * 8 + i];
+        q8k_quantize_to_image(v, img_blk);
     }
-}
-
-// Quantise a row held in shared memory into Q8_0 blocks (warp per block), bit-exact with q8.rs:81-103.
-__device__ void quant_q8_0_block_row(const float* xs, int n, uint8_t* out) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int b = warp; b < n / 32; b += nw) {
-        const float v = xs[b * 32 + lane];
+    if (q80_blk && warp < 8) {
+        const float v = xs[warp * 32 + lane];
         float amax = fabsf(v);
         for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
         const float dd = __fdiv_rn(amax, 127.0f);
         const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-        const float qf = roundf(__fmul_rn(v, id));
+        const float qf = roundf(__fmul_rn(v, id));  // round half away from zero, then `as i8` (saturating)
         const int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
         const int lo = __shfl_sync(0xffffffffu, qi, (2 * lane - 2) & 31);
         const int hi = __shfl_sync(0xffffffffu, qi, (2 * lane - 1) & 31);
-        uint16_t* o = reinterpret_cast<uint16_t*>(out + (size_t)b * Q8_0_BLOCK_BYTES);
+        uint16_t* o = reinterpret_cast<uint16_t*>(q80_blk + (size_t)warp * Q8_0_BLOCK_BYTES);
         if (lane == 0) o[0] = __half_as_ushort(__float2half_rn(dd));
         else if (lane <= 16) o[lane] = (uint16_t)((lo & 0xff) | ((hi & 0xff) << 8));
     }
 }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace
 
-// One CTA per row.  h = a + b (b may be null: h = a), written to h_out when given; y = rmsnorm(h, w) written
-// to y_out when given; y quantised into q8k_out / q80_out rows when given.
-__global__ void resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ h_out,
-                                        const float* __restrict__ w, float eps, int n, float* __restrict__ y_out,
-                                        uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
+// Grid (n / 256 chunks, rows), 256 threads.  h = a + b (b may be null: h = a); the CTA of chunk c writes chunk c
+// of h to h_out (which must not alias a or b: every CTA of the row reads the whole row); y = rmsnorm(h, w)
+// (rmsnorm.rs:14-76, the 8-lane sum over the whole row, recomputed by every CTA of the row) for its chunk,
+// written to y_out when given and quantised into the Q8_K image / Q8_0 rows when given.
+__global__ void __launch_bounds__(256)
+resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ h_out,
+                        const float* __restrict__ w, float eps, int n, float* __restrict__ y_out,
+                        uint8_t* __restrict__ img_out, uint8_t* __restrict__ q80_out) {
     extern __shared__ __align__(16) float sm[];
-    float* xs = sm;
-    float* red = sm + n;
-    const int row = blockIdx.x;
-    const float* ar = a + (size_t)row * n;
-    const float* br = b ? b + (size_t)row * n : nullptr;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float h = br ? __fadd_rn(ar[i], br[i]) : ar[i];
-        xs[i] = h;
-        if (h_out) h_out[(size_t)row * n + i] = h;
+    float* xs = sm;             // the whole row h
+    float* red = sm + n;        // 16
+    float* ys = red + 16;       // this chunk's normed values
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.y, c0 = blockIdx.x * 256;
+    const float4* a4 = reinterpret_cast<const float4*>(a + (size_t)row * n);
+    const float4* b4 = b ? reinterpret_cast<const float4*>(b + (size_t)row * n) : nullptr;
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+        float4 v = a4[i];
+        if (b4) {
+            const float4 u = b4[i];
+            v.x = __fadd_rn(v.x, u.x), v.y = __fadd_rn(v.y, u.y), v.z = __fadd_rn(v.z, u.z), v.w = __fadd_rn(v.w, u.w);
+        }
+        reinterpret_cast<float4*>(xs)[i] = v;
     }
     __syncthreads();
+    if (h_out) h_out[(size_t)row * n + c0 + threadIdx.x] = xs[c0 + threadIdx.x];
     const float inv = inv_rms_of(sum_squares_8lane_block(xs, n, red), n, eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float y = __fmul_rn(__fmul_rn(xs[i], inv), w[i]);
-        xs[i] = y;
-        if (y_out) y_out[(size_t)row * n + i] = y;
-    }
+    const float y = __fmul_rn(__fmul_rn(xs[c0 + threadIdx.x], inv), w[c0 + threadIdx.x]);
+    ys[threadIdx.x] = y;
+    if (y_out) y_out[(size_t)row * n + c0 + threadIdx.x] = y;
     __syncthreads();
-    if (q8k_out) quant_q8k_block_row(xs, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
-    if (q80_out) quant_q8_0_block_row(xs, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+    quant_chunk(ys, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
+                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
 }
 
 // One CTA per row: y[row * y_ld + i] = rmsnorm(x[row * x_ld ..], w)[i] (rmsnorm.rs:25-33).
@@ -156,29 +131,34 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, int x_ld, const
     for (int i = threadIdx.x; i < n; i += blockDim.x) y[(size_t)blockIdx.x * y_ld + i] = __fmul_rn(__fmul_rn(xs[i], inv), w[i]);
 }
 
-// One CTA per row: h = silu(g) * u (act.rs:24), optionally written, then quantised.
-__global__ void swiglu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int n, float* __restrict__ h_out,
-                                    uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
-    extern __shared__ __align__(16) float sm[];
-    const int row = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float h = __fmul_rn(silu_f32(g[(size_t)row * n + i]), u[(size_t)row * n + i]);
-        sm[i] = h;
-        if (h_out) h_out[(size_t)row * n + i] = h;
-    }
+// Grid (n / 256, rows), 256 threads: h = silu(g) * u (act.rs:24) for one chunk, optionally written, quantised.
+__global__ void __launch_bounds__(256)
+swiglu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int n, float* __restrict__ h_out,
+                    uint8_t* __restrict__ img_out, uint8_t* __restrict__ q80_out) {
+    __shared__ float hs[256];
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.y;
+    const size_t i = (size_t)row * n + blockIdx.x * 256 + threadIdx.x;
+    const float h = __fmul_rn(silu_f32(g[i]), u[i]);
+    hs[threadIdx.x] = h;
+    if (h_out) h_out[i] = h;
     __syncthreads();
-    if (q8k_out) quant_q8k_block_row(sm, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
-    if (q80_out) quant_q8_0_block_row(sm, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+    quant_chunk(hs, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
+                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
 }
 
-// Quantise rows already in global memory (one CTA per row) -- used for the mixer outputs.
-__global__ void quant_rows_kernel(const float* __restrict__ x, int n, uint8_t* __restrict__ q8k_out, uint8_t* __restrict__ q80_out) {
-    extern __shared__ __align__(16) float sm[];
-    const int row = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = x[(size_t)row * n + i];
+// Grid (n / 256, rows), 256 threads: quantise rows already in global memory (the mixer outputs).
+__global__ void __launch_bounds__(256)
+quant_rows_kernel(const float* __restrict__ x, int n, uint8_t* __restrict__ img_out, uint8_t* __restrict__ q80_out) {
+    __shared__ float hs[256];
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.y;
+    hs[threadIdx.x] = x[(size_t)row * n + blockIdx.x * 256 + threadIdx.x];
     __syncthreads();
-    if (q8k_out) quant_q8k_block_row(sm, n, q8k_out + (size_t)row * (n / 256) * Q8K_BLOCK_BYTES);
-    if (q80_out) quant_q8_0_block_row(sm, n, q80_out + (size_t)row * (n / 32) * Q8_0_BLOCK_BYTES);
+    quant_chunk(hs, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
+                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
 }
 
 // Causal depthwise conv1d (+ SiLU) for t rows, one thread per channel (conv.rs:11-36).  The committed window
@@ -401,44 +381,94 @@ __global__ void attention_kernel(const AttnArgs a) {
     }
 }
 
-// One CTA per row: out[row] = the first index of the maximum (model.rs:505-513: strict > scan from 0).
-__global__ void argmax_kernel(const float* __restrict__ x, int n, int32_t* __restrict__ out) {
-    const float* r = x + (size_t)blockIdx.x * n;
-    float best = r[0];
-    int bi = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+// out[row] = the first index of the maximum (model.rs:505-513: best = x[0], then a strict > scan; NaN is never
+// taken, and a NaN x[0] is kept).  Grid (chunks, rows): each CTA reduces ARGMAX_CHUNK values to its first
+// maximum (ties -> smaller index; NaN skipped), writes it, and the last CTA of the row to finish combines the
+// chunk results in chunk order with the strict > rule and resets the row's counter.
+constexpr int ARGMAX_CHUNK = 8192;
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, int n, int32_t* __restrict__ out,
+                                                     float* __restrict__ pval, int* __restrict__ pidx,
+                                                     unsigned* __restrict__ counter) {
+    griddep_wait();
+    griddep_launch();
+    const int row = blockIdx.y, chunks = gridDim.x, c = blockIdx.x;
+    const float* r = x + (size_t)row * n;
+    const int lo = c * ARGMAX_CHUNK, hi = min(n, lo + ARGMAX_CHUNK);
+    float best = -INFINITY;
+    int bi = -1;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float v = r[i];
-        if (v > best || (v == best && i < bi)) best = v, bi = i;
+        if (v > best || (bi < 0 && v == best)) best = v, bi = i;  // the first -inf counts as a candidate too
     }
-    // the reference keeps index 0 unless a strictly greater value appears; r[0] seeds every thread
     for (int off = 16; off > 0; off >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, off);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > best || (ov == best && oi < bi)) best = ov, bi = oi;
+        if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) best = ov, bi = oi;
     }
-    __shared__ float bv[32];
-    __shared__ int bx[32];
+    __shared__ float bv[8];
+    __shared__ int bx[8];
+    __shared__ bool last;
     if ((threadIdx.x & 31) == 0) bv[threadIdx.x >> 5] = best, bx[threadIdx.x >> 5] = bi;
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x >> 5); w++)
-            if (bv[w] > best || (bv[w] == best && bx[w] < bi)) best = bv[w], bi = bx[w];
-        out[blockIdx.x] = bi;
+            if (bx[w] >= 0 && (bi < 0 || bv[w] > best || (bv[w] == best && bx[w] < bi))) best = bv[w], bi = bx[w];
+        pval[(size_t)row * chunks + c] = best;
+        pidx[(size_t)row * chunks + c] = bi;
+        __threadfence();
+        last = atomicAdd(&counter[row], 1u) == (unsigned)chunks - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        float g = r[0];  // the reference's seed: x[0] at index 0
+        int gi = 0;
+        for (int k = 0; k < chunks; k++) {
+            const volatile float* pv = pval + (size_t)row * chunks;
+            const volatile int* pi = pidx + (size_t)row * chunks;
+            if (pi[k] >= 0 && pv[k] > g) g = pv[k], gi = pi[k];
+        }
+        out[row] = gi;
+        counter[row] = 0u;
     }
 }
 
 // ------------------------------------------------------------------------------------------- launchers
 
+namespace {
+// Launch with the programmatic-dependent attribute: the kernel calls griddepcontrol.wait before touching
+// anything its predecessor writes, and triggers its own dependents at once.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+}  // namespace
+
 cudaError_t launch_resid_norm_quant(const float* a, const float* b, float* h_out, const float* w, float eps, int n, int rows,
-                                    float* y_out, uint8_t* q8k_out, uint8_t* q80_out, cudaStream_t s) {
+                                    float* y_out, uint8_t* img_out, uint8_t* q80_out, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    const size_t smem = (size_t)(n + 16) * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(resid_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (n % 256) return cudaErrorInvalidValue;
+    if (h_out && (h_out == a || h_out == b)) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(n + 16 + 256) * sizeof(float);
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(resid_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
+        attr_done = true;
     }
-    resid_norm_quant_kernel<<<rows, 512, smem, s>>>(a, b, h_out, w, eps, n, y_out, q8k_out, q80_out);
-    return cudaGetLastError();
+    return launch_pdl(resid_norm_quant_kernel, dim3(n / 256, rows), dim3(256), smem, s, a, b, h_out, w, eps, n, y_out, img_out,
+                      q80_out);
 }
 
 cudaError_t launch_rmsnorm_rows(const float* x, int x_ld, const float* w, float eps, int n, int rows, float* y, int y_ld,
@@ -453,27 +483,17 @@ cudaError_t launch_rmsnorm_rows(const float* x, int x_ld, const float* w, float 
     return cudaGetLastError();
 }
 
-cudaError_t launch_swiglu_quant(const float* g, const float* u, int n, int rows, float* h_out, uint8_t* q8k_out,
+cudaError_t launch_swiglu_quant(const float* g, const float* u, int n, int rows, float* h_out, uint8_t* img_out,
                                 uint8_t* q80_out, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    const size_t smem = (size_t)n * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(swiglu_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    swiglu_quant_kernel<<<rows, 512, smem, s>>>(g, u, n, h_out, q8k_out, q80_out);
-    return cudaGetLastError();
+    if (n % 256) return cudaErrorInvalidValue;
+    return launch_pdl(swiglu_quant_kernel, dim3(n / 256, rows), dim3(256), 0, s, g, u, n, h_out, img_out, q80_out);
 }
 
-cudaError_t launch_quant_rows(const float* x, int n, int rows, uint8_t* q8k_out, uint8_t* q80_out, cudaStream_t s) {
+cudaError_t launch_quant_rows(const float* x, int n, int rows, uint8_t* img_out, uint8_t* q80_out, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    const size_t smem = (size_t)n * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(quant_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    quant_rows_kernel<<<rows, 512, smem, s>>>(x, n, q8k_out, q80_out);
-    return cudaGetLastError();
+    if (n % 256) return cudaErrorInvalidValue;
+    return launch_pdl(quant_rows_kernel, dim3(n / 256, rows), dim3(256), 0, s, x, n, img_out, q80_out);
 }
 
 cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, const float* x, int t, float* out,
@@ -503,18 +523,29 @@ cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
     const dim3 grid(a.n_head, t);
     const size_t smem = (size_t)(a.head_dim + a.max_len + 16) * sizeof(float);
-    if (smem > 48 * 1024) {
+    static size_t cap = 48 * 1024;  // raised only when a longer cache needs it (before any graph capture)
+    if (smem > cap) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        cap = smem;
     }
     attention_kernel<<<grid, 256, smem, s>>>(a);
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, cudaStream_t s) {
+size_t argmax_scratch_bytes(int n, int rows) {
+    const int chunks = (n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK;
+    return (size_t)rows * chunks * 8 + (size_t)rows * 4 + 64;
+}
+
+cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, void* scratch, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    argmax_kernel<<<rows, 1024, 0, s>>>(x, n, out);
-    return cudaGetLastError();
+    const int chunks = (n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK;
+    // scratch: counters (zero at rest: every launch leaves them zero), then the per-chunk values and indices
+    unsigned* counter = (unsigned*)scratch;
+    float* pval = (float*)((uint8_t*)scratch + ((size_t)rows * 4 + 15) / 16 * 16);
+    int* pidx = (int*)(pval + (size_t)rows * chunks);
+    return launch_pdl(argmax_kernel, dim3(chunks, rows), dim3(256), 0, s, x, n, out, pval, pidx, counter);
 }
 
 }  // namespace qdec

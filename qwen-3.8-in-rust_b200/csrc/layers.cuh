@@ -63,6 +63,8 @@ cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, 
 cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s);
 cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s);
-cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, cudaStream_t s);
+// scratch: argmax_scratch_bytes(n, rows) bytes, zero-filled once before the first use (launches keep it so).
+size_t argmax_scratch_bytes(int n, int rows);
+cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, void* scratch, cudaStream_t s);
 
 }  // namespace qdec

@@ -63,6 +63,43 @@ __global__ void q8k_quantize_kernel(const float* __restrict__ x, int n, int rows
     }
 }
 
+// f32 rows -> the engine's Q8_K device image (common.cuh), one warp per 256-value block.
+__global__ void q8k_image_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ img) {
+    const int nb = n / QK_K;
+    const long long total = (long long)rows * nb;
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < total; b += nwarps) {
+        const long long r = b / nb, sb = b % nb;
+        const float4* blk = reinterpret_cast<const float4*>(x + r * (long long)n + sb * QK_K);
+        const float4 a0 = blk[2 * lane], a1 = blk[2 * lane + 1];
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        q8k_quantize_to_image(v, img + b * Q8K_IMG_BYTES);
+    }
+}
+
+// ggml block_q8_K rows -> the device image: the same values, rearranged (one warp per block).
+__global__ void q8k_raw_to_image_kernel(const uint8_t* __restrict__ raw, long long nblocks, uint8_t* __restrict__ img) {
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < nblocks; b += nwarps) {
+        const uint32_t* r = reinterpret_cast<const uint32_t*>(raw + b * Q8K_BLOCK_BYTES);
+        uint32_t* o = reinterpret_cast<uint32_t*>(img + b * Q8K_IMG_BYTES);
+        for (int c = lane; c < 64; c += 32) o[(c & 7) * 8 + (c >> 3)] = r[1 + c];  // codes word c: s = c/8, g = c%8
+        if (lane < 8) {
+            const uint32_t pr = r[65 + lane];  // bsums[2g], bsums[2g+1]
+            o[Q8K_IMG_BSP / 4 + lane] = pr;
+            const int q8s = (int)(int16_t)((int16_t)(pr & 0xffff) + (int16_t)(pr >> 16));  // q8s[lane]
+            const int q8s_hi = __shfl_down_sync(0xffu, q8s, 1, 8);
+            if ((lane & 1) == 0) o[Q8K_IMG_Q8S / 4 + lane / 2] = (uint32_t)(q8s & 0xffff) | ((uint32_t)(q8s_hi & 0xffff) << 16);
+        }
+        if (lane == 8) o[Q8K_IMG_D / 4] = r[0];
+        if (lane >= 9 && lane < 12) o[Q8K_IMG_D / 4 + lane - 8] = 0u;
+    }
+}
+
 // One warp per 32-value block; lane i holds value i.
 __global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out) {
     const int nb = n / 32;

@@ -61,8 +61,8 @@ def lib():
             "qdec_matvec_noalloc": [I, P, I, I, P, I, P, P],
             "qdec_dequant_rows": [I, P, I, I, P, I, P, P],
             "qdec_repack_q6k": [P, I, I, P, P],
-            "qdec_tune_gemv_lanes_per_row": [I],
-            "qdec_tune_gemv": [I, I, I],
+            "qdec_repack_tiles": [I, P, I, I, P, P],
+            "qdec_tune_gemv": [I, I],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
@@ -152,15 +152,18 @@ def matvec_noalloc_max_bytes():
     return lib().qdec_matvec_noalloc_max_bytes()
 
 
-def tune_gemv_lanes_per_row(lpr):
-    """Force the GEMV's lanes per row (1, 2, 4, 8; 0 = automatic). Results are identical for every value."""
-    _check(lib().qdec_tune_gemv_lanes_per_row(lpr))
+def tune_gemv(impl=0, config=0):
+    """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
+    image kernel's configuration (0 automatic, 1..8). Results are identical for every value."""
+    _check(lib().qdec_tune_gemv(impl, config))
 
 
-def tune_gemv(impl=0, lanes_per_thread=0, depth=0):
-    """Select the GEMV kernel (0 automatic, 2, 4, 5) and the register-streamed kernel's lanes per thread and
-    depth (0 = automatic). Results are identical for every value."""
-    _check(lib().qdec_tune_gemv(impl, lanes_per_thread, depth))
+def repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream=0):
+    """ggml Q4_K/Q5_K/Q6_K rows -> the tile layout (type TILE[t])."""
+    _check(lib().qdec_repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream))
+
+
+TILE = {12: 112, 13: 113, 14: 116}
 
 
 def repack_q6k(src_ptr, rows, cols, dst_ptr, stream=0):

@@ -175,25 +175,8 @@ def run_gemv_raw(q, t, wd, rows, cols, x):
     return y.cpu().numpy().reshape(n, rows)
 
 
-@pytest.mark.parametrize("lpr", [1, 2, 4, 8])
-@pytest.mark.parametrize("t", [12, 13])
-def test_gemv_every_lanes_per_row_bit_exact(q, orc, t, lpr):
-    """The bulk-copy GEMV gives the same bits whichever number of lanes shares a row."""
-    rows, cols = 333, 6144
-    w = random_blocks(t, rows, cols, seed=5 + t)
-    x = np.random.default_rng(lpr).standard_normal((4, cols)).astype(np.float32)
-    want = orc.matmul(t, w, rows, cols, x)
-    q.tune_gemv_lanes_per_row(lpr)
-    try:
-        for n in (1, 3, 4):
-            got = run_gemv_raw(q, t, to_dev(w), rows, cols, x[:n])
-            assert bits_equal(got, want[:n]), (t, lpr, n)
-    finally:
-        q.tune_gemv_lanes_per_row(0)
-
-
-@pytest.mark.parametrize("lpr", [0, 1, 2, 8])
-def test_gemv_q6k_split_layout_bit_exact(q, orc, lpr):
+@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4])
+def test_gemv_q6k_split_layout_bit_exact(q, orc, cfg):
     """Q6_K repacked into the split device layout (208-byte blocks + f16 scales) gives the ggml-layout bits."""
     rows, cols = 515, 5120
     w = random_blocks(14, rows, cols, seed=99)
@@ -203,48 +186,100 @@ def test_gemv_q6k_split_layout_bit_exact(q, orc, lpr):
     torch.cuda.synchronize()
     x = np.random.default_rng(3).standard_normal((4, cols)).astype(np.float32)
     want = orc.matmul(14, w, rows, cols, x)
-    q.tune_gemv_lanes_per_row(lpr)
+    q.tune_gemv(6, cfg)
     try:
         for n in (1, 2, 4):
             got = run_gemv_raw(q, q.Q6_K_SPLIT, dst, rows, cols, x[:n])
-            assert bits_equal(got, want[:n]), (lpr, n)
+            assert bits_equal(got, want[:n]), (cfg, n)
     finally:
-        q.tune_gemv_lanes_per_row(0)
+        q.tune_gemv(0, 0)
 
 
 @pytest.mark.parametrize("t", [12, 13, 114])
-@pytest.mark.parametrize("gl,depth", [(1, 4), (1, 8), (2, 4), (2, 8)])
-def test_gemv_register_streamed_bit_exact(q, orc, t, gl, depth):
-    """The register-streamed GEMV at every lanes-per-thread / depth: the oracle's bits for 1..4 columns, on a
-    ragged row count and a width whose super-block count is not a multiple of the depth."""
+@pytest.mark.parametrize("cfg", range(1, 9))
+def test_gemv_image_kernel_every_config_bit_exact(q, orc, t, cfg):
+    """The image-reading GEMV in each configuration (lanes per thread, rows per thread, depth, integer or FP32
+    scale multiply): the oracle's bits for 1..5 columns, on a ragged row count and a width whose super-block
+    count is not a multiple of any depth, through both entry points (f32 columns and block_q8_K columns)."""
     rows, cols = 389, 5376  # 21 super-blocks
     base = 14 if t == 114 else t
     w = random_blocks(base, rows, cols, seed=7 + t)
-    x = np.random.default_rng(gl * 10 + depth).standard_normal((4, cols)).astype(np.float32)
+    x = np.random.default_rng(cfg).standard_normal((5, cols)).astype(np.float32)
+    x[1] *= 1e-30  # tiny and hostile scales
+    x[2, ::7] = 0.0
     want = orc.matmul(base, w, rows, cols, x)
     wd = to_dev(w)
     if t == 114:
         dst = torch.empty_like(wd)
         q.repack_q6k(wd.data_ptr(), rows, cols, dst.data_ptr())
         wd = dst
-    q.tune_gemv(5, gl, depth)
+    q.tune_gemv(6, cfg)
     try:
-        for n in (1, 2, 3, 4):
+        for n in (1, 2, 3, 4, 5):
             got = run_gemv_raw(q, t, wd, rows, cols, x[:n])
-            assert bits_equal(got, want[:n]), (t, gl, depth, n)
+            assert bits_equal(got, want[:n]), (t, cfg, n)
+        act = gpu_q8k(q, x[:4])  # reference-layout block_q8_K columns through qdec_gemv
+        ad = to_dev(np.ascontiguousarray(act).reshape(-1))
+        y = torch.empty(4 * rows, dtype=torch.float32, device="cuda")
+        q.gemv(t, wd.data_ptr(), rows, cols, ad.data_ptr(), 4, y.data_ptr())
+        torch.cuda.synchronize()
+        assert bits_equal(y.cpu().numpy().reshape(4, rows), want[:4]), (t, cfg, "gemv")
     finally:
-        q.tune_gemv(0, 0, 0)
+        q.tune_gemv(0, 0)
 
 
 @pytest.mark.parametrize("rows,cols", [(1, 256), (5, 17408), (4099, 256)])
-def test_gemv_register_streamed_edge_shapes(q, orc, rows, cols):
-    """One row, one super-block per row, and the widest activation the kernel stages."""
+def test_gemv_image_kernel_edge_shapes(q, orc, rows, cols):
+    """One row, one super-block per row, and the widest activation rows of the model."""
     w = random_blocks(12, rows, cols, seed=rows)
     x = np.random.default_rng(2).standard_normal((4, cols)).astype(np.float32)
     want = orc.matmul(12, w, rows, cols, x)
-    q.tune_gemv(5, 0, 0)
-    try:
-        got = run_gemv_raw(q, 12, to_dev(w), rows, cols, x)
-    finally:
-        q.tune_gemv(0, 0, 0)
+    got = run_gemv_raw(q, 12, to_dev(w), rows, cols, x)
     assert bits_equal(got, want)
+
+
+@pytest.mark.parametrize("t", [12, 13, 14])
+def test_gemv_reference_layout_kernel_bit_exact(q, orc, t):
+    """The kernel that reads block_q8_K columns in the reference layout (forced for Q4_K/Q5_K; the ggml Q6_K
+    layout always takes it)."""
+    rows, cols = 261, 5120
+    w = random_blocks(t, rows, cols, seed=3 + t)
+    x = np.random.default_rng(t).standard_normal((4, cols)).astype(np.float32)
+    want = orc.matmul(t, w, rows, cols, x)
+    q.tune_gemv(2, 0)
+    try:
+        got = run_gemv_raw(q, t, to_dev(w), rows, cols, x)
+    finally:
+        q.tune_gemv(0, 0)
+    assert bits_equal(got, want)
+
+
+@pytest.mark.parametrize("t", [12, 13, 14])
+@pytest.mark.parametrize("cfg", range(1, 15))
+def test_gemv_tile_layout_every_config_bit_exact(q, orc, t, cfg):
+    """Weights repacked into the tile layout (8 rows x one super-block per tile block): the oracle's bits for
+    1..5 columns in every configuration, a super-block count that is not a multiple of any depth, a tile count
+    that is not a multiple of two."""
+    rows, cols = 8 * 37, 5376
+    w = random_blocks(t, rows, cols, seed=31 + t)
+    x = np.random.default_rng(100 + cfg).standard_normal((5, cols)).astype(np.float32)
+    x[3] *= 1e20
+    want = orc.matmul(t, w, rows, cols, x)
+    src = to_dev(w)
+    dst = torch.empty_like(src)
+    q.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr())
+    torch.cuda.synchronize()
+    q.tune_gemv(6, cfg)
+    try:
+        for n in (1, 2, 3, 4, 5):
+            got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (t, cfg, n)
+    finally:
+        q.tune_gemv(0, 0)
+
+
+def test_tile_repack_rejects_ragged_rows(q):
+    src = torch.zeros(12 * 144, dtype=torch.uint8, device="cuda")
+    dst = torch.empty_like(src)
+    with pytest.raises(q.QdecError):
+        q.repack_tiles(12, src.data_ptr(), 12, 256, dst.data_ptr())
