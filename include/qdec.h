@@ -42,6 +42,9 @@ extern "C" {
 #define QDEC_TYPE_Q4_K_TILE 112
 #define QDEC_TYPE_Q5_K_TILE 113
 #define QDEC_TYPE_Q6_K_TILE 116
+/* Q8_0 / Q4_0 in the tile layout: 8 rows x 8 blocks per tile block; rows % 8 == 0 and cols % 256 == 0. */
+#define QDEC_TYPE_Q8_0_TILE 108
+#define QDEC_TYPE_Q4_0_TILE 102
 
 /* Library version string, e.g. "qdec 0.1.0 sm_100a". */
 const char *qdec_version(void);
@@ -78,6 +81,16 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
 int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols, float *y_dev,
                 void *stream);
 
+/* The library's activation image (no counterpart in the reference; the same values as block_q8_K / block_q8_0
+ * rows, rearranged for the GEMV): bytes of one row of `cols` values for weights of `ggml_type` (0 when the
+ * type reads no image), quantising f32 rows into it, and the GEMV that reads it directly -- what qdec_gemv
+ * does after rearranging block_q8_K / block_q8_0 columns, without that step.  K-quant types (ggml, split,
+ * tile) read the Q8_K image, QDEC_TYPE_Q8_0_TILE / _Q4_0_TILE the Q8_0 image. */
+size_t qdec_image_row_bytes(int ggml_type, int cols);
+int qdec_quantize_image(int ggml_type, const float *x_dev, int n, int rows, void *img_dev, void *stream);
+int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const void *img_dev, int n_cols, float *y_dev,
+                    void *stream);
+
 /* Tuning knob of the K-quant GEMV (process-wide): the kernel (0 = automatic; 2 = the kernel that reads
  * block_q8_K activations in the reference layout; 6 = the kernel that reads the library's activation image) and
  * the image kernel's configuration (0 = automatic, 1..8: lanes per thread, rows per thread, super-blocks in
@@ -89,8 +102,8 @@ int qdec_tune_gemv(int impl, int config);
  * buffer) that qdec_gemv reads as QDEC_TYPE_Q6_K_SPLIT.  No counterpart in the reference (a device layout). */
 int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void *stream);
 
-/* Repack rows x cols of ggml Q4_K / Q5_K / Q6_K (src) into the tile layout (dst: the same number of bytes, a
- * distinct 16-byte aligned buffer) that qdec_gemv reads as QDEC_TYPE_Q4_K_TILE / _Q5_K_TILE / _Q6_K_TILE.
+/* Repack rows x cols of ggml Q4_K / Q5_K / Q6_K / Q8_0 / Q4_0 (src) into the tile layout (dst: the same number
+ * of bytes, a distinct 16-byte aligned buffer) that qdec_gemv reads as QDEC_TYPE_*_TILE.
  * No counterpart in the reference (a device layout). */
 int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, void *dst_dev, void *stream);
 

@@ -33,7 +33,7 @@ void clear_error() { g_last_error.clear(); }
 
 bool supported_type(int t) {
     return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q6_K_SPLIT ||
-           t == T_Q4_K_TILE || t == T_Q5_K_TILE || t == T_Q6_K_TILE;
+           t == T_Q4_K_TILE || t == T_Q5_K_TILE || t == T_Q6_K_TILE || t == T_Q8_0_TILE || t == T_Q4_0_TILE;
 }
 
 // Shape checks of the reference's assert!s (matvec.rs:73-77, :300, :338; kdot.rs:179-191).
@@ -46,6 +46,8 @@ int check_gemv_shape(int type, int rows, int cols, int ncols) {
         return fail(QDEC_EINVAL, "cols %d: Q8_0/Q4_0 rows must hold an even number of 32-blocks", cols);
     if (tile_base_type(type) != type && rows % 8)
         return fail(QDEC_EINVAL, "rows %d: the tile layout holds a multiple of 8 rows", rows);
+    if ((type == T_Q8_0_TILE || type == T_Q4_0_TILE) && cols % 256)
+        return fail(QDEC_EINVAL, "cols %d: the Q8_0/Q4_0 tile layout holds a multiple of 256 columns", cols);
     if (is_kquant(type)) {
         const size_t smem = (size_t)4 * (cols / 256) * 324 + 64;  // the raw-activation kernel stages 4 columns
         if (smem > 220 * 1024) return fail(QDEC_EINVAL, "cols %d too wide for the staged activations", cols);
@@ -87,6 +89,7 @@ size_t image_bytes(int cols, int n_cols) { return (size_t)(cols / QK_K) * Q8K_IM
 
 size_t matvec_scratch_bytes(int type, const void *w_dev, int cols, int n_cols) {
     if (type == T_F32) return 0;
+    if (type == T_Q8_0_TILE || type == T_Q4_0_TILE) return (size_t)(cols / 32) * Q80_IMG_BYTES * n_cols;
     if (uses_image(type, w_dev)) return image_bytes(cols, n_cols);
     return act_row_bytes(type, cols) * n_cols;
 }
@@ -97,6 +100,12 @@ int matvec_run(int type, const void *w_dev, int rows, int cols, const float *x_d
     cudaError_t e;
     if (type == T_F32) {
         e = launch_gemv(type, w, rows, cols, x_dev, n_cols, y_dev, s);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, who);
+    }
+    if (type == T_Q8_0_TILE || type == T_Q4_0_TILE) {
+        e = launch_quantize_q80_image(x_dev, cols, n_cols, (uint8_t *)scratch, s);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+        e = launch_gemv_q80_img(type, w, rows, cols, scratch, n_cols, y_dev, s, false);
         return e == cudaSuccess ? QDEC_OK : cuda_fail(e, who);
     }
     if (uses_image(type, w_dev)) {
@@ -148,6 +157,15 @@ int qdec_gemv(int ggml_type, const void *w_dev, int rows, int cols, const void *
     if (!w_dev || !act_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_gemv: null pointer");
     if (n_cols == 0 || rows == 0) return QDEC_OK;
     cudaStream_t s = (cudaStream_t)stream;
+    if (ggml_type == T_Q8_0_TILE || ggml_type == T_Q4_0_TILE) {  // block_q8_0 rows -> the Q8_0 row image
+        void *img = nullptr;
+        rc = act_buffer((size_t)(cols / 32) * Q80_IMG_BYTES * n_cols, &img);
+        if (rc) return rc;
+        cudaError_t e = launch_q80_raw_to_image((const uint8_t *)act_dev, cols, n_cols, (uint8_t *)img, s);
+        if (e != cudaSuccess) return cuda_fail(e, "qdec_gemv: activation image");
+        e = launch_gemv_q80_img(ggml_type, (const uint8_t *)w_dev, rows, cols, img, n_cols, y_dev, s, false);
+        return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv");
+    }
     if (uses_image(ggml_type, w_dev)) {  // rearrange the block_q8_K rows into the image the kernel reads
         void *img = nullptr;
         rc = act_buffer(image_bytes(cols, n_cols), &img);
@@ -176,6 +194,37 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
     return matvec_run(ggml_type, w_dev, rows, cols, x_dev, n_cols, y_dev, (cudaStream_t)stream, act, "qdec_matvec");
 }
 
+size_t qdec_image_row_bytes(int ggml_type, int cols) {
+    if (cols <= 0) return 0;
+    if (is_q80(ggml_type)) return cols % 32 ? 0 : (size_t)(cols / 32) * Q80_IMG_BYTES;
+    if (is_kquant(ggml_type)) return cols % QK_K ? 0 : (size_t)(cols / QK_K) * Q8K_IMG_BYTES;
+    return 0;
+}
+
+int qdec_quantize_image(int ggml_type, const float *x_dev, int n, int rows, void *img_dev, void *stream) {
+    if (!x_dev || !img_dev || rows < 0 || !qdec_image_row_bytes(ggml_type, n))
+        return fail(QDEC_EINVAL, "qdec_quantize_image: bad argument (type %d, length %d)", ggml_type, n);
+    cudaError_t e = is_q80(ggml_type) ? launch_quantize_q80_image(x_dev, n, rows, (uint8_t *)img_dev, (cudaStream_t)stream)
+                                      : launch_quantize_q8k_image(x_dev, n, rows, (uint8_t *)img_dev, (cudaStream_t)stream);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_quantize_image");
+}
+
+int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const void *img_dev, int n_cols, float *y_dev,
+                    void *stream) {
+    int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
+    if (rc) return rc;
+    if (!w_dev || !img_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_gemv_image: null pointer");
+    if (((uintptr_t)w_dev & 15) != 0) return fail(QDEC_EINVAL, "qdec_gemv_image: weights must be 16-byte aligned");
+    cudaError_t e;
+    if (ggml_type == T_Q8_0_TILE || ggml_type == T_Q4_0_TILE)
+        e = launch_gemv_q80_img(ggml_type, (const uint8_t *)w_dev, rows, cols, img_dev, n_cols, y_dev, (cudaStream_t)stream, false);
+    else if (v6_gemv_supported(ggml_type))
+        e = launch_gemv_img(ggml_type, (const uint8_t *)w_dev, rows, cols, img_dev, n_cols, y_dev, (cudaStream_t)stream, false);
+    else
+        return fail(QDEC_EINVAL, "qdec_gemv_image: type %d does not read the activation image", ggml_type);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv_image");
+}
+
 int qdec_tune_gemv(int impl, int config) {
     if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2 or 6");
     if (config < 0 || config > 14) return fail(QDEC_EINVAL, "gemv configuration must be 0..14");
@@ -193,13 +242,16 @@ int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void
 }
 
 int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, void *dst_dev, void *stream) {
-    if (ggml_type != T_Q4_K && ggml_type != T_Q5_K && ggml_type != T_Q6_K)
+    if (ggml_type != T_Q4_K && ggml_type != T_Q5_K && ggml_type != T_Q6_K && ggml_type != T_Q8_0 && ggml_type != T_Q4_0)
         return fail(QDEC_EINVAL, "qdec_repack_tiles: type %d has no tile layout", ggml_type);
     if (!src_dev || !dst_dev || rows < 0 || rows % 8 || cols <= 0 || cols % 256)
         return fail(QDEC_EINVAL, "qdec_repack_tiles: bad argument (rows %d must be a multiple of 8, cols %d of 256)", rows, cols);
     if (src_dev == dst_dev) return fail(QDEC_EINVAL, "qdec_repack_tiles: source and destination must differ");
     if (((uintptr_t)dst_dev & 15) != 0) return fail(QDEC_EINVAL, "qdec_repack_tiles: destination must be 16-byte aligned");
-    cudaError_t e = launch_repack_tiles(ggml_type, (const uint8_t *)src_dev, rows, cols, (uint8_t *)dst_dev, (cudaStream_t)stream);
+    const bool q80 = ggml_type == T_Q8_0 || ggml_type == T_Q4_0;
+    if (q80 && cols % 256) return fail(QDEC_EINVAL, "qdec_repack_tiles: Q8_0/Q4_0 tiles hold a multiple of 256 columns");
+    cudaError_t e = q80 ? launch_repack_q80_tiles(ggml_type, (const uint8_t *)src_dev, rows, cols, (uint8_t *)dst_dev, (cudaStream_t)stream)
+                        : launch_repack_tiles(ggml_type, (const uint8_t *)src_dev, rows, cols, (uint8_t *)dst_dev, (cudaStream_t)stream);
     return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_repack_tiles");
 }
 

@@ -10,14 +10,21 @@
 
 namespace qdec {
 
+// Programmatic dependent launch on (default) or off (QDEC_PDL=0: every kernel waits for its predecessor to finish
+// before it starts, which is what per-kernel timings need).
+bool pdl_enabled();
+
 // ggml tensor type ids (GGUF), the same numbering as crates/core/src/gguf.rs GgmlType.
 enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 // Q6_K in the split layout: 208-byte blocks [ql | qh | scales], then every block's f16 d (gemv_v6.cu).
 constexpr int T_Q6_K_SPLIT = 114;
 // K-quants in the tile layout of gemv_v6.cu (8 rows x one super-block per tile block; rows % 8 == 0).
 constexpr int T_Q4_K_TILE = 112, T_Q5_K_TILE = 113, T_Q6_K_TILE = 116;
+// Q8_0 / Q4_0 in the tile layout (8 rows x 8 blocks per tile block; rows % 8 == 0, cols % 256 == 0).
+constexpr int T_Q8_0_TILE = 108, T_Q4_0_TILE = 102;
 __host__ __device__ inline int tile_base_type(int t) {
-    return t == T_Q4_K_TILE ? T_Q4_K : t == T_Q5_K_TILE ? T_Q5_K : t == T_Q6_K_TILE ? T_Q6_K : t;
+    return t == T_Q4_K_TILE ? T_Q4_K : t == T_Q5_K_TILE ? T_Q5_K : t == T_Q6_K_TILE ? T_Q6_K
+         : t == T_Q8_0_TILE ? T_Q8_0 : t == T_Q4_0_TILE ? T_Q4_0 : t;
 }
 
 constexpr int QK_K = 256;
@@ -31,9 +38,15 @@ constexpr int Q8K_BLOCK_BYTES = 292;  // f32 d, 256 x i8, 16 x i16 (ggml block_q
 //   [304, 320) 4 x (q8s[2i] | q8s[2i+1] << 16), q8s[j] = bsums[2j] + bsums[2j+1]  -- the Q4_K/Q5_K min pairs
 constexpr int Q8K_IMG_BYTES = 320;
 constexpr int Q8K_IMG_D = 256, Q8K_IMG_BSP = 272, Q8K_IMG_Q8S = 304;
+
+// The engine's device image of a row of Q8_0 blocks (the same values as block_q8_0, rearranged): the 32 codes
+// of every block back to back (32 bytes per block, 16-byte aligned), then per block {f32 d (the f16 scale,
+// converted exactly), i32 sum of the 32 codes} -- 40 bytes per block in all.
+constexpr int Q80_IMG_BYTES = 40;
 constexpr int Q8_0_BLOCK_BYTES = 34;  // f16 d, 32 x i8 (ggml block_q8_0)
 
 __host__ __device__ inline int block_elems(int t) {
+    t = tile_base_type(t);
     return (t == T_F32) ? 1 : (t == T_Q4_0 || t == T_Q8_0) ? 32 : 256;
 }
 __host__ __device__ inline int block_bytes(int t) {
@@ -48,6 +61,10 @@ __host__ __device__ inline int block_bytes(int t) {
     case T_Q6_K_SPLIT: return 210;  // 208 in the block array + 2 in the scale array
     default: return 0;
     }
+}
+__host__ __device__ inline bool is_q80(int t) {
+    t = tile_base_type(t);
+    return t == T_Q8_0 || t == T_Q4_0;
 }
 __host__ __device__ inline bool is_kquant(int t) {
     t = tile_base_type(t);
@@ -131,6 +148,29 @@ __device__ __forceinline__ void q8k_quantize_to_image(const float (&v)[8], uint8
     if (lane == 0) {
         ow[Q8K_IMG_D / 4] = __float_as_uint(__fdiv_rn(1.0f, iscale));
         ow[Q8K_IMG_D / 4 + 1] = ow[Q8K_IMG_D / 4 + 2] = ow[Q8K_IMG_D / 4 + 3] = 0u;
+    }
+}
+
+// One Q8_0 block quantised by a warp (lane i holds value i) into the row image: codes at `codes`, {d, sum} at
+// `meta`.  Bit-exact with crates/core/src/kernels/q8.rs:81-103: d = amax / 127 stored as f16, id = 1/d (0 for a
+// zero block), q = round-half-away(x * id) saturated to i8.
+__device__ __forceinline__ void q80_quantize_to_image(float v, uint8_t* __restrict__ codes, uint8_t* __restrict__ meta) {
+    const int lane = threadIdx.x & 31;
+    float amax = fabsf(v);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+    const float qf = roundf(__fmul_rn(v, id));
+    const int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
+    const uint32_t b = (uint32_t)(qi & 0xff) << (8 * (lane & 3));
+    uint32_t wv = b | __shfl_xor_sync(0xffffffffu, b, 1);
+    wv |= __shfl_xor_sync(0xffffffffu, wv, 2);
+    const int sum = __reduce_add_sync(0xffffffffu, qi);
+    if ((lane & 3) == 0) reinterpret_cast<uint32_t*>(codes)[lane >> 2] = wv;
+    if (lane == 0) {
+        reinterpret_cast<float*>(meta)[0] = __half2float(__float2half_rn(dd));
+        reinterpret_cast<int*>(meta)[1] = sum;
     }
 }
 

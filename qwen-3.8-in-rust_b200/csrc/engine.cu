@@ -142,13 +142,20 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     uint8_t* repack_tmp = nullptr;
     uint64_t repack_cap = 0;
     for (const TensorInfo& t : g.tensors())
-        if (is_kquant(t.type) && t.name != "token_embd.weight") repack_cap = std::max(repack_cap, t.byte_size);
+        if ((is_kquant(t.type) || t.type == T_Q8_0 || t.type == T_Q4_0) && t.name != "token_embd.weight")
+            repack_cap = std::max(repack_cap, t.byte_size);
     if (repack_cap) ck(cudaMalloc(&repack_tmp, repack_cap), "repack buffer");
     auto repack = [&](const TensorInfo& t, int rows, int cols) -> int {
         uint8_t* p = m->blob_ + t.rel_offset;
         ck(cudaMemcpy(repack_tmp, p, t.byte_size, cudaMemcpyDeviceToDevice), "repack copy");
         int type = t.type;
-        if (rows % 8 == 0 && ((uintptr_t)p & 15) == 0) {
+        const bool aligned = rows % 8 == 0 && ((uintptr_t)p & 15) == 0;
+        if ((t.type == T_Q8_0 || t.type == T_Q4_0) && aligned && cols % 256 == 0) {
+            ck(launch_repack_q80_tiles(t.type, repack_tmp, rows, cols, p, 0), "repack");
+            type = t.type == T_Q8_0 ? T_Q8_0_TILE : T_Q4_0_TILE;
+        } else if (t.type == T_Q8_0 || t.type == T_Q4_0) {
+            throw ConfigError("tensor " + t.name + ": Q8_0/Q4_0 matrices need rows % 8 == 0 and cols % 256 == 0 here");
+        } else if (aligned) {
             ck(launch_repack_tiles(t.type, repack_tmp, rows, cols, p, 0), "repack");
             type = t.type == T_Q4_K ? T_Q4_K_TILE : t.type == T_Q5_K ? T_Q5_K_TILE : T_Q6_K_TILE;
         } else if (t.type == T_Q6_K) {
@@ -171,7 +178,8 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         d.cols = (int)cols;
         d.p = ptr(t);
         d.bytes = t.byte_size;
-        if (is_kquant(t.type) && name != "token_embd.weight") d.type = repack(t, (int)rows, (int)cols);
+        if ((is_kquant(t.type) || t.type == T_Q8_0 || t.type == T_Q4_0) && name != "token_embd.weight")
+            d.type = repack(t, (int)rows, (int)cols);
         return d;
     };
     auto vec = [&](const std::string& name, uint64_t len) -> const float* {
@@ -284,7 +292,7 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
     const size_t H = c.hidden_size, FF = c.intermediate_size, T = T_;
     size_t maxw = std::max<size_t>(std::max<size_t>(2 * H, FF), std::max<size_t>(c.dn_v_dim, (size_t)c.n_head * c.head_dim_k));
     q8k_stride_ = maxw / 256 * Q8K_IMG_BYTES;  // the Q8_K device image
-    q80_stride_ = maxw / 32 * 34 + 64;
+    q80_stride_ = maxw / 32 * Q80_IMG_BYTES;  // the Q8_0 row image
     d_ids = (int32_t*)dalloc(T * 4);
     d_argmax = (int32_t*)dalloc(T * 4);
     d_pos = (int*)dalloc(4);
@@ -375,7 +383,7 @@ static bool needs_q8k(std::initializer_list<int> ts) {
     return false;
 }
 static bool needs_q80(std::initializer_list<int> ts) {
-    for (int t : ts) if (t == T_Q8_0 || t == T_Q4_0) return true;
+    for (int t : ts) if (is_q80(t)) return true;
     return false;
 }
 
@@ -387,9 +395,14 @@ void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y) {
         ck(launch_gemv_img(w.type, w.p, w.rows, w.cols, q8k_, rows, y, stream, true), "gemv");
         return;
     }
-    const void* act = w.type == T_F32 ? (const void*)normed_f32 : (const void*)q80_;
+    if (w.type == T_Q8_0_TILE || w.type == T_Q4_0_TILE) {
+        count_launch((rows + 3) / 4);
+        ck(launch_gemv_q80_img(w.type, w.p, w.rows, w.cols, q80_, rows, y, stream, true), "gemv");
+        return;
+    }
+    if (w.type != T_F32) throw std::logic_error("gemv: a Q8_0/Q4_0 matrix outside the tile layout");
     count_launch((rows + 3) / 4);
-    ck(launch_gemv(w.type, w.p, w.rows, w.cols, act, rows, y, stream), "gemv");
+    ck(launch_gemv(w.type, w.p, w.rows, w.cols, normed_f32, rows, y, stream), "gemv");
 }
 
 // h = h + delta (delta null: h as it is) into the other residual buffer, normed and quantised on the way.
@@ -404,7 +417,7 @@ void State::resid_norm(const float* delta, const float* w, int t, float* y_out, 
 }
 
 void State::quant_for(int type, const float* x, int n, int rows) {
-    count_launch(); ck(launch_quant_rows(x, n, rows, is_kquant(type) ? q8k_ : nullptr, (type == T_Q8_0 || type == T_Q4_0) ? q80_ : nullptr, stream),
+    count_launch(); ck(launch_quant_rows(x, n, rows, is_kquant(type) ? q8k_ : nullptr, is_q80(type) ? q80_ : nullptr, stream),
        "quantise");
 }
 
@@ -454,7 +467,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     gemv(L.ffn_up, normed_, t, u_);
     const int dt = L.ffn_down.type;
     count_launch(); ck(launch_swiglu_quant(g_, u_, (int)c.intermediate_size, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
-                           (dt == T_Q8_0 || dt == T_Q4_0) ? q80_ : nullptr, stream), "swiglu");
+                           is_q80(dt) ? q80_ : nullptr, stream), "swiglu");
     gemv(L.ffn_down, g_, t, mlp_out_);
 }
 
@@ -474,7 +487,7 @@ void State::forward_rows(int t, const int32_t* ids_dev, bool want_logits_all) {
     }
     // final norm (model.rs:430-438): the post-norm rows are what the lm_head and the MTP read
     const int ht = m_.lm_head.type;
-    resid_norm(mlp_out_, m_.output_norm, t, final_, is_kquant(ht), ht == T_Q8_0 || ht == T_Q4_0);
+    resid_norm(mlp_out_, m_.output_norm, t, final_, is_kquant(ht), is_q80(ht));
     if (capture_ && !capture_h_.empty())
         ck(cudaMemcpyAsync(capture_h_[m_.layers.size()], final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "capture");
     if (want_logits_all) {

@@ -381,53 +381,47 @@ q80_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nblk, const uint8_t
 
 // ---------------------------------------------------------------------------- F32 x f32
 
-// One warp per row (4 warps per CTA): lane j computes the 32-element partials of blocks j, j+32, ... (left to
-// right inside a block) into shared memory, then lane n < NC chains column n's block partials in order and adds
+// One warp per (row, column), 4 warps per CTA: lane j computes the 32-element partials of blocks j, j+32, ...
+// (left to right inside a block) into shared memory, then lane 0 chains the block partials in order and adds
 // the tail partial (dot.rs:180-198).
-template <int NC>
-__global__ void __launch_bounds__(128) f32_gemv_kernel(const float* __restrict__ w, int rows, int cols, const float* __restrict__ x,
-                                                       float* __restrict__ y) {
+__global__ void __launch_bounds__(128) f32_gemv_kernel(const float* __restrict__ w, int rows, int cols, int ncols,
+                                                       const float* __restrict__ x, float* __restrict__ y) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nfull = cols / 32, nparts = nfull + (cols % 32 ? 1 : 0);
-    float* part = reinterpret_cast<float*>(smem) + (size_t)warp * NC * (nfull + 1);
-    const int row = blockIdx.x * 4 + warp;
-    if (row >= rows) return;
+    float* part = reinterpret_cast<float*>(smem) + (size_t)warp * (nfull + 1);
+    const int item = blockIdx.x * 4 + warp;
+    if (item >= rows * ncols) return;
+    const int row = item / ncols, n = item % ncols;
     const float* wr = w + (size_t)row * cols;
+    const float* xr = x + (size_t)n * cols;
     const bool vec = (cols % 4) == 0;
     for (int j = lane; j < nparts; j += 32) {
         const int lo = j * 32, hi = min(cols, lo + 32);
-        float p[NC];
-#pragma unroll
-        for (int n = 0; n < NC; n++) p[n] = 0.0f;
+        float p = 0.0f;
         if (vec && hi - lo == 32) {
+            float4 wv[8], xv[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) wv[q] = __ldg(reinterpret_cast<const float4*>(wr + lo) + q), xv[q] = __ldg(reinterpret_cast<const float4*>(xr + lo) + q);
 #pragma unroll
             for (int q = 0; q < 8; q++) {
-                const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + lo) + q);
-#pragma unroll
-                for (int n = 0; n < NC; n++) {
-                    const float4 xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)n * cols + lo) + q);
-                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.x, xv.x));
-                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.y, xv.y));
-                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.z, xv.z));
-                    p[n] = __fadd_rn(p[n], __fmul_rn(wv.w, xv.w));
-                }
+                p = __fadd_rn(p, __fmul_rn(wv[q].x, xv[q].x));
+                p = __fadd_rn(p, __fmul_rn(wv[q].y, xv[q].y));
+                p = __fadd_rn(p, __fmul_rn(wv[q].z, xv[q].z));
+                p = __fadd_rn(p, __fmul_rn(wv[q].w, xv[q].w));
             }
         } else {
-            for (int i = lo; i < hi; i++)
-#pragma unroll
-                for (int n = 0; n < NC; n++) p[n] = __fadd_rn(p[n], __fmul_rn(wr[i], x[(size_t)n * cols + i]));
+            for (int i = lo; i < hi; i++) p = __fadd_rn(p, __fmul_rn(wr[i], xr[i]));
         }
-#pragma unroll
-        for (int n = 0; n < NC; n++) part[n * (nfull + 1) + j] = p[n];
+        part[j] = p;
     }
     __syncwarp();
-    if (lane < NC) {
-        const float* pp = part + lane * (nfull + 1);
+    if (lane == 0) {
         float acc = 0.0f;
-        for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, pp[j]);
-        acc = __fadd_rn(acc, nparts > nfull ? pp[nfull] : 0.0f);  // the tail partial, +0 when empty (dot.rs:194-197)
-        y[(size_t)lane * rows + row] = acc;
+#pragma unroll 8
+        for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, part[j]);
+        acc = __fadd_rn(acc, nparts > nfull ? part[nfull] : 0.0f);  // the tail partial, +0 when empty (dot.rs:194-197)
+        y[(size_t)n * rows + row] = acc;
     }
 }
 
@@ -490,13 +484,9 @@ cudaError_t launch_q80(const uint8_t* w, int rows, int cols, const void* act, fl
 
 template <int NC>
 cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
-    const size_t smem = (size_t)4 * NC * (cols / 32 + 1) * 4;
-    auto kern = f32_gemv_kernel<NC>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    kern<<<(rows + 3) / 4, 128, smem, s>>>((const float*)w, rows, cols, (const float*)act, y);
+    const size_t smem = (size_t)4 * (cols / 32 + 1) * 4;
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;  // cols > 12000: not a shape of this model family
+    f32_gemv_kernel<<<(rows * NC + 3) / 4, 128, smem, s>>>((const float*)w, rows, cols, NC, (const float*)act, y);
     return cudaGetLastError();
 }
 
@@ -520,6 +510,14 @@ cudaError_t dispatch_type(int type, const uint8_t* w, int rows, int cols, const 
 }
 
 }  // namespace
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("QDEC_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 int num_sms() {
     if (g_num_sms == 0) {

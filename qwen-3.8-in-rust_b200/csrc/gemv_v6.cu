@@ -461,7 +461,7 @@ cudaError_t launch_tile(const uint8_t* w, int rows, int nb, const void* img, flo
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kq_gemv_tile_kernel<TYPE, NC, R, D, FPS>, w, rows, nb, (const uint8_t*)img, y);
 }
 
@@ -603,7 +603,7 @@ cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, fl
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS>, w, rows, nb, (const uint8_t*)img, y);
 }
 
@@ -617,7 +617,9 @@ template <int TYPE, int NC>
 cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr bool KQ = TYPE != T_Q6_K;
     int cfg = g_tile_cfg;
-    if (cfg == 0) cfg = NC == 1 ? 1 : 7;
+    // measured on B200 (17408 x 5120 ... 248320 x 5120): the vocabulary-size matrix streams best as plain tiles
+    // (two per warp, two super-blocks in flight); everything else with the super-block range split over 4 warps
+    if (cfg == 0) cfg = rows >= 65536 ? 4 : (NC == 1 ? 9 : 10);
     switch (cfg) {
     case 1: return launch_tile<TYPE, NC, 1, 4, false>(w, rows, nb, img, y, s, pdl);
     case 2: return launch_tile<TYPE, NC, 1, 8, false>(w, rows, nb, img, y, s, pdl);
@@ -697,7 +699,7 @@ cudaError_t launch_v6(const uint8_t* w, const uint16_t* dsplit, int rows, int nb
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;  // without the attribute griddepcontrol.wait returns at once
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;  // without the attribute griddepcontrol.wait returns at once
     return cudaLaunchKernelEx(&cfg, kq_gemv_v6_kernel<TYPE, NC, GL, R, D, FPS>, w, dsplit, rows, nb, (const uint8_t*)img, y);
 }
 

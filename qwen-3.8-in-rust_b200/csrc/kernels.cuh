@@ -9,6 +9,8 @@ namespace qdec {
 __global__ void q8k_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
 __global__ void q8k_image_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ img);
 __global__ void q8k_raw_to_image_kernel(const uint8_t* __restrict__ raw, long long nblocks, uint8_t* __restrict__ img);
+__global__ void q80_image_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ img);
+__global__ void q80_raw_to_image_kernel(const uint8_t* __restrict__ raw, int nb, int rows, uint8_t* __restrict__ img);
 __global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out);
 __global__ void dequant_rows_kernel(int type, const uint8_t* __restrict__ w, size_t row_bytes, int n,
                                     const int32_t* __restrict__ ids, int nids, float* __restrict__ out);
@@ -46,6 +48,12 @@ void set_gemv_v6_config(int cfg);
 cudaError_t launch_repack_q6k(const uint8_t* src, size_t nblocks, uint8_t* dst, cudaStream_t s);
 // ggml Q4_K / Q5_K / Q6_K rows (rows % 8 == 0) -> the tile layout (gemv_v6.cu); dst holds the same bytes.
 cudaError_t launch_repack_tiles(int ggml_type, const uint8_t* src, int rows, int cols, uint8_t* dst, cudaStream_t s);
+// Q8_0 / Q4_0: the engine's Q8_0 row image (common.cuh), the tile layout, and the GEMV over both (gemv_q80.cu).
+cudaError_t launch_quantize_q80_image(const float* x, int n, int rows, uint8_t* img, cudaStream_t s);
+cudaError_t launch_q80_raw_to_image(const uint8_t* raw, int n, int rows, uint8_t* img, cudaStream_t s);
+cudaError_t launch_repack_q80_tiles(int ggml_type, const uint8_t* src, int rows, int cols, uint8_t* dst, cudaStream_t s);
+cudaError_t launch_gemv_q80_img(int type, const uint8_t* w, int rows, int cols, const void* img, int ncols, float* y,
+                                cudaStream_t s, bool pdl);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
 

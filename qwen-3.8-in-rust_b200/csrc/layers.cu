@@ -52,8 +52,9 @@ __device__ __forceinline__ float inv_rms_of(float ss, int n, float eps) {
 }
 
 // Quantise the 256 values of one chunk held in shared memory: warp 0 writes the Q8_K image block
-// (q8k.rs:76-114), warps 0..7 the eight Q8_0 blocks (q8.rs:81-103).  Block of 256 threads.
-__device__ void quant_chunk(const float* xs, uint8_t* img_blk, uint8_t* q80_blk) {
+// (q8k.rs:76-114), warps 0..7 the chunk's eight Q8_0 blocks into the row's Q8_0 image (q8.rs:81-103), whose
+// codes start at q80_row and {d, sum} entries after the row's n/32 blocks of codes.  Block of 256 threads.
+__device__ void quant_chunk(const float* xs, uint8_t* img_blk, uint8_t* q80_row, int n, int chunk) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (img_blk && warp == 0) {
         float v[8];
@@ -61,19 +62,9 @@ __device__ void quant_chunk(const float* xs, uint8_t* img_blk, uint8_t* q80_blk)
         for (int i = 0; i < 8; i++) v[i] = xs[lane * 8 + i];
         q8k_quantize_to_image(v, img_blk);
     }
-    if (q80_blk && warp < 8) {
-        const float v = xs[warp * 32 + lane];
-        float amax = fabsf(v);
-        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float dd = __fdiv_rn(amax, 127.0f);
-        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-        const float qf = roundf(__fmul_rn(v, id));  // round half away from zero, then `as i8` (saturating)
-        const int qi = qf > 127.0f ? 127 : (qf < -128.0f ? -128 : (int)qf);
-        const int lo = __shfl_sync(0xffffffffu, qi, (2 * lane - 2) & 31);
-        const int hi = __shfl_sync(0xffffffffu, qi, (2 * lane - 1) & 31);
-        uint16_t* o = reinterpret_cast<uint16_t*>(q80_blk + (size_t)warp * Q8_0_BLOCK_BYTES);
-        if (lane == 0) o[0] = __half_as_ushort(__float2half_rn(dd));
-        else if (lane <= 16) o[lane] = (uint16_t)((lo & 0xff) | ((hi & 0xff) << 8));
+    if (q80_row && warp < 8) {
+        const int blk = chunk * 8 + warp;
+        q80_quantize_to_image(xs[warp * 32 + lane], q80_row + (size_t)blk * 32, q80_row + (size_t)(n / 32) * 32 + (size_t)blk * 8);
     }
 }
 
@@ -115,7 +106,7 @@ resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b
     if (y_out) y_out[(size_t)row * n + c0 + threadIdx.x] = y;
     __syncthreads();
     quant_chunk(ys, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
-                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
+                q80_out ? q80_out + (size_t)row * (n / 32) * Q80_IMG_BYTES : nullptr, n, blockIdx.x);
 }
 
 // One CTA per row: y[row * y_ld + i] = rmsnorm(x[row * x_ld ..], w)[i] (rmsnorm.rs:25-33).
@@ -145,7 +136,7 @@ swiglu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, in
     if (h_out) h_out[i] = h;
     __syncthreads();
     quant_chunk(hs, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
-                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
+                q80_out ? q80_out + (size_t)row * (n / 32) * Q80_IMG_BYTES : nullptr, n, blockIdx.x);
 }
 
 // Grid (n / 256, rows), 256 threads: quantise rows already in global memory (the mixer outputs).
@@ -158,7 +149,7 @@ quant_rows_kernel(const float* __restrict__ x, int n, uint8_t* __restrict__ img_
     hs[threadIdx.x] = x[(size_t)row * n + blockIdx.x * 256 + threadIdx.x];
     __syncthreads();
     quant_chunk(hs, img_out ? img_out + ((size_t)row * (n / 256) + blockIdx.x) * Q8K_IMG_BYTES : nullptr,
-                q80_out ? q80_out + ((size_t)row * (n / 32) + blockIdx.x * 8) * Q8_0_BLOCK_BYTES : nullptr);
+                q80_out ? q80_out + (size_t)row * (n / 32) * Q80_IMG_BYTES : nullptr, n, blockIdx.x);
 }
 
 // Causal depthwise conv1d (+ SiLU) for t rows, one thread per channel (conv.rs:11-36).  The committed window
@@ -450,7 +441,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 }  // namespace

@@ -100,6 +100,44 @@ __global__ void q8k_raw_to_image_kernel(const uint8_t* __restrict__ raw, long lo
     }
 }
 
+// f32 rows -> the engine's Q8_0 row image (common.cuh), one warp per 32-value block.
+__global__ void q80_image_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ img) {
+    const int nb = n / 32;
+    const long long total = (long long)rows * nb;
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < total; b += nwarps) {
+        const long long r = b / nb, blk = b % nb;
+        uint8_t* row = img + r * nb * Q80_IMG_BYTES;
+        q80_quantize_to_image(x[r * (long long)n + blk * 32 + lane], row + blk * 32, row + (size_t)nb * 32 + blk * 8);
+    }
+}
+
+// block_q8_0 rows -> the Q8_0 row image: the same values, rearranged (one warp per block).
+__global__ void q80_raw_to_image_kernel(const uint8_t* __restrict__ raw, int nb, int rows, uint8_t* __restrict__ img) {
+    const long long total = (long long)rows * nb;
+    const int lane = threadIdx.x & 31;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < total; b += nwarps) {
+        const long long r = b / nb, blk = b % nb;
+        const uint8_t* src = raw + b * Q8_0_BLOCK_BYTES;
+        uint8_t* row = img + r * nb * Q80_IMG_BYTES;
+        const int q = (int)(int8_t)src[2 + lane];
+        const uint32_t bb = (uint32_t)(q & 0xff) << (8 * (lane & 3));
+        uint32_t wv = bb | __shfl_xor_sync(0xffffffffu, bb, 1);
+        wv |= __shfl_xor_sync(0xffffffffu, wv, 2);
+        const int sum = __reduce_add_sync(0xffffffffu, q);
+        if ((lane & 3) == 0) reinterpret_cast<uint32_t*>(row + blk * 32)[lane >> 2] = wv;
+        if (lane == 0) {
+            uint8_t* meta = row + (size_t)nb * 32 + blk * 8;
+            reinterpret_cast<float*>(meta)[0] = f16_bits_to_f32((uint16_t)(src[0] | (src[1] << 8)));
+            reinterpret_cast<int*>(meta)[1] = sum;
+        }
+    }
+}
+
 // One warp per 32-value block; lane i holds value i.
 __global__ void q8_0_quantize_kernel(const float* __restrict__ x, int n, int rows, uint8_t* __restrict__ out) {
     const int nb = n / 32;

@@ -63,11 +63,15 @@ def lib():
             "qdec_repack_q6k": [P, I, I, P, P],
             "qdec_repack_tiles": [I, P, I, I, P, P],
             "qdec_tune_gemv": [I, I],
+            "qdec_quantize_image": [I, P, I, I, P, P],
+            "qdec_gemv_image": [I, P, I, I, P, I, P, P],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
             fn.argtypes = args
         L.qdec_act_row_bytes.restype = S
+        L.qdec_image_row_bytes.restype = S
+        L.qdec_image_row_bytes.argtypes = [I, I]
         L.qdec_act_row_bytes.argtypes = [I, I]
         L.qdec_matvec_noalloc_max_bytes.restype = S
         L.qdec_matvec_noalloc_max_bytes.argtypes = []
@@ -152,6 +156,19 @@ def matvec_noalloc_max_bytes():
     return lib().qdec_matvec_noalloc_max_bytes()
 
 
+def image_row_bytes(t, cols):
+    return lib().qdec_image_row_bytes(t, cols)
+
+
+def quantize_image(t, x_ptr, n, rows, img_ptr, stream=0):
+    """f32 rows -> the activation image weights of type t read (Q8_K image or Q8_0 image)."""
+    _check(lib().qdec_quantize_image(t, x_ptr, n, rows, img_ptr, stream))
+
+
+def gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream=0):
+    _check(lib().qdec_gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream))
+
+
 def tune_gemv(impl=0, config=0):
     """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
     image kernel's configuration (0 automatic, 1..8). Results are identical for every value."""
@@ -163,7 +180,7 @@ def repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream=0):
     _check(lib().qdec_repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream))
 
 
-TILE = {12: 112, 13: 113, 14: 116}
+TILE = {12: 112, 13: 113, 14: 116, 8: 108, 2: 102}
 
 
 def repack_q6k(src_ptr, rows, cols, dst_ptr, stream=0):

@@ -283,3 +283,46 @@ def test_tile_repack_rejects_ragged_rows(q):
     dst = torch.empty_like(src)
     with pytest.raises(q.QdecError):
         q.repack_tiles(12, src.data_ptr(), 12, 256, dst.data_ptr())
+
+
+@pytest.mark.parametrize("t", [8, 2])
+def test_gemv_q80_tile_layout_bit_exact(q, orc, t):
+    """Q8_0 / Q4_0 weights in the tile layout (8 rows x 8 blocks per tile block) against the Q8_0 activation
+    image: the oracle's bits for 1..5 columns, from f32 columns and from block_q8_0 columns."""
+    rows, cols = 8 * 29, 6144
+    w = random_blocks(t, rows, cols, seed=57 + t)
+    x = np.random.default_rng(t).standard_normal((5, cols)).astype(np.float32)
+    x[2] *= 1e-25
+    x[4, :40] = 0.0
+    want = orc.matmul(t, w, rows, cols, x)
+    src = to_dev(w)
+    dst = torch.empty_like(src)
+    q.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr())
+    torch.cuda.synchronize()
+    for n in (1, 2, 3, 4, 5):
+        got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
+        assert bits_equal(got, want[:n]), (t, n)
+    act = to_dev(np.ascontiguousarray(gpu_q8_0(q, x[:4])).reshape(-1))
+    y = torch.empty(4 * rows, dtype=torch.float32, device="cuda")
+    q.gemv(q.TILE[t], dst.data_ptr(), rows, cols, act.data_ptr(), 4, y.data_ptr())
+    torch.cuda.synchronize()
+    assert bits_equal(y.cpu().numpy().reshape(4, rows), want[:4])
+
+
+@pytest.mark.parametrize("t,base", [(112, 12), (116, 14), (108, 8), (102, 2)])
+def test_gemv_image_entry_points(q, orc, t, base):
+    """qdec_quantize_image + qdec_gemv_image (activations already in the library's image) give the oracle's bits."""
+    rows, cols = 64, 5120
+    w = random_blocks(base, rows, cols, seed=t)
+    x = np.random.default_rng(t).standard_normal((3, cols)).astype(np.float32)
+    want = orc.matmul(base, w, rows, cols, x)
+    src = to_dev(w)
+    dst = torch.empty_like(src)
+    q.repack_tiles(base, src.data_ptr(), rows, cols, dst.data_ptr())
+    xd = to_dev(x)
+    img = torch.empty(3 * q.image_row_bytes(t, cols), dtype=torch.uint8, device="cuda")
+    q.quantize_image(t, xd.data_ptr(), cols, 3, img.data_ptr())
+    y = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+    q.gemv_image(t, dst.data_ptr(), rows, cols, img.data_ptr(), 3, y.data_ptr())
+    torch.cuda.synchronize()
+    assert bits_equal(y.cpu().numpy().reshape(3, rows), want)
