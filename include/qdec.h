@@ -91,10 +91,11 @@ int qdec_quantize_image(int ggml_type, const float *x_dev, int n, int rows, void
 int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const void *img_dev, int n_cols, float *y_dev,
                     void *stream);
 
-/* Tuning knob of the K-quant GEMV (process-wide): the kernel (0 = automatic; 2 = the kernel that reads
+/* Tuning knob of the GEMV (process-wide): the K-quant kernel (0 = automatic; 2 = the kernel that reads
  * block_q8_K activations in the reference layout; 6 = the kernel that reads the library's activation image) and
- * the image kernel's configuration (0 = automatic, 1..8: lanes per thread, rows per thread, super-blocks in
- * flight, integer or FP32 scale multiply).  Results do not depend on it; it exists for tests and sweeps.
+ * the image kernel's configuration (0 = automatic, 1..21: lanes and rows per thread, tiles per warp, warps per
+ * tile, super-blocks in flight, integer or FP32 scale multiply); or, with impl = 8, the Q8_0 / Q4_0 tile kernel
+ * (config 0 = automatic, 1 = one warp per tile, 2 = the group range split over 4 warps).  Results do not depend on it; it exists for tests and sweeps.
  * No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
 

@@ -226,8 +226,13 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
 }
 
 int qdec_tune_gemv(int impl, int config) {
-    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2 or 6");
-    if (config < 0 || config > 14) return fail(QDEC_EINVAL, "gemv configuration must be 0..14");
+    if (impl == 8) {  // the Q8_0 / Q4_0 tile kernel: 0 automatic, 1 one warp per tile, 2 split group range
+        if (config < 0 || config > 2) return fail(QDEC_EINVAL, "Q8_0 gemv configuration must be 0, 1 or 2");
+        set_q80_split(config - 1);
+        return QDEC_OK;
+    }
+    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6 or 8");
+    if (config < 0 || config > 21) return fail(QDEC_EINVAL, "gemv configuration must be 0..21");
     set_gemv_impl(impl);
     set_gemv_v6_config(config);
     return QDEC_OK;

@@ -449,8 +449,16 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         resid_norm(li == 0 ? nullptr : mlp_out_, L.attn_norm, t, normed_, k8, k0);
         gemv(L.qkv, normed_, t, qkv_);
         gemv(L.gate_z, normed_, t, z_);
-        gemv(L.alpha, normed_, t, alpha_);
-        gemv(L.beta, normed_, t, beta_);
+        if (L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == L.beta.cols) {
+            // ssm_alpha and ssm_beta read the same normed rows: one launch (gated_deltanet.rs:148-149)
+            count_launch();
+            ck(launch_gemv_f32_pair((const float*)L.alpha.p, L.alpha.rows, alpha_, (const float*)L.beta.p, L.beta.rows, beta_,
+                                    L.alpha.cols, normed_, t, stream),
+               "alpha/beta");
+        } else {
+            gemv(L.alpha, normed_, t, alpha_);
+            gemv(L.beta, normed_, t, beta_);
+        }
         count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, (int)c.dn_qkv_dim, qkv_, t, conved_, d.pend_x,
                             commit_dn ? d_keep : nullptr, T_, stream), "conv");
         DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,

@@ -381,22 +381,22 @@ q80_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nblk, const uint8_t
 
 // ---------------------------------------------------------------------------- F32 x f32
 
-// One warp per (row, column), 4 warps per CTA: lane j computes the 32-element partials of blocks j, j+32, ...
-// (left to right inside a block) into shared memory, then lane 0 chains the block partials in order and adds
-// the tail partial (dot.rs:180-198).
-__global__ void __launch_bounds__(128) f32_gemv_kernel(const float* __restrict__ w, int rows, int cols, int ncols,
-                                                       const float* __restrict__ x, float* __restrict__ y) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nfull = cols / 32, nparts = nfull + (cols % 32 ? 1 : 0);
-    float* part = reinterpret_cast<float*>(smem) + (size_t)warp * (nfull + 1);
-    const int item = blockIdx.x * 4 + warp;
-    if (item >= rows * ncols) return;
-    const int row = item / ncols, n = item % ncols;
-    const float* wr = w + (size_t)row * cols;
+// One CTA per (row, column) of up to two matrices sharing the input columns (rows [0, rows_a) of w_a, then
+// [0, rows_b) of w_b): thread j computes the 32-element partial of block j (left to right), then thread 0 chains
+// the block partials in order and adds the tail partial (dot.rs:180-198).  All partials of a row are computed at
+// once, so the row costs one load latency plus the two dependent chains.
+__global__ void __launch_bounds__(256) f32_gemv_kernel(const float* __restrict__ w_a, int rows_a, float* __restrict__ y_a,
+                                                       const float* __restrict__ w_b, int rows_b, float* __restrict__ y_b,
+                                                       int cols, const float* __restrict__ x) {
+    __shared__ float part[512];
+    const int n = blockIdx.y;
+    const bool first = (int)blockIdx.x < rows_a;
+    const int row = first ? blockIdx.x : blockIdx.x - rows_a;
+    const float* wr = (first ? w_a : w_b) + (size_t)row * cols;
     const float* xr = x + (size_t)n * cols;
+    const int nfull = cols / 32, nparts = nfull + (cols % 32 ? 1 : 0);
     const bool vec = (cols % 4) == 0;
-    for (int j = lane; j < nparts; j += 32) {
+    for (int j = threadIdx.x; j < nparts; j += blockDim.x) {
         const int lo = j * 32, hi = min(cols, lo + 32);
         float p = 0.0f;
         if (vec && hi - lo == 32) {
@@ -415,13 +415,13 @@ __global__ void __launch_bounds__(128) f32_gemv_kernel(const float* __restrict__
         }
         part[j] = p;
     }
-    __syncwarp();
-    if (lane == 0) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
         float acc = 0.0f;
 #pragma unroll 8
         for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, part[j]);
         acc = __fadd_rn(acc, nparts > nfull ? part[nfull] : 0.0f);  // the tail partial, +0 when empty (dot.rs:194-197)
-        y[(size_t)n * rows + row] = acc;
+        (first ? y_a : y_b)[(size_t)n * (first ? rows_a : rows_b) + row] = acc;
     }
 }
 
@@ -484,10 +484,7 @@ cudaError_t launch_q80(const uint8_t* w, int rows, int cols, const void* act, fl
 
 template <int NC>
 cudaError_t launch_f32(const uint8_t* w, int rows, int cols, const void* act, float* y, cudaStream_t s) {
-    const size_t smem = (size_t)4 * (cols / 32 + 1) * 4;
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;  // cols > 12000: not a shape of this model family
-    f32_gemv_kernel<<<(rows * NC + 3) / 4, 128, smem, s>>>((const float*)w, rows, cols, NC, (const float*)act, y);
-    return cudaGetLastError();
+    return launch_gemv_f32_pair((const float*)w, rows, y, nullptr, 0, nullptr, cols, (const float*)act, NC, s);
 }
 
 int g_gemv_impl = [] {
@@ -557,6 +554,14 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
         c0 += nc;
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_gemv_f32_pair(const float* w_a, int rows_a, float* y_a, const float* w_b, int rows_b, float* y_b, int cols,
+                                 const float* x, int ncols, cudaStream_t s) {
+    if (cols > 512 * 32) return cudaErrorInvalidValue;  // 512 partials of shared memory: cols <= 16384
+    if (rows_a + rows_b == 0 || ncols == 0) return cudaSuccess;
+    f32_gemv_kernel<<<dim3(rows_a + rows_b, ncols), 256, 0, s>>>(w_a, rows_a, y_a, w_b, rows_b, y_b, cols, x);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_quantize_q8k(const float* x, int n, int rows, uint8_t* out, cudaStream_t s) {

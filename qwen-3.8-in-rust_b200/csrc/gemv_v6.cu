@@ -126,7 +126,7 @@ struct Dec<T_Q6_K, GL> {
     float dw;
 };
 
-template <int TYPE, int GL, bool FPS>
+template <int TYPE, int GL, int FPS>
 __device__ __forceinline__ void decode(const Frag<TYPE, GL>& f, int tg, Dec<TYPE, GL>& o) {
     const int g0 = tg * GL;
     if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
@@ -139,9 +139,9 @@ __device__ __forceinline__ void decode(const Frag<TYPE, GL>& f, int tg, Dec<TYPE
             o.sc[s] = (int)((sc03 >> (8 * s)) & 0xff);
             o.sc[s + 4] = (int)((sc47 >> (8 * s)) & 0xff);
         }
-        if constexpr (FPS) {
+        if constexpr (FPS != 0) {
 #pragma unroll
-            for (int s = 0; s < 8; s++) o.scf[s] = __fsub_rn(__int_as_float(0x4B000000 | o.sc[s]), 8388608.0f);
+            for (int s = (FPS == 2 ? 4 : 0); s < 8; s++) o.scf[s] = __fsub_rn(__int_as_float(0x4B000000 | o.sc[s]), 8388608.0f);
         }
 #pragma unroll
         for (int p = 0; p < 4; p++)
@@ -182,15 +182,26 @@ __device__ __forceinline__ void decode(const Frag<TYPE, GL>& f, int tg, Dec<TYPE
 }
 
 // The reference's integer lane sum of lane gi (as an exact f32) for one column.
-template <int TYPE, int GL, bool FPS>
+template <int TYPE, int GL, int FPS>
 __device__ __forceinline__ float lane_sum(const Dec<TYPE, GL>& o, const uint32_t* xw, int gi, uint32_t bsp) {
     if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        if constexpr (FPS) {
+        if constexpr (FPS == 1) {
             float a = 0.0f;
 #pragma unroll
             for (int s = 0; s < 8; s++)
                 a = __fmaf_rn(o.scf[s], biased_to_f32(__dp4a((int)o.code[s][gi], (int)xw[gi * 8 + s], MAGIC_I)), a);
             return a;  // every partial sum is an integer of magnitude < 2^23: exact
+        } else if constexpr (FPS == 2) {
+            // sub-blocks 0..3 on the integer pipe, 4..7 on the FP32 pipe; each half's sum is below 2^22 in
+            // magnitude (Q5_K: 4 * 63 * 4 * 31 * 127 < 2^22), so both halves and their sum are exact
+            int sumi = MAGIC_I;
+#pragma unroll
+            for (int s = 0; s < 4; s++) sumi += o.sc[s] * __dp4a((int)o.code[s][gi], (int)xw[gi * 8 + s], 0);
+            float a = 0.0f;
+#pragma unroll
+            for (int s = 4; s < 8; s++)
+                a = __fmaf_rn(o.scf[s], biased_to_f32(__dp4a((int)o.code[s][gi], (int)xw[gi * 8 + s], MAGIC_I)), a);
+            return __fadd_rn(biased_to_f32(sumi), a);
         } else if constexpr (TYPE == T_Q4_K) {
             int sumi = MAGIC_I;  // |sum| <= 8 * 63 * 4 * 15 * 127 < 2^22
 #pragma unroll
@@ -211,7 +222,7 @@ __device__ __forceinline__ float lane_sum(const Dec<TYPE, GL>& o, const uint32_t
     }
 }
 
-template <int TYPE, int NC, int GL, int R, int D, bool FPS>
+template <int TYPE, int NC, int GL, int R, int D, int FPS>
 __global__ void __launch_bounds__(32)
 kq_gemv_v6_kernel(const uint8_t* __restrict__ w, const uint16_t* __restrict__ dsplit, int rows, int nb,
                   const uint8_t* __restrict__ img, float* __restrict__ y) {
@@ -356,7 +367,7 @@ __device__ __forceinline__ void load_frag_tile(const uint8_t* ts, int L, int rs,
 }
 
 // One warp = R tiles (8R rows); thread L = 4 * rs + tg owns row rs of each tile and lanes 2tg, 2tg+1.
-template <int TYPE, int NC, int R, int D, bool FPS>
+template <int TYPE, int NC, int R, int D, int FPS>
 __global__ void __launch_bounds__(32)
 kq_gemv_tile_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8_t* __restrict__ img, float* __restrict__ y) {
     constexpr int GL = 2, TB = TileB<TYPE>::value;
@@ -450,7 +461,7 @@ kq_gemv_tile_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8
         }
 }
 
-template <int TYPE, int NC, int R, int D, bool FPS>
+template <int TYPE, int NC, int R, int D, int FPS>
 cudaError_t launch_tile(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((rows / 8 + R - 1) / R);
@@ -476,8 +487,8 @@ struct SplitTerms {  // one window buffer: [S][R][NC][8 rows][12] (8 main lanes,
     static constexpr int PER_SB = R * NC * 8 * 12;
 };
 
-template <int TYPE, int NC, int R, int D, int S, bool FPS>
-__global__ void __launch_bounds__(32 * S)
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1>
+__global__ void __launch_bounds__(32 * S, MINB)
 kq_gemv_split_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8_t* __restrict__ img, float* __restrict__ y) {
     constexpr int GL = 2, TB = TileB<TYPE>::value, PER_SB = SplitTerms<NC, R>::PER_SB;
     constexpr bool Q6 = TYPE == T_Q6_K;
@@ -567,7 +578,9 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint
                         constexpr int LPC = Q6 ? 8 : 12;
                         const int slot = (ci / LPC) * 12 + ci % LPC;
                         float a = cacc[c];
-                        for (int k = 0; k < nsb; k++) a = __fadd_rn(a, tw[k * PER_SB + slot]);
+#pragma unroll
+                        for (int k = 0; k < S; k++)
+                            if (k < nsb) a = __fadd_rn(a, tw[k * PER_SB + slot]);
                         cacc[c] = a;
                     }
                 }
@@ -592,7 +605,7 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint
     }
 }
 
-template <int TYPE, int NC, int R, int D, int S, bool FPS>
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1>
 cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((rows / 8 + R - 1) / R);
@@ -604,7 +617,7 @@ cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, fl
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS>, w, rows, nb, (const uint8_t*)img, y);
+    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS, MINB>, w, rows, nb, (const uint8_t*)img, y);
 }
 
 int g_tile_cfg = [] {
@@ -617,9 +630,10 @@ template <int TYPE, int NC>
 cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr bool KQ = TYPE != T_Q6_K;
     int cfg = g_tile_cfg;
-    // measured on B200 (17408 x 5120 ... 248320 x 5120): the vocabulary-size matrix streams best as plain tiles
-    // (two per warp, two super-blocks in flight); everything else with the super-block range split over 4 warps
-    if (cfg == 0) cfg = rows >= 65536 ? 4 : (NC == 1 ? 9 : 10);
+    // measured on B200 (shapes 5120 x 17408 ... 248320 x 5120): the super-block range split over 4 warps, two
+    // tiles per warp, one super-block in flight per warp, at most 128 registers (4 CTAs per SM); for one column
+    // on short matrices one tile per warp and two in flight
+    if (cfg == 0) cfg = (NC == 1 && rows <= 6144) ? 9 : 20;
     switch (cfg) {
     case 1: return launch_tile<TYPE, NC, 1, 4, false>(w, rows, nb, img, y, s, pdl);
     case 2: return launch_tile<TYPE, NC, 1, 8, false>(w, rows, nb, img, y, s, pdl);
@@ -634,7 +648,14 @@ cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img,
     case 11: return launch_split<TYPE, NC, 1, 2, 4, KQ>(w, rows, nb, img, y, s, pdl);
     case 12: return launch_split<TYPE, NC, 2, 2, 4, KQ>(w, rows, nb, img, y, s, pdl);
     case 13: return launch_split<TYPE, NC, 2, 2, 2, KQ>(w, rows, nb, img, y, s, pdl);
-    default: return launch_split<TYPE, NC, 1, 4, 2, KQ>(w, rows, nb, img, y, s, pdl);
+    case 14: return launch_split<TYPE, NC, 1, 4, 2, KQ>(w, rows, nb, img, y, s, pdl);
+    case 15: return launch_split<TYPE, NC, 2, 2, 4, KQ ? 2 : 0>(w, rows, nb, img, y, s, pdl);
+    case 16: return launch_split<TYPE, NC, 1, 2, 4, KQ ? 2 : 0>(w, rows, nb, img, y, s, pdl);
+    case 17: return launch_tile<TYPE, NC, 2, 2, KQ ? 2 : 0>(w, rows, nb, img, y, s, pdl);
+    case 18: return launch_split<TYPE, NC, 2, 2, 4, 0, 4>(w, rows, nb, img, y, s, pdl);
+    case 19: return launch_split<TYPE, NC, 2, 2, 4, 0, 5>(w, rows, nb, img, y, s, pdl);
+    case 20: return launch_split<TYPE, NC, 2, 1, 4, 0, 4>(w, rows, nb, img, y, s, pdl);
+    default: return launch_split<TYPE, NC, 2, 2, 2, 0, 8>(w, rows, nb, img, y, s, pdl);
     }
 }
 
@@ -687,7 +708,7 @@ __global__ void repack_tiles_kernel(const uint8_t* __restrict__ src, int nb, uin
     }
 }
 
-template <int TYPE, int NC, int GL, int R, int D, bool FPS>
+template <int TYPE, int NC, int GL, int R, int D, int FPS>
 cudaError_t launch_v6(const uint8_t* w, const uint16_t* dsplit, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr int RPC = 4 * GL * R;  // rows per CTA (one warp)
     cudaLaunchConfig_t cfg = {};

@@ -25,6 +25,10 @@ cudaError_t launch_dequant_rows(int type, const uint8_t* w, size_t row_bytes, in
 // block_q8_K rows (K-quants), block_q8_0 rows (Q8_0, Q4_0) or f32 rows (F32), `ncols` rows back to back.
 cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const void* act, int ncols, float* y,
                         cudaStream_t s);
+// F32 weights: rows of w_a then rows of w_b (w_b may be null) against the same f32 columns, y_a / y_b laid out
+// [column][row]; cols <= 16384.
+cudaError_t launch_gemv_f32_pair(const float* w_a, int rows_a, float* y_a, const float* w_b, int rows_b, float* y_b, int cols,
+                                 const float* x, int ncols, cudaStream_t s);
 // Bytes of one activation row of `cols` values in the form `type` consumes (reference layouts).
 size_t act_row_bytes(int type, int cols);
 int num_sms();
@@ -52,6 +56,8 @@ cudaError_t launch_repack_tiles(int ggml_type, const uint8_t* src, int rows, int
 cudaError_t launch_quantize_q80_image(const float* x, int n, int rows, uint8_t* img, cudaStream_t s);
 cudaError_t launch_q80_raw_to_image(const uint8_t* raw, int n, int rows, uint8_t* img, cudaStream_t s);
 cudaError_t launch_repack_q80_tiles(int ggml_type, const uint8_t* src, int rows, int cols, uint8_t* dst, cudaStream_t s);
+// Tuning: -1 = automatic, 0 = one warp per tile, 1 = the group range split over 4 warps.
+void set_q80_split(int mode);
 cudaError_t launch_gemv_q80_img(int type, const uint8_t* w, int rows, int cols, const void* img, int ncols, float* y,
                                 cudaStream_t s, bool pdl);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.

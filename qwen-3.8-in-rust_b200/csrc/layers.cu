@@ -14,7 +14,10 @@
 //   argmax            first index of the maximum                            (model.rs:505-513)
 //
 // "Bit-exact" holds with the transcendentals of common.cuh (exp/log1p evaluated in double, rounded once).
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "layers.cuh"
@@ -226,7 +229,9 @@ __global__ void __launch_bounds__(128) deltanet_heads_kernel(const DeltaArgs a) 
         if (j == 0 || j == 32) {
             float* vec = j == 0 ? qs : ks;
             float ss = 0.0f;
-            for (int k = 0; k < dk; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+            // dk == DK: unrolled so the shared-memory loads run ahead of the dependent adds
+#pragma unroll
+            for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
             scal[j == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
         }
         if (j == (int)blockDim.x - 1) {
@@ -267,6 +272,120 @@ __global__ void __launch_bounds__(128) deltanet_heads_kernel(const DeltaArgs a) 
         a.heads[(size_t)i * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
         __syncthreads();
     }
+}
+
+// The same computation split over a cluster of dv / 32 single-warp CTAs per V head (thread block clusters,
+// sm_90+): CTA c owns value columns 32c .. 32c+31, so a head's 128 columns run on 4 SMs and each thread's state
+// column S[:, j] stays in registers.  Every CTA recomputes the head's l2norms and gates (the same operations on
+// the same data); the gated RMSNorm's 8-lane sum over all dv outputs reads the other CTAs' outputs through
+// distributed shared memory, one cluster barrier per row (outputs double-buffered by row parity).
+template <int DK>
+__global__ void __launch_bounds__(32) deltanet_cluster_kernel(const DeltaArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int nct = a.dv / 32;
+    const int p = blockIdx.x / nct, cpart = blockIdx.x % nct, lane = threadIdx.x;
+    const int j = cpart * 32 + lane;
+    const int dk = DK, dv = a.dv;
+    const int kh = p % a.n_k;
+    __shared__ float qs[DK], ks[DK], obuf[2][32], red[16];
+    __shared__ float scal[4];
+    griddep_wait();
+    griddep_launch();
+    float S[DK];
+    float* Sg = a.S + (size_t)p * dk * dv;
+#pragma unroll
+    for (int k = 0; k < DK; k++) S[k] = Sg[(size_t)k * dv + j];
+    const int keep = a.keep_prev ? *a.keep_prev : 0;
+    for (int i = 0; i < keep; i++) {  // commit the previous call's accepted rows (spec.rs:395-415 replay order)
+        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
+        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk;
+        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
+    }
+    if (keep > 0) {
+#pragma unroll
+        for (int k = 0; k < DK; k++) Sg[(size_t)k * dv + j] = S[k];
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
+    for (int i = 0; i < a.t; i++) {
+        const float* row = a.conved + (size_t)i * a.conv_dim;
+        for (int k = lane; k < dk; k += 32) {
+            qs[k] = row[kh * dk + k];
+            ks[k] = row[a.kd + kh * dk + k];
+        }
+        __syncwarp();
+        // l2norm(q) on lane 0, l2norm(k) on lane 1 (deltanet.rs:19-27): sums left to right; gates on lane 31
+        if (lane < 2) {
+            const float* vec = lane == 0 ? qs : ks;
+            float ss = 0.0f;
+            // dk == DK: unrolled so the shared-memory loads run ahead of the dependent adds
+#pragma unroll
+            for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+            scal[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+        }
+        if (lane == 31) {
+            const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)i * a.n_v + p], a.dt_bias[p])));
+            scal[2] = exp_f32(g);                                  // decay = exp(g)
+            scal[3] = sigmoid_f32(a.beta[(size_t)i * a.n_v + p]);  // beta = sigmoid(b)
+        }
+        __syncwarp();
+        for (int k = lane; k < dk; k += 32) {
+            qs[k] = __fmul_rn(__fmul_rn(qs[k], scal[0]), scale);
+            ks[k] = __fmul_rn(ks[k], scal[1]);
+        }
+        __syncwarp();
+        const float decay = scal[2], beta = scal[3];
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
+        float kv = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+        const float v = row[2 * a.kd + p * dv + j];
+        const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
+#pragma unroll
+        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
+        float o = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+        if (i < a.max_t) {
+            if (j == 0) a.pend_decay[(size_t)i * a.n_v + p] = decay;
+            if (cpart == 0)
+                for (int k = lane; k < dk; k += 32) a.pend_k[((size_t)i * a.n_v + p) * dk + k] = ks[k];
+            a.pend_delta[((size_t)i * a.n_v + p) * dv + j] = delta;
+        }
+        // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47): 8-lane sum across the cluster
+        float* ob = obuf[i & 1];
+        ob[lane] = o;
+        cluster.sync();
+        if (lane < 8) {
+            // lane l sums o[l], o[l+8], ... (dv <= 256: at most 32 terms), fetched first, then chained in order
+            float vals[32];
+            const int cnt = dv / 8;
+#pragma unroll
+            for (int q = 0; q < 32; q++)
+                if (q < cnt) {
+                    const int idx = lane + 8 * q;
+                    vals[q] = cluster.map_shared_rank(ob, idx / 32)[idx % 32];
+                }
+            float acc = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 32; q++)
+                if (q < cnt) acc = __fadd_rn(acc, __fmul_rn(vals[q], vals[q]));
+            red[lane] = acc;
+        }
+        __syncwarp();
+        if (lane == 0) red[8] = reduce8(red);  // dv % 8 == 0: no tail
+        __syncwarp();
+        const float inv = inv_rms_of(red[8], dv, a.eps);
+        const float z = a.z[(size_t)i * a.n_v * dv + p * dv + j];
+        a.heads[(size_t)i * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
+        __syncwarp();
+    }
+    cluster.sync();  // no CTA leaves while another may still read its outputs
 }
 
 // Per (row i, head): RMSNorm of q (heads 0..nh-1) or k (heads nh..nh+nkv-1) with the 8-lane order, then
@@ -493,8 +612,38 @@ cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, 
     return cudaGetLastError();
 }
 
+template <int DK>
+cudaError_t launch_deltanet_cluster(const DeltaArgs& a, cudaStream_t s) {
+    const int nct = a.dv / 32;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_v * nct);
+    cfg.blockDim = dim3(32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = nct;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, deltanet_cluster_kernel<DK>, a);
+}
+
 cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s) {
     if (a.dv > 256 || a.dv % 32) return cudaErrorInvalidValue;
+    static const bool plain = [] {
+        // one CTA per head unless QDEC_DELTANET_CLUSTER=1 (a cluster of dv/32 single-warp CTAs per head, which
+        // measured slower on B200: the per-column chains do not shorten and one warp per SM hides no latency)
+        const char* e = getenv("QDEC_DELTANET_CLUSTER");
+        return !(e && e[0] == '1');
+    }();
+    if (!plain && a.dv % 8 == 0 && a.dv / 32 <= 8 && (a.dk == 128 || a.dk == 64)) {
+        cudaError_t e = a.dk == 128 ? launch_deltanet_cluster<128>(a, s) : launch_deltanet_cluster<64>(a, s);
+        return e == cudaSuccess ? cudaGetLastError() : e;
+    }
     switch (a.dk) {
     case 128: deltanet_heads_kernel<128><<<a.n_v, a.dv, 0, s>>>(a); break;
     case 64: deltanet_heads_kernel<64><<<a.n_v, a.dv, 0, s>>>(a); break;

@@ -255,7 +255,7 @@ def test_gemv_reference_layout_kernel_bit_exact(q, orc, t):
 
 
 @pytest.mark.parametrize("t", [12, 13, 14])
-@pytest.mark.parametrize("cfg", range(1, 15))
+@pytest.mark.parametrize("cfg", range(1, 22))
 def test_gemv_tile_layout_every_config_bit_exact(q, orc, t, cfg):
     """Weights repacked into the tile layout (8 rows x one super-block per tile block): the oracle's bits for
     1..5 columns in every configuration, a super-block count that is not a multiple of any depth, a tile count
@@ -285,8 +285,9 @@ def test_tile_repack_rejects_ragged_rows(q):
         q.repack_tiles(12, src.data_ptr(), 12, 256, dst.data_ptr())
 
 
+@pytest.mark.parametrize("split", [1, 2])
 @pytest.mark.parametrize("t", [8, 2])
-def test_gemv_q80_tile_layout_bit_exact(q, orc, t):
+def test_gemv_q80_tile_layout_bit_exact(q, orc, t, split):
     """Q8_0 / Q4_0 weights in the tile layout (8 rows x 8 blocks per tile block) against the Q8_0 activation
     image: the oracle's bits for 1..5 columns, from f32 columns and from block_q8_0 columns."""
     rows, cols = 8 * 29, 6144
@@ -299,14 +300,18 @@ def test_gemv_q80_tile_layout_bit_exact(q, orc, t):
     dst = torch.empty_like(src)
     q.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr())
     torch.cuda.synchronize()
-    for n in (1, 2, 3, 4, 5):
-        got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
-        assert bits_equal(got, want[:n]), (t, n)
-    act = to_dev(np.ascontiguousarray(gpu_q8_0(q, x[:4])).reshape(-1))
-    y = torch.empty(4 * rows, dtype=torch.float32, device="cuda")
-    q.gemv(q.TILE[t], dst.data_ptr(), rows, cols, act.data_ptr(), 4, y.data_ptr())
-    torch.cuda.synchronize()
-    assert bits_equal(y.cpu().numpy().reshape(4, rows), want[:4])
+    q.tune_gemv(8, split)
+    try:
+        for n in (1, 2, 3, 4, 5):
+            got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (t, n)
+        act = to_dev(np.ascontiguousarray(gpu_q8_0(q, x[:4])).reshape(-1))
+        y = torch.empty(4 * rows, dtype=torch.float32, device="cuda")
+        q.gemv(q.TILE[t], dst.data_ptr(), rows, cols, act.data_ptr(), 4, y.data_ptr())
+        torch.cuda.synchronize()
+        assert bits_equal(y.cpu().numpy().reshape(4, rows), want[:4])
+    finally:
+        q.tune_gemv(8, 0)
 
 
 @pytest.mark.parametrize("t,base", [(112, 12), (116, 14), (108, 8), (102, 2)])
