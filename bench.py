@@ -127,6 +127,10 @@ def dist_setup(backend):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if backend == "nccl":
+        import torch
+
+        torch.cuda.set_device(local)  # before the process group, so NCCL binds this rank's GPU
     if world > 1:
         import datetime
 

@@ -471,8 +471,17 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     // h = x + mixer(x); then the MLP on post_attention_norm(h) (mlp.rs:53-64)
     const bool k8 = needs_q8k({L.ffn_gate.type, L.ffn_up.type}), k0 = needs_q80({L.ffn_gate.type, L.ffn_up.type});
     resid_norm(mix_out_, L.post_norm, t, normed_, k8, k0);
-    gemv(L.ffn_gate, normed_, t, g_);
-    gemv(L.ffn_up, normed_, t, u_);
+    if (L.ffn_gate.type == L.ffn_up.type && L.ffn_gate.cols == L.ffn_up.cols &&
+        (L.ffn_gate.type == T_Q4_K_TILE || L.ffn_gate.type == T_Q5_K_TILE || L.ffn_gate.type == T_Q6_K_TILE)) {
+        // gate and up read the same normed rows: one launch over both (mlp.rs:55, matvec2)
+        count_launch((t + 3) / 4);
+        ck(launch_gemv_img_pair(L.ffn_gate.type, L.ffn_gate.p, L.ffn_gate.rows, g_, L.ffn_up.p, L.ffn_up.rows, u_, L.ffn_gate.cols,
+                                q8k_, t, stream, true),
+           "gate/up");
+    } else {
+        gemv(L.ffn_gate, normed_, t, g_);
+        gemv(L.ffn_up, normed_, t, u_);
+    }
     const int dt = L.ffn_down.type;
     count_launch(); ck(launch_swiglu_quant(g_, u_, (int)c.intermediate_size, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
                            is_q80(dt) ? q80_ : nullptr, stream), "swiglu");

@@ -43,6 +43,10 @@ cudaError_t launch_q8k_raw_to_image(const uint8_t* raw, long long nblocks, uint8
 bool v6_gemv_supported(int type);
 cudaError_t launch_gemv_img(int type, const uint8_t* w, int rows, int cols, const void* img, int ncols, float* y,
                             cudaStream_t s, bool pdl);
+// Two K-quant tile matrices of one type reading the same image columns (e.g. ffn_gate and ffn_up) in one
+// launch: y_a = W_a x, y_b = W_b x; rows % 8 == 0.
+cudaError_t launch_gemv_img_pair(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
+                                 int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
 // Tuning: the K-quant GEMV implementation (0 = automatic, 2 = the raw-Q8_K register path, 6 = the image kernel)
 // and the image kernel's configuration (0 = automatic, 1..8).
 void set_gemv_impl(int impl);

@@ -274,6 +274,125 @@ __global__ void __launch_bounds__(128) deltanet_heads_kernel(const DeltaArgs a) 
     }
 }
 
+// The same computation with two threads per value column (blockDim.x == 2 * dv): lanes l and l + 16 of a warp
+// share column j, each holding half of S[:, j] (k < DK/2 and k >= DK/2) in registers, which keeps the state in
+// registers without spilling.  The two k-ordered sums (kv = sum_k S[k] k[k], o = sum_k S[k] q[k]) stay single
+// left-to-right chains: the low half runs its 64 terms, hands the partial sum to the high half by one shuffle,
+// and the high half continues from it.
+template <int DK>
+__global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
+    constexpr int HK = DK / 2;
+    constexpr int CH = 8;  // rows whose q/k norms and gates are computed together (they do not depend on S)
+    const int p = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int h = lane >> 4, j = warp * 16 + (lane & 15);
+    const int k0 = h * HK;
+    const int dk = DK, dv = a.dv;
+    const int kh = p % a.n_k;
+    __shared__ __align__(16) float qs_all[CH][DK], ks_all[CH][DK];
+    __shared__ float gate[CH][2], nrm[CH][2];  // (decay, beta), (1/|q|, 1/|k|)
+    __shared__ float red[16], outs[256];
+    griddep_wait();
+    griddep_launch();
+    float S[HK];
+    float* Sg = a.S + (size_t)p * dk * dv;
+#pragma unroll
+    for (int k = 0; k < HK; k++) S[k] = Sg[(size_t)(k0 + k) * dv + j];
+    const int keep = a.keep_prev ? *a.keep_prev : 0;
+    for (int i = 0; i < keep; i++) {  // commit the previous call's accepted rows (spec.rs:395-415 replay order)
+        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
+        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk + k0;
+        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
+#pragma unroll
+        for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
+#pragma unroll
+        for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
+    }
+    if (keep > 0) {
+#pragma unroll
+        for (int k = 0; k < HK; k++) Sg[(size_t)(k0 + k) * dv + j] = S[k];
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
+    for (int c0 = 0; c0 < a.t; c0 += CH) {
+        const int nr = min(CH, a.t - c0);
+        for (int e = t; e < nr * DK; e += blockDim.x) {
+            const int i = e / DK, k = e % DK;
+            const float* row = a.conved + (size_t)(c0 + i) * a.conv_dim;
+            qs_all[i][k] = row[kh * dk + k];
+            ks_all[i][k] = row[a.kd + kh * dk + k];
+        }
+        __syncthreads();
+        // l2norm (deltanet.rs:19-27, sums left to right): warp w normalises q of rows w, w + warps, .. on lane 0
+        // and k on lane 16; gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) on lane 8
+        for (int i = warp; i < nr && (lane & 7) == 0; i += blockDim.x / 32) {
+            if (lane == 8) {
+                const int r = c0 + i;
+                const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)r * a.n_v + p], a.dt_bias[p])));
+                gate[i][0] = exp_f32(g);
+                gate[i][1] = sigmoid_f32(a.beta[(size_t)r * a.n_v + p]);
+            } else if (lane != 24) {
+                const float* vec = lane == 0 ? qs_all[i] : ks_all[i];
+                float ss = 0.0f;
+#pragma unroll
+                for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+                nrm[i][lane == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+            }
+        }
+        __syncthreads();
+        for (int e = t; e < nr * DK; e += blockDim.x) {
+            const int i = e / DK, k = e % DK;
+            qs_all[i][k] = __fmul_rn(__fmul_rn(qs_all[i][k], nrm[i][0]), scale);
+            ks_all[i][k] = __fmul_rn(ks_all[i][k], nrm[i][1]);
+        }
+        __syncthreads();
+        for (int i = 0; i < nr; i++) {
+            const int r = c0 + i;
+            const float* qs = qs_all[i];
+            const float* ks = ks_all[i];
+            const float v = a.conved[(size_t)r * a.conv_dim + 2 * a.kd + p * dv + j];
+            const float z = a.z[(size_t)r * a.n_v * dv + p * dv + j];
+            const float decay = gate[i][0], beta = gate[i][1];
+#pragma unroll
+            for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
+            // kv: the low half's terms from 0, then the high half's from the low half's sum
+            float kv = 0.0f;
+            if (h == 0) {
+#pragma unroll
+                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+            }
+            kv = __shfl_sync(0xffffffffu, kv, lane & 15);
+            if (h == 1) {
+#pragma unroll
+                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[HK + k]));
+            }
+            kv = __shfl_sync(0xffffffffu, kv, 16 + (lane & 15));
+            const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
+#pragma unroll
+            for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k0 + k], delta));
+            float o = 0.0f;
+            if (h == 0) {
+#pragma unroll
+                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+            }
+            o = __shfl_sync(0xffffffffu, o, lane & 15);
+            if (h == 1) {
+#pragma unroll
+                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[HK + k]));
+            }
+            if (r < a.max_t) {
+                if (t == 0) a.pend_decay[(size_t)r * a.n_v + p] = decay;
+                for (int k = t; k < dk; k += blockDim.x) a.pend_k[((size_t)r * a.n_v + p) * dk + k] = ks[k];
+                if (h == 1) a.pend_delta[((size_t)r * a.n_v + p) * dv + j] = delta;
+            }
+            // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47); the helper ends with a barrier, after
+            // which outs and this chunk's rows may be overwritten
+            if (h == 1) outs[j] = o;
+            __syncthreads();
+            const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
+            if (h == 1) a.heads[(size_t)r * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
+        }
+    }
+}
+
 // The same computation split over a cluster of dv / 32 single-warp CTAs per V head (thread block clusters,
 // sm_90+): CTA c owns value columns 32c .. 32c+31, so a head's 128 columns run on 4 SMs and each thread's state
 // column S[:, j] stays in registers.  Every CTA recomputes the head's l2norms and gates (the same operations on
@@ -642,6 +761,11 @@ cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s) {
     }();
     if (!plain && a.dv % 8 == 0 && a.dv / 32 <= 8 && (a.dk == 128 || a.dk == 64)) {
         cudaError_t e = a.dk == 128 ? launch_deltanet_cluster<128>(a, s) : launch_deltanet_cluster<64>(a, s);
+        return e == cudaSuccess ? cudaGetLastError() : e;
+    }
+    if (a.dv % 16 == 0 && a.dv <= 128 && (a.dk == 128 || a.dk == 64)) {
+        cudaError_t e = a.dk == 128 ? launch_pdl(deltanet_pair_kernel<128>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a)
+                                    : launch_pdl(deltanet_pair_kernel<64>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a);
         return e == cudaSuccess ? cudaGetLastError() : e;
     }
     switch (a.dk) {
