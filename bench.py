@@ -140,6 +140,18 @@ def dist_setup(backend):
     return world, rank, local
 
 
+def max_over_ranks(values, device):
+    """The element-wise maximum over the ranks of a list of floats (the slowest rank's times); one rank: as is."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def oracle_spec_sample(path, k, prompt_len, rounds):
     """The reference's greedy --spec k loop restated on the CPU (oracle/model.c, OpenMP over all host threads) on
     the 27B checkpoint: a short prompt, then `rounds` rounds; returns (tok/s over the rounds, stats, cores)."""
@@ -473,6 +485,52 @@ def dominant_gemv_timing(dev, launches=200):
     return alg, ms
 
 
+def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
+    """--spec k rounds of ONE sequence tensor-parallel over the `world` ranks (every rank runs the same rounds on its
+    shard; the sharded activations are exchanged GPU to GPU): device time of the timed rounds on each rank's
+    stream, max over ranks, and the host wall time of the same calls (the C ABI per round: x_p in, ids out)."""
+    import torch
+    import torch.distributed as dist
+
+    import qdec
+
+    model = qdec.Model(path, device=local, max_pos=max_pos, tp=(rank, world))
+    st = model.new_state(spec_k=k, max_rows=32)
+    st.tp_connect_group()
+    stream = torch.cuda.ExternalStream(st.stream)
+    x = st.spec_prefill(prompt)
+    for _ in range(args.warmup):
+        x = st.spec_round(x)[-1]
+    torch.cuda.synchronize()
+    dist.barrier()
+    l0 = st.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    emitted = 0
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        em = st.spec_round(x)
+        emitted += len(em)
+        x = em[-1]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms, wall_ms = max_over_ranks([e0.elapsed_time(e1), wall * 1e3], torch.device("cuda", local))
+    launches = st.launches - l0
+    info = model.info
+    dist.barrier()  # every rank's last exchange is done before any rank frees its exchange block
+    st.free()
+    model.close()
+    s_round = ms / 1e3 / args.steps
+    return {"value": round(emitted / (ms / 1e3), 3), "unit": "tok/s", "ms_per_step": round(ms / args.steps, 4),
+            "scaling": "strong", "parallelism": f"tp{world}", "gpu_launches_per_rank": launches,
+            "e2e": {"value": round(emitted / (wall_ms / 1e3), 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * world,
+                    "d2h_bytes_per_step": 4 * (k + 2) * world},
+            "per_rank_verify_bytes": info.decode_bytes,
+            "round_frac_per_rank": None,
+            "_s_round": s_round, "_bytes": info.decode_bytes + k * (info.mtp_bytes + info.lm_head_bytes)}
+
+
 def run_spec_qdec(args, world, rank, local):
     import torch
 
@@ -489,6 +547,11 @@ def run_spec_qdec(args, world, rank, local):
     path = checkpoint_path(preset, SPEC_SEED)
     k = SPEC_K
     max_pos = PROMPT_LEN + (args.warmup + args.steps) * (k + 1) * 2 + 64
+    tp_res = None
+    if world > 1 and not args.no_tp:
+        # one sequence over all the GPUs first (its prompt is the same on every rank), then the replicas
+        vocab = qdec.tp_plan(path, 0, 1)["v_rows"]
+        tp_res = tp_spec_timing(path, args, world, rank, local, k, spec_prompt(vocab, SPEC_SEED + 1), max_pos)
     model = qdec.Model(path, device=local, max_pos=max_pos)
     info = model.info
     prompt = spec_prompt(info.vocab, SPEC_SEED + 1 + rank)
@@ -549,9 +612,7 @@ def run_spec_qdec(args, world, rank, local):
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([ms, wall * 1e3, forced_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, wall_ms, forced_ms = t.tolist()
+        ms, wall_ms, forced_ms = max_over_ranks([ms, wall * 1e3, forced_ms], torch.device("cuda", local))
         wall = wall_ms / 1e3
         tt = torch.tensor([emitted, forced_tokens], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt)
@@ -597,6 +658,10 @@ def run_spec_qdec(args, world, rank, local):
                                "north_star_frac": round(17.8e9 / s_round / 1e9 / peak, 4)}},
         "clocks": clk.summary(),
     }
+    if tp_res is not None:
+        s_r, b = tp_res.pop("_s_round"), tp_res.pop("_bytes")
+        tp_res["round_frac_per_rank"] = round(b / s_r / 1e9 / peak, 4)
+        line["tp"] = tp_res
     if world == 1 and not args.no_cpu_baseline:
         tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 1)
         line["cpu_baseline"] = {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port",
@@ -613,6 +678,7 @@ def main():
     ap.add_argument("--workload", choices=["spec", "gemv"], default="spec")
     ap.add_argument("--preset", default="27b", help="synthetic checkpoint of the spec workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="with --gpus > 1: replicas only (no tensor-parallel run)")
     ap.add_argument("--profile-gemv", action="store_true",
                     help="run the dominant GEMV (Q4_K 17408x5120 N=4, tile layout) 4 times and exit: the ncu capture target")
     args = ap.parse_args()

@@ -153,6 +153,27 @@ typedef struct qdec_model_info {
  * reference's GgufError / ConfigError message. */
 int qdec_open(const char *gguf_path, const qdec_opts *opts, qdec_model **out);
 int qdec_close(qdec_model *m);
+
+/* Tensor parallelism over the GPUs of one node, one process per GPU (rank tp_rank of tp_world, 1..8).  Each
+ * rank holds the output-row slices of every matrix (the reference's matvec row partition,
+ * crates/core/src/kernels/matvec.rs:446-467, spread over GPUs instead of cores): the DeltaNet K heads and the V
+ * heads tied to them, the attention q and kv heads, a 256-row range of the FFN, a range of the hidden-size
+ * outputs and of the vocabulary.  Every row is computed whole, so the ids are those of one GPU; the sharded
+ * activations are all-gathered between the ranks over peer memory.  A TP state must be connected
+ * (qdec_tp_export on every rank, the handles gathered in rank order, qdec_tp_connect on every rank) before its
+ * first prefill; all ranks then make the same calls with the same ids, and free their states only after every
+ * rank's last call has returned.  QDEC_EFORMAT when the model's dimensions do not split over tp_world.
+ * No counterpart in the reference (CPU-only, one process). */
+int qdec_open_tp(const char *gguf_path, const qdec_opts *opts, int tp_rank, int tp_world, qdec_model **out);
+/* The shard of rank tp_rank from the GGUF header alone (no device): out = {rank, world, kh_lo, nk, nv, qh_lo,
+ * nq, kv_lo, nkv, ff_lo, ff_rows, h_lo, h_rows, v_lo, v_rows, 0} (first row / head and count of each range). */
+int qdec_tp_plan(const char *gguf_path, int tp_rank, int tp_world, int32_t out[16]);
+/* The same from the dimensions: dims = {hidden, ffn, vocab, n_head, n_head_kv, dn_n_k_heads, dn_n_v_heads,
+ * has_deltanet_layers}. */
+int qdec_tp_plan_dims(const uint32_t dims[8], int tp_rank, int tp_world, int32_t out[16]);
+#define QDEC_TP_HANDLE_BYTES 80
+int qdec_tp_export(const qdec_state *s, void *handle_out);
+int qdec_tp_connect(qdec_state *s, const void *handles);
 int qdec_model_get_info(const qdec_model *m, qdec_model_info *info);
 /* Nonzero when `id` is a stop id: the GGUF EOS ids plus the architecture's (crates/core/src/arch.rs:79-90).
  * Replaces Model::is_stop (crates/core/src/model.rs:492). */

@@ -64,6 +64,71 @@ int qdec_open(const char* path, const qdec_opts* opts, qdec_model** out) {
     });
 }
 
+int qdec_open_tp(const char* path, const qdec_opts* opts, int tp_rank, int tp_world, qdec_model** out) {
+    if (!path || !out) return qdec::fail(QDEC_EINVAL, "qdec_open_tp: null argument");
+    *out = nullptr;
+    return guard("qdec_open_tp", [&] {
+        qdec::LoadOptions o;
+        if (opts) {
+            o.device = opts->device;
+            if (opts->max_pos > 0) o.max_pos = opts->max_pos;
+        }
+        o.tp_rank = tp_rank;
+        o.tp_world = tp_world;
+        auto m = qdec::Model::load(path, o);
+        *out = new qdec_model{std::move(m)};
+        return QDEC_OK;
+    });
+}
+
+int qdec_tp_plan(const char* path, int tp_rank, int tp_world, int32_t out[16]) {
+    if (!path || !out) return qdec::fail(QDEC_EINVAL, "qdec_tp_plan: null argument");
+    return guard("qdec_tp_plan", [&] {
+        qdec::Gguf g(path);
+        const qdec::TpPlan p = qdec::make_tp_plan(qdec::ModelConfig::from_gguf(g), tp_rank, tp_world);
+        const int32_t v[16] = {p.rank, p.world, p.kh_lo, p.nk, p.nv, p.qh_lo, p.nq, p.kv_lo, p.nkv, p.ff_lo, p.ff_rows,
+                               p.h_lo, p.h_rows, p.v_lo, p.v_rows, 0};
+        std::memcpy(out, v, sizeof v);
+        return QDEC_OK;
+    });
+}
+
+int qdec_tp_plan_dims(const uint32_t dims[8], int tp_rank, int tp_world, int32_t out[16]) {
+    if (!dims || !out) return qdec::fail(QDEC_EINVAL, "qdec_tp_plan_dims: null argument");
+    return guard("qdec_tp_plan_dims", [&] {
+        qdec::ModelConfig c;
+        c.hidden_size = dims[0];
+        c.intermediate_size = dims[1];
+        c.vocab_size = dims[2];
+        c.n_head = dims[3];
+        c.n_head_kv = dims[4];
+        c.dn_n_k_heads = dims[5];
+        c.dn_n_v_heads = dims[6];
+        if (dims[7]) c.deltanet_layers.push_back(0);
+        const qdec::TpPlan p = qdec::make_tp_plan(c, tp_rank, tp_world);
+        const int32_t v[16] = {p.rank, p.world, p.kh_lo, p.nk, p.nv, p.qh_lo, p.nq, p.kv_lo, p.nkv, p.ff_lo, p.ff_rows,
+                               p.h_lo, p.h_rows, p.v_lo, p.v_rows, 0};
+        std::memcpy(out, v, sizeof v);
+        return QDEC_OK;
+    });
+}
+
+int qdec_tp_export(const qdec_state* s, void* handle_out) {
+    if (!s || !handle_out) return qdec::fail(QDEC_EINVAL, "qdec_tp_export: null argument");
+    return guard("qdec_tp_export", [&] {
+        s->s->tp_export(handle_out);
+        return QDEC_OK;
+    });
+}
+
+int qdec_tp_connect(qdec_state* s, const void* handles) {
+    if (!s || !handles) return qdec::fail(QDEC_EINVAL, "qdec_tp_connect: null argument");
+    return guard("qdec_tp_connect", [&] {
+        s->s->tp_connect(handles);
+        return QDEC_OK;
+    });
+}
+
 int qdec_close(qdec_model* m) {
     delete m;
     return QDEC_OK;

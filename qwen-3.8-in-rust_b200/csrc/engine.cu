@@ -28,6 +28,7 @@
 #include "gguf.h"
 #include "kernels.cuh"
 #include "layers.cuh"
+#include "tp.cuh"
 
 namespace qdec {
 
@@ -78,7 +79,50 @@ __global__ void select_row_kernel(const float* __restrict__ src, const int* __re
 
 // ------------------------------------------------------------------------------------------------ Model
 
+TpPlan make_tp_plan(const ModelConfig& c, int rank, int world) {
+    if (world < 1 || world > 8 || rank < 0 || rank >= world)
+        throw ConfigError("tensor parallelism: rank " + std::to_string(rank) + " of " + std::to_string(world) + " (1..8 ranks)");
+    auto need = [&](bool ok, const char* what) {
+        if (!ok) throw ConfigError("tensor parallelism over " + std::to_string(world) + " GPUs: " + what);
+    };
+    TpPlan p;
+    p.rank = rank;
+    p.world = world;
+    if (!c.deltanet_layers.empty()) {
+        need(c.dn_n_k_heads % world == 0, "the DeltaNet K heads do not divide among the ranks");
+        need(c.dn_n_v_heads % c.dn_n_k_heads == 0, "the DeltaNet V heads are not a multiple of the K heads");
+        p.nk = (int)c.dn_n_k_heads / world;
+        p.kh_lo = rank * p.nk;
+        p.nv = p.nk * (int)(c.dn_n_v_heads / c.dn_n_k_heads);
+    }
+    need(c.n_head % world == 0 && c.n_head_kv > 0 && c.n_head % c.n_head_kv == 0, "the attention heads do not divide among the ranks");
+    p.nq = (int)c.n_head / world;
+    p.qh_lo = rank * p.nq;
+    const int group = (int)(c.n_head / c.n_head_kv);
+    if (c.n_head_kv % world == 0) {
+        p.nkv = (int)c.n_head_kv / world;
+        p.kv_lo = rank * p.nkv;
+    } else {
+        need(group % p.nq == 0, "a rank's query heads would span two kv heads");
+        p.nkv = 1;
+        p.kv_lo = p.qh_lo / group;
+    }
+    need(c.intermediate_size % 256 == 0 && (int)c.intermediate_size / 256 >= world, "the FFN width does not split on 256-row blocks");
+    const int nb = (int)c.intermediate_size / 256;
+    const int b0 = rank * nb / world, b1 = (rank + 1) * nb / world;
+    p.ff_lo = b0 * 256;
+    p.ff_rows = (b1 - b0) * 256;
+    need(c.hidden_size % (8u * world) == 0, "the hidden size does not split into 8-row tiles");
+    p.h_rows = (int)c.hidden_size / world;
+    p.h_lo = rank * p.h_rows;
+    need(c.vocab_size % (8u * world) == 0, "the vocabulary does not split into 8-row tiles");
+    p.v_rows = (int)c.vocab_size / world;
+    p.v_lo = rank * p.v_rows;
+    return p;
+}
+
 Model::~Model() {
+    for (void* p : shard_allocs_) cudaFree(p);
     if (blob_) cudaFree(blob_);
     if (rope_cos) cudaFree(rope_cos);
     if (rope_sin) cudaFree(rope_sin);
@@ -95,8 +139,10 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     m->cfg = ModelConfig::from_gguf(g);
     m->device = opt.device;
     m->max_pos = opt.max_pos;
+    m->tp = make_tp_plan(m->cfg, opt.tp_rank, opt.tp_world);
     ck(cudaSetDevice(opt.device), "cudaSetDevice");
     const ModelConfig& c = m->cfg;
+    const TpPlan& P = m->tp;
 
     // the data section, unchanged, in one allocation
     const uint64_t data_bytes = g.file_size() - g.data_offset();
@@ -145,25 +191,27 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         if ((is_kquant(t.type) || t.type == T_Q8_0 || t.type == T_Q4_0) && t.name != "token_embd.weight")
             repack_cap = std::max(repack_cap, t.byte_size);
     if (repack_cap) ck(cudaMalloc(&repack_tmp, repack_cap), "repack buffer");
-    auto repack = [&](const TensorInfo& t, int rows, int cols) -> int {
-        uint8_t* p = m->blob_ + t.rel_offset;
-        ck(cudaMemcpy(repack_tmp, p, t.byte_size, cudaMemcpyDeviceToDevice), "repack copy");
-        int type = t.type;
+    auto repack_at = [&](uint8_t* p, int ttype, uint64_t bytes, int rows, int cols, const std::string& name) -> int {
+        ck(cudaMemcpy(repack_tmp, p, bytes, cudaMemcpyDeviceToDevice), "repack copy");
+        int type = ttype;
         const bool aligned = rows % 8 == 0 && ((uintptr_t)p & 15) == 0;
-        if ((t.type == T_Q8_0 || t.type == T_Q4_0) && aligned && cols % 256 == 0) {
-            ck(launch_repack_q80_tiles(t.type, repack_tmp, rows, cols, p, 0), "repack");
-            type = t.type == T_Q8_0 ? T_Q8_0_TILE : T_Q4_0_TILE;
-        } else if (t.type == T_Q8_0 || t.type == T_Q4_0) {
-            throw ConfigError("tensor " + t.name + ": Q8_0/Q4_0 matrices need rows % 8 == 0 and cols % 256 == 0 here");
+        if ((ttype == T_Q8_0 || ttype == T_Q4_0) && aligned && cols % 256 == 0) {
+            ck(launch_repack_q80_tiles(ttype, repack_tmp, rows, cols, p, 0), "repack");
+            type = ttype == T_Q8_0 ? T_Q8_0_TILE : T_Q4_0_TILE;
+        } else if (ttype == T_Q8_0 || ttype == T_Q4_0) {
+            throw ConfigError("tensor " + name + ": Q8_0/Q4_0 matrices need rows % 8 == 0 and cols % 256 == 0 here");
         } else if (aligned) {
-            ck(launch_repack_tiles(t.type, repack_tmp, rows, cols, p, 0), "repack");
-            type = t.type == T_Q4_K ? T_Q4_K_TILE : t.type == T_Q5_K ? T_Q5_K_TILE : T_Q6_K_TILE;
-        } else if (t.type == T_Q6_K) {
-            ck(launch_repack_q6k(repack_tmp, t.byte_size / 210, p, 0), "repack");
+            ck(launch_repack_tiles(ttype, repack_tmp, rows, cols, p, 0), "repack");
+            type = ttype == T_Q4_K ? T_Q4_K_TILE : ttype == T_Q5_K ? T_Q5_K_TILE : T_Q6_K_TILE;
+        } else if (ttype == T_Q6_K) {
+            ck(launch_repack_q6k(repack_tmp, bytes / 210, p, 0), "repack");
             type = T_Q6_K_SPLIT;
         }
         ck(cudaDeviceSynchronize(), "repack");
         return type;
+    };
+    auto repack = [&](const TensorInfo& t, int rows, int cols) -> int {
+        return repack_at(m->blob_ + t.rel_offset, t.type, t.byte_size, rows, cols, t.name);
     };
     auto mat = [&](const std::string& name, uint64_t rows, uint64_t cols) {
         const TensorInfo& t = g.tensor(name);
@@ -188,9 +236,53 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         if (t.type != T_F32) throw ConfigError("tensor " + name + ": 1-D weights must be F32 here");
         return reinterpret_cast<const float*>(ptr(t));
     };
+    // tensor parallelism: a rank keeps the rows `segs` ({first row, count} in order) of a sharded tensor, copied
+    // out of the uploaded data section into an allocation of its own (then repacked like a whole matrix)
+    using Segs = std::vector<std::pair<uint64_t, uint64_t>>;
+    auto shard_copy = [&](const TensorInfo& t, uint64_t row_bytes, const Segs& segs, uint64_t& nrows) -> uint8_t* {
+        nrows = 0;
+        for (const auto& sg : segs) nrows += sg.second;
+        uint8_t* d = nullptr;
+        ck(cudaMalloc(&d, nrows * row_bytes + 256), "shard allocation");
+        m->shard_allocs_.push_back(d);
+        uint64_t o = 0;
+        for (const auto& sg : segs) {
+            ck(cudaMemcpy(d + o, ptr(t) + sg.first * row_bytes, sg.second * row_bytes, cudaMemcpyDeviceToDevice), "shard copy");
+            o += sg.second * row_bytes;
+        }
+        return d;
+    };
+    auto mat_rows = [&](const std::string& name, uint64_t rows, uint64_t cols, const Segs& segs) {
+        if (P.world == 1) return mat(name, rows, cols);
+        const TensorInfo& t = g.tensor(name);
+        const auto sh = t.shape_numpy();
+        if (sh.size() != 2 || sh[0] != rows || sh[1] != cols)
+            throw ConfigError("tensor " + name + ": expected shape [" + std::to_string(rows) + ", " + std::to_string(cols) + "]");
+        if (!(t.type == T_F32 || t.type == T_Q4_0 || t.type == T_Q8_0 || is_kquant(t.type)))
+            throw ConfigError("tensor " + name + ": no kernel for ggml type " + std::to_string(t.type));
+        const uint64_t rb = t.byte_size / rows;
+        uint64_t n = 0;
+        uint8_t* d = shard_copy(t, rb, segs, n);
+        DevMat dm;
+        dm.type = t.type;
+        dm.rows = (int)n;
+        dm.cols = (int)cols;
+        dm.p = d;
+        dm.bytes = n * rb;
+        if (is_kquant(t.type) || t.type == T_Q8_0 || t.type == T_Q4_0) dm.type = repack_at(d, t.type, dm.bytes, (int)n, (int)cols, name);
+        return dm;
+    };
+    auto vec_rows = [&](const std::string& name, uint64_t len, uint64_t per, const Segs& segs) -> const float* {
+        const float* full = vec(name, len);
+        if (P.world == 1) return full;
+        uint64_t n = 0;
+        return reinterpret_cast<const float*>(shard_copy(g.tensor(name), per * 4, segs, n));
+    };
     const uint64_t H = c.hidden_size;
+    const Segs hseg{{(uint64_t)P.h_lo, (uint64_t)P.h_rows}};
     m->embed = mat("token_embd.weight", c.vocab_size, H);
-    m->lm_head = mat(c.tie_word_embeddings ? "token_embd.weight" : "output.weight", c.vocab_size, H);
+    m->lm_head = mat_rows(c.tie_word_embeddings ? "token_embd.weight" : "output.weight", c.vocab_size, H,
+                          Segs{{(uint64_t)P.v_lo, (uint64_t)P.v_rows}});
     m->output_norm = vec("output_norm.weight", H);
     auto load_layer = [&](uint32_t i, bool attention) {
         LayerW L;
@@ -201,26 +293,35 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         L.post_norm = vec(p + "post_attention_norm.weight", H);
         if (attention) {
             const uint64_t hd = c.head_dim_k;
-            L.q = mat(p + "attn_q.weight", 2ull * c.n_head * hd, H);
-            L.k = mat(p + "attn_k.weight", (uint64_t)c.n_head_kv * hd, H);
-            L.v = mat(p + "attn_v.weight", (uint64_t)c.n_head_kv * hd, H);
-            L.o = mat(p + "attn_output.weight", H, (uint64_t)c.n_head * hd);
+            L.q = mat_rows(p + "attn_q.weight", 2ull * c.n_head * hd, H, Segs{{2ull * P.qh_lo * hd, 2ull * P.nq * hd}});
+            L.k = mat_rows(p + "attn_k.weight", (uint64_t)c.n_head_kv * hd, H, Segs{{(uint64_t)P.kv_lo * hd, (uint64_t)P.nkv * hd}});
+            L.v = mat_rows(p + "attn_v.weight", (uint64_t)c.n_head_kv * hd, H, Segs{{(uint64_t)P.kv_lo * hd, (uint64_t)P.nkv * hd}});
+            L.o = mat_rows(p + "attn_output.weight", H, (uint64_t)c.n_head * hd, hseg);
             L.q_norm = vec(p + "attn_q_norm.weight", hd);
             L.k_norm = vec(p + "attn_k_norm.weight", hd);
         } else {
-            L.qkv = mat(p + "attn_qkv.weight", c.dn_qkv_dim, H);
-            L.gate_z = mat(p + "attn_gate.weight", c.dn_v_dim, H);
-            L.alpha = mat(p + "ssm_alpha.weight", c.dn_n_v_heads, H);
-            L.beta = mat(p + "ssm_beta.weight", c.dn_n_v_heads, H);
-            L.ssm_a = vec(p + "ssm_a", c.dn_n_v_heads);
-            L.dt_bias = vec(p + "ssm_dt.bias", c.dn_n_v_heads);
-            L.conv_w = vec(p + "ssm_conv1d.weight", (uint64_t)c.dn_qkv_dim * c.dn_conv_kernel);
+            // this rank's K heads (q and k rows) and the V heads tied to them (v rows, gate rows, per-head scalars)
+            const uint64_t dk = c.dn_head_dim_k, dv = c.dn_head_dim_v, nkg = c.dn_n_k_heads, G = c.dn_n_v_heads / nkg;
+            Segs qkv_rows{{P.kh_lo * dk, P.nk * dk}, {nkg * dk + P.kh_lo * dk, P.nk * dk}}, v_rows, head_rows;
+            for (uint64_t gi = 0; gi < G; gi++) {
+                qkv_rows.push_back({2 * nkg * dk + (gi * nkg + P.kh_lo) * dv, P.nk * dv});
+                v_rows.push_back({(gi * nkg + P.kh_lo) * dv, P.nk * dv});
+                head_rows.push_back({gi * nkg + P.kh_lo, (uint64_t)P.nk});
+            }
+            L.qkv = mat_rows(p + "attn_qkv.weight", c.dn_qkv_dim, H, qkv_rows);
+            L.gate_z = mat_rows(p + "attn_gate.weight", c.dn_v_dim, H, v_rows);
+            L.alpha = mat_rows(p + "ssm_alpha.weight", c.dn_n_v_heads, H, head_rows);
+            L.beta = mat_rows(p + "ssm_beta.weight", c.dn_n_v_heads, H, head_rows);
+            L.ssm_a = vec_rows(p + "ssm_a", c.dn_n_v_heads, 1, head_rows);
+            L.dt_bias = vec_rows(p + "ssm_dt.bias", c.dn_n_v_heads, 1, head_rows);
+            L.conv_w = vec_rows(p + "ssm_conv1d.weight", (uint64_t)c.dn_qkv_dim * c.dn_conv_kernel, c.dn_conv_kernel, qkv_rows);
             L.ssm_norm = vec(p + "ssm_norm.weight", c.dn_head_dim_v);
-            L.ssm_out = mat(p + "ssm_out.weight", H, c.dn_v_dim);
+            L.ssm_out = mat_rows(p + "ssm_out.weight", H, c.dn_v_dim, hseg);
         }
-        L.ffn_gate = mat(p + "ffn_gate.weight", c.intermediate_size, H);
-        L.ffn_up = mat(p + "ffn_up.weight", c.intermediate_size, H);
-        L.ffn_down = mat(p + "ffn_down.weight", H, c.intermediate_size);
+        const Segs ffseg{{(uint64_t)P.ff_lo, (uint64_t)P.ff_rows}};
+        L.ffn_gate = mat_rows(p + "ffn_gate.weight", c.intermediate_size, H, ffseg);
+        L.ffn_up = mat_rows(p + "ffn_up.weight", c.intermediate_size, H, ffseg);
+        L.ffn_down = mat_rows(p + "ffn_down.weight", H, c.intermediate_size, hseg);
         return L;
     };
     for (uint32_t i = 0; i < c.n_layer; i++) m->layers.push_back(load_layer(i, c.is_attention(i)));
@@ -228,7 +329,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         const uint32_t mi = c.mtp_layers[0];
         const std::string p = "blk." + std::to_string(mi) + ".nextn.";
         m->mtp.block = load_layer(mi, true);
-        m->mtp.eh_proj = mat(p + "eh_proj.weight", H, 2 * H);
+        m->mtp.eh_proj = mat_rows(p + "eh_proj.weight", H, 2 * H, hseg);
         m->mtp.enorm = vec(p + "enorm.weight", H);
         m->mtp.hnorm = vec(p + "hnorm.weight", H);
         m->mtp.head_norm = vec(p + "shared_head_norm.weight", H);
@@ -265,6 +366,22 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     for (uint32_t mi : c.mtp_layers) {
         uint64_t s0, e0;
         if (g.layer_span(mi, s0, e0)) m->mtp_bytes += e0 - s0;
+    }
+    if (P.world > 1) {  // the bytes this rank streams: its matrix slices (the small replicated vectors left out)
+        auto mats = [](const LayerW& L) {
+            uint64_t b = 0;
+            for (const DevMat* d : {&L.qkv, &L.gate_z, &L.alpha, &L.beta, &L.ssm_out, &L.q, &L.k, &L.v, &L.o, &L.ffn_gate, &L.ffn_up,
+                                    &L.ffn_down})
+                b += d->bytes;
+            return b;
+        };
+        uint64_t lb = 0;
+        for (const LayerW& L : m->layers) lb += mats(L);
+        m->decode_bytes = lb + m->lm_head.bytes + 4ull * H + m->embed.bytes / c.vocab_size;
+        if (m->has_mtp) m->mtp_bytes = mats(m->mtp.block) + m->mtp.eh_proj.bytes;
+        for (const DevMat* d : {&m->lm_head}) m->weight_bytes += d->bytes;
+        for (const LayerW& L : m->layers) m->weight_bytes += mats(L);
+        if (m->has_mtp) m->weight_bytes += mats(m->mtp.block) + m->mtp.eh_proj.bytes;
     }
     m->load_secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     return m;
@@ -326,24 +443,51 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
     qr_ = (float*)dalloc(T * qd * 4);
     gate_ = (float*)dalloc(T * qd * 4);
     attn_ = (float*)dalloc(T * qd * 4);
+    // the persistent per-layer state covers this rank's heads (all of them on one GPU)
+    const TpPlan& P = m.tp;
+    const size_t kvd_r = (size_t)P.nkv * hd;
+    const size_t qkv_r = 2 * (size_t)P.nk * c.dn_head_dim_k + (size_t)P.nv * c.dn_head_dim_v;
     for (const LayerW& L : m.layers) {
         if (L.attn) {
-            kv_.push_back({(float*)dalloc((size_t)max_pos * kvd * 4), (float*)dalloc((size_t)max_pos * kvd * 4)});
+            kv_.push_back({(float*)dalloc((size_t)max_pos * kvd_r * 4), (float*)dalloc((size_t)max_pos * kvd_r * 4)});
             dn_.push_back({});
         } else {
             DnState d;
-            d.S = (float*)dalloc(c.dn_state_elems_per_layer * 4);
-            d.conv = (float*)dalloc(c.dn_conv_state_elems_per_layer * 4);
-            d.pend_x = (float*)dalloc(T * c.dn_qkv_dim * 4);
-            d.pend_decay = (float*)dalloc(T * c.dn_n_v_heads * 4);
-            d.pend_k = (float*)dalloc(T * c.dn_n_v_heads * c.dn_head_dim_k * 4);
-            d.pend_delta = (float*)dalloc(T * c.dn_n_v_heads * c.dn_head_dim_v * 4);
+            d.S = (float*)dalloc((size_t)P.nv * c.dn_head_dim_k * c.dn_head_dim_v * 4);
+            d.conv = (float*)dalloc(qkv_r * (c.dn_conv_kernel - 1) * 4);
+            d.pend_x = (float*)dalloc(T * qkv_r * 4);
+            d.pend_decay = (float*)dalloc(T * P.nv * 4);
+            d.pend_k = (float*)dalloc(T * P.nv * c.dn_head_dim_k * 4);
+            d.pend_delta = (float*)dalloc(T * P.nv * c.dn_head_dim_v * 4);
             dn_.push_back(d);
             kv_.push_back({});
         }
     }
+    if (P.world > 1) {
+        // the exchange block: flags [XSLOTS][8], then the receive buffers (full-width rows)
+        size_t off = (size_t)XSLOTS * 8 * 4;
+        auto take = [&](size_t bytes) {
+            const size_t o = off;
+            off += (bytes + 255) & ~(size_t)255;
+            return o;
+        };
+        xo_mix_ = take(T * H * 4);
+        xo_mlp_ = take(T * H * 4);
+        xo_eh_ = take(T * H * 4);
+        xo_heads_ = take(T * std::max<size_t>(c.dn_v_dim, 1) * 4);
+        xo_attn_ = take(T * qd * 4);
+        xo_ffn_ = take(T * std::max<size_t>(FF / 256 * Q8K_IMG_BYTES, FF / 32 * Q80_IMG_BYTES));
+        xo_amx_ = take(T * 8 * 16);
+        xblk_bytes_ = off;
+        xblk_ = (uint8_t*)dalloc(xblk_bytes_);
+        xpeer_[P.rank] = xblk_;
+        xcnt_ = (unsigned*)dalloc(XSLOTS * 4);
+        xepoch_ = (unsigned*)dalloc(4);
+        xerr_ = (unsigned*)dalloc(4);
+        amx_pairs_ = (uint8_t*)dalloc(T * 16);
+    }
     if (m.has_mtp) {
-        mtp_kv_ = {(float*)dalloc((size_t)mtp_cap_ * kvd * 4), (float*)dalloc((size_t)mtp_cap_ * kvd * 4)};
+        mtp_kv_ = {(float*)dalloc((size_t)mtp_cap_ * kvd_r * 4), (float*)dalloc((size_t)mtp_cap_ * kvd_r * 4)};
         d_vids = (int32_t*)dalloc(T * 4);
         d_mids = (int32_t*)dalloc(T * 4);
         d_mpos = (int*)dalloc(T * 4);
@@ -355,10 +499,13 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
         mtp_hout_ = (float*)dalloc(T * H * 4);
     }
     counters.hist.assign(spec_k + 1, 0);
+    ck(cudaDeviceSynchronize(), "state init");  // the zeroed flags are in place before the block is exported
 }
 
 State::~State() {
     if (stream) cudaStreamSynchronize(stream);
+    for (int k = 0; k < m_.tp.world; k++)
+        if (k != m_.tp.rank && xpeer_[k]) cudaIpcCloseMemHandle(xpeer_[k]);
     if (round_exec_) cudaGraphExecDestroy(round_exec_);
     if (h_io_) cudaFreeHost(h_io_);
     for (void* p : allocs_) cudaFree(p);
@@ -370,6 +517,105 @@ void State::sync() {
     ck(cudaStreamSynchronize(stream), "decode step");
     const unsigned err = read_kernel_error(true);
     if (err) throw std::runtime_error("a device-side wait gave up (code " + std::to_string(err) + ")");
+    if (tp()) {
+        unsigned xe = 0;
+        ck(cudaMemcpy(&xe, xerr_, 4, cudaMemcpyDeviceToHost), "exchange status");
+        if (xe) {
+            const unsigned z = 0;
+            cudaMemcpy(xerr_, &z, 4, cudaMemcpyHostToDevice);
+            throw std::runtime_error("tensor-parallel exchange: a peer's slice did not arrive in time (slot " +
+                                     std::to_string(xe & 0xffff) + ")");
+        }
+    }
+}
+
+void State::tp_export(void* out) const {
+    if (!tp()) throw std::logic_error("tp_export: not a tensor-parallel state");
+    cudaIpcMemHandle_t h;
+    ck(cudaIpcGetMemHandle(&h, xblk_), "exchange export");
+    uint8_t* o = static_cast<uint8_t*>(out);
+    std::memset(o, 0, TP_HANDLE_BYTES);
+    std::memcpy(o, &h, sizeof h);
+    const uint64_t bytes = xblk_bytes_;
+    const int32_t rw[2] = {m_.tp.rank, m_.tp.world};
+    std::memcpy(o + 64, &bytes, 8);
+    std::memcpy(o + 72, rw, 8);
+}
+
+void State::tp_connect(const void* handles) {
+    if (!tp()) throw std::logic_error("tp_connect: not a tensor-parallel state");
+    if (tp_connected_) throw std::logic_error("tp_connect: already connected");
+    const uint8_t* in = static_cast<const uint8_t*>(handles);
+    for (int k = 0; k < m_.tp.world; k++) {
+        const uint8_t* hk = in + (size_t)k * TP_HANDLE_BYTES;
+        uint64_t bytes = 0;
+        int32_t rw[2];
+        std::memcpy(&bytes, hk + 64, 8);
+        std::memcpy(rw, hk + 72, 8);
+        if (rw[0] != k || rw[1] != m_.tp.world)
+            throw std::invalid_argument("tp_connect: handle " + std::to_string(k) + " is not rank " + std::to_string(k) + "'s");
+        if (bytes != xblk_bytes_)
+            throw std::invalid_argument("tp_connect: rank " + std::to_string(k) + " built its state with other sizes (spec_k, max_rows)");
+    }
+    for (int k = 0; k < m_.tp.world; k++) {
+        if (k == m_.tp.rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, in + (size_t)k * TP_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "exchange import");
+        xpeer_[k] = static_cast<uint8_t*>(p);
+    }
+    tp_connected_ = true;
+}
+
+void State::begin_session() {
+    if (!tp()) return;
+    if (!tp_connected_) throw std::logic_error("tensor-parallel state used before tp_connect");
+    count_launch();
+    ck(launch_tp_epoch(xepoch_, stream), "epoch");
+    xslot_ = 0;
+}
+
+void State::exchange(const void* src, size_t src_ld, size_t dst_off, size_t dst_ld, const int (*segs)[3], int nseg, int rows) {
+    if (xslot_ >= XSLOTS) throw std::logic_error("exchange: too many exchanges in one session");
+    XArgs a{};
+    a.src = static_cast<const uint8_t*>(src);
+    a.src_ld = (long long)src_ld;
+    a.dst_ld = (long long)dst_ld;
+    a.nseg = nseg;
+    a.rows = rows;
+    for (int i = 0; i < nseg; i++) a.seg_src[i] = segs[i][0], a.seg_dst[i] = segs[i][1], a.seg_len[i] = segs[i][2];
+    for (int k = 0; k < m_.tp.world; k++) {
+        a.dst[k] = xpeer_[k] + dst_off;
+        a.pflags[k] = reinterpret_cast<unsigned*>(xpeer_[k]);
+    }
+    a.lflags = reinterpret_cast<const unsigned*>(xblk_);
+    a.cnt = xcnt_;
+    a.epoch = xepoch_;
+    a.err = xerr_;
+    a.slot = xslot_++;
+    a.rank = m_.tp.rank;
+    a.world = m_.tp.world;
+    count_launch();
+    ck(launch_exchange(a, stream), "exchange");
+}
+
+// Greedy ids of t logits rows: on one GPU the argmax kernel; over TP ranks each rank reduces its vocabulary
+// slice to (value, global index), the pairs are exchanged and combined in rank order with the strict > rule,
+// which is the whole row's first maximum (model.rs:505-513).
+void State::argmax_rows(const float* logits, int t, int32_t* out_dev) {
+    if (!tp()) {
+        count_launch();
+        ck(launch_argmax(logits, (int)m_.cfg.vocab_size, t, out_dev, amx_scratch_, stream), "argmax");
+        return;
+    }
+    const TpPlan& P = m_.tp;
+    count_launch();
+    ck(launch_argmax_pairs(logits, P.v_rows, t, amx_pairs_, P.v_lo, P.rank == 0, amx_scratch_, stream), "argmax");
+    const int seg[1][3] = {{0, 16 * P.rank, 16}};
+    exchange(amx_pairs_, 16, xo_amx_, 16 * (size_t)P.world, seg, 1, t);
+    count_launch();
+    ck(launch_argmax_combine(xblk_ + xo_amx_, P.world, t, out_dev, stream), "argmax combine");
 }
 
 void State::upload_ids(const uint32_t* ids, int n) {
@@ -387,17 +633,18 @@ static bool needs_q80(std::initializer_list<int> ts) {
     return false;
 }
 
-void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y) {
-    // activation rows are laid out back to back at the stride of this weight's width
+void State::gemv(const DevMat& w, const float* normed_f32, int rows, float* y, const uint8_t* img) {
+    // activation rows are laid out back to back at the stride of this weight's width; `img` (when given)
+    // replaces the state's own Q8_K / Q8_0 image
     if (is_kquant(w.type)) {
         // weights are written once at load, so the GEMV may stream them before its predecessor finishes
         count_launch((rows + 3) / 4);
-        ck(launch_gemv_img(w.type, w.p, w.rows, w.cols, q8k_, rows, y, stream, true), "gemv");
+        ck(launch_gemv_img(w.type, w.p, w.rows, w.cols, img ? img : q8k_, rows, y, stream, true), "gemv");
         return;
     }
     if (w.type == T_Q8_0_TILE || w.type == T_Q4_0_TILE) {
         count_launch((rows + 3) / 4);
-        ck(launch_gemv_q80_img(w.type, w.p, w.rows, w.cols, q80_, rows, y, stream, true), "gemv");
+        ck(launch_gemv_q80_img(w.type, w.p, w.rows, w.cols, img ? img : q80_, rows, y, stream, true), "gemv");
         return;
     }
     if (w.type != T_F32) throw std::logic_error("gemv: a Q8_0/Q4_0 matrix outside the tile layout");
@@ -421,32 +668,42 @@ void State::quant_for(int type, const float* x, int n, int rows) {
        "quantise");
 }
 
-// One decoder layer over t rows (layers/mod.rs:335-377): the residual stream h_ enters as (h_ + mlp_out_) of
-// the previous layer (or the layer input `first_in` for layer 0 / the MTP block), leaves in h_ + mlp_out_.
+// One decoder layer over t rows (layers/mod.rs:335-377): the residual stream h_ enters as (h_ + mlp_in()) of
+// the previous layer (or the layer input `first_in` for layer 0 / the MTP block), leaves in h_ + mlp_in().
+// Over TP ranks the matrices produce this rank's rows; the head outputs, the mixer output, the SwiGLU image
+// and the FFN output are exchanged so that every rank continues from the full rows.
 void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int* pos_dev, bool commit_dn) {
     const ModelConfig& c = m_.cfg;
+    const TpPlan& P = m_.tp;
     const int H = (int)c.hidden_size;
     const float eps = c.rms_norm_eps;
     if (L.attn) {
+        const int hd = (int)c.head_dim_k;
         const bool k8 = needs_q8k({L.q.type, L.k.type, L.v.type}), k0 = needs_q80({L.q.type, L.k.type, L.v.type});
-        resid_norm(li == 0 ? nullptr : mlp_out_, L.attn_norm, t, normed_, k8, k0);
+        resid_norm(li == 0 ? nullptr : mlp_in(), L.attn_norm, t, normed_, k8, k0);
         gemv(L.q, normed_, t, qg_);
         gemv(L.k, normed_, t, kk_);
         gemv(L.v, normed_, t, vv_);
         QkArgs qa{qg_, kk_, vv_, L.q_norm, L.k_norm, m_.rope_cos, m_.rope_sin, pos_dev, qr_, gate_, kv->k, kv->v,
-                  (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k, (int)c.rope_dim, eps};
+                  P.nq, P.nkv, hd, (int)c.rope_dim, eps};
         count_launch(); ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
-        AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, (int)c.n_head, (int)c.n_head_kv, (int)c.head_dim_k,
+        AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, P.nq, P.nkv, hd,
                     kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
                     m_.attn_scaling};
         count_launch(); ck(launch_attention(aa, t, stream), "attention");
-        quant_for(L.o.type, attn_, L.o.cols, t);
-        gemv(L.o, attn_, t, mix_out_);
+        const float* attn_full = attn_;
+        if (tp()) {
+            const int seg[1][3] = {{0, P.qh_lo * hd * 4, P.nq * hd * 4}};
+            exchange(attn_, (size_t)P.nq * hd * 4, xo_attn_, (size_t)c.n_head * hd * 4, seg, 1, t);
+            attn_full = xg(xo_attn_);
+        }
+        quant_for(L.o.type, attn_full, L.o.cols, t);
+        gemv(L.o, attn_full, t, mix_out_);
     } else {
         const DnState& d = dn_[li];
         const bool k8 = needs_q8k({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
         const bool k0 = needs_q80({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
-        resid_norm(li == 0 ? nullptr : mlp_out_, L.attn_norm, t, normed_, k8, k0);
+        resid_norm(li == 0 ? nullptr : mlp_in(), L.attn_norm, t, normed_, k8, k0);
         gemv(L.qkv, normed_, t, qkv_);
         gemv(L.gate_z, normed_, t, z_);
         if (L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == L.beta.cols) {
@@ -459,18 +716,36 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
             gemv(L.alpha, normed_, t, alpha_);
             gemv(L.beta, normed_, t, beta_);
         }
-        count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, (int)c.dn_qkv_dim, qkv_, t, conved_, d.pend_x,
+        const int channels = L.qkv.rows;  // this rank's q, k and v channels
+        count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, channels, qkv_, t, conved_, d.pend_x,
                             commit_dn ? d_keep : nullptr, T_, stream), "conv");
+        const int dk = (int)c.dn_head_dim_k, dv = (int)c.dn_head_dim_v;
         DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,
-                     commit_dn ? d_keep : nullptr, t, T_, (int)c.dn_n_k_heads, (int)c.dn_n_v_heads, (int)c.dn_head_dim_k,
-                     (int)c.dn_head_dim_v, (int)c.dn_k_dim, (int)c.dn_qkv_dim, eps};
+                     commit_dn ? d_keep : nullptr, t, T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps};
         count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
-        quant_for(L.ssm_out.type, heads_, L.ssm_out.cols, t);
-        gemv(L.ssm_out, heads_, t, mix_out_);
+        const float* heads_full = heads_;
+        if (tp()) {
+            // local V heads g * nk + j are global heads g * n_k + kh_lo + j
+            const int G = (int)(c.dn_n_v_heads / c.dn_n_k_heads);
+            int seg[4][3];
+            for (int gi = 0; gi < G; gi++) {
+                seg[gi][0] = gi * P.nk * dv * 4;
+                seg[gi][1] = (gi * (int)c.dn_n_k_heads + P.kh_lo) * dv * 4;
+                seg[gi][2] = P.nk * dv * 4;
+            }
+            exchange(heads_, (size_t)P.nv * dv * 4, xo_heads_, (size_t)c.dn_v_dim * 4, seg, G, t);
+            heads_full = xg(xo_heads_);
+        }
+        quant_for(L.ssm_out.type, heads_full, L.ssm_out.cols, t);
+        gemv(L.ssm_out, heads_full, t, mix_out_);
+    }
+    if (tp()) {
+        const int seg[1][3] = {{0, P.h_lo * 4, P.h_rows * 4}};
+        exchange(mix_out_, (size_t)P.h_rows * 4, xo_mix_, (size_t)H * 4, seg, 1, t);
     }
     // h = x + mixer(x); then the MLP on post_attention_norm(h) (mlp.rs:53-64)
     const bool k8 = needs_q8k({L.ffn_gate.type, L.ffn_up.type}), k0 = needs_q80({L.ffn_gate.type, L.ffn_up.type});
-    resid_norm(mix_out_, L.post_norm, t, normed_, k8, k0);
+    resid_norm(mix_in(), L.post_norm, t, normed_, k8, k0);
     if (L.ffn_gate.type == L.ffn_up.type && L.ffn_gate.cols == L.ffn_up.cols &&
         (L.ffn_gate.type == T_Q4_K_TILE || L.ffn_gate.type == T_Q5_K_TILE || L.ffn_gate.type == T_Q6_K_TILE)) {
         // gate and up read the same normed rows: one launch over both (mlp.rs:55, matvec2)
@@ -483,14 +758,31 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         gemv(L.ffn_up, normed_, t, u_);
     }
     const int dt = L.ffn_down.type;
-    count_launch(); ck(launch_swiglu_quant(g_, u_, (int)c.intermediate_size, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
+    const int ffr = L.ffn_gate.rows;  // this rank's FFN rows
+    count_launch(); ck(launch_swiglu_quant(g_, u_, ffr, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
                            is_q80(dt) ? q80_ : nullptr, stream), "swiglu");
-    gemv(L.ffn_down, g_, t, mlp_out_);
+    if (tp()) {
+        const size_t FF = c.intermediate_size;
+        if (is_kquant(dt)) {
+            const int seg[1][3] = {{0, P.ff_lo / 256 * Q8K_IMG_BYTES, ffr / 256 * Q8K_IMG_BYTES}};
+            exchange(q8k_, (size_t)ffr / 256 * Q8K_IMG_BYTES, xo_ffn_, FF / 256 * Q8K_IMG_BYTES, seg, 1, t);
+        } else {
+            // Q8_0 image row: [codes: 32 B per block][{d, sum}: 8 B per block]
+            const int seg[2][3] = {{0, P.ff_lo, ffr}, {ffr, (int)FF + P.ff_lo / 32 * 8, ffr / 32 * 8}};
+            exchange(q80_, (size_t)ffr / 32 * Q80_IMG_BYTES, xo_ffn_, FF / 32 * Q80_IMG_BYTES, seg, 2, t);
+        }
+        gemv(L.ffn_down, g_, t, mlp_out_, xblk_ + xo_ffn_);
+        const int seg[1][3] = {{0, P.h_lo * 4, P.h_rows * 4}};
+        exchange(mlp_out_, (size_t)P.h_rows * 4, xo_mlp_, (size_t)H * 4, seg, 1, t);
+    } else {
+        gemv(L.ffn_down, g_, t, mlp_out_);
+    }
 }
 
 void State::forward_rows(int t, const int32_t* ids_dev, bool want_logits_all) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
+    begin_session();
     count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, ids_dev, t, h_, stream), "embed");
     for (size_t li = 0; li < m_.layers.size(); li++) {
         layer_forward(m_.layers[li], (int)li, t, &kv_[li], d_pos, true);
@@ -499,22 +791,22 @@ void State::forward_rows(int t, const int32_t* ids_dev, bool want_logits_all) {
                 capture_h_.assign(m_.layers.size() + 1, nullptr);
                 for (auto& p : capture_h_) ck(cudaMalloc(&p, (size_t)T_ * H * 4), "capture buffer");
             }
-            add_rows_kernel<<<64, 256, 0, stream>>>(h_, mlp_out_, capture_h_[li], (size_t)t * H);
+            add_rows_kernel<<<64, 256, 0, stream>>>(h_, mlp_in(), capture_h_[li], (size_t)t * H);
         }
     }
     // final norm (model.rs:430-438): the post-norm rows are what the lm_head and the MTP read
     const int ht = m_.lm_head.type;
-    resid_norm(mlp_out_, m_.output_norm, t, final_, is_kquant(ht), is_q80(ht));
+    resid_norm(mlp_in(), m_.output_norm, t, final_, is_kquant(ht), is_q80(ht));
     if (capture_ && !capture_h_.empty())
         ck(cudaMemcpyAsync(capture_h_[m_.layers.size()], final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "capture");
     if (want_logits_all) {
         gemv(m_.lm_head, final_, t, logits_);
-        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, t, d_argmax, amx_scratch_, stream), "argmax");
+        argmax_rows(logits_, t, d_argmax);
     } else {
         // only the last row's logits (prefill): quantise that row alone at row 0
         quant_for(ht, final_ + (size_t)(t - 1) * H, H, 1);
         gemv(m_.lm_head, final_ + (size_t)(t - 1) * H, 1, logits_);
-        count_launch(); ck(launch_argmax(logits_, (int)c.vocab_size, 1, d_argmax, amx_scratch_, stream), "argmax");
+        argmax_rows(logits_, 1, d_argmax);
     }
 }
 
@@ -551,12 +843,14 @@ uint32_t State::step(uint32_t id, float* logits) {
     set_dev_int(d_pos, pos_, stream);
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
+    if (logits && tp()) throw std::invalid_argument("step: logits are split over the tensor-parallel ranks");
     if (logits) ck(cudaMemcpyAsync(logits, logits_, (size_t)m_.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, stream), "logits");
     sync();
     return (uint32_t)a;
 }
 
 void State::logits_row(int row, float* out) const {
+    if (tp()) throw std::invalid_argument("logits: split over the tensor-parallel ranks");
     ck(cudaMemcpy(out, logits_ + (size_t)row * m_.cfg.vocab_size, (size_t)m_.cfg.vocab_size * 4, cudaMemcpyDeviceToHost), "logits");
 }
 
@@ -573,13 +867,22 @@ void State::mtp_rows(int t, const int32_t* ids_dev, const float* hidden, const i
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     const MtpW& M = m_.mtp;
+    begin_session();
     count_launch(); ck(launch_dequant_rows(m_.embed.type, m_.embed.p, m_.embed.bytes / m_.embed.rows, H, ids_dev, t, embed_, stream), "embed");
     count_launch(); ck(launch_rmsnorm_rows(embed_, H, M.enorm, c.rms_norm_eps, H, t, cat_, 2 * H, stream), "enorm");
     count_launch(); ck(launch_rmsnorm_rows(hidden, H, M.hnorm, c.rms_norm_eps, H, t, cat_ + H, 2 * H, stream), "hnorm");
     quant_for(M.eh_proj.type, cat_, 2 * H, t);
-    gemv(M.eh_proj, cat_, t, h_);  // u rows become the block's residual input
+    if (tp()) {
+        const TpPlan& P = m_.tp;
+        gemv(M.eh_proj, cat_, t, mix_out_);
+        const int seg[1][3] = {{0, P.h_lo * 4, P.h_rows * 4}};
+        exchange(mix_out_, (size_t)P.h_rows * 4, xo_eh_, (size_t)H * 4, seg, 1, t);
+        ck(cudaMemcpyAsync(h_, xg(xo_eh_), (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "eh rows");
+    } else {
+        gemv(M.eh_proj, cat_, t, h_);  // u rows become the block's residual input
+    }
     layer_forward(M.block, 0, t, &mtp_kv_, pos_dev, false);
-    resid_norm(mlp_out_, M.head_norm, t, mtp_hout_, false, false);
+    resid_norm(mlp_in(), M.head_norm, t, mtp_hout_, false, false);
 }
 
 // The draft of the MTP row held in mtp_h_: the shared lm_head, greedy (spec.rs:205-215, mtp.rs:132-137).
@@ -587,9 +890,10 @@ void State::enqueue_draft(int32_t* out_dev) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     float* lg = logits_ + (size_t)(T_ - 1) * c.vocab_size;
+    begin_session();
     quant_for(m_.lm_head.type, mtp_h_, H, 1);
     gemv(m_.lm_head, mtp_h_, 1, lg);
-    count_launch(); ck(launch_argmax(lg, (int)c.vocab_size, 1, out_dev, amx_scratch_, stream), "argmax");
+    argmax_rows(lg, 1, out_dev);
 }
 
 // Drafts from..k-1 by chaining single MTP rows (spec.rs:205-222): draft i comes from the MTP row of token

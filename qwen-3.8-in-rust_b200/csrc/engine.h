@@ -48,7 +48,27 @@ constexpr int ROPE_SLACK = 64;
 struct LoadOptions {
     int device = 0;
     int max_pos = 4096;  // RoPE table length
+    int tp_rank = 0, tp_world = 1;  // tensor-parallel shard of this process (world 1: the whole model)
 };
+
+// Tensor-parallel shard of one rank.  Every matrix is split by output rows, so each rank computes complete dot
+// products for its rows -- the same bits as one GPU -- and the four activations a layer produces sharded (the
+// mixer's head outputs, the mixer output, the SwiGLU output image, the FFN output) are all-gathered before the
+// next matrix reads them; the residual stream, norms and quantisation are replicated.
+//   DeltaNet: K heads [kh_lo, kh_lo + nk) and the V heads p with p % n_k in that range (V head p reads K head
+//   p % n_k), in V-head order: groups g = 0 .. n_v/n_k - 1 of nk heads starting at g * n_k + kh_lo.
+//   GQA: q heads [qh_lo, qh_lo + nq) and kv heads [kv_lo, kv_lo + nkv) (a kv head may serve two ranks).
+//   FFN rows [ff_lo, ff_lo + ff_rows) on 256-row boundaries (the SwiGLU output is exchanged as Q8_K blocks);
+//   hidden-size outputs (attn_output, ssm_out, ffn_down, eh_proj) rows [h_lo, h_lo + h_rows);
+//   lm_head rows [v_lo, v_lo + v_rows) with a (value, index) argmax exchange.
+struct TpPlan {
+    int rank = 0, world = 1;
+    int kh_lo = 0, nk = 0, nv = 0;
+    int qh_lo = 0, nq = 0, kv_lo = 0, nkv = 0;
+    int ff_lo = 0, ff_rows = 0, h_lo = 0, h_rows = 0, v_lo = 0, v_rows = 0;
+};
+// throws ConfigError when the model's dimensions do not split over `world` ranks
+TpPlan make_tp_plan(const ModelConfig& c, int rank, int world);
 
 class Model {
   public:
@@ -69,10 +89,12 @@ class Model {
     uint64_t decode_bytes = 0;   // weight bytes one plain token reads (model.rs:274)
     uint64_t mtp_bytes = 0;      // the MTP block's bytes (blk.{n_layer})
     double load_secs = 0;
+    TpPlan tp;                   // this rank's shard (world 1: everything)
     bool is_stop(uint32_t id) const;
 
   private:
     uint8_t* blob_ = nullptr;
+    std::vector<void*> shard_allocs_;  // the rank's row slices of the sharded tensors
 };
 
 struct SpecCounters {  // spec.rs:21-42
@@ -98,6 +120,13 @@ class State {
     // forced drafts for the next round (spec.rs:439-452, used by the identity tests)
     void set_drafts(const uint32_t* d, int k);
     std::vector<uint32_t> drafts() const;
+
+    // tensor parallelism: the exchange block (receive buffers + flags) is exported with a CUDA IPC handle; every
+    // rank opens all the others' before the first forward (tp_connect)
+    static constexpr int TP_HANDLE_BYTES = 80;
+    void tp_export(void* out) const;
+    void tp_connect(const void* handles);  // world x TP_HANDLE_BYTES, in rank order
+    bool tp_ready() const { return tp_connected_; }
 
     // debugging / parity: the residual stream after layer `layer` of the last forward's row `row`
     // (layer = n_layer: the post-final-norm row the lm_head read)
@@ -141,6 +170,28 @@ class State {
     float *g_ = nullptr, *u_ = nullptr, *final_ = nullptr, *logits_ = nullptr;
     float *cat_ = nullptr, *mtp_h_ = nullptr, *mtp_hout_ = nullptr;
     size_t q8k_stride_ = 0, q80_stride_ = 0;  // bytes per row of the activation buffers
+    // tensor-parallel exchange (world > 1): one device allocation, exported over CUDA IPC, holding the per-slot
+    // arrival flags [XSLOTS][8] and the receive buffers; xcnt_ (CTA counters per slot), xepoch_ (session count)
+    // and xerr_ (set when a bounded wait gave up) are local
+    static constexpr int XSLOTS = 1024;
+    uint8_t* xblk_ = nullptr;
+    size_t xblk_bytes_ = 0;
+    uint8_t* xpeer_[8] = {};  // every rank's exchange block as mapped here (xpeer_[rank] = xblk_)
+    bool tp_connected_ = false;
+    unsigned *xcnt_ = nullptr, *xepoch_ = nullptr, *xerr_ = nullptr;
+    int xslot_ = 0;
+    size_t xo_mix_ = 0, xo_mlp_ = 0, xo_eh_ = 0, xo_heads_ = 0, xo_attn_ = 0, xo_ffn_ = 0, xo_amx_ = 0;
+    uint8_t* amx_pairs_ = nullptr;  // this rank's (value, index) per row before the exchange
+    bool tp() const { return m_.tp.world > 1; }
+    float* xg(size_t off) const { return reinterpret_cast<float*>(xblk_ + off); }
+    void begin_session();
+    // copy `rows` rows of `segs` (byte ranges {src offset, dst offset, length}) from the local `src` into every
+    // rank's exchange buffer at `dst_off`, then wait until every rank's slice has arrived here
+    void exchange(const void* src, size_t src_ld, size_t dst_off, size_t dst_ld, const int (*segs)[3], int nseg, int rows);
+    void argmax_rows(const float* logits, int t, int32_t* out_dev);
+    const float* mix_in() const { return tp() ? xg(xo_mix_) : mix_out_; }
+    const float* mlp_in() const { return tp() ? xg(xo_mlp_) : mlp_out_; }
+
     struct DnState { float *S, *conv, *pend_x, *pend_decay, *pend_k, *pend_delta; };
     struct KvState { float *k, *v; };
     std::vector<DnState> dn_;
@@ -149,7 +200,7 @@ class State {
     std::vector<float*> capture_h_;  // per layer residual rows when capturing
 
     void upload_ids(const uint32_t* ids, int n);
-    void gemv(const DevMat& w, const float* normed_f32, int rows, float* y);
+    void gemv(const DevMat& w, const float* normed_f32, int rows, float* y, const uint8_t* img = nullptr);
     void resid_norm(const float* delta, const float* w, int t, float* y_out, bool k8, bool k0);
     void quant_for(int type, const float* x, int n, int rows);
     void layer_forward(const LayerW& L, int li, int t, KvState* kv, const int* pos_dev, bool commit_dn);

@@ -487,7 +487,7 @@ struct SplitTerms {  // one window buffer: [S][R][NC][8 rows][12] (8 main lanes,
     static constexpr int PER_SB = R * NC * 8 * 12;
 };
 
-template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1>
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false>
 __global__ void __launch_bounds__(32 * S, MINB)
 kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
                      int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
@@ -542,23 +542,41 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restr
 #pragma unroll
                         for (int j = 0; j < R; j++) load_frag_tile<TYPE>(wt[j] + (size_t)(sb + D * S) * TB, lane, rs, ring[d][j]);
                     }
+                    // activation words of column n + 1 are requested while column n computes (XP)
+                    uint4 xv[2][2 * GL];
+                    float xd[2];
+                    uint32_t xa[2][GL];
+                    auto load_x = [&](int n, int b) {
+                        const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+#pragma unroll
+                        for (int c = 0; c < 2 * GL; c++) xv[b][c] = __ldg(reinterpret_cast<const uint4*>(xb + 32 * g0) + c);
+                        xd[b] = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                        if constexpr (Q6) {
+                            const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
+                            xa[b][0] = a2.x, xa[b][1] = a2.y;
+                        } else {
+                            xa[b][0] = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
+                        }
+                    };
+                    if constexpr (XP) load_x(0, 0);
 #pragma unroll
                     for (int n = 0; n < NC; n++) {
-                        const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+                        const int b = XP ? (n & 1) : 0;
+                        if constexpr (XP) {
+                            if (n + 1 < NC) load_x(n + 1, b ^ 1);
+                        } else {
+                            load_x(n, 0);
+                        }
                         uint32_t xw[8 * GL];
 #pragma unroll
                         for (int c = 0; c < 2 * GL; c++) {
-                            const uint4 v = __ldg(reinterpret_cast<const uint4*>(xb + 32 * g0) + c);
+                            const uint4 v = xv[b][c];
                             xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
                         }
-                        const float dx = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                        const float dx = xd[b];
                         uint32_t aux[GL];
-                        if constexpr (Q6) {
-                            const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
-                            aux[0] = a2.x, aux[1] = a2.y;
-                        } else {
-                            aux[0] = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
-                        }
+#pragma unroll
+                        for (int gi = 0; gi < GL; gi++) aux[gi] = xa[b][gi];
 #pragma unroll
                         for (int j = 0; j < R; j++) {
                             const float dd = __fmul_rn(dx, dec[j].dw);
@@ -613,7 +631,7 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restr
     }
 }
 
-template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1>
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false>
 cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl,
                          const uint8_t* w_b = nullptr, int rows_b = 0, float* y_b = nullptr) {
     cudaLaunchConfig_t cfg = {};
@@ -626,7 +644,7 @@ cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, fl
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS, MINB>, w, rows, y, w_b, rows_b, y_b, nb,
+    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS, MINB, XP>, w, rows, y, w_b, rows_b, y_b, nb,
                               (const uint8_t*)img);
 }
 
@@ -710,7 +728,7 @@ __global__ void __launch_bounds__(32 * S)
 kq_gemv_bulk_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8_t* __restrict__ img, float* __restrict__ y) {
     using G = BulkGeo<TYPE, NC, R, D, S>;
     constexpr int GL = 2, TB = G::TB, PER_SB = G::PER_SB;
-    constexpr bool Q6 = TYPE == T_Q6_K;
+    constexpr bool Q6 = TYPE == T_Q6_K, XP = false;
     constexpr int CHAINS = R * NC * 8 * (Q6 ? 8 : 12);
     constexpr int CPT = (CHAINS + 32 * S - 1) / (32 * S);
     static_assert(S * D <= 16, "mbarrier region");
@@ -769,23 +787,41 @@ kq_gemv_bulk_kernel(const uint8_t* __restrict__ w, int rows, int nb, const uint8
                     __syncwarp();
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     if (sb + D * S < nb) issue(d, sb + D * S);
+                    // activation words of column n + 1 are requested while column n computes (XP)
+                    uint4 xv[2][2 * GL];
+                    float xd[2];
+                    uint32_t xa[2][GL];
+                    auto load_x = [&](int n, int b) {
+                        const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+#pragma unroll
+                        for (int c = 0; c < 2 * GL; c++) xv[b][c] = __ldg(reinterpret_cast<const uint4*>(xb + 32 * g0) + c);
+                        xd[b] = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                        if constexpr (Q6) {
+                            const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
+                            xa[b][0] = a2.x, xa[b][1] = a2.y;
+                        } else {
+                            xa[b][0] = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
+                        }
+                    };
+                    if constexpr (XP) load_x(0, 0);
 #pragma unroll
                     for (int n = 0; n < NC; n++) {
-                        const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+                        const int b = XP ? (n & 1) : 0;
+                        if constexpr (XP) {
+                            if (n + 1 < NC) load_x(n + 1, b ^ 1);
+                        } else {
+                            load_x(n, 0);
+                        }
                         uint32_t xw[8 * GL];
 #pragma unroll
                         for (int c = 0; c < 2 * GL; c++) {
-                            const uint4 v = __ldg(reinterpret_cast<const uint4*>(xb + 32 * g0) + c);
+                            const uint4 v = xv[b][c];
                             xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
                         }
-                        const float dx = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                        const float dx = xd[b];
                         uint32_t aux[GL];
-                        if constexpr (Q6) {
-                            const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
-                            aux[0] = a2.x, aux[1] = a2.y;
-                        } else {
-                            aux[0] = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
-                        }
+#pragma unroll
+                        for (int gi = 0; gi < GL; gi++) aux[gi] = xa[b][gi];
 #pragma unroll
                         for (int j = 0; j < R; j++) {
                             const float dd = __fmul_rn(dx, dec[j].dw);
@@ -879,10 +915,11 @@ template <int TYPE, int NC>
 cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr bool KQ = TYPE != T_Q6_K;
     int cfg = g_tile_cfg;
-    // measured on B200 (shapes 5120 x 17408 ... 248320 x 5120): the super-block range split over 4 warps, two
-    // tiles per warp, one super-block in flight per warp, at most 128 registers (4 CTAs per SM); for one column
-    // on short matrices one tile per warp and two in flight
-    if (cfg == 0) cfg = (NC == 1 && rows <= 6144) ? 9 : 20;
+    // measured on B200 (shapes 5120 x 17408 ... 248320 x 5120): the super-block range split over 4 warps, one
+    // super-block in flight per warp, the next column's activation words requested while a column computes; two
+    // tiles per warp at most 128 registers (4 CTAs per SM), except short matrices (<= 6144 rows, too few CTAs to
+    // fill the SMs): one tile per warp for one column, 168 registers (3 CTAs per SM) for several
+    if (cfg == 0) cfg = rows <= 6144 ? (NC == 1 ? 30 : 29) : 28;
     switch (cfg) {
     case 1: return launch_tile<TYPE, NC, 1, 4, false>(w, rows, nb, img, y, s, pdl);
     case 2: return launch_tile<TYPE, NC, 1, 8, false>(w, rows, nb, img, y, s, pdl);
@@ -910,7 +947,11 @@ cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img,
     case 24: return launch_bulk<TYPE, NC, 1, 4, 4>(w, rows, nb, img, y, s, pdl);
     case 25: return launch_bulk<TYPE, NC, 2, 2, 4>(w, rows, nb, img, y, s, pdl);
     case 26: return launch_split<TYPE, NC, 1, 1, 8, 0, 2>(w, rows, nb, img, y, s, pdl);
-    default: return launch_split<TYPE, NC, 1, 2, 8, 0, 2>(w, rows, nb, img, y, s, pdl);
+    case 27: return launch_split<TYPE, NC, 1, 2, 8, 0, 2>(w, rows, nb, img, y, s, pdl);
+    case 28: return launch_split<TYPE, NC, 2, 1, 4, 0, 4, true>(w, rows, nb, img, y, s, pdl);
+    case 29: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, true>(w, rows, nb, img, y, s, pdl);
+    case 30: return launch_split<TYPE, NC, 1, 1, 4, 0, 4, true>(w, rows, nb, img, y, s, pdl);
+    default: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, true>(w, rows, nb, img, y, s, pdl);
     }
 }
 
@@ -1058,10 +1099,10 @@ template <int TYPE>
 cudaError_t launch_pair_type(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                              const void* img, int nc, cudaStream_t s, bool pdl) {
     switch (nc) {
-    case 1: return launch_split<TYPE, 1, 2, 1, 4, 0, 4>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    case 2: return launch_split<TYPE, 2, 2, 1, 4, 0, 4>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    case 3: return launch_split<TYPE, 3, 2, 1, 4, 0, 4>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    default: return launch_split<TYPE, 4, 2, 1, 4, 0, 4>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 1: return launch_split<TYPE, 1, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 2: return launch_split<TYPE, 2, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 3: return launch_split<TYPE, 3, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    default: return launch_split<TYPE, 4, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
     }
 }
 }  // namespace

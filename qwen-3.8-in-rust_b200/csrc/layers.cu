@@ -616,9 +616,13 @@ __global__ void attention_kernel(const AttnArgs a) {
 // chunk results in chunk order with the strict > rule and resets the row's counter.
 constexpr int ARGMAX_CHUNK = 8192;
 
+// With `pairs` (a tensor-parallel rank's vocabulary slice starting at index `base`): the row's result is
+// written as {float value, int index + base} at pairs + 16 * row, and the seed x[0] is used only when `seed`
+// (rank 0); otherwise the slice's own first maximum (index -1 when it holds only NaN).
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, int n, int32_t* __restrict__ out,
                                                      float* __restrict__ pval, int* __restrict__ pidx,
-                                                     unsigned* __restrict__ counter) {
+                                                     unsigned* __restrict__ counter, uint8_t* __restrict__ pairs, int base,
+                                                     int seed) {
     griddep_wait();
     griddep_launch();
     const int row = blockIdx.y, chunks = gridDim.x, c = blockIdx.x;
@@ -651,14 +655,19 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x
     __syncthreads();
     if (last && threadIdx.x == 0) {
         __threadfence();
-        float g = r[0];  // the reference's seed: x[0] at index 0
-        int gi = 0;
+        float g = seed ? r[0] : -INFINITY;  // the reference's seed: x[0] at index 0
+        int gi = seed ? 0 : -1;
         for (int k = 0; k < chunks; k++) {
             const volatile float* pv = pval + (size_t)row * chunks;
             const volatile int* pi = pidx + (size_t)row * chunks;
-            if (pi[k] >= 0 && pv[k] > g) g = pv[k], gi = pi[k];
+            if (pi[k] >= 0 && (gi < 0 || pv[k] > g)) g = pv[k], gi = pi[k];
         }
-        out[row] = gi;
+        if (pairs) {
+            *reinterpret_cast<float*>(pairs + 16 * (size_t)row) = g;
+            *reinterpret_cast<int*>(pairs + 16 * (size_t)row + 4) = gi < 0 ? -1 : gi + base;
+        } else {
+            out[row] = gi;
+        }
         counter[row] = 0u;
     }
 }
@@ -809,7 +818,18 @@ cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, void* s
     unsigned* counter = (unsigned*)scratch;
     float* pval = (float*)((uint8_t*)scratch + ((size_t)rows * 4 + 15) / 16 * 16);
     int* pidx = (int*)(pval + (size_t)rows * chunks);
-    return launch_pdl(argmax_kernel, dim3(chunks, rows), dim3(256), 0, s, x, n, out, pval, pidx, counter);
+    return launch_pdl(argmax_kernel, dim3(chunks, rows), dim3(256), 0, s, x, n, out, pval, pidx, counter, (uint8_t*)nullptr, 0, 1);
+}
+
+cudaError_t launch_argmax_pairs(const float* x, int n, int rows, uint8_t* pairs, int base, bool seed, void* scratch,
+                                cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const int chunks = (n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK;
+    unsigned* counter = (unsigned*)scratch;
+    float* pval = (float*)((uint8_t*)scratch + ((size_t)rows * 4 + 15) / 16 * 16);
+    int* pidx = (int*)(pval + (size_t)rows * chunks);
+    return launch_pdl(argmax_kernel, dim3(chunks, rows), dim3(256), 0, s, x, n, (int32_t*)nullptr, pval, pidx, counter, pairs,
+                      base, seed ? 1 : 0);
 }
 
 }  // namespace qdec

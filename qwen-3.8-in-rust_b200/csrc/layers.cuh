@@ -66,5 +66,9 @@ cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s);
 // scratch: argmax_scratch_bytes(n, rows) bytes, zero-filled once before the first use (launches keep it so).
 size_t argmax_scratch_bytes(int n, int rows);
 cudaError_t launch_argmax(const float* x, int n, int rows, int32_t* out, void* scratch, cudaStream_t s);
+// a tensor-parallel rank's slice [base, base + n) of each row: {float value, int global index} at pairs + 16 * row
+// (the seed element 0 only when `seed`, i.e. on rank 0)
+cudaError_t launch_argmax_pairs(const float* x, int n, int rows, uint8_t* pairs, int base, bool seed, void* scratch,
+                                cudaStream_t s);
 
 }  // namespace qdec

@@ -79,6 +79,11 @@ def lib():
         U32P = ctypes.POINTER(ctypes.c_uint32)
         for name, args in {
             "qdec_open": [ctypes.c_char_p, ctypes.POINTER(Opts), PP],
+            "qdec_open_tp": [ctypes.c_char_p, ctypes.POINTER(Opts), I, I, PP],
+            "qdec_tp_plan": [ctypes.c_char_p, I, I, ctypes.POINTER(ctypes.c_int32)],
+            "qdec_tp_plan_dims": [ctypes.POINTER(ctypes.c_uint32), I, I, ctypes.POINTER(ctypes.c_int32)],
+            "qdec_tp_export": [P, P],
+            "qdec_tp_connect": [P, P],
             "qdec_close": [P],
             "qdec_model_get_info": [P, ctypes.POINTER(ModelInfo)],
             "qdec_is_stop": [P, ctypes.c_uint32],
@@ -203,13 +208,48 @@ def synth_gguf(path, preset, seed, threads=0):
     _check(lib().qdec_synth_gguf(str(path).encode(), preset.encode(), seed, threads))
 
 
-class Model:
-    """Model::load_with (crates/core/src/model.rs:184): the GGUF's weights resident on `device`."""
+TP_HANDLE_BYTES = 80
+TP_PLAN_FIELDS = ("rank", "world", "kh_lo", "nk", "nv", "qh_lo", "nq", "kv_lo", "nkv", "ff_lo", "ff_rows", "h_lo", "h_rows",
+                  "v_lo", "v_rows")
 
-    def __init__(self, path, device=0, max_pos=4096):
+
+def tp_plan(path, rank, world):
+    """The rows / heads rank `rank` of `world` keeps (from the GGUF header; no device needed)."""
+    out = (ctypes.c_int32 * 16)()
+    _check(lib().qdec_tp_plan(str(path).encode(), rank, world, out))
+    return dict(zip(TP_PLAN_FIELDS, list(out)))
+
+
+def tp_plan_dims(hidden, ffn, vocab, n_head, n_head_kv, dn_k_heads, dn_v_heads, rank, world):
+    """tp_plan from the dimensions alone (a model with DeltaNet layers when dn_k_heads > 0)."""
+    dims = _u32([hidden, ffn, vocab, n_head, n_head_kv, dn_k_heads, dn_v_heads, 1 if dn_k_heads else 0])
+    out = (ctypes.c_int32 * 16)()
+    _check(lib().qdec_tp_plan_dims(dims, rank, world, out))
+    return dict(zip(TP_PLAN_FIELDS, list(out)))
+
+
+def gather_handles(handle, group=None):
+    """Every rank's exchange handle, in rank order, over a torch.distributed process group."""
+    import torch.distributed as dist
+
+    hs = [None] * dist.get_world_size(group)
+    dist.all_gather_object(hs, handle, group=group)
+    return hs
+
+
+class Model:
+    """Model::load_with (crates/core/src/model.rs:184): the GGUF's weights resident on `device`.
+
+    tp=(rank, world) loads rank `rank`'s shard for tensor parallelism over `world` GPUs (one process each)."""
+
+    def __init__(self, path, device=0, max_pos=4096, tp=None):
         self._h = ctypes.c_void_p()
         o = Opts(device, max_pos)
-        _check(lib().qdec_open(str(path).encode(), ctypes.byref(o), ctypes.byref(self._h)))
+        self.tp = tuple(tp) if tp else (0, 1)
+        if tp:
+            _check(lib().qdec_open_tp(str(path).encode(), ctypes.byref(o), self.tp[0], self.tp[1], ctypes.byref(self._h)))
+        else:
+            _check(lib().qdec_open(str(path).encode(), ctypes.byref(o), ctypes.byref(self._h)))
         info = ModelInfo()
         _check(lib().qdec_model_get_info(self._h, ctypes.byref(info)))
         self.info = info
@@ -255,6 +295,22 @@ class State:
     @property
     def pos(self):
         return lib().qdec_state_pos(self._h)
+
+    def tp_export(self):
+        """This rank's exchange handle (bytes) for the other ranks."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        _check(lib().qdec_tp_export(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Open every rank's exchange block: `handles` = all ranks' tp_export() results in rank order."""
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _check(lib().qdec_tp_connect(self._h, buf))
+
+    def tp_connect_group(self, group=None):
+        """tp_export + all_gather over a torch.distributed process group + tp_connect."""
+        self.tp_connect(gather_handles(self.tp_export(), group))
 
     @property
     def stream(self):
