@@ -174,6 +174,9 @@ int qdec_tp_plan_dims(const uint32_t dims[8], int tp_rank, int tp_world, int32_t
 #define QDEC_TP_HANDLE_BYTES 80
 int qdec_tp_export(const qdec_state *s, void *handle_out);
 int qdec_tp_connect(qdec_state *s, const void *handles);
+/* Exchange timing totals of a TP state (device clock, first thread of each exchange): {exchanges, ns writing
+ * its slice to every rank, ns until the other ranks' lines had arrived, 0}. */
+int qdec_tp_stats(const qdec_state *s, uint64_t out4[4]);
 int qdec_model_get_info(const qdec_model *m, qdec_model_info *info);
 /* Nonzero when `id` is a stop id: the GGUF EOS ids plus the architecture's (crates/core/src/arch.rs:79-90).
  * Replaces Model::is_stop (crates/core/src/model.rs:492). */

@@ -121,6 +121,14 @@ int qdec_tp_export(const qdec_state* s, void* handle_out) {
     });
 }
 
+int qdec_tp_stats(const qdec_state* s, uint64_t out4[4]) {
+    if (!s || !out4) return qdec::fail(QDEC_EINVAL, "qdec_tp_stats: null argument");
+    return guard("qdec_tp_stats", [&] {
+        s->s->tp_stats(out4);
+        return QDEC_OK;
+    });
+}
+
 int qdec_tp_connect(qdec_state* s, const void* handles) {
     if (!s || !handles) return qdec::fail(QDEC_EINVAL, "qdec_tp_connect: null argument");
     return guard("qdec_tp_connect", [&] {

@@ -464,8 +464,12 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
         }
     }
     if (P.world > 1) {
-        // the exchange block: flags [XSLOTS][8], then the receive buffers (full-width rows)
-        size_t off = (size_t)XSLOTS * 8 * 4;
+        // the exchange block: two line buffers (2 bytes of lines per byte of the largest exchange), then the
+        // receive buffers (full-width rows)
+        const size_t ext = std::max({T * H * 4, T * std::max<size_t>(c.dn_v_dim, 1) * 4, T * qd * 4,
+                                     T * std::max<size_t>(FF / 256 * Q8K_IMG_BYTES, FF / 32 * Q80_IMG_BYTES), T * 8 * 16});
+        xll_bytes_ = (2 * ext + 255) & ~(size_t)255;
+        size_t off = 2 * xll_bytes_;
         auto take = [&](size_t bytes) {
             const size_t o = off;
             off += (bytes + 255) & ~(size_t)255;
@@ -478,12 +482,13 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
         xo_attn_ = take(T * qd * 4);
         xo_ffn_ = take(T * std::max<size_t>(FF / 256 * Q8K_IMG_BYTES, FF / 32 * Q80_IMG_BYTES));
         xo_amx_ = take(T * 8 * 16);
+        xo_pad_ = take(8 * 16);
         xblk_bytes_ = off;
         xblk_ = (uint8_t*)dalloc(xblk_bytes_);
         xpeer_[P.rank] = xblk_;
-        xcnt_ = (unsigned*)dalloc(XSLOTS * 4);
         xepoch_ = (unsigned*)dalloc(4);
         xerr_ = (unsigned*)dalloc(4);
+        xstats_ = (unsigned long long*)dalloc(4 * 8);
         amx_pairs_ = (uint8_t*)dalloc(T * 16);
     }
     if (m.has_mtp) {
@@ -568,6 +573,13 @@ void State::tp_connect(const void* handles) {
     tp_connected_ = true;
 }
 
+void State::tp_stats(uint64_t out[4]) const {
+    for (int i = 0; i < 4; i++) out[i] = 0;
+    if (!tp()) return;
+    ck(cudaStreamSynchronize(stream), "sync");
+    ck(cudaMemcpy(out, xstats_, 4 * 8, cudaMemcpyDeviceToHost), "exchange stats");
+}
+
 void State::begin_session() {
     if (!tp()) return;
     if (!tp_connected_) throw std::logic_error("tensor-parallel state used before tp_connect");
@@ -578,6 +590,7 @@ void State::begin_session() {
 
 void State::exchange(const void* src, size_t src_ld, size_t dst_off, size_t dst_ld, const int (*segs)[3], int nseg, int rows) {
     if (xslot_ >= XSLOTS) throw std::logic_error("exchange: too many exchanges in one session");
+    if ((size_t)rows * dst_ld * 2 > xll_bytes_) throw std::logic_error("exchange: larger than the line buffers");
     XArgs a{};
     a.src = static_cast<const uint8_t*>(src);
     a.src_ld = (long long)src_ld;
@@ -585,14 +598,13 @@ void State::exchange(const void* src, size_t src_ld, size_t dst_off, size_t dst_
     a.nseg = nseg;
     a.rows = rows;
     for (int i = 0; i < nseg; i++) a.seg_src[i] = segs[i][0], a.seg_dst[i] = segs[i][1], a.seg_len[i] = segs[i][2];
-    for (int k = 0; k < m_.tp.world; k++) {
-        a.dst[k] = xpeer_[k] + dst_off;
-        a.pflags[k] = reinterpret_cast<unsigned*>(xpeer_[k]);
-    }
-    a.lflags = reinterpret_cast<const unsigned*>(xblk_);
-    a.cnt = xcnt_;
+    const size_t ll = (xseq_++ & 1) * xll_bytes_;  // consecutive exchanges alternate between the line buffers
+    for (int k = 0; k < m_.tp.world; k++) a.ll[k] = xpeer_[k] + ll;
+    a.ll_local = xblk_ + ll;
+    a.out = xblk_ + dst_off;
     a.epoch = xepoch_;
     a.err = xerr_;
+    a.stats = xstats_;
     a.slot = xslot_++;
     a.rank = m_.tp.rank;
     a.world = m_.tp.world;
@@ -709,8 +721,9 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         if (L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == L.beta.cols) {
             // ssm_alpha and ssm_beta read the same normed rows: one launch (gated_deltanet.rs:148-149)
             count_launch();
+            // normed_ comes from the norm two launches back: the pair runs alongside the gate_z GEMV
             ck(launch_gemv_f32_pair((const float*)L.alpha.p, L.alpha.rows, alpha_, (const float*)L.beta.p, L.beta.rows, beta_,
-                                    L.alpha.cols, normed_, t, stream),
+                                    L.alpha.cols, normed_, t, stream, true),
                "alpha/beta");
         } else {
             gemv(L.alpha, normed_, t, alpha_);
@@ -967,6 +980,7 @@ void State::enqueue_round() {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     const int t = k_ + 1;
+    const uint64_t xseq0 = xseq_;
     ck(cudaMemcpyAsync(d_vids, h_io_, 4, cudaMemcpyHostToDevice, stream), "x_p");
     forward_rows(t, d_vids, true);  // the verify batch: x_p, d_1..d_k
     count_launch();
@@ -979,6 +993,12 @@ void State::enqueue_round() {
     ck(cudaGetLastError(), "select row");
     enqueue_draft(d_vids + 1);
     enqueue_chain(1);
+    if (tp() && ((xseq_ - xseq0) & 1)) {
+        // an even number of exchanges per round keeps consecutive exchanges on alternate line buffers from one
+        // replay of the round graph to the next: pad with a 16-byte exchange
+        const int seg[1][3] = {{0, 16 * m_.tp.rank, 16}};
+        exchange(amx_pairs_, 16, xo_pad_, 16 * (size_t)m_.tp.world, seg, 1, 1);
+    }
     ck(cudaMemcpyAsync(h_io_ + 16, d_emit, (size_t)(k_ + 2) * 4, cudaMemcpyDeviceToHost, stream), "emitted");
 }
 

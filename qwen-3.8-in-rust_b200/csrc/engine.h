@@ -127,6 +127,8 @@ class State {
     void tp_export(void* out) const;
     void tp_connect(const void* handles);  // world x TP_HANDLE_BYTES, in rank order
     bool tp_ready() const { return tp_connected_; }
+    // exchange timing totals since the state was made: {exchanges, ns copying, ns fencing + flagging, ns waiting}
+    void tp_stats(uint64_t out[4]) const;
 
     // debugging / parity: the residual stream after layer `layer` of the last forward's row `row`
     // (layer = n_layer: the post-final-norm row the lm_head read)
@@ -170,17 +172,19 @@ class State {
     float *g_ = nullptr, *u_ = nullptr, *final_ = nullptr, *logits_ = nullptr;
     float *cat_ = nullptr, *mtp_h_ = nullptr, *mtp_hout_ = nullptr;
     size_t q8k_stride_ = 0, q80_stride_ = 0;  // bytes per row of the activation buffers
-    // tensor-parallel exchange (world > 1): one device allocation, exported over CUDA IPC, holding the per-slot
-    // arrival flags [XSLOTS][8] and the receive buffers; xcnt_ (CTA counters per slot), xepoch_ (session count)
-    // and xerr_ (set when a bounded wait gave up) are local
+    // tensor-parallel exchange (world > 1): one device allocation, exported over CUDA IPC, holding two line
+    // buffers (the peers write into them; consecutive exchanges alternate) and the receive buffers; xepoch_
+    // (session count), xerr_ (set when a bounded wait gave up) and xstats_ are local
     static constexpr int XSLOTS = 1024;
     uint8_t* xblk_ = nullptr;
-    size_t xblk_bytes_ = 0;
+    size_t xblk_bytes_ = 0, xll_bytes_ = 0;  // whole block; one line buffer (2 x the largest exchange)
     uint8_t* xpeer_[8] = {};  // every rank's exchange block as mapped here (xpeer_[rank] = xblk_)
     bool tp_connected_ = false;
-    unsigned *xcnt_ = nullptr, *xepoch_ = nullptr, *xerr_ = nullptr;
+    unsigned *xepoch_ = nullptr, *xerr_ = nullptr;
+    unsigned long long* xstats_ = nullptr;
     int xslot_ = 0;
-    size_t xo_mix_ = 0, xo_mlp_ = 0, xo_eh_ = 0, xo_heads_ = 0, xo_attn_ = 0, xo_ffn_ = 0, xo_amx_ = 0;
+    uint64_t xseq_ = 0;  // exchanges enqueued so far (graph replays advance it by an even count)
+    size_t xo_mix_ = 0, xo_mlp_ = 0, xo_eh_ = 0, xo_heads_ = 0, xo_attn_ = 0, xo_ffn_ = 0, xo_amx_ = 0, xo_pad_ = 0;
     uint8_t* amx_pairs_ = nullptr;  // this rank's (value, index) per row before the exchange
     bool tp() const { return m_.tp.world > 1; }
     float* xg(size_t off) const { return reinterpret_cast<float*>(xblk_ + off); }

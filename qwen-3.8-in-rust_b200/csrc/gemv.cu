@@ -385,10 +385,16 @@ q80_gemv_kernel(const uint8_t* __restrict__ w, int rows, int nblk, const uint8_t
 // [0, rows_b) of w_b): thread j computes the 32-element partial of block j (left to right), then thread 0 chains
 // the block partials in order and adds the tail partial (dot.rs:180-198).  All partials of a row are computed at
 // once, so the row costs one load latency plus the two dependent chains.
+// `early`: x was written at least two kernels before this one (never by the kernel right before it), so the
+// whole product runs before griddepcontrol.wait, alongside the preceding kernel.
 __global__ void __launch_bounds__(256) f32_gemv_kernel(const float* __restrict__ w_a, int rows_a, float* __restrict__ y_a,
                                                        const float* __restrict__ w_b, int rows_b, float* __restrict__ y_b,
-                                                       int cols, const float* __restrict__ x) {
+                                                       int cols, const float* __restrict__ x, int early) {
     __shared__ float part[512];
+    if (!early) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    }
     const int n = blockIdx.y;
     const bool first = (int)blockIdx.x < rows_a;
     const int row = first ? blockIdx.x : blockIdx.x - rows_a;
@@ -422,6 +428,10 @@ __global__ void __launch_bounds__(256) f32_gemv_kernel(const float* __restrict__
         for (int j = 0; j < nfull; j++) acc = __fadd_rn(acc, part[j]);
         acc = __fadd_rn(acc, nparts > nfull ? part[nfull] : 0.0f);  // the tail partial, +0 when empty (dot.rs:194-197)
         (first ? y_a : y_b)[(size_t)n * (first ? rows_a : rows_b) + row] = acc;
+    }
+    if (early) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
 }
 
@@ -557,11 +567,23 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
 }
 
 cudaError_t launch_gemv_f32_pair(const float* w_a, int rows_a, float* y_a, const float* w_b, int rows_b, float* y_b, int cols,
-                                 const float* x, int ncols, cudaStream_t s) {
+                                 const float* x, int ncols, cudaStream_t s, bool early) {
     if (cols > 512 * 32) return cudaErrorInvalidValue;  // 512 partials of shared memory: cols <= 16384
     if (rows_a + rows_b == 0 || ncols == 0) return cudaSuccess;
-    f32_gemv_kernel<<<dim3(rows_a + rows_b, ncols), 256, 0, s>>>(w_a, rows_a, y_a, w_b, rows_b, y_b, cols, x);
-    return cudaGetLastError();
+    if (!early) {
+        f32_gemv_kernel<<<dim3(rows_a + rows_b, ncols), 256, 0, s>>>(w_a, rows_a, y_a, w_b, rows_b, y_b, cols, x, 0);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows_a + rows_b, ncols);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, f32_gemv_kernel, w_a, rows_a, y_a, w_b, rows_b, y_b, cols, x, 1);
 }
 
 cudaError_t launch_quantize_q8k(const float* x, int n, int rows, uint8_t* out, cudaStream_t s) {

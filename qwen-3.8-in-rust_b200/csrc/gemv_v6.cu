@@ -910,16 +910,25 @@ int g_tile_cfg = [] {
     return e ? atoi(e) : 0;
 }();
 
+// The default configuration for `rows` rows (all of them split kernels with one super-block in flight per warp
+// and the next column's activation words requested while a column computes), measured on B200 over the shapes of
+// one GPU and of the tensor-parallel slices (640 .. 248320 rows, 5120 .. 17408 columns): the fewer the rows, the
+// fewer CTAs, so short matrices take one tile per warp and split the super-blocks over 8 warps, long ones two
+// tiles per warp over 4 warps at <= 128 registers (4 CTAs per SM).
+inline int default_split_cfg(int nc, int rows) {
+    if (nc == 1) return rows <= 6144 ? 30 : 28;
+    if (rows <= 2048) return 31;  // R1, S8, 2 CTAs per SM
+    if (rows <= 3072) return 30;  // R1, S4
+    if (rows <= 6144) return 29;  // R2, S4, 168 registers
+    return 28;                    // R2, S4, 128 registers
+}
+
 // Configurations (R tiles per warp, D super-blocks in flight, FP32 scale multiply for Q4_K/Q5_K).
 template <int TYPE, int NC>
 cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr bool KQ = TYPE != T_Q6_K;
     int cfg = g_tile_cfg;
-    // measured on B200 (shapes 5120 x 17408 ... 248320 x 5120): the super-block range split over 4 warps, one
-    // super-block in flight per warp, the next column's activation words requested while a column computes; two
-    // tiles per warp at most 128 registers (4 CTAs per SM), except short matrices (<= 6144 rows, too few CTAs to
-    // fill the SMs): one tile per warp for one column, 168 registers (3 CTAs per SM) for several
-    if (cfg == 0) cfg = rows <= 6144 ? (NC == 1 ? 30 : 29) : 28;
+    if (cfg == 0) cfg = default_split_cfg(NC, rows);
     switch (cfg) {
     case 1: return launch_tile<TYPE, NC, 1, 4, false>(w, rows, nb, img, y, s, pdl);
     case 2: return launch_tile<TYPE, NC, 1, 8, false>(w, rows, nb, img, y, s, pdl);
@@ -1095,14 +1104,26 @@ cudaError_t launch_gemv_img(int type, const uint8_t* w, int rows, int cols, cons
 }
 
 namespace {
+template <int TYPE, int NC>
+cudaError_t launch_pair_nc(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                           const void* img, cudaStream_t s, bool pdl) {
+    // the configuration of one matrix with the rows of both (the launch has the CTAs of both)
+    switch (default_split_cfg(NC, rows_a + rows_b)) {
+    case 31: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 30: return launch_split<TYPE, NC, 1, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 29: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    default: return launch_split<TYPE, NC, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    }
+}
+
 template <int TYPE>
 cudaError_t launch_pair_type(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                              const void* img, int nc, cudaStream_t s, bool pdl) {
     switch (nc) {
-    case 1: return launch_split<TYPE, 1, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    case 2: return launch_split<TYPE, 2, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    case 3: return launch_split<TYPE, 3, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
-    default: return launch_split<TYPE, 4, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 1: return launch_pair_nc<TYPE, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch_pair_nc<TYPE, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch_pair_nc<TYPE, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    default: return launch_pair_nc<TYPE, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }
 }  // namespace

@@ -27,8 +27,10 @@ cudaError_t launch_gemv(int type, const uint8_t* w, int rows, int cols, const vo
                         cudaStream_t s);
 // F32 weights: rows of w_a then rows of w_b (w_b may be null) against the same f32 columns, y_a / y_b laid out
 // [column][row]; cols <= 16384.
+// early: x was written two or more kernels back (not by the kernel right before), so the product may run
+// before griddepcontrol.wait, alongside its predecessor (launched as a programmatic dependent)
 cudaError_t launch_gemv_f32_pair(const float* w_a, int rows_a, float* y_a, const float* w_b, int rows_b, float* y_b, int cols,
-                                 const float* x, int ncols, cudaStream_t s);
+                                 const float* x, int ncols, cudaStream_t s, bool early = false);
 // Bytes of one activation row of `cols` values in the form `type` consumes (reference layouts).
 size_t act_row_bytes(int type, int cols);
 int num_sms();

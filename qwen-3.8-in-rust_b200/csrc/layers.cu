@@ -85,12 +85,13 @@ resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b
                         const float* __restrict__ w, float eps, int n, float* __restrict__ y_out,
                         uint8_t* __restrict__ img_out, uint8_t* __restrict__ q80_out) {
     extern __shared__ __align__(16) float sm[];
-    float* xs = sm;             // the whole row h
+    float* sq = sm;             // squares of the row, lane-major: sq[l * (n / 8) + k] = h[8k + l]^2 (n % 256 == 0)
     float* red = sm + n;        // 16
     float* ys = red + 16;       // this chunk's normed values
+    __shared__ float hc[256];   // this chunk of h
     griddep_wait();
     griddep_launch();
-    const int row = blockIdx.y, c0 = blockIdx.x * 256;
+    const int row = blockIdx.y, c0 = blockIdx.x * 256, per = n / 8;
     const float4* a4 = reinterpret_cast<const float4*>(a + (size_t)row * n);
     const float4* b4 = b ? reinterpret_cast<const float4*>(b + (size_t)row * n) : nullptr;
     for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
@@ -99,12 +100,30 @@ resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b
             const float4 u = b4[i];
             v.x = __fadd_rn(v.x, u.x), v.y = __fadd_rn(v.y, u.y), v.z = __fadd_rn(v.z, u.z), v.w = __fadd_rn(v.w, u.w);
         }
-        reinterpret_cast<float4*>(xs)[i] = v;
+        // elements 4i .. 4i+3: lanes (4i) % 8 .. +3, position (4i) / 8 in each lane
+        const int l0 = (4 * i) & 7, k = (4 * i) >> 3;
+        sq[(l0 + 0) * per + k] = __fmul_rn(v.x, v.x);
+        sq[(l0 + 1) * per + k] = __fmul_rn(v.y, v.y);
+        sq[(l0 + 2) * per + k] = __fmul_rn(v.z, v.z);
+        sq[(l0 + 3) * per + k] = __fmul_rn(v.w, v.w);
+        if (4 * i >= c0 && 4 * i < c0 + 256) reinterpret_cast<float4*>(hc)[(4 * i - c0) >> 2] = v;
     }
     __syncthreads();
-    if (h_out) h_out[(size_t)row * n + c0 + threadIdx.x] = xs[c0 + threadIdx.x];
-    const float inv = inv_rms_of(sum_squares_8lane_block(xs, n, red), n, eps);
-    const float y = __fmul_rn(__fmul_rn(xs[c0 + threadIdx.x], inv), w[c0 + threadIdx.x]);
+    if (h_out) h_out[(size_t)row * n + c0 + threadIdx.x] = hc[threadIdx.x];
+    // the 8-lane sum of squares (rmsnorm.rs:55-76): lane l adds h[l]^2, h[l+8]^2, ... left to right
+    if (threadIdx.x < 8) {
+        const float4* q = reinterpret_cast<const float4*>(sq + threadIdx.x * per);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int k = 0; k < per / 4; k++) {
+            const float4 v = q[k];
+            acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+        }
+        red[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    const float inv = inv_rms_of(reduce8(red), n, eps);
+    const float y = __fmul_rn(__fmul_rn(hc[threadIdx.x], inv), w[c0 + threadIdx.x]);
     ys[threadIdx.x] = y;
     if (y_out) y_out[(size_t)row * n + c0 + threadIdx.x] = y;
     __syncthreads();
@@ -158,11 +177,21 @@ quant_rows_kernel(const float* __restrict__ x, int n, uint8_t* __restrict__ img_
 // Causal depthwise conv1d (+ SiLU) for t rows, one thread per channel (conv.rs:11-36).  The committed window
 // `state` (channels x (K-1)) first absorbs the `keep` pending inputs of the previous call (the accepted rows of
 // the previous round), then the t new rows are stepped from it; their inputs become the new pending rows.
+// Launched as a programmatic dependent of the ssm_alpha/ssm_beta GEMV, whose outputs it does not read: x (the
+// qkv projection) is three launches back, so the whole step runs before griddepcontrol.wait.
+__device__ __forceinline__ void conv_done() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __global__ void conv_step_kernel(float* __restrict__ state, const float* __restrict__ w, int K, int channels,
                                  const float* __restrict__ x, int t, float* __restrict__ out, float* __restrict__ pend_x,
                                  const int* __restrict__ keep_prev, int max_t) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= channels) return;
+    if (c >= channels) {
+        conv_done();
+        return;
+    }
     float st[8];
     for (int j = 0; j < K - 1; j++) st[j] = state[(size_t)c * (K - 1) + j];
     const int keep = keep_prev ? *keep_prev : 0;
@@ -182,6 +211,7 @@ __global__ void conv_step_kernel(float* __restrict__ state, const float* __restr
         out[(size_t)i * channels + c] = silu_f32(acc);
         if (i < max_t) pend_x[(size_t)i * channels + c] = xn;
     }
+    conv_done();
 }
 
 // One CTA per V head p, one thread per value column j (blockDim.x == dv, dk <= DK_MAX); the head's state column
@@ -311,6 +341,18 @@ __global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
 #pragma unroll
         for (int k = 0; k < HK; k++) Sg[(size_t)(k0 + k) * dv + j] = S[k];
     }
+    // gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) of the first chunk's rows
+    const int nr0 = min(CH, a.t);
+    if (t < nr0) {
+        const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)t * a.n_v + p], a.dt_bias[p])));
+        gate[t][0] = exp_f32(g);
+        gate[t][1] = sigmoid_f32(a.beta[(size_t)t * a.n_v + p]);
+    }
+    float zr[CH];
+#pragma unroll
+    for (int i = 0; i < CH; i++) zr[i] = (h == 1 && i < nr0) ? a.z[(size_t)i * a.n_v * dv + p * dv + j] : 0.0f;
+    griddep_wait();
+    griddep_launch();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
     for (int c0 = 0; c0 < a.t; c0 += CH) {
         const int nr = min(CH, a.t - c0);
@@ -322,9 +364,10 @@ __global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
         }
         __syncthreads();
         // l2norm (deltanet.rs:19-27, sums left to right): warp w normalises q of rows w, w + warps, .. on lane 0
-        // and k on lane 16; gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) on lane 8
+        // and k on lane 16; the gates of later chunks on lane 8
         for (int i = warp; i < nr && (lane & 7) == 0; i += blockDim.x / 32) {
             if (lane == 8) {
+                if (c0 == 0) continue;
                 const int r = c0 + i;
                 const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)r * a.n_v + p], a.dt_bias[p])));
                 gate[i][0] = exp_f32(g);
@@ -389,6 +432,152 @@ __global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
             __syncthreads();
             const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
             if (h == 1) a.heads[(size_t)r * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
+        }
+    }
+}
+
+// The same computation with the two halves of each value column in two different warps (blockDim.x == 2 * dv):
+// warp w < dv/32 holds S[0, DK/2) of columns 32w .. 32w+31, warp w + dv/32 holds S[DK/2, DK) of the same
+// columns, so every warp runs all 32 lanes on one half.  The k-ordered sums (kv, o) stay single left-to-right
+// chains: the low-half warp sums its 64 terms from 0 and hands the partial sum through shared memory, the
+// high-half warp continues from it.
+template <int DK>
+__global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a) {
+    constexpr int HK = DK / 2;
+    constexpr int CH = 8;  // rows whose q/k norms and gates are computed together (they do not depend on S)
+    const int p = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int dv = a.dv, wph = dv / 32;  // warps per half
+    const int h = warp >= wph ? 1 : 0, j = (warp - h * wph) * 32 + lane;
+    const int k0 = h * HK;
+    const int dk = DK;
+    const int kh = p % a.n_k;
+    __shared__ __align__(16) float qs_all[CH][DK], ks_all[CH][DK];
+    __shared__ float gate[CH][2], nrm[CH][2];  // (decay, beta), (1/|q|, 1/|k|)
+    __shared__ float red[16], outs[128], part[128], dlt[128];
+    // Before griddepcontrol.wait: everything the conv kernel (launched right before) does not write -- the state
+    // and the previous call's pending rows (this layer's own), the gates of the first rows (ssm_alpha/ssm_beta,
+    // two launches back) and their z rows (attn_gate, three back).
+    float S[HK];
+    float* Sg = a.S + (size_t)p * dk * dv;
+#pragma unroll
+    for (int k = 0; k < HK; k++) S[k] = Sg[(size_t)(k0 + k) * dv + j];
+    const int keep = a.keep_prev ? *a.keep_prev : 0;
+    for (int i = 0; i < keep; i++) {  // commit the previous call's accepted rows (spec.rs:395-415 replay order)
+        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
+        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk + k0;
+        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
+#pragma unroll
+        for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
+#pragma unroll
+        for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
+    }
+    if (keep > 0) {
+#pragma unroll
+        for (int k = 0; k < HK; k++) Sg[(size_t)(k0 + k) * dv + j] = S[k];
+    }
+    // gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) of the first chunk's rows
+    const int nr0 = min(CH, a.t);
+    if (t < nr0) {
+        const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)t * a.n_v + p], a.dt_bias[p])));
+        gate[t][0] = exp_f32(g);
+        gate[t][1] = sigmoid_f32(a.beta[(size_t)t * a.n_v + p]);
+    }
+    float zr[CH];
+#pragma unroll
+    for (int i = 0; i < CH; i++) zr[i] = (h == 1 && i < nr0) ? a.z[(size_t)i * a.n_v * dv + p * dv + j] : 0.0f;
+    griddep_wait();
+    griddep_launch();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
+    for (int c0 = 0; c0 < a.t; c0 += CH) {
+        const int nr = min(CH, a.t - c0);
+        for (int e = t; e < nr * DK; e += blockDim.x) {
+            const int i = e / DK, k = e % DK;
+            const float* row = a.conved + (size_t)(c0 + i) * a.conv_dim;
+            qs_all[i][k] = row[kh * dk + k];
+            ks_all[i][k] = row[a.kd + kh * dk + k];
+        }
+        __syncthreads();
+        // l2norm (deltanet.rs:19-27, sums left to right): warp w normalises q of rows w, w + warps, .. on lane 0
+        // and k on lane 16; the gates of later chunks on lane 8
+        for (int i = warp; i < nr && (lane & 7) == 0; i += blockDim.x / 32) {
+            if (lane == 8) {
+                if (c0 == 0) continue;
+                const int r = c0 + i;
+                const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)r * a.n_v + p], a.dt_bias[p])));
+                gate[i][0] = exp_f32(g);
+                gate[i][1] = sigmoid_f32(a.beta[(size_t)r * a.n_v + p]);
+            } else if (lane != 24) {
+                const float* vec = lane == 0 ? qs_all[i] : ks_all[i];
+                float ss = 0.0f;
+#pragma unroll
+                for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+                nrm[i][lane == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+            }
+        }
+        __syncthreads();
+        for (int e = t; e < nr * DK; e += blockDim.x) {
+            const int i = e / DK, k = e % DK;
+            qs_all[i][k] = __fmul_rn(__fmul_rn(qs_all[i][k], nrm[i][0]), scale);
+            ks_all[i][k] = __fmul_rn(ks_all[i][k], nrm[i][1]);
+        }
+        __syncthreads();
+        for (int i = 0; i < nr; i++) {
+            const int r = c0 + i;
+            const float* qs = qs_all[i] + k0;
+            const float* ks = ks_all[i] + k0;
+            const float decay = gate[i][0], beta = gate[i][1];
+#pragma unroll
+            for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
+            // kv = sum_k S[k] k[k]: the low half from 0, the high half from the low half's sum
+            float kv = 0.0f;
+            if (h == 0) {
+#pragma unroll
+                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+                part[j] = kv;
+            }
+            __syncthreads();
+            if (h == 1) {
+                kv = part[j];
+#pragma unroll
+                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+                const float v = a.conved[(size_t)r * a.conv_dim + 2 * a.kd + p * dv + j];
+                dlt[j] = __fmul_rn(__fsub_rn(v, kv), beta);
+            }
+            __syncthreads();
+            const float delta = dlt[j];
+#pragma unroll
+            for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
+            if (h == 0) {
+                float o = 0.0f;
+#pragma unroll
+                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+                part[j] = o;
+            }
+            if (r < a.max_t) {
+                if (t == 0) a.pend_decay[(size_t)r * a.n_v + p] = decay;
+                for (int k = t; k < dk; k += blockDim.x) a.pend_k[((size_t)r * a.n_v + p) * dk + k] = ks_all[i][k];
+                if (h == 1) a.pend_delta[((size_t)r * a.n_v + p) * dv + j] = delta;
+            }
+            __syncthreads();
+            float o = 0.0f;
+            if (h == 1) {
+                o = part[j];
+#pragma unroll
+                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+                outs[j] = o;
+            }
+            __syncthreads();
+            // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47); the helper ends with a barrier, after
+            // which outs, part, dlt and this chunk's rows may be overwritten
+            const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
+            if (h == 1) {
+                float z = 0.0f;
+#pragma unroll
+                for (int q = 0; q < CH; q++)
+                    if (q == i) z = zr[q];
+                if (c0 > 0) z = a.z[(size_t)r * a.n_v * dv + p * dv + j];
+                a.heads[(size_t)r * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
+            }
         }
     }
 }
@@ -699,6 +888,7 @@ cudaError_t launch_resid_norm_quant(const float* a, const float* b, float* h_out
     if (n % 256) return cudaErrorInvalidValue;
     if (h_out && (h_out == a || h_out == b)) return cudaErrorInvalidValue;
     const size_t smem = (size_t)(n + 16 + 256) * sizeof(float);
+    if (n % 256 || smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr_done = false;
     if (!attr_done) {
         cudaError_t e = cudaFuncSetAttribute(resid_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -736,8 +926,9 @@ cudaError_t launch_quant_rows(const float* x, int n, int rows, uint8_t* img_out,
 
 cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, const float* x, int t, float* out,
                              float* pend_x, const int* keep_prev, int max_t, cudaStream_t s) {
-    conv_step_kernel<<<(channels + 255) / 256, 256, 0, s>>>(state, w, K, channels, x, t, out, pend_x, keep_prev, max_t);
-    return cudaGetLastError();
+    const cudaError_t e = launch_pdl(conv_step_kernel, dim3((channels + 255) / 256), dim3(256), 0, s, state, w, K, channels, x, t,
+                                     out, pend_x, keep_prev, max_t);
+    return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 template <int DK>
@@ -770,6 +961,16 @@ cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s) {
     }();
     if (!plain && a.dv % 8 == 0 && a.dv / 32 <= 8 && (a.dk == 128 || a.dk == 64)) {
         cudaError_t e = a.dk == 128 ? launch_deltanet_cluster<128>(a, s) : launch_deltanet_cluster<64>(a, s);
+        return e == cudaSuccess ? cudaGetLastError() : e;
+    }
+    static const bool pair = [] {
+        // the two halves of a column in one warp (QDEC_DELTANET=pair) instead of two warps
+        const char* e = getenv("QDEC_DELTANET");
+        return e && strcmp(e, "pair") == 0;
+    }();
+    if (!pair && a.dv % 32 == 0 && a.dv <= 128 && (a.dk == 128 || a.dk == 64)) {
+        cudaError_t e = a.dk == 128 ? launch_pdl(deltanet_halves_kernel<128>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a)
+                                    : launch_pdl(deltanet_halves_kernel<64>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a);
         return e == cudaSuccess ? cudaGetLastError() : e;
     }
     if (a.dv % 16 == 0 && a.dv <= 128 && (a.dk == 128 || a.dk == 64)) {

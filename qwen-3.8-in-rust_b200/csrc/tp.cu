@@ -1,7 +1,8 @@
 // Tensor-parallel exchange kernels.  The ranks are processes on the GPUs of one node; each maps the others'
-// exchange blocks (CUDA IPC, plain peer loads and stores over NVLink -- no multicast) and the all-gather of a
-// sharded activation is one kernel per rank: copy the slice to every rank, fence, flag, wait for every flag.
-// Stream order then makes the gathered rows visible to the kernels that read them.
+// exchange blocks (CUDA IPC, plain peer stores over NVLink -- no multicast) and the all-gather of a sharded
+// activation is one kernel per rank: write its slice to every rank as tagged 16-byte lines, poll its own line
+// buffer until every line of the full rows carries the step's tag, unpack.  Stream order then makes the
+// gathered rows visible to the kernels that read them.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -13,57 +14,83 @@ namespace qdec {
 namespace {
 
 constexpr unsigned long long EXCHANGE_WAIT_NS = 5000000000ull;  // 5 s: a peer this late is treated as gone
+constexpr unsigned XSLOT_TAGS = 1024;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_line(uint8_t* p, uint32_t d0, uint32_t d1, uint32_t tag) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(d0), "r"(tag), "r"(d1), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint4 ld_line(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+// which segment (and offset in it) a byte offset of a slice row falls in
+__device__ __forceinline__ int seg_of(const XArgs& a, int& o) {
+    int s = 0;
+    while (s + 1 < a.nseg && o >= a.seg_len[s]) o -= a.seg_len[s++];
+    return s;
 }
 
 __global__ void __launch_bounds__(256) exchange_kernel(const XArgs a) {
+    // launched as a programmatic dependent: wait for the producer of `src`, then let the consumer be scheduled
+    // (its own griddepcontrol.wait holds it until this kernel has completed, polls included)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const unsigned long long t0 = globaltimer_ns();
+    const unsigned tag = *reinterpret_cast<const volatile unsigned*>(a.epoch) * XSLOT_TAGS + (unsigned)a.slot + 1u;
+    const long long nthr = (long long)gridDim.x * blockDim.x, tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     int rb = 0;
     for (int s = 0; s < a.nseg; s++) rb += a.seg_len[s];
-    const int vpr = rb / 16;
-    const long long total = (long long)vpr * a.rows;
-    for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < total; v += (long long)gridDim.x * blockDim.x) {
-        const int row = (int)(v / vpr);
-        int o = (int)(v % vpr) * 16, s = 0;
-        while (s + 1 < a.nseg && o >= a.seg_len[s]) o -= a.seg_len[s++];
-        const uint4 val = *reinterpret_cast<const uint4*>(a.src + row * a.src_ld + a.seg_src[s] + o);
-        for (int k = 0; k < a.world; k++) *reinterpret_cast<uint4*>(a.dst[k] + row * a.dst_ld + a.seg_dst[s] + o) = val;
+    // push: this rank's slice, 8 bytes per line, to every other rank; and into its own receive buffer
+    const int upr = rb / 8;
+    for (long long u = tid; u < (long long)upr * a.rows; u += nthr) {
+        const int row = (int)(u / upr);
+        int o = (int)(u % upr) * 8;
+        const int s = seg_of(a, o);
+        const uint2 d = *reinterpret_cast<const uint2*>(a.src + row * a.src_ld + a.seg_src[s] + o);
+        const long long pos = row * a.dst_ld + a.seg_dst[s] + o;  // byte offset in the full rows
+        *reinterpret_cast<uint2*>(a.out + pos) = d;
+        for (int k = 0; k < a.world; k++)
+            if (k != a.rank) st_line(a.ll[k] + pos * 2, d.x, d.y, tag);
     }
-    __shared__ bool last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();  // this CTA's stores (ordered by the barrier) before its count
-        last = atomicAdd(&a.cnt[a.slot], 1u) == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!last || threadIdx.x != 0) return;
-    a.cnt[a.slot] = 0u;
-    __threadfence_system();  // every CTA's stores before the flags
-    const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.epoch);
-    for (int k = 0; k < a.world; k++) st_release_sys(a.pflags[k] + a.slot * 8 + a.rank, e);
-    const unsigned long long t0 = globaltimer_ns();
-    for (int k = 0; k < a.world; k++) {
-        // flags only grow (one session's value per use); a peer cannot run a whole session ahead of this rank
-        while ((int)(ld_acquire_sys(a.lflags + a.slot * 8 + k) - e) < 0) {
-            if (globaltimer_ns() - t0 > EXCHANGE_WAIT_NS) {
-                atomicCAS(a.err, 0u, 0x10000u | (unsigned)a.slot);
-                return;
-            }
-            __nanosleep(64);
+    const unsigned long long t1 = globaltimer_ns();
+    // poll: every line of the full rows outside this rank's own slice
+    const int lpr = (int)(a.dst_ld / 8);
+    bool ok = true;
+    for (long long u = tid; u < (long long)lpr * a.rows && ok; u += nthr) {
+        const int row = (int)(u / lpr);
+        const int b = (int)(u % lpr) * 8;
+        bool mine = false;
+        for (int s = 0; s < a.nseg; s++) mine |= b >= a.seg_dst[s] && b < a.seg_dst[s] + a.seg_len[s];
+        if (mine) continue;
+        const long long pos = row * a.dst_ld + b;
+        uint4 v = ld_line(a.ll_local + pos * 2);
+        if (v.y != tag || v.w != tag) {
+            const unsigned long long w0 = globaltimer_ns();
+            do {
+                __nanosleep(32);
+                v = ld_line(a.ll_local + pos * 2);
+                if (globaltimer_ns() - w0 > EXCHANGE_WAIT_NS) {
+                    atomicCAS(a.err, 0u, 0x10000u | (unsigned)a.slot);
+                    ok = false;
+                    break;
+                }
+            } while (v.y != tag || v.w != tag);
         }
+        *reinterpret_cast<uint2*>(a.out + pos) = make_uint2(v.x, v.z);
     }
-    __threadfence_system();
+    if (a.stats && threadIdx.x == 0 && blockIdx.x == 0) {
+        const unsigned long long t2 = globaltimer_ns();
+        atomicAdd(a.stats, 1ull);
+        atomicAdd(a.stats + 1, t1 - t0);
+        atomicAdd(a.stats + 2, t2 - t1);
+    }
 }
 
 __global__ void epoch_kernel(unsigned* e) { *e += 1u; }
@@ -86,16 +113,22 @@ __global__ void argmax_combine_kernel(const uint8_t* __restrict__ pairs, int wor
 
 cudaError_t launch_exchange(const XArgs& a, cudaStream_t s) {
     if (a.world < 1 || a.world > 8 || a.nseg < 1 || a.nseg > 4 || a.rows <= 0) return cudaErrorInvalidValue;
-    int rb = 0;
-    for (int i = 0; i < a.nseg; i++) {
-        if (a.seg_len[i] <= 0 || (a.seg_len[i] | a.seg_src[i] | a.seg_dst[i]) % 16) return cudaErrorInvalidValue;
-        rb += a.seg_len[i];
-    }
+    for (int i = 0; i < a.nseg; i++)
+        if (a.seg_len[i] <= 0 || (a.seg_len[i] | a.seg_src[i] | a.seg_dst[i]) % 16 || a.seg_dst[i] + a.seg_len[i] > a.dst_ld)
+            return cudaErrorInvalidValue;
     if (a.src_ld % 16 || a.dst_ld % 16) return cudaErrorInvalidValue;
-    const long long vec = (long long)rb / 16 * a.rows;
-    const int grid = (int)std::min<long long>((vec + 255) / 256, 64);
-    exchange_kernel<<<grid, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    const long long lines = a.dst_ld / 8 * a.rows;
+    const int grid = (int)std::max<long long>(1, std::min<long long>((lines + 255) / 256, 32));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, exchange_kernel, a);
 }
 
 cudaError_t launch_tp_epoch(unsigned* epoch, cudaStream_t s) {

@@ -5,28 +5,33 @@
 
 namespace qdec {
 
-// One all-gather step.  Every rank copies `rows` rows of its slice -- up to four byte ranges per row, {seg_src,
-// seg_dst, seg_len}, multiples of 16 bytes -- from `src` into every rank's receive buffer dst[k] (peer memory
-// opened over CUDA IPC; dst[rank] is local), then raises its flag for `slot` in every rank's flag array
-// (pflags[k][slot * 8 + rank] = the session epoch) and waits until all ranks' flags for `slot` have arrived in
-// its own array (lflags).  The wait is bounded in time: on expiry it records 0x10000 | slot in *err and returns.
+// One all-gather step in the low-latency line format: every 8 data bytes travel as a 16-byte line
+// {d0, tag, d1, tag} written with one vector store, so a line that shows this step's tag in both halves holds
+// its data -- no fences or separate flags.  Each rank writes the lines of its slice (`rows` rows of up to four
+// byte ranges {seg_src, seg_dst, seg_len}, multiples of 16 bytes, from `src`) into every other rank's line
+// buffer ll[k] at the position that mirrors the slice's place in the full rows (line index = byte offset / 8,
+// row stride dst_ld), copies it straight into its own receive buffer `out`, then polls its own line buffer
+// `ll_local` for the rest of the full rows (rows x dst_ld bytes) and unpacks them into `out`.  tag =
+// epoch * 1024 + slot + 1 changes every step; consecutive steps alternate between two line buffers, and a
+// rank cannot run two steps ahead of another, so a line is never overwritten before it is read.  The poll is
+// bounded in time: on expiry the step records 0x10000 | slot in *err and returns.
 struct XArgs {
     const uint8_t* src;
     long long src_ld;
-    uint8_t* dst[8];
+    uint8_t* ll[8];          // every rank's line buffer for this step (ll[rank] unused)
+    const uint8_t* ll_local;  // this rank's line buffer for this step
+    uint8_t* out;            // this rank's receive buffer (full rows)
     long long dst_ld;
     int seg_src[4], seg_dst[4], seg_len[4];
     int nseg, rows;
-    unsigned* pflags[8];
-    const unsigned* lflags;
-    unsigned* cnt;          // local: CTAs of this slot that finished copying
-    const unsigned* epoch;  // local: the session counter
+    const unsigned* epoch;   // local: the session counter
     unsigned* err;
+    unsigned long long* stats;  // local: {steps, ns until pushed, ns until all arrived, 0}
     int slot, rank, world;
 };
 
 cudaError_t launch_exchange(const XArgs& a, cudaStream_t s);
-// *epoch += 1: a new session (its exchanges reuse the slots from 0 with a larger flag value)
+// *epoch += 1: a new session (its exchanges reuse the slots from 0 with new tags)
 cudaError_t launch_tp_epoch(unsigned* epoch, cudaStream_t s);
 // out[row] = the first maximum over the ranks' (value, index) pairs, 16 bytes per rank per row, in rank order
 // with the strict > rule (rank 0's pair is seeded with the row's element 0); pairs with index < 0 are skipped.

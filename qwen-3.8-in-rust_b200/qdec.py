@@ -84,6 +84,7 @@ def lib():
             "qdec_tp_plan_dims": [ctypes.POINTER(ctypes.c_uint32), I, I, ctypes.POINTER(ctypes.c_int32)],
             "qdec_tp_export": [P, P],
             "qdec_tp_connect": [P, P],
+            "qdec_tp_stats": [P, ctypes.POINTER(ctypes.c_uint64)],
             "qdec_close": [P],
             "qdec_model_get_info": [P, ctypes.POINTER(ModelInfo)],
             "qdec_is_stop": [P, ctypes.c_uint32],
@@ -307,6 +308,11 @@ class State:
         blob = b"".join(handles)
         buf = ctypes.create_string_buffer(blob, len(blob))
         _check(lib().qdec_tp_connect(self._h, buf))
+
+    def tp_stats(self):
+        buf = (ctypes.c_uint64 * 4)()
+        _check(lib().qdec_tp_stats(self._h, buf))
+        return dict(zip(("exchanges", "ns_push", "ns_wait", "unused"), list(buf)))
 
     def tp_connect_group(self, group=None):
         """tp_export + all_gather over a torch.distributed process group + tp_connect."""
