@@ -232,7 +232,7 @@ int qdec_tune_gemv(int impl, int config) {
         return QDEC_OK;
     }
     if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6 or 8");
-    if (config < 0 || config > 31) return fail(QDEC_EINVAL, "gemv configuration must be 0..31");
+    if (config < 0 || config > 35) return fail(QDEC_EINVAL, "gemv configuration must be 0..35");
     set_gemv_impl(impl);
     set_gemv_v6_config(config);
     return QDEC_OK;

@@ -487,7 +487,7 @@ struct SplitTerms {  // one window buffer: [S][R][NC][8 rows][12] (8 main lanes,
     static constexpr int PER_SB = R * NC * 8 * 12;
 };
 
-template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false>
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false, bool XR = false>
 __global__ void __launch_bounds__(32 * S, MINB)
 kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
                      int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
@@ -535,6 +535,48 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restr
                 const int sb = win * S + ws;
                 float* tb = terms[win & 1] + ws * PER_SB;
                 if (sb < nb) {
+                  if constexpr (XR) {
+                    // every column's activation words for this super-block stay in registers while the R tiles
+                    // are decoded one at a time against them (one load of each word serves R rows)
+                    uint32_t xw[NC][8 * GL];
+                    float xdv[NC];
+                    uint32_t xav[NC][GL];
+#pragma unroll
+                    for (int n = 0; n < NC; n++) {
+                        const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+#pragma unroll
+                        for (int c = 0; c < 2 * GL; c++) {
+                            const uint4 v = __ldg(reinterpret_cast<const uint4*>(xb + 32 * g0) + c);
+                            xw[n][4 * c] = v.x, xw[n][4 * c + 1] = v.y, xw[n][4 * c + 2] = v.z, xw[n][4 * c + 3] = v.w;
+                        }
+                        xdv[n] = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                        if constexpr (Q6) {
+                            const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
+                            xav[n][0] = a2.x, xav[n][1] = a2.y;
+                        } else {
+                            xav[n][0] = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < R; j++) {
+                        Dec<TYPE, GL> dj;
+                        decode<TYPE, GL, FPS>(ring[d][j], tg, dj);
+                        if (sb + D * S < nb) load_frag_tile<TYPE>(wt[j] + (size_t)(sb + D * S) * TB, lane, rs, ring[d][j]);
+#pragma unroll
+                        for (int n = 0; n < NC; n++) {
+                            const float dd = __fmul_rn(xdv[n], dj.dw);
+                            float* t = tb + ((j * NC + n) * 8 + rs) * 12;
+                            float2 mt;
+                            mt.x = __fmul_rn(dd, lane_sum<TYPE, GL, FPS>(dj, xw[n], 0, Q6 ? xav[n][0] : 0u));
+                            mt.y = __fmul_rn(dd, lane_sum<TYPE, GL, FPS>(dj, xw[n], 1, Q6 ? xav[n][1] : 0u));
+                            *reinterpret_cast<float2*>(t + 2 * tg) = mt;
+                            if constexpr (!Q6) {
+                                const float prod = biased_to_f32(dp2a_lo(xav[n][0], dj.mpair, MAGIC_I));
+                                t[8 + tg] = __fmul_rn(__fmul_rn(-xdv[n], dj.dminw), prod);
+                            }
+                        }
+                    }
+                  } else {
                     Dec<TYPE, GL> dec[R];
 #pragma unroll
                     for (int j = 0; j < R; j++) decode<TYPE, GL, FPS>(ring[d][j], tg, dec[j]);
@@ -591,6 +633,7 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restr
                             }
                         }
                     }
+                  }
                 }
                 __syncthreads();
                 // chain owners: add this window's terms in super-block order
@@ -631,7 +674,7 @@ kq_gemv_split_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restr
     }
 }
 
-template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false>
+template <int TYPE, int NC, int R, int D, int S, int FPS, int MINB = 1, bool XP = false, bool XR = false>
 cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl,
                          const uint8_t* w_b = nullptr, int rows_b = 0, float* y_b = nullptr) {
     cudaLaunchConfig_t cfg = {};
@@ -644,7 +687,7 @@ cudaError_t launch_split(const uint8_t* w, int rows, int nb, const void* img, fl
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS, MINB, XP>, w, rows, y, w_b, rows_b, y_b, nb,
+    return cudaLaunchKernelEx(&cfg, kq_gemv_split_kernel<TYPE, NC, R, D, S, FPS, MINB, XP, XR>, w, rows, y, w_b, rows_b, y_b, nb,
                               (const uint8_t*)img);
 }
 
@@ -915,10 +958,15 @@ int g_tile_cfg = [] {
 // one GPU and of the tensor-parallel slices (640 .. 248320 rows, 5120 .. 17408 columns): the fewer the rows, the
 // fewer CTAs, so short matrices take one tile per warp and split the super-blocks over 8 warps, long ones two
 // tiles per warp over 4 warps at <= 128 registers (4 CTAs per SM).
+// For Q4_K / Q5_K at several columns the R tiles of a warp are decoded one after another against every column's
+// activation words held in registers (one load of a word serves R rows), which relieves the L1 pipe; Q6_K
+// (twice the decode registers) keeps the column-by-column order.
+template <int TYPE>
 inline int default_split_cfg(int nc, int rows) {
     if (nc == 1) return rows <= 6144 ? 30 : 28;
     if (rows <= 2048) return 31;  // R1, S8, 2 CTAs per SM
     if (rows <= 3072) return 30;  // R1, S4
+    if (TYPE != T_Q6_K) return rows <= 12288 ? 32 : 34;  // resident activations: R2 S4 3 CTAs / R4 S2 2 CTAs per SM
     if (rows <= 6144) return 29;  // R2, S4, 168 registers
     return 28;                    // R2, S4, 128 registers
 }
@@ -928,7 +976,7 @@ template <int TYPE, int NC>
 cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr bool KQ = TYPE != T_Q6_K;
     int cfg = g_tile_cfg;
-    if (cfg == 0) cfg = default_split_cfg(NC, rows);
+    if (cfg == 0) cfg = default_split_cfg<TYPE>(NC, rows);
     switch (cfg) {
     case 1: return launch_tile<TYPE, NC, 1, 4, false>(w, rows, nb, img, y, s, pdl);
     case 2: return launch_tile<TYPE, NC, 1, 8, false>(w, rows, nb, img, y, s, pdl);
@@ -960,7 +1008,11 @@ cudaError_t launch_tile_cfg(const uint8_t* w, int rows, int nb, const void* img,
     case 28: return launch_split<TYPE, NC, 2, 1, 4, 0, 4, true>(w, rows, nb, img, y, s, pdl);
     case 29: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, true>(w, rows, nb, img, y, s, pdl);
     case 30: return launch_split<TYPE, NC, 1, 1, 4, 0, 4, true>(w, rows, nb, img, y, s, pdl);
-    default: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, true>(w, rows, nb, img, y, s, pdl);
+    case 31: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, true>(w, rows, nb, img, y, s, pdl);
+    case 32: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, false, true>(w, rows, nb, img, y, s, pdl);
+    case 33: return launch_split<TYPE, NC, 2, 1, 4, 0, 4, false, true>(w, rows, nb, img, y, s, pdl);
+    case 34: return launch_split<TYPE, NC, 4, 1, 2, 0, 2, false, true>(w, rows, nb, img, y, s, pdl);
+    default: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, false, true>(w, rows, nb, img, y, s, pdl);
     }
 }
 
@@ -1108,10 +1160,12 @@ template <int TYPE, int NC>
 cudaError_t launch_pair_nc(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                            const void* img, cudaStream_t s, bool pdl) {
     // the configuration of one matrix with the rows of both (the launch has the CTAs of both)
-    switch (default_split_cfg(NC, rows_a + rows_b)) {
+    switch (default_split_cfg<TYPE>(NC, rows_a + rows_b)) {
     case 31: return launch_split<TYPE, NC, 1, 1, 8, 0, 2, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
     case 30: return launch_split<TYPE, NC, 1, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
     case 29: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 32: return launch_split<TYPE, NC, 2, 1, 4, 0, 3, false, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
+    case 34: return launch_split<TYPE, NC, 4, 1, 2, 0, 2, false, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
     default: return launch_split<TYPE, NC, 2, 1, 4, 0, 4, true>(w_a, rows_a, nb, img, y_a, s, pdl, w_b, rows_b, y_b);
     }
 }

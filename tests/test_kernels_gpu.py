@@ -255,7 +255,7 @@ def test_gemv_reference_layout_kernel_bit_exact(q, orc, t):
 
 
 @pytest.mark.parametrize("t", [12, 13, 14])
-@pytest.mark.parametrize("cfg", range(1, 32))
+@pytest.mark.parametrize("cfg", range(1, 36))
 def test_gemv_tile_layout_every_config_bit_exact(q, orc, t, cfg):
     """Weights repacked into the tile layout (8 rows x one super-block per tile block): the oracle's bits for
     1..5 columns in every configuration, a super-block count that is not a multiple of any depth, a tile count
