@@ -471,15 +471,19 @@ def dominant_gemv_timing(dev, launches=200):
     for i in range(min(10, launches)):
         qdec.gemv_image(t, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
     torch.cuda.synchronize()
-    pairs = []
-    for i in range(launches):
+    # back-to-back launches between two events on the launching stream (the weight sets rotate, 150 MB > L2):
+    # the average launch duration, without per-launch event records in between; median of 5 batches
+    batch = max(1, launches // 5)
+    per = []
+    for b in range(5):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        qdec.gemv_image(t, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
+        for i in range(batch):
+            qdec.gemv_image(t, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
         e1.record(stream)
-        pairs.append((e0, e1))
-    torch.cuda.synchronize()
-    ms = statistics.median(a.elapsed_time(b) for a, b in pairs)
+        torch.cuda.synchronize()
+        per.append(e0.elapsed_time(e1) / batch)
+    ms = statistics.median(per)
     alg = rows * (cols // 256) * Q4K_BB + n * (cols // 256) * 292 + 4 * n * rows
     del sets
     return alg, ms
