@@ -555,7 +555,13 @@ def run_spec_qdec(args, world, rank, local):
     if world > 1 and not args.no_tp:
         # one sequence over all the GPUs first (its prompt is the same on every rank), then the replicas
         vocab = qdec.tp_plan(path, 0, 1)["v_rows"]
-        tp_res = tp_spec_timing(path, args, world, rank, local, k, spec_prompt(vocab, SPEC_SEED + 1), max_pos)
+        try:
+            tp_res = tp_spec_timing(path, args, world, rank, local, k, spec_prompt(vocab, SPEC_SEED + 1), max_pos)
+        except qdec.QdecError as e:  # e.g. a model whose heads do not split over this many GPUs: report, go on
+            tp_res = {"error": str(e)[:300], "_s_round": None, "_bytes": None}
+            import torch.distributed as dist
+
+            dist.barrier()
     model = qdec.Model(path, device=local, max_pos=max_pos)
     info = model.info
     prompt = spec_prompt(info.vocab, SPEC_SEED + 1 + rank)
@@ -664,7 +670,8 @@ def run_spec_qdec(args, world, rank, local):
     }
     if tp_res is not None:
         s_r, b = tp_res.pop("_s_round"), tp_res.pop("_bytes")
-        tp_res["round_frac_per_rank"] = round(b / s_r / 1e9 / peak, 4)
+        if s_r:
+            tp_res["round_frac_per_rank"] = round(b / s_r / 1e9 / peak, 4)
         line["tp"] = tp_res
     if world == 1 and not args.no_cpu_baseline:
         tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 1)
