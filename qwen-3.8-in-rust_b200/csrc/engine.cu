@@ -441,6 +441,8 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
     kk_ = (float*)dalloc(T * kvd * 4);
     vv_ = (float*)dalloc(T * kvd * 4);
     qr_ = (float*)dalloc(T * qd * 4);
+    // attention scores of every row and query head over the longest cache (the MTP cache's)
+    att_scores_ = (float*)dalloc(T * c.n_head * (((size_t)std::max(max_pos, mtp_cap_) + 3) & ~(size_t)3) * 4);
     gate_ = (float*)dalloc(T * qd * 4);
     attn_ = (float*)dalloc(T * qd * 4);
     // the persistent per-layer state covers this rank's heads (all of them on one GPU)
@@ -701,7 +703,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         count_launch(); ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
         AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, P.nq, P.nkv, hd,
                     kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
-                    m_.attn_scaling};
+                    m_.attn_scaling, att_scores_};
         count_launch(); ck(launch_attention(aa, t, stream), "attention");
         const float* attn_full = attn_;
         if (tp()) {

@@ -169,7 +169,7 @@ class State {
     uint8_t *q8k_ = nullptr, *q80_ = nullptr;
     float *qkv_ = nullptr, *conved_ = nullptr, *z_ = nullptr, *alpha_ = nullptr, *beta_ = nullptr, *heads_ = nullptr;
     float *qg_ = nullptr, *kk_ = nullptr, *vv_ = nullptr, *qr_ = nullptr, *gate_ = nullptr, *attn_ = nullptr;
-    float *g_ = nullptr, *u_ = nullptr, *final_ = nullptr, *logits_ = nullptr;
+    float *g_ = nullptr, *u_ = nullptr, *final_ = nullptr, *logits_ = nullptr, *att_scores_ = nullptr;
     float *cat_ = nullptr, *mtp_h_ = nullptr, *mtp_hout_ = nullptr;
     size_t q8k_stride_ = 0, q80_stride_ = 0;  // bytes per row of the activation buffers
     // tensor-parallel exchange (world > 1): one device allocation, exported over CUDA IPC, holding two line

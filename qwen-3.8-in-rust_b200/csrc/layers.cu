@@ -799,6 +799,184 @@ __global__ void attention_kernel(const AttnArgs a) {
     }
 }
 
+// Long-context attention in two kernels, the same arithmetic in the same order as attention_kernel.
+// Scores: a CTA takes up to 8 (query head, row) pairs that read the same kv head (pair p = query head
+// kvh * group + p % group of row p / group) and strides over 256-position chunks of the cache; each warp stages the
+// keys of 32 positions 32 dims at a time in shared memory (coalesced loads; rows padded to 36 floats so the
+// 16-byte reads of 8 lanes hit 32 distinct banks) and lane l continues the left-to-right dots of position l for
+// all the pairs -- every score is the reference's sequential sum, and a key is read once per 8 pairs.
+constexpr int ATT_KCH = 32;      // dims staged per pass
+constexpr int ATT_SGRID = 32;    // CTAs per (kv head, pair group) over the positions
+constexpr int ATT_PAIRS = 8;     // (query head, row) pairs per CTA
+
+__global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a, int rows) {
+    __shared__ __align__(16) float kt[8][32][ATT_KCH + 4];
+    __shared__ __align__(16) float qs[ATT_PAIRS][256];
+    const int hd = a.head_dim, group = a.n_head / a.n_kv, npairs = group * rows;
+    const int kvh = blockIdx.y, pg = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = *a.pos;
+    const int np = min(ATT_PAIRS, npairs - pg * ATT_PAIRS);
+    int hh[ATT_PAIRS], ii[ATT_PAIRS];
+#pragma unroll
+    for (int j = 0; j < ATT_PAIRS; j++) {
+        const int pi = pg * ATT_PAIRS + min(j, np - 1);
+        hh[j] = kvh * group + pi % group;
+        ii[j] = pi / group;
+    }
+    for (int e = threadIdx.x; e < np * hd; e += blockDim.x) {
+        const int j = e / hd, d = e % hd;
+        const int pi = pg * ATT_PAIRS + j, h = kvh * group + pi % group, i = pi / group;
+        qs[j][d] = a.q[(size_t)i * a.n_head * hd + (size_t)h * hd + d];
+    }
+    __syncthreads();
+    const int len = pos + ii[np - 1] + 1;  // the longest row of the group (rows ascend with the pair index)
+    const size_t rstride = (size_t)a.n_kv * hd;
+    for (int c = blockIdx.x; c * 256 < len; c += gridDim.x) {
+        const int p0 = c * 256 + warp * 32;
+        if (p0 >= len) continue;  // warp-uniform
+        float acc[ATT_PAIRS];
+#pragma unroll
+        for (int j = 0; j < ATT_PAIRS; j++) acc[j] = 0.0f;
+        for (int d0 = 0; d0 < hd; d0 += ATT_KCH) {
+            // 32 positions x 32 dims: lane l loads 16-byte piece (l % 8) of positions l / 8 + 4j
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int pp = lane / 8 + 4 * j, t = p0 + pp;
+                if (t < len) {
+                    const float4 v = *reinterpret_cast<const float4*>(a.k_cache + (size_t)t * rstride + (size_t)kvh * hd + d0 + (lane % 8) * 4);
+                    *reinterpret_cast<float4*>(&kt[warp][pp][(lane % 8) * 4]) = v;
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int d = 0; d < ATT_KCH; d += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(&kt[warp][lane][d]);
+#pragma unroll
+                for (int j = 0; j < ATT_PAIRS; j++) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(&qs[j][d0 + d]);
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(q4.x, k4.x));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(q4.y, k4.y));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(q4.z, k4.z));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(q4.w, k4.w));
+                }
+            }
+            __syncwarp();
+        }
+        const int t = p0 + lane;
+#pragma unroll
+        for (int j = 0; j < ATT_PAIRS; j++)
+            if (j < np && t < pos + ii[j] + 1)
+                a.scores[((size_t)ii[j] * a.n_head + hh[j]) * ((a.max_len + 3) & ~3) + t] = __fmul_rn(acc[j], a.scaling);
+    }
+}
+
+// Softmax of each (head, row) score row in place (softmax.rs:22-50): m = max, e = exp(x - m), the 8-lane sum
+// (lane l adds e[l], e[l+8], ... left to right; reduce8; the tail), p = e / sum.  One CTA of 256 per row.
+__global__ void __launch_bounds__(256) attn_softmax_kernel(const AttnArgs a) {
+    __shared__ float red[16];
+    const int h = blockIdx.x, i = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    const int len = *a.pos + i + 1;
+    float* p = a.scores + ((size_t)i * a.n_head + h) * ((a.max_len + 3) & ~3);
+    float m = -INFINITY;
+    for (int t = tid; t < len; t += 256) m = fmaxf(m, p[t]);
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int w = 1; w < 8; w++) mm = fmaxf(mm, red[w]);
+        red[15] = mm;
+    }
+    __syncthreads();
+    m = red[15];
+    for (int t = tid; t < len; t += 256) p[t] = exp_f32(__fsub_rn(p[t], m));
+    __syncthreads();  // global writes of this CTA are visible to its own threads after the barrier
+    const int n8 = len / 8 * 8;
+    if (tid < 8) {
+        float acc = 0.0f;
+        for (int t = tid; t < n8; t += 8) acc = __fadd_rn(acc, p[t]);
+        red[tid] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float sum = reduce8(red);
+        for (int t = n8; t < len; t++) sum = __fadd_rn(sum, p[t]);
+        red[8] = sum;
+    }
+    __syncthreads();
+    const float ssum = red[8];
+    for (int t = tid; t < len; t += 256) p[t] = __fdiv_rn(p[t], ssum);
+}
+
+// The value sum: one CTA per (32 output dims, kv head, group of 4 (query head, row) pairs reading that kv head),
+// warp j = pair j, lane = output dim: out[d] = sum_t p[t] * v_t[d] left to right over t, times sigmoid(gate)
+// (gqa_attention.rs:376-409).  The value rows (32 dims) and the pairs' probabilities stream through a 4-stage
+// ring of cp.async copies, 64 positions per stage, so a value row is read once for the 4 pairs.
+constexpr int ATT_VT = 64, ATT_VS = 4, ATT_VP = 4;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_stages() { asm volatile("cp.async.wait_group %0;" ::"n"(ATT_VS - 2) : "memory"); }
+
+__global__ void __launch_bounds__(32 * ATT_VP) attn_pv_kernel(const AttnArgs a, int rows) {
+    __shared__ __align__(16) float vs[ATT_VS][ATT_VT][32];
+    __shared__ __align__(16) float ps[ATT_VS][ATT_VP][ATT_VT];
+    const int dc = blockIdx.x, kvh = blockIdx.y, pg = blockIdx.z, hd = a.head_dim;
+    const int group = a.n_head / a.n_kv, npairs = group * rows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int np = min(ATT_VP, npairs - pg * ATT_VP);
+    const int pos = *a.pos;
+    const int sld = (a.max_len + 3) & ~3;
+    const int pw = pg * ATT_VP + min(warp, np - 1);  // this warp's pair
+    const int h = kvh * group + pw % group, i = pw / group;
+    const int len = pos + i + 1;
+    const int lenmax = pos + (pg * ATT_VP + np - 1) / group + 1;  // the group's longest row (rows ascend)
+    const size_t rstride = (size_t)a.n_kv * hd;
+    const float* vbase = a.v_cache + (size_t)kvh * hd + dc * 32;
+    const int ntiles = (lenmax + ATT_VT - 1) / ATT_VT;
+    auto issue = [&](int k) {
+        const int st = k % ATT_VS;
+        for (int e = tid; e < ATT_VT * 8; e += 32 * ATT_VP) {  // 64 positions x 8 pieces of 16 bytes
+            const int tt = e / 8, cc = e % 8, t = k * ATT_VT + tt;
+            if (t < lenmax) cp_async16(&vs[st][tt][cc * 4], vbase + (size_t)t * rstride + cc * 4);
+        }
+        for (int e = tid; e < np * (ATT_VT / 4); e += 32 * ATT_VP) {  // the pairs' probabilities, 16 per row
+            const int j = e / (ATT_VT / 4), cc = e % (ATT_VT / 4), t = k * ATT_VT + cc * 4;
+            const int pj = pg * ATT_VP + j, hj = kvh * group + pj % group, ij = pj / group;
+            if (t < pos + ij + 1) cp_async16(&ps[st][j][cc * 4], a.scores + ((size_t)ij * a.n_head + hj) * sld + t);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < ATT_VS - 1; s++) {
+        if (s < ntiles) issue(s);
+        cp_async_commit();
+    }
+    float o = 0.0f;
+    for (int k = 0; k < ntiles; k++) {
+        cp_async_wait_stages();
+        __syncthreads();  // tile k landed for every thread; every thread is done with tile k - 1
+        if (k + ATT_VS - 1 < ntiles) issue(k + ATT_VS - 1);
+        cp_async_commit();
+        const int st = k % ATT_VS;
+        const int tn = min(ATT_VT, len - k * ATT_VT);  // warp-uniform: the pair's own length
+        if (tn == ATT_VT) {
+#pragma unroll
+            for (int tt = 0; tt < ATT_VT; tt++) o = __fadd_rn(o, __fmul_rn(ps[st][warp][tt], vs[st][tt][lane]));
+        } else {
+            for (int tt = 0; tt < tn; tt++) o = __fadd_rn(o, __fmul_rn(ps[st][warp][tt], vs[st][tt][lane]));
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (warp < np) {
+        const int d = dc * 32 + lane;
+        const float g = a.gate[(size_t)i * a.n_head * hd + (size_t)h * hd + d];
+        a.out[(size_t)i * a.n_head * hd + (size_t)h * hd + d] = __fmul_rn(o, sigmoid_f32(g));
+    }
+}
+
 // out[row] = the first index of the maximum (model.rs:505-513: best = x[0], then a strict > scan; NaN is never
 // taken, and a NaN x[0] is kept).  Grid (chunks, rows): each CTA reduces ARGMAX_CHUNK values to its first
 // maximum (ties -> smaller index; NaN skipped), writes it, and the last CTA of the row to finish combines the
@@ -995,6 +1173,18 @@ cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
 }
 
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
+    if (a.scores && a.head_dim % 64 == 0 && a.head_dim <= 256) {
+        const int group = a.n_head / a.n_kv, npairs = group * t;
+        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + ATT_PAIRS - 1) / ATT_PAIRS);
+        attn_scores_kernel<<<sgrid, 256, 0, s>>>(a, t);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        attn_softmax_kernel<<<dim3(a.n_head, t), 256, 0, s>>>(a);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        attn_pv_kernel<<<dim3(a.head_dim / 32, a.n_kv, (npairs + ATT_VP - 1) / ATT_VP), 32 * ATT_VP, 0, s>>>(a, t);
+        return cudaGetLastError();
+    }
     const dim3 grid(a.n_head, t);
     const size_t smem = (size_t)(a.head_dim + a.max_len + 16) * sizeof(float);
     static size_t cap = 48 * 1024;  // raised only when a longer cache needs it (before any graph capture)

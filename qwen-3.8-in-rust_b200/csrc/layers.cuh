@@ -49,6 +49,7 @@ struct AttnArgs {
     float* out;               // [t][n_head * hd]
     int n_head, n_kv, head_dim, max_len;
     float scaling;
+    float* scores;            // scratch [t][n_head][max_len rounded up to 4] (null: the single-kernel path)
 };
 
 cudaError_t launch_resid_norm_quant(const float* a, const float* b, float* h_out, const float* w, float eps, int n, int rows,
