@@ -648,7 +648,7 @@ def run_spec_qdec(args, world, rank, local):
         "unit": "tok/s", "n_gpus": world, "steps": rounds, "warmup": args.warmup, "ms_per_step": round(ms / rounds, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "Q4_K_M weights x Q8_K activations, f32",
         "data": "synthetic (seeded N(0,0.02) weights in the Q4_K_M recipe; seeded uniform prompt ids)",
-        "config": {"workload": f"{preset} --spec 3 (BASELINE config 4)", "prompt": PROMPT_LEN, "k": k,
+        "config": {"workload": f"{preset} --spec 3 (BASELINE config {4 if PROMPT_LEN <= 1024 else 5})", "prompt": PROMPT_LEN, "k": k,
                    "global_batch": world, "parallelism": f"replicas x{world}",
                    "l2": f"weights {info.weight_bytes / 1e9:.1f} GB >> 126 MB L2"},
         "spec": {"s_per_round": round(s_round, 6), "accepted_per_round": (c1["accepted"] - c0["accepted"]) / rounds,
@@ -690,6 +690,8 @@ def main():
     ap.add_argument("--preset", default="27b", help="synthetic checkpoint of the spec workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="with --gpus > 1: replicas only (no tensor-parallel run)")
+    ap.add_argument("--prompt-len", type=int, default=None,
+                    help="prompt ids before the timed rounds (default 128; 8064 grows the KV cache to ~8192: config 5)")
     ap.add_argument("--profile-gemv", action="store_true",
                     help="run the dominant GEMV (Q4_K 17408x5120 N=4, tile layout) 4 times and exit: the ncu capture target")
     args = ap.parse_args()
@@ -699,6 +701,9 @@ def main():
         torch.cuda.set_device(0)
         dominant_gemv_timing(torch.device("cuda", 0), launches=4)
         return
+    if args.prompt_len:
+        global PROMPT_LEN
+        PROMPT_LEN = args.prompt_len
     if args.steps is None:
         args.steps = 2000 if args.workload == "gemv" else 50
     if args.warmup is None:
