@@ -145,3 +145,27 @@ def test_forced_drafts_every_acceptance_count(model, omodel):
     assert all(h > 0 for h in hist), hist
     want, stats, _ = omodel.state(512).spec_generate(p, len(seq), k, stop=False, forced=forced)
     assert want[: len(seq)] == seq
+
+
+def test_long_context_ids_and_logits_match_oracle(tiny, omodel):
+    """A 700-token prompt: the attention runs over several 256-position score chunks and wraps the value
+    stream's stage ring; greedy ids, the last prompt row's logits and --spec 3 ids match the oracle."""
+    import qdec
+
+    m = qdec.Model(tiny, max_pos=1024)
+    p = [int(v) for v in np.random.default_rng(SEED + 7).integers(0, 4096, 700)]
+    want = omodel.state(1024).generate(p, 12, stop=False)
+    st = m.new_state(max_rows=32)
+    got = qdec.generate(st, p, 12, stop=False)
+    assert got == want
+    os_ = omodel.state(1024)
+    lg = None
+    for tok in p[:300]:
+        lg, _ = os_.forward_token(tok)
+    s1 = m.new_state(max_rows=32)
+    s1.prefill(p[:299])
+    _, glg = s1.step(p[299], want_logits=True)
+    assert np.array_equal(glg.view(np.uint32), lg.view(np.uint32))
+    sp = m.new_state(spec_k=3, max_rows=32)
+    assert qdec.generate_spec(sp, p, 12, stop=False) == want
+    m.close()
