@@ -93,9 +93,10 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
 
 /* Tuning knob of the GEMV (process-wide): the K-quant kernel (0 = automatic; 2 = the kernel that reads
  * block_q8_K activations in the reference layout; 6 = the kernel that reads the library's activation image) and
- * the image kernel's configuration (0 = automatic, 1..21: lanes and rows per thread, tiles per warp, warps per
- * tile, super-blocks in flight, integer or FP32 scale multiply); or, with impl = 8, the Q8_0 / Q4_0 tile kernel
- * (config 0 = automatic, 1 = one warp per tile, 2 = the group range split over 4 warps).  Results do not depend on it; it exists for tests and sweeps.
+ * the image kernel's configuration (0 = automatic, 1..35: lanes and rows per thread, tiles per warp, warps per
+ * tile, super-blocks in flight, integer or FP32 scale multiply, activation prefetch / residency); or, with
+ * impl = 8, the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
+ * over 4 warps, 3 = the same with two tiles per CTA).  Results do not depend on it; it exists for tests and sweeps.
  * No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
 

@@ -226,8 +226,9 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
 }
 
 int qdec_tune_gemv(int impl, int config) {
-    if (impl == 8) {  // the Q8_0 / Q4_0 tile kernel: 0 automatic, 1 one warp per tile, 2 split group range
-        if (config < 0 || config > 2) return fail(QDEC_EINVAL, "Q8_0 gemv configuration must be 0, 1 or 2");
+    if (impl == 8) {  // the Q8_0 / Q4_0 tile kernel: 0 automatic, 1 one warp per tile, 2 split group range,
+                      // 3 split group range with two tiles per CTA
+        if (config < 0 || config > 3) return fail(QDEC_EINVAL, "Q8_0 gemv configuration must be 0..3");
         set_q80_split(config - 1);
         return QDEC_OK;
     }

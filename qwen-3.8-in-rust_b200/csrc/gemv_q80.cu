@@ -130,87 +130,110 @@ q80_tile_kernel(const uint8_t* __restrict__ w, int rows, int groups, const uint8
     if (active && tg < NC) y[(size_t)tg * rows + tile * 8 + rs] = acc;
 }
 
-// Split group range: one CTA of S warps per tile; warp w computes groups w, w+S, ... and writes their block
-// terms to shared memory; after each window of S groups, threads tg = n of warp 0 add the window's terms in
-// block order (the reference's chain).  S times the warps stream each tile, which 5120-row matrices need.
-template <int TYPE, int NC, int S>
+// Split group range: one CTA of S warps per R tiles; warp w computes groups w, w+S, ... of every tile and writes
+// their block terms to shared memory; after each window of S groups, the chain owners (thread (tile j, row rs,
+// column tg < NC) of the first R warps) add the window's terms in block order (the reference's chain).  S times
+// the warps stream each tile, which 5120-row matrices need; with R = 2 one load of a column's activation words
+// serves both tiles.
+template <int TYPE, int NC, int S, int R = 1>
 __global__ void __launch_bounds__(32 * S)
 q80_split_kernel(const uint8_t* __restrict__ w, int rows, int groups, const uint8_t* __restrict__ img, float* __restrict__ y) {
     constexpr int TB = Q80Tile<TYPE>::TB;
-    __shared__ __align__(16) float terms[2][S][8][NC][8];
+    static_assert(R <= S, "chain owners: one warp per tile");
+    __shared__ __align__(16) float terms[2][S][R][8][NC][8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rs = lane >> 2, tg = lane & 3;
-    const int tile = blockIdx.x;
-    const uint8_t* wt = w + (size_t)tile * groups * TB;
+    const int tiles = rows / 8;
+    const uint8_t* wt[R];
+#pragma unroll
+    for (int j = 0; j < R; j++) wt[j] = w + (size_t)min((int)blockIdx.x * R + j, tiles - 1) * groups * TB;
     const int nb = groups * 8;
-    QFrag<TYPE> nxt;
-    if (warp < groups) load_qfrag<TYPE>(wt + (size_t)warp * TB, lane, rs, tg, nxt);
+    QFrag<TYPE> nxt[R];
+    if (warp < groups) {
+#pragma unroll
+        for (int j = 0; j < R; j++) load_qfrag<TYPE>(wt[j] + (size_t)warp * TB, lane, rs, tg, nxt[j]);
+    }
 
     griddep_wait();  // the activation image is the previous kernel's output
     griddep_launch();
 
-    float acc = 0.0f;  // warp 0: column tg of row rs (tg < NC)
+    float acc = 0.0f;  // warp j < R: column tg of row rs of tile j (tg < NC)
     const int nwin = (groups + S - 1) / S;
     for (int win = 0; win < nwin; win++) {
         const int g = win * S + warp;
         if (g < groups) {
-            const QFrag<TYPE> f = nxt;
-            if (g + S < groups) load_qfrag<TYPE>(wt + (size_t)(g + S) * TB, lane, rs, tg, nxt);
-            const float dw0 = f16_bits_to_f32((uint16_t)(f.sc & 0xffff)), dw1 = f16_bits_to_f32((uint16_t)(f.sc >> 16));
+            QFrag<TYPE> f[R];
+            float dw0[R], dw1[R];
+#pragma unroll
+            for (int j = 0; j < R; j++) {
+                f[j] = nxt[j];
+                if (g + S < groups) load_qfrag<TYPE>(wt[j] + (size_t)(g + S) * TB, lane, rs, tg, nxt[j]);
+                dw0[j] = f16_bits_to_f32((uint16_t)(f[j].sc & 0xffff));
+                dw1[j] = f16_bits_to_f32((uint16_t)(f[j].sc >> 16));
+            }
             const int blk = g * 8 + 2 * tg;
 #pragma unroll
             for (int n = 0; n < NC; n++) {
                 const uint8_t* xr = img + (size_t)n * nb * Q80_IMG_BYTES;
                 const uint4* xc = reinterpret_cast<const uint4*>(xr + (size_t)blk * 32);
                 const uint4 meta = __ldg(reinterpret_cast<const uint4*>(xr + (size_t)nb * 32 + (size_t)blk * 8));
-                float t2[2];
+                uint32_t xw[2][8];
 #pragma unroll
                 for (int k = 0; k < 2; k++) {
                     const uint4 xa = __ldg(xc + 2 * k), xb = __ldg(xc + 2 * k + 1);
-                    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                    int sacc;
-                    if constexpr (TYPE == T_Q8_0) {
-                        const uint4 wa = f.c[2 * k], wb = f.c[2 * k + 1];
-                        const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-                        sacc = MAGIC_I;
-#pragma unroll
-                        for (int i = 0; i < 8; i++) sacc = __dp4a((int)ww[i], (int)xw[i], sacc);
-                    } else {  // q - 8 per nibble: sum q x - 8 sum x (dot.rs:46-63)
-                        const uint4 wa = f.c[k];
-                        const uint32_t ww[4] = {wa.x, wa.y, wa.z, wa.w};
-                        sacc = MAGIC_I - 8 * (int)(k ? meta.w : meta.y);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            sacc = __dp4a((int)(ww[i] & 0x0F0F0F0Fu), (int)xw[i], sacc);
-                            sacc = __dp4a((int)((ww[i] >> 4) & 0x0F0F0F0Fu), (int)xw[4 + i], sacc);
-                        }
-                    }
-                    const float dx = __uint_as_float(k ? meta.z : meta.x);
-                    t2[k] = __fmul_rn(__fmul_rn(k ? dw1 : dw0, dx), __fsub_rn(__int_as_float(sacc), MAGIC_F));
+                    xw[k][0] = xa.x, xw[k][1] = xa.y, xw[k][2] = xa.z, xw[k][3] = xa.w;
+                    xw[k][4] = xb.x, xw[k][5] = xb.y, xw[k][6] = xb.z, xw[k][7] = xb.w;
                 }
-                *reinterpret_cast<float2*>(&terms[win & 1][warp][rs][n][2 * tg]) = make_float2(t2[0], t2[1]);
+#pragma unroll
+                for (int j = 0; j < R; j++) {
+                    float t2[2];
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        int sacc;
+                        if constexpr (TYPE == T_Q8_0) {
+                            const uint4 wa = f[j].c[2 * k], wb = f[j].c[2 * k + 1];
+                            const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                            sacc = MAGIC_I;
+#pragma unroll
+                            for (int i = 0; i < 8; i++) sacc = __dp4a((int)ww[i], (int)xw[k][i], sacc);
+                        } else {  // q - 8 per nibble: sum q x - 8 sum x (dot.rs:46-63)
+                            const uint4 wa = f[j].c[k];
+                            const uint32_t ww[4] = {wa.x, wa.y, wa.z, wa.w};
+                            sacc = MAGIC_I - 8 * (int)(k ? meta.w : meta.y);
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                sacc = __dp4a((int)(ww[i] & 0x0F0F0F0Fu), (int)xw[k][i], sacc);
+                                sacc = __dp4a((int)((ww[i] >> 4) & 0x0F0F0F0Fu), (int)xw[k][4 + i], sacc);
+                            }
+                        }
+                        const float dx = __uint_as_float(k ? meta.z : meta.x);
+                        t2[k] = __fmul_rn(__fmul_rn(k ? dw1[j] : dw0[j], dx), __fsub_rn(__int_as_float(sacc), MAGIC_F));
+                    }
+                    *reinterpret_cast<float2*>(&terms[win & 1][warp][j][rs][n][2 * tg]) = make_float2(t2[0], t2[1]);
+                }
             }
         }
         __syncthreads();
-        if (warp == 0 && tg < NC) {
+        if (warp < R && tg < NC) {
             const int ng = min(S, groups - win * S);
 #pragma unroll
             for (int k = 0; k < S; k++)
                 if (k < ng) {
-                    const float4 a = *reinterpret_cast<const float4*>(&terms[win & 1][k][rs][tg][0]);
-                    const float4 b = *reinterpret_cast<const float4*>(&terms[win & 1][k][rs][tg][4]);
+                    const float4 a = *reinterpret_cast<const float4*>(&terms[win & 1][k][warp][rs][tg][0]);
+                    const float4 b = *reinterpret_cast<const float4*>(&terms[win & 1][k][warp][rs][tg][4]);
                     acc = __fadd_rn(acc, a.x), acc = __fadd_rn(acc, a.y), acc = __fadd_rn(acc, a.z), acc = __fadd_rn(acc, a.w);
                     acc = __fadd_rn(acc, b.x), acc = __fadd_rn(acc, b.y), acc = __fadd_rn(acc, b.z), acc = __fadd_rn(acc, b.w);
                 }
         }
     }
-    if (warp == 0 && tg < NC) y[(size_t)tg * rows + tile * 8 + rs] = acc;
+    const int tile = (int)blockIdx.x * R + warp;
+    if (warp < R && tg < NC && tile < tiles) y[(size_t)tg * rows + tile * 8 + rs] = acc;
 }
 
-template <int TYPE, int NC>
+template <int TYPE, int NC, int R = 1>
 cudaError_t launch_q80_split_nc(const uint8_t* w, int rows, int groups, const void* img, float* y, cudaStream_t s, bool pdl) {
     constexpr int S = 4;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows / 8);
+    cfg.gridDim = dim3((rows / 8 + R - 1) / R);
     cfg.blockDim = dim3(32 * S);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
@@ -219,7 +242,7 @@ cudaError_t launch_q80_split_nc(const uint8_t* w, int rows, int groups, const vo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, q80_split_kernel<TYPE, NC, S>, w, rows, groups, (const uint8_t*)img, y);
+    return cudaLaunchKernelEx(&cfg, q80_split_kernel<TYPE, NC, S, R>, w, rows, groups, (const uint8_t*)img, y);
 }
 
 template <int TYPE, int NC>
@@ -245,8 +268,18 @@ int g_q80_split = [] {
 template <int TYPE>
 cudaError_t launch_q80_tile_type(const uint8_t* w, int rows, int groups, const void* img, int ncols, float* y, cudaStream_t s,
                                  bool pdl) {
-    // split the group range over 4 warps unless the matrix alone gives every SM ~16 warps
+    // split the group range over 4 warps unless the matrix alone gives every SM ~16 warps; two tiles per CTA
+    // (one load of the activation words for both) for several columns on matrices with >= 4096 rows
     const bool split = g_q80_split >= 0 ? g_q80_split != 0 : rows / 8 < num_sms() * 16;
+    const bool two = g_q80_split >= 0 ? g_q80_split == 2 : (ncols > 1 && rows >= 4096);
+    if (split && two) {
+        switch (ncols) {
+        case 1: return launch_q80_split_nc<TYPE, 1, 2>(w, rows, groups, img, y, s, pdl);
+        case 2: return launch_q80_split_nc<TYPE, 2, 2>(w, rows, groups, img, y, s, pdl);
+        case 3: return launch_q80_split_nc<TYPE, 3, 2>(w, rows, groups, img, y, s, pdl);
+        default: return launch_q80_split_nc<TYPE, 4, 2>(w, rows, groups, img, y, s, pdl);
+        }
+    }
     if (split) {
         switch (ncols) {
         case 1: return launch_q80_split_nc<TYPE, 1>(w, rows, groups, img, y, s, pdl);

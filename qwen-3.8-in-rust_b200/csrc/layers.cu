@@ -807,8 +807,9 @@ __global__ void attention_kernel(const AttnArgs a) {
 // all the pairs -- every score is the reference's sequential sum, and a key is read once per 8 pairs.
 constexpr int ATT_KCH = 32;      // dims staged per pass
 constexpr int ATT_SGRID = 32;    // CTAs per (kv head, pair group) over the positions
-constexpr int ATT_PAIRS = 8;     // (query head, row) pairs per CTA
-
+// ATT_PAIRS: (query head, row) pairs per CTA -- 8 for long caches (a key is read once per 8 pairs), 2 for short
+// ones (4x the CTAs, so a short context still spreads over the SMs)
+template <int ATT_PAIRS>
 __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a, int rows) {
     __shared__ __align__(16) float kt[8][32][ATT_KCH + 4];
     __shared__ __align__(16) float qs[ATT_PAIRS][256];
@@ -1175,8 +1176,10 @@ cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
     if (a.scores && a.head_dim % 64 == 0 && a.head_dim <= 256) {
         const int group = a.n_head / a.n_kv, npairs = group * t;
-        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + ATT_PAIRS - 1) / ATT_PAIRS);
-        attn_scores_kernel<<<sgrid, 256, 0, s>>>(a, t);
+        const int pairs = a.max_len > 2048 ? 8 : 2;
+        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + pairs - 1) / pairs);
+        if (pairs == 8) attn_scores_kernel<8><<<sgrid, 256, 0, s>>>(a, t);
+        else attn_scores_kernel<2><<<sgrid, 256, 0, s>>>(a, t);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         attn_softmax_kernel<<<dim3(a.n_head, t), 256, 0, s>>>(a);

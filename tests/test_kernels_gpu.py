@@ -285,7 +285,7 @@ def test_tile_repack_rejects_ragged_rows(q):
         q.repack_tiles(12, src.data_ptr(), 12, 256, dst.data_ptr())
 
 
-@pytest.mark.parametrize("split", [1, 2])
+@pytest.mark.parametrize("split", [1, 2, 3])
 @pytest.mark.parametrize("t", [8, 2])
 def test_gemv_q80_tile_layout_bit_exact(q, orc, t, split):
     """Q8_0 / Q4_0 weights in the tile layout (8 rows x 8 blocks per tile block) against the Q8_0 activation
