@@ -208,6 +208,13 @@ int qdec_spec_round(qdec_state *s, uint32_t x_p, uint32_t *emitted_out, int *n_e
 /* Replace the drafts of the next round (k ids) -- the forced drafts of the identity tests
  * (Model::spec_set_drafts, crates/core/src/spec.rs:439); qdec_get_drafts reads the current ones. */
 int qdec_set_drafts(qdec_state *s, const uint32_t *drafts, int k);
+/* The state's sampler (SamplerConfig + Sampler::new / reseed, crates/core/src/sample.rs:58-170): temperature
+ * <= 0 is greedy (the default); otherwise every emitted token is drawn as the reference draws it -- candidates
+ * sorted by logit (ties: the lower id), the top_k of them (0: all), softmax at the temperature, top_p, min_p,
+ * renormalised, one xoshiro256** uniform per draw -- and --spec k accepts drafts by the exact speculative rule
+ * (accept_or_resample, sample.rs:279).  The RNG restarts from `seed`.  Set it before the first prefill of a
+ * sequence.  QDEC_EINVAL on a tensor-parallel state (its logits are split over the ranks). */
+int qdec_set_sampler(qdec_state *s, float temperature, int top_k, float top_p, float min_p, uint64_t seed);
 int qdec_get_drafts(const qdec_state *s, uint32_t *drafts_out, int k);
 /* The CUDA stream every kernel of this state runs on (to time it with events), and the number of kernels the
  * state has launched so far (for launch accounting); no counterpart in the reference (CPU-only). */

@@ -563,19 +563,26 @@ static int is_stop(OModel *m, uint32_t id) { return id == m->eos || id == m->sto
 
 /* The plain greedy loop (crates/cli/src/run.rs:329-350): prefill the prompt, then one token per step;
  * stops after a stop id when `stop` is set.  Returns the number of ids written. */
-int oracle_generate(OState *s, const uint32_t *prompt, int n, int n_out, int stop, uint32_t *out) {
+/* smp (optional): the sampler; greedy (argmax) without one or at temperature <= 0, else sample() on every
+ * token (run.rs:313-318, :348) */
+int oracle_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, int stop, OSampler *smp, uint32_t *out) {
     OModel *m = s->m;
     float *lg = (float *)malloc((size_t)m->vocab * 4);
+    const int greedy = !smp || oracle_sampler_greedy(smp);
     for (int i = 0; i < n; i++)
         if (oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, NULL)) { free(lg); return -1; }
     int c = 0;
-    out[c++] = oracle_argmax(lg, m->vocab);
+    out[c++] = greedy ? oracle_argmax(lg, m->vocab) : oracle_sampler_sample(smp, lg);
     while (c < n_out && !(stop && is_stop(m, out[c - 1]))) {
         if (oracle_forward_token(s, out[c - 1], lg, NULL, NULL)) break;
-        out[c++] = oracle_argmax(lg, m->vocab);
+        out[c++] = greedy ? oracle_argmax(lg, m->vocab) : oracle_sampler_sample(smp, lg);
     }
     free(lg);
     return c;
+}
+
+int oracle_generate(OState *s, const uint32_t *prompt, int n, int n_out, int stop, uint32_t *out) {
+    return oracle_generate_s(s, prompt, n, n_out, stop, NULL, out);
 }
 
 /* The --spec k loop (spec.rs:229-433, run.rs:353-383), greedy: spec_prefill, then rounds of verify
@@ -592,11 +599,39 @@ static double now_s(void) {
     return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
 }
 
+/* One draft from the MTP's post-norm row hout through the shared lm_head (spec.rs:190-203): greedy argmax, or
+ * process + draw with the processed distribution written densely to q_dense (the acceptance rule's q). */
+static uint32_t draft_token(OState *s, OSampler *smp, const float *hout, float *q_dense) {
+    OModel *m = s->m;
+    float *lg = (float *)malloc((size_t)m->vocab * 4);
+    matvec(&m->lm_head, hout, lg);
+    uint32_t d;
+    if (!smp || oracle_sampler_greedy(smp)) {
+        d = oracle_argmax(lg, m->vocab);
+    } else {
+        oracle_sampler_process(smp, lg, NULL, NULL);
+        d = oracle_sampler_draw(smp);
+        oracle_sampler_write_dense(smp, q_dense);
+    }
+    free(lg);
+    return d;
+}
+
+int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, int k, int stop, const uint32_t *forced,
+                           int n_forced, OSampler *smp, uint32_t *out, uint64_t *stats4, uint32_t *drafts_log);
+
 int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, int k, int stop, const uint32_t *forced,
                          int n_forced, uint32_t *out, uint64_t *stats4, uint32_t *drafts_log) {
+    return oracle_spec_generate_s(s, prompt, n, n_out, k, stop, forced, n_forced, NULL, out, stats4, drafts_log);
+}
+
+int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, int k, int stop, const uint32_t *forced,
+                           int n_forced, OSampler *smp, uint32_t *out, uint64_t *stats4, uint32_t *drafts_log) {
     OModel *m = s->m;
     const int H = m->hidden, t = k + 1;
     if (!m->has_mtp || k < 1 || k + 1 > MAXT) return -1;
+    const int greedy = !smp || oracle_sampler_greedy(smp);
+    float *q_dense = greedy ? NULL : (float *)malloc((size_t)m->vocab * 4 * k);
     float *lg = (float *)malloc((size_t)m->vocab * 4 * t);
     float *normed = (float *)malloc((size_t)H * 4 * (n > t ? n : t));
     float *hout = (float *)malloc((size_t)H * 4), *hprev = (float *)malloc((size_t)H * 4);
@@ -605,14 +640,18 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
     /* spec_prefill (spec.rs:229-285) */
     int p = s->pos;
     for (int i = 0; i < n; i++) oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, normed + (size_t)i * H);
-    uint32_t x_t = oracle_argmax(lg, m->vocab);
+    uint32_t x_t = greedy ? oracle_argmax(lg, m->vocab) : oracle_sampler_sample(smp, lg);
     s->mtp_len = p;
     for (int j = 0; j < n; j++) {
         uint32_t x = (j + 1 < n) ? prompt[j + 1] : x_t;
-        uint32_t d = mtp_row(s, x, normed + (size_t)j * H, hout, j == n - 1);
-        if (j == n - 1) drafts[0] = d;
+        mtp_row(s, x, normed + (size_t)j * H, hout, 0);
     }
-    for (int i = 1; i < k; i++) { memcpy(hprev, hout, (size_t)H * 4); drafts[i] = mtp_row(s, drafts[i - 1], hprev, hout, 1); }
+    drafts[0] = draft_token(s, smp, hout, q_dense);
+    for (int i = 1; i < k; i++) {
+        memcpy(hprev, hout, (size_t)H * 4);
+        mtp_row(s, drafts[i - 1], hprev, hout, 0);
+        drafts[i] = draft_token(s, smp, hout, q_dense ? q_dense + (size_t)i * m->vocab : NULL);
+    }
     out[c++] = x_t;
     uint32_t x_p = x_t;
     const double t_rounds = now_s();
@@ -627,13 +666,28 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
         for (int i = 0; i < k; i++) batch[i + 1] = drafts[i];
         for (int i = 0; i < t; i++) oracle_forward_token(s, batch[i], lg + (size_t)i * m->vocab, NULL, normed + (size_t)i * H);
         int mm = 0, ne = 0;
-        while (mm < k) {
-            uint32_t a = oracle_argmax(lg + (size_t)mm * m->vocab, m->vocab);
-            emitted[ne++] = a;
-            if (a != drafts[mm]) break;
-            mm++;
+        if (greedy) {
+            while (mm < k) {
+                uint32_t a = oracle_argmax(lg + (size_t)mm * m->vocab, m->vocab);
+                emitted[ne++] = a;
+                if (a != drafts[mm]) break;
+                mm++;
+            }
+            if (mm == k) emitted[ne++] = oracle_argmax(lg + (size_t)k * m->vocab, m->vocab);
+        } else {  /* spec.rs:367-379: accept_or_resample per position, then the bonus draw */
+            while (mm < k) {
+                uint32_t tok;
+                const int ok = oracle_sampler_accept(smp, lg + (size_t)mm * m->vocab, q_dense + (size_t)mm * m->vocab,
+                                                     drafts[mm], &tok);
+                emitted[ne++] = tok;
+                if (!ok) break;
+                mm++;
+            }
+            if (mm == k) {
+                oracle_sampler_process(smp, lg + (size_t)k * m->vocab, NULL, NULL);
+                emitted[ne++] = oracle_sampler_draw(smp);
+            }
         }
-        if (mm == k) emitted[ne++] = oracle_argmax(lg + (size_t)k * m->vocab, m->vocab);
         int keep = mm + 1;
         if (keep < t) {
             /* restore and replay the kept rows (the replay reruns their recurrence on the same inputs, so the
@@ -647,13 +701,12 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
         /* the MTP: truncate to p, re-feed the kept pairs (emitted_i, normed_i), draft, chain */
         s->mtp_len = p;
         for (int i = 0; i < keep; i++) mtp_row(s, emitted[i], normed + (size_t)i * H, hout, 0);
-        {
-            float *lg1 = (float *)malloc((size_t)m->vocab * 4);
-            matvec(&m->lm_head, hout, lg1);
-            drafts[0] = oracle_argmax(lg1, m->vocab);
-            free(lg1);
+        drafts[0] = draft_token(s, smp, hout, q_dense);
+        for (int i = 1; i < k; i++) {
+            memcpy(hprev, hout, (size_t)H * 4);
+            mtp_row(s, drafts[i - 1], hprev, hout, 0);
+            drafts[i] = draft_token(s, smp, hout, q_dense ? q_dense + (size_t)i * m->vocab : NULL);
         }
-        for (int i = 1; i < k; i++) { memcpy(hprev, hout, (size_t)H * 4); drafts[i] = mtp_row(s, drafts[i - 1], hprev, hout, 1); }
         for (int i = 0; i < keep && c < n_out; i++) {
             out[c++] = emitted[i];
             if (stop && is_stop(m, emitted[i])) break;
@@ -662,7 +715,7 @@ int oracle_spec_generate(OState *s, const uint32_t *prompt, int n, int n_out, in
         round++;
     }
     g_round_seconds = now_s() - t_rounds;
-    free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted);
+    free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted); free(q_dense);
     return c;
 }
 

@@ -85,6 +85,26 @@ void oracle_deltanet_step(const float *q, const float *k, const float *v, int dk
 uint32_t oracle_argmax(const float *v, int n);
 uint32_t oracle_crc32(const uint8_t *p, size_t n);
 
+/* the sampler (sample.c, crates/core/src/sample.rs) */
+typedef struct {
+    float temperature;  /* <= 0: greedy */
+    int top_k;          /* 0: off */
+    float top_p, min_p;
+    uint64_t seed;
+} OSamplerCfg;
+typedef struct oracle_sampler OSampler;
+void oracle_rng_seed(uint64_t s_out[4], uint64_t seed);
+uint64_t oracle_rng_next(uint64_t s[4]);
+float oracle_rng_f32(uint64_t s[4]);
+OSampler *oracle_sampler_new(const OSamplerCfg *cfg, int vocab);
+void oracle_sampler_free(OSampler *s);
+int oracle_sampler_greedy(const OSampler *s);
+int oracle_sampler_process(OSampler *s, const float *logits, uint32_t *ids_out, float *probs_out);
+uint32_t oracle_sampler_draw(OSampler *s);
+uint32_t oracle_sampler_sample(OSampler *s, const float *logits);
+int oracle_sampler_accept(OSampler *s, const float *target_logits, const float *q_dense, uint32_t d, uint32_t *tok_out);
+void oracle_sampler_write_dense(const OSampler *s, float *out);
+
 #ifdef __cplusplus
 }
 #endif

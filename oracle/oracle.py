@@ -74,6 +74,16 @@ def lib():
             "oracle_forward_token": (I, [P, ctypes.c_uint32, P, P, P]),
             "oracle_generate": (I, [P, U32P, I, I, I, U32P]),
             "oracle_spec_generate": (I, [P, U32P, I, I, I, I, U32P, I, U32P, ctypes.POINTER(ctypes.c_uint64), U32P]),
+            "oracle_generate_s": (I, [P, U32P, I, I, I, P, U32P]),
+            "oracle_spec_generate_s": (I, [P, U32P, I, I, I, I, U32P, I, P, U32P, ctypes.POINTER(ctypes.c_uint64), U32P]),
+            "oracle_sampler_new": (P, [ctypes.POINTER(SamplerCfg), I]),
+            "oracle_sampler_free": (None, [P]),
+            "oracle_sampler_process": (I, [P, P, U32P, P]),
+            "oracle_sampler_draw": (ctypes.c_uint32, [P]),
+            "oracle_sampler_sample": (ctypes.c_uint32, [P, P]),
+            "oracle_sampler_accept": (I, [P, P, P, ctypes.c_uint32, U32P]),
+            "oracle_rng_seed": (None, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint64]),
+            "oracle_rng_next": (ctypes.c_uint64, [ctypes.POINTER(ctypes.c_uint64)]),
         })
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -85,6 +95,52 @@ def lib():
 
 def _p(a):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class SamplerCfg(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int), ("top_p", ctypes.c_float),
+                ("min_p", ctypes.c_float), ("seed", ctypes.c_uint64)]
+
+
+class OracleSampler:
+    """The reference's Sampler (crates/core/src/sample.rs) on the CPU: process / draw / sample / accept."""
+
+    def __init__(self, vocab, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, seed=0):
+        self.vocab = vocab
+        self.cfg = SamplerCfg(temperature, top_k, top_p, min_p, seed)
+        self._h = lib().oracle_sampler_new(ctypes.byref(self.cfg), vocab)
+
+    def __del__(self):
+        try:
+            lib().oracle_sampler_free(self._h)
+        except Exception:
+            pass
+
+    def process(self, logits):
+        lg = np.ascontiguousarray(logits, np.float32)
+        ids = (ctypes.c_uint32 * self.vocab)()
+        ps = np.empty(self.vocab, np.float32)
+        n = lib().oracle_sampler_process(self._h, _p(lg), ids, _p(ps))
+        return list(ids[:n]), ps[:n].copy()
+
+    def draw(self):
+        return lib().oracle_sampler_draw(self._h)
+
+    def sample(self, logits):
+        return lib().oracle_sampler_sample(self._h, _p(np.ascontiguousarray(logits, np.float32)))
+
+    def accept(self, target_logits, q_dense, d):
+        tok = ctypes.c_uint32()
+        ok = lib().oracle_sampler_accept(self._h, _p(np.ascontiguousarray(target_logits, np.float32)),
+                                         _p(np.ascontiguousarray(q_dense, np.float32)), d, ctypes.byref(tok))
+        return bool(ok), tok.value
+
+
+def rng_u64(seed, n):
+    """The first n outputs of the sampler's xoshiro256** seeded through splitmix64."""
+    st = (ctypes.c_uint64 * 4)()
+    lib().oracle_rng_seed(st, seed)
+    return [lib().oracle_rng_next(st) for _ in range(n)]
 
 
 def set_libm(mode):
@@ -324,15 +380,15 @@ class OracleState:
             raise ValueError("oracle: forward_token failed (id out of range or sequence full)")
         return lg, cap
 
-    def generate(self, prompt, n_out, stop=True):
+    def generate(self, prompt, n_out, stop=True, sampler=None):
         out = (ctypes.c_uint32 * n_out)()
         arr = (ctypes.c_uint32 * len(prompt))(*prompt)
-        c = lib().oracle_generate(self._h, arr, len(prompt), n_out, 1 if stop else 0, out)
+        c = lib().oracle_generate_s(self._h, arr, len(prompt), n_out, 1 if stop else 0, sampler._h if sampler else None, out)
         if c < 0:
             raise ValueError("oracle: generate failed")
         return list(out[:c])
 
-    def spec_generate(self, prompt, n_out, k, stop=True, forced=None):
+    def spec_generate(self, prompt, n_out, k, stop=True, forced=None, sampler=None):
         """Returns (ids, stats dict, drafts used per round)."""
         out = (ctypes.c_uint32 * n_out)()
         arr = (ctypes.c_uint32 * len(prompt))(*prompt)
@@ -344,7 +400,8 @@ class OracleState:
             n_forced = len(forced)
             fz = (ctypes.c_uint32 * len(flat))(*flat)
         log = (ctypes.c_uint32 * (k * (n_out + 2)))()
-        c = lib().oracle_spec_generate(self._h, arr, len(prompt), n_out, k, 1 if stop else 0, fz, n_forced, out, st, log)
+        c = lib().oracle_spec_generate_s(self._h, arr, len(prompt), n_out, k, 1 if stop else 0, fz, n_forced,
+                                         sampler._h if sampler else None, out, st, log)
         if c < 0:
             raise ValueError("oracle: spec_generate failed")
         stats = dict(zip(("rounds", "drafted", "accepted", "emitted"), list(st)))

@@ -113,6 +113,20 @@ int qdec_tp_plan_dims(const uint32_t dims[8], int tp_rank, int tp_world, int32_t
     });
 }
 
+int qdec_set_sampler(qdec_state* s, float temperature, int top_k, float top_p, float min_p, uint64_t seed) {
+    if (!s) return qdec::fail(QDEC_EINVAL, "qdec_set_sampler: null state");
+    return guard("qdec_set_sampler", [&] {
+        qdec::SamplerCfg c;
+        c.temperature = temperature;
+        c.top_k = top_k;
+        c.top_p = top_p;
+        c.min_p = min_p;
+        c.seed = seed;
+        s->s->set_sampler(c);
+        return QDEC_OK;
+    });
+}
+
 int qdec_tp_export(const qdec_state* s, void* handle_out) {
     if (!s || !handle_out) return qdec::fail(QDEC_EINVAL, "qdec_tp_export: null argument");
     return guard("qdec_tp_export", [&] {

@@ -29,6 +29,7 @@
 #include "kernels.cuh"
 #include "layers.cuh"
 #include "tp.cuh"
+#include "sample.cuh"
 
 namespace qdec {
 
@@ -842,6 +843,7 @@ uint32_t State::prefill(const uint32_t* ids, int n) {
         pos_ += t;
     }
     set_dev_int(d_pos, pos_, stream);
+    if (sampling()) sample_row(logits_, 0, d_argmax, nullptr);  // the prompt's last row (run.rs:313-318)
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
     sync();
@@ -856,6 +858,7 @@ uint32_t State::step(uint32_t id, float* logits) {
     set_dev_int(d_keep, 1, stream);
     pos_ += 1;
     set_dev_int(d_pos, pos_, stream);
+    if (sampling()) sample_row(logits_, 0, d_argmax, nullptr);  // run.rs:348
     int32_t a = 0;
     ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
     if (logits && tp()) throw std::invalid_argument("step: logits are split over the tensor-parallel ranks");
@@ -901,14 +904,55 @@ void State::mtp_rows(int t, const int32_t* ids_dev, const float* hidden, const i
 }
 
 // The draft of the MTP row held in mtp_h_: the shared lm_head, greedy (spec.rs:205-215, mtp.rs:132-137).
-void State::enqueue_draft(int32_t* out_dev) {
+void State::enqueue_draft(int i) {
     const ModelConfig& c = m_.cfg;
     const int H = (int)c.hidden_size;
     float* lg = logits_ + (size_t)(T_ - 1) * c.vocab_size;
     begin_session();
     quant_for(m_.lm_head.type, mtp_h_, H, 1);
     gemv(m_.lm_head, mtp_h_, 1, lg);
-    argmax_rows(lg, 1, out_dev);
+    if (sampling()) sample_row(lg, k_ + 1, d_vids + 1 + i, q_dense_ + (size_t)i * c.vocab_size);  // spec.rs:190-203
+    else argmax_rows(lg, 1, d_vids + 1 + i);
+}
+
+void State::sample_row(const float* logits, int slot, int32_t* out_dev, float* q) {
+    const int V = (int)m_.cfg.vocab_size;
+    int32_t* ids = kept_ids_ + (size_t)slot * V;
+    float* probs = kept_probs_ + (size_t)slot * V;
+    count_launch(4);
+    ck(launch_sample_process(logits, V, samp_, samp_scratch_, ids, probs, kept_n_ + slot, stream), "sampler");
+    ck(launch_sample_draw(d_rng_, ids, probs, kept_n_ + slot, out_dev, stream), "sampler draw");
+    if (q) {
+        count_launch();
+        ck(launch_sample_dense(ids, probs, kept_n_ + slot, V, q, stream), "sampler q");
+    }
+}
+
+void State::set_sampler(const SamplerCfg& cfg) {
+    if (cfg.temperature > 0.0f && tp()) throw std::invalid_argument("sampling: a tensor-parallel state's logits are split over its ranks");
+    if (cfg.top_k < 0) throw std::invalid_argument("sampling: top_k < 0");
+    ck(cudaStreamSynchronize(stream), "sync");
+    const int V = (int)m_.cfg.vocab_size;
+    if (cfg.temperature > 0.0f && !d_rng_) {
+        const size_t slots = (size_t)k_ + 2;
+        d_rng_ = (uint64_t*)dalloc(32);
+        samp_scratch_ = dalloc(sampler_sort_scratch_bytes(V));
+        kept_ids_ = (int32_t*)dalloc(slots * V * 4);
+        kept_probs_ = (float*)dalloc(slots * V * 4);
+        kept_n_ = (int*)dalloc(slots * 4);
+        q_dense_ = (float*)dalloc((size_t)std::max(k_, 1) * V * 4);
+        samp_work_ = (float*)dalloc((size_t)V * 4);
+    }
+    if (d_rng_) {
+        uint64_t st[4];
+        sampler_seed_state(cfg.seed, st);
+        ck(cudaMemcpy(d_rng_, st, sizeof st, cudaMemcpyHostToDevice), "sampler seed");
+    }
+    samp_ = cfg;
+    if (round_exec_) {  // the captured round holds the previous mode's kernels
+        cudaGraphExecDestroy(round_exec_);
+        round_exec_ = nullptr;
+    }
 }
 
 // Drafts from..k-1 by chaining single MTP rows (spec.rs:205-222): draft i comes from the MTP row of token
@@ -918,7 +962,7 @@ void State::enqueue_chain(int from) {
     for (int i = from; i < k_; i++) {
         mtp_rows(1, d_vids + i, mtp_h_, d_mpos + i);
         ck(cudaMemcpyAsync(mtp_h_, mtp_hout_, (size_t)H * 4, cudaMemcpyDeviceToDevice, stream), "hprev");
-        enqueue_draft(d_vids + 1 + i);
+        enqueue_draft(i);
     }
 }
 
@@ -944,6 +988,7 @@ uint32_t State::spec_prefill(const uint32_t* ids, int n) {
             pos_ += t;
             ck(cudaMemcpyAsync(normed_all + (size_t)off * H, final_, (size_t)t * H * 4, cudaMemcpyDeviceToDevice, stream), "rows");
         }
+        if (sampling()) sample_row(logits_, 0, d_argmax, nullptr);  // x_T (spec.rs:241)
         int32_t a = 0;
         ck(cudaMemcpyAsync(&a, d_argmax, 4, cudaMemcpyDeviceToHost, stream), "argmax");
         sync();
@@ -961,7 +1006,7 @@ uint32_t State::spec_prefill(const uint32_t* ids, int n) {
             sync();
         }
         // the first draft from the last prompt row, then the chain at p + n, p + n + 1, ...
-        enqueue_draft(d_vids + 1);
+        enqueue_draft(0);
         for (int i = 1; i < k_; i++) mp[i] = p + n + i - 1;
         ck(cudaMemcpyAsync(d_mpos, mp.data(), (size_t)T_ * 4, cudaMemcpyHostToDevice, stream), "mtp pos");
         enqueue_chain(1);
@@ -985,15 +1030,30 @@ void State::enqueue_round() {
     const uint64_t xseq0 = xseq_;
     ck(cudaMemcpyAsync(d_vids, h_io_, 4, cudaMemcpyHostToDevice, stream), "x_p");
     forward_rows(t, d_vids, true);  // the verify batch: x_p, d_1..d_k
-    count_launch();
-    spec_accept_kernel<<<1, 32, 0, stream>>>(d_argmax, d_vids, k_, d_pos, d_keep, d_mpos, d_mids, d_sel, d_emit);
-    ck(cudaGetLastError(), "accept");
+    if (sampling()) {
+        // the target's processed distribution of every verify row, then accept_or_resample in order (spec.rs:367-379)
+        const int V = (int)c.vocab_size;
+        for (int r = 0; r < t; r++) {
+            count_launch(3);
+            ck(launch_sample_process(logits_ + (size_t)r * V, V, samp_, samp_scratch_, kept_ids_ + (size_t)r * V,
+                                     kept_probs_ + (size_t)r * V, kept_n_ + r, stream),
+               "sampler");
+        }
+        SpecAcceptArgs sa{d_rng_, kept_ids_, kept_probs_, kept_n_, (size_t)V, q_dense_, V, d_vids, k_, d_pos, d_keep, d_mpos,
+                          d_mids, d_sel, d_emit, samp_work_};
+        count_launch();
+        ck(launch_spec_accept_sampled(sa, stream), "accept");
+    } else {
+        count_launch();
+        spec_accept_kernel<<<1, 32, 0, stream>>>(d_argmax, d_vids, k_, d_pos, d_keep, d_mpos, d_mids, d_sel, d_emit);
+        ck(cudaGetLastError(), "accept");
+    }
     // the MTP re-feed: all t rows (rows past keep are scratch; their cache slots are rewritten before any read)
     mtp_rows(t, d_mids, final_, d_mpos);
     count_launch();
     select_row_kernel<<<8, 256, 0, stream>>>(mtp_hout_, d_sel, H, mtp_h_);
     ck(cudaGetLastError(), "select row");
-    enqueue_draft(d_vids + 1);
+    enqueue_draft(0);
     enqueue_chain(1);
     if (tp() && ((xseq_ - xseq0) & 1)) {
         // an even number of exchanges per round keeps consecutive exchanges on alternate line buffers from one

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "config.h"
+#include "sample.cuh"
 
 namespace qdec {
 
@@ -119,6 +120,9 @@ class State {
     int spec_round(uint32_t x_p, uint32_t* out);
     // forced drafts for the next round (spec.rs:439-452, used by the identity tests)
     void set_drafts(const uint32_t* d, int k);
+    // the sampler of this state (crates/core/src/sample.rs): temperature <= 0 is greedy; the RNG restarts from
+    // cfg.seed.  One GPU only (a tensor-parallel state's logits are split over its ranks).
+    void set_sampler(const SamplerCfg& cfg);
     std::vector<uint32_t> drafts() const;
 
     // tensor parallelism: the exchange block (receive buffers + flags) is exported with a CUDA IPC handle; every
@@ -212,8 +216,20 @@ class State {
     void forward_rows(int t, const int32_t* ids_dev, bool want_logits_all);
     // the MTP block over t rows (tokens ids_dev, hidden rows, MTP position of row 0 at *pos_dev) into mtp_hout_
     void mtp_rows(int t, const int32_t* ids_dev, const float* hidden_rows, const int* pos_dev);
-    // greedy draft from mtp_h_ (one row) through the shared lm_head into *out_dev
-    void enqueue_draft(int32_t* out_dev);
+    // draft i from mtp_h_ (one row) through the shared lm_head into d_vids[1 + i]: the argmax, or a sampled id
+    // with its processed distribution written densely to q_dense_[i]
+    void enqueue_draft(int i);
+    // the sampled id of one logits row into *out_dev (q: its processed distribution, dense, when non-null)
+    void sample_row(const float* logits, int slot, int32_t* out_dev, float* q);
+    bool sampling() const { return samp_.temperature > 0.0f; }
+    SamplerCfg samp_{};
+    uint64_t* d_rng_ = nullptr;
+    void* samp_scratch_ = nullptr;
+    int32_t* kept_ids_ = nullptr;  // [k + 2][vocab]: processed rows (verify rows 0..k, one for single draws)
+    float* kept_probs_ = nullptr;
+    int* kept_n_ = nullptr;
+    float* q_dense_ = nullptr;     // [k][vocab]: the drafts' distributions
+    float* samp_work_ = nullptr;   // [vocab]
     // drafts from..k-1, each an MTP row chained from the previous one (positions d_mpos[i])
     void enqueue_chain(int from);
     // the whole speculative round on the stream: verify, accept, rollback bookkeeping, MTP re-feed, drafts

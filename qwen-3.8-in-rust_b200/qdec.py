@@ -85,6 +85,7 @@ def lib():
             "qdec_tp_export": [P, P],
             "qdec_tp_connect": [P, P],
             "qdec_tp_stats": [P, ctypes.POINTER(ctypes.c_uint64)],
+            "qdec_set_sampler": [P, ctypes.c_float, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64],
             "qdec_close": [P],
             "qdec_model_get_info": [P, ctypes.POINTER(ModelInfo)],
             "qdec_is_stop": [P, ctypes.c_uint32],
@@ -353,6 +354,10 @@ class State:
         n = ctypes.c_int()
         _check(lib().qdec_spec_round(self._h, x_p, buf, ctypes.byref(n)))
         return list(buf[: n.value])
+
+    def set_sampler(self, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, seed=0):
+        """Sampler::new(SamplerConfig{..}) for this state (temperature <= 0: greedy); the RNG restarts at seed."""
+        _check(lib().qdec_set_sampler(self._h, temperature, top_k, top_p, min_p, seed))
 
     def set_drafts(self, drafts):
         _check(lib().qdec_set_drafts(self._h, _u32(drafts), len(drafts)))

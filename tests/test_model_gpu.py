@@ -169,3 +169,56 @@ def test_long_context_ids_and_logits_match_oracle(tiny, omodel):
     sp = m.new_state(spec_k=3, max_rows=32)
     assert qdec.generate_spec(sp, p, 12, stop=False) == want
     m.close()
+
+
+SAMPLERS = [dict(temperature=0.8, top_k=20, top_p=0.95, seed=3), dict(temperature=1.0, top_k=0, top_p=1.0, seed=11),
+            dict(temperature=0.6, top_k=50, top_p=0.9, min_p=0.05, seed=42)]
+
+
+@pytest.mark.parametrize("cfg", SAMPLERS)
+def test_sampled_ids_match_oracle(model, omodel, orc, cfg):
+    """Sampled decoding (crates/core/src/sample.rs, run.rs:313-348): the device's candidate sort, softmax, top-k /
+    top-p / min-p, xoshiro256** draws give the oracle's ids, plain and --spec 3 (exact acceptance rule)."""
+    import qdec
+
+    p = prompt16()
+    st = model.new_state(max_rows=32)
+    st.set_sampler(**cfg)
+    got = qdec.generate(st, p, N_TOKENS, stop=False)
+    want = omodel.state(512).generate(p, N_TOKENS, stop=False, sampler=orc.OracleSampler(4096, **cfg))
+    assert got == want
+    sp = model.new_state(spec_k=3, max_rows=32)
+    sp.set_sampler(**cfg)
+    got_s = qdec.generate_spec(sp, p, N_TOKENS, stop=False)
+    want_s, stats, _ = omodel.state(512).spec_generate(p, N_TOKENS, 3, stop=False, sampler=orc.OracleSampler(4096, **cfg))
+    assert got_s == want_s
+    c = sp.counters()
+    assert c["rounds"] == stats["rounds"] and c["accepted"] == stats["accepted"]
+
+
+def test_sampler_switch_to_greedy_mid_sequence(model):
+    """temperature 0 after sampled rounds: the captured round is rebuilt greedy, and the continuation equals
+    plain greedy decoding from the same history."""
+    import qdec
+
+    p = prompt16()
+    a = model.new_state(spec_k=3, max_rows=32)
+    a.set_sampler(temperature=0.9, top_k=10, seed=1)
+    x = a.spec_prefill(p)  # x_T, then sampled rounds (the first captures the sampled round)
+    hist = [x]
+    for _ in range(4):
+        em = a.spec_round(x)
+        hist += em
+        x = em[-1]
+    a.set_sampler(temperature=0.0)
+    x = hist[-1]
+    cont = []
+    while len(cont) < 12:
+        em = a.spec_round(x)
+        cont += em
+        x = em[-1]
+    b2 = model.new_state(max_rows=32)  # prefill the same history, then greedy steps
+    plain = [b2.prefill(p + hist)]
+    while len(plain) < 12:
+        plain.append(b2.step(plain[-1]))
+    assert cont[:12] == plain

@@ -292,3 +292,72 @@ def test_deltanet_step_within_budget(orc):
 def test_argmax_first_on_ties(orc):
     v = np.array([1.0, 3.0, 2.0, 3.0], np.float32)
     assert orc.argmax(v) == 1
+
+
+# --------------------------------------------------------------------- the sampler (crates/core/src/sample.rs)
+
+def _xoshiro_py(seed, n):
+    """splitmix64 seeding + xoshiro256** (Blackman & Vigna), restated independently in Python."""
+    M = (1 << 64) - 1
+    x, s = seed, []
+    for _ in range(4):
+        x = (x + 0x9E3779B97F4A7C15) & M
+        z = x
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        s.append(z ^ (z >> 31))
+    rotl = lambda v, k: ((v << k) | (v >> (64 - k))) & M
+    out = []
+    for _ in range(n):
+        out.append((rotl((s[1] * 5) & M, 7) * 9) & M)
+        t = (s[1] << 17) & M
+        s[2] ^= s[0]; s[3] ^= s[1]; s[1] ^= s[2]; s[0] ^= s[3]; s[2] ^= t
+        s[3] = rotl(s[3], 45)
+    return out
+
+
+def test_sampler_rng_is_xoshiro256starstar_seeded_by_splitmix64(orc):
+    for seed in (0, 1, 42, 2**63 + 5):
+        assert orc.rng_u64(seed, 64) == _xoshiro_py(seed, 64)
+
+
+def test_sampler_keeps_the_reference_sets(orc):
+    """sample.rs:492-517: top-k, top-p (the crossing token stays), min-p and greedy on six logits."""
+    logits = np.array([1.0, 2.0, 3.0, 0.0, -1.0, 4.0], np.float32)
+    ids, ps = orc.OracleSampler(6, 1.0, top_k=3, seed=1).process(logits)
+    assert ids == [5, 2, 1] and abs(float(ps.sum()) - 1.0) < 1e-6
+    assert orc.OracleSampler(6, 1.0, top_p=0.5, seed=1).process(logits)[0] == [5]
+    assert orc.OracleSampler(6, 1.0, top_p=0.9, seed=1).process(logits)[0] == [5, 2, 1]
+    assert orc.OracleSampler(6, 1.0, top_p=0.85, seed=1).process(logits)[0] == [5, 2]
+    assert orc.OracleSampler(6, 1.0, min_p=0.2, seed=1).process(logits)[0] == [5, 2]
+    g = orc.OracleSampler(6, 0.0)
+    assert g.process(logits)[0] == [5] and g.sample(logits) == 5
+
+
+def test_sampler_seeded_draws_are_reproducible(orc):
+    """sample.rs:518-529: the same seed gives the same 200 draws, another seed others."""
+    logits = np.array([((i * 7919) % 101) / 10.0 for i in range(1000)], np.float32)
+    mk = lambda seed: orc.OracleSampler(1000, 1.0, top_k=20, top_p=0.95, seed=seed)
+    a, b, c = mk(42), mk(42), mk(43)
+    xa = [a.sample(logits) for _ in range(200)]
+    assert xa == [b.sample(logits) for _ in range(200)]
+    assert xa != [c.sample(logits) for _ in range(200)]
+    ids, _ = mk(1).process(logits)
+    assert set(xa) <= set(ids)
+
+
+def test_sampler_accept_rule(orc):
+    """accept_or_resample (sample.rs:279-313): a draft drawn from q = p is always accepted; with q putting all
+    its mass on a token p does not keep, the draft is rejected and the resample comes from p's kept set."""
+    logits = np.array([((i * 31) % 17) / 4.0 for i in range(64)], np.float32)
+    s = orc.OracleSampler(64, 0.8, top_k=10, top_p=0.9, seed=7)
+    ids, ps = s.process(logits)
+    q = np.zeros(64, np.float32)
+    q[ids] = ps
+    for d in ids:
+        assert s.accept(logits, q, d) == (True, d)
+    outside = next(i for i in range(64) if i not in ids)
+    q2 = np.zeros(64, np.float32)
+    q2[outside] = 1.0
+    ok, tok = s.accept(logits, q2, outside)
+    assert not ok and tok in ids
