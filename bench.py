@@ -619,6 +619,28 @@ def run_spec_qdec(args, world, rank, local):
     f1.record(fstream)
     torch.cuda.synchronize()
     forced_ms = f0.elapsed_time(f1)
+    fs.free()
+    # sampled decoding (temperature 0.8, top-k 20, top-p 0.95): the exact acceptance rule instead of greedy
+    ss = model.new_state(spec_k=k, max_rows=32)
+    ss.set_sampler(temperature=0.8, top_k=20, top_p=0.95, seed=SPEC_SEED)
+    sx = ss.spec_prefill(prompt)
+    for _ in range(3):
+        sx = ss.spec_round(sx)[-1]
+    sstream = torch.cuda.ExternalStream(ss.stream)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sc0 = ss.counters()
+    n_samp = min(args.steps, 64)
+    s_tokens = 0
+    s0.record(sstream)
+    for _ in range(n_samp):
+        em = ss.spec_round(sx)
+        s_tokens += len(em)
+        sx = em[-1]
+    s1.record(sstream)
+    torch.cuda.synchronize()
+    sampled_ms = s0.elapsed_time(s1)
+    sc1 = ss.counters()
+    ss.free()
     if world > 1:
         import torch.distributed as dist
 
@@ -654,7 +676,11 @@ def run_spec_qdec(args, world, rank, local):
         "spec": {"s_per_round": round(s_round, 6), "accepted_per_round": (c1["accepted"] - c0["accepted"]) / rounds,
                  "emitted_per_round": (c1["emitted"] - c0["emitted"]) / rounds,
                  "forced_drafts_tok_s": round(forced_all / (forced_ms / 1e3), 3),
-                 "forced_s_per_round": round(forced_ms / 1e3 / n_forced, 6)},
+                 "forced_s_per_round": round(forced_ms / 1e3 / n_forced, 6),
+                 "sampled": {"sampler": "temperature 0.8, top_k 20, top_p 0.95", "rounds": n_samp,
+                             "tok_s_rank0": round(s_tokens / (sampled_ms / 1e3), 3),
+                             "s_per_round": round(sampled_ms / 1e3 / n_samp, 6),
+                             "accepted_per_round": (sc1["accepted"] - sc0["accepted"]) / n_samp}},
         # through the C ABI from the host: x_p in (4 bytes), {keep, emitted ids} out, one round per call
         "e2e": {"value": round(emitted_all / wall, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * (k + 2)},

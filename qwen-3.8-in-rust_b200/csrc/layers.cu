@@ -441,6 +441,24 @@ __global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
 // columns, so every warp runs all 32 lanes on one half.  The k-ordered sums (kv, o) stay single left-to-right
 // chains: the low-half warp sums its 64 terms from 0 and hands the partial sum through shared memory, the
 // high-half warp continues from it.
+// acc + sum_k S[k] * v[k] for k = 0 .. HK-1, left to right; v (shared memory, 16-byte aligned) is read four values
+// at a time with the next quad requested one step ahead, so the dependent adds do not wait on each load
+template <int HK>
+__device__ __forceinline__ float chain_dot(const float (&S)[HK], const float* v, float acc) {
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    float4 nx = v4[0];
+#pragma unroll
+    for (int q = 0; q < HK / 4; q++) {
+        const float4 cur = nx;
+        if (q + 1 < HK / 4) nx = v4[q + 1];
+        acc = __fadd_rn(acc, __fmul_rn(S[4 * q], cur.x));
+        acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 1], cur.y));
+        acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 2], cur.z));
+        acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 3], cur.w));
+    }
+    return acc;
+}
+
 template <int DK>
 __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a) {
     constexpr int HK = DK / 2;
@@ -531,28 +549,26 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             // kv = sum_k S[k] k[k]: the low half from 0, the high half from the low half's sum
             float kv = 0.0f;
             if (h == 0) {
-#pragma unroll
-                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+                kv = chain_dot<HK>(S, ks, 0.0f);
                 part[j] = kv;
             }
             __syncthreads();
             if (h == 1) {
-                kv = part[j];
-#pragma unroll
-                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
+                kv = chain_dot<HK>(S, ks, part[j]);
                 const float v = a.conved[(size_t)r * a.conv_dim + 2 * a.kd + p * dv + j];
                 dlt[j] = __fmul_rn(__fsub_rn(v, kv), beta);
             }
             __syncthreads();
             const float delta = dlt[j];
 #pragma unroll
-            for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
-            if (h == 0) {
-                float o = 0.0f;
-#pragma unroll
-                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
-                part[j] = o;
+            for (int q = 0; q < HK / 4; q++) {
+                const float4 k4 = reinterpret_cast<const float4*>(ks)[q];
+                S[4 * q] = __fadd_rn(S[4 * q], __fmul_rn(k4.x, delta));
+                S[4 * q + 1] = __fadd_rn(S[4 * q + 1], __fmul_rn(k4.y, delta));
+                S[4 * q + 2] = __fadd_rn(S[4 * q + 2], __fmul_rn(k4.z, delta));
+                S[4 * q + 3] = __fadd_rn(S[4 * q + 3], __fmul_rn(k4.w, delta));
             }
+            if (h == 0) part[j] = chain_dot<HK>(S, qs, 0.0f);
             if (r < a.max_t) {
                 if (t == 0) a.pend_decay[(size_t)r * a.n_v + p] = decay;
                 for (int k = t; k < dk; k += blockDim.x) a.pend_k[((size_t)r * a.n_v + p) * dk + k] = ks_all[i][k];
@@ -561,9 +577,7 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             __syncthreads();
             float o = 0.0f;
             if (h == 1) {
-                o = part[j];
-#pragma unroll
-                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
+                o = chain_dot<HK>(S, qs, part[j]);
                 outs[j] = o;
             }
             __syncthreads();
