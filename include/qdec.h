@@ -96,8 +96,10 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
  * the image kernel's configuration (0 = automatic, 1..35: lanes and rows per thread, tiles per warp, warps per
  * tile, super-blocks in flight, integer or FP32 scale multiply, activation prefetch / residency); or, with
  * impl = 8, the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
- * over 4 warps, 3 = the same with two tiles per CTA).  Results do not depend on it; it exists for tests and sweeps.
- * No counterpart in the reference. */
+ * over 4 warps, 3 = the same with two tiles per CTA); or, with impl = 9, the tensor-core prefill GEMM that K-quant
+ * tile matrices take for many columns (config = the smallest column count routed there, 8 by default, 0 = never;
+ * decode's 1..4 verify columns stay on the GEMV at any value >= 5).  Results do not depend on it; it exists for
+ * tests and sweeps.  No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
 
 /* Repack rows x cols of ggml Q6_K (src) into the split layout (dst, the same number of bytes, a distinct

@@ -232,7 +232,12 @@ int qdec_tune_gemv(int impl, int config) {
         set_q80_split(config - 1);
         return QDEC_OK;
     }
-    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6 or 8");
+    if (impl == 9) {  // the tensor-core prefill GEMM: the smallest column count routed to it (0 = never)
+        if (config < 0) return fail(QDEC_EINVAL, "prefill GEMM minimum column count must be >= 0");
+        set_gemm_tc_min_cols(config);
+        return QDEC_OK;
+    }
+    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 8 or 9");
     if (config < 0 || config > 35) return fail(QDEC_EINVAL, "gemv configuration must be 0..35");
     set_gemv_impl(impl);
     set_gemv_v6_config(config);

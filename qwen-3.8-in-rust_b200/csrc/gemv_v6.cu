@@ -1134,6 +1134,7 @@ cudaError_t launch_gemv_img(int type, const uint8_t* w, int rows, int cols, cons
                             bool pdl) {
     const int nb = cols / QK_K;
     if (rows <= 0 || ncols <= 0) return cudaSuccess;
+    if (gemm_tc_applies(type, ncols)) return launch_gemm_tc(type, w, rows, y, nullptr, 0, nullptr, cols, img, ncols, s, pdl);
     for (int c0 = 0; c0 < ncols; c0 += 4) {  // columns beyond 4 in groups of at most 4
         const int nc = std::min(4, ncols - c0);
         const uint8_t* im = (const uint8_t*)img + (size_t)c0 * nb * Q8K_IMG_BYTES;
@@ -1185,6 +1186,7 @@ cudaError_t launch_pair_type(const uint8_t* w_a, int rows_a, float* y_a, const u
 cudaError_t launch_gemv_img_pair(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
                                  int cols, const void* img, int ncols, cudaStream_t s, bool pdl) {
     if (rows_a % 8 || rows_b % 8) return cudaErrorInvalidValue;
+    if (gemm_tc_applies(type, ncols)) return launch_gemm_tc(type, w_a, rows_a, y_a, w_b, rows_b, y_b, cols, img, ncols, s, pdl);
     const int nb = cols / QK_K;
     for (int c0 = 0; c0 < ncols; c0 += 4) {
         const int nc = std::min(4, ncols - c0);
@@ -1245,7 +1247,8 @@ unsigned read_kernel_error(bool clear) {
         const unsigned z = 0;
         cudaMemcpyToSymbol(g_kernel_error, &z, sizeof z);
     }
-    return v;
+    const unsigned t = read_gemm_tc_error(clear);
+    return v ? v : t;
 }
 
 }  // namespace qdec

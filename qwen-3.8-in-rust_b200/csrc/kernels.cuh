@@ -68,5 +68,15 @@ cudaError_t launch_gemv_q80_img(int type, const uint8_t* w, int rows, int cols, 
                                 cudaStream_t s, bool pdl);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
+// Prompt-prefill GEMM on the tensor cores (gemm_tc.cu): K-quant tile matrices (one, or two reading the same
+// image columns) against `ncols` Q8_K image columns, bit-exact with the GEMV.  launch_gemv_img and
+// launch_gemv_img_pair route there when gemm_tc_applies(type, ncols): tile types and ncols >= the minimum
+// column count (8 by default; 0 disables the path).
+bool gemm_tc_applies(int type, int ncols);
+void set_gemm_tc_min_cols(int n);
+int gemm_tc_min_cols();
+cudaError_t launch_gemm_tc(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
+                           int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
+unsigned read_gemm_tc_error(bool clear);
 
 }  // namespace qdec

@@ -178,8 +178,13 @@ def gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream=0):
 
 def tune_gemv(impl=0, config=0):
     """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
-    image kernel's configuration (0 automatic, 1..8). Results are identical for every value."""
+    image kernel's configuration (0 automatic, 1..35); impl 8 the Q8_0/Q4_0 tile kernel (0..3); impl 9 the
+    smallest column count of the tensor-core prefill GEMM (default 8, 0 never). Results are identical for every
+    value."""
     _check(lib().qdec_tune_gemv(impl, config))
+
+
+PREFILL_GEMM_MIN_COLS = 8
 
 
 def repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream=0):
