@@ -535,6 +535,37 @@ def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
             "_s_round": s_round, "_bytes": info.decode_bytes + k * (info.mtp_bytes + info.lm_head_bytes)}
 
 
+def prefill_timing(model, info, max_pos, seed, rows=128):
+    """Prompt prefill (Model::prefill, model.rs:443) of a seeded prompt in chunks of `rows` rows, CUDA-event
+    timed on the state's stream: with the tensor-core GEMM for the K-quant matrices (the default), and with the
+    CUDA-core GEMV forced for comparison.  The second of two runs is the one reported."""
+    import torch
+
+    import qdec
+
+    n = min(512, max_pos - 8)
+    prompt = [int(v) for v in np.random.default_rng(seed).integers(0, min(info.vocab, 248044), n)]
+    out = {"tokens": n, "rows_per_chunk": rows}
+    for key, min_cols in (("tok_s", qdec.PREFILL_GEMM_MIN_COLS), ("tok_s_gemv_path", 0)):
+        qdec.tune_gemv(9, min_cols)
+        try:
+            for _ in range(2):
+                st = model.new_state(spec_k=0, max_rows=rows)
+                stream = torch.cuda.ExternalStream(st.stream)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                a.record(stream)
+                st.prefill(prompt)
+                b.record(stream)
+                torch.cuda.synchronize()
+                st.free()
+            out[key] = round(n / (a.elapsed_time(b) / 1e3), 1)
+        finally:
+            qdec.tune_gemv(9, qdec.PREFILL_GEMM_MIN_COLS)
+    out["gemm"] = "K-quant matrices: tcgen05 GEMM, 128 rows x 16 columns per CTA (bit-exact); tok_s_gemv_path: 4-column GEMV passes"
+    return out
+
+
 def run_spec_qdec(args, world, rank, local):
     import torch
 
@@ -641,6 +672,7 @@ def run_spec_qdec(args, world, rank, local):
     sampled_ms = s0.elapsed_time(s1)
     sc1 = ss.counters()
     ss.free()
+    pre = prefill_timing(model, info, max_pos, SPEC_SEED + 7)
     if world > 1:
         import torch.distributed as dist
 
@@ -693,6 +725,7 @@ def run_spec_qdec(args, world, rank, local):
                                "frac": round(round_bytes / s_round / 1e9 / peak, 4),
                                "north_star_frac": round(17.8e9 / s_round / 1e9 / peak, 4)}},
         "clocks": clk.summary(),
+        "prefill": pre,
     }
     if tp_res is not None:
         s_r, b = tp_res.pop("_s_round"), tp_res.pop("_bytes")

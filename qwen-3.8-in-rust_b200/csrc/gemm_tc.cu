@@ -50,7 +50,7 @@ constexpr int TC_A_STEP = TC_M * 32;      // one lane's K step (16 f16) over the
 constexpr int TC_A_PART = 8 * TC_A_STEP;  // eight lanes: one operand tile (half a super-block of one part)
 constexpr int TC_B_STEP = TC_N * 32;
 constexpr int TC_B_BUF = 8 * TC_B_STEP;
-constexpr int TC_META = 17;  // floats per column and super-block: dx, then q8s[8] (Q4_K/Q5_K) or 2*bsums[16] (Q6_K)
+constexpr int TC_META = 20;  // floats per column and super-block: dx, 3 unused, then q8s[8] (Q4_K/Q5_K) or 2*bsums[16] (Q6_K)
 constexpr int TC_STAGES = 4;                       // raw super-blocks in flight (bulk copies)
 constexpr int TC_IMG_STAGE = TC_N * Q8K_IMG_BYTES;  // the image blocks of one super-block's 16 columns
 constexpr unsigned long long TC_WAIT_NS = 1000000000ull;
@@ -320,16 +320,16 @@ __device__ __forceinline__ void tc_load(const TcArgs& a, int ngroups, int col0, 
                 const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
                 for (int g = 0; g < 8; g++) {
-                    meta[1 + 2 * g] = __fmul_rn(2.0f, s16f(pw[g] & 0xFFFFu));
-                    meta[2 + 2 * g] = __fmul_rn(2.0f, s16f(pw[g] >> 16));
+                    meta[4 + 2 * g] = __fmul_rn(2.0f, s16f(pw[g] & 0xFFFFu));
+                    meta[5 + 2 * g] = __fmul_rn(2.0f, s16f(pw[g] >> 16));
                 }
             } else {
                 const uint4 p = *reinterpret_cast<const uint4*>(blk + Q8K_IMG_Q8S);
                 const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
                 for (int g = 0; g < 4; g++) {
-                    meta[1 + 2 * g] = s16f(pw[g] & 0xFFFFu);
-                    meta[2 + 2 * g] = s16f(pw[g] >> 16);
+                    meta[4 + 2 * g] = s16f(pw[g] & 0xFFFFu);
+                    meta[5 + 2 * g] = s16f(pw[g] >> 16);
                 }
             }
         } else {
@@ -343,6 +343,17 @@ __device__ __forceinline__ void tmem_ld1(uint32_t addr, float& v0) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r0) : "r"(addr));
     v0 = __uint_as_float(r0);
 }
+__device__ __forceinline__ void tmem_ld2(uint32_t addr, float& v0, float& v1) {
+    uint32_t r0, r1;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+    v0 = __uint_as_float(r0), v1 = __uint_as_float(r1);
+}
+
+// f32 pairs: two of the reference's independent chains side by side, each step the scalar IEEE
+// round-to-nearest operation.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
 
 // The epilogue's per-row values of a super-block (from the row's tile block in the raw stage): the f16 scales
 // as f32 and the Q4_K/Q5_K mins or the Q6_K chunk scales.
@@ -376,15 +387,17 @@ __device__ __forceinline__ void tc_row_vals(const uint8_t* smem, int sb, int m, 
     }
 }
 
-// Epilogue of super-block sb for this thread's column I (of its four: row m, columns 4*cb..+3): the lane sums
-// from TMEM buffer sb & 1, the reference's f32 steps into the per-lane chains.
-template <int TYPE, int I>
-__device__ __forceinline__ void tc_epilogue_col(const uint8_t* smem, uint32_t tmem, int sb, int q, int cb, const RowVals& rv,
-                                                float (&acc)[4][8], float (&accm)[4][4]) {
+// Epilogue of super-block sb for this thread's columns I .. I + NCOL - 1 (of its four: row m, columns 4*cb..+3):
+// the lane sums from TMEM buffer sb & 1, the reference's f32 steps into the per-lane chains, two lanes (or two
+// mins groups) per packed instruction.  acc[i][p] holds lanes 2p, 2p+1; accm[i][p] mins groups 2p, 2p+1.
+template <int TYPE, int I, int NCOL>
+__device__ __forceinline__ void tc_epilogue_cols(const uint8_t* smem, uint32_t tmem, int sb, int q, int cb, const RowVals& rv,
+                                                 float2 (&acc)[4][4], float2 (&accm)[4][2]) {
     using C = TcType<TYPE>;
-    const float* mc = reinterpret_cast<const float*>(smem + C::OFF_META) + ((sb % 3) * TC_N + 4 * cb + I) * TC_META;
+    const float4* meta = reinterpret_cast<const float4*>(smem + C::OFF_META) + ((sb % 3) * TC_N + 4 * cb + I) * (TC_META / 4);
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((sb & 1) * C::ACC_COLS + 4 * cb + I);
     if constexpr (TYPE == T_Q6_K) {
+        static_assert(NCOL == 1, "Q6_K takes one column per step");
         float dlo[8], dhi[8];
 #pragma unroll
         for (int l = 0; l < 8; l++) {
@@ -392,28 +405,43 @@ __device__ __forceinline__ void tc_epilogue_col(const uint8_t* smem, uint32_t tm
             tmem_ld1(trow + (8 + l) * TC_N, dhi[l]);
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const float d = __fmul_rn(mc[0], rv.dw);
+        const float d = __fmul_rn(meta[0].x, rv.dw);
+        const float4 b0 = meta[1], b1 = meta[2], b2 = meta[3], b3 = meta[4];  // 2 * bsums[0..15]
+        const float bs[16] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w, b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
 #pragma unroll
-        for (int l = 0; l < 8; l++) {
-            // sumi = (sc*lo) + 16 (sc*hi) - 32 (bsum[2l] sc[2l] + bsum[2l+1] sc[2l+1]), one rounding
-            const float c2 = __fadd_rn(__fmul_rn(mc[1 + 2 * l], rv.v[2 * l]), __fmul_rn(mc[2 + 2 * l], rv.v[2 * l + 1]));
-            const float sumi = __fadd_rn(__fmul_rn(16.0f, __fsub_rn(dhi[l], c2)), dlo[l]);
-            acc[I][l] = __fadd_rn(acc[I][l], __fmul_rn(d, sumi));
+        for (int p = 0; p < 4; p++) {
+            // lanes l = 2p, 2p+1: sumi = (sc*lo) + 16 (sc*hi - 2 (bsum[2l] sc[2l] + bsum[2l+1] sc[2l+1])), one rounding
+            const int l = 2 * p;
+            const float2 ca = mul2(f2(bs[2 * l], bs[2 * l + 1]), f2(rv.v[2 * l], rv.v[2 * l + 1]));
+            const float2 cb2 = mul2(f2(bs[2 * l + 2], bs[2 * l + 3]), f2(rv.v[2 * l + 2], rv.v[2 * l + 3]));
+            const float2 c2 = f2(__fadd_rn(ca.x, ca.y), __fadd_rn(cb2.x, cb2.y));
+            const float2 t = add2(f2(dhi[l], dhi[l + 1]), f2(-c2.x, -c2.y));
+            const float2 sumi = add2(mul2(f2(16.0f, 16.0f), t), f2(dlo[l], dlo[l + 1]));
+            acc[I][p] = add2(acc[I][p], mul2(f2(d, d), sumi));
         }
     } else {
-        float s[8];
+        float s[8][NCOL];
 #pragma unroll
-        for (int l = 0; l < 8; l++) tmem_ld1(trow + l * TC_N, s[l]);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const float dx = mc[0];
-        const float d = __fmul_rn(dx, rv.dw), dmin = __fmul_rn(-dx, rv.dminw);
-#pragma unroll
-        for (int g = 0; g < 4; g++) {  // exact: |prod| < 2^20
-            const float prod = __fadd_rn(__fmul_rn(rv.v[2 * g], mc[1 + 2 * g]), __fmul_rn(rv.v[2 * g + 1], mc[2 + 2 * g]));
-            accm[I][g] = __fadd_rn(accm[I][g], __fmul_rn(dmin, prod));
+        for (int l = 0; l < 8; l++) {
+            if constexpr (NCOL == 2) tmem_ld2(trow + l * TC_N, s[l][0], s[l][1]);
+            else tmem_ld1(trow + l * TC_N, s[l][0]);
         }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int l = 0; l < 8; l++) acc[I][l] = __fadd_rn(acc[I][l], __fmul_rn(d, s[l]));
+        for (int j = 0; j < NCOL; j++) {
+            const float4* mc = meta + j * (TC_META / 4);
+            const float dx = mc[0].x;
+            const float4 qa = mc[1], qb = mc[2];  // q8s[0..7]
+            const float d = __fmul_rn(dx, rv.dw), dmin = __fmul_rn(-dx, rv.dminw);
+            // prod_g = mn[2g] q8s[2g] + mn[2g+1] q8s[2g+1], exact (|prod| < 2^20)
+            const float2 p0 = mul2(f2(rv.v[0], rv.v[1]), f2(qa.x, qa.y)), p1 = mul2(f2(rv.v[2], rv.v[3]), f2(qa.z, qa.w));
+            const float2 p2 = mul2(f2(rv.v[4], rv.v[5]), f2(qb.x, qb.y)), p3 = mul2(f2(rv.v[6], rv.v[7]), f2(qb.z, qb.w));
+            const float2 dm = f2(dmin, dmin), dd = f2(d, d);
+            accm[I + j][0] = add2(accm[I + j][0], mul2(dm, f2(__fadd_rn(p0.x, p0.y), __fadd_rn(p1.x, p1.y))));
+            accm[I + j][1] = add2(accm[I + j][1], mul2(dm, f2(__fadd_rn(p2.x, p2.y), __fadd_rn(p3.x, p3.y))));
+#pragma unroll
+            for (int p = 0; p < 4; p++) acc[I + j][p] = add2(acc[I + j][p], mul2(dd, f2(s[2 * p][j], s[2 * p + 1][j])));
+        }
     }
 }
 
@@ -421,23 +449,18 @@ __device__ __forceinline__ void tc_epilogue_col(const uint8_t* smem, uint32_t tm
 // columns per step, Q6_K one.
 template <int TYPE>
 __device__ __forceinline__ void tc_epilogue_step(const uint8_t* smem, uint32_t tmem, int sb, int st, int q, int cb, int m,
-                                                 RowVals& rv, float (&acc)[4][8], float (&accm)[4][4]) {
+                                                 RowVals& rv, float2 (&acc)[4][4], float2 (&accm)[4][2]) {
     if (st == 0) tc_row_vals<TYPE>(smem, sb, m, rv);
     if constexpr (TYPE == T_Q6_K) {
         switch (st) {
-        case 0: tc_epilogue_col<TYPE, 0>(smem, tmem, sb, q, cb, rv, acc, accm); break;
-        case 1: tc_epilogue_col<TYPE, 1>(smem, tmem, sb, q, cb, rv, acc, accm); break;
-        case 2: tc_epilogue_col<TYPE, 2>(smem, tmem, sb, q, cb, rv, acc, accm); break;
-        default: tc_epilogue_col<TYPE, 3>(smem, tmem, sb, q, cb, rv, acc, accm); break;
+        case 0: tc_epilogue_cols<TYPE, 0, 1>(smem, tmem, sb, q, cb, rv, acc, accm); break;
+        case 1: tc_epilogue_cols<TYPE, 1, 1>(smem, tmem, sb, q, cb, rv, acc, accm); break;
+        case 2: tc_epilogue_cols<TYPE, 2, 1>(smem, tmem, sb, q, cb, rv, acc, accm); break;
+        default: tc_epilogue_cols<TYPE, 3, 1>(smem, tmem, sb, q, cb, rv, acc, accm); break;
         }
     } else {
-        if (st == 0) {
-            tc_epilogue_col<TYPE, 0>(smem, tmem, sb, q, cb, rv, acc, accm);
-            tc_epilogue_col<TYPE, 1>(smem, tmem, sb, q, cb, rv, acc, accm);
-        } else {
-            tc_epilogue_col<TYPE, 2>(smem, tmem, sb, q, cb, rv, acc, accm);
-            tc_epilogue_col<TYPE, 3>(smem, tmem, sb, q, cb, rv, acc, accm);
-        }
+        if (st == 0) tc_epilogue_cols<TYPE, 0, 2>(smem, tmem, sb, q, cb, rv, acc, accm);
+        else tc_epilogue_cols<TYPE, 2, 2>(smem, tmem, sb, q, cb, rv, acc, accm);
     }
 }
 
@@ -482,13 +505,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) kq_gemm_tc_kernel(const __grid_
 
     // epilogue ownership: row m (TMEM lane), columns 4 * cb .. + 3
     const int q = warp & 3, cb = warp >> 2, m = q * 32 + lane;
-    float acc[4][8], accm[4][4];
+    float2 acc[4][4], accm[4][2];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
 #pragma unroll
-        for (int l = 0; l < 8; l++) acc[i][l] = 0.0f;
-#pragma unroll
-        for (int g = 0; g < 4; g++) accm[i][g] = 0.0f;
+        for (int p = 0; p < 4; p++) acc[i][p] = f2(0.0f, 0.0f);
+        accm[i][0] = accm[i][1] = f2(0.0f, 0.0f);
     }
     RowVals rv;
 
@@ -562,10 +584,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) kq_gemm_tc_kernel(const __grid_
         for (int i = 0; i < 4; i++) {
             const int col = col0 + 4 * cb + i;
             if (col < a.ncols) {
-                float v = __fadd_rn(__fadd_rn(__fadd_rn(acc[i][0], acc[i][4]), __fadd_rn(acc[i][2], acc[i][6])),
-                                    __fadd_rn(__fadd_rn(acc[i][1], acc[i][5]), __fadd_rn(acc[i][3], acc[i][7])));  // reduce8 (kdot.rs:20-29)
-                if constexpr (TYPE != T_Q6_K)
-                    v = __fadd_rn(v, __fadd_rn(__fadd_rn(accm[i][0], accm[i][2]), __fadd_rn(accm[i][1], accm[i][3])));  // reduce4
+                // reduce8 (kdot.rs:20-29): ((l0 + l4) + (l2 + l6)) + ((l1 + l5) + (l3 + l7))
+                const float2 r = add2(add2(acc[i][0], acc[i][2]), add2(acc[i][1], acc[i][3]));
+                float v = __fadd_rn(r.x, r.y);
+                if constexpr (TYPE != T_Q6_K) {  // reduce4: (m0 + m2) + (m1 + m3)
+                    const float2 rm = add2(accm[i][0], accm[i][1]);
+                    v = __fadd_rn(v, __fadd_rn(rm.x, rm.y));
+                }
                 y[(size_t)col * rows + row] = v;
             }
         }
