@@ -447,14 +447,15 @@ def spec_prompt(vocab, seed):
     return [int(v) for v in np.random.default_rng(seed).integers(0, min(vocab, 248044), PROMPT_LEN)]
 
 
-def dominant_gemv_timing(dev, launches=200):
+def dominant_gemv_timing(dev, launches=200, n=4):
     """The verify's dominant kernel timed alone on the launching stream with CUDA events: the Q4_K GEMV of
-    ffn_gate/ffn_up (17408 x 5120, tile layout, N = 4 columns), weights rotating over 3 sets (> L2)."""
+    ffn_gate/ffn_up (17408 x 5120, tile layout, N = 4 columns), weights rotating over 3 sets (> L2).  With
+    n >= 8 columns the same call runs the prefill's tensor-core GEMM."""
     import torch
 
     import qdec
 
-    rows, cols, n = UP[0], UP[1], 4
+    rows, cols = UP[0], UP[1]
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     sets = []
@@ -753,12 +754,17 @@ def main():
                     help="prompt ids before the timed rounds (default 128; 8064 grows the KV cache to ~8192: config 5)")
     ap.add_argument("--profile-gemv", action="store_true",
                     help="run the dominant GEMV (Q4_K 17408x5120 N=4, tile layout) 4 times and exit: the ncu capture target")
+    ap.add_argument("--profile-prefill-gemm", action="store_true",
+                    help="run the prefill's tensor-core GEMM (Q4_K 17408x5120, 32 columns) 4 times, print its event time "
+                         "and exit: the ncu capture target")
     args = ap.parse_args()
-    if args.profile_gemv:
+    if args.profile_gemv or args.profile_prefill_gemm:
         import torch
 
         torch.cuda.set_device(0)
-        dominant_gemv_timing(torch.device("cuda", 0), launches=4)
+        n = 32 if args.profile_prefill_gemm else 4
+        _, ms = dominant_gemv_timing(torch.device("cuda", 0), launches=4, n=n)
+        print(json.dumps({"kernel": f"Q4_K 17408x5120 x {n} columns", "us_per_launch": round(ms * 1e3, 2)}))
         return
     if args.prompt_len:
         global PROMPT_LEN
