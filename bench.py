@@ -594,7 +594,9 @@ def run_spec_qdec(args, world, rank, local):
             import torch.distributed as dist
 
             dist.barrier()
+    t_load = time.perf_counter()
     model = qdec.Model(path, device=local, max_pos=max_pos)
+    load_s = time.perf_counter() - t_load
     info = model.info
     prompt = spec_prompt(info.vocab, SPEC_SEED + 1 + rank)
     st = model.new_state(spec_k=k, max_rows=32)
@@ -727,6 +729,9 @@ def run_spec_qdec(args, world, rank, local):
                                "north_star_frac": round(17.8e9 / s_round / 1e9 / peak, 4)}},
         "clocks": clk.summary(),
         "prefill": pre,
+        # qdec_open: the GGUF data section read by several threads into pinned staging, uploaded chunk by chunk,
+        # repacked in place (the checkpoint file sits in /dev/shm, so this is the memory-to-HBM path)
+        "load": {"seconds": round(load_s, 3), "gb_s": round(info.weight_bytes / load_s / 1e9, 2)},
     }
     if tp_res is not None:
         s_r, b = tp_res.pop("_s_round"), tp_res.pop("_bytes")

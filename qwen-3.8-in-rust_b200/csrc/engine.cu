@@ -22,6 +22,8 @@
 #include <cmath>
 #include <cstring>
 #include <stdexcept>
+#include <cstdlib>
+#include <thread>
 
 #include "common.cuh"
 #include "engine.h"
@@ -133,6 +135,17 @@ bool Model::is_stop(uint32_t id) const {
     return std::find(cfg.stop_ids.begin(), cfg.stop_ids.end(), id) != cfg.stop_ids.end();
 }
 
+// Readers of the weight file: QDEC_LOAD_THREADS, else half the hardware threads, 2..16.
+static int load_threads() {
+    static const int n = [] {
+        const char* e = getenv("QDEC_LOAD_THREADS");
+        if (e && atoi(e) > 0) return std::min(atoi(e), 64);
+        const int hw = (int)std::thread::hardware_concurrency();
+        return std::max(2, std::min(16, hw / 2));
+    }();
+    return n;
+}
+
 std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& opt) {
     const auto t0 = std::chrono::steady_clock::now();
     Gguf g(path);
@@ -145,7 +158,8 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     const ModelConfig& c = m->cfg;
     const TpPlan& P = m->tp;
 
-    // the data section, unchanged, in one allocation
+    // the data section, unchanged, in one allocation: read in 256 MiB chunks by several threads into pinned
+    // staging (two buffers), each chunk's upload overlapping the next chunk's read
     const uint64_t data_bytes = g.file_size() - g.data_offset();
     ck(cudaMalloc(&m->blob_, data_bytes + 256), "weights allocation");
     m->weight_bytes = data_bytes;
@@ -165,7 +179,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
                 const uint64_t len = std::min<uint64_t>(CH, data_bytes - off);
                 if (used[b]) ck(cudaEventSynchronize(done[b]), "staging wait");
                 uint8_t* hb = static_cast<uint8_t*>(host) + b * CH;
-                g.read_at(g.data_offset() + off, hb, len);
+                g.read_at_parallel(g.data_offset() + off, hb, len, load_threads());
                 ck(cudaMemcpyAsync(m->blob_ + off, hb, len, cudaMemcpyHostToDevice, s), "weights upload");
                 ck(cudaEventRecord(done[b], s), "event");
                 used[b] = true;

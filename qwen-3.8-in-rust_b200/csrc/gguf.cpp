@@ -8,6 +8,8 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 namespace qdec {
 
@@ -308,6 +310,34 @@ void Gguf::read_at(uint64_t off, void *dst, uint64_t len) const {
         if (k <= 0) gerr("io error: short read of %s at %llu", path_.c_str(), (unsigned long long)(off + got));
         got += (uint64_t)k;
     }
+}
+
+void Gguf::read_at_parallel(uint64_t off, void *dst, uint64_t len, int threads) const {
+    // contiguous parts of >= 16 MiB on 4 KiB boundaries, one positional read loop per thread (page-cache copies
+    // and NVMe queues both scale with readers); the first error is rethrown after every part has finished
+    const uint64_t part_min = 16ull << 20;
+    int n = (int)std::min<uint64_t>((uint64_t)std::max(threads, 1), std::max<uint64_t>(1, len / part_min));
+    if (n <= 1) {
+        read_at(off, dst, len);
+        return;
+    }
+    const uint64_t per = ((len + n - 1) / n + 4095) & ~4095ull;
+    std::vector<std::thread> ts;
+    std::vector<std::string> errs(n);
+    for (int i = 0; i < n; i++) {
+        const uint64_t a = std::min<uint64_t>(len, (uint64_t)i * per), b = std::min<uint64_t>(len, a + per);
+        if (a >= b) break;
+        ts.emplace_back([this, off, dst, a, b, i, &errs] {
+            try {
+                read_at(off + a, static_cast<uint8_t *>(dst) + a, b - a);
+            } catch (const std::exception &e) {
+                errs[i] = e.what();
+            }
+        });
+    }
+    for (std::thread &t : ts) t.join();
+    for (const std::string &e : errs)
+        if (!e.empty()) throw GgufError(e);
 }
 
 void Gguf::read_into(const std::string &name, void *dst, uint64_t len) const {

@@ -71,6 +71,8 @@ class Gguf {
     void read_into(const std::string &name, void *dst, uint64_t len) const;
     // read `len` bytes at absolute file offset `off`
     void read_at(uint64_t off, void *dst, uint64_t len) const;
+    // the same bytes read by up to `threads` threads in contiguous parts
+    void read_at_parallel(uint64_t off, void *dst, uint64_t len, int threads) const;
 
   private:
     std::string path_;
