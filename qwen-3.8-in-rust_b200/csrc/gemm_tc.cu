@@ -46,8 +46,10 @@ namespace {
 __device__ unsigned int g_tc_error = 0;  // first error code of a bounded wait that gave up
 
 constexpr int TC_M = 128, TC_N = 16, TC_COMPUTE = 512, TC_THREADS = TC_COMPUTE + 32;  // 16 compute warps + the issuing warp
-constexpr int TC_A_STEP = TC_M * 32;      // one lane's K step (16 f16) over the 128 rows
-constexpr int TC_A_PART = 8 * TC_A_STEP;  // eight lanes: one operand tile (half a super-block of one part)
+constexpr int TC_A_STEP = TC_M * 32;        // one lane's K step (16 f16) over the 128 rows
+constexpr int TC_A_PITCH = TC_A_STEP + 16;  // steps 16 bytes apart beyond their size: the four lane pairs that a
+                                            // quarter-warp of the dequantisation stores fall in distinct banks
+constexpr int TC_A_PART = 8 * TC_A_PITCH;   // eight lanes: one operand tile (half a super-block of one part)
 constexpr int TC_B_STEP = TC_N * 32;
 constexpr int TC_B_BUF = 8 * TC_B_STEP;
 constexpr int TC_META = 20;  // floats per column and super-block: dx, 3 unused, then q8s[8] (Q4_K/Q5_K) or 2*bsums[16] (Q6_K)
@@ -160,7 +162,7 @@ __device__ __forceinline__ void st_shared_v4(uint8_t* p, uint2 a, uint2 b) {
 }
 
 // Dequantise one item of half super-block h: row r of a tile block (in shared memory), lane pair (2tg, 2tg+1),
-// into the operand buffer `a` (step l at l * TC_A_STEP, core column at 2048 per K half, row m at
+// into the operand buffer `a` (step l at l * TC_A_PITCH, core column at 2048 per K half, row m at
 // (m/8)*128 + (m%8)*16).  Q6_K writes part PART: sc * lo4 (0) or sc * hi2 (1).
 template <int TYPE, int PART>
 __device__ __forceinline__ void dequant_item(const uint8_t* tile, int r, int tg, int h, uint8_t* a, int m) {
@@ -189,7 +191,7 @@ __device__ __forceinline__ void dequant_item(const uint8_t* tile, int r, int tg,
                 q2 |= ((hb >> 2) & 0x01010101u) << 4;
                 q3 |= ((hb >> 3) & 0x01010101u) << 4;
             }
-            uint8_t* step = row + (2 * tg + e) * TC_A_STEP;
+            uint8_t* step = row + (2 * tg + e) * TC_A_PITCH;
             st_shared_v4(step, scaled4(q0, sc[0], cc[0]), scaled4(q1, sc[1], cc[1]));
             st_shared_v4(step + 2048, scaled4(q2, sc[2], cc[2]), scaled4(q3, sc[3], cc[3]));
         }
@@ -216,7 +218,7 @@ __device__ __forceinline__ void dequant_item(const uint8_t* tile, int r, int tg,
             __half2 sc[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) sc[k] = signed_scale_pair((k < 2 ? sw0 : sw1) >> (8 * (2 * (k & 1) + (lane >> 2))));
-            uint8_t* step = row + lane * TC_A_STEP;
+            uint8_t* step = row + lane * TC_A_PITCH;
             st_shared_v4(step, scaled4_signed(v[0], sc[0]), scaled4_signed(v[1], sc[1]));
             st_shared_v4(step + 2048, scaled4_signed(v[2], sc[2]), scaled4_signed(v[3], sc[3]));
         }
@@ -276,7 +278,7 @@ __device__ __forceinline__ void tc_load(const TcArgs& a, int ngroups, int col0, 
     const uint8_t* raw = smem + (sb % TC_STAGES) * C::RAW;
     // weights: warp = row group (8 rows), lane = (row, lane pair)
     {
-        const int r = lane & 7, tg = lane >> 3, m = warp * 8 + r;
+        const int r = lane >> 2, tg = lane & 3, m = warp * 8 + r;  // lane = the tile block's 16-byte chunk (contiguous reads)
         uint8_t* abuf = smem + C::OFF_A + (gs & 1) * TC_A_PART;
         if (warp < ngroups) {
             if (part == 0) dequant_item<TYPE, 0>(raw + warp * C::TB, r, tg, h, abuf, m);
@@ -285,7 +287,7 @@ __device__ __forceinline__ void tc_load(const TcArgs& a, int ngroups, int col0, 
             uint8_t* row = abuf + (m >> 3) * 128 + (m & 7) * 16;
 #pragma unroll
             for (int e = 0; e < 2; e++) {
-                uint8_t* step = row + (2 * tg + e) * TC_A_STEP;
+                uint8_t* step = row + (2 * tg + e) * TC_A_PITCH;
                 *reinterpret_cast<uint4*>(step) = make_uint4(0, 0, 0, 0);
                 *reinterpret_cast<uint4*>(step + 2048) = make_uint4(0, 0, 0, 0);
             }
@@ -536,7 +538,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) kq_gemm_tc_kernel(const __grid_
                 const uint32_t accumulate = st / C::PARTS;  // the second half adds to the first
 #pragma unroll
                 for (int l = 0; l < 8; l++)
-                    tc_mma(dbase + (uint32_t)(l * TC_N), smem_desc(abase + l * TC_A_STEP, 2048, 128),
+                    tc_mma(dbase + (uint32_t)(l * TC_N), smem_desc(abase + l * TC_A_PITCH, 2048, 128),
                            smem_desc(bbase + l * TC_B_STEP, TC_N * 16, 128), accumulate);
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(mma_bar))
                              : "memory");
