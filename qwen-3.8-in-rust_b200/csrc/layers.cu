@@ -80,6 +80,8 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 // of h to h_out (which must not alias a or b: every CTA of the row reads the whole row); y = rmsnorm(h, w)
 // (rmsnorm.rs:14-76, the 8-lane sum over the whole row, recomputed by every CTA of the row) for its chunk,
 // written to y_out when given and quantised into the Q8_K image / Q8_0 rows when given.
+constexpr int RN_REG_VECS = 8;  // float4 of a row held per thread (rows up to 8192 values at 256 threads)
+
 __global__ void __launch_bounds__(256)
 resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ h_out,
                         const float* __restrict__ w, float eps, int n, float* __restrict__ y_out,
@@ -94,12 +96,7 @@ resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b
     const int row = blockIdx.y, c0 = blockIdx.x * 256, per = n / 8;
     const float4* a4 = reinterpret_cast<const float4*>(a + (size_t)row * n);
     const float4* b4 = b ? reinterpret_cast<const float4*>(b + (size_t)row * n) : nullptr;
-    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
-        float4 v = a4[i];
-        if (b4) {
-            const float4 u = b4[i];
-            v.x = __fadd_rn(v.x, u.x), v.y = __fadd_rn(v.y, u.y), v.z = __fadd_rn(v.z, u.z), v.w = __fadd_rn(v.w, u.w);
-        }
+    auto put = [&](int i, float4 v) {
         // elements 4i .. 4i+3: lanes (4i) % 8 .. +3, position (4i) / 8 in each lane
         const int l0 = (4 * i) & 7, k = (4 * i) >> 3;
         sq[(l0 + 0) * per + k] = __fmul_rn(v.x, v.x);
@@ -107,6 +104,29 @@ resid_norm_quant_kernel(const float* __restrict__ a, const float* __restrict__ b
         sq[(l0 + 2) * per + k] = __fmul_rn(v.z, v.z);
         sq[(l0 + 3) * per + k] = __fmul_rn(v.w, v.w);
         if (4 * i >= c0 && 4 * i < c0 + 256) reinterpret_cast<float4*>(hc)[(4 * i - c0) >> 2] = v;
+    };
+    auto sum4 = [](float4 v, float4 u) {
+        return make_float4(__fadd_rn(v.x, u.x), __fadd_rn(v.y, u.y), __fadd_rn(v.z, u.z), __fadd_rn(v.w, u.w));
+    };
+    if (n / 4 <= RN_REG_VECS * (int)blockDim.x) {
+        // rows up to RN_REG_VECS float4 per thread: every load issued before the first use, so the row arrives
+        // in one memory round trip rather than one per iteration
+        float4 va[RN_REG_VECS], vb[RN_REG_VECS];
+#pragma unroll
+        for (int j = 0; j < RN_REG_VECS; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n / 4) {
+                va[j] = a4[i];
+                if (b4) vb[j] = b4[i];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < RN_REG_VECS; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n / 4) put(i, b4 ? sum4(va[j], vb[j]) : va[j]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) put(i, b4 ? sum4(a4[i], b4[i]) : a4[i]);
     }
     __syncthreads();
     if (h_out) h_out[(size_t)row * n + c0 + threadIdx.x] = hc[threadIdx.x];
