@@ -15,19 +15,18 @@
 // Q4_K/Q5_K mins term, the Q6_K -32 * bsum correction) then run on the CUDA cores in the reference's order, in
 // registers, across super-blocks.
 //
-// Work split.  A CTA owns 128 weight rows (the MMA's M, one TMEM lane each) and 16 activation columns (N); its
-// 512 threads (16 warps) walk the super-blocks in steps of one MMA operand tile (half a super-block; for Q6_K
-// half a super-block of the low or of the high parts).  The raw bytes of a super-block -- its 16 tile blocks
-// (8 rows each, contiguous in the tile layout) and the 16 columns' image blocks -- arrive by bulk asynchronous
-// copies (cp.async.bulk, completing on an mbarrier) into a ring of four stages, issued by one thread at least
-// three steps ahead.  Per step: one thread issues the step's eight MMAs (operands from one of two shared-memory
-// buffers, accumulators in the TMEM buffer of this super-block) and commits them to an mbarrier; meanwhile all
-// threads run their share of the previous super-block's epilogue from the other TMEM buffer (warp w: TMEM lanes
-// 32*(w%4).., i.e. rows, and one or two of its columns 4*(w/4)..+3) and dequantise the next step into the other
-// operand buffer; one warp then waits for the MMAs and a single barrier ends the step.  Every wait is bounded:
-// after about a second the kernel records an error code, drains its copies, frees its TMEM and returns.  Column
-// groups are the fastest grid dimension, so the CTAs that share a weight tile run together and the tile is read
-// from HBM once.
+// Work split.  A CTA owns 128 weight rows (the MMA's M, one TMEM lane each) and 16 activation columns (N).  Its
+// 16 compute warps walk the super-blocks in steps of one MMA operand tile (half a super-block; for Q6_K half a
+// super-block of the low or of the high parts); a 17th warp issues the copies and the MMAs.  The raw bytes of a
+// super-block -- its 16 tile blocks (8 rows each, contiguous in the tile layout) and the 16 columns' image blocks
+// -- arrive by two 2-D TMA tensor copies (completing on an mbarrier) into a ring of four stages, at least three
+// steps ahead.  Per step the issuing warp starts the step's eight MMAs (operands from one of two shared-memory
+// buffers, accumulators in the TMEM buffer of this super-block), commits them to an mbarrier and waits for them;
+// meanwhile the compute warps run their share of the previous super-block's epilogue from the other TMEM buffer
+// (warp w: TMEM lanes 32*(w%4).., i.e. rows, and one or two of its columns 4*(w/4)..+3) and dequantise the next
+// step into the other operand buffer; one barrier ends the step.  Every wait is bounded: after about a second
+// the kernel records an error code, drains its copies, frees its TMEM and returns.  Column groups are the
+// fastest grid dimension, so the CTAs that share a weight tile run together and the tile is read from HBM once.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -53,7 +52,7 @@ constexpr int TC_A_PART = 8 * TC_A_PITCH;   // eight lanes: one operand tile (ha
 constexpr int TC_B_STEP = TC_N * 32;
 constexpr int TC_B_BUF = 8 * TC_B_STEP;
 constexpr int TC_META = 20;  // floats per column and super-block: dx, 3 unused, then q8s[8] (Q4_K/Q5_K) or 2*bsums[16] (Q6_K)
-constexpr int TC_STAGES = 4;                       // raw super-blocks in flight (bulk copies)
+constexpr int TC_STAGES = 4;                       // raw super-blocks in flight (TMA tensor copies)
 constexpr int TC_IMG_STAGE = TC_N * Q8K_IMG_BYTES;  // the image blocks of one super-block's 16 columns
 constexpr unsigned long long TC_WAIT_NS = 1000000000ull;
 constexpr unsigned TC_ERR_WAIT = 0x7c01;
