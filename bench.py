@@ -499,7 +499,9 @@ def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
 
     import qdec
 
-    model = qdec.Model(path, device=local, max_pos=max_pos, tp=(rank, world))
+    t_load = time.perf_counter()
+    model = qdec.Model(path, device=local, max_pos=max_pos, tp=(rank, world))  # each rank reads its shard rows
+    load_s = time.perf_counter() - t_load
     st = model.new_state(spec_k=k, max_rows=32)
     st.tp_connect_group()
     stream = torch.cuda.ExternalStream(st.stream)
@@ -520,7 +522,7 @@ def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
     e1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    ms, wall_ms = max_over_ranks([e0.elapsed_time(e1), wall * 1e3], torch.device("cuda", local))
+    ms, wall_ms, load_s = max_over_ranks([e0.elapsed_time(e1), wall * 1e3, load_s], torch.device("cuda", local))
     launches = st.launches - l0
     info = model.info
     dist.barrier()  # every rank's last exchange is done before any rank frees its exchange block
@@ -532,6 +534,7 @@ def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
             "e2e": {"value": round(emitted / (wall_ms / 1e3), 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * world,
                     "d2h_bytes_per_step": 4 * (k + 2) * world},
             "per_rank_verify_bytes": info.decode_bytes,
+            "load_seconds_max_over_ranks": round(load_s, 3),
             "round_frac_per_rank": None,
             "_s_round": s_round, "_bytes": info.decode_bytes + k * (info.mtp_bytes + info.lm_head_bytes)}
 

@@ -24,6 +24,8 @@
 #include <stdexcept>
 #include <cstdlib>
 #include <thread>
+#include <memory>
+#include <unordered_set>
 
 #include "common.cuh"
 #include "engine.h"
@@ -159,11 +161,14 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     const TpPlan& P = m->tp;
 
     // the data section, unchanged, in one allocation: read in 256 MiB chunks by several threads into pinned
-    // staging (two buffers), each chunk's upload overlapping the next chunk's read
+    // staging (two buffers), each chunk's upload overlapping the next chunk's read.  A tensor-parallel rank
+    // instead reads what it keeps: the replicated tensors whole (on first use) and only its rows of the sharded
+    // ones, straight into their shard allocations.
     const uint64_t data_bytes = g.file_size() - g.data_offset();
     ck(cudaMalloc(&m->blob_, data_bytes + 256), "weights allocation");
     m->weight_bytes = data_bytes;
-    {
+    const bool per_rank = P.world > 1;
+    if (!per_rank) {
         const size_t CH = 256ull << 20;
         void* host = nullptr;
         ck(cudaHostAlloc(&host, 2 * CH, cudaHostAllocDefault), "pinned staging");
@@ -196,7 +201,25 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         cudaFreeHost(host);
         cudaStreamDestroy(s);
     }
-    auto ptr = [&](const TensorInfo& t) { return m->blob_ + t.rel_offset; };
+    const size_t STG = 64ull << 20;
+    std::unique_ptr<void, cudaError_t (*)(void*)> stage(nullptr, cudaFreeHost);
+    if (per_rank) {
+        void* h = nullptr;
+        ck(cudaHostAlloc(&h, STG, cudaHostAllocDefault), "pinned staging");
+        stage.reset(h);
+    }
+    auto upload = [&](uint64_t file_off, uint8_t* dst, uint64_t len) {  // file bytes -> device, STG at a time
+        for (uint64_t o = 0; o < len; o += STG) {
+            const uint64_t n = std::min<uint64_t>(STG, len - o);
+            g.read_at_parallel(file_off + o, stage.get(), n, load_threads());
+            ck(cudaMemcpy(dst + o, stage.get(), n, cudaMemcpyHostToDevice), "weights upload");
+        }
+    };
+    std::unordered_set<const TensorInfo*> resident;  // (tensor-parallel) tensors already read whole
+    auto ptr = [&](const TensorInfo& t) {
+        if (per_rank && resident.insert(&t).second) upload(t.abs_offset, m->blob_ + t.rel_offset, t.byte_size);
+        return m->blob_ + t.rel_offset;
+    };
     // K-quant matrices are repacked in place (same bytes) into the tile layout the GEMV streams (rows % 8 == 0),
     // else Q6_K into the split layout; the embedding table keeps the ggml layout because rows of it are
     // dequantised directly
@@ -262,7 +285,8 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         m->shard_allocs_.push_back(d);
         uint64_t o = 0;
         for (const auto& sg : segs) {
-            ck(cudaMemcpy(d + o, ptr(t) + sg.first * row_bytes, sg.second * row_bytes, cudaMemcpyDeviceToDevice), "shard copy");
+            if (per_rank && !resident.count(&t)) upload(t.abs_offset + sg.first * row_bytes, d + o, sg.second * row_bytes);
+            else ck(cudaMemcpy(d + o, ptr(t) + sg.first * row_bytes, sg.second * row_bytes, cudaMemcpyDeviceToDevice), "shard copy");
             o += sg.second * row_bytes;
         }
         return d;
