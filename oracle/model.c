@@ -489,22 +489,28 @@ static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int 
     free(qg); free(k); free(v); free(q); free(attn); free(tmp); free(inv); free(cs); free(sn); free(sc); free(pr);
 }
 
+/* layers/mlp.rs:53-64: y = down(swiglu(gate(x), up(x))) */
+static void mlp_token(OModel *m, const OLayer *L, const float *x, float *y) {
+    float *g = (float *)malloc((size_t)m->ffn * 4), *u = (float *)malloc((size_t)m->ffn * 4), *hh = (float *)malloc((size_t)m->ffn * 4);
+    matvec(&L->gate, x, g);
+    matvec(&L->up, x, u);
+    oracle_swiglu(g, u, m->ffn, hh);
+    matvec(&L->down, hh, y);
+    free(g); free(u); free(hh);
+}
+
 /* layers/mod.rs:295-330: h = x + mixer(norm(x)); y = h + mlp(norm(h)) */
 static void layer_token(OModel *m, const OLayer *L, OLayerState *st, float *K, float *V, int pos, const float *x, float *y) {
     const int H = m->hidden;
     float *normed = (float *)malloc((size_t)H * 4), *mixed = (float *)malloc((size_t)H * 4), *resid = (float *)malloc((size_t)H * 4);
-    float *g = (float *)malloc((size_t)m->ffn * 4), *u = (float *)malloc((size_t)m->ffn * 4), *hh = (float *)malloc((size_t)m->ffn * 4);
     oracle_rmsnorm(x, L->attn_norm, H, m->eps, normed);
     if (L->attn) attention_token(m, L, K, V, pos, normed, mixed);
     else deltanet_token(m, L, st, normed, mixed);
     for (int i = 0; i < H; i++) resid[i] = x[i] + mixed[i];
     oracle_rmsnorm(resid, L->post_norm, H, m->eps, normed);
-    matvec(&L->gate, normed, g);
-    matvec(&L->up, normed, u);
-    oracle_swiglu(g, u, m->ffn, hh);
-    matvec(&L->down, hh, mixed);
+    mlp_token(m, L, normed, mixed);
     for (int i = 0; i < H; i++) y[i] = resid[i] + mixed[i];
-    free(normed); free(mixed); free(resid); free(g); free(u); free(hh);
+    free(normed); free(mixed); free(resid);
 }
 
 static void embed_row(OModel *m, uint32_t id, float *out) {
@@ -720,3 +726,86 @@ int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, 
 }
 
 int oracle_state_pos(OState *s) { return s->pos; }
+
+/* ------------------------------------------------------------------------- carried state, for the tests */
+
+/* The carried state of layer `layer` (spec_identity.rs:5-9 compares it after every round): what = 0 the DeltaNet
+ * recurrent state f32 [n_v][dk][dv], 1 its conv window f32 [conv_dim][conv_k - 1], 2 / 3 the attention K / V
+ * cache rows [0, pos) f32 [pos][n_kv * head_dim].  Returns the number of floats written (0: not this kind of
+ * layer), or the number needed when out is NULL. */
+long oracle_state_get(OState *s, int layer, int what, float *out) {
+    OModel *m = s->m;
+    if (layer < 0 || layer >= m->n_layer) return -1;
+    const OLayer *L = &m->layers[layer];
+    const OLayerState *ls = &s->ls[layer];
+    size_t n = 0;
+    const float *src = NULL;
+    if (!L->attn && what == 0) { n = (size_t)m->n_v * m->dk * m->dv; src = ls->S; }
+    else if (!L->attn && what == 1) { n = (size_t)m->conv_dim * (m->conv_k - 1); src = ls->conv; }
+    else if (L->attn && (what == 2 || what == 3)) { n = (size_t)s->pos * m->n_kv * m->hd; src = what == 2 ? ls->K : ls->V; }
+    if (out && n) memcpy(out, src, n * 4);
+    return (long)n;
+}
+
+/* --------------------------------------------------------------- one layer on caller-held F32 weights */
+
+/* The reference checks its layer code against HF module outputs on F32 weights (crates/core/tests/layers.rs:
+ * WeightMat::from_f32, a prefill of t rows, then one step on the carried state / KV cache).  This runs the
+ * oracle's own layer functions -- the ones oracle_forward_token uses -- on such weights, row by row from
+ * position pos0.  dims = {hidden, ffn, n_head, n_kv, head_dim, rope_dim, conv_kernel, dk, n_k, n_v, dv},
+ * fdims = {eps, theta}, w = OW_COUNT weight pointers (oracle.h; the ones a kind does not use may be NULL).
+ * State in and out: S [n_v][dk][dv] and conv [conv_dim][conv_kernel - 1] (DeltaNet kinds), K and V
+ * [pos][n_kv * head_dim] (attention kinds, rows pos0 .. pos0 + t - 1 written).  y: t rows of hidden. */
+int oracle_layer_f32(const int *dims, const float *fdims, const float *const *w, int kind, const float *x, int t,
+                     int pos0, float *S, float *conv, float *K, float *V, float *y) {
+    OModel m;
+    memset(&m, 0, sizeof m);
+    m.hidden = dims[0]; m.ffn = dims[1]; m.n_head = dims[2]; m.n_kv = dims[3]; m.hd = dims[4]; m.rope_dim = dims[5];
+    m.conv_k = dims[6]; m.dk = dims[7]; m.n_k = dims[8]; m.n_v = dims[9]; m.dv = dims[10];
+    m.eps = fdims[0];
+    m.theta = fdims[1];
+    m.kd = m.n_k * m.dk;
+    m.vd = m.n_v * m.dv;
+    m.conv_dim = 2 * m.kd + m.vd;
+    m.scaling = m.hd > 0 ? powf((float)m.hd, -0.5f) : 0.0f;
+    OLayer L;
+    memset(&L, 0, sizeof L);
+#define FMAT(field, idx, r, c) do { L.field.type = OT_F32; L.field.rows = (r); L.field.cols = (c); L.field.data = (const uint8_t *)w[idx]; } while (0)
+    L.attn_norm = w[OW_ATTN_NORM];
+    L.post_norm = w[OW_POST_NORM];
+    FMAT(qkv, OW_QKV, m.conv_dim, m.hidden);
+    FMAT(gate_z, OW_GATE_Z, m.vd, m.hidden);
+    FMAT(alpha, OW_ALPHA, m.n_v, m.hidden);
+    FMAT(beta, OW_BETA, m.n_v, m.hidden);
+    L.ssm_a = w[OW_SSM_A];
+    L.dt_bias = w[OW_DT_BIAS];
+    L.conv_w = w[OW_CONV];
+    L.ssm_norm = w[OW_SSM_NORM];
+    FMAT(ssm_out, OW_SSM_OUT, m.hidden, m.vd);
+    FMAT(q, OW_Q, 2 * m.n_head * m.hd, m.hidden);
+    FMAT(k, OW_K, m.n_kv * m.hd, m.hidden);
+    FMAT(v, OW_V, m.n_kv * m.hd, m.hidden);
+    FMAT(o, OW_O, m.hidden, m.n_head * m.hd);
+    L.q_norm = w[OW_Q_NORM];
+    L.k_norm = w[OW_K_NORM];
+    FMAT(gate, OW_FFN_GATE, m.ffn, m.hidden);
+    FMAT(up, OW_FFN_UP, m.ffn, m.hidden);
+    FMAT(down, OW_FFN_DOWN, m.hidden, m.ffn);
+#undef FMAT
+    OLayerState st = {S, conv, K, V};
+    L.attn = kind == OL_ATTENTION || kind == OL_DECODER_ATTENTION;
+    const size_t H = (size_t)m.hidden;
+    for (int i = 0; i < t; i++) {
+        const float *xi = x + (size_t)i * H;
+        float *yi = y + (size_t)i * H;
+        switch (kind) {
+        case OL_DELTANET: deltanet_token(&m, &L, &st, xi, yi); break;
+        case OL_ATTENTION: attention_token(&m, &L, K, V, pos0 + i, xi, yi); break;
+        case OL_MLP: mlp_token(&m, &L, xi, yi); break;
+        case OL_DECODER_DELTANET:
+        case OL_DECODER_ATTENTION: layer_token(&m, &L, &st, K, V, pos0 + i, xi, yi); break;
+        default: return -1;
+        }
+    }
+    return 0;
+}

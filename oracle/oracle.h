@@ -105,6 +105,20 @@ uint32_t oracle_sampler_sample(OSampler *s, const float *logits);
 int oracle_sampler_accept(OSampler *s, const float *target_logits, const float *q_dense, uint32_t d, uint32_t *tok_out);
 void oracle_sampler_write_dense(const OSampler *s, float *out);
 
+
+/* --- model level (model.c) --- */
+/* the carried state of one layer of an oracle state: what = 0 DeltaNet S, 1 conv window, 2 / 3 K / V rows [0, pos);
+ * returns the floats written (or needed, out NULL), 0 when the layer has no such state */
+typedef struct oracle_state OState;
+long oracle_state_get(OState *s, int layer, int what, float *out);
+
+/* one layer on caller-held F32 weights (crates/core/tests/layers.rs): weight slots and kinds */
+enum { OW_ATTN_NORM, OW_POST_NORM, OW_QKV, OW_GATE_Z, OW_ALPHA, OW_BETA, OW_SSM_A, OW_DT_BIAS, OW_CONV, OW_SSM_NORM,
+       OW_SSM_OUT, OW_Q, OW_K, OW_V, OW_O, OW_Q_NORM, OW_K_NORM, OW_FFN_GATE, OW_FFN_UP, OW_FFN_DOWN, OW_COUNT };
+enum { OL_DELTANET = 0, OL_ATTENTION = 1, OL_MLP = 2, OL_DECODER_DELTANET = 3, OL_DECODER_ATTENTION = 4 };
+int oracle_layer_f32(const int *dims, const float *fdims, const float *const *w, int kind, const float *x, int t,
+                     int pos0, float *S, float *conv, float *K, float *V, float *y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,9 @@ def lib():
             "oracle_sampler_accept": (I, [P, P, P, ctypes.c_uint32, U32P]),
             "oracle_rng_seed": (None, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint64]),
             "oracle_rng_next": (ctypes.c_uint64, [ctypes.POINTER(ctypes.c_uint64)]),
+            "oracle_state_get": (ctypes.c_long, [P, I, I, P]),
+            "oracle_layer_f32": (I, [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_float),
+                                     ctypes.POINTER(ctypes.c_void_p), I, P, I, I, P, P, P, P, P]),
         })
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -327,6 +330,47 @@ def crc32(b):
     return lib().oracle_crc32(_p(b), b.size)
 
 
+# weight slots of oracle_layer_f32 (oracle.h OW_*), by GGUF tensor name
+LAYER_WEIGHTS = ("attn_norm.weight", "post_attention_norm.weight", "attn_qkv.weight", "attn_gate.weight",
+                 "ssm_alpha.weight", "ssm_beta.weight", "ssm_a", "ssm_dt.bias", "ssm_conv1d.weight", "ssm_norm.weight",
+                 "ssm_out.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
+                 "attn_q_norm.weight", "attn_k_norm.weight", "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight")
+LAYER_KINDS = {"deltanet": 0, "attention": 1, "mlp": 2, "decoder_deltanet": 3, "decoder_attention": 4}
+
+
+class LayerF32:
+    """One layer of the oracle (the functions oracle_forward_token runs) on caller-held F32 weights, as the
+    reference's crates/core/tests/layers.rs loads them (WeightMat::from_f32): `dims` = dict(hidden, ffn, n_head,
+    n_kv, head_dim, rope_dim, conv_kernel, dk, n_k, n_v, dv, eps, theta); `weights` = GGUF name -> f32 array.
+    The carried state (S, conv window, K and V rows) lives in this object across calls."""
+
+    def __init__(self, kind, dims, weights, max_pos=64):
+        self.kind = LAYER_KINDS[kind]
+        self.d = dims
+        self._w = [np.ascontiguousarray(weights[n], np.float32) if n in weights else None for n in LAYER_WEIGHTS]
+        self._wp = (ctypes.c_void_p * len(LAYER_WEIGHTS))(*[(_p(a).value if a is not None else None) for a in self._w])
+        self._dims = (ctypes.c_int * 11)(*[int(dims[k]) for k in ("hidden", "ffn", "n_head", "n_kv", "head_dim", "rope_dim",
+                                                                  "conv_kernel", "dk", "n_k", "n_v", "dv")])
+        self._f = (ctypes.c_float * 2)(dims["eps"], dims["theta"])
+        conv_dim = 2 * dims["n_k"] * dims["dk"] + dims["n_v"] * dims["dv"]
+        self.S = np.zeros((max(dims["n_v"], 1), max(dims["dk"], 1), max(dims["dv"], 1)), np.float32)
+        self.conv = np.zeros((max(conv_dim, 1), max(dims["conv_kernel"] - 1, 1)), np.float32)
+        kvd = max(dims["n_kv"] * dims["head_dim"], 1)
+        self.K = np.zeros((max_pos, kvd), np.float32)
+        self.V = np.zeros((max_pos, kvd), np.float32)
+        self.pos = 0
+
+    def __call__(self, x):
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, self.d["hidden"])
+        y = np.empty_like(x)
+        rc = lib().oracle_layer_f32(self._dims, self._f, self._wp, self.kind, _p(x), x.shape[0], self.pos, _p(self.S),
+                                    _p(self.conv), _p(self.K), _p(self.V), _p(y))
+        if rc != 0:
+            raise ValueError("oracle_layer_f32 failed")
+        self.pos += x.shape[0]
+        return y
+
+
 class OracleModel:
     """The reference's model seam restated on the CPU (oracle/model.c): forward_token, the plain greedy loop and
     the greedy --spec k loop, over a GGUF read through mmap."""
@@ -379,6 +423,15 @@ class OracleState:
         if rc != 0:
             raise ValueError("oracle: forward_token failed (id out of range or sequence full)")
         return lg, cap
+
+    def carried(self, layer, what):
+        """The carried state of `layer` (0 DeltaNet S, 1 conv window, 2 K rows, 3 V rows [0, pos)), or None."""
+        n = lib().oracle_state_get(self._h, layer, what, None)
+        if n <= 0:
+            return None
+        out = np.empty(n, np.float32)
+        lib().oracle_state_get(self._h, layer, what, _p(out))
+        return out
 
     def generate(self, prompt, n_out, stop=True, sampler=None):
         out = (ctypes.c_uint32 * n_out)()

@@ -164,6 +164,36 @@ def main(ref):
             arrs[base + "__deq"] = np.load(os.path.join(d, base + ".npy")).astype(np.float32)
     save("dequant", arrs, {"spec": m["spec"], "types": types, "hostile": hostile})
 
+    # --- layers: HF module outputs on F32 weights (tests/fixtures/layers/layers, checked by
+    # crates/core/tests/layers.rs): every case's weights, prefill and step arrays, copied whole
+    d = os.path.join(fx, "layers", "layers")
+    m = load_manifest(d)
+    arrs, cases = {}, []
+    for c in m["cases"]:
+        cc = {}
+        for k, v in c.items():
+            if k == "weights":
+                cc[k] = {}
+                for wn, wf in v.items():
+                    arrs[c["case"] + "__w__" + wn] = npy(d, wf).astype(np.float32)
+                    cc[k][wn] = {"shape": wf["shape"]}
+            elif k in ("prefill", "step"):
+                cc[k] = {}
+                for fk, fv in v.items():
+                    if isinstance(fv, dict) and "file" in fv:
+                        arrs[c["case"] + "__" + k + "__" + fk] = npy(d, fv).astype(np.float32)
+                        cc[k][fk] = {"shape": fv["shape"]}
+                    else:
+                        cc[k][fk] = fv
+            else:
+                cc[k] = v
+        cases.append(cc)
+    meta = {k: v for k, v in m.items() if k != "cases"}
+    meta["cases"] = cases
+    save("layers", arrs, meta)
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the reference project root>")
+    main(sys.argv[1])
