@@ -168,7 +168,19 @@ def oracle_spec_sample(path, k, prompt_len, rounds):
     secs = stats["round_seconds"]
     emitted = len(ids) - 1
     om.close()
+    stats["prompt"], stats["ids"] = prompt, ids
     return emitted / secs, secs / max(1, stats["rounds"]), stats, cores
+
+
+def gpu_spec_ids(model, k, prompt, n_ids):
+    """The GPU's --spec k ids for `prompt` (spec_prefill, then rounds until n_ids ids): the ids the parity object
+    compares with the CPU leg's."""
+    import qdec
+
+    st = model.new_state(spec_k=k, max_rows=32)
+    ids = qdec.generate_spec(st, prompt, n_ids, stop=False)
+    st.free()
+    return ids
 
 
 def run_reference_spec(args, world, rank):
@@ -742,9 +754,14 @@ def run_spec_qdec(args, world, rank, local):
             tp_res["round_frac_per_rank"] = round(b / s_r / 1e9 / peak, 4)
         line["tp"] = tp_res
     if world == 1 and not args.no_cpu_baseline:
-        tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 1)
+        tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 2)
         line["cpu_baseline"] = {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port",
-                                "sample": f"1 --spec {k} round after a 2-token prompt ({s_rnd:.1f} s/round)"}
+                                "sample": f"{stats['rounds']} --spec {k} rounds after a 2-token prompt ({s_rnd:.1f} s/round)"}
+        # parity on the full 27B checkpoint: the GPU's ids for the CPU leg's prompt and round count
+        want = stats["ids"]
+        got = gpu_spec_ids(model, k, stats["prompt"], len(want))
+        line["parity"] = {"ids_equal": got == want, "n_ids": len(want), "prompt_len": len(stats["prompt"]),
+                          "against": "the CPU oracle's --spec 3 loop on the same checkpoint (the cpu_baseline run)"}
     print(json.dumps(line), flush=True)
 
 

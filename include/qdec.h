@@ -231,6 +231,13 @@ int qdec_spec_counters(const qdec_state *s, uint64_t out4[4]);
 int qdec_set_capture(qdec_state *s, int on);
 int qdec_debug_hidden(qdec_state *s, int layer, int row, float *out);
 int qdec_debug_logits(qdec_state *s, int row, float *out);
+/* The carried state of layer `layer` after the last call, as the reference's State holds it (the deferred rows
+ * of the last forward applied on a copy; the state itself is not changed) -- what the reference's
+ * crates/core/tests/spec_identity.rs:5-9 compares after every round: what = 0 the DeltaNet recurrent state
+ * f32 [n_v][dk][dv], 1 its conv window f32 [conv channels][conv_kernel - 1], 2 / 3 the K / V cache rows
+ * [0, pos) f32 [pos][n_kv][head_dim] (a tensor-parallel rank: its own heads).  *n_floats: in, the capacity of
+ * `out`; out, the floats written -- or, with out NULL, the floats needed (0 when the layer holds no such state). */
+int qdec_debug_state(qdec_state *s, int layer, int what, float *out, size_t *n_floats);
 
 /* Write a synthetic Qwen3.8-style GGUF (preset "tiny", "27b" or "27b-L<n>") seeded with `seed`, with
  * `threads` host threads (0 = all): the stand-in checkpoint of the benchmarks and parity tests. */

@@ -414,12 +414,13 @@ class OracleState:
     def pos(self):
         return lib().oracle_state_pos(self._h)
 
-    def forward_token(self, tok, capture=False):
-        """Returns (logits, captured per-layer residual rows [n_layer + 1][hidden] or None)."""
+    def forward_token(self, tok, capture=False, logits=True):
+        """Returns (logits or None, captured per-layer residual rows [n_layer + 1][hidden] or None); with
+        logits=False the lm_head is skipped (a prompt row)."""
         m = self.model
-        lg = np.empty(m.vocab, np.float32)
+        lg = np.empty(m.vocab, np.float32) if logits else None
         cap = np.empty((m.n_layer + 1, m.hidden), np.float32) if capture else None
-        rc = lib().oracle_forward_token(self._h, tok, _p(lg), _p(cap) if capture else None, None)
+        rc = lib().oracle_forward_token(self._h, tok, _p(lg) if logits else None, _p(cap) if capture else None, None)
         if rc != 0:
             raise ValueError("oracle: forward_token failed (id out of range or sequence full)")
         return lg, cap

@@ -268,6 +268,14 @@ int qdec_set_capture(qdec_state* s, int on) {
     return QDEC_OK;
 }
 
+int qdec_debug_state(qdec_state* s, int layer, int what, float* out, size_t* n_floats) {
+    if (!s || !n_floats) return qdec::fail(QDEC_EINVAL, "qdec_debug_state: bad argument");
+    return guard("qdec_debug_state", [&] {
+        *n_floats = s->s->debug_state(layer, what, out, *n_floats);
+        return QDEC_OK;
+    });
+}
+
 int qdec_debug_hidden(qdec_state* s, int layer, int row, float* out) {
     if (!s || !out) return qdec::fail(QDEC_EINVAL, "qdec_debug_hidden: bad argument");
     return guard("qdec_debug_hidden", [&] {

@@ -74,6 +74,37 @@ __global__ void spec_accept_kernel(const int32_t* __restrict__ argmax, const int
     *sel = keep - 1;
 }
 
+// The committed DeltaNet state with the `*keep` pending rows of the last call applied (the commit of
+// deltanet_halves_kernel: S *= decay_i, then S += k_i (x) delta_i, per row in order), into `out`; one thread per
+// state element.
+__global__ void debug_commit_state_kernel(const float* __restrict__ S, const float* __restrict__ pend_decay,
+                                          const float* __restrict__ pend_k, const float* __restrict__ pend_delta,
+                                          const int* __restrict__ keep, int n_v, int dk, int dv, float* __restrict__ out) {
+    const size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (e >= (size_t)n_v * dk * dv) return;
+    const int j = (int)(e % dv), k = (int)((e / dv) % dk), p = (int)(e / ((size_t)dk * dv));
+    float v = S[e];
+    for (int i = 0; i < *keep; i++) {
+        v = __fmul_rn(v, pend_decay[(size_t)i * n_v + p]);
+        v = __fadd_rn(v, __fmul_rn(pend_k[((size_t)i * n_v + p) * dk + k], pend_delta[((size_t)i * n_v + p) * dv + j]));
+    }
+    out[e] = v;
+}
+
+// The conv window with the `*keep` pending inputs shifted in (conv_step_kernel's commit), into `out`.
+__global__ void debug_commit_conv_kernel(const float* __restrict__ state, const float* __restrict__ pend_x,
+                                         const int* __restrict__ keep, int channels, int K, float* __restrict__ out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= channels) return;
+    float st[8];
+    for (int j = 0; j < K - 1; j++) st[j] = state[(size_t)c * (K - 1) + j];
+    for (int i = 0; i < *keep; i++) {
+        for (int j = 0; j < K - 2; j++) st[j] = st[j + 1];
+        if (K >= 2) st[K - 2] = pend_x[(size_t)i * channels + c];
+    }
+    for (int j = 0; j < K - 1; j++) out[(size_t)c * (K - 1) + j] = st[j];
+}
+
 // dst[0..n) = src rows[*sel][0..n)
 __global__ void select_row_kernel(const float* __restrict__ src, const int* __restrict__ sel, int n, float* __restrict__ dst) {
     const float* r = src + (size_t)(*sel) * n;
@@ -914,6 +945,44 @@ void State::debug_hidden(int layer, int row, float* out) {
     if (!capture_ || capture_h_.empty() || layer < 0 || layer > (int)m_.layers.size()) throw std::invalid_argument("debug_hidden: no capture");
     ck(cudaStreamSynchronize(stream), "sync");
     ck(cudaMemcpy(out, capture_h_[layer] + (size_t)row * m_.cfg.hidden_size, m_.cfg.hidden_size * 4, cudaMemcpyDeviceToHost), "capture");
+}
+
+size_t State::debug_state(int layer, int what, float* out, size_t cap) {
+    const ModelConfig& c = m_.cfg;
+    const TpPlan& P = m_.tp;
+    if (layer < 0 || layer >= (int)m_.layers.size()) throw std::invalid_argument("debug_state: no such layer");
+    const LayerW& L = m_.layers[layer];
+    size_t n = 0;
+    if (!L.attn && (what == 0 || what == 1)) {
+        n = what == 0 ? (size_t)P.nv * c.dn_head_dim_k * c.dn_head_dim_v : (size_t)L.qkv.rows * (c.dn_conv_kernel - 1);
+    } else if (L.attn && (what == 2 || what == 3)) {
+        n = (size_t)pos_ * P.nkv * c.head_dim_k;
+    }
+    if (!out || n == 0) return n;
+    if (cap < n) throw std::invalid_argument("debug_state: output buffer too small");
+    ck(cudaStreamSynchronize(stream), "sync");
+    if (what >= 2) {
+        const KvState& kv = kv_[layer];
+        ck(cudaMemcpy(out, what == 2 ? kv.k : kv.v, n * 4, cudaMemcpyDeviceToHost), "kv rows");
+        return n;
+    }
+    const DnState& d = dn_[layer];
+    float* tmp = nullptr;
+    ck(cudaMalloc(&tmp, n * 4), "debug buffer");
+    cudaError_t e;
+    if (what == 0) {
+        debug_commit_state_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+            d.S, d.pend_decay, d.pend_k, d.pend_delta, d_keep, P.nv, (int)c.dn_head_dim_k, (int)c.dn_head_dim_v, tmp);
+    } else {
+        debug_commit_conv_kernel<<<(L.qkv.rows + 255) / 256, 256, 0, stream>>>(d.conv, d.pend_x, d_keep, L.qkv.rows,
+                                                                               (int)c.dn_conv_kernel, tmp);
+    }
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess) e = cudaMemcpy(out, tmp, n * 4, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    ck(e, "debug state");
+    return n;
 }
 
 // The MTP block over t rows (layers/mtp.rs:95-130): row i is [rmsnorm(embed(ids[i]), enorm) |

@@ -138,6 +138,13 @@ class State {
     // (layer = n_layer: the post-final-norm row the lm_head read)
     void debug_hidden(int layer, int row, float* out);
     void set_capture(bool on) { capture_ = on; }
+    // parity: the carried state of layer `layer` as the reference holds it after the last call -- the DeltaNet
+    // rows this engine commits lazily (the accepted rows of the last forward) applied to a copy.  what = 0: the
+    // DeltaNet state f32 [n_v][dk][dv]; 1: its conv window f32 [channels][conv_kernel - 1]; 2 / 3: the K / V
+    // cache rows [0, pos) f32 [pos][n_kv][head_dim] (this rank's heads over tensor parallelism).  Returns the
+    // floats of the result (0: the layer has no such state); copies them to `out` when it is non-null and
+    // holds `cap` floats.
+    size_t debug_state(int layer, int what, float* out, size_t cap);
     void logits_row(int row, float* out) const;
 
     int pos() const { return pos_; }

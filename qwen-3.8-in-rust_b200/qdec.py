@@ -102,6 +102,7 @@ def lib():
             "qdec_set_capture": [P, I],
             "qdec_debug_hidden": [P, I, I, P],
             "qdec_debug_logits": [P, I, P],
+            "qdec_debug_state": [P, I, I, P, ctypes.POINTER(S)],
             "qdec_synth_gguf": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, I],
         }.items():
             fn = getattr(L, name)
@@ -385,6 +386,19 @@ class State:
 
         out = np.empty(self.model.info.hidden, np.float32)
         _check(lib().qdec_debug_hidden(self._h, layer, row, out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def carried(self, layer, what):
+        """The carried state of `layer` after the last call (what: 0 DeltaNet state, 1 conv window, 2 K rows,
+        3 V rows [0, pos)) as a float32 array, or None when the layer holds no such state."""
+        import numpy as np
+
+        n = ctypes.c_size_t(0)
+        _check(lib().qdec_debug_state(self._h, layer, what, None, ctypes.byref(n)))
+        if n.value == 0:
+            return None
+        out = np.empty(n.value, np.float32)
+        _check(lib().qdec_debug_state(self._h, layer, what, out.ctypes.data_as(ctypes.c_void_p), ctypes.byref(n)))
         return out
 
     def logits(self, row=0):

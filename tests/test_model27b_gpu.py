@@ -1,0 +1,179 @@
+"""GPU parity at the 27B dimensions against the CPU oracle, on the `27b-L4` synthetic checkpoint: the full 27B
+widths (hidden 5120, DeltaNet 16 K / 48 V heads of 128, GQA 24 q / 4 kv heads of 256 with rope_dim 64 in sections
+{11, 11, 10}, FFN 17408, vocabulary 248320, the Q4_K_M type recipe, the MTP block) with 4 layers (3 DeltaNet + 1
+attention).  This runs the kernels the headline runs -- deltanet_halves<128>, head_dim-256 attention, the
+248320-row lm_head and argmax -- against the oracle:
+
+  - every layer's residual row, the post-final-norm row and the logits, bit for bit, over 6 positions;
+  - greedy ids after a batched prompt (the prefill's multi-row path);
+  - --spec 3 ids (equal to plain decoding and to the oracle's spec loop, with the same round / accept counts);
+  - forced drafts reaching every acceptance count 0..3, and after every round the whole carried state (DeltaNet
+    states, conv windows, KV rows [0, pos), position) bit-identical to a plain state that stepped through the
+    same tokens -- the reference's crates/core/tests/spec_identity.rs:1-9 -- and, at the end, to the oracle's.
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+PRESET = "27b-L4"
+SEED = 20261201
+K = 3
+MAX_POS = 512
+
+
+def _prompt(n, seed):
+    return [int(v) for v in np.random.default_rng(seed).integers(0, 248044, n)]
+
+
+@pytest.fixture(scope="module")
+def ck27(tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import qdec
+
+    base = "/dev/shm" if os.path.isdir("/dev/shm") else str(tmp_path_factory.mktemp("ck27"))
+    path = os.path.join(base, f"qdec_test_{PRESET}_{SEED}_{os.getpid()}.gguf")
+    qdec.synth_gguf(path, PRESET, SEED)
+    yield path
+    os.remove(path)
+
+
+@pytest.fixture(scope="module")
+def m27(ck27):
+    import qdec
+
+    m = qdec.Model(ck27, max_pos=MAX_POS)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def o27(ck27, orc):
+    orc.set_threads(os.cpu_count() or 1)
+    om = orc.OracleModel(ck27)
+    yield om
+    om.close()
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_27b_dimensions(m27):
+    i = m27.info
+    assert (i.hidden, i.ffn, i.vocab, i.n_head, i.n_head_kv, i.head_dim) == (5120, 17408, 248320, 24, 4, 256)
+    assert (i.dn_n_k_heads, i.dn_n_v_heads, i.dn_head_dim_k, i.dn_head_dim_v, i.n_layer, i.has_mtp) == (16, 48, 128, 128, 4, 1)
+
+
+def test_hidden_states_and_logits_bit_exact_27b(m27, o27):
+    """Every layer's residual row, the post-final-norm row and the logits at 6 positions, bit for bit."""
+    st = m27.new_state(max_rows=1)
+    st.set_capture(True)
+    os_ = o27.state(MAX_POS)
+    for pos, tok in enumerate(_prompt(6, SEED + 11)):
+        st.step(tok)
+        lg, cap = os_.forward_token(tok, capture=True)
+        for layer in range(m27.info.n_layer + 1):
+            h = st.hidden(layer)
+            bad = np.flatnonzero(_bits(h) != _bits(cap[layer]))
+            assert bad.size == 0, f"layer {layer} at position {pos}: {bad.size} of 5120 differ (first {bad[:4]})"
+        g = st.logits(0)
+        bad = np.flatnonzero(_bits(g) != _bits(lg))
+        assert bad.size == 0, f"logits at position {pos}: {bad.size} differ"
+    st.free()
+
+
+def test_greedy_ids_27b(m27, o27):
+    """An 8-token prompt prefilled as one batch, then 8 greedy tokens: the oracle's ids."""
+    import qdec
+
+    p = _prompt(8, SEED + 1)
+    want = o27.state(MAX_POS).generate(p, 8, stop=False)
+    got = qdec.generate(m27.new_state(max_rows=32), p, 8, stop=False)
+    assert got == want
+
+
+def test_spec3_ids_27b(m27, o27):
+    """--spec 3: ids equal plain decoding and the oracle's spec loop, with its round and acceptance counts."""
+    import qdec
+
+    p = _prompt(6, SEED + 2)
+    n = 6
+    plain = qdec.generate(m27.new_state(max_rows=32), p, n, stop=False)
+    st = m27.new_state(spec_k=K, max_rows=32)
+    got = qdec.generate_spec(st, p, n, stop=False)
+    assert got == plain
+    want, stats, _ = o27.state(MAX_POS).spec_generate(p, n, K, stop=False)
+    assert want == plain
+    c = st.counters()
+    assert c["rounds"] == stats["rounds"] and c["accepted"] == stats["accepted"]
+
+
+def _carried(st, n_layer):
+    out = {}
+    for layer in range(n_layer):
+        for what in range(4):
+            v = st.carried(layer, what)
+            if v is not None:
+                out[(layer, what)] = v
+    return out
+
+
+def test_forced_drafts_every_acceptance_count_and_carried_state_27b(m27, o27):
+    """Forced drafts (the plain run's next tokens, one wrong at position j, so exactly j are accepted) reach every
+    acceptance count; after every round the spec state's whole carried state equals, bit for bit, that of a plain
+    state stepped through the same tokens (spec_identity.rs:5-9), and the ids equal plain decoding and the
+    oracle's spec loop under the same forced drafts; the final carried state equals the oracle's."""
+    import qdec
+
+    n_layer = m27.info.n_layer
+    p = _prompt(5, SEED + 3)
+    n_tokens = 12
+    plain_ids = qdec.generate(m27.new_state(max_rows=32), p, n_tokens + K + 2, stop=False)
+    st = m27.new_state(spec_k=K, max_rows=32)
+    ref = m27.new_state(max_rows=32)  # the plain state, stepped through the tokens the spec state consumes
+    seq = [st.spec_prefill(p)]
+    assert ref.prefill(p) == seq[0]
+    consumed = list(p)
+    forced, hist, r = [], [0] * (K + 1), 0
+    while len(seq) < n_tokens:
+        want = plain_ids[len(seq):len(seq) + K]
+        miss = r % (K + 1)
+        d = list(want)
+        if miss < K:
+            d[miss] = (d[miss] + 1) % 248044
+        forced.append(d)
+        st.set_drafts(d)
+        x_p = seq[-1]
+        em = st.spec_round(x_p)
+        assert len(em) == miss + 1 if miss < K else len(em) == K + 1
+        hist[len(em) - 1] += 1
+        fed = [x_p] + em[:-1]  # the rows the round kept: x_p and the accepted drafts
+        for tok in fed:
+            ref.step(tok)
+        consumed += fed
+        seq += em
+        r += 1
+        assert st.pos == ref.pos == len(consumed)
+        a, b = _carried(st, n_layer), _carried(ref, n_layer)
+        assert a.keys() == b.keys() and len(a) == 3 * 2 + 2
+        for key in a:
+            bad = np.flatnonzero(_bits(a[key]) != _bits(b[key]))
+            assert bad.size == 0, f"round {r}: carried state {key} differs from the plain state's in {bad.size} places"
+    assert seq[:n_tokens] == plain_ids[:n_tokens]
+    assert all(h > 0 for h in hist), hist
+    want, stats, _ = o27.state(MAX_POS).spec_generate(p, len(seq), K, stop=False, forced=forced)
+    assert want[: len(seq)] == seq
+    # the final carried state against the oracle's after the same tokens
+    ost = o27.state(MAX_POS)
+    for tok in consumed:
+        ost.forward_token(tok, logits=False)
+    for (layer, what), v in _carried(st, n_layer).items():
+        o = ost.carried(layer, what)
+        assert o is not None and o.size == v.size, (layer, what)
+        bad = np.flatnonzero(_bits(v) != _bits(o))
+        assert bad.size == 0, f"carried state {(layer, what)} differs from the oracle's in {bad.size} places"
