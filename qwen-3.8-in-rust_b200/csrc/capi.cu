@@ -237,7 +237,14 @@ int qdec_tune_gemv(int impl, int config) {
         set_gemm_tc_min_cols(config);
         return QDEC_OK;
     }
-    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 8 or 9");
+    if (impl == 7) {  // the decode GEMV of tile matrices: 0 automatic by shape, 1..10 a fixed configuration
+        if (config < 0 || config > 10) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..10");
+        set_gemv_impl(0);
+        set_gemv7_config(config);
+        return QDEC_OK;
+    }
+    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 7, 8 or 9");
+    if (impl == 0) set_gemv7_config(0);
     if (config < 0 || config > 35) return fail(QDEC_EINVAL, "gemv configuration must be 0..35");
     set_gemv_impl(impl);
     set_gemv_v6_config(config);

@@ -1,0 +1,466 @@
+// The decode GEMV of K-quant tile matrices (Q4_K, Q5_K, Q6_K in the tile layout) against 1..4 Q8_K image
+// columns: the verify pass's ffn / attention / DeltaNet projections and the drafts' lm_head.  Bit-exact with
+// crates/core/src/kernels/kdot.rs:37-141 (single row) and :176-333 (blocked), which is what matvec / matmul_t
+// compute per row and column.
+//
+// Arithmetic.  The reference keeps, per row, column and super-block, eight exact i32 lanes (lane g = positions
+// 4g..4g+3 of every 32-element chunk) with the chunk scale multiplied in, converts each lane once to f32, and
+// accumulates d * lane into an 8-lane f32 chain over the super-blocks (plus, for Q4_K / Q5_K, four min lanes
+// -dx * dmin * (mn[2i] q8s[2i] + mn[2i+1] q8s[2i+1])); the row's value is reduce8 + reduce4 of the chains.
+// Here each lane's integer sum is built with 8 dp4a (one per 32-element chunk, exact), the eight chunk results
+// packed two per register as 16-bit halves (PRMT) and scaled by their chunk scales with 4 dp2a straight from
+// the packed scale bytes -- two multiply-adds per instruction, and no per-scale unpacking.  Q4_K / Q5_K chunk
+// results are biased by 2^15 into unsigned halves and the bias (2^15 * sum of the scales) is folded into the
+// accumulator's start; Q6_K results fit signed halves.  For Q4_K the start also carries 1.5 * 2^23, so the
+// finished sum read as a float minus 1.5 * 2^23 is the lane as f32 (|lane| < 2^22); Q5_K and Q6_K lanes (which
+// may exceed that) are converted with a rounding I2F, as the reference's `as f32`.  All integer steps are exact,
+// so the f32 operations are the reference's, in its order.
+//
+// Work split.  Four threads share a weight row (thread tg holds lanes 2tg, 2tg+1 and min lane tg), eight rows
+// make a tile (one tile block per super-block: 8 x the block bytes, contiguous, in the order the threads read
+// it), a warp owns R tiles.  A CTA of S warps splits the super-block range: warp w takes super-blocks w, w+S, ...
+// (S = 1: every chain stays in the owning thread's registers).  With S > 1 each warp writes its f32 lane terms
+// (d * lane) to shared memory and, after every window of S super-blocks, one owner thread per (tile, column,
+// row, lane) adds the window's terms in super-block order -- the reference's own chain of additions.  Short
+// matrices (5120 rows) take S > 1 so that enough warps stream their weights.
+//
+// Data movement.  Weight bytes stream from HBM into registers with 16-byte non-allocating loads, D super-blocks
+// ahead per warp (a register ring; every warp-wide load is 512 contiguous bytes); the first D are requested
+// before griddepcontrol.wait, so the stream overlaps the kernel that produced the activations (weights are
+// never written after load).  Activation words are read through L1 (every warp of an SM reads the same few KB),
+// once per super-block and column for all R tiles of the warp.
+#include <algorithm>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace qdec {
+
+namespace {
+
+constexpr uint32_t G7_MAGIC_I = 0x4B400000u;  // bits of 12582912.0f = 1.5 * 2^23
+constexpr float G7_MAGIC_F = 12582912.0f;
+
+template <int TYPE>
+struct G7 {
+    static constexpr int TB = TYPE == T_Q4_K ? 1152 : TYPE == T_Q5_K ? 1408 : 1680;  // tile block bytes
+    static constexpr bool MINS = TYPE != T_Q6_K;
+    static constexpr int LPC = MINS ? 12 : 8;  // f32 chains per (row, column): 8 lanes (+ 4 min lanes)
+};
+
+// One thread's share of a tile block (tile layout, gemv_v6.cu): thread L = 4 * row + tg.
+template <int TYPE>
+struct W7;
+template <>
+struct W7<T_Q4_K> {
+    uint4 c0, c1, hdr;  // code chunks (qs groups 0,1 | 2,3: 8 bytes of each at 8tg), header of the row
+};
+template <>
+struct W7<T_Q5_K> {
+    uint4 c0, c1, hdr;
+    uint2 qh;  // qh bytes 16 + 8tg .. +8 (bit s: the fifth bit of chunk s)
+};
+template <>
+struct W7<T_Q6_K> {
+    uint4 c0, c1, c2, sc;  // ql 8tg | ql 32+8tg; ql 64+8tg | ql 96+8tg; qh 128+8tg | qh 160+8tg; the row's scales
+    uint32_t d;           // the row's f16 d (low half)
+};
+
+__device__ __forceinline__ uint2 ld_nc_u64_(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+template <int TYPE>
+__device__ __forceinline__ void load_w7(const uint8_t* ts, int L, int rs, W7<TYPE>& f) {
+    f.c0 = ld_nc_u128(ts + L * 16);
+    f.c1 = ld_nc_u128(ts + 512 + L * 16);
+    if constexpr (TYPE == T_Q4_K) {
+        f.hdr = ld_nc_u128(ts + 1024 + rs * 16);
+    } else if constexpr (TYPE == T_Q5_K) {
+        f.qh = ld_nc_u64_(ts + 1024 + L * 8);
+        f.hdr = ld_nc_u128(ts + 1280 + rs * 16);
+    } else {
+        f.c2 = ld_nc_u128(ts + 1024 + L * 16);
+        f.sc = ld_nc_u128(ts + 1536 + rs * 16);
+        f.d = ld_nc_u16(ts + 1664 + rs * 2);
+    }
+}
+
+// The row-dependent decode of one super-block, shared by every column.
+template <int TYPE>
+struct Dec7 {
+    uint32_t code[8][2];  // chunk s, lane 2tg+gi: four codes as bytes
+    uint32_t scw[2];      // chunk scales as bytes: Q4_K/Q5_K sc0..3 | sc4..7; Q6_K this thread's chunk scales per half
+    uint32_t start;       // the lane accumulator's start (bias terms)
+    uint32_t spair;       // Q6_K: the row's scale bytes 4tg .. 4tg+3 (the -32 bsum correction of lanes 2tg, 2tg+1)
+    uint32_t mpair;       // Q4_K/Q5_K: the mins of chunks 2tg, 2tg+1 in bytes 0, 1
+    float dw, dminw;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void decode7(const W7<TYPE>& f, int tg, Dec7<TYPE>& o) {
+    if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        const uint32_t qs[4][2] = {{f.c0.x, f.c0.y}, {f.c0.z, f.c0.w}, {f.c1.x, f.c1.y}, {f.c1.z, f.c1.w}};
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+#pragma unroll
+            for (int gi = 0; gi < 2; gi++) {
+                o.code[2 * p][gi] = qs[p][gi] & 0x0F0F0F0Fu;
+                o.code[2 * p + 1][gi] = (qs[p][gi] >> 4) & 0x0F0F0F0Fu;
+            }
+        if constexpr (TYPE == T_Q5_K) {
+            const uint32_t qh[2] = {f.qh.x, f.qh.y};
+#pragma unroll
+            for (int s = 0; s < 8; s++)
+#pragma unroll
+                for (int gi = 0; gi < 2; gi++) o.code[s][gi] |= ((qh[gi] >> s) & 0x01010101u) << 4;
+        }
+        // get_scale_min_k4 (quant.rs:45-51) on all eight chunks at once: hdr bytes 4..15 are q[0..11]
+        o.scw[0] = f.hdr.y & 0x3F3F3F3Fu;
+        o.scw[1] = (f.hdr.w & 0x0F0F0F0Fu) | ((f.hdr.y >> 2) & 0x30303030u);
+        const uint32_t mw = tg < 2 ? (f.hdr.z & 0x3F3F3F3Fu) : (((f.hdr.w >> 4) & 0x0F0F0F0Fu) | ((f.hdr.z >> 2) & 0x30303030u));
+        o.mpair = mw >> (16 * (tg & 1));
+        const uint32_t ssum = (uint32_t)__dp4a((int)o.scw[0], 0x01010101, __dp4a((int)o.scw[1], 0x01010101, 0));
+        o.start = (TYPE == T_Q4_K ? G7_MAGIC_I : 0u) - 32768u * ssum;  // mod 2^32
+        o.dw = f16_bits_to_f32((uint16_t)(f.hdr.x & 0xffff));
+        o.dminw = f16_bits_to_f32((uint16_t)(f.hdr.x >> 16));
+    } else {
+        const uint32_t ql[4][2] = {{f.c0.x, f.c0.y}, {f.c0.z, f.c0.w}, {f.c1.x, f.c1.y}, {f.c1.z, f.c1.w}};
+        const uint32_t qh[2][2] = {{f.c2.x, f.c2.y}, {f.c2.z, f.c2.w}};
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int gi = 0; gi < 2; gi++) {
+                    const uint32_t lo = (ql[2 * h + (k & 1)][gi] >> (4 * (k >> 1))) & 0x0F0F0F0Fu;
+                    const uint32_t hi = ((qh[h][gi] >> (2 * k)) & 0x03030303u) << 4;
+                    o.code[4 * h + k][gi] = lo | hi;
+                }
+        // chunk (h, k) of lane 2tg+gi takes scale byte 8h + 2k + (tg >> 1) (kdot.rs:117, sc[2k + l/16])
+        const uint32_t sel = (tg >> 1) ? 0x7531u : 0x6420u;
+        o.scw[0] = __byte_perm(f.sc.x, f.sc.y, sel);
+        o.scw[1] = __byte_perm(f.sc.z, f.sc.w, sel);
+        const uint32_t scv[4] = {f.sc.x, f.sc.y, f.sc.z, f.sc.w};
+        o.spair = scv[tg];
+        o.start = 0u;
+        o.dw = f16_bits_to_f32((uint16_t)(f.d & 0xffff));
+    }
+}
+
+__device__ __forceinline__ uint32_t dp2a_lo_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("dp2a.lo.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t dp2a_hi_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("dp2a.hi.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ int dp2a_lo_s(uint32_t a, uint32_t b, int c) {
+    int r;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ int dp2a_hi_s(uint32_t a, uint32_t b, int c) {
+    int r;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// The exact integer lane gi of one row, super-block and column, as f32 (the reference's `sumi[g] as f32`).
+template <int TYPE>
+__device__ __forceinline__ float lane7(const Dec7<TYPE>& o, const uint32_t* xw, int gi, uint32_t bsp) {
+    if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int a = __dp4a((int)o.code[2 * p][gi], (int)xw[gi * 8 + 2 * p], 32768);
+            const int b = __dp4a((int)o.code[2 * p + 1][gi], (int)xw[gi * 8 + 2 * p + 1], 32768);
+            pk[p] = __byte_perm((uint32_t)a, (uint32_t)b, 0x5410);
+        }
+        uint32_t s = dp2a_lo_u(pk[0], o.scw[0], o.start);
+        s = dp2a_hi_u(pk[1], o.scw[0], s);
+        s = dp2a_lo_u(pk[2], o.scw[1], s);
+        s = dp2a_hi_u(pk[3], o.scw[1], s);
+        if constexpr (TYPE == T_Q4_K) return __fsub_rn(__uint_as_float(s), G7_MAGIC_F);
+        else return __int2float_rn((int)s);
+    } else {
+        uint32_t pk[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int a = __dp4a((int)o.code[2 * p][gi], (int)xw[gi * 8 + 2 * p], 0);
+            const int b = __dp4a((int)o.code[2 * p + 1][gi], (int)xw[gi * 8 + 2 * p + 1], 0);
+            pk[p] = __byte_perm((uint32_t)a, (uint32_t)b, 0x5410);
+        }
+        // chunks (h, 2j), (h, 2j+1) pair with the scale bytes 2j, 2j+1 of half h
+        int s = dp2a_lo_s(pk[0], o.scw[0], 0);
+        s = dp2a_hi_s(pk[1], o.scw[0], s);
+        s = dp2a_lo_s(pk[2], o.scw[1], s);
+        s = dp2a_hi_s(pk[3], o.scw[1], s);
+        // - 32 * (bsums[2g] sc[2g] + bsums[2g+1] sc[2g+1])  (kdot.rs:128-133)
+        const int corr = gi == 0 ? dp2a_lo_s(bsp, o.spair, 0) : dp2a_hi_s(bsp, o.spair, 0);
+        return __int2float_rn(s - 32 * corr);
+    }
+}
+
+template <int TYPE, int NC, int R, int S>
+struct Smem7 {
+    static constexpr int PER_SB = R * NC * 8 * 12;                        // one warp's terms of one super-block
+    static constexpr int TERMS = S > 1 ? 2 * S * PER_SB : 1;              // double-buffered windows
+    static constexpr int FIN = S > 1 ? R * NC * 8 * 12 : 1;
+};
+
+__device__ __forceinline__ void gd_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void gd_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <int TYPE, int NC, int R, int S, int D, int MINB>
+__global__ void __launch_bounds__(32 * S, MINB)
+kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
+                int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
+    using G = G7<TYPE>;
+    using SM = Smem7<TYPE, NC, R, S>;
+    constexpr int TB = G::TB, LPC = G::LPC;
+    constexpr int CHAINS = R * NC * 8 * LPC;
+    constexpr int CPT = (CHAINS + 32 * S - 1) / (32 * S);  // chains per owner thread (S > 1)
+    __shared__ __align__(16) float terms[SM::TERMS];
+    __shared__ float fin[SM::FIN];
+    const int lane = threadIdx.x & 31, ws = threadIdx.x >> 5, rs = lane >> 2, tg = lane & 3;
+    // two matrices reading the same columns (e.g. ffn_gate and ffn_up): the CTAs of the first, then the second
+    const int ctas_a = (rows_a / 8 + R - 1) / R;
+    const bool second = (int)blockIdx.x >= ctas_a;
+    const uint8_t* w = second ? w_b : w_a;
+    const int rows = second ? rows_b : rows_a;
+    float* y = second ? y_b : y_a;
+    const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
+    const int tiles = rows / 8;
+    const uint8_t* wt[R];
+#pragma unroll
+    for (int j = 0; j < R; j++) wt[j] = w + (size_t)min(bid * R + j, tiles - 1) * nb * TB;
+
+    W7<TYPE> ring[D][R];
+#pragma unroll
+    for (int d = 0; d < D; d++) {
+        const int sb = d * S + ws;
+        if (sb < nb) {
+#pragma unroll
+            for (int j = 0; j < R; j++) load_w7<TYPE>(wt[j] + (size_t)sb * TB, lane, rs, ring[d][j]);
+        }
+    }
+    gd_wait();  // the activation image is the previous kernel's output
+    gd_launch();
+
+    float acc[R][NC][2], accm[R][NC];  // S == 1: this thread's chains
+    float cacc[CPT];                   // S > 1: the chains this thread owns
+#pragma unroll
+    for (int j = 0; j < R; j++)
+#pragma unroll
+        for (int n = 0; n < NC; n++) acc[j][n][0] = acc[j][n][1] = accm[j][n] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CPT; c++) cacc[c] = 0.0f;
+
+    const int nwin = (nb + S - 1) / S;
+    for (int w0 = 0; w0 < nwin; w0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            const int win = w0 + d;
+            if (win >= nwin) break;  // uniform over the CTA
+            const int sb = win * S + ws;
+            float* tb = terms + (size_t)((win & 1) * S + ws) * SM::PER_SB;
+            if (sb < nb) {
+                Dec7<TYPE> dec[R];
+#pragma unroll
+                for (int j = 0; j < R; j++) decode7<TYPE>(ring[d][j], tg, dec[j]);
+                if (sb + D * S < nb) {
+#pragma unroll
+                    for (int j = 0; j < R; j++) load_w7<TYPE>(wt[j] + (size_t)(sb + D * S) * TB, lane, rs, ring[d][j]);
+                }
+#pragma unroll
+                for (int n = 0; n < NC; n++) {
+                    const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+                    uint32_t xw[16];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const uint4 v = __ldg(reinterpret_cast<const uint4*>(xb + 64 * tg) + c);
+                        xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
+                    }
+                    const float dx = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
+                    uint32_t bsp = 0, q8s = 0;
+                    if constexpr (G::MINS) q8s = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
+                    else bsp = 0;  // read per lane below
+                    uint2 bsp2 = make_uint2(0, 0);
+                    if constexpr (!G::MINS) bsp2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
+#pragma unroll
+                    for (int j = 0; j < R; j++) {
+                        const float dd = __fmul_rn(dx, dec[j].dw);  // d = dx * d_w (kdot.rs:50)
+                        float t0, t1;
+                        if constexpr (G::MINS) {
+                            t0 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp));
+                            t1 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp));
+                        } else {
+                            t0 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp2.x));
+                            t1 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp2.y));
+                        }
+                        float tm = 0.0f;
+                        if constexpr (G::MINS) {  // (-dx * dmin) * (mn[2i] q8s[2i] + mn[2i+1] q8s[2i+1]), i = tg
+                            const float prod = __fsub_rn(__int_as_float(dp2a_lo_s(q8s, dec[j].mpair, (int)G7_MAGIC_I)), G7_MAGIC_F);
+                            tm = __fmul_rn(__fmul_rn(-dx, dec[j].dminw), prod);
+                        }
+                        if constexpr (S == 1) {
+                            acc[j][n][0] = __fadd_rn(acc[j][n][0], t0);
+                            acc[j][n][1] = __fadd_rn(acc[j][n][1], t1);
+                            if constexpr (G::MINS) accm[j][n] = __fadd_rn(accm[j][n], tm);
+                        } else {
+                            float* t = tb + ((j * NC + n) * 8 + rs) * 12;
+                            *reinterpret_cast<float2*>(t + 2 * tg) = make_float2(t0, t1);
+                            if constexpr (G::MINS) t[8 + tg] = tm;
+                        }
+                    }
+                }
+            }
+            if constexpr (S > 1) {
+                __syncthreads();
+                // the owners add this window's terms in super-block order
+                const float* tw = terms + (size_t)(win & 1) * S * SM::PER_SB;
+                const int nsb = min(S, nb - win * S);
+#pragma unroll
+                for (int c = 0; c < CPT; c++) {
+                    const int ci = threadIdx.x + c * 32 * S;
+                    if (ci < CHAINS) {
+                        const int slot = (ci / LPC) * 12 + ci % LPC;
+                        float a = cacc[c];
+#pragma unroll
+                        for (int k = 0; k < S; k++)
+                            if (k < nsb) a = __fadd_rn(a, tw[k * SM::PER_SB + slot]);
+                        cacc[c] = a;
+                    }
+                }
+            }
+        }
+    }
+    // per (tile, column, row): reduce8 of the 8 main lanes + reduce4 of the 4 min lanes (kdot.rs:75)
+    if constexpr (S == 1) {
+        const int base = rs * 4;
+#pragma unroll
+        for (int j = 0; j < R; j++)
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                float l8[8], m4[4];
+#pragma unroll
+                for (int g = 0; g < 8; g++) l8[g] = __shfl_sync(0xffffffffu, acc[j][n][g & 1], base + (g >> 1));
+#pragma unroll
+                for (int m = 0; m < 4; m++) m4[m] = __shfl_sync(0xffffffffu, accm[j][n], base + m);
+                const int tile = bid * R + j;
+                if (tg == 0 && tile < tiles) {
+                    float v = reduce8(l8);
+                    if constexpr (G::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
+                    y[(size_t)n * rows + tile * 8 + rs] = v;
+                }
+            }
+    } else {
+#pragma unroll
+        for (int c = 0; c < CPT; c++) {
+            const int ci = threadIdx.x + c * 32 * S;
+            if (ci < CHAINS) fin[(ci / LPC) * 12 + ci % LPC] = cacc[c];
+        }
+        __syncthreads();
+        for (int o = threadIdx.x; o < R * NC * 8; o += 32 * S) {
+            const int r = o % 8, n = (o / 8) % NC, j = o / (8 * NC);
+            const float* f = fin + o * 12;
+            float v = reduce8(f);
+            if constexpr (G::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(f[8], f[10]), __fadd_rn(f[9], f[11])));
+            const int tile = bid * R + j;
+            if (tile < tiles) y[(size_t)n * rows + tile * 8 + r] = v;
+        }
+    }
+}
+
+template <int TYPE, int NC, int R, int S, int D, int MINB>
+cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                    const void* img, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows_a / 8 + R - 1) / R + (w_b ? (rows_b / 8 + R - 1) / R : 0));
+    cfg.blockDim = dim3(32 * S);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kq_gemv7_kernel<TYPE, NC, R, S, D, MINB>, w_a, rows_a, y_a, w_b, rows_b, y_b, nb,
+                              (const uint8_t*)img);
+}
+
+int g_cfg7 = [] {
+    const char* e = getenv("QDEC_GEMV7_CFG");
+    return e ? atoi(e) : 0;
+}();
+
+// Configurations (R tiles per warp, S warps splitting the super-blocks, D super-blocks in flight per warp).
+template <int TYPE, int NC>
+cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                        const void* img, cudaStream_t s, bool pdl) {
+    if (cfg == 0) {
+        const int rows = rows_a + (w_b ? rows_b : 0);
+        if (rows >= 16384) cfg = 1;
+        else if (rows >= 8192) cfg = 4;
+        else cfg = 5;
+    }
+    // (R, S, D, min CTAs per SM -- which caps the registers: 65536 / (32 S MINB))
+    switch (cfg) {
+    case 1: return launch7<TYPE, NC, 1, 1, 2, 16>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch7<TYPE, NC, 1, 1, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch7<TYPE, NC, 1, 1, 3, 12>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4: return launch7<TYPE, NC, 1, 2, 2, 8>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 5: return launch7<TYPE, NC, 1, 4, 2, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 6: return launch7<TYPE, NC, 1, 8, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 7: return launch7<TYPE, NC, 2, 1, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 8: return launch7<TYPE, NC, 1, 4, 3, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 9: return launch7<TYPE, NC, 1, 2, 3, 6>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    default: return launch7<TYPE, NC, 1, 1, 4, 12>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    }
+}
+
+template <int TYPE>
+cudaError_t launch7_type(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                         const void* img, int nc, cudaStream_t s, bool pdl) {
+    switch (nc) {
+    case 1: return launch7_cfg<TYPE, 1>(g_cfg7, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch7_cfg<TYPE, 2>(g_cfg7, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch7_cfg<TYPE, 3>(g_cfg7, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    default: return launch7_cfg<TYPE, 4>(g_cfg7, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    }
+}
+
+}  // namespace
+
+bool gemv7_supported(int type) { return type == T_Q4_K_TILE || type == T_Q5_K_TILE || type == T_Q6_K_TILE; }
+
+void set_gemv7_config(int cfg) { g_cfg7 = cfg; }
+
+cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
+                         int cols, const void* img, int ncols, cudaStream_t s, bool pdl) {
+    if (rows_a % 8 || (w_b && rows_b % 8) || cols % QK_K) return cudaErrorInvalidValue;
+    if (rows_a <= 0 || ncols <= 0) return cudaSuccess;
+    const int nb = cols / QK_K;
+    for (int c0 = 0; c0 < ncols; c0 += 4) {  // columns beyond 4 in groups of at most 4
+        const int nc = std::min(4, ncols - c0);
+        const uint8_t* im = (const uint8_t*)img + (size_t)c0 * nb * Q8K_IMG_BYTES;
+        float* ya = y_a + (size_t)c0 * rows_a;
+        float* yb = w_b ? y_b + (size_t)c0 * rows_b : nullptr;
+        cudaError_t e;
+        if (type == T_Q4_K_TILE) e = launch7_type<T_Q4_K>(w_a, rows_a, ya, w_b, rows_b, yb, nb, im, nc, s, pdl);
+        else if (type == T_Q5_K_TILE) e = launch7_type<T_Q5_K>(w_a, rows_a, ya, w_b, rows_b, yb, nb, im, nc, s, pdl);
+        else if (type == T_Q6_K_TILE) e = launch7_type<T_Q6_K>(w_a, rows_a, ya, w_b, rows_b, yb, nb, im, nc, s, pdl);
+        else return cudaErrorInvalidValue;
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace qdec

@@ -1135,6 +1135,7 @@ cudaError_t launch_gemv_img(int type, const uint8_t* w, int rows, int cols, cons
     const int nb = cols / QK_K;
     if (rows <= 0 || ncols <= 0) return cudaSuccess;
     if (gemm_tc_applies(type, ncols)) return launch_gemm_tc(type, w, rows, y, nullptr, 0, nullptr, cols, img, ncols, s, pdl);
+    if (gemv7_supported(type) && gemv_impl() != 6) return launch_gemv7(type, w, rows, y, nullptr, 0, nullptr, cols, img, ncols, s, pdl);
     for (int c0 = 0; c0 < ncols; c0 += 4) {  // columns beyond 4 in groups of at most 4
         const int nc = std::min(4, ncols - c0);
         const uint8_t* im = (const uint8_t*)img + (size_t)c0 * nb * Q8K_IMG_BYTES;
@@ -1187,6 +1188,7 @@ cudaError_t launch_gemv_img_pair(int type, const uint8_t* w_a, int rows_a, float
                                  int cols, const void* img, int ncols, cudaStream_t s, bool pdl) {
     if (rows_a % 8 || rows_b % 8) return cudaErrorInvalidValue;
     if (gemm_tc_applies(type, ncols)) return launch_gemm_tc(type, w_a, rows_a, y_a, w_b, rows_b, y_b, cols, img, ncols, s, pdl);
+    if (gemv7_supported(type) && gemv_impl() != 6) return launch_gemv7(type, w_a, rows_a, y_a, w_b, rows_b, y_b, cols, img, ncols, s, pdl);
     const int nb = cols / QK_K;
     for (int c0 = 0; c0 < ncols; c0 += 4) {
         const int nc = std::min(4, ncols - c0);

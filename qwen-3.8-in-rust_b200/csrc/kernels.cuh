@@ -66,6 +66,13 @@ cudaError_t launch_repack_q80_tiles(int ggml_type, const uint8_t* src, int rows,
 void set_q80_split(int mode);
 cudaError_t launch_gemv_q80_img(int type, const uint8_t* w, int rows, int cols, const void* img, int ncols, float* y,
                                 cudaStream_t s, bool pdl);
+// The decode GEMV of K-quant tile matrices (gemv7.cu): one matrix, or two reading the same image columns (w_b
+// non-null, e.g. ffn_gate and ffn_up), against `ncols` Q8_K image columns (groups of at most 4 per launch).
+// Bit-exact with crates/core/src/kernels/kdot.rs.  rows % 8 == 0, cols % 256 == 0.
+bool gemv7_supported(int type);
+void set_gemv7_config(int cfg);  // 0 = automatic by shape; 1..8 a fixed configuration (tests, sweeps)
+cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
+                         int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
 // Prompt-prefill GEMM on the tensor cores (gemm_tc.cu): K-quant tile matrices (one, or two reading the same

@@ -177,6 +177,9 @@ def gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream=0):
     _check(lib().qdec_gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream))
 
 
+GEMV7_CONFIGS = 10
+
+
 def tune_gemv(impl=0, config=0):
     """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
     image kernel's configuration (0 automatic, 1..35); impl 8 the Q8_0/Q4_0 tile kernel (0..3); impl 9 the

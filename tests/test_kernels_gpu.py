@@ -331,3 +331,66 @@ def test_gemv_image_entry_points(q, orc, t, base):
     q.gemv_image(t, dst.data_ptr(), rows, cols, img.data_ptr(), 3, y.data_ptr())
     torch.cuda.synchronize()
     assert bits_equal(y.cpu().numpy().reshape(3, rows), want)
+
+
+def _repack(q, t, w, rows, cols):
+    src = to_dev(w)
+    dst = torch.empty_like(src)
+    q.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr())
+    torch.cuda.synchronize()
+    return dst
+
+
+@pytest.mark.parametrize("t", [12, 13, 14])
+@pytest.mark.parametrize("cfg", range(0, 11))
+def test_gemv7_every_config_bit_exact(q, orc, t, cfg):
+    """The decode GEMV of tile matrices (gemv7.cu) in each configuration (tiles per warp, warps splitting the
+    super-blocks, depth, register cap): the oracle's bits for 1..5 columns on a tile count that is not a multiple
+    of any split and 21 super-blocks (not a multiple of any depth or split), with tiny, huge and zero columns."""
+    rows, cols = 8 * 37, 5376
+    w = random_blocks(t, rows, cols, seed=71 + t)
+    x = np.random.default_rng(200 + cfg).standard_normal((5, cols)).astype(np.float32)
+    x[1] *= 1e-30
+    x[3] *= 1e20
+    x[4, ::3] = 0.0
+    want = orc.matmul(t, w, rows, cols, x)
+    dst = _repack(q, t, w, rows, cols)
+    q.tune_gemv(7, cfg)
+    try:
+        for n in (1, 2, 3, 4, 5):
+            got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (t, cfg, n)
+    finally:
+        q.tune_gemv(0, 0)
+
+
+def _extreme_blocks(t, rows, cols, seed, neg_scales=False):
+    """Blocks at the integer extremes of the dot: every code at its maximum (Q4_K 15, Q5_K 31, Q6_K 63), every
+    6-bit scale and min 63 (Q6_K int8 scales -128 or +127), finite random f16 d / dmin."""
+    w = random_blocks(t, rows, cols, seed).reshape(-1, {12: 144, 13: 176, 14: 210}[t]).copy()
+    if t in (12, 13):
+        w[:, 4:] = 0xFF
+    else:
+        w[:, :192] = 0xFF
+        w[:, 192:208] = 0x80 if neg_scales else 0x7F
+    return w.reshape(-1)
+
+
+@pytest.mark.parametrize("t,neg", [(12, False), (13, False), (14, False), (14, True)])
+@pytest.mark.parametrize("cfg", [0, 1, 5])
+def test_gemv7_integer_extremes_bit_exact(q, orc, t, neg, cfg):
+    """The largest lane sums the formats allow (the packed 16-bit chunk sums and the biased lane conversion at
+    their limits): activation codes all -127, all +127 and alternating, against maximal codes and scales."""
+    rows, cols = 64, 2048
+    w = _extreme_blocks(t, rows, cols, seed=t, neg_scales=neg)
+    x = np.stack([np.full(cols, 3.0, np.float32), np.full(cols, -3.0, np.float32),
+                  np.where(np.arange(cols) % 2 == 0, 2.0, -2.0).astype(np.float32),
+                  np.random.default_rng(t).standard_normal(cols).astype(np.float32)])
+    want = orc.matmul(t, w, rows, cols, x)
+    dst = _repack(q, t, w, rows, cols)
+    q.tune_gemv(7, cfg)
+    try:
+        got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x)
+    finally:
+        q.tune_gemv(0, 0)
+    assert bits_equal(got, want), (t, neg, cfg)
