@@ -460,8 +460,11 @@ static size_t act_bytes(int type, int cols) {
 }
 
 /* matvec.rs:377-385, 511-539: every row computed once per column with the single-row arithmetic */
+int oracle_matmul_fast(int type, const uint8_t *w, int rows, int cols, const void *act, size_t act_stride, int ncols, float *y);
+
 void oracle_matmul_act(int type, const uint8_t *w, int rows, int cols, const void *act, size_t act_stride, int ncols,
                        float *y) {
+    if (oracle_matmul_fast(type, w, rows, cols, act, act_stride, ncols, y)) return;
     size_t rb = oracle_row_bytes(type, cols);
 #ifdef _OPENMP
     int nt = g_threads > 0 ? g_threads : omp_get_max_threads();
@@ -625,3 +628,183 @@ uint32_t oracle_crc32(const uint8_t *p, size_t n) { /* quant.rs:234-249 */
     for (size_t i = 0; i < n; i++) crc = table[(crc ^ p[i]) & 0xFF] ^ (crc >> 8);
     return crc ^ 0xFFFFFFFFu;
 }
+
+/* ------------------------------------------------------------------------------------------------------------
+ * The timed CPU baseline's kernels: an AVX2 restatement of the reference's SIMD dots
+ * (crates/core/src/kernels/avx2.rs:934-1087, the blocked form of kdot.rs:176-333 that matmul_t runs:
+ * one weight row decoded once per super-block for up to 16 activation rows), bit-identical to the scalar
+ * kernels above -- the exact integer lanes come from maddubs (u8 x s8 pair sums, no saturation at these
+ * magnitudes) and madd (the pair sums times the chunk scale, adjacent pairs added: i32 lane k = positions
+ * 4k .. 4k+3 of the chunk, the reference's lane), and the f32 steps are the same multiply-then-add per lane in
+ * the same order.  Q8_0 / Q4_0 blocks use the sign trick for the signed x signed byte products; F32 stays
+ * scalar (its 32-term partial sums are sequential chains).  Rows are split over OpenMP threads, as the
+ * reference splits them over its pool (kernels/matvec.rs:446-467).  oracle_set_simd(0) routes every matmul to
+ * the scalar kernels.
+ * ------------------------------------------------------------------------------------------------------------ */
+#if defined(__x86_64__)
+#include <immintrin.h>
+#define OR_AVX2 __attribute__((target("avx2")))
+
+static int g_simd = -1; /* -1: use AVX2 when the CPU has it */
+void oracle_set_simd(int on) { g_simd = on; }
+static int simd_on(void) {
+    if (g_simd < 0) g_simd = __builtin_cpu_supports("avx2") ? 1 : 0;
+    return g_simd;
+}
+
+OR_AVX2 static inline float hsum_lane_order8(__m256 v) { /* reduce8 in the reference order */
+    float l[8];
+    _mm256_storeu_ps(l, v);
+    return oracle_reduce8(l);
+}
+OR_AVX2 static inline float hsum_lane_order4(__m128 v) {
+    float m[4];
+    _mm_storeu_ps(m, v);
+    return reduce4(m);
+}
+OR_AVX2 static inline int hsum_epi32(__m256i v) { /* an exact integer sum: any order */
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4e));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xb1));
+    return _mm_cvtsi128_si32(s);
+}
+
+/* Q4_K / Q5_K row x t Q8_K rows (kdot.rs:194-260, avx2.rs dot_q4_k_q8k_t / dot_q5_k_q8k_t) */
+OR_AVX2 static void dot_q45_k_t_avx2(const uint8_t *w, const uint8_t *const *x, int t, int nb, int q5, float *out) {
+    __m256 acc[16];
+    __m128 accm[16];
+    for (int c = 0; c < t; c++) acc[c] = _mm256_setzero_ps(), accm[c] = _mm_setzero_ps();
+    const int bbytes = q5 ? 176 : 144;
+    const __m256i m4 = _mm256_set1_epi8(0x0F), one = _mm256_set1_epi8(1);
+    for (int sb = 0; sb < nb; sb++) {
+        const uint8_t *wb = w + (size_t)sb * bbytes;
+        const float dw = f16_at(wb, 0), dminw = f16_at(wb, 2);
+        int sc[8], mn[8];
+        for (int s = 0; s < 8; s++) scale_min_k4(s, wb + 4, &sc[s], &mn[s]);
+        __m256i q[8], scv[8];
+        const uint8_t *qs = wb + (q5 ? 48 : 16);
+        __m256i qh = q5 ? _mm256_loadu_si256((const __m256i *)(wb + 16)) : _mm256_setzero_si256();
+        for (int p = 0; p < 4; p++) {
+            const __m256i raw = _mm256_loadu_si256((const __m256i *)(qs + 32 * p));
+            q[2 * p] = _mm256_and_si256(raw, m4);
+            q[2 * p + 1] = _mm256_and_si256(_mm256_srli_epi16(raw, 4), m4);
+        }
+        if (q5)
+            for (int s = 0; s < 8; s++)
+                q[s] = _mm256_or_si256(q[s], _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(qh, s), one), 4));
+        for (int s = 0; s < 8; s++) scv[s] = _mm256_set1_epi16((short)sc[s]);
+        const __m128i mins = _mm_setr_epi16((short)mn[0], (short)mn[1], (short)mn[2], (short)mn[3], (short)mn[4], (short)mn[5],
+                                            (short)mn[6], (short)mn[7]);
+        for (int c = 0; c < t; c++) {
+            const uint8_t *xb = x[c] + (size_t)sb * 292;
+            const float dx = q8k_d(xb);
+            const int8_t *xq = (const int8_t *)(xb + 4);
+            __m256i sumi = _mm256_setzero_si256();
+            for (int s = 0; s < 8; s++) {
+                const __m256i xs = _mm256_loadu_si256((const __m256i *)(xq + 32 * s));
+                sumi = _mm256_add_epi32(sumi, _mm256_madd_epi16(_mm256_maddubs_epi16(q[s], xs), scv[s]));
+            }
+            /* q8s[s] = bsums[2s] + bsums[2s+1] (q8k.rs:185-193), then mn . q8s pairwise: 4 exact i32 lanes */
+            const __m128i bs0 = _mm_loadu_si128((const __m128i *)(xb + 260)), bs1 = _mm_loadu_si128((const __m128i *)(xb + 276));
+            const __m128i q8s = _mm_hadd_epi16(bs0, bs1);
+            const __m128i prod = _mm_madd_epi16(q8s, mins);
+            const float d = dx * dw, dmin = -dx * dminw;
+            accm[c] = _mm_add_ps(accm[c], _mm_mul_ps(_mm_set1_ps(dmin), _mm_cvtepi32_ps(prod)));
+            acc[c] = _mm256_add_ps(acc[c], _mm256_mul_ps(_mm256_set1_ps(d), _mm256_cvtepi32_ps(sumi)));
+        }
+    }
+    for (int c = 0; c < t; c++) out[c] = hsum_lane_order8(acc[c]) + hsum_lane_order4(accm[c]);
+}
+
+/* Q6_K row x t Q8_K rows (kdot.rs:262-312, avx2.rs dot_q6_k_q8k_t) */
+OR_AVX2 static void dot_q6_k_t_avx2(const uint8_t *w, const uint8_t *const *x, int t, int nb, float *out) {
+    __m256 acc[16];
+    for (int c = 0; c < t; c++) acc[c] = _mm256_setzero_ps();
+    const __m256i m4 = _mm256_set1_epi8(0x0F), m2 = _mm256_set1_epi8(0x03);
+    for (int sb = 0; sb < nb; sb++) {
+        const uint8_t *wb = w + (size_t)sb * 210;
+        const float dw = f16_at(wb, 208);
+        __m256i q[8], scv[8];
+        for (int h = 0; h < 2; h++) {
+            const __m256i ql0 = _mm256_loadu_si256((const __m256i *)(wb + 64 * h));
+            const __m256i ql1 = _mm256_loadu_si256((const __m256i *)(wb + 64 * h + 32));
+            const __m256i qh = _mm256_loadu_si256((const __m256i *)(wb + 128 + 32 * h));
+            const __m256i lo[4] = {_mm256_and_si256(ql0, m4), _mm256_and_si256(ql1, m4), _mm256_and_si256(_mm256_srli_epi16(ql0, 4), m4),
+                                   _mm256_and_si256(_mm256_srli_epi16(ql1, 4), m4)};
+            for (int k = 0; k < 4; k++) {
+                const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(qh, 2 * k), m2);
+                q[4 * h + k] = _mm256_or_si256(lo[k], _mm256_slli_epi16(hi, 4));
+                const int8_t *sc = (const int8_t *)(wb + 192 + 8 * h + 2 * k);
+                scv[4 * h + k] = _mm256_setr_m128i(_mm_set1_epi16(sc[0]), _mm_set1_epi16(sc[1]));
+            }
+        }
+        /* the 16 scales as i16, for the -32 * (bsums . scales) correction of each lane */
+        const __m256i sc16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(wb + 192)));
+        for (int c = 0; c < t; c++) {
+            const uint8_t *xb = x[c] + (size_t)sb * 292;
+            const int8_t *xq = (const int8_t *)(xb + 4);
+            __m256i sumi = _mm256_setzero_si256();
+            for (int s = 0; s < 8; s++) {
+                const __m256i xs = _mm256_loadu_si256((const __m256i *)(xq + 32 * s));
+                sumi = _mm256_add_epi32(sumi, _mm256_madd_epi16(_mm256_maddubs_epi16(q[s], xs), scv[s]));
+            }
+            const __m256i bs = _mm256_loadu_si256((const __m256i *)(xb + 260));
+            sumi = _mm256_sub_epi32(sumi, _mm256_slli_epi32(_mm256_madd_epi16(bs, sc16), 5));
+            const float d = q8k_d(xb) * dw;
+            acc[c] = _mm256_add_ps(acc[c], _mm256_mul_ps(_mm256_set1_ps(d), _mm256_cvtepi32_ps(sumi)));
+        }
+    }
+    for (int c = 0; c < t; c++) out[c] = hsum_lane_order8(acc[c]);
+}
+
+/* Q8_0 / Q4_0 row x one Q8_0 row (dot.rs:29-64): per 32-block an exact i32 sum, then the f32 chain */
+OR_AVX2 static float dot_q80_avx2(const uint8_t *w, const uint8_t *x, int nb, int q4) {
+    float acc = 0.0f;
+    const __m256i m4 = _mm256_set1_epi8(0x0F), eight = _mm256_set1_epi8(8), ones = _mm256_set1_epi16(1);
+    for (int b = 0; b < nb; b++) {
+        const uint8_t *wb = w + (size_t)b * (q4 ? 18 : 34), *xb = x + (size_t)b * 34;
+        __m256i wv;
+        if (q4) {
+            const __m128i raw = _mm_loadu_si128((const __m128i *)(wb + 2));
+            wv = _mm256_sub_epi8(_mm256_and_si256(_mm256_setr_m128i(raw, _mm_srli_epi16(raw, 4)), m4), eight);
+        } else {
+            wv = _mm256_loadu_si256((const __m256i *)(wb + 2));
+        }
+        const __m256i xv = _mm256_loadu_si256((const __m256i *)(xb + 2));
+        const __m256i p16 = _mm256_maddubs_epi16(_mm256_sign_epi8(wv, wv), _mm256_sign_epi8(xv, wv));
+        const int isum = hsum_epi32(_mm256_madd_epi16(p16, ones));
+        acc += (f16_at(wb, 0) * f16_at(xb, 0)) * (float)isum;
+    }
+    return acc;
+}
+
+int oracle_matmul_fast(int type, const uint8_t *w, int rows, int cols, const void *act, size_t act_stride, int ncols, float *y) {
+    if (!simd_on() || type == OT_F32) return 0;
+    const size_t rb = oracle_row_bytes(type, cols);
+    const int nt = g_threads > 0 ? g_threads : omp_get_max_threads();
+    for (int c0 = 0; c0 < ncols; c0 += 16) {
+        const int tc = ncols - c0 < 16 ? ncols - c0 : 16;
+        const uint8_t *xs[16];
+        for (int c = 0; c < tc; c++) xs[c] = (const uint8_t *)act + (size_t)(c0 + c) * act_stride;
+#pragma omp parallel for schedule(static) num_threads(nt)
+        for (int r = 0; r < rows; r++) {
+            const uint8_t *wr = w + (size_t)r * rb;
+            float o[16];
+            switch (type) {
+            case OT_Q4_K: dot_q45_k_t_avx2(wr, xs, tc, cols / 256, 0, o); break;
+            case OT_Q5_K: dot_q45_k_t_avx2(wr, xs, tc, cols / 256, 1, o); break;
+            case OT_Q6_K: dot_q6_k_t_avx2(wr, xs, tc, cols / 256, o); break;
+            default:
+                for (int c = 0; c < tc; c++) o[c] = dot_q80_avx2(wr, xs[c], cols / 32, type == OT_Q4_0);
+            }
+            for (int c = 0; c < tc; c++) y[(size_t)(c0 + c) * rows + r] = o[c];
+        }
+    }
+    return 1;
+}
+#else
+void oracle_set_simd(int on) { (void)on; }
+int oracle_matmul_fast(int type, const uint8_t *w, int rows, int cols, const void *act, size_t act_stride, int ncols, float *y) {
+    return 0;
+}
+#endif

@@ -29,6 +29,7 @@
 #include "oracle.h"
 
 #define MAXT 2048
+#define MAXB 16 /* rows of one batched forward (the reference's matmul_t tile, kdot.rs T_MAX) */
 
 typedef struct {
     char *name;
@@ -77,6 +78,9 @@ typedef struct oracle_model {
 typedef struct {
     float *S, *conv;  /* DeltaNet */
     float *K, *V;     /* attention: [max_pos][n_kv*hd] */
+    /* the projections of the last batched call of a DeltaNet layer (the reference's DeltaBatch, spec.rs replay):
+     * mixed [MAXB][conv_dim], z [MAXB][vd], a / b [MAXB][n_v] */
+    float *sv_mixed, *sv_z, *sv_ga, *sv_gb;
 } OLayerState;
 
 typedef struct oracle_state {
@@ -360,6 +364,10 @@ OState *oracle_state_new(OModel *m, int max_pos) {
         } else {
             s->ls[i].S = (float *)calloc((size_t)m->n_v * m->dk * m->dv, 4);
             s->ls[i].conv = (float *)calloc((size_t)m->conv_dim * (m->conv_k - 1), 4);
+            s->ls[i].sv_mixed = (float *)calloc((size_t)MAXB * m->conv_dim, 4);
+            s->ls[i].sv_z = (float *)calloc((size_t)MAXB * m->vd, 4);
+            s->ls[i].sv_ga = (float *)calloc((size_t)MAXB * m->n_v, 4);
+            s->ls[i].sv_gb = (float *)calloc((size_t)MAXB * m->n_v, 4);
         }
     }
     if (m->has_mtp) {
@@ -374,6 +382,10 @@ void oracle_state_free(OState *s) {
     for (int i = 0; i < s->m->n_layer; i++) {
         free(s->ls[i].S);
         free(s->ls[i].conv);
+        free(s->ls[i].sv_mixed);
+        free(s->ls[i].sv_z);
+        free(s->ls[i].sv_ga);
+        free(s->ls[i].sv_gb);
         free(s->ls[i].K);
         free(s->ls[i].V);
     }
@@ -414,19 +426,21 @@ static void restore(OState *s, const float *snap) {
 
 static void matvec(const OMat *w, const float *x, float *y) { oracle_matmul_f32in(w->type, w->data, w->rows, w->cols, x, 1, y); }
 
-/* gated_deltanet.rs:548-602 */
-static void deltanet_token(OModel *m, const OLayer *L, OLayerState *st, const float *x, float *y) {
-    float *mixed = (float *)malloc((size_t)m->conv_dim * 4), *conved = (float *)malloc((size_t)m->conv_dim * 4);
-    float *z = (float *)malloc((size_t)m->vd * 4), *ga = (float *)malloc((size_t)m->n_v * 4), *gb = (float *)malloc((size_t)m->n_v * 4);
-    float *heads = (float *)malloc((size_t)m->vd * 4), *qn = (float *)malloc((size_t)m->dk * 4), *kn = (float *)malloc((size_t)m->dk * 4);
-    float *o = (float *)malloc((size_t)m->dv * 4);
-    matvec(&L->qkv, x, mixed);
-    matvec(&L->gate_z, x, z);
-    matvec(&L->alpha, x, ga);
-    matvec(&L->beta, x, gb);
+static void matmul_rows(const OMat *w, const float *x, int t, float *y) {
+    oracle_matmul_f32in(w->type, w->data, w->rows, w->cols, x, t, y);
+}
+
+/* The DeltaNet recurrence of one row from its projections (gated_deltanet.rs:562-598): the conv step, then per V
+ * head p (K head p % n_k) l2norm, the gates, the delta rule and the gated RMSNorm into heads.  The heads are
+ * independent (each has its own state), so they are spread over the threads. */
+static void deltanet_recur(OModel *m, const OLayer *L, OLayerState *st, const float *mixed, const float *z, const float *ga,
+                           const float *gb, float *heads) {
+    float *conved = (float *)malloc((size_t)m->conv_dim * 4);
     oracle_conv1d_step(st->conv, L->conv_w, m->conv_k, mixed, m->conv_dim, conved, 1);
     const float scale = 1.0f / sqrtf((float)m->dk);
+#pragma omp parallel for schedule(static) if (m->n_v >= 16)
     for (int p = 0; p < m->n_v; p++) {
+        float qn[256], kn[256], o[256];
         int kh = p % m->n_k;
         memcpy(qn, conved + kh * m->dk, (size_t)m->dk * 4);
         memcpy(kn, conved + m->kd + kh * m->dk, (size_t)m->dk * 4);
@@ -436,30 +450,34 @@ static void deltanet_token(OModel *m, const OLayer *L, OLayerState *st, const fl
         float g = oracle_gate_g(ga[p], L->dt_bias[p], L->ssm_a[p]);
         float beta = oracle_gate_beta(gb[p]);
         oracle_deltanet_step(qn, kn, conved + 2 * m->kd + p * m->dv, m->dk, m->dv, g, beta, st->S + (size_t)p * m->dk * m->dv, o);
-        oracle_rmsnorm_gated(o, z + p * m->dv, L->ssm_norm, m->dv, m->eps, heads + p * m->dv);
+        if (heads) oracle_rmsnorm_gated(o, z + p * m->dv, L->ssm_norm, m->dv, m->eps, heads + p * m->dv);
     }
-    matvec(&L->ssm_out, heads, y);
-    free(mixed); free(conved); free(z); free(ga); free(gb); free(heads); free(qn); free(kn); free(o);
+    free(conved);
 }
 
-/* gqa_attention.rs:155-234 */
-static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int pos, const float *x, float *y) {
+/* gated_deltanet.rs:548-602 */
+static void deltanet_token(OModel *m, const OLayer *L, OLayerState *st, const float *x, float *y) {
+    float *mixed = (float *)malloc((size_t)m->conv_dim * 4), *z = (float *)malloc((size_t)m->vd * 4);
+    float *ga = (float *)malloc((size_t)m->n_v * 4), *gb = (float *)malloc((size_t)m->n_v * 4), *heads = (float *)malloc((size_t)m->vd * 4);
+    matmul_rows(&L->qkv, x, 1, mixed);
+    matmul_rows(&L->gate_z, x, 1, z);
+    matmul_rows(&L->alpha, x, 1, ga);
+    matmul_rows(&L->beta, x, 1, gb);
+    deltanet_recur(m, L, st, mixed, z, ga, gb, heads);
+    matmul_rows(&L->ssm_out, heads, 1, y);
+    free(mixed); free(z); free(ga); free(gb); free(heads);
+}
+
+/* The attention of one row at `pos` from its projections (gqa_attention.rs:170-228): q/k RMSNorm, RoPE on the
+ * first rope_dim dims, the K/V append, scores over the cache, softmax, the value sum and the sigmoid gate into
+ * attn (n_head * head_dim).  k is normed and rotated in place.  The query heads are spread over the threads. */
+static void attention_recur(OModel *m, const OLayer *L, float *K, float *V, int pos, const float *qg, float *k, const float *v,
+                            float *attn) {
     const int nh = m->n_head, nkv = m->n_kv, hd = m->hd, rd = m->rope_dim, group = nh / nkv;
-    float *qg = (float *)malloc((size_t)2 * nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4), *v = (float *)malloc((size_t)nkv * hd * 4);
-    float *q = (float *)malloc((size_t)nh * hd * 4), *attn = (float *)malloc((size_t)nh * hd * 4), *tmp = (float *)malloc((size_t)hd * 4);
-    float *inv = (float *)malloc((size_t)rd / 2 * 4 + 4), *cs = (float *)malloc((size_t)rd * 4 + 4), *sn = (float *)malloc((size_t)rd * 4 + 4);
-    int len = pos + 1;
-    float *sc = (float *)malloc((size_t)len * 4), *pr = (float *)malloc((size_t)len * 4);
-    matvec(&L->q, x, qg);
-    matvec(&L->k, x, k);
-    matvec(&L->v, x, v);
+    float inv[128], cs[256], sn[256], tmp[512];
+    const int len = pos + 1;
     oracle_inv_freq(rd, m->theta, inv);
     oracle_cos_sin((uint32_t)pos, inv, rd / 2, cs, sn);
-    for (int h = 0; h < nh; h++) {
-        oracle_rmsnorm(qg + (size_t)h * 2 * hd, L->q_norm, hd, m->eps, tmp);
-        oracle_apply_rope(tmp, hd, hd, rd, cs, sn);
-        memcpy(q + (size_t)h * hd, tmp, (size_t)hd * 4);
-    }
     for (int h = 0; h < nkv; h++) {
         oracle_rmsnorm(k + (size_t)h * hd, L->k_norm, hd, m->eps, tmp);
         oracle_apply_rope(tmp, hd, hd, rd, cs, sn);
@@ -467,9 +485,13 @@ static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int 
     }
     memcpy(K + (size_t)pos * nkv * hd, k, (size_t)nkv * hd * 4);
     memcpy(V + (size_t)pos * nkv * hd, v, (size_t)nkv * hd * 4);
+#pragma omp parallel for schedule(static) if (nh >= 8 && len >= 64)
     for (int h = 0; h < nh; h++) {
+        float qh[512];
+        float *sc = (float *)malloc((size_t)len * 4), *pr = (float *)malloc((size_t)len * 4);
+        oracle_rmsnorm(qg + (size_t)h * 2 * hd, L->q_norm, hd, m->eps, qh);
+        oracle_apply_rope(qh, hd, hd, rd, cs, sn);
         int kvh = h / group;
-        const float *qh = q + (size_t)h * hd;
         for (int t = 0; t < len; t++) {
             const float *kt = K + ((size_t)t * nkv + kvh) * hd;
             float s = 0.0f;
@@ -484,9 +506,22 @@ static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int 
             for (int d = 0; d < hd; d++) out[d] += pr[t] * vt[d];
         }
         for (int d = 0; d < hd; d++) out[d] *= oracle_sigmoid(qg[(size_t)h * 2 * hd + hd + d]);
+        free(sc);
+        free(pr);
     }
-    matvec(&L->o, attn, y);
-    free(qg); free(k); free(v); free(q); free(attn); free(tmp); free(inv); free(cs); free(sn); free(sc); free(pr);
+}
+
+/* gqa_attention.rs:155-234 */
+static void attention_token(OModel *m, const OLayer *L, float *K, float *V, int pos, const float *x, float *y) {
+    const int nh = m->n_head, nkv = m->n_kv, hd = m->hd;
+    float *qg = (float *)malloc((size_t)2 * nh * hd * 4), *k = (float *)malloc((size_t)nkv * hd * 4), *v = (float *)malloc((size_t)nkv * hd * 4);
+    float *attn = (float *)malloc((size_t)nh * hd * 4);
+    matmul_rows(&L->q, x, 1, qg);
+    matmul_rows(&L->k, x, 1, k);
+    matmul_rows(&L->v, x, 1, v);
+    attention_recur(m, L, K, V, pos, qg, k, v, attn);
+    matmul_rows(&L->o, attn, 1, y);
+    free(qg); free(k); free(v); free(attn);
 }
 
 /* layers/mlp.rs:53-64: y = down(swiglu(gate(x), up(x))) */
@@ -511,6 +546,54 @@ static void layer_token(OModel *m, const OLayer *L, OLayerState *st, float *K, f
     mlp_token(m, L, normed, mixed);
     for (int i = 0; i < H; i++) y[i] = resid[i] + mixed[i];
     free(normed); free(mixed); free(resid);
+}
+
+/* layers/mod.rs:335-377 (DecoderLayer::forward_batch_in): t rows at positions pos0 .. pos0 + t - 1.  Every matrix
+ * multiplies the t rows in one pass over its weights (matmul_t), the recurrences (conv + DeltaNet state, K/V append
+ * + attention) run row by row in order -- the reference's batched form, bit-identical to its token form.  A
+ * DeltaNet layer keeps its projections for the replay of a rolled-back verify (st->sv_*). */
+static void layer_rows(OModel *m, const OLayer *L, OLayerState *st, float *K, float *V, int pos0, int t, const float *x, float *y) {
+    const size_t H = (size_t)m->hidden;
+    float *normed = (float *)malloc(t * H * 4), *out = (float *)malloc(t * H * 4), *resid = (float *)malloc(t * H * 4);
+    for (int i = 0; i < t; i++) oracle_rmsnorm(x + i * H, L->attn_norm, (int)H, m->eps, normed + i * H);
+    if (L->attn) {
+        const size_t qd = (size_t)2 * m->n_head * m->hd, kvd = (size_t)m->n_kv * m->hd, ad = (size_t)m->n_head * m->hd;
+        float *qg = (float *)malloc(t * qd * 4), *k = (float *)malloc(t * kvd * 4), *v = (float *)malloc(t * kvd * 4);
+        float *attn = (float *)malloc(t * ad * 4);
+        matmul_rows(&L->q, normed, t, qg);
+        matmul_rows(&L->k, normed, t, k);
+        matmul_rows(&L->v, normed, t, v);
+        for (int i = 0; i < t; i++) attention_recur(m, L, K, V, pos0 + i, qg + i * qd, k + i * kvd, v + i * kvd, attn + i * ad);
+        matmul_rows(&L->o, attn, t, out);
+        free(qg); free(k); free(v); free(attn);
+    } else {
+        const size_t cd = (size_t)m->conv_dim, vd = (size_t)m->vd, nv = (size_t)m->n_v;
+        float *mixed = (float *)malloc(t * cd * 4), *z = (float *)malloc(t * vd * 4), *ga = (float *)malloc(t * nv * 4);
+        float *gb = (float *)malloc(t * nv * 4), *heads = (float *)malloc(t * vd * 4);
+        matmul_rows(&L->qkv, normed, t, mixed);
+        matmul_rows(&L->gate_z, normed, t, z);
+        matmul_rows(&L->alpha, normed, t, ga);
+        matmul_rows(&L->beta, normed, t, gb);
+        if (st->sv_mixed && t <= MAXB) {
+            memcpy(st->sv_mixed, mixed, t * cd * 4);
+            memcpy(st->sv_z, z, t * vd * 4);
+            memcpy(st->sv_ga, ga, t * nv * 4);
+            memcpy(st->sv_gb, gb, t * nv * 4);
+        }
+        for (int i = 0; i < t; i++) deltanet_recur(m, L, st, mixed + i * cd, z + i * vd, ga + i * nv, gb + i * nv, heads + i * vd);
+        matmul_rows(&L->ssm_out, heads, t, out);
+        free(mixed); free(z); free(ga); free(gb); free(heads);
+    }
+    for (size_t i = 0; i < t * H; i++) resid[i] = x[i] + out[i];
+    for (int i = 0; i < t; i++) oracle_rmsnorm(resid + i * H, L->post_norm, (int)H, m->eps, normed + i * H);
+    const size_t F = (size_t)m->ffn;
+    float *g = (float *)malloc(t * F * 4), *u = (float *)malloc(t * F * 4), *hh = (float *)malloc(t * F * 4);
+    matmul_rows(&L->gate, normed, t, g);
+    matmul_rows(&L->up, normed, t, u);
+    oracle_swiglu(g, u, (int)(t * F), hh);
+    matmul_rows(&L->down, hh, t, out);
+    for (size_t i = 0; i < t * H; i++) y[i] = resid[i] + out[i];
+    free(g); free(u); free(hh); free(normed); free(out); free(resid);
 }
 
 static void embed_row(OModel *m, uint32_t id, float *out) {
@@ -538,6 +621,64 @@ int oracle_forward_token(OState *s, uint32_t id, float *logits, float *capture, 
     s->pos++;
     free(x); free(y); free(nrm);
     return 0;
+}
+
+/* Model::prefill / forward_batch (model.rs:401-461, spec.rs:301): t <= MAXB rows from s->pos; logits of every row
+ * (logits_rows = t) or of the last one (1) or none (0); normed_out: the t post-final-norm rows. */
+static int forward_rows(OState *s, const uint32_t *ids, int t, float *logits, int logits_rows, float *normed_out) {
+    OModel *m = s->m;
+    const size_t H = (size_t)m->hidden;
+    if (t <= 0 || t > MAXB || s->pos + t > s->max_pos) return -1;
+    for (int i = 0; i < t; i++)
+        if (ids[i] >= (uint32_t)m->vocab) return -1;
+    float *x = (float *)malloc(t * H * 4), *y = (float *)malloc(t * H * 4), *nrm = (float *)malloc(t * H * 4);
+    for (int i = 0; i < t; i++) embed_row(m, ids[i], x + i * H);
+    for (int l = 0; l < m->n_layer; l++) {
+        layer_rows(m, &m->layers[l], &s->ls[l], s->ls[l].K, s->ls[l].V, s->pos, t, x, y);
+        float *tmp = x;
+        x = y;
+        y = tmp;
+    }
+    for (int i = 0; i < t; i++) oracle_rmsnorm(x + i * H, m->out_norm, (int)H, m->eps, nrm + i * H);
+    if (normed_out) memcpy(normed_out, nrm, t * H * 4);
+    if (logits && logits_rows == t) matmul_rows(&m->lm_head, nrm, t, logits);
+    else if (logits && logits_rows == 1) matmul_rows(&m->lm_head, nrm + (t - 1) * H, 1, logits);
+    s->pos += t;
+    free(x); free(y); free(nrm);
+    return 0;
+}
+
+/* The prompt through forward_rows in chunks of MAXB rows (Model::prefill); logits of the last row, the post-norm
+ * rows of every prompt position into normed_all when given. */
+static int prefill_rows(OState *s, const uint32_t *ids, int n, float *logits, float *normed_all) {
+    const size_t H = (size_t)s->m->hidden;
+    for (int off = 0; off < n; off += MAXB) {
+        const int t = n - off < MAXB ? n - off : MAXB;
+        if (forward_rows(s, ids + off, t, off + t == n ? logits : NULL, off + t == n ? 1 : 0, normed_all ? normed_all + off * H : NULL))
+            return -1;
+    }
+    return 0;
+}
+
+/* The MTP block over t rows (layers/mtp.rs:95-130, rows_in): row i = [enorm(embed(toks[i])) | hnorm(h_i)] ->
+ * eh_proj -> the block's attention decoder layer at MTP positions mtp_len .. -> shared_head_norm into hout. */
+static void mtp_rows_batch(OState *s, const uint32_t *toks, const float *h, int t, float *hout) {
+    OModel *m = s->m;
+    const size_t H = (size_t)m->hidden;
+    float *e = (float *)malloc(H * 4), *cat = (float *)malloc(t * 2 * H * 4), *u = (float *)malloc(t * H * 4);
+    float *yy = (float *)malloc(t * H * 4);
+    for (int i = 0; i < t; i++) {
+        embed_row(m, toks[i], e);
+        oracle_rmsnorm(e, m->enorm, (int)H, m->eps, cat + i * 2 * H);
+        oracle_rmsnorm(h + i * H, m->hnorm, (int)H, m->eps, cat + i * 2 * H + H);
+    }
+    matmul_rows(&m->eh_proj, cat, t, u);
+    OLayerState none;
+    memset(&none, 0, sizeof none);
+    layer_rows(m, &m->mtp_block, &none, s->mtpK, s->mtpV, s->mtp_len, t, u, yy);
+    for (int i = 0; i < t; i++) oracle_rmsnorm(yy + i * H, m->head_norm, (int)H, m->eps, hout + i * H);
+    s->mtp_len += t;
+    free(e); free(cat); free(u); free(yy);
 }
 
 /* One MTP row (layers/mtp.rs:95-137): hout = head_norm(block([enorm(embed(tok)) | hnorm(h)] @ eh_proj)),
@@ -575,8 +716,7 @@ int oracle_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, int s
     OModel *m = s->m;
     float *lg = (float *)malloc((size_t)m->vocab * 4);
     const int greedy = !smp || oracle_sampler_greedy(smp);
-    for (int i = 0; i < n; i++)
-        if (oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, NULL)) { free(lg); return -1; }
+    if (prefill_rows(s, prompt, n, lg, NULL)) { free(lg); return -1; }  /* batched, as Model::prefill */
     int c = 0;
     out[c++] = greedy ? oracle_argmax(lg, m->vocab) : oracle_sampler_sample(smp, lg);
     while (c < n_out && !(stop && is_stop(m, out[c - 1]))) {
@@ -643,14 +783,21 @@ int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, 
     float *hout = (float *)malloc((size_t)H * 4), *hprev = (float *)malloc((size_t)H * 4);
     uint32_t *drafts = (uint32_t *)malloc(sizeof(uint32_t) * k), *emitted = (uint32_t *)malloc(sizeof(uint32_t) * t);
     int c = 0, round = 0;
-    /* spec_prefill (spec.rs:229-285) */
+    /* spec_prefill (spec.rs:229-285): the batched prefill, x_T, the MTP over the prompt rows (x_{j+1}, h_j) */
     int p = s->pos;
-    for (int i = 0; i < n; i++) oracle_forward_token(s, prompt[i], i == n - 1 ? lg : NULL, NULL, normed + (size_t)i * H);
+    if (prefill_rows(s, prompt, n, lg, normed)) goto fail;
     uint32_t x_t = greedy ? oracle_argmax(lg, m->vocab) : oracle_sampler_sample(smp, lg);
     s->mtp_len = p;
-    for (int j = 0; j < n; j++) {
-        uint32_t x = (j + 1 < n) ? prompt[j + 1] : x_t;
-        mtp_row(s, x, normed + (size_t)j * H, hout, 0);
+    {
+        uint32_t xs[MAXB];
+        float *ho = (float *)malloc((size_t)MAXB * H * 4);
+        for (int off = 0; off < n; off += MAXB) {
+            const int tt = n - off < MAXB ? n - off : MAXB;
+            for (int j = 0; j < tt; j++) xs[j] = (off + j + 1 < n) ? prompt[off + j + 1] : x_t;
+            mtp_rows_batch(s, xs, normed + (size_t)off * H, tt, ho);
+            if (off + tt == n) memcpy(hout, ho + (size_t)(tt - 1) * H, (size_t)H * 4);
+        }
+        free(ho);
     }
     drafts[0] = draft_token(s, smp, hout, q_dense);
     for (int i = 1; i < k; i++) {
@@ -670,7 +817,8 @@ int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, 
         uint32_t batch[MAXT];
         batch[0] = x_p;
         for (int i = 0; i < k; i++) batch[i + 1] = drafts[i];
-        for (int i = 0; i < t; i++) oracle_forward_token(s, batch[i], lg + (size_t)i * m->vocab, NULL, normed + (size_t)i * H);
+        /* the verify: the t rows in one batched forward (spec.rs:337-350) */
+        if (forward_rows(s, batch, t, lg, t, normed)) { free(snap); break; }
         int mm = 0, ne = 0;
         if (greedy) {
             while (mm < k) {
@@ -696,17 +844,29 @@ int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, 
         }
         int keep = mm + 1;
         if (keep < t) {
-            /* restore and replay the kept rows (the replay reruns their recurrence on the same inputs, so the
-             * states are the verify's states after `keep` rows, bit for bit); the KV caches end at p + keep */
+            /* spec.rs:395-415: restore the DeltaNet snapshot and replay the kept rows' recurrence (conv + delta
+             * rule) from the verify's saved projections -- the states after `keep` rows, bit for bit, with no
+             * second pass over the weights; the KV caches end at p + keep */
             restore(s, snap);
-            s->pos = p;
-            for (int i = 0; i < keep; i++) oracle_forward_token(s, batch[i], NULL, NULL, NULL);
+            for (int l = 0; l < m->n_layer; l++) {
+                if (m->layers[l].attn) continue;
+                OLayerState *ls = &s->ls[l];
+                for (int i = 0; i < keep; i++)
+                    deltanet_recur(m, &m->layers[l], ls, ls->sv_mixed + (size_t)i * m->conv_dim, ls->sv_z + (size_t)i * m->vd,
+                                   ls->sv_ga + (size_t)i * m->n_v, ls->sv_gb + (size_t)i * m->n_v, NULL);
+            }
+            s->pos = p + keep;
         }
         free(snap);
         if (stats4) { stats4[0]++; stats4[1] += k; stats4[2] += mm; stats4[3] += keep; }
         /* the MTP: truncate to p, re-feed the kept pairs (emitted_i, normed_i), draft, chain */
         s->mtp_len = p;
-        for (int i = 0; i < keep; i++) mtp_row(s, emitted[i], normed + (size_t)i * H, hout, 0);
+        {
+            float *ho = (float *)malloc((size_t)t * H * 4);
+            mtp_rows_batch(s, emitted, normed, keep, ho);  /* the re-feed rows in one batch (mtp.rs rows_in) */
+            memcpy(hout, ho + (size_t)(keep - 1) * H, (size_t)H * 4);
+            free(ho);
+        }
         drafts[0] = draft_token(s, smp, hout, q_dense);
         for (int i = 1; i < k; i++) {
             memcpy(hprev, hout, (size_t)H * 4);
@@ -723,6 +883,9 @@ int oracle_spec_generate_s(OState *s, const uint32_t *prompt, int n, int n_out, 
     g_round_seconds = now_s() - t_rounds;
     free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted); free(q_dense);
     return c;
+fail:
+    free(lg); free(normed); free(hout); free(hprev); free(drafts); free(emitted); free(q_dense);
+    return -1;
 }
 
 int oracle_state_pos(OState *s) { return s->pos; }
@@ -792,7 +955,7 @@ int oracle_layer_f32(const int *dims, const float *fdims, const float *const *w,
     FMAT(up, OW_FFN_UP, m.ffn, m.hidden);
     FMAT(down, OW_FFN_DOWN, m.hidden, m.ffn);
 #undef FMAT
-    OLayerState st = {S, conv, K, V};
+    OLayerState st = {S, conv, K, V, NULL, NULL, NULL, NULL};
     L.attn = kind == OL_ATTENTION || kind == OL_DECODER_ATTENTION;
     const size_t H = (size_t)m.hidden;
     for (int i = 0; i < t; i++) {

@@ -65,6 +65,10 @@ void oracle_matmul_f32in(int type, const uint8_t *w, int rows, int cols, const f
 void oracle_matmul_act(int type, const uint8_t *w, int rows, int cols, const void *act, size_t act_stride,
                        int ncols, float *y);
 
+/* The matmuls run the AVX2 kernels (bit-identical to the scalar ones, blocked over up to 16 columns) when the CPU
+ * has AVX2; oracle_set_simd(0) forces the scalar kernels, 1 the AVX2 ones, -1 back to detection. */
+void oracle_set_simd(int on);
+
 float oracle_reduce8(const float *l);
 float oracle_sum_squares_8lane(const float *x, int n);
 float oracle_inv_rms(const float *x, int n, float eps);

@@ -85,6 +85,7 @@ def lib():
             "oracle_rng_seed": (None, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint64]),
             "oracle_rng_next": (ctypes.c_uint64, [ctypes.POINTER(ctypes.c_uint64)]),
             "oracle_state_get": (ctypes.c_long, [P, I, I, P]),
+            "oracle_set_simd": (None, [I]),
             "oracle_layer_f32": (I, [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_float),
                                      ctypes.POINTER(ctypes.c_void_p), I, P, I, I, P, P, P, P, P]),
         })
@@ -152,6 +153,11 @@ def set_libm(mode):
 
 def set_threads(n):
     lib().oracle_set_threads(n)
+
+
+def set_simd(on):
+    """1: the AVX2 matmul kernels (bit-identical to the scalar ones), 0: the scalar kernels, -1: by CPU detection."""
+    lib().oracle_set_simd(on)
 
 
 def row_bytes(t, cols):

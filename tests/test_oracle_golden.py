@@ -361,3 +361,37 @@ def test_sampler_accept_rule(orc):
     q2[outside] = 1.0
     ok, tok = s.accept(logits, q2, outside)
     assert not ok and tok in ids
+
+
+@pytest.mark.parametrize("t", [12, 13, 14, 8, 2])
+def test_simd_matmul_bit_identical_to_scalar(orc, t):
+    """The timed baseline's AVX2 kernels (blocked over up to 16 columns) give the scalar restatement's bits --
+    the reference asks the same of its own AVX2 path (tests/avx2.rs): random blocks, blocks at the integer
+    extremes, hostile activation rows, 1..17 columns."""
+    from helpers import hostile_rows, random_blocks
+
+    rows, cols = 37, 2048
+    w = random_blocks(t, rows, cols, seed=5 + t)
+    bb = {12: 144, 13: 176, 14: 210, 8: 34, 2: 18}[t]
+    wx = w.reshape(-1, bb).copy()
+    if t in (12, 13):
+        wx[::3, 4:] = 0xFF  # every third block: maximal codes, scales and mins
+    elif t == 14:
+        wx[::3, :192] = 0xFF
+        wx[::3, 192:208] = 0x80
+    elif t == 8:
+        wx[::3, 2:] = 0x80  # -128 codes
+    w = wx.reshape(-1)
+    x = np.concatenate([hostile_rows(cols, 3), np.random.default_rng(t).standard_normal((7, cols)).astype(np.float32)])
+    x = np.nan_to_num(x, posinf=0, neginf=0)
+    try:
+        orc.set_simd(0)
+        want = orc.matmul(t, w, rows, cols, x)
+        orc.set_simd(1)
+        got = orc.matmul(t, w, rows, cols, x)
+        for n in (1, 3, 16):
+            got_n = orc.matmul(t, w, rows, cols, x[:n])
+            assert np.array_equal(got_n.view(np.uint32), want[:n].view(np.uint32)), (t, n)
+    finally:
+        orc.set_simd(-1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
