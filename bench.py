@@ -153,8 +153,11 @@ def max_over_ranks(values, device):
 
 
 def oracle_spec_sample(path, k, prompt_len, rounds):
-    """The reference's greedy --spec k loop restated on the CPU (oracle/model.c, OpenMP over all host threads) on
-    the 27B checkpoint: a short prompt, then `rounds` rounds; returns (tok/s over the rounds, stats, cores)."""
+    """The reference's greedy --spec k loop on the host cores: the oracle (oracle/model.c) with its AVX2 kernels
+    (bit-identical to the scalar restatement) and the reference's batching -- the prompt in 16-row chunks and the
+    k + 1 verify rows through one blocked pass over the weights (matmul_t), the rollback by replaying the kept
+    rows' recurrence -- OpenMP over all host threads.  The given prompt length, then `rounds` rounds; returns
+    (tok/s over the rounds, s/round, stats with the prompt and ids, threads)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
@@ -164,12 +167,20 @@ def oracle_spec_sample(path, k, prompt_len, rounds):
     om = oracle.OracleModel(path)
     st = om.state(max_pos=prompt_len + (k + 1) * (rounds + 2) + 8)
     prompt = spec_prompt(om.vocab, SPEC_SEED + 1)[:prompt_len]
+    t0 = time.perf_counter()
     ids, stats, _ = st.spec_generate(prompt, 1 + rounds, k, stop=False)
+    total = time.perf_counter() - t0
     secs = stats["round_seconds"]
     emitted = len(ids) - 1
     om.close()
     stats["prompt"], stats["ids"] = prompt, ids
+    stats["prefill_seconds"] = total - secs
     return emitted / secs, secs / max(1, stats["rounds"]), stats, cores
+
+
+CPU_KIND = "port"
+CPU_VARIANT = ("the oracle's AVX2 kernels (bit-identical to its scalar restatement of kdot.rs), blocked over the verify "
+               "rows like matmul_t, batched prefill, replay rollback; OpenMP over every host thread")
 
 
 def gpu_spec_ids(model, k, prompt, n_ids):
@@ -186,21 +197,30 @@ def gpu_spec_ids(model, k, prompt, n_ids):
 def run_reference_spec(args, world, rank):
     if rank != 0:
         return
-    path = ensure_checkpoint(args.preset, SPEC_SEED)
+    # the checkpoint is written by a child process, so this arm maps none of the product's libraries
+    path = checkpoint_path(args.preset, SPEC_SEED)
+    if not os.path.exists(path):
+        import subprocess
+
+        subprocess.run([sys.executable, "-c", "import sys; sys.path.insert(0, sys.argv[1]); import bench; "
+                        "bench.ensure_checkpoint(sys.argv[2], int(sys.argv[3]))", ROOT, args.preset, str(SPEC_SEED)],
+                       check=True, cwd=ROOT)
     k = SPEC_K
-    # each step is one round; the CPU restatement needs tens of seconds per 27B round, so the run is capped
-    rounds = max(1, min(args.steps, 2))
-    tok_s, s_round, stats, cores = oracle_spec_sample(path, k, 4, rounds)
-    sample = (f"{stats['rounds']} --spec {k} rounds after a 4-token prompt on the {args.preset} checkpoint "
-              f"(of {args.steps} requested steps; {s_round:.1f} s/round)")
+    # the same workload as the GPU arm -- the 128-token prompt, then --spec 3 rounds -- with a bounded number of
+    # timed rounds (each a whole pass over the 17.8 GB of weights on the host cores)
+    rounds = max(2, min(args.steps, 6))
+    tok_s, s_round, stats, cores = oracle_spec_sample(path, k, PROMPT_LEN, rounds)
+    sample = (f"{stats['rounds']} --spec {k} rounds after the {PROMPT_LEN}-token prompt on the {args.preset} checkpoint "
+              f"(of {args.steps} requested steps; {s_round:.2f} s/round; prompt prefill {stats['prefill_seconds']:.1f} s)")
     line = {
         "metric": "decode tok/s (greedy, --spec 3) Qwen3.8-27B Q4_K_M", "value": round(tok_s, 5), "unit": "tok/s",
         "n_gpus": world, "steps": stats["rounds"], "warmup": 0, "ms_per_step": round(s_round * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "Q4_K_M weights x Q8_K activations, f32", "data": "synthetic",
-        "config": {"workload": f"{args.preset} --spec 3 (BASELINE config 4)", "k": k},
+        "config": {"workload": f"{args.preset} --spec 3, {PROMPT_LEN}-token prompt", "prompt": PROMPT_LEN, "k": k},
         "impl": "reference",
-        "cpu_baseline": {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": CPU_KIND,
+                         "variant": CPU_VARIANT, "sample": sample},
         "e2e": {"value": round(tok_s, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -502,6 +522,131 @@ def dominant_gemv_timing(dev, launches=200, n=4):
     return alg, ms
 
 
+BLOCK = {12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 2: (32, 18)}
+
+
+def synth_blocks(t, rows, cols, seed):
+    """Seeded random blocks of ggml type t whose f16 scales are finite (magnitudes 2^-3 .. 2^3): the config-2
+    weights for the types other than Q4_K."""
+    be, bb = BLOCK[t]
+    rng = np.random.default_rng(seed)
+    data = rng.integers(0, 256, size=(rows * (cols // be), bb), dtype=np.uint8)
+    for off in ((0, 2) if t in (12, 13) else (208,) if t == 14 else (0,)):
+        bits = data[:, off].astype(np.uint16) | (data[:, off + 1].astype(np.uint16) << 8)
+        fixed = (bits & 0x83FF) | ((12 + (bits >> 10) % 7) << 10)
+        data[:, off], data[:, off + 1] = (fixed & 0xFF).astype(np.uint8), (fixed >> 8).astype(np.uint8)
+    return data.reshape(-1)
+
+
+def gemv_table(dev):
+    """Config 2: every weight type of the model (tile layout) on W_up 17408 x 5120 and W_down 5120 x 17408 at N = 1,
+    2, 4 columns: CUDA-event time of back-to-back launches over rotating weight sets (> L2), the weight GB/s of the
+    reference bench (crates/cli/src/bench.rs:65-91: rows * row bytes / s) and the algorithmic GB/s (weights +
+    activation image + outputs)."""
+    import torch
+
+    import qdec
+
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    out = {}
+    names = {12: "Q4_K", 13: "Q5_K", 14: "Q6_K", 8: "Q8_0", 2: "Q4_0"}
+    for t in (12, 13, 14, 8, 2):
+        for rows, cols in (UP, DOWN):
+            be, bb = BLOCK[t]
+            wbytes = rows * (cols // be) * bb
+            sets = []
+            for s in range(N_SETS):
+                src = torch.from_numpy(synth_q4k(rows, cols, 300 + s) if t == 12 else synth_blocks(t, rows, cols, 300 + s)).to(dev)
+                dst = torch.empty_like(src)
+                qdec.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr(), sp)
+                del src
+                sets.append(dst)
+            tt = qdec.TILE[t]
+            x = torch.randn(4, cols, generator=torch.Generator().manual_seed(t), dtype=torch.float32).to(dev)
+            img = torch.empty(4 * qdec.image_row_bytes(tt, cols), dtype=torch.uint8, device=dev)
+            qdec.quantize_image(tt, x.data_ptr(), cols, 4, img.data_ptr(), sp)
+            y = torch.empty(4 * rows, dtype=torch.float32, device=dev)
+            for n in NS:
+                for i in range(6):
+                    qdec.gemv_image(tt, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
+                per = []
+                for b in range(5):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for i in range(12):
+                        qdec.gemv_image(tt, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    per.append(e0.elapsed_time(e1) / 12)
+                us = statistics.median(per) * 1e3
+                img_b = n * qdec.image_row_bytes(tt, cols)
+                out[f"{names[t]} {rows}x{cols} N={n}"] = {"us": round(us, 2), "weight_gb_s": round(wbytes / us / 1e3, 1),
+                                                         "alg_gb_s": round((wbytes + img_b + 4 * n * rows) / us / 1e3, 1)}
+            del sets
+            torch.cuda.empty_cache()
+    return out
+
+
+def plain_decode_timing(model, prompt, steps):
+    """Config 3: plain greedy decode (run.rs:329-350) after the prompt, `steps` tokens, CUDA-event time on the
+    state's stream; tokens/s and the weight bytes one token streams (model.rs:274) per second."""
+    import torch
+
+    st = model.new_state(spec_k=0, max_rows=32)
+    stream = torch.cuda.ExternalStream(st.stream)
+    x = st.prefill(prompt)
+    for _ in range(3):
+        x = st.step(x)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        x = st.step(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    st.free()
+    s_tok = ms / 1e3 / steps
+    return {"tokens": steps, "tok_s": round(1.0 / s_tok, 2), "s_per_token": round(s_tok, 6),
+            "weight_gb_s": round(model.info.decode_bytes / s_tok / 1e9, 1)}
+
+
+def long_kv_timing(path, dev_index, k, rounds, prompt_len=8064):
+    """Config 5 on one GPU: the KV cache grown to ~8.2K positions (an 8064-token prompt prefilled on the device),
+    then --spec 3 rounds; s/round from CUDA events."""
+    import torch
+
+    import qdec
+
+    max_pos = prompt_len + (rounds + 8) * (k + 1) * 2 + 64
+    m = qdec.Model(path, device=dev_index, max_pos=max_pos)
+    prompt = [int(v) for v in np.random.default_rng(SPEC_SEED + 9).integers(0, min(m.info.vocab, 248044), prompt_len)]
+    st = m.new_state(spec_k=k, max_rows=128)
+    stream = torch.cuda.ExternalStream(st.stream)
+    t0 = time.perf_counter()
+    x = st.spec_prefill(prompt)
+    prefill_s = time.perf_counter() - t0
+    for _ in range(3):
+        x = st.spec_round(x)[-1]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    emitted = 0
+    for _ in range(rounds):
+        em = st.spec_round(x)
+        emitted += len(em)
+        x = em[-1]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    pos = st.pos
+    st.free()
+    m.close()
+    return {"kv_positions": pos, "rounds": rounds, "s_per_round": round(ms / 1e3 / rounds, 6),
+            "tok_s": round(emitted / (ms / 1e3), 2), "prompt_prefill_s": round(prefill_s, 2)}
+
+
 def tp_spec_timing(path, args, world, rank, local, k, prompt, max_pos):
     """--spec k rounds of ONE sequence tensor-parallel over the `world` ranks (every rank runs the same rounds on its
     shard; the sharded activations are exchanged GPU to GPU): device time of the timed rounds on each rank's
@@ -691,6 +836,7 @@ def run_spec_qdec(args, world, rank, local):
     sc1 = ss.counters()
     ss.free()
     pre = prefill_timing(model, info, max_pos, SPEC_SEED + 7)
+    plain_res = plain_decode_timing(model, prompt, min(args.steps, 64)) if not args.quick else None
     if world > 1:
         import torch.distributed as dist
 
@@ -748,20 +894,27 @@ def run_spec_qdec(args, world, rank, local):
         # repacked in place (the checkpoint file sits in /dev/shm, so this is the memory-to-HBM path)
         "load": {"seconds": round(load_s, 3), "gb_s": round(info.weight_bytes / load_s / 1e9, 2)},
     }
+    if plain_res is not None:
+        line["plain_decode"] = plain_res
+    if not args.quick:
+        line["gemv"] = gemv_table(torch.device("cuda", local))
+        line["long_kv"] = long_kv_timing(path, local, k, min(args.steps, 20))
     if tp_res is not None:
         s_r, b = tp_res.pop("_s_round"), tp_res.pop("_bytes")
         if s_r:
             tp_res["round_frac_per_rank"] = round(b / s_r / 1e9 / peak, 4)
         line["tp"] = tp_res
     if world == 1 and not args.no_cpu_baseline:
-        tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, 2, 2)
-        line["cpu_baseline"] = {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": "port",
-                                "sample": f"{stats['rounds']} --spec {k} rounds after a 2-token prompt ({s_rnd:.1f} s/round)"}
+        tok_s, s_rnd, stats, cores = oracle_spec_sample(path, k, PROMPT_LEN, 3)
+        line["cpu_baseline"] = {"value": round(tok_s, 5), "unit": "tok/s", "cores": cores, "kind": CPU_KIND,
+                                "variant": CPU_VARIANT,
+                                "sample": f"{stats['rounds']} --spec {k} rounds after the {PROMPT_LEN}-token prompt "
+                                          f"({s_rnd:.2f} s/round; prompt prefill {stats['prefill_seconds']:.1f} s)"}
         # parity on the full 27B checkpoint: the GPU's ids for the CPU leg's prompt and round count
         want = stats["ids"]
         got = gpu_spec_ids(model, k, stats["prompt"], len(want))
         line["parity"] = {"ids_equal": got == want, "n_ids": len(want), "prompt_len": len(stats["prompt"]),
-                          "against": "the CPU oracle's --spec 3 loop on the same checkpoint (the cpu_baseline run)"}
+                          "against": "the CPU oracle's --spec 3 loop on the same checkpoint and prompt (the cpu_baseline run)"}
     print(json.dumps(line), flush=True)
 
 
@@ -774,6 +927,7 @@ def main():
     ap.add_argument("--workload", choices=["spec", "gemv"], default="spec")
     ap.add_argument("--preset", default="27b", help="synthetic checkpoint of the spec workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="only the headline rounds (no plain decode, GEMV table or 8K-KV run)")
     ap.add_argument("--no-tp", action="store_true", help="with --gpus > 1: replicas only (no tensor-parallel run)")
     ap.add_argument("--prompt-len", type=int, default=None,
                     help="prompt ids before the timed rounds (default 128; 8064 grows the KV cache to ~8192: config 5)")
