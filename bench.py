@@ -1,17 +1,23 @@
 """Benchmark of the qdec hot path on B200 (one process per GPU; torchrun for N > 1).
 
-Workload (the isolated K-quant GEMV microbench): Q4_K weight matrices W_up 17408 x 5120
-and W_down 5120 x 17408 (256-weight super-blocks, f16 d ~ U(1e-3, 4e-3) and dmin ~ U(0, 1e-3), 6-bit
-scales and mins ~ U{0..63}, 4-bit codes ~ U{0..15}, seeded) times x ~ N(0, 1) f32 activations quantised to
-Q8_K on the device.  One step = for N in (1, 2, 4): quantise x_up (N x 5120), GEMV W_up, quantise x_down
-(N x 17408), GEMV W_down -- 12 kernel launches, 6 weight passes.  Three weight sets (301 MB) rotate so no
-step finds its weights in the 126 MB L2.  Metric: weight bytes streamed / second (the reference bench's
-definition, crates/cli/src/bench.rs:65-91), whole job over all ranks.
+Default workload (`--workload spec`): `--spec 3` decoding of the 27B architecture (64 layers: 48 Gated DeltaNet
++ 16 gated GQA, hidden 5120, FFN 17408, vocabulary 248320, the MTP block) with synthetic Q4_K_M weights (seeded,
+the reference's type recipe), after a 128-token prompt prefilled as one batch.  One step = one speculative round
+(k = 3 MTP drafts, one verify pass over 4 rows, rollback, the MTP re-feed) replayed as one CUDA graph.  Metric:
+accepted tokens / second, whole job over all ranks (replicas, or one tensor-parallel model with --gpus N).  The
+JSON line also carries the plain-decode rate, the prefill rate, the K-quant GEMV table of the config-2 shapes
+(Q4_K / Q5_K / Q6_K / Q8_0 / Q4_0 at N = 1, 2, 4), an 8K-position KV run, the roofline of the dominant GEMV,
+parity against the CPU oracle and the CPU baseline (the AVX2 C restatement of the reference's decode on all host
+cores, on the same 128-token prompt).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qdec|reference]
+`--workload gemv`: the isolated K-quant GEMV microbench -- Q4_K W_up 17408 x 5120 and W_down 5120 x 17408 times
+N = 1, 2, 4 quantised columns, three rotating weight sets (301 MB) so no step finds its weights in the 126 MB L2;
+metric weight bytes streamed / second (crates/cli/src/bench.rs:65-91).
 
-`--impl reference` times the reference's CPU path (its C restatement in oracle/, OpenMP over all host
-threads, the reference's row-parallel matvec) on a bounded sample of the same workload.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qdec|reference] [--workload spec|gemv]
+
+`--impl reference` times the reference's CPU path (its C restatement in oracle/, all host threads) on a bounded
+sample of the same workload, without loading the product library.
 """
 import argparse
 import json
@@ -452,7 +458,7 @@ def run_qdec(args, world, rank, local):
 
 
 # ------------------------------------------------------------------------------------------------------
-# The --spec 3 decode workload: the full 27B architecture, synthetic Q4_K_M weights.
+# The --spec 3 decode workload: the full 27B architecture, synthetic Q4_K_M weights, a 128-token prompt.
 
 SPEC_K = 3
 PROMPT_LEN = 128

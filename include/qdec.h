@@ -85,7 +85,8 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
  * rows, rearranged for the GEMV): bytes of one row of `cols` values for weights of `ggml_type` (0 when the
  * type reads no image), quantising f32 rows into it, and the GEMV that reads it directly -- what qdec_gemv
  * does after rearranging block_q8_K / block_q8_0 columns, without that step.  K-quant types (ggml, split,
- * tile) read the Q8_K image, QDEC_TYPE_Q8_0_TILE / _Q4_0_TILE the Q8_0 image. */
+ * tile) read the Q8_K image, QDEC_TYPE_Q8_0_TILE / _Q4_0_TILE the Q8_0 image.  qdec_gemv_image wants the weights
+ * and the image 16-byte aligned (QDEC_EINVAL otherwise). */
 size_t qdec_image_row_bytes(int ggml_type, int cols);
 int qdec_quantize_image(int ggml_type, const float *x_dev, int n, int rows, void *img_dev, void *stream);
 int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const void *img_dev, int n_cols, float *y_dev,
@@ -98,9 +99,21 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
  * impl = 8, the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
  * over 4 warps, 3 = the same with two tiles per CTA); or, with impl = 9, the tensor-core prefill GEMM that K-quant
  * tile matrices take for many columns (config = the smallest column count routed there, 8 by default, 0 = never;
- * decode's 1..4 verify columns stay on the GEMV at any value >= 5).  Results do not depend on it; it exists for
+ * decode's 1..4 verify columns stay on the GEMV at any value >= 5); or, with impl = 7, the decode GEMV that K-quant
+ * tile matrices take for 1..7 columns (config 0 = by shape, 1..10 = a fixed split of tile groups, super-block
+ * phases, tiles per warp and windows in flight; impl 6 routes those matrices to the older image kernel).
+ * Results do not depend on it; it exists for
  * tests and sweeps.  No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
+
+/* Failure-handling self-test of one bounded device wait on the current device, in this process, without a peer
+ * or a fault: `which` = 0 runs a tensor-parallel exchange step whose peer lines never arrive (they carry the
+ * previous step's tag), 1 a decode GEMV whose first stage waits for bytes nothing sends.  Each wait must give up
+ * after wait_ms (1..10000), record its error word and let the kernel return with the context usable; the same work
+ * is then run normally and must give the right result.  QDEC_OK when all of that held, QDEC_ECUDA (with the step
+ * that misbehaved in qdec_last_error()) otherwise.  The engine's own waits give up the same way and surface as
+ * QDEC_ETIMEOUT.  No counterpart in the reference (its CPU code has no device waits). */
+int qdec_selftest_wait(int which, int wait_ms);
 
 /* Repack rows x cols of ggml Q6_K (src) into the split layout (dst, the same number of bytes, a distinct
  * buffer) that qdec_gemv reads as QDEC_TYPE_Q6_K_SPLIT.  No counterpart in the reference (a device layout). */
@@ -115,9 +128,15 @@ int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, vo
  * belongs to another allocator, or a decode loop that must stay allocation-free while it runs.  Same arguments,
  * same results as qdec_matvec, but the quantised columns live in a fixed array inside the library
  * (qdec_matvec_noalloc_max_bytes() bytes, held on every device that loads the library until exit); sizes that
- * do not fit are rejected with QDEC_EINVAL.  K-quant columns take cols/256 * 320 bytes each there (the library's
- * activation image), Q8_0/Q4_0 columns cols/32 * 34.  The first call on a device looks the array's address up, so make it
- * before any stream capture.  All calls on a device share the array: calls that overlap on the GPU race.
+ * do not fit are rejected with QDEC_EINVAL.  Bytes each column takes there, by the path the weights take:
+ *   QDEC_TYPE_*_TILE K-quants, QDEC_TYPE_Q6_K_SPLIT and 16-byte aligned ggml Q4_K / Q5_K: cols/256 * 320
+ *     (the library's Q8_K activation image);
+ *   other K-quants (ggml Q6_K, unaligned Q4_K / Q5_K): cols/256 * 292 (block_q8_K rows);
+ *   QDEC_TYPE_Q8_0_TILE / _Q4_0_TILE: cols/32 * 40 (the Q8_0 image);  ggml Q8_0 / Q4_0: cols/32 * 34 (block_q8_0);
+ *   F32: none.
+ * The first call on a device looks the array's address up and caches it, so make it before any stream capture;
+ * cudaDeviceReset invalidates that cached address, so a process that resets a device must not call this entry
+ * point on that device again.  All calls on a device share the array: calls that overlap on the GPU race.
  * This entry point has no counterpart in the reference, whose CPU matvec quantises into caller-owned rows. */
 int qdec_matvec_noalloc(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols,
                         float *y_dev, void *stream);

@@ -10,6 +10,7 @@
 #include "capi_util.h"
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tp.cuh"
 
 namespace qdec {
 
@@ -215,6 +216,7 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
     if (rc) return rc;
     if (!w_dev || !img_dev || !y_dev) return fail(QDEC_EINVAL, "qdec_gemv_image: null pointer");
     if (((uintptr_t)w_dev & 15) != 0) return fail(QDEC_EINVAL, "qdec_gemv_image: weights must be 16-byte aligned");
+    if (((uintptr_t)img_dev & 15) != 0) return fail(QDEC_EINVAL, "qdec_gemv_image: the image must be 16-byte aligned");
     cudaError_t e;
     if (ggml_type == T_Q8_0_TILE || ggml_type == T_Q4_0_TILE)
         e = launch_gemv_q80_img(ggml_type, (const uint8_t *)w_dev, rows, cols, img_dev, n_cols, y_dev, (cudaStream_t)stream, false);
@@ -249,6 +251,20 @@ int qdec_tune_gemv(int impl, int config) {
     set_gemv_impl(impl);
     set_gemv_v6_config(config);
     return QDEC_OK;
+}
+
+int qdec_selftest_wait(int which, int wait_ms) {
+    if (which < 0 || which > 1 || wait_ms <= 0 || wait_ms > 10000)
+        return fail(QDEC_EINVAL, "qdec_selftest_wait: which must be 0 or 1 and wait_ms in 1..10000");
+    const unsigned long long ns = (unsigned long long)wait_ms * 1000000ull;
+    const int rc = which == 0 ? selftest_exchange(ns) : selftest_gemv7_timeout(ns);
+    if (rc == 0) return QDEC_OK;
+    static const char *what[] = {"", "setting up", "the timed-out run did not complete as a kernel",
+                                 "the wait did not report that it gave up", "the normal run afterwards failed",
+                                 "the normal run afterwards reported an error", "the normal run afterwards gave wrong data",
+                                 "the pushed lines are wrong"};
+    return fail(QDEC_ECUDA, "qdec_selftest_wait(%s): %s", which == 0 ? "exchange poll" : "GEMV stage wait",
+                rc > 0 && rc < 8 ? what[rc] : "?");
 }
 
 int qdec_repack_q6k(const void *src_dev, int rows, int cols, void *dst_dev, void *stream) {

@@ -10,7 +10,9 @@
 // The array is a file-scope __device__ object of NOALLOC_SCRATCH_BYTES; every GPU that loads the library holds
 // one copy until the process exits.  Host code cannot use the array's name as a device address, so the first
 // call on each device looks the address up with cudaGetSymbolAddress (with that device current) and caches it;
-// make that first call before any stream capture.  All calls on a device share the one array and it keeps the
+// make that first call before any stream capture.  The cached address belongs to the device's primary context:
+// cudaDeviceReset destroys that context (and the module copy of the array with it), after which the cached value
+// is stale, so a process that resets a device must not call this entry point on that device again.  All calls on a device share the one array and it keeps the
 // last call's contents: two calls whose kernels overlap on the GPU (different streams, or host threads) race on
 // it.  Nothing in it has to start at zero: every call overwrites the bytes it reads.
 #include <cuda_runtime.h>

@@ -25,7 +25,7 @@
 #include <cstdlib>
 #include <thread>
 #include <memory>
-#include <unordered_set>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "engine.h"
@@ -193,13 +193,13 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
 
     // the data section, unchanged, in one allocation: read in 256 MiB chunks by several threads into pinned
     // staging (two buffers), each chunk's upload overlapping the next chunk's read.  A tensor-parallel rank
-    // instead reads what it keeps: the replicated tensors whole (on first use) and only its rows of the sharded
-    // ones, straight into their shard allocations.
+    // instead reads what it keeps, each into an allocation of its own: the replicated tensors whole (on first
+    // use) and only its rows of the sharded ones -- so a rank holds its share of the model, not all of it.
     const uint64_t data_bytes = g.file_size() - g.data_offset();
-    ck(cudaMalloc(&m->blob_, data_bytes + 256), "weights allocation");
-    m->weight_bytes = data_bytes;
     const bool per_rank = P.world > 1;
+    m->weight_bytes = per_rank ? 0 : data_bytes;
     if (!per_rank) {
+        ck(cudaMalloc(&m->blob_, data_bytes + 256), "weights allocation");
         const size_t CH = 256ull << 20;
         void* host = nullptr;
         ck(cudaHostAlloc(&host, 2 * CH, cudaHostAllocDefault), "pinned staging");
@@ -246,10 +246,22 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
             ck(cudaMemcpy(dst + o, stage.get(), n, cudaMemcpyHostToDevice), "weights upload");
         }
     };
-    std::unordered_set<const TensorInfo*> resident;  // (tensor-parallel) tensors already read whole
-    auto ptr = [&](const TensorInfo& t) {
-        if (per_rank && resident.insert(&t).second) upload(t.abs_offset, m->blob_ + t.rel_offset, t.byte_size);
-        return m->blob_ + t.rel_offset;
+    auto own_alloc = [&](uint64_t bytes, const char* what) {  // (tensor-parallel) an allocation the rank keeps
+        uint8_t* d = nullptr;
+        ck(cudaMalloc(&d, bytes + 256), what);
+        m->shard_allocs_.push_back(d);
+        m->weight_bytes += bytes;
+        return d;
+    };
+    std::unordered_map<const TensorInfo*, uint8_t*> resident;  // (tensor-parallel) tensors already read whole
+    auto ptr = [&](const TensorInfo& t) -> uint8_t* {
+        if (!per_rank) return m->blob_ + t.rel_offset;
+        auto it = resident.find(&t);
+        if (it != resident.end()) return it->second;
+        uint8_t* d = own_alloc(t.byte_size, "replicated tensor allocation");
+        upload(t.abs_offset, d, t.byte_size);
+        resident.emplace(&t, d);
+        return d;
     };
     // K-quant matrices are repacked in place (same bytes) into the tile layout the GEMV streams (rows % 8 == 0),
     // else Q6_K into the split layout; the embedding table keeps the ggml layout because rows of it are
@@ -280,7 +292,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         return type;
     };
     auto repack = [&](const TensorInfo& t, int rows, int cols) -> int {
-        return repack_at(m->blob_ + t.rel_offset, t.type, t.byte_size, rows, cols, t.name);
+        return repack_at(ptr(t), t.type, t.byte_size, rows, cols, t.name);
     };
     auto mat = [&](const std::string& name, uint64_t rows, uint64_t cols) {
         const TensorInfo& t = g.tensor(name);
@@ -311,9 +323,7 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     auto shard_copy = [&](const TensorInfo& t, uint64_t row_bytes, const Segs& segs, uint64_t& nrows) -> uint8_t* {
         nrows = 0;
         for (const auto& sg : segs) nrows += sg.second;
-        uint8_t* d = nullptr;
-        ck(cudaMalloc(&d, nrows * row_bytes + 256), "shard allocation");
-        m->shard_allocs_.push_back(d);
+        uint8_t* d = own_alloc(nrows * row_bytes, "shard allocation");
         uint64_t o = 0;
         for (const auto& sg : segs) {
             if (per_rank && !resident.count(&t)) upload(t.abs_offset + sg.first * row_bytes, d + o, sg.second * row_bytes);
@@ -449,9 +459,6 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         for (const LayerW& L : m->layers) lb += mats(L);
         m->decode_bytes = lb + m->lm_head.bytes + 4ull * H + m->embed.bytes / c.vocab_size;
         if (m->has_mtp) m->mtp_bytes = mats(m->mtp.block) + m->mtp.eh_proj.bytes;
-        for (const DevMat* d : {&m->lm_head}) m->weight_bytes += d->bytes;
-        for (const LayerW& L : m->layers) m->weight_bytes += mats(L);
-        if (m->has_mtp) m->weight_bytes += mats(m->mtp.block) + m->mtp.eh_proj.bytes;
     }
     m->load_secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     return m;
@@ -600,7 +607,7 @@ void State::sync() {
         if (xe) {
             const unsigned z = 0;
             cudaMemcpy(xerr_, &z, 4, cudaMemcpyHostToDevice);
-            throw std::runtime_error("tensor-parallel exchange: a peer's slice did not arrive in time (slot " +
+            throw std::runtime_error("tensor-parallel exchange: the poll gave up, a peer's slice did not arrive in time (slot " +
                                      std::to_string(xe & 0xffff) + ")");
         }
     }

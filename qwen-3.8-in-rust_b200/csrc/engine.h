@@ -95,7 +95,7 @@ class Model {
 
   private:
     uint8_t* blob_ = nullptr;
-    std::vector<void*> shard_allocs_;  // the rank's row slices of the sharded tensors
+    std::vector<void*> shard_allocs_;  // tensor parallel: the replicated tensors and the rank's row slices, each its own
 };
 
 struct SpecCounters {  // spec.rs:21-42

@@ -18,17 +18,21 @@
 //
 // Work split.  Four threads share a weight row (thread tg holds lanes 2tg, 2tg+1 and min lane tg), eight rows
 // make a tile (one tile block per super-block: 8 x the block bytes, contiguous, in the order the threads read
-// it), a warp owns R tiles.  A CTA of S warps splits the super-block range: warp w takes super-blocks w, w+S, ...
-// (S = 1: every chain stays in the owning thread's registers).  With S > 1 each warp writes its f32 lane terms
-// (d * lane) to shared memory and, after every window of S super-blocks, one owner thread per (tile, column,
-// row, lane) adds the window's terms in super-block order -- the reference's own chain of additions.  Short
-// matrices (5120 rows) take S > 1 so that enough warps stream their weights.
+// it), a warp owns R tiles.  A CTA is G x S warps: G groups of R tiles each, and S warps per group splitting the
+// super-block range (warp phase p takes super-blocks p, p+S, ...).  S = 1: every chain stays in the owning
+// thread's registers.  S > 1: each warp writes its f32 lane terms (d * lane) to shared memory and, after every
+// window of S super-blocks, one owner thread per (tile, column, row, lane) adds the window's terms in
+// super-block order -- the reference's own chain of additions.  Short matrices (5120 rows) take S > 1 so that
+// enough warps share the work.
 //
-// Data movement.  Weight bytes stream from HBM into registers with 16-byte non-allocating loads, D super-blocks
-// ahead per warp (a register ring; every warp-wide load is 512 contiguous bytes); the first D are requested
-// before griddepcontrol.wait, so the stream overlaps the kernel that produced the activations (weights are
-// never written after load).  Activation words are read through L1 (every warp of an SM reads the same few KB),
-// once per super-block and column for all R tiles of the warp.
+// Data movement.  One thread keeps D windows in flight with bulk asynchronous copies (cp.async.bulk, no
+// multicast) into a ring of shared-memory stages, each completing on its own mbarrier: per window a copy of S
+// contiguous tile blocks per tile and a copy of S contiguous image blocks per column, so the bytes in flight cost
+// no registers and the activation words are fetched once per CTA.  The weight copies of the first D windows are
+// issued before griddepcontrol.wait (weights are never written after load), overlapping the kernel that
+// produces the activations; the image copies after it.  A stage is refilled after a CTA barrier; every wait is
+// bounded in time, and a CTA whose copy never arrived records an error word, lets its other copies land and
+// returns.
 #include <algorithm>
 #include <cstdlib>
 
@@ -66,28 +70,6 @@ struct W7<T_Q6_K> {
     uint4 c0, c1, c2, sc;  // ql 8tg | ql 32+8tg; ql 64+8tg | ql 96+8tg; qh 128+8tg | qh 160+8tg; the row's scales
     uint32_t d;           // the row's f16 d (low half)
 };
-
-__device__ __forceinline__ uint2 ld_nc_u64_(const void* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-
-template <int TYPE>
-__device__ __forceinline__ void load_w7(const uint8_t* ts, int L, int rs, W7<TYPE>& f) {
-    f.c0 = ld_nc_u128(ts + L * 16);
-    f.c1 = ld_nc_u128(ts + 512 + L * 16);
-    if constexpr (TYPE == T_Q4_K) {
-        f.hdr = ld_nc_u128(ts + 1024 + rs * 16);
-    } else if constexpr (TYPE == T_Q5_K) {
-        f.qh = ld_nc_u64_(ts + 1024 + L * 8);
-        f.hdr = ld_nc_u128(ts + 1280 + rs * 16);
-    } else {
-        f.c2 = ld_nc_u128(ts + 1024 + L * 16);
-        f.sc = ld_nc_u128(ts + 1536 + rs * 16);
-        f.d = ld_nc_u16(ts + 1664 + rs * 2);
-    }
-}
 
 // The row-dependent decode of one super-block, shared by every column.
 template <int TYPE>
@@ -208,51 +190,149 @@ __device__ __forceinline__ float lane7(const Dec7<TYPE>& o, const uint32_t* xw, 
     }
 }
 
-template <int TYPE, int NC, int R, int S>
-struct Smem7 {
-    static constexpr int PER_SB = R * NC * 8 * 12;                        // one warp's terms of one super-block
-    static constexpr int TERMS = S > 1 ? 2 * S * PER_SB : 1;              // double-buffered windows
-    static constexpr int FIN = S > 1 ? R * NC * 8 * 12 : 1;
-};
-
 __device__ __forceinline__ void gd_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void gd_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-template <int TYPE, int NC, int R, int S, int D, int MINB>
-__global__ void __launch_bounds__(32 * S, MINB)
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init7(uint64_t* bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)));
+}
+__device__ __forceinline__ void mbar_expect7(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test7(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// How long a stage wait lasts before it gives up (device clock), and a test knob: extra bytes the first window's
+// barrier expects, which never arrive -- the failure-handling self-test's "data nothing sends".
+__device__ unsigned long long g7_wait_ns = 2000000000ull;
+__device__ unsigned g7_test_extra_tx = 0;
+
+__device__ __forceinline__ unsigned long long gtimer7() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// A wait that gives up after g7_wait_ns and returns false.
+__device__ __forceinline__ bool mbar_wait7(uint64_t* bar, uint32_t parity) {
+    if (mbar_test7(bar, parity)) return true;
+    const unsigned long long t0 = gtimer7(), lim = g7_wait_ns;
+    while (!mbar_test7(bar, parity))
+        if (gtimer7() - t0 > lim) return false;
+    return true;
+}
+// bytes global -> shared, completing on `bar` (no multicast); 16-byte aligned addresses, size a multiple of 16
+__device__ __forceinline__ void bulk7(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ unsigned int g7_error = 0;  // set when a bounded wait of this file's kernels gave up
+
+// Shared memory of a CTA: D stage buffers, each one window of S super-blocks for the CTA's G x R tiles (a copy of
+// S contiguous tile blocks per tile) and the NC activation columns (a copy of S contiguous image blocks per
+// column); then, with S > 1, the double-buffered lane terms and the final chains.
+template <int TYPE, int NC, int G, int S, int R, int D>
+struct Geo7 {
+    static constexpr int TB = G7<TYPE>::TB;
+    static constexpr int WST = G * R * S * TB;
+    static constexpr int STAGE = WST + NC * S * Q8K_IMG_BYTES;
+    static constexpr int PER_SB = R * NC * 8 * 12;  // one warp's terms of one super-block
+    static constexpr size_t BAR = 128;
+    static constexpr size_t ST0 = BAR;
+    static constexpr size_t TERMS = ST0 + (size_t)D * STAGE;
+    static constexpr size_t FIN = TERMS + (S > 1 ? (size_t)2 * G * S * PER_SB * 4 : 0);
+    static constexpr size_t BYTES = FIN + (S > 1 ? (size_t)G * R * NC * 8 * 12 * 4 : 0);
+    static_assert(D <= 16, "mbarriers");
+    static_assert(STAGE % 16 == 0, "stage alignment");
+};
+
+// One thread's share of a tile block held in shared memory (the same offsets as the global tile layout).
+template <int TYPE>
+__device__ __forceinline__ void lds_w7(const uint8_t* ts, int L, int rs, W7<TYPE>& f) {
+    auto v4 = [](const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); };
+    f.c0 = v4(ts + L * 16);
+    f.c1 = v4(ts + 512 + L * 16);
+    if constexpr (TYPE == T_Q4_K) {
+        f.hdr = v4(ts + 1024 + rs * 16);
+    } else if constexpr (TYPE == T_Q5_K) {
+        f.qh = *reinterpret_cast<const uint2*>(ts + 1024 + L * 8);
+        f.hdr = v4(ts + 1280 + rs * 16);
+    } else {
+        f.c2 = v4(ts + 1024 + L * 16);
+        f.sc = v4(ts + 1536 + rs * 16);
+        f.d = *reinterpret_cast<const uint16_t*>(ts + 1664 + rs * 2);
+    }
+}
+
+// CTA = G x S warps: warp w serves tile group w % G (R tiles of 8 rows) and super-block phase w / G, i.e.
+// super-blocks w/G, w/G + S, ... of its tiles.  Thread 0 keeps D windows of S super-blocks in flight.
+template <int TYPE, int NC, int G, int S, int R, int D>
+__global__ void __launch_bounds__(32 * G * S)
 kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
-    using G = G7<TYPE>;
-    using SM = Smem7<TYPE, NC, R, S>;
-    constexpr int TB = G::TB, LPC = G::LPC;
-    constexpr int CHAINS = R * NC * 8 * LPC;
-    constexpr int CPT = (CHAINS + 32 * S - 1) / (32 * S);  // chains per owner thread (S > 1)
-    __shared__ __align__(16) float terms[SM::TERMS];
-    __shared__ float fin[SM::FIN];
-    const int lane = threadIdx.x & 31, ws = threadIdx.x >> 5, rs = lane >> 2, tg = lane & 3;
-    // two matrices reading the same columns (e.g. ffn_gate and ffn_up): the CTAs of the first, then the second
-    const int ctas_a = (rows_a / 8 + R - 1) / R;
+    using G_ = G7<TYPE>;
+    using Geo = Geo7<TYPE, NC, G, S, R, D>;
+    constexpr int TB = G_::TB, LPC = G_::LPC, PER_SB = Geo::PER_SB;
+    constexpr int CHAINS = G * R * NC * 8 * LPC;
+    constexpr int NT = 32 * G * S;
+    constexpr int CPT = (CHAINS + NT - 1) / NT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_abort;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    uint8_t* stages = smem + Geo::ST0;
+    float* terms = reinterpret_cast<float*>(smem + Geo::TERMS);
+    float* fin = reinterpret_cast<float*>(smem + Geo::FIN);
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, gi = wid % G, si = wid / G;
+    const int rs = lane >> 2, tg = lane & 3;
+    const int ctas_a = (rows_a / 8 + G * R - 1) / (G * R);
     const bool second = (int)blockIdx.x >= ctas_a;
     const uint8_t* w = second ? w_b : w_a;
     const int rows = second ? rows_b : rows_a;
     float* y = second ? y_b : y_a;
     const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
     const int tiles = rows / 8;
-    const uint8_t* wt[R];
-#pragma unroll
-    for (int j = 0; j < R; j++) wt[j] = w + (size_t)min(bid * R + j, tiles - 1) * nb * TB;
+    const int nwin = (nb + S - 1) / S;
 
-    W7<TYPE> ring[D][R];
-#pragma unroll
-    for (int d = 0; d < D; d++) {
-        const int sb = d * S + ws;
-        if (sb < nb) {
-#pragma unroll
-            for (int j = 0; j < R; j++) load_w7<TYPE>(wt[j] + (size_t)sb * TB, lane, rs, ring[d][j]);
+    // window `win` into slot win % D: the weights (G*R copies of up to S tile blocks), then -- separately, after
+    // the activations exist -- the NC image copies; one expect_tx for both
+    auto win_sbs = [&](int win) { return min(S, nb - win * S); };
+    auto issue_w = [&](int win) {
+        uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE;
+        const int n = win_sbs(win);
+        mbar_expect7(&bar[win % D], (uint32_t)(n * (G * R * TB + NC * Q8K_IMG_BYTES)) + (win == 0 ? g7_test_extra_tx : 0u));
+        for (int k = 0; k < G * R; k++) {
+            const int t = min(bid * G * R + k, tiles - 1);
+            bulk7(st + (size_t)k * S * TB, w + ((size_t)t * nb + (size_t)win * S) * TB, (uint32_t)(n * TB), &bar[win % D]);
         }
+    };
+    auto issue_x = [&](int win) {
+        uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE + Geo::WST;
+        const int n = win_sbs(win);
+        for (int c = 0; c < NC; c++)
+            bulk7(st + (size_t)c * S * Q8K_IMG_BYTES, img + ((size_t)c * nb + (size_t)win * S) * Q8K_IMG_BYTES,
+                  (uint32_t)(n * Q8K_IMG_BYTES), &bar[win % D]);
+    };
+    if (tid == 0) {
+        s_abort = 0;
+        for (int d = 0; d < D; d++) mbar_init7(&bar[d]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int d = 0; d < D && d < nwin; d++) issue_w(d);  // weights are never written after load: before the wait
     }
     gd_wait();  // the activation image is the previous kernel's output
     gd_launch();
+    if (tid == 0)
+        for (int d = 0; d < D && d < nwin; d++) issue_x(d);
+    __syncthreads();
 
     float acc[R][NC][2], accm[R][NC];  // S == 1: this thread's chains
     float cacc[CPT];                   // S > 1: the chains this thread owns
@@ -263,81 +343,86 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
 #pragma unroll
     for (int c = 0; c < CPT; c++) cacc[c] = 0.0f;
 
-    const int nwin = (nb + S - 1) / S;
-    for (int w0 = 0; w0 < nwin; w0 += D) {
+    for (int win = 0; win < nwin; win++) {
+        const int slot = win % D;
+        const bool ok = mbar_wait7(&bar[slot], (uint32_t)((win / D) & 1));
+        if (!ok) s_abort = 1;
+        const int sb = win * S + si;
+        if (ok && sb < nb) {
+            const uint8_t* st = stages + (size_t)slot * Geo::STAGE;
+            Dec7<TYPE> dec[R];
 #pragma unroll
-        for (int d = 0; d < D; d++) {
-            const int win = w0 + d;
-            if (win >= nwin) break;  // uniform over the CTA
-            const int sb = win * S + ws;
-            float* tb = terms + (size_t)((win & 1) * S + ws) * SM::PER_SB;
-            if (sb < nb) {
-                Dec7<TYPE> dec[R];
+            for (int j = 0; j < R; j++) {
+                W7<TYPE> f;
+                lds_w7<TYPE>(st + ((size_t)(gi * R + j) * S + si) * TB, lane, rs, f);
+                decode7<TYPE>(f, tg, dec[j]);
+            }
+            float* tb = terms + (size_t)(((win & 1) * S + si) * G + gi) * PER_SB;
 #pragma unroll
-                for (int j = 0; j < R; j++) decode7<TYPE>(ring[d][j], tg, dec[j]);
-                if (sb + D * S < nb) {
+            for (int n = 0; n < NC; n++) {
+                const uint8_t* xb = st + Geo::WST + (size_t)(n * S + si) * Q8K_IMG_BYTES;
+                uint32_t xw[16];
 #pragma unroll
-                    for (int j = 0; j < R; j++) load_w7<TYPE>(wt[j] + (size_t)(sb + D * S) * TB, lane, rs, ring[d][j]);
+                for (int c = 0; c < 4; c++) {
+                    const uint4 v = reinterpret_cast<const uint4*>(xb + 64 * tg)[c];
+                    xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
                 }
+                const float dx = *reinterpret_cast<const float*>(xb + Q8K_IMG_D);
+                uint32_t q8s = 0;
+                uint2 bsp2 = make_uint2(0, 0);
+                if constexpr (G_::MINS) q8s = reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S)[tg];
+                else bsp2 = reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP)[tg];
 #pragma unroll
-                for (int n = 0; n < NC; n++) {
-                    const uint8_t* xb = img + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
-                    uint32_t xw[16];
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const uint4 v = __ldg(reinterpret_cast<const uint4*>(xb + 64 * tg) + c);
-                        xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
+                for (int j = 0; j < R; j++) {
+                    const float dd = __fmul_rn(dx, dec[j].dw);  // d = dx * d_w (kdot.rs:50)
+                    const float t0 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp2.x));
+                    const float t1 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp2.y));
+                    float tm = 0.0f;
+                    if constexpr (G_::MINS) {  // (-dx * dmin) * (mn[2i] q8s[2i] + mn[2i+1] q8s[2i+1]), i = tg
+                        const float prod = __fsub_rn(__int_as_float(dp2a_lo_s(q8s, dec[j].mpair, (int)G7_MAGIC_I)), G7_MAGIC_F);
+                        tm = __fmul_rn(__fmul_rn(-dx, dec[j].dminw), prod);
                     }
-                    const float dx = __ldg(reinterpret_cast<const float*>(xb + Q8K_IMG_D));
-                    uint32_t bsp = 0, q8s = 0;
-                    if constexpr (G::MINS) q8s = __ldg(reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S) + tg);
-                    else bsp = 0;  // read per lane below
-                    uint2 bsp2 = make_uint2(0, 0);
-                    if constexpr (!G::MINS) bsp2 = __ldg(reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP) + tg);
-#pragma unroll
-                    for (int j = 0; j < R; j++) {
-                        const float dd = __fmul_rn(dx, dec[j].dw);  // d = dx * d_w (kdot.rs:50)
-                        float t0, t1;
-                        if constexpr (G::MINS) {
-                            t0 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp));
-                            t1 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp));
-                        } else {
-                            t0 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp2.x));
-                            t1 = __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp2.y));
-                        }
-                        float tm = 0.0f;
-                        if constexpr (G::MINS) {  // (-dx * dmin) * (mn[2i] q8s[2i] + mn[2i+1] q8s[2i+1]), i = tg
-                            const float prod = __fsub_rn(__int_as_float(dp2a_lo_s(q8s, dec[j].mpair, (int)G7_MAGIC_I)), G7_MAGIC_F);
-                            tm = __fmul_rn(__fmul_rn(-dx, dec[j].dminw), prod);
-                        }
-                        if constexpr (S == 1) {
-                            acc[j][n][0] = __fadd_rn(acc[j][n][0], t0);
-                            acc[j][n][1] = __fadd_rn(acc[j][n][1], t1);
-                            if constexpr (G::MINS) accm[j][n] = __fadd_rn(accm[j][n], tm);
-                        } else {
-                            float* t = tb + ((j * NC + n) * 8 + rs) * 12;
-                            *reinterpret_cast<float2*>(t + 2 * tg) = make_float2(t0, t1);
-                            if constexpr (G::MINS) t[8 + tg] = tm;
-                        }
+                    if constexpr (S == 1) {
+                        acc[j][n][0] = __fadd_rn(acc[j][n][0], t0);
+                        acc[j][n][1] = __fadd_rn(acc[j][n][1], t1);
+                        if constexpr (G_::MINS) accm[j][n] = __fadd_rn(accm[j][n], tm);
+                    } else {
+                        float* t = tb + ((j * NC + n) * 8 + rs) * 12;
+                        *reinterpret_cast<float2*>(t + 2 * tg) = make_float2(t0, t1);
+                        if constexpr (G_::MINS) t[8 + tg] = tm;
                     }
                 }
             }
-            if constexpr (S > 1) {
-                __syncthreads();
-                // the owners add this window's terms in super-block order
-                const float* tw = terms + (size_t)(win & 1) * S * SM::PER_SB;
-                const int nsb = min(S, nb - win * S);
+        }
+        __syncthreads();  // every warp is done with this slot (and has written its terms)
+        if (s_abort) {
+            // a copy never arrived: record it, let the copies still in flight (this window's included) land, each wait
+                // bounded, and stop
+            if (tid == 0) {
+                atomicCAS(&g7_error, 0u, 0x700u | (unsigned)TYPE);
+                for (int k = win; k < nwin && k < win + D; k++) mbar_wait7(&bar[k % D], (uint32_t)((k / D) & 1));
+            }
+            return;
+        }
+        if (tid == 0 && win + D < nwin) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the async refill
+            issue_w(win + D);
+            issue_x(win + D);
+        }
+        if constexpr (S > 1) {  // the owners add this window's terms in super-block order
+            const int nsb = win_sbs(win);
 #pragma unroll
-                for (int c = 0; c < CPT; c++) {
-                    const int ci = threadIdx.x + c * 32 * S;
-                    if (ci < CHAINS) {
-                        const int slot = (ci / LPC) * 12 + ci % LPC;
-                        float a = cacc[c];
+            for (int c = 0; c < CPT; c++) {
+                const int ci = tid + c * NT;
+                if (ci < CHAINS) {
+                    const int g = ci / (R * NC * 8 * LPC), r = ci % (R * NC * 8 * LPC);
+                    const int slot_i = (r / LPC) * 12 + r % LPC;
+                    const float* tw = terms + (size_t)((win & 1) * S * G + g) * PER_SB + slot_i;
+                    float a = cacc[c];
 #pragma unroll
-                        for (int k = 0; k < S; k++)
-                            if (k < nsb) a = __fadd_rn(a, tw[k * SM::PER_SB + slot]);
-                        cacc[c] = a;
-                    }
+                    for (int k = 0; k < S; k++)
+                        if (k < nsb) a = __fadd_rn(a, tw[(size_t)k * G * PER_SB]);
+                    cacc[c] = a;
                 }
             }
         }
@@ -354,46 +439,56 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
                 for (int g = 0; g < 8; g++) l8[g] = __shfl_sync(0xffffffffu, acc[j][n][g & 1], base + (g >> 1));
 #pragma unroll
                 for (int m = 0; m < 4; m++) m4[m] = __shfl_sync(0xffffffffu, accm[j][n], base + m);
-                const int tile = bid * R + j;
+                const int tile = (bid * G + gi) * R + j;
                 if (tg == 0 && tile < tiles) {
                     float v = reduce8(l8);
-                    if constexpr (G::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
+                    if constexpr (G_::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
                     y[(size_t)n * rows + tile * 8 + rs] = v;
                 }
             }
     } else {
 #pragma unroll
         for (int c = 0; c < CPT; c++) {
-            const int ci = threadIdx.x + c * 32 * S;
-            if (ci < CHAINS) fin[(ci / LPC) * 12 + ci % LPC] = cacc[c];
+            const int ci = tid + c * NT;
+            if (ci < CHAINS) {
+                const int g = ci / (R * NC * 8 * LPC), r = ci % (R * NC * 8 * LPC);
+                fin[(size_t)g * R * NC * 8 * 12 + (r / LPC) * 12 + r % LPC] = cacc[c];
+            }
         }
         __syncthreads();
-        for (int o = threadIdx.x; o < R * NC * 8; o += 32 * S) {
-            const int r = o % 8, n = (o / 8) % NC, j = o / (8 * NC);
-            const float* f = fin + o * 12;
+        for (int o = tid; o < G * R * NC * 8; o += NT) {
+            const int r = o % 8, n = (o / 8) % NC, j = (o / (8 * NC)) % R, g = o / (8 * NC * R);
+            const float* f = fin + (size_t)o * 12;
             float v = reduce8(f);
-            if constexpr (G::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(f[8], f[10]), __fadd_rn(f[9], f[11])));
-            const int tile = bid * R + j;
+            if constexpr (G_::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(f[8], f[10]), __fadd_rn(f[9], f[11])));
+            const int tile = (bid * G + g) * R + j;
             if (tile < tiles) y[(size_t)n * rows + tile * 8 + r] = v;
         }
     }
 }
 
-template <int TYPE, int NC, int R, int S, int D, int MINB>
+template <int TYPE, int NC, int G, int S, int R, int D>
 cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                     const void* img, cudaStream_t s, bool pdl) {
+    using Geo = Geo7<TYPE, NC, G, S, R, D>;
+    auto kern = kq_gemv7_kernel<TYPE, NC, G, S, R, D>;
+    static bool attr_done = false;  // per instantiation
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Geo::BYTES);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((rows_a / 8 + R - 1) / R + (w_b ? (rows_b / 8 + R - 1) / R : 0));
-    cfg.blockDim = dim3(32 * S);
-    cfg.dynamicSmemBytes = 0;
+    cfg.gridDim = dim3((rows_a / 8 + G * R - 1) / (G * R) + (w_b ? (rows_b / 8 + G * R - 1) / (G * R) : 0));
+    cfg.blockDim = dim3(32 * G * S);
+    cfg.dynamicSmemBytes = Geo::BYTES;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kq_gemv7_kernel<TYPE, NC, R, S, D, MINB>, w_a, rows_a, y_a, w_b, rows_b, y_b, nb,
-                              (const uint8_t*)img);
+    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
 }
 
 int g_cfg7 = [] {
@@ -401,28 +496,26 @@ int g_cfg7 = [] {
     return e ? atoi(e) : 0;
 }();
 
-// Configurations (R tiles per warp, S warps splitting the super-blocks, D super-blocks in flight per warp).
+// Configurations (G tile groups, S super-block phases, R tiles per warp, D windows in flight).
 template <int TYPE, int NC>
 cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                         const void* img, cudaStream_t s, bool pdl) {
     if (cfg == 0) {
         const int rows = rows_a + (w_b ? rows_b : 0);
-        if (rows >= 16384) cfg = 1;
-        else if (rows >= 8192) cfg = 4;
-        else cfg = 5;
+        if (rows >= 16384) cfg = 2;
+        else cfg = 8;
     }
-    // (R, S, D, min CTAs per SM -- which caps the registers: 65536 / (32 S MINB))
     switch (cfg) {
-    case 1: return launch7<TYPE, NC, 1, 1, 2, 16>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 2: return launch7<TYPE, NC, 1, 1, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 3: return launch7<TYPE, NC, 1, 1, 3, 12>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 4: return launch7<TYPE, NC, 1, 2, 2, 8>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 5: return launch7<TYPE, NC, 1, 4, 2, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 6: return launch7<TYPE, NC, 1, 8, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 7: return launch7<TYPE, NC, 2, 1, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 8: return launch7<TYPE, NC, 1, 4, 3, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 9: return launch7<TYPE, NC, 1, 2, 3, 6>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    default: return launch7<TYPE, NC, 1, 1, 4, 12>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 1: return launch7<TYPE, NC, 4, 1, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch7<TYPE, NC, 4, 1, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch7<TYPE, NC, 4, 1, 1, 6>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4: return launch7<TYPE, NC, 8, 1, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 5: return launch7<TYPE, NC, 2, 2, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 6: return launch7<TYPE, NC, 2, 1, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 7: return launch7<TYPE, NC, 1, 4, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 8: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 9: return launch7<TYPE, NC, 2, 4, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    default: return launch7<TYPE, NC, 1, 8, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }
 
@@ -443,9 +536,69 @@ bool gemv7_supported(int type) { return type == T_Q4_K_TILE || type == T_Q5_K_TI
 
 void set_gemv7_config(int cfg) { g_cfg7 = cfg; }
 
+unsigned read_gemv7_error(bool clear) {
+    unsigned v = 0;
+    cudaMemcpyFromSymbol(&v, g7_error, sizeof v);
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g7_error, &z, sizeof z);
+    }
+    return v;
+}
+
+// Failure-handling self-test: a decode GEMV whose first stage waits for bytes nothing sends must give up after
+// wait_ns, record its error word and leave the context usable; the same GEMV run normally afterwards must give the
+// right result (zero weights: zeros).  Returns 0, or a code naming the half that misbehaved.
+int selftest_gemv7_timeout(unsigned long long wait_ns) {
+    const int rows = 64, cols = 256;
+    uint8_t *w = nullptr, *img = nullptr;
+    float* y = nullptr;
+    cudaStream_t st = nullptr;
+    int rc = 0;
+    if (cudaMalloc(&w, (size_t)rows / 8 * 1152) || cudaMalloc(&img, Q8K_IMG_BYTES) || cudaMalloc(&y, rows * 4) ||
+        cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking))
+        rc = 1;
+    if (!rc) {
+        cudaMemset(w, 0, (size_t)rows / 8 * 1152);
+        cudaMemset(img, 0, Q8K_IMG_BYTES);
+        cudaMemset(y, 0xff, rows * 4);
+        read_gemv7_error(true);
+        const unsigned extra = 16;
+        cudaMemcpyToSymbol(g7_test_extra_tx, &extra, sizeof extra);
+        cudaMemcpyToSymbol(g7_wait_ns, &wait_ns, sizeof wait_ns);
+        if (launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            rc = 2;  // the timed-out run must still complete as a kernel
+        else if ((read_gemv7_error(true) & 0xff00u) != 0x700u)
+            rc = 3;  // the wait did not report that it gave up
+        const unsigned zero = 0;
+        const unsigned long long dflt = 2000000000ull;
+        cudaMemcpyToSymbol(g7_test_extra_tx, &zero, sizeof zero);
+        cudaMemcpyToSymbol(g7_wait_ns, &dflt, sizeof dflt);
+        if (!rc) {
+            float h[64];
+            if (launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess || cudaMemcpy(h, y, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
+                rc = 4;
+            else if (read_gemv7_error(true) != 0)
+                rc = 5;
+            else
+                for (int i = 0; i < rows && !rc; i++)
+                    if (h[i] != 0.0f) rc = 6;  // the normal run after the timeout gives the right result
+        }
+    }
+    if (st) cudaStreamDestroy(st);
+    cudaFree(w);
+    cudaFree(img);
+    cudaFree(y);
+    return rc;
+}
+
 cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
                          int cols, const void* img, int ncols, cudaStream_t s, bool pdl) {
     if (rows_a % 8 || (w_b && rows_b % 8) || cols % QK_K) return cudaErrorInvalidValue;
+    // the bulk copies need 16-byte aligned weights and activation image
+    if (((uintptr_t)w_a | (uintptr_t)w_b | (uintptr_t)img) & 15) return cudaErrorMisalignedAddress;
     if (rows_a <= 0 || ncols <= 0) return cudaSuccess;
     const int nb = cols / QK_K;
     for (int c0 = 0; c0 < ncols; c0 += 4) {  // columns beyond 4 in groups of at most 4

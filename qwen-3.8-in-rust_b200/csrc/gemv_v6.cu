@@ -1250,7 +1250,8 @@ unsigned read_kernel_error(bool clear) {
         cudaMemcpyToSymbol(g_kernel_error, &z, sizeof z);
     }
     const unsigned t = read_gemm_tc_error(clear);
-    return v ? v : t;
+    const unsigned g7 = read_gemv7_error(clear);
+    return v ? v : t ? t : g7;
 }
 
 }  // namespace qdec

@@ -73,6 +73,8 @@ bool gemv7_supported(int type);
 void set_gemv7_config(int cfg);  // 0 = automatic by shape; 1..8 a fixed configuration (tests, sweeps)
 cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
                          int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
+unsigned read_gemv7_error(bool clear);  // the error word of gemv7.cu's bounded waits (0 = none)
+int selftest_gemv7_timeout(unsigned long long wait_ns);  // failure-handling self-test of the stage wait (0 = as designed)
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
 // Prompt-prefill GEMM on the tensor cores (gemm_tc.cu): K-quant tile matrices (one, or two reading the same

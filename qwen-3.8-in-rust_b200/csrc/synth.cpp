@@ -217,7 +217,7 @@ struct Dims {
 };
 
 bool preset(const std::string &p, Dims &d, std::string &err) {
-    // "tiny": the reference's CPU-runnable toy; "27b": docs/model-facts.md:26-76;
+    // "tiny": the reference's CPU-runnable toy (a few layers of small widths); "27b": docs/model-facts.md:26-76;
     // "27b-L<n>": the 27B dimensions with n layers (n a multiple of the attention interval), for parity runs.
     if (p == "tiny") {
         d = {256, 4, 768, 4096, 4, 2, 64, 16, 4, 2, 64, 4, 256, 4, {3, 3, 2, 0}, "Qwen3.8 tiny synthetic"};

@@ -65,6 +65,7 @@ def lib():
             "qdec_tune_gemv": [I, I],
             "qdec_quantize_image": [I, P, I, I, P, P],
             "qdec_gemv_image": [I, P, I, I, P, I, P, P],
+            "qdec_selftest_wait": [I, I],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
@@ -182,13 +183,21 @@ GEMV7_CONFIGS = 10
 
 def tune_gemv(impl=0, config=0):
     """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
-    image kernel's configuration (0 automatic, 1..35); impl 8 the Q8_0/Q4_0 tile kernel (0..3); impl 9 the
-    smallest column count of the tensor-core prefill GEMM (default 8, 0 never). Results are identical for every
-    value."""
+    image kernel's configuration (0 automatic, 1..35); impl 7 the decode GEMV of K-quant tile matrices (0 by
+    shape, 1..10; impl 6 sends those matrices to the older image kernel); impl 8 the Q8_0/Q4_0 tile kernel
+    (0..3); impl 9 the smallest column count of the tensor-core prefill GEMM (default 8, 0 never). Results are
+    identical for every value."""
     _check(lib().qdec_tune_gemv(impl, config))
 
 
 PREFILL_GEMM_MIN_COLS = 8
+
+
+def selftest_wait(which, wait_ms=200):
+    """Run a bounded device wait into its limit on the current device, then the same work normally
+    (0 = the tensor-parallel exchange poll, 1 = the decode GEMV's stage wait); raises QdecError when the wait
+    did not give up and report as designed, or the normal run afterwards failed."""
+    _check(lib().qdec_selftest_wait(which, wait_ms))
 
 
 def repack_tiles(t, src_ptr, rows, cols, dst_ptr, stream=0):

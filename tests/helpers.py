@@ -58,3 +58,52 @@ def bits_equal(a, b):
     a = np.ascontiguousarray(a, dtype=np.float32)
     b = np.ascontiguousarray(b, dtype=np.float32)
     return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def gguf_tensors(path):
+    """The tensor index of a GGUF v3 file: [(name, ggml type, dims (innermost first), bytes)] -- the header layout
+    of crates/core/src/gguf.rs:483, read independently of the library."""
+    import struct
+
+    with open(path, "rb") as f:
+        buf = f.read(64 << 20)
+    o = 0
+
+    def take(fmt):
+        nonlocal o
+        v = struct.unpack_from("<" + fmt, buf, o)
+        o += struct.calcsize("<" + fmt)
+        return v[0] if len(v) == 1 else v
+
+    def string():
+        nonlocal o
+        n = take("Q")
+        s = buf[o:o + n].decode()
+        o += n
+        return s
+
+    scalar = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
+
+    def value(t):
+        if t == 8:
+            return string()
+        if t == 9:
+            et, n = take("I"), take("Q")
+            return [value(et) for _ in range(n)]
+        return take(scalar[t])
+
+    assert buf[:4] == b"GGUF" and take("4sI")[1] == 3
+    n_t, n_kv = take("Q"), take("Q")
+    for _ in range(n_kv):
+        string()
+        value(take("I"))
+    out = []
+    for _ in range(n_t):
+        name = string()
+        dims = [take("Q") for _ in range(take("I"))]
+        t = take("I")
+        take("Q")
+        n = int(np.prod(dims))
+        be, bb = {0: (1, 4), 1: (1, 2), **LAYOUT}[t]
+        out.append((name, t, dims, n // be * bb))
+    return out

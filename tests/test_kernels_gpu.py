@@ -108,7 +108,8 @@ def test_gemv_real_weights_bit_exact(q, orc, name, t):
 
 @pytest.mark.parametrize("rows,cols", [(17408, 5120), (5120, 17408)])
 def test_gemv_config2_full_size_bit_exact(q, orc, rows, cols):
-    """The BASELINE config-2 shapes, Q4_K, N = 4: every output bit-identical to the oracle."""
+    """The GEMV microbench shapes (17408 x 5120 and 5120 x 17408), Q4_K, N = 4: every output bit-identical to the
+    oracle."""
     t = 12
     w = random_blocks(t, rows, cols, seed=rows)
     x = np.random.default_rng(9).standard_normal((4, cols)).astype(np.float32)

@@ -177,3 +177,41 @@ def test_forced_drafts_every_acceptance_count_and_carried_state_27b(m27, o27):
         assert o is not None and o.size == v.size, (layer, what)
         bad = np.flatnonzero(_bits(v) != _bits(o))
         assert bad.size == 0, f"carried state {(layer, what)} differs from the oracle's in {bad.size} places"
+
+
+# tensors a tensor-parallel rank slices by rows (each row on exactly one rank at these dimensions); every other
+# tensor is held whole by every rank, and the three per-head DeltaNet vectors are also sliced from that copy
+SLICED = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight", "attn_qkv.weight", "attn_gate.weight",
+          "ssm_alpha.weight", "ssm_beta.weight", "ssm_out.weight", "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight",
+          "nextn.eh_proj.weight")
+VEC_SLICED = ("ssm_a", "ssm_dt.bias", "ssm_conv1d.weight")
+
+
+def test_tp_rank_holds_its_share_not_the_whole_model(ck27):
+    """A tensor-parallel rank allocates the replicated tensors plus its slices, not the whole data section: over
+    the two ranks of world 2 the weight bytes add up to 2 x replicated + every sliced byte once, each rank's device
+    memory grows by its weight bytes (plus the RoPE tables and allocation rounding), well under the whole model."""
+    import qdec
+    from helpers import gguf_tensors
+
+    ts = gguf_tensors(ck27)
+    total = sum(b for _, _, _, b in ts)
+    names = {n for n, _, _, _ in ts}
+    tied = "output.weight" not in names
+    sliced = sum(b for n, _, _, b in ts if n.endswith(SLICED) or n == "output.weight")
+    replicated = total - sliced
+    vec_sliced = sum(b for n, _, _, b in ts if n.endswith(VEC_SLICED))
+    lm_from_embd = sum(b for n, _, _, b in ts if n == "token_embd.weight") if tied else 0
+    got = []
+    for rank in range(2):
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        m = qdec.Model(ck27, max_pos=64, tp=(rank, 2))
+        torch.cuda.synchronize()
+        grew = free0 - torch.cuda.mem_get_info()[0]
+        wb = m.info.weight_bytes
+        m.close()
+        got.append(wb)
+        assert wb < 0.75 * total, f"rank {rank} holds {wb} of {total} bytes"
+        assert wb <= grew <= wb + (512 << 20), f"rank {rank}: device memory grew by {grew}, weight bytes {wb}"
+    assert sum(got) == 2 * replicated + sliced + vec_sliced + lm_from_embd

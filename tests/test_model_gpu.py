@@ -1,5 +1,5 @@
-"""GPU parity of the whole decode path (the tiny synthetic Qwen3.8-style checkpoint) against
-the CPU oracle: greedy ids, per-layer hidden states and logits, the --spec 3 loop (ids identical to plain decoding
+"""GPU parity of the whole decode path (the tiny synthetic Qwen3.8-style checkpoint, the reference's CPU-runnable
+toy) against the CPU oracle: greedy ids, per-layer hidden states and logits, the --spec 3 loop (ids identical to plain decoding
 and to the oracle, MTP drafts identical), and forced drafts that exercise every acceptance count
 (the device of crates/core/tests/spec_identity.rs)."""
 import numpy as np
