@@ -187,6 +187,11 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
     m->device = opt.device;
     m->max_pos = opt.max_pos;
     m->tp = make_tp_plan(m->cfg, opt.tp_rank, opt.tp_world);
+    if (!deltanet_dims_supported((int)m->cfg.dn_head_dim_k, (int)m->cfg.dn_head_dim_v))
+        throw ConfigError("no device kernel for DeltaNet heads of key dim " + std::to_string(m->cfg.dn_head_dim_k) + " and value dim " +
+                          std::to_string(m->cfg.dn_head_dim_v) + " (key 64 or 128, value 32..128 in steps of 32)");
+    if (!attention_dims_supported((int)m->cfg.head_dim_k))
+        throw ConfigError("no device kernel for attention heads of dim " + std::to_string(m->cfg.head_dim_k) + " (64..256 in steps of 64)");
     ck(cudaSetDevice(opt.device), "cudaSetDevice");
     const ModelConfig& c = m->cfg;
     const TpPlan& P = m->tp;

@@ -274,6 +274,162 @@ __device__ __forceinline__ void lds_w7(const uint8_t* ts, int L, int rs, W7<TYPE
     }
 }
 
+// Streaming form for matrices with enough tiles to fill the GPU with one warp per R tiles (S = 1): every warp
+// streams its own tiles' super-blocks through a private ring of D stages of P super-blocks (one bulk copy of P
+// contiguous tile blocks per tile and stage, completing on the warp's own mbarrier), so warps never wait for one
+// another; the activation image of all NC columns and super-blocks is copied once per CTA and stays resident.
+// Chains stay in the owning thread's registers, in super-block order.
+template <int TYPE, int NC, int G, int R, int D, int P>
+struct GeoS7 {
+    static constexpr int TB = G7<TYPE>::TB;
+    static constexpr size_t BAR = 1024;                   // x barrier + G x D stage barriers
+    static constexpr size_t STAGE = (size_t)R * P * TB;  // one warp's stage
+    static constexpr size_t RING = (size_t)G * D * STAGE;
+    static size_t bytes(int nb) { return BAR + RING + (size_t)NC * nb * Q8K_IMG_BYTES; }
+    static_assert(8 * (1 + G * D) <= BAR, "barriers");
+    static_assert(STAGE % 16 == 0, "stage alignment");
+};
+
+template <int TYPE, int NC, int G, int R, int D, int P>
+__global__ void __launch_bounds__(32 * G)
+kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
+                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
+    using G_ = G7<TYPE>;
+    using Geo = GeoS7<TYPE, NC, G, R, D, P>;
+    constexpr int TB = G_::TB;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int rs = lane >> 2, tg = lane & 3;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* bar = xbar + 1 + wid * D;
+    uint8_t* ring = smem + Geo::BAR + (size_t)wid * D * Geo::STAGE;
+    const uint8_t* xs = smem + Geo::BAR + Geo::RING;
+    const int ctas_a = (rows_a / 8 + G * R - 1) / (G * R);
+    const bool second = (int)blockIdx.x >= ctas_a;
+    const uint8_t* w = second ? w_b : w_a;
+    const int rows = second ? rows_b : rows_a;
+    float* y = second ? y_b : y_a;
+    const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
+    const int tiles = rows / 8;
+    const int t0 = (bid * G + wid) * R;  // this warp's first tile
+    const bool active = t0 < tiles;
+    const int nwin = (nb + P - 1) / P;
+
+    auto issue = [&](int win) {  // lane 0: the tile blocks of window `win` (P super-blocks) of this warp's tiles
+        uint8_t* st = ring + (size_t)(win % D) * Geo::STAGE;
+        const int n = min(P, nb - win * P);
+        mbar_expect7(&bar[win % D], (uint32_t)(R * n * TB));
+        for (int j = 0; j < R; j++) {
+            const int t = min(t0 + j, tiles - 1);
+            bulk7(st + (size_t)j * P * TB, w + ((size_t)t * nb + (size_t)win * P) * TB, (uint32_t)(n * TB), &bar[win % D]);
+        }
+    };
+    if (tid == 0) mbar_init7(xbar);
+    if (lane == 0 && active)
+        for (int d = 0; d < D; d++) mbar_init7(&bar[d]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();  // the x barrier is waited on by every warp
+    if (lane == 0 && active)
+        for (int d = 0; d < D && d < nwin; d++) issue(d);  // weights are never written after load: before the wait
+    gd_wait();  // the activation image is the previous kernel's output
+    gd_launch();
+    if (tid == 0) {
+        mbar_expect7(xbar, (uint32_t)(NC * nb * Q8K_IMG_BYTES) + g7_test_extra_tx);
+        for (int c = 0; c < NC; c++)
+            bulk7(smem + Geo::BAR + Geo::RING + (size_t)c * nb * Q8K_IMG_BYTES, img + (size_t)c * nb * Q8K_IMG_BYTES,
+                  (uint32_t)(nb * Q8K_IMG_BYTES), xbar);
+    }
+    if (!active) {
+        if (tid == 0) mbar_wait7(xbar, 0);  // the x copies land before the CTA can end
+        return;
+    }
+    float acc[R][NC][2], accm[R][NC];
+#pragma unroll
+    for (int j = 0; j < R; j++)
+#pragma unroll
+        for (int n = 0; n < NC; n++) acc[j][n][0] = acc[j][n][1] = accm[j][n] = 0.0f;
+
+    bool ok = __all_sync(0xffffffffu, mbar_wait7(xbar, 0));
+    int win = 0;
+    for (; ok && win < nwin; win++) {
+        const int slot = win % D;
+        if (!__all_sync(0xffffffffu, mbar_wait7(&bar[slot], (uint32_t)((win / D) & 1)))) {
+            ok = false;
+            break;
+        }
+        const uint8_t* st = ring + (size_t)slot * Geo::STAGE;
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int sb = win * P + p;
+            if (P > 1 && sb >= nb) break;
+            Dec7<TYPE> dec[R];
+#pragma unroll
+            for (int j = 0; j < R; j++) {
+                W7<TYPE> f;
+                lds_w7<TYPE>(st + (size_t)(j * P + p) * TB, lane, rs, f);
+                decode7<TYPE>(f, tg, dec[j]);
+            }
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                const uint8_t* xb = xs + ((size_t)n * nb + sb) * Q8K_IMG_BYTES;
+                uint32_t xw[16];
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const uint4 v = reinterpret_cast<const uint4*>(xb + 64 * tg)[c];
+                    xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
+                }
+                const float dx = *reinterpret_cast<const float*>(xb + Q8K_IMG_D);
+                uint32_t q8s = 0;
+                uint2 bsp2 = make_uint2(0, 0);
+                if constexpr (G_::MINS) q8s = reinterpret_cast<const uint32_t*>(xb + Q8K_IMG_Q8S)[tg];
+                else bsp2 = reinterpret_cast<const uint2*>(xb + Q8K_IMG_BSP)[tg];
+#pragma unroll
+                for (int j = 0; j < R; j++) {
+                    const float dd = __fmul_rn(dx, dec[j].dw);  // d = dx * d_w (kdot.rs:50)
+                    acc[j][n][0] = __fadd_rn(acc[j][n][0], __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 0, bsp2.x)));
+                    acc[j][n][1] = __fadd_rn(acc[j][n][1], __fmul_rn(dd, lane7<TYPE>(dec[j], xw, 1, bsp2.y)));
+                    if constexpr (G_::MINS) {  // (-dx * dmin) * (mn[2i] q8s[2i] + mn[2i+1] q8s[2i+1]), i = tg
+                        const float prod = __fsub_rn(__int_as_float(dp2a_lo_s(q8s, dec[j].mpair, (int)G7_MAGIC_I)), G7_MAGIC_F);
+                        accm[j][n] = __fadd_rn(accm[j][n], __fmul_rn(__fmul_rn(-dx, dec[j].dminw), prod));
+                    }
+                }
+            }
+        }
+        __syncwarp();  // every lane is done with this slot
+        if (lane == 0 && win + D < nwin) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the async refill
+            issue(win + D);
+        }
+    }
+    if (!ok) {
+        // a copy never arrived: record it, let this warp's copies still in flight land (each wait bounded), stop
+        if (lane == 0) {
+            atomicCAS(&g7_error, 0u, 0x700u | (unsigned)TYPE);
+            for (int k = win; k < nwin && k < win + D; k++) mbar_wait7(&bar[k % D], (uint32_t)((k / D) & 1));
+        }
+        if (tid == 0) mbar_wait7(xbar, 0);
+        return;
+    }
+    // per (tile, column, row): reduce8 of the 8 main lanes + reduce4 of the 4 min lanes (kdot.rs:75)
+    const int base = rs * 4;
+#pragma unroll
+    for (int j = 0; j < R; j++)
+#pragma unroll
+        for (int n = 0; n < NC; n++) {
+            float l8[8], m4[4];
+#pragma unroll
+            for (int g = 0; g < 8; g++) l8[g] = __shfl_sync(0xffffffffu, acc[j][n][g & 1], base + (g >> 1));
+#pragma unroll
+            for (int m = 0; m < 4; m++) m4[m] = __shfl_sync(0xffffffffu, accm[j][n], base + m);
+            const int tile = t0 + j;
+            if (tg == 0 && tile < tiles) {
+                float v = reduce8(l8);
+                if constexpr (G_::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
+                y[(size_t)n * rows + tile * 8 + rs] = v;
+            }
+        }
+}
+
 // CTA = G x S warps: warp w serves tile group w % G (R tiles of 8 rows) and super-block phase w / G, i.e.
 // super-blocks w/G, w/G + S, ... of its tiles.  Thread 0 keeps D windows of S super-blocks in flight.
 template <int TYPE, int NC, int G, int S, int R, int D>
@@ -491,27 +647,53 @@ cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w
     return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
 }
 
+template <int TYPE, int NC, int G, int R, int D, int P>
+cudaError_t launch7s(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                     const void* img, cudaStream_t s, bool pdl) {
+    using Geo = GeoS7<TYPE, NC, G, R, D, P>;
+    auto kern = kq_gemv7s_kernel<TYPE, NC, G, R, D, P>;
+    const size_t bytes = Geo::bytes(nb);
+    static size_t attr_bytes = 0;  // per instantiation: the largest dynamic shared memory enabled so far
+    if (bytes > 48 * 1024 && bytes > attr_bytes) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        attr_bytes = bytes;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows_a / 8 + G * R - 1) / (G * R) + (w_b ? (rows_b / 8 + G * R - 1) / (G * R) : 0));
+    cfg.blockDim = dim3(32 * G);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
+}
+
 int g_cfg7 = [] {
     const char* e = getenv("QDEC_GEMV7_CFG");
     return e ? atoi(e) : 0;
 }();
 
-// Configurations (G tile groups, S super-block phases, R tiles per warp, D windows in flight).
+// Configurations: the streaming kernel (G warps of R tiles, D stages of P super-blocks per warp) for matrices with
+// enough tiles, the windowed kernel (G tile groups x S super-block phases, R tiles per warp, D windows) otherwise.
 template <int TYPE, int NC>
 cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                         const void* img, cudaStream_t s, bool pdl) {
     if (cfg == 0) {
         const int rows = rows_a + (w_b ? rows_b : 0);
-        if (rows >= 16384) cfg = 2;
+        if (rows >= 16384) cfg = 1;
         else cfg = 8;
     }
     switch (cfg) {
-    case 1: return launch7<TYPE, NC, 4, 1, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 2: return launch7<TYPE, NC, 4, 1, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 3: return launch7<TYPE, NC, 4, 1, 1, 6>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 4: return launch7<TYPE, NC, 8, 1, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 1: return launch7s<TYPE, NC, 4, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch7s<TYPE, NC, 4, 2, 3, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch7s<TYPE, NC, 4, 1, 3, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4: return launch7s<TYPE, NC, 8, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 5: return launch7<TYPE, NC, 2, 2, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 6: return launch7<TYPE, NC, 2, 1, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 6: return launch7s<TYPE, NC, 2, 2, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 7: return launch7<TYPE, NC, 1, 4, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 8: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 9: return launch7<TYPE, NC, 2, 4, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
@@ -563,6 +745,11 @@ int selftest_gemv7_timeout(unsigned long long wait_ns) {
         cudaMemset(img, 0, Q8K_IMG_BYTES);
         cudaMemset(y, 0xff, rows * 4);
         read_gemv7_error(true);
+    }
+    const int saved_cfg = g_cfg7;
+    for (int cfg : {1, 8}) {  // the streaming kernel's x wait, the windowed kernel's first window
+        if (rc) break;
+        g_cfg7 = cfg;
         const unsigned extra = 16;
         cudaMemcpyToSymbol(g7_test_extra_tx, &extra, sizeof extra);
         cudaMemcpyToSymbol(g7_wait_ns, &wait_ns, sizeof wait_ns);
@@ -577,7 +764,8 @@ int selftest_gemv7_timeout(unsigned long long wait_ns) {
         cudaMemcpyToSymbol(g7_wait_ns, &dflt, sizeof dflt);
         if (!rc) {
             float h[64];
-            if (launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
+            if (cudaMemset(y, 0xff, rows * 4) != cudaSuccess ||
+                launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
                 cudaStreamSynchronize(st) != cudaSuccess || cudaMemcpy(h, y, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
                 rc = 4;
             else if (read_gemv7_error(true) != 0)
@@ -587,6 +775,7 @@ int selftest_gemv7_timeout(unsigned long long wait_ns) {
                     if (h[i] != 0.0f) rc = 6;  // the normal run after the timeout gives the right result
         }
     }
+    g_cfg7 = saved_cfg;
     if (st) cudaStreamDestroy(st);
     cudaFree(w);
     cudaFree(img);

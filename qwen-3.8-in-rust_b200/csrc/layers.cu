@@ -14,7 +14,6 @@
 //   argmax            first index of the maximum                            (model.rs:505-513)
 //
 // "Bit-exact" holds with the transcendentals of common.cuh (exp/log1p evaluated in double, rounded once).
-#include <cooperative_groups.h>
 
 #include <algorithm>
 #include <cstdlib>
@@ -234,229 +233,15 @@ __global__ void conv_step_kernel(float* __restrict__ state, const float* __restr
     conv_done();
 }
 
-// One CTA per V head p, one thread per value column j (blockDim.x == dv, dk <= DK_MAX); the head's state column
-// S[:, j] lives in the thread's registers.  Steps:
+// Gated DeltaNet recurrence of one call (t rows) for every V head p: one CTA per head, blockDim.x == 2 * dv.
+// Steps:
 //   1. load S (the committed state of the previous call) and apply its `keep` pending rows: S *= decay_i;
 //      S += k_i (x) delta_i -- the same element operations, in the same order, as the reference's replay of the
 //      accepted rows from a snapshot (spec.rs:395-415), so the state is bit-identical; store S back.
 //   2. for each of the t new rows: l2norm q and k, scale q, gates, the delta rule, gated RMSNorm; record
 //      (decay, k, delta) as the pending rows.  The state after the t rows is not stored: the next call commits
 //      exactly the rows the accept step keeps.
-template <int DK>
-__global__ void __launch_bounds__(128) deltanet_heads_kernel(const DeltaArgs a) {
-    const int p = blockIdx.x, j = threadIdx.x;
-    const int dk = DK, dv = a.dv;
-    const int kh = p % a.n_k;
-    __shared__ float qs[DK], ks[DK], red[16], outs[256];
-    __shared__ float scal[4];
-    float S[DK];
-    float* Sg = a.S + (size_t)p * dk * dv;
-#pragma unroll
-    for (int k = 0; k < DK; k++) S[k] = Sg[(size_t)k * dv + j];
-    const int keep = a.keep_prev ? *a.keep_prev : 0;
-    for (int i = 0; i < keep; i++) {
-        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
-        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk;
-        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
-    }
-    if (keep > 0) {
-#pragma unroll
-        for (int k = 0; k < DK; k++) Sg[(size_t)k * dv + j] = S[k];
-    }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
-    for (int i = 0; i < a.t; i++) {
-        const float* row = a.conved + (size_t)i * a.conv_dim;
-        for (int k = j; k < dk; k += blockDim.x) {
-            qs[k] = row[kh * dk + k];
-            ks[k] = row[a.kd + kh * dk + k];
-        }
-        __syncthreads();
-        // l2norm(q) on thread 0, l2norm(k) on thread 32 (deltanet.rs:19-27): sum left to right
-        if (j == 0 || j == 32) {
-            float* vec = j == 0 ? qs : ks;
-            float ss = 0.0f;
-            // dk == DK: unrolled so the shared-memory loads run ahead of the dependent adds
-#pragma unroll
-            for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
-            scal[j == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
-        }
-        if (j == (int)blockDim.x - 1) {
-            const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)i * a.n_v + p], a.dt_bias[p])));
-            scal[2] = exp_f32(g);                                        // decay = exp(g)
-            scal[3] = sigmoid_f32(a.beta[(size_t)i * a.n_v + p]);        // beta = sigmoid(b)
-        }
-        __syncthreads();
-        for (int k = j; k < dk; k += blockDim.x) {
-            qs[k] = __fmul_rn(__fmul_rn(qs[k], scal[0]), scale);
-            ks[k] = __fmul_rn(ks[k], scal[1]);
-        }
-        __syncthreads();
-        const float decay = scal[2], beta = scal[3];
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
-        float kv = 0.0f;
-#pragma unroll
-        for (int k = 0; k < DK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
-        const float v = row[2 * a.kd + p * dv + j];
-        const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
-        float o = 0.0f;
-#pragma unroll
-        for (int k = 0; k < DK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
-        // pending row i of this call
-        if (i < a.max_t) {
-            if (j == 0) a.pend_decay[(size_t)i * a.n_v + p] = decay;
-            for (int k = j; k < dk; k += blockDim.x) a.pend_k[((size_t)i * a.n_v + p) * dk + k] = ks[k];
-            a.pend_delta[((size_t)i * a.n_v + p) * dv + j] = delta;
-        }
-        // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47)
-        outs[j] = o;
-        __syncthreads();
-        const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
-        const float z = a.z[(size_t)i * a.n_v * dv + p * dv + j];
-        a.heads[(size_t)i * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
-        __syncthreads();
-    }
-}
-
-// The same computation with two threads per value column (blockDim.x == 2 * dv): lanes l and l + 16 of a warp
-// share column j, each holding half of S[:, j] (k < DK/2 and k >= DK/2) in registers, which keeps the state in
-// registers without spilling.  The two k-ordered sums (kv = sum_k S[k] k[k], o = sum_k S[k] q[k]) stay single
-// left-to-right chains: the low half runs its 64 terms, hands the partial sum to the high half by one shuffle,
-// and the high half continues from it.
-template <int DK>
-__global__ void __launch_bounds__(256) deltanet_pair_kernel(const DeltaArgs a) {
-    constexpr int HK = DK / 2;
-    constexpr int CH = 8;  // rows whose q/k norms and gates are computed together (they do not depend on S)
-    const int p = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int h = lane >> 4, j = warp * 16 + (lane & 15);
-    const int k0 = h * HK;
-    const int dk = DK, dv = a.dv;
-    const int kh = p % a.n_k;
-    __shared__ __align__(16) float qs_all[CH][DK], ks_all[CH][DK];
-    __shared__ float gate[CH][2], nrm[CH][2];  // (decay, beta), (1/|q|, 1/|k|)
-    __shared__ float red[16], outs[256];
-    griddep_wait();
-    griddep_launch();
-    float S[HK];
-    float* Sg = a.S + (size_t)p * dk * dv;
-#pragma unroll
-    for (int k = 0; k < HK; k++) S[k] = Sg[(size_t)(k0 + k) * dv + j];
-    const int keep = a.keep_prev ? *a.keep_prev : 0;
-    for (int i = 0; i < keep; i++) {  // commit the previous call's accepted rows (spec.rs:395-415 replay order)
-        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
-        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk + k0;
-        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
-#pragma unroll
-        for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
-#pragma unroll
-        for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
-    }
-    if (keep > 0) {
-#pragma unroll
-        for (int k = 0; k < HK; k++) Sg[(size_t)(k0 + k) * dv + j] = S[k];
-    }
-    // gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) of the first chunk's rows
-    const int nr0 = min(CH, a.t);
-    if (t < nr0) {
-        const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)t * a.n_v + p], a.dt_bias[p])));
-        gate[t][0] = exp_f32(g);
-        gate[t][1] = sigmoid_f32(a.beta[(size_t)t * a.n_v + p]);
-    }
-    float zr[CH];
-#pragma unroll
-    for (int i = 0; i < CH; i++) zr[i] = (h == 1 && i < nr0) ? a.z[(size_t)i * a.n_v * dv + p * dv + j] : 0.0f;
-    griddep_wait();
-    griddep_launch();
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
-    for (int c0 = 0; c0 < a.t; c0 += CH) {
-        const int nr = min(CH, a.t - c0);
-        for (int e = t; e < nr * DK; e += blockDim.x) {
-            const int i = e / DK, k = e % DK;
-            const float* row = a.conved + (size_t)(c0 + i) * a.conv_dim;
-            qs_all[i][k] = row[kh * dk + k];
-            ks_all[i][k] = row[a.kd + kh * dk + k];
-        }
-        __syncthreads();
-        // l2norm (deltanet.rs:19-27, sums left to right): warp w normalises q of rows w, w + warps, .. on lane 0
-        // and k on lane 16; the gates of later chunks on lane 8
-        for (int i = warp; i < nr && (lane & 7) == 0; i += blockDim.x / 32) {
-            if (lane == 8) {
-                if (c0 == 0) continue;
-                const int r = c0 + i;
-                const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)r * a.n_v + p], a.dt_bias[p])));
-                gate[i][0] = exp_f32(g);
-                gate[i][1] = sigmoid_f32(a.beta[(size_t)r * a.n_v + p]);
-            } else if (lane != 24) {
-                const float* vec = lane == 0 ? qs_all[i] : ks_all[i];
-                float ss = 0.0f;
-#pragma unroll
-                for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
-                nrm[i][lane == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
-            }
-        }
-        __syncthreads();
-        for (int e = t; e < nr * DK; e += blockDim.x) {
-            const int i = e / DK, k = e % DK;
-            qs_all[i][k] = __fmul_rn(__fmul_rn(qs_all[i][k], nrm[i][0]), scale);
-            ks_all[i][k] = __fmul_rn(ks_all[i][k], nrm[i][1]);
-        }
-        __syncthreads();
-        for (int i = 0; i < nr; i++) {
-            const int r = c0 + i;
-            const float* qs = qs_all[i];
-            const float* ks = ks_all[i];
-            const float v = a.conved[(size_t)r * a.conv_dim + 2 * a.kd + p * dv + j];
-            const float z = a.z[(size_t)r * a.n_v * dv + p * dv + j];
-            const float decay = gate[i][0], beta = gate[i][1];
-#pragma unroll
-            for (int k = 0; k < HK; k++) S[k] = __fmul_rn(S[k], decay);
-            // kv: the low half's terms from 0, then the high half's from the low half's sum
-            float kv = 0.0f;
-            if (h == 0) {
-#pragma unroll
-                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
-            }
-            kv = __shfl_sync(0xffffffffu, kv, lane & 15);
-            if (h == 1) {
-#pragma unroll
-                for (int k = 0; k < HK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[HK + k]));
-            }
-            kv = __shfl_sync(0xffffffffu, kv, 16 + (lane & 15));
-            const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-#pragma unroll
-            for (int k = 0; k < HK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k0 + k], delta));
-            float o = 0.0f;
-            if (h == 0) {
-#pragma unroll
-                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
-            }
-            o = __shfl_sync(0xffffffffu, o, lane & 15);
-            if (h == 1) {
-#pragma unroll
-                for (int k = 0; k < HK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[HK + k]));
-            }
-            if (r < a.max_t) {
-                if (t == 0) a.pend_decay[(size_t)r * a.n_v + p] = decay;
-                for (int k = t; k < dk; k += blockDim.x) a.pend_k[((size_t)r * a.n_v + p) * dk + k] = ks[k];
-                if (h == 1) a.pend_delta[((size_t)r * a.n_v + p) * dv + j] = delta;
-            }
-            // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47); the helper ends with a barrier, after
-            // which outs and this chunk's rows may be overwritten
-            if (h == 1) outs[j] = o;
-            __syncthreads();
-            const float inv = inv_rms_of(sum_squares_8lane_block(outs, dv, red), dv, a.eps);
-            if (h == 1) a.heads[(size_t)r * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
-        }
-    }
-}
-
-// The same computation with the two halves of each value column in two different warps (blockDim.x == 2 * dv):
+// The two halves of each value column live in two different warps:
 // warp w < dv/32 holds S[0, DK/2) of columns 32w .. 32w+31, warp w + dv/32 holds S[DK/2, DK) of the same
 // columns, so every warp runs all 32 lanes on one half.  The k-ordered sums (kv, o) stay single left-to-right
 // chains: the low-half warp sums its 64 terms from 0 and hands the partial sum through shared memory, the
@@ -616,120 +401,6 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
     }
 }
 
-// The same computation split over a cluster of dv / 32 single-warp CTAs per V head (thread block clusters,
-// sm_90+): CTA c owns value columns 32c .. 32c+31, so a head's 128 columns run on 4 SMs and each thread's state
-// column S[:, j] stays in registers.  Every CTA recomputes the head's l2norms and gates (the same operations on
-// the same data); the gated RMSNorm's 8-lane sum over all dv outputs reads the other CTAs' outputs through
-// distributed shared memory, one cluster barrier per row (outputs double-buffered by row parity).
-template <int DK>
-__global__ void __launch_bounds__(32) deltanet_cluster_kernel(const DeltaArgs a) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int nct = a.dv / 32;
-    const int p = blockIdx.x / nct, cpart = blockIdx.x % nct, lane = threadIdx.x;
-    const int j = cpart * 32 + lane;
-    const int dk = DK, dv = a.dv;
-    const int kh = p % a.n_k;
-    __shared__ float qs[DK], ks[DK], obuf[2][32], red[16];
-    __shared__ float scal[4];
-    griddep_wait();
-    griddep_launch();
-    float S[DK];
-    float* Sg = a.S + (size_t)p * dk * dv;
-#pragma unroll
-    for (int k = 0; k < DK; k++) S[k] = Sg[(size_t)k * dv + j];
-    const int keep = a.keep_prev ? *a.keep_prev : 0;
-    for (int i = 0; i < keep; i++) {  // commit the previous call's accepted rows (spec.rs:395-415 replay order)
-        const float decay = a.pend_decay[(size_t)i * a.n_v + p];
-        const float* kp = a.pend_k + ((size_t)i * a.n_v + p) * dk;
-        const float delta = a.pend_delta[((size_t)i * a.n_v + p) * dv + j];
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(kp[k], delta));
-    }
-    if (keep > 0) {
-#pragma unroll
-        for (int k = 0; k < DK; k++) Sg[(size_t)k * dv + j] = S[k];
-    }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dk));  // 1 / sqrt(dk) (gated_deltanet.rs:574)
-    for (int i = 0; i < a.t; i++) {
-        const float* row = a.conved + (size_t)i * a.conv_dim;
-        for (int k = lane; k < dk; k += 32) {
-            qs[k] = row[kh * dk + k];
-            ks[k] = row[a.kd + kh * dk + k];
-        }
-        __syncwarp();
-        // l2norm(q) on lane 0, l2norm(k) on lane 1 (deltanet.rs:19-27): sums left to right; gates on lane 31
-        if (lane < 2) {
-            const float* vec = lane == 0 ? qs : ks;
-            float ss = 0.0f;
-            // dk == DK: unrolled so the shared-memory loads run ahead of the dependent adds
-#pragma unroll
-            for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
-            scal[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
-        }
-        if (lane == 31) {
-            const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)i * a.n_v + p], a.dt_bias[p])));
-            scal[2] = exp_f32(g);                                  // decay = exp(g)
-            scal[3] = sigmoid_f32(a.beta[(size_t)i * a.n_v + p]);  // beta = sigmoid(b)
-        }
-        __syncwarp();
-        for (int k = lane; k < dk; k += 32) {
-            qs[k] = __fmul_rn(__fmul_rn(qs[k], scal[0]), scale);
-            ks[k] = __fmul_rn(ks[k], scal[1]);
-        }
-        __syncwarp();
-        const float decay = scal[2], beta = scal[3];
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fmul_rn(S[k], decay);
-        float kv = 0.0f;
-#pragma unroll
-        for (int k = 0; k < DK; k++) kv = __fadd_rn(kv, __fmul_rn(S[k], ks[k]));
-        const float v = row[2 * a.kd + p * dv + j];
-        const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-#pragma unroll
-        for (int k = 0; k < DK; k++) S[k] = __fadd_rn(S[k], __fmul_rn(ks[k], delta));
-        float o = 0.0f;
-#pragma unroll
-        for (int k = 0; k < DK; k++) o = __fadd_rn(o, __fmul_rn(S[k], qs[k]));
-        if (i < a.max_t) {
-            if (j == 0) a.pend_decay[(size_t)i * a.n_v + p] = decay;
-            if (cpart == 0)
-                for (int k = lane; k < dk; k += 32) a.pend_k[((size_t)i * a.n_v + p) * dk + k] = ks[k];
-            a.pend_delta[((size_t)i * a.n_v + p) * dv + j] = delta;
-        }
-        // gated RMSNorm over the head's dv outputs (rmsnorm.rs:36-47): 8-lane sum across the cluster
-        float* ob = obuf[i & 1];
-        ob[lane] = o;
-        cluster.sync();
-        if (lane < 8) {
-            // lane l sums o[l], o[l+8], ... (dv <= 256: at most 32 terms), fetched first, then chained in order
-            float vals[32];
-            const int cnt = dv / 8;
-#pragma unroll
-            for (int q = 0; q < 32; q++)
-                if (q < cnt) {
-                    const int idx = lane + 8 * q;
-                    vals[q] = cluster.map_shared_rank(ob, idx / 32)[idx % 32];
-                }
-            float acc = 0.0f;
-#pragma unroll
-            for (int q = 0; q < 32; q++)
-                if (q < cnt) acc = __fadd_rn(acc, __fmul_rn(vals[q], vals[q]));
-            red[lane] = acc;
-        }
-        __syncwarp();
-        if (lane == 0) red[8] = reduce8(red);  // dv % 8 == 0: no tail
-        __syncwarp();
-        const float inv = inv_rms_of(red[8], dv, a.eps);
-        const float z = a.z[(size_t)i * a.n_v * dv + p * dv + j];
-        a.heads[(size_t)i * a.n_v * dv + p * dv + j] = __fmul_rn(__fmul_rn(a.norm_w[j], __fmul_rn(o, inv)), silu_f32(z));
-        __syncwarp();
-    }
-    cluster.sync();  // no CTA leaves while another may still read its outputs
-}
-
 // Per (row i, head): RMSNorm of q (heads 0..nh-1) or k (heads nh..nh+nkv-1) with the 8-lane order, then
 // rotate-half RoPE on the first rope_dim dims (rope.rs:31-45); q written to q_out with its gate copied to
 // gate_out; k and v appended to the cache at position pos0 + i (gqa_attention.rs:343-362).
@@ -770,70 +441,9 @@ __global__ void qk_norm_rope_kernel(const QkArgs a) {
     }
 }
 
-// One CTA per (row i, head h): scores s[t] = (sum_d q[d] k_t[d]) * scaling over the cache positions
-// 0..pos0+i (sum left to right over d), softmax (max, exp, 8-lane sum, divide), out[d] = sum_t p[t] v_t[d]
-// (left to right over t), times sigmoid(gate) (gqa_attention.rs:376-409).
-__global__ void attention_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    const int i = blockIdx.y, h = blockIdx.x;
-    const int hd = a.head_dim, kvh = h / (a.n_head / a.n_kv);
-    const int len = *a.pos + i + 1;
-    float* qs = sm;
-    float* p = sm + hd;           // len scores / probabilities
-    float* red = p + a.max_len;   // 16 floats
-    const float* q = a.q + (size_t)i * a.n_head * hd + (size_t)h * hd;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
-    __syncthreads();
-    for (int t = threadIdx.x; t < len; t += blockDim.x) {
-        const float* kt = a.k_cache + ((size_t)t * a.n_kv + kvh) * hd;
-        float s = 0.0f;
-        for (int d = 0; d < hd; d++) s = __fadd_rn(s, __fmul_rn(qs[d], kt[d]));
-        p[t] = __fmul_rn(s, a.scaling);
-    }
-    __syncthreads();
-    // softmax (softmax.rs:22-50): m = max; e = exp(x - m); 8-lane sum; divide
-    float m = -INFINITY;
-    for (int t = threadIdx.x; t < len; t += blockDim.x) m = fmaxf(m, p[t]);
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float mm = red[0];
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
-        red[15] = mm;
-    }
-    __syncthreads();
-    m = red[15];
-    __syncthreads();
-    for (int t = threadIdx.x; t < len; t += blockDim.x) p[t] = exp_f32(__fsub_rn(p[t], m));
-    __syncthreads();
-    const int n8 = len / 8 * 8;
-    if (threadIdx.x < 8) {
-        float acc = 0.0f;
-        for (int t = threadIdx.x; t < n8; t += 8) acc = __fadd_rn(acc, p[t]);
-        red[threadIdx.x] = acc;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = reduce8(red);
-        for (int t = n8; t < len; t++) s = __fadd_rn(s, p[t]);
-        red[8] = s;
-    }
-    __syncthreads();
-    const float ssum = red[8];
-    for (int t = threadIdx.x; t < len; t += blockDim.x) p[t] = __fdiv_rn(p[t], ssum);
-    __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.0f;
-        const float* vcol = a.v_cache + (size_t)kvh * hd + d;
-        const size_t stride = (size_t)a.n_kv * hd;
-        for (int t = 0; t < len; t++) o = __fadd_rn(o, __fmul_rn(p[t], vcol[(size_t)t * stride]));
-        const float g = a.gate[(size_t)i * a.n_head * hd + (size_t)h * hd + d];
-        a.out[(size_t)i * a.n_head * hd + (size_t)h * hd + d] = __fmul_rn(o, sigmoid_f32(g));
-    }
-}
-
-// Long-context attention in two kernels, the same arithmetic in the same order as attention_kernel.
+// Attention of row i and query head h (gqa_attention.rs:376-409): scores s[t] = (sum_d q[d] k_t[d]) * scaling
+// over the cache positions 0..pos0+i (sum left to right over d), softmax (max, exp, 8-lane sum, divide),
+// out[d] = sum_t p[t] v_t[d] (left to right over t), times sigmoid(gate) -- in three kernels.
 // Scores: a CTA takes up to 8 (query head, row) pairs that read the same kv head (pair p = query head
 // kvh * group + p % group of row p / group) and strides over 256-position chunks of the cache; each warp stages the
 // keys of 32 positions 32 dims at a time in shared memory (coalesced loads; rows padded to 36 floats so the
@@ -1144,60 +754,11 @@ cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, 
     return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
-template <int DK>
-cudaError_t launch_deltanet_cluster(const DeltaArgs& a, cudaStream_t s) {
-    const int nct = a.dv / 32;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_v * nct);
-    cfg.blockDim = dim3(32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = nct;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, deltanet_cluster_kernel<DK>, a);
-}
-
 cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s) {
-    if (a.dv > 256 || a.dv % 32) return cudaErrorInvalidValue;
-    static const bool plain = [] {
-        // one CTA per head unless QDEC_DELTANET_CLUSTER=1 (a cluster of dv/32 single-warp CTAs per head, which
-        // measured slower on B200: the per-column chains do not shorten and one warp per SM hides no latency)
-        const char* e = getenv("QDEC_DELTANET_CLUSTER");
-        return !(e && e[0] == '1');
-    }();
-    if (!plain && a.dv % 8 == 0 && a.dv / 32 <= 8 && (a.dk == 128 || a.dk == 64)) {
-        cudaError_t e = a.dk == 128 ? launch_deltanet_cluster<128>(a, s) : launch_deltanet_cluster<64>(a, s);
-        return e == cudaSuccess ? cudaGetLastError() : e;
-    }
-    static const bool pair = [] {
-        // the two halves of a column in one warp (QDEC_DELTANET=pair) instead of two warps
-        const char* e = getenv("QDEC_DELTANET");
-        return e && strcmp(e, "pair") == 0;
-    }();
-    if (!pair && a.dv % 32 == 0 && a.dv <= 128 && (a.dk == 128 || a.dk == 64)) {
-        cudaError_t e = a.dk == 128 ? launch_pdl(deltanet_halves_kernel<128>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a)
-                                    : launch_pdl(deltanet_halves_kernel<64>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a);
-        return e == cudaSuccess ? cudaGetLastError() : e;
-    }
-    if (a.dv % 16 == 0 && a.dv <= 128 && (a.dk == 128 || a.dk == 64)) {
-        cudaError_t e = a.dk == 128 ? launch_pdl(deltanet_pair_kernel<128>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a)
-                                    : launch_pdl(deltanet_pair_kernel<64>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a);
-        return e == cudaSuccess ? cudaGetLastError() : e;
-    }
-    switch (a.dk) {
-    case 128: deltanet_heads_kernel<128><<<a.n_v, a.dv, 0, s>>>(a); break;
-    case 64: deltanet_heads_kernel<64><<<a.n_v, a.dv, 0, s>>>(a); break;
-    case 8: deltanet_heads_kernel<8><<<a.n_v, a.dv, 0, s>>>(a); break;
-    default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+    if (!deltanet_dims_supported(a.dk, a.dv)) return cudaErrorInvalidValue;
+    cudaError_t e = a.dk == 128 ? launch_pdl(deltanet_halves_kernel<128>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a)
+                                : launch_pdl(deltanet_halves_kernel<64>, dim3(a.n_v), dim3(2 * a.dv), 0, s, a);
+    return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
@@ -1208,29 +769,18 @@ cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
 }
 
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
-    if (a.scores && a.head_dim % 64 == 0 && a.head_dim <= 256) {
-        const int group = a.n_head / a.n_kv, npairs = group * t;
-        const int pairs = a.max_len > 2048 ? 8 : 2;
-        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + pairs - 1) / pairs);
-        if (pairs == 8) attn_scores_kernel<8><<<sgrid, 256, 0, s>>>(a, t);
-        else attn_scores_kernel<2><<<sgrid, 256, 0, s>>>(a, t);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-        attn_softmax_kernel<<<dim3(a.n_head, t), 256, 0, s>>>(a);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-        attn_pv_kernel<<<dim3(a.head_dim / 32, a.n_kv, (npairs + ATT_VP - 1) / ATT_VP), 32 * ATT_VP, 0, s>>>(a, t);
-        return cudaGetLastError();
-    }
-    const dim3 grid(a.n_head, t);
-    const size_t smem = (size_t)(a.head_dim + a.max_len + 16) * sizeof(float);
-    static size_t cap = 48 * 1024;  // raised only when a longer cache needs it (before any graph capture)
-    if (smem > cap) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        cap = smem;
-    }
-    attention_kernel<<<grid, 256, smem, s>>>(a);
+    if (!a.scores || !attention_dims_supported(a.head_dim)) return cudaErrorInvalidValue;
+    const int group = a.n_head / a.n_kv, npairs = group * t;
+    const int pairs = a.max_len > 2048 ? 8 : 2;
+    const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + pairs - 1) / pairs);
+    if (pairs == 8) attn_scores_kernel<8><<<sgrid, 256, 0, s>>>(a, t);
+    else attn_scores_kernel<2><<<sgrid, 256, 0, s>>>(a, t);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    attn_softmax_kernel<<<dim3(a.n_head, t), 256, 0, s>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    attn_pv_kernel<<<dim3(a.head_dim / 32, a.n_kv, (npairs + ATT_VP - 1) / ATT_VP), 32 * ATT_VP, 0, s>>>(a, t);
     return cudaGetLastError();
 }
 

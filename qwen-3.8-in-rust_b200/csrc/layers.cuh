@@ -61,6 +61,11 @@ cudaError_t launch_swiglu_quant(const float* g, const float* u, int n, int rows,
 cudaError_t launch_quant_rows(const float* x, int n, int rows, uint8_t* q8k_out, uint8_t* q80_out, cudaStream_t s);
 cudaError_t launch_conv_step(float* state, const float* w, int K, int channels, const float* x, int t, float* out,
                              float* pend_x, const int* keep_prev, int max_t, cudaStream_t s);
+// The head shapes the device kernels are built for (the Qwen3.8 family's): DeltaNet K heads of 64 or 128 with V
+// heads of 32..128 in steps of 32; attention heads of 64..256 in steps of 64.  A model outside them is refused at
+// load time.
+inline bool deltanet_dims_supported(int dk, int dv) { return (dk == 64 || dk == 128) && dv % 32 == 0 && dv >= 32 && dv <= 128; }
+inline bool attention_dims_supported(int head_dim) { return head_dim % 64 == 0 && head_dim >= 64 && head_dim <= 256; }
 cudaError_t launch_deltanet_heads(const DeltaArgs& a, cudaStream_t s);
 cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s);

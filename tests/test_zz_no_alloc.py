@@ -89,9 +89,10 @@ import sys
 import numpy as np
 sys.path.insert(0, sys.argv[1])
 sys.path.insert(0, sys.argv[2])
+import qdec
+qdec.lib()  # the library is loaded before the CUDA context exists, so eager module loading places its device code
 import torch
 from helpers import random_blocks, to_dev
-import qdec
 rows, cols, t = 512, 5120, 12
 w = to_dev(random_blocks(t, rows, cols, seed=5))
 x = to_dev(np.random.default_rng(6).standard_normal((4, cols)).astype(np.float32))
@@ -115,9 +116,10 @@ print("FREE", f0, f1, "SAME", int(same))
 
 @pytest.mark.gpu
 def test_noalloc_allocates_nothing_in_a_fresh_process():
-    """In a fresh process whose first library call is qdec_matvec_noalloc, the device's free memory is the same
-    before and after three calls (modules loaded eagerly, torch's stream taken before the first reading), and the
-    result equals qdec_matvec's, run afterwards."""
+    """In a fresh process whose first compute call is qdec_matvec_noalloc, the device's free memory is the same
+    before and after three calls, and the result equals qdec_matvec's, run afterwards.  The library is loaded
+    before the CUDA context is created and modules load eagerly, so its device code and fixed arrays are in place
+    before the first reading; torch's stream is taken before it too."""
     _cuda()
     pkg = os.path.join(os.path.dirname(HERE), "qwen-3.8-in-rust_b200")
     env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
