@@ -802,7 +802,11 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         resid_norm(li == 0 ? nullptr : mlp_in(), L.attn_norm, t, normed_, k8, k0);
         gemv(L.qkv, normed_, t, qkv_);
         gemv(L.gate_z, normed_, t, z_);
-        if (L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == L.beta.cols) {
+        const bool ab_fused = L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == H && L.beta.cols == H &&
+                              t <= 8 && H <= 5120 && H % 4 == 0;
+        if (ab_fused) {
+            // the DeltaNet kernel computes alpha and beta of its head itself (before its wait, alongside the conv)
+        } else if (L.alpha.type == T_F32 && L.beta.type == T_F32 && L.alpha.cols == L.beta.cols) {
             // ssm_alpha and ssm_beta read the same normed rows: one launch (gated_deltanet.rs:148-149)
             count_launch();
             // normed_ comes from the norm two launches back: the pair runs alongside the gate_z GEMV
@@ -818,7 +822,9 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
                             commit_dn ? d_keep : nullptr, T_, stream), "conv");
         const int dk = (int)c.dn_head_dim_k, dv = (int)c.dn_head_dim_v;
         DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,
-                     commit_dn ? d_keep : nullptr, t, T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps};
+                     commit_dn ? d_keep : nullptr, t, T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps,
+                     ab_fused ? (const float*)L.alpha.p : nullptr, ab_fused ? (const float*)L.beta.p : nullptr,
+                     ab_fused ? normed_ : nullptr, H};
         count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
         const float* heads_full = heads_;
         if (tp()) {

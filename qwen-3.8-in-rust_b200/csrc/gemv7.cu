@@ -241,11 +241,15 @@ __device__ unsigned int g7_error = 0;  // set when a bounded wait of this file's
 // Shared memory of a CTA: D stage buffers, each one window of S super-blocks for the CTA's G x R tiles (a copy of
 // S contiguous tile blocks per tile) and the NC activation columns (a copy of S contiguous image blocks per
 // column); then, with S > 1, the double-buffered lane terms and the final chains.
-template <int TYPE, int NC, int G, int S, int R, int D>
+template <int TYPE, int NC, int G, int S, int R, int D, bool X2>
 struct Geo7 {
     static constexpr int TB = G7<TYPE>::TB;
     static constexpr int WST = G * R * S * TB;
-    static constexpr int STAGE = WST + NC * S * Q8K_IMG_BYTES;
+    // X2: the window's image blocks twice -- threads tg < 2 read copy A, tg >= 2 copy B, which sits 16 bytes off
+    // the 128-byte bank period from A, so the four threads of a row read four different bank groups
+    static constexpr int XW = NC * S * Q8K_IMG_BYTES;
+    static constexpr int XOFF = X2 ? (XW + 127) / 128 * 128 + 16 : 0;
+    static constexpr int STAGE = WST + XOFF + XW;
     static constexpr int PER_SB = R * NC * 8 * 12;  // one warp's terms of one super-block
     static constexpr size_t BAR = 128;
     static constexpr size_t ST0 = BAR;
@@ -277,16 +281,18 @@ __device__ __forceinline__ void lds_w7(const uint8_t* ts, int L, int rs, W7<TYPE
 // Streaming form for matrices with enough tiles to fill the GPU with one warp per R tiles (S = 1): every warp
 // streams its own tiles' super-blocks through a private ring of D stages of P super-blocks (one bulk copy of P
 // contiguous tile blocks per tile and stage, completing on the warp's own mbarrier), so warps never wait for one
-// another; the activation image of all NC columns and super-blocks is copied once per CTA and stays resident.
-// Chains stay in the owning thread's registers, in super-block order.
+// another.  The activation image of all NC columns and super-blocks is staged once per CTA and stays resident,
+// its code words rearranged so that the four threads of a row read them without bank conflicts: the 16-byte
+// quad q = 4 tg + c of a block (thread tg's quad c) is stored at 4 c + tg.  Chains stay in the owning thread's
+// registers, in super-block order.
 template <int TYPE, int NC, int G, int R, int D, int P>
 struct GeoS7 {
     static constexpr int TB = G7<TYPE>::TB;
-    static constexpr size_t BAR = 1024;                   // x barrier + G x D stage barriers
+    static constexpr size_t BAR = 1024;                   // G x D stage barriers
     static constexpr size_t STAGE = (size_t)R * P * TB;  // one warp's stage
     static constexpr size_t RING = (size_t)G * D * STAGE;
     static size_t bytes(int nb) { return BAR + RING + (size_t)NC * nb * Q8K_IMG_BYTES; }
-    static_assert(8 * (1 + G * D) <= BAR, "barriers");
+    static_assert(8 * G * D <= BAR, "barriers");
     static_assert(STAGE % 16 == 0, "stage alignment");
 };
 
@@ -300,10 +306,9 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int rs = lane >> 2, tg = lane & 3;
-    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* bar = xbar + 1 + wid * D;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem) + wid * D;
     uint8_t* ring = smem + Geo::BAR + (size_t)wid * D * Geo::STAGE;
-    const uint8_t* xs = smem + Geo::BAR + Geo::RING;
+    uint8_t* xs = smem + Geo::BAR + Geo::RING;
     const int ctas_a = (rows_a / 8 + G * R - 1) / (G * R);
     const bool second = (int)blockIdx.x >= ctas_a;
     const uint8_t* w = second ? w_b : w_a;
@@ -318,40 +323,42 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
     auto issue = [&](int win) {  // lane 0: the tile blocks of window `win` (P super-blocks) of this warp's tiles
         uint8_t* st = ring + (size_t)(win % D) * Geo::STAGE;
         const int n = min(P, nb - win * P);
-        mbar_expect7(&bar[win % D], (uint32_t)(R * n * TB));
+        mbar_expect7(&bar[win % D], (uint32_t)(R * n * TB) + (win == 0 && wid == 0 ? g7_test_extra_tx : 0u));
         for (int j = 0; j < R; j++) {
             const int t = min(t0 + j, tiles - 1);
             bulk7(st + (size_t)j * P * TB, w + ((size_t)t * nb + (size_t)win * P) * TB, (uint32_t)(n * TB), &bar[win % D]);
         }
     };
-    if (tid == 0) mbar_init7(xbar);
-    if (lane == 0 && active)
+    if (lane == 0 && active) {
         for (int d = 0; d < D; d++) mbar_init7(&bar[d]);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncthreads();  // the x barrier is waited on by every warp
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
     if (lane == 0 && active)
         for (int d = 0; d < D && d < nwin; d++) issue(d);  // weights are never written after load: before the wait
     gd_wait();  // the activation image is the previous kernel's output
     gd_launch();
-    if (tid == 0) {
-        mbar_expect7(xbar, (uint32_t)(NC * nb * Q8K_IMG_BYTES) + g7_test_extra_tx);
-        for (int c = 0; c < NC; c++)
-            bulk7(smem + Geo::BAR + Geo::RING + (size_t)c * nb * Q8K_IMG_BYTES, img + (size_t)c * nb * Q8K_IMG_BYTES,
-                  (uint32_t)(nb * Q8K_IMG_BYTES), xbar);
+    {  // stage the image, code quads rearranged (q = 4 tg + c -> 4 c + tg)
+        const uint4* src = reinterpret_cast<const uint4*>(img);
+        uint4* dst = reinterpret_cast<uint4*>(xs);
+        const int nq = NC * nb * (Q8K_IMG_BYTES / 16);
+        for (int i = tid; i < nq; i += 32 * G) {
+            const int blk = i / (Q8K_IMG_BYTES / 16), q = i % (Q8K_IMG_BYTES / 16);
+            const int qd = q < 16 ? 4 * (q & 3) + (q >> 2) : q;
+            dst[blk * (Q8K_IMG_BYTES / 16) + qd] = src[i];
+        }
     }
-    if (!active) {
-        if (tid == 0) mbar_wait7(xbar, 0);  // the x copies land before the CTA can end
-        return;
-    }
+    __syncthreads();
+    if (!active) return;
     float acc[R][NC][2], accm[R][NC];
 #pragma unroll
     for (int j = 0; j < R; j++)
 #pragma unroll
         for (int n = 0; n < NC; n++) acc[j][n][0] = acc[j][n][1] = accm[j][n] = 0.0f;
 
-    bool ok = __all_sync(0xffffffffu, mbar_wait7(xbar, 0));
+    bool ok = true;
     int win = 0;
-    for (; ok && win < nwin; win++) {
+    for (; win < nwin; win++) {
         const int slot = win % D;
         if (!__all_sync(0xffffffffu, mbar_wait7(&bar[slot], (uint32_t)((win / D) & 1)))) {
             ok = false;
@@ -375,7 +382,7 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
                 uint32_t xw[16];
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    const uint4 v = reinterpret_cast<const uint4*>(xb + 64 * tg)[c];
+                    const uint4 v = reinterpret_cast<const uint4*>(xb)[4 * c + tg];
                     xw[4 * c] = v.x, xw[4 * c + 1] = v.y, xw[4 * c + 2] = v.z, xw[4 * c + 3] = v.w;
                 }
                 const float dx = *reinterpret_cast<const float*>(xb + Q8K_IMG_D);
@@ -407,7 +414,6 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
             atomicCAS(&g7_error, 0u, 0x700u | (unsigned)TYPE);
             for (int k = win; k < nwin && k < win + D; k++) mbar_wait7(&bar[k % D], (uint32_t)((k / D) & 1));
         }
-        if (tid == 0) mbar_wait7(xbar, 0);
         return;
     }
     // per (tile, column, row): reduce8 of the 8 main lanes + reduce4 of the 4 min lanes (kdot.rs:75)
@@ -432,12 +438,12 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
 
 // CTA = G x S warps: warp w serves tile group w % G (R tiles of 8 rows) and super-block phase w / G, i.e.
 // super-blocks w/G, w/G + S, ... of its tiles.  Thread 0 keeps D windows of S super-blocks in flight.
-template <int TYPE, int NC, int G, int S, int R, int D>
+template <int TYPE, int NC, int G, int S, int R, int D, bool X2>
 __global__ void __launch_bounds__(32 * G * S)
 kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
     using G_ = G7<TYPE>;
-    using Geo = Geo7<TYPE, NC, G, S, R, D>;
+    using Geo = Geo7<TYPE, NC, G, S, R, D, X2>;
     constexpr int TB = G_::TB, LPC = G_::LPC, PER_SB = Geo::PER_SB;
     constexpr int CHAINS = G * R * NC * 8 * LPC;
     constexpr int NT = 32 * G * S;
@@ -465,7 +471,7 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
     auto issue_w = [&](int win) {
         uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE;
         const int n = win_sbs(win);
-        mbar_expect7(&bar[win % D], (uint32_t)(n * (G * R * TB + NC * Q8K_IMG_BYTES)) + (win == 0 ? g7_test_extra_tx : 0u));
+        mbar_expect7(&bar[win % D], (uint32_t)(n * (G * R * TB + (X2 ? 2 : 1) * NC * Q8K_IMG_BYTES)) + (win == 0 ? g7_test_extra_tx : 0u));
         for (int k = 0; k < G * R; k++) {
             const int t = min(bid * G * R + k, tiles - 1);
             bulk7(st + (size_t)k * S * TB, w + ((size_t)t * nb + (size_t)win * S) * TB, (uint32_t)(n * TB), &bar[win % D]);
@@ -475,8 +481,9 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
         uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE + Geo::WST;
         const int n = win_sbs(win);
         for (int c = 0; c < NC; c++)
-            bulk7(st + (size_t)c * S * Q8K_IMG_BYTES, img + ((size_t)c * nb + (size_t)win * S) * Q8K_IMG_BYTES,
-                  (uint32_t)(n * Q8K_IMG_BYTES), &bar[win % D]);
+            for (int copy = 0; copy < (X2 ? 2 : 1); copy++)
+                bulk7(st + (copy ? Geo::XOFF : 0) + (size_t)c * S * Q8K_IMG_BYTES,
+                      img + ((size_t)c * nb + (size_t)win * S) * Q8K_IMG_BYTES, (uint32_t)(n * Q8K_IMG_BYTES), &bar[win % D]);
     };
     if (tid == 0) {
         s_abort = 0;
@@ -516,7 +523,7 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
             float* tb = terms + (size_t)(((win & 1) * S + si) * G + gi) * PER_SB;
 #pragma unroll
             for (int n = 0; n < NC; n++) {
-                const uint8_t* xb = st + Geo::WST + (size_t)(n * S + si) * Q8K_IMG_BYTES;
+                const uint8_t* xb = st + Geo::WST + (X2 && tg >= 2 ? Geo::XOFF : 0) + (size_t)(n * S + si) * Q8K_IMG_BYTES;
                 uint32_t xw[16];
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
@@ -623,11 +630,11 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
     }
 }
 
-template <int TYPE, int NC, int G, int S, int R, int D>
+template <int TYPE, int NC, int G, int S, int R, int D, bool X2 = false>
 cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                     const void* img, cudaStream_t s, bool pdl) {
-    using Geo = Geo7<TYPE, NC, G, S, R, D>;
-    auto kern = kq_gemv7_kernel<TYPE, NC, G, S, R, D>;
+    using Geo = Geo7<TYPE, NC, G, S, R, D, X2>;
+    auto kern = kq_gemv7_kernel<TYPE, NC, G, S, R, D, X2>;
     static bool attr_done = false;  // per instantiation
     if (!attr_done) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Geo::BYTES);
@@ -682,21 +689,23 @@ int g_cfg7 = [] {
 template <int TYPE, int NC>
 cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                         const void* img, cudaStream_t s, bool pdl) {
-    if (cfg == 0) {
+    if (cfg == 0) {  // by the rows of the launch (both matrices of a pair) and the column count, as measured
         const int rows = rows_a + (w_b ? rows_b : 0);
-        if (rows >= 16384) cfg = 1;
-        else cfg = 8;
+        if (rows >= 100000) cfg = NC == 1 ? 1 : 4;
+        else if (rows >= 16384) cfg = NC == 1 ? 6 : 5;
+        else if (rows >= 8192) cfg = 3;
+        else cfg = TYPE == T_Q4_K ? 8 : 9;
     }
     switch (cfg) {
     case 1: return launch7s<TYPE, NC, 4, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 2: return launch7s<TYPE, NC, 4, 2, 3, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 3: return launch7s<TYPE, NC, 4, 1, 3, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 4: return launch7s<TYPE, NC, 8, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 5: return launch7<TYPE, NC, 2, 2, 1, 4>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4: return launch7s<TYPE, NC, 4, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 5: return launch7s<TYPE, NC, 4, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 6: return launch7s<TYPE, NC, 2, 2, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 7: return launch7<TYPE, NC, 1, 4, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 8: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 9: return launch7<TYPE, NC, 2, 4, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 9: return launch7<TYPE, NC, 2, 4, 1, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     default: return launch7<TYPE, NC, 1, 8, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }
@@ -747,7 +756,7 @@ int selftest_gemv7_timeout(unsigned long long wait_ns) {
         read_gemv7_error(true);
     }
     const int saved_cfg = g_cfg7;
-    for (int cfg : {1, 8}) {  // the streaming kernel's x wait, the windowed kernel's first window
+    for (int cfg : {1, 8}) {  // the streaming kernel's first weight stage, the windowed kernel's first window
         if (rc) break;
         g_cfg7 = cfg;
         const unsigned extra = 16;

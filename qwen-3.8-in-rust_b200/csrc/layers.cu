@@ -277,9 +277,60 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
     __shared__ __align__(16) float qs_all[CH][DK], ks_all[CH][DK];
     __shared__ float gate[CH][2], nrm[CH][2];  // (decay, beta), (1/|q|, 1/|k|)
     __shared__ float red[16], outs[128], part[128], dlt[128];
+    __shared__ float ab_part[2 * CH * 160], ab_val[2][CH];  // the in-kernel alpha / beta products
     // Before griddepcontrol.wait: everything the conv kernel (launched right before) does not write -- the state
-    // and the previous call's pending rows (this layer's own), the gates of the first rows (ssm_alpha/ssm_beta,
-    // two launches back) and their z rows (attn_gate, three back).
+    // and the previous call's pending rows (this layer's own), the gates of the first rows (ssm_alpha/ssm_beta
+    // two launches back, or their products from the normed rows, further back) and their z rows (attn_gate).
+    const int nr0 = min(CH, a.t);
+    if (a.w_alpha) {
+        // alpha, beta of this head for the t rows: dot_f32 (dot.rs:180-198) of the F32 weight rows with the normed
+        // rows -- 32-element partials left to right, then the partials chained in order plus the tail partial
+        // thread jp: partial jp of both weight rows against every normed row (each weight segment read once)
+        const int H = a.hid, np = (H + 31) / 32, nfull = H / 32;
+        const float* wa = a.w_alpha + (size_t)p * H;
+        const float* wb = a.w_beta + (size_t)p * H;
+        for (int jp = t; jp < nfull; jp += blockDim.x) {
+            float4 w4[2][8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                w4[0][q] = __ldg(reinterpret_cast<const float4*>(wa + jp * 32) + q);
+                w4[1][q] = __ldg(reinterpret_cast<const float4*>(wb + jp * 32) + q);
+            }
+            for (int r = 0; r < nr0; r++) {
+                float4 x4[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) x4[q] = __ldg(reinterpret_cast<const float4*>(a.xn + (size_t)r * H + jp * 32) + q);
+#pragma unroll
+                for (int which = 0; which < 2; which++) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        acc = __fadd_rn(acc, __fmul_rn(w4[which][q].x, x4[q].x));
+                        acc = __fadd_rn(acc, __fmul_rn(w4[which][q].y, x4[q].y));
+                        acc = __fadd_rn(acc, __fmul_rn(w4[which][q].z, x4[q].z));
+                        acc = __fadd_rn(acc, __fmul_rn(w4[which][q].w, x4[q].w));
+                    }
+                    ab_part[(which * CH + r) * 160 + jp] = acc;
+                }
+            }
+        }
+        if (t < 2 * nr0 && np > nfull) {  // the tail partial (hid % 32 elements)
+            const int which = t / nr0, r = t % nr0;
+            const float* wr = (which ? wb : wa);
+            float acc = 0.0f;
+            for (int i = nfull * 32; i < H; i++) acc = __fadd_rn(acc, __fmul_rn(wr[i], a.xn[(size_t)r * H + i]));
+            ab_part[(which * CH + r) * 160 + nfull] = acc;
+        }
+        __syncthreads();
+        if (t < 2 * nr0) {
+            const int which = t / nr0, r = t % nr0;
+            const float* pp = ab_part + (which * CH + r) * 160;
+            float acc = 0.0f;
+            for (int jp = 0; jp < nfull; jp++) acc = __fadd_rn(acc, pp[jp]);
+            ab_val[which][r] = __fadd_rn(acc, np > nfull ? pp[nfull] : 0.0f);
+        }
+        __syncthreads();
+    }
     float S[HK];
     float* Sg = a.S + (size_t)p * dk * dv;
 #pragma unroll
@@ -299,11 +350,12 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
         for (int k = 0; k < HK; k++) Sg[(size_t)(k0 + k) * dv + j] = S[k];
     }
     // gates (g = a * softplus(alpha + dt_bias), decay = exp(g), beta = sigmoid(b)) of the first chunk's rows
-    const int nr0 = min(CH, a.t);
     if (t < nr0) {
-        const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(a.alpha[(size_t)t * a.n_v + p], a.dt_bias[p])));
+        const float al = a.w_alpha ? ab_val[0][t] : a.alpha[(size_t)t * a.n_v + p];
+        const float be = a.w_alpha ? ab_val[1][t] : a.beta[(size_t)t * a.n_v + p];
+        const float g = __fmul_rn(a.ssm_a[p], softplus_f32(__fadd_rn(al, a.dt_bias[p])));
         gate[t][0] = exp_f32(g);
-        gate[t][1] = sigmoid_f32(a.beta[(size_t)t * a.n_v + p]);
+        gate[t][1] = sigmoid_f32(be);
     }
     float zr[CH];
 #pragma unroll

@@ -21,6 +21,12 @@ struct DeltaArgs {
     const int* keep_prev;     // device int: pending rows of the previous call to commit (null: 0)
     int t, max_t, n_k, n_v, dk, dv, kd, conv_dim;
     float eps;
+    // optional (t <= 8, hid <= 5120): the F32 ssm_alpha / ssm_beta rows [n_v][hid] and the normed rows [t][hid];
+    // when set, the kernel computes alpha and beta itself instead of reading them
+    const float* w_alpha;
+    const float* w_beta;
+    const float* xn;
+    int hid;
 };
 
 struct QkArgs {
