@@ -486,9 +486,10 @@ def spec_prompt(vocab, seed):
 
 
 def dominant_gemv_timing(dev, launches=200, n=4):
-    """The verify's dominant kernel timed alone on the launching stream with CUDA events: the Q4_K GEMV of
-    ffn_gate/ffn_up (17408 x 5120, tile layout, N = 4 columns), weights rotating over 3 sets (> L2).  With
-    n >= 8 columns the same call runs the prefill's tensor-core GEMM."""
+    """The verify's dominant kernel timed alone on the launching stream with CUDA events: the fused Q4_K GEMV of
+    ffn_gate and ffn_up (two 17408 x 5120 tile matrices against the same N = 4 image columns, one launch, as the
+    layer runs it), weight pairs rotating over 3 sets (300 MB > L2).  With n >= 8 columns the same call runs the
+    prefill's tensor-core GEMM."""
     import torch
 
     import qdec
@@ -498,19 +499,28 @@ def dominant_gemv_timing(dev, launches=200, n=4):
     sp = stream.cuda_stream
     sets = []
     for s in range(N_SETS):
-        src = torch.from_numpy(synth_q4k(rows, cols, seed=500 + s)).to(dev)
-        dst = torch.empty_like(src)
-        qdec.repack_tiles(qdec.Q4_K, src.data_ptr(), rows, cols, dst.data_ptr(), sp)
-        sets.append(dst)
+        pair = []
+        for m in range(2):
+            src = torch.from_numpy(synth_q4k(rows, cols, seed=500 + 2 * s + m)).to(dev)
+            dst = torch.empty_like(src)
+            qdec.repack_tiles(qdec.Q4_K, src.data_ptr(), rows, cols, dst.data_ptr(), sp)
+            pair.append(dst)
+        sets.append(pair)
     x = torch.randn(n, cols, generator=torch.Generator().manual_seed(7), dtype=torch.float32).to(dev)
     t = qdec.TILE[qdec.Q4_K]
     img = torch.empty(n * qdec.image_row_bytes(t, cols), dtype=torch.uint8, device=dev)
-    y = torch.empty(n * rows, dtype=torch.float32, device=dev)
+    y1 = torch.empty(n * rows, dtype=torch.float32, device=dev)
+    y2 = torch.empty(n * rows, dtype=torch.float32, device=dev)
     qdec.quantize_image(t, x.data_ptr(), cols, n, img.data_ptr(), sp)
+
+    def launch(i):
+        w1, w2 = sets[i % N_SETS]
+        qdec.gemv_image_pair(t, w1.data_ptr(), w2.data_ptr(), rows, cols, img.data_ptr(), n, y1.data_ptr(), y2.data_ptr(), sp)
+
     for i in range(min(10, launches)):
-        qdec.gemv_image(t, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
+        launch(i)
     torch.cuda.synchronize()
-    # back-to-back launches between two events on the launching stream (the weight sets rotate, 150 MB > L2):
+    # back-to-back launches between two events on the launching stream (the weight sets rotate, 300 MB > L2):
     # the average launch duration, without per-launch event records in between; median of 5 batches
     batch = max(1, launches // 5)
     per = []
@@ -518,12 +528,13 @@ def dominant_gemv_timing(dev, launches=200, n=4):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(batch):
-            qdec.gemv_image(t, sets[i % N_SETS].data_ptr(), rows, cols, img.data_ptr(), n, y.data_ptr(), sp)
+            launch(i)
         e1.record(stream)
         torch.cuda.synchronize()
         per.append(e0.elapsed_time(e1) / batch)
     ms = statistics.median(per)
-    alg = rows * (cols // 256) * Q4K_BB + n * (cols // 256) * 292 + 4 * n * rows
+    # algorithmic bytes of one launch: both weight matrices once, the image columns once, both outputs
+    alg = 2 * rows * (cols // 256) * Q4K_BB + n * (cols // 256) * 320 + 2 * 4 * n * rows
     del sets
     return alg, ms
 
@@ -887,7 +898,7 @@ def run_spec_qdec(args, world, rank, local):
         "e2e": {"value": round(emitted_all / wall, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * (k + 2)},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "Q4_K GEMV 17408x5120 N=4 (verify ffn_gate/ffn_up, tile layout)",
+        "roofline": {"bound": "hbm", "kernel": "kq_gemv7s_kernel: ffn_gate + ffn_up Q4_K 2 x 17408x5120, N=4 (one launch)",
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "alg_bytes_per_launch": alg,
                      "launch_us": round(kern_ms * 1e3, 2),
@@ -938,7 +949,8 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=None,
                     help="prompt ids before the timed rounds (default 128; 8064 grows the KV cache to ~8192: config 5)")
     ap.add_argument("--profile-gemv", action="store_true",
-                    help="run the dominant GEMV (Q4_K 17408x5120 N=4, tile layout) 4 times and exit: the ncu capture target")
+                    help="run the dominant GEMV (ffn_gate + ffn_up, Q4_K 2 x 17408x5120, N=4, one launch) 4 times and exit: "
+                         "the ncu capture target")
     ap.add_argument("--profile-prefill-gemm", action="store_true",
                     help="run the prefill's tensor-core GEMM (Q4_K 17408x5120, 32 columns) 4 times, print its event time "
                          "and exit: the ncu capture target")
@@ -949,7 +961,7 @@ def main():
         torch.cuda.set_device(0)
         n = 32 if args.profile_prefill_gemm else 4
         _, ms = dominant_gemv_timing(torch.device("cuda", 0), launches=4, n=n)
-        print(json.dumps({"kernel": f"Q4_K 17408x5120 x {n} columns", "us_per_launch": round(ms * 1e3, 2)}))
+        print(json.dumps({"kernel": f"Q4_K 2 x 17408x5120 (gate + up) x {n} columns", "us_per_launch": round(ms * 1e3, 2)}))
         return
     if args.prompt_len:
         global PROMPT_LEN

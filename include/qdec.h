@@ -88,22 +88,28 @@ int qdec_matvec(int ggml_type, const void *w_dev, int rows, int cols, const floa
  * tile) read the Q8_K image, QDEC_TYPE_Q8_0_TILE / _Q4_0_TILE the Q8_0 image.  qdec_gemv_image wants the weights
  * and the image 16-byte aligned (QDEC_EINVAL otherwise). */
 size_t qdec_image_row_bytes(int ggml_type, int cols);
+/* Two K-quant tile matrices of the same shape against the same image columns in one launch (the MLP's gate and
+ * up): y1[c * rows + r] = W1[r] . x_c, y2[c * rows + r] = W2[r] . x_c.  Replaces matvec2
+ * (crates/core/src/kernels/matvec.rs:349) for the case x1 == x2 that mlp.rs:55 uses; the bits of each output are
+ * those of qdec_gemv_image on that matrix alone. */
+int qdec_gemv_image_pair(int ggml_type, const void *w1_dev, const void *w2_dev, int rows, int cols, const void *img_dev,
+                         int n_cols, float *y1_dev, float *y2_dev, void *stream);
 int qdec_quantize_image(int ggml_type, const float *x_dev, int n, int rows, void *img_dev, void *stream);
 int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const void *img_dev, int n_cols, float *y_dev,
                     void *stream);
 
-/* Tuning knob of the GEMV (process-wide): the K-quant kernel (0 = automatic; 2 = the kernel that reads
- * block_q8_K activations in the reference layout; 6 = the kernel that reads the library's activation image) and
- * the image kernel's configuration (0 = automatic, 1..35: lanes and rows per thread, tiles per warp, warps per
- * tile, super-blocks in flight, integer or FP32 scale multiply, activation prefetch / residency); or, with
- * impl = 8, the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
- * over 4 warps, 3 = the same with two tiles per CTA); or, with impl = 9, the tensor-core prefill GEMM that K-quant
- * tile matrices take for many columns (config = the smallest column count routed there, 8 by default, 0 = never;
- * decode's 1..4 verify columns stay on the GEMV at any value >= 5); or, with impl = 7, the decode GEMV that K-quant
- * tile matrices take for 1..7 columns (config 0 = by shape, 1..10 = a fixed split of tile groups, super-block
- * phases, tiles per warp and windows in flight; impl 6 routes those matrices to the older image kernel).
- * Results do not depend on it; it exists for
- * tests and sweeps.  No counterpart in the reference. */
+/* Tuning knob of the GEMV (process-wide; results do not depend on it -- it exists for tests and sweeps):
+ *   impl 0 / 6: the kernel for ggml-layout Q4_K / Q5_K and split-layout Q6_K weights that reads the library's
+ *     activation image (config 0 = automatic, 1..8 = lanes and rows per thread, depth, integer or FP32 scale
+ *     multiply); impl 2: the kernel that reads block_q8_K activations in the reference layout instead;
+ *   impl 7: the decode GEMV of K-quant tile matrices (config 0 = by shape, 1..10 = the streaming or windowed
+ *     kernel with a fixed number of warps, tiles per warp, super-block phases and stages in flight);
+ *   impl 8: the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
+ *     over 4 warps, 3 = the same with two tiles per CTA);
+ *   impl 9: the tensor-core prefill GEMM that K-quant tile matrices take for many columns (config = the smallest
+ *     column count routed there, 8 by default, 0 = never; the 1..4 verify columns stay on the GEMV at any value
+ *     >= 5).
+ * No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
 
 /* Failure-handling self-test of one bounded device wait on the current device, in this process, without a peer

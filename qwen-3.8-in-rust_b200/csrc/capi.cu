@@ -227,6 +227,21 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
     return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv_image");
 }
 
+int qdec_gemv_image_pair(int ggml_type, const void *w1_dev, const void *w2_dev, int rows, int cols, const void *img_dev,
+                         int n_cols, float *y1_dev, float *y2_dev, void *stream) {
+    int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);
+    if (rc) return rc;
+    if (!w1_dev || !w2_dev || !img_dev || !y1_dev || !y2_dev) return fail(QDEC_EINVAL, "qdec_gemv_image_pair: null pointer");
+    if (ggml_type != T_Q4_K_TILE && ggml_type != T_Q5_K_TILE && ggml_type != T_Q6_K_TILE)
+        return fail(QDEC_EINVAL, "qdec_gemv_image_pair: type %d is not a K-quant tile type", ggml_type);
+    if ((((uintptr_t)w1_dev | (uintptr_t)w2_dev | (uintptr_t)img_dev) & 15) != 0)
+        return fail(QDEC_EINVAL, "qdec_gemv_image_pair: weights and image must be 16-byte aligned");
+    if (n_cols == 0 || rows == 0) return QDEC_OK;
+    const cudaError_t e = launch_gemv_img_pair(ggml_type, (const uint8_t *)w1_dev, rows, y1_dev, (const uint8_t *)w2_dev, rows,
+                                               y2_dev, cols, img_dev, n_cols, (cudaStream_t)stream, false);
+    return e == cudaSuccess ? QDEC_OK : cuda_fail(e, "qdec_gemv_image_pair");
+}
+
 int qdec_tune_gemv(int impl, int config) {
     if (impl == 8) {  // the Q8_0 / Q4_0 tile kernel: 0 automatic, 1 one warp per tile, 2 split group range,
                       // 3 split group range with two tiles per CTA
@@ -247,7 +262,7 @@ int qdec_tune_gemv(int impl, int config) {
     }
     if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 7, 8 or 9");
     if (impl == 0) set_gemv7_config(0);
-    if (config < 0 || config > 35) return fail(QDEC_EINVAL, "gemv configuration must be 0..35");
+    if (config < 0 || config > 8) return fail(QDEC_EINVAL, "gemv configuration must be 0..8");
     set_gemv_impl(impl);
     set_gemv_v6_config(config);
     return QDEC_OK;

@@ -66,6 +66,7 @@ def lib():
             "qdec_quantize_image": [I, P, I, I, P, P],
             "qdec_gemv_image": [I, P, I, I, P, I, P, P],
             "qdec_selftest_wait": [I, I],
+            "qdec_gemv_image_pair": [I, P, P, I, I, P, I, P, P, P],
         }.items():
             fn = getattr(L, name)
             fn.restype = I
@@ -178,15 +179,19 @@ def gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream=0):
     _check(lib().qdec_gemv_image(t, w_ptr, rows, cols, img_ptr, ncols, y_ptr, stream))
 
 
+def gemv_image_pair(t, w1_ptr, w2_ptr, rows, cols, img_ptr, ncols, y1_ptr, y2_ptr, stream=0):
+    """matvec2 (crates/core/src/kernels/matvec.rs:349) over the image: two tile matrices, one launch."""
+    _check(lib().qdec_gemv_image_pair(t, w1_ptr, w2_ptr, rows, cols, img_ptr, ncols, y1_ptr, y2_ptr, stream))
+
+
 GEMV7_CONFIGS = 10
 
 
 def tune_gemv(impl=0, config=0):
-    """Select the K-quant GEMV kernel (0 automatic, 2 reference-layout activations, 6 activation image) and the
-    image kernel's configuration (0 automatic, 1..35); impl 7 the decode GEMV of K-quant tile matrices (0 by
-    shape, 1..10; impl 6 sends those matrices to the older image kernel); impl 8 the Q8_0/Q4_0 tile kernel
-    (0..3); impl 9 the smallest column count of the tensor-core prefill GEMM (default 8, 0 never). Results are
-    identical for every value."""
+    """Select a GEMV kernel / configuration (qdec_tune_gemv): impl 0/6 the image kernel of ggml-layout Q4_K/Q5_K
+    and split Q6_K weights (config 0..8), impl 2 the reference-layout activation kernel, impl 7 the decode GEMV of
+    K-quant tile matrices (0 by shape, 1..10), impl 8 the Q8_0/Q4_0 tile kernel (0..3), impl 9 the smallest column
+    count of the tensor-core prefill GEMM (default 8, 0 never). Results are identical for every value."""
     _check(lib().qdec_tune_gemv(impl, config))
 
 

@@ -255,30 +255,6 @@ def test_gemv_reference_layout_kernel_bit_exact(q, orc, t):
     assert bits_equal(got, want)
 
 
-@pytest.mark.parametrize("t", [12, 13, 14])
-@pytest.mark.parametrize("cfg", range(1, 36))
-def test_gemv_tile_layout_every_config_bit_exact(q, orc, t, cfg):
-    """Weights repacked into the tile layout (8 rows x one super-block per tile block): the oracle's bits for
-    1..5 columns in every configuration, a super-block count that is not a multiple of any depth, a tile count
-    that is not a multiple of two."""
-    rows, cols = 8 * 37, 5376
-    w = random_blocks(t, rows, cols, seed=31 + t)
-    x = np.random.default_rng(100 + cfg).standard_normal((5, cols)).astype(np.float32)
-    x[3] *= 1e20
-    want = orc.matmul(t, w, rows, cols, x)
-    src = to_dev(w)
-    dst = torch.empty_like(src)
-    q.repack_tiles(t, src.data_ptr(), rows, cols, dst.data_ptr())
-    torch.cuda.synchronize()
-    q.tune_gemv(6, cfg)
-    try:
-        for n in (1, 2, 3, 4, 5):
-            got = run_gemv_raw(q, q.TILE[t], dst, rows, cols, x[:n])
-            assert bits_equal(got, want[:n]), (t, cfg, n)
-    finally:
-        q.tune_gemv(0, 0)
-
-
 def test_tile_repack_rejects_ragged_rows(q):
     src = torch.zeros(12 * 144, dtype=torch.uint8, device="cuda")
     dst = torch.empty_like(src)
@@ -363,6 +339,31 @@ def test_gemv7_every_config_bit_exact(q, orc, t, cfg):
             assert bits_equal(got, want[:n]), (t, cfg, n)
     finally:
         q.tune_gemv(0, 0)
+
+
+@pytest.mark.parametrize("t", [12, 14])
+def test_gemv_image_pair_bit_exact(q, orc, t):
+    """qdec_gemv_image_pair (matvec2, matvec.rs:349): two tile matrices against the same image columns in one
+    launch give, matrix by matrix, the oracle's bits for 1..5 columns."""
+    rows, cols = 8 * 45, 5120
+    w1 = random_blocks(t, rows, cols, seed=81 + t)
+    w2 = random_blocks(t, rows, cols, seed=91 + t)
+    x = np.random.default_rng(t).standard_normal((5, cols)).astype(np.float32)
+    x[2] *= 1e-20
+    want1 = orc.matmul(t, w1, rows, cols, x)
+    want2 = orc.matmul(t, w2, rows, cols, x)
+    d1, d2 = _repack(q, t, w1, rows, cols), _repack(q, t, w2, rows, cols)
+    tt = q.TILE[t]
+    for n in (1, 2, 3, 4, 5):
+        xd = to_dev(x[:n])
+        img = torch.empty(n * q.image_row_bytes(tt, cols), dtype=torch.uint8, device="cuda")
+        q.quantize_image(tt, xd.data_ptr(), cols, n, img.data_ptr())
+        y1 = torch.empty(n * rows, dtype=torch.float32, device="cuda")
+        y2 = torch.empty(n * rows, dtype=torch.float32, device="cuda")
+        q.gemv_image_pair(tt, d1.data_ptr(), d2.data_ptr(), rows, cols, img.data_ptr(), n, y1.data_ptr(), y2.data_ptr())
+        torch.cuda.synchronize()
+        assert bits_equal(y1.cpu().numpy().reshape(n, rows), want1[:n]), (t, n, 1)
+        assert bits_equal(y2.cpu().numpy().reshape(n, rows), want2[:n]), (t, n, 2)
 
 
 def _extreme_blocks(t, rows, cols, seed, neg_scales=False):
