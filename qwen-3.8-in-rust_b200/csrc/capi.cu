@@ -255,7 +255,7 @@ int qdec_tune_gemv(int impl, int config) {
         return QDEC_OK;
     }
     if (impl == 7) {  // the decode GEMV of tile matrices: 0 automatic by shape, 1..10 a fixed configuration
-        if (config < 0 || config > 10) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..10");
+        if (config < 0 || config > 14) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..14");
         set_gemv_impl(0);
         set_gemv7_config(config);
         return QDEC_OK;

@@ -691,10 +691,10 @@ cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, con
                         const void* img, cudaStream_t s, bool pdl) {
     if (cfg == 0) {  // by the rows of the launch (both matrices of a pair) and the column count, as measured
         const int rows = rows_a + (w_b ? rows_b : 0);
-        if (rows >= 100000) cfg = NC == 1 ? 1 : 4;
-        else if (rows >= 16384) cfg = NC == 1 ? 6 : 5;
+        if (rows >= 100000) cfg = NC == 1 ? 1 : 12;
+        else if (rows >= 16384) cfg = 11;
         else if (rows >= 8192) cfg = 3;
-        else cfg = TYPE == T_Q4_K ? 8 : 9;
+        else cfg = 13;
     }
     switch (cfg) {
     case 1: return launch7s<TYPE, NC, 4, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
@@ -706,6 +706,10 @@ cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, con
     case 7: return launch7<TYPE, NC, 1, 4, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 8: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 9: return launch7<TYPE, NC, 2, 4, 1, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 11: return launch7s<TYPE, NC, 5, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 12: return launch7s<TYPE, NC, 6, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 13: return launch7<TYPE, NC, 1, 4, 2, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 14: return launch7<TYPE, NC, 2, 4, 1, 3, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     default: return launch7<TYPE, NC, 1, 8, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }

@@ -319,7 +319,7 @@ def _repack(q, t, w, rows, cols):
 
 
 @pytest.mark.parametrize("t", [12, 13, 14])
-@pytest.mark.parametrize("cfg", range(0, 11))
+@pytest.mark.parametrize("cfg", range(0, 15))
 def test_gemv7_every_config_bit_exact(q, orc, t, cfg):
     """The decode GEMV of tile matrices (gemv7.cu) in each configuration (tiles per warp, warps splitting the
     super-blocks, depth, register cap): the oracle's bits for 1..5 columns on a tile count that is not a multiple
