@@ -872,7 +872,7 @@ def run_spec_qdec(args, world, rank, local):
     alg, kern_ms = dominant_gemv_timing(torch.device("cuda", local))
     achieved = alg / (kern_ms / 1e3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "q4k_gemv_n4_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "gemv_pair_q4k_n4_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
