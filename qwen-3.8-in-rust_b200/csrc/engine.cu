@@ -506,6 +506,9 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
     mlp_out_ = (float*)dalloc(T * H * 4);
     q8k_ = (uint8_t*)dalloc(T * q8k_stride_);
     q80_ = (uint8_t*)dalloc(T * q80_stride_);
+    ffn_img_ = (uint8_t*)dalloc(T * q8k_stride_);
+    ffn_cnt_ = (unsigned*)dalloc((c.intermediate_size / 256 + 1) * sizeof(unsigned));
+    dn_cnt_ = (unsigned*)dalloc((c.dn_v_dim / 256 + 1) * sizeof(unsigned));
     g_ = (float*)dalloc(T * FF * 4);
     u_ = (float*)dalloc(T * FF * 4);
     final_ = (float*)dalloc(T * H * 4);
@@ -821,10 +824,15 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, channels, qkv_, t, conved_, d.pend_x,
                             commit_dn ? d_keep : nullptr, T_, stream), "conv");
         const int dk = (int)c.dn_head_dim_k, dv = (int)c.dn_head_dim_v;
+        // one GPU: the kernel also quantises its head outputs for ssm_out (over TP ranks the f32 heads are
+        // exchanged first and the full rows quantised after)
+        const int ot = L.ssm_out.type;
+        const bool q_fused = !tp() && (is_kquant(ot) || is_q80(ot)) && 256 % dv == 0 && (P.nv * dv) % 256 == 0;
         DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,
                      commit_dn ? d_keep : nullptr, t, T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps,
                      ab_fused ? (const float*)L.alpha.p : nullptr, ab_fused ? (const float*)L.beta.p : nullptr,
-                     ab_fused ? normed_ : nullptr, H};
+                     ab_fused ? normed_ : nullptr, H,
+                     q_fused && is_kquant(ot) ? q8k_ : nullptr, q_fused && is_q80(ot) ? q80_ : nullptr, dn_cnt_};
         count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
         const float* heads_full = heads_;
         if (tp()) {
@@ -839,7 +847,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
             exchange(heads_, (size_t)P.nv * dv * 4, xo_heads_, (size_t)c.dn_v_dim * 4, seg, G, t);
             heads_full = xg(xo_heads_);
         }
-        quant_for(L.ssm_out.type, heads_full, L.ssm_out.cols, t);
+        if (!q_fused) quant_for(L.ssm_out.type, heads_full, L.ssm_out.cols, t);
         gemv(L.ssm_out, heads_full, t, mix_out_);
     }
     if (tp()) {
@@ -849,7 +857,21 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
     // h = x + mixer(x); then the MLP on post_attention_norm(h) (mlp.rs:53-64)
     const bool k8 = needs_q8k({L.ffn_gate.type, L.ffn_up.type}), k0 = needs_q80({L.ffn_gate.type, L.ffn_up.type});
     resid_norm(mix_in(), L.post_norm, t, normed_, k8, k0);
-    if (L.ffn_gate.type == L.ffn_up.type && L.ffn_gate.cols == L.ffn_up.cols &&
+    const int dt = L.ffn_down.type;
+    const int ffr = L.ffn_gate.rows;  // this rank's FFN rows
+    // gate, up, silu(gate) * up and its Q8_K quantisation in one launch (the verify's and decode's few columns;
+    // a prompt chunk takes the tensor-core GEMM and the separate step)
+    const bool fused = L.ffn_gate.type == L.ffn_up.type && L.ffn_gate.rows == L.ffn_up.rows && L.ffn_gate.cols == L.ffn_up.cols &&
+                       gemv7_supported(L.ffn_gate.type) && is_kquant(dt) && ffr % 256 == 0 &&
+                       !gemm_tc_applies(L.ffn_gate.type, t);
+    const uint8_t* down_img = nullptr;  // the down projection's input image: the fused launch's, else the default
+    if (fused) {
+        count_launch((t + 3) / 4);
+        ck(launch_gemv7_swiglu(L.ffn_gate.type, L.ffn_gate.p, L.ffn_up.p, ffr, L.ffn_gate.cols, q8k_, t, g_, ffn_img_, ffn_cnt_,
+                               stream, true),
+           "gate/up/swiglu");
+        down_img = ffn_img_;
+    } else if (L.ffn_gate.type == L.ffn_up.type && L.ffn_gate.cols == L.ffn_up.cols &&
         (L.ffn_gate.type == T_Q4_K_TILE || L.ffn_gate.type == T_Q5_K_TILE || L.ffn_gate.type == T_Q6_K_TILE)) {
         // gate and up read the same normed rows: one launch over both (mlp.rs:55, matvec2)
         count_launch((t + 3) / 4);
@@ -860,15 +882,15 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         gemv(L.ffn_gate, normed_, t, g_);
         gemv(L.ffn_up, normed_, t, u_);
     }
-    const int dt = L.ffn_down.type;
-    const int ffr = L.ffn_gate.rows;  // this rank's FFN rows
-    count_launch(); ck(launch_swiglu_quant(g_, u_, ffr, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
-                           is_q80(dt) ? q80_ : nullptr, stream), "swiglu");
+    if (!fused) {
+        count_launch(); ck(launch_swiglu_quant(g_, u_, ffr, t, nullptr, is_kquant(dt) ? q8k_ : nullptr,
+                               is_q80(dt) ? q80_ : nullptr, stream), "swiglu");
+    }
     if (tp()) {
         const size_t FF = c.intermediate_size;
         if (is_kquant(dt)) {
             const int seg[1][3] = {{0, P.ff_lo / 256 * Q8K_IMG_BYTES, ffr / 256 * Q8K_IMG_BYTES}};
-            exchange(q8k_, (size_t)ffr / 256 * Q8K_IMG_BYTES, xo_ffn_, FF / 256 * Q8K_IMG_BYTES, seg, 1, t);
+            exchange(down_img ? down_img : q8k_, (size_t)ffr / 256 * Q8K_IMG_BYTES, xo_ffn_, FF / 256 * Q8K_IMG_BYTES, seg, 1, t);
         } else {
             // Q8_0 image row: [codes: 32 B per block][{d, sum}: 8 B per block]
             const int seg[2][3] = {{0, P.ff_lo, ffr}, {ffr, (int)FF + P.ff_lo / 32 * 8, ffr / 32 * 8}};
@@ -878,7 +900,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         const int seg[1][3] = {{0, P.h_lo * 4, P.h_rows * 4}};
         exchange(mlp_out_, (size_t)P.h_rows * 4, xo_mlp_, (size_t)H * 4, seg, 1, t);
     } else {
-        gemv(L.ffn_down, g_, t, mlp_out_);
+        gemv(L.ffn_down, g_, t, mlp_out_, down_img);
     }
 }
 

@@ -178,6 +178,9 @@ class State {
     void* amx_scratch_ = nullptr;  // argmax partials and counters
     float *h_ = nullptr, *h_alt_ = nullptr, *embed_ = nullptr, *normed_ = nullptr, *mix_out_ = nullptr, *mlp_out_ = nullptr;
     uint8_t *q8k_ = nullptr, *q80_ = nullptr;
+    uint8_t* ffn_img_ = nullptr;    // the fused gate/up launch's Q8_K image of h (the down projection's input)
+    unsigned* ffn_cnt_ = nullptr;   // its per-256-row-block completion counters (zero at rest)
+    unsigned* dn_cnt_ = nullptr;    // the DeltaNet kernel's per-block counters of its head-output quantisation
     float *qkv_ = nullptr, *conved_ = nullptr, *z_ = nullptr, *alpha_ = nullptr, *beta_ = nullptr, *heads_ = nullptr;
     float *qg_ = nullptr, *kk_ = nullptr, *vv_ = nullptr, *qr_ = nullptr, *gate_ = nullptr, *attn_ = nullptr;
     float *g_ = nullptr, *u_ = nullptr, *final_ = nullptr, *logits_ = nullptr, *att_scores_ = nullptr;

@@ -296,10 +296,17 @@ struct GeoS7 {
     static_assert(STAGE % 16 == 0, "stage alignment");
 };
 
-template <int TYPE, int NC, int G, int R, int D, int P>
+// SWIGLU (the MLP's gate and up, R = 2): a warp's two tiles are tile t of w_a (gate) and tile t of w_b (up), so it
+// ends holding both values of its 8 rows; it writes h = silu(g) * u (act.rs:24) to y_a, and the warp that
+// finishes last among the 32 tiles of a 256-row block (a counter per block, reset by that warp) quantises the
+// block of every column into the Q8_K image img_out -- the swiglu and quantise step of mlp.rs:114-132 without a
+// launch of its own.
+template <int TYPE, int NC, int G, int R, int D, int P, bool SWIGLU = false>
 __global__ void __launch_bounds__(32 * G)
 kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
-                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
+                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img, uint8_t* __restrict__ img_out,
+                 unsigned* __restrict__ blk_cnt) {
+    static_assert(!SWIGLU || R == 2, "the gate/up pairing holds one tile of each matrix");
     using G_ = G7<TYPE>;
     using Geo = GeoS7<TYPE, NC, G, R, D, P>;
     constexpr int TB = G_::TB;
@@ -309,14 +316,15 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem) + wid * D;
     uint8_t* ring = smem + Geo::BAR + (size_t)wid * D * Geo::STAGE;
     uint8_t* xs = smem + Geo::BAR + Geo::RING;
-    const int ctas_a = (rows_a / 8 + G * R - 1) / (G * R);
-    const bool second = (int)blockIdx.x >= ctas_a;
+    constexpr int TPW = SWIGLU ? 1 : R;  // tile indices per warp
+    const int ctas_a = (rows_a / 8 + G * TPW - 1) / (G * TPW);
+    const bool second = !SWIGLU && (int)blockIdx.x >= ctas_a;
     const uint8_t* w = second ? w_b : w_a;
     const int rows = second ? rows_b : rows_a;
     float* y = second ? y_b : y_a;
     const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
     const int tiles = rows / 8;
-    const int t0 = (bid * G + wid) * R;  // this warp's first tile
+    const int t0 = (bid * G + wid) * TPW;  // this warp's first tile
     const bool active = t0 < tiles;
     const int nwin = (nb + P - 1) / P;
 
@@ -325,8 +333,9 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
         const int n = min(P, nb - win * P);
         mbar_expect7(&bar[win % D], (uint32_t)(R * n * TB) + (win == 0 && wid == 0 ? g7_test_extra_tx : 0u));
         for (int j = 0; j < R; j++) {
-            const int t = min(t0 + j, tiles - 1);
-            bulk7(st + (size_t)j * P * TB, w + ((size_t)t * nb + (size_t)win * P) * TB, (uint32_t)(n * TB), &bar[win % D]);
+            const int t = SWIGLU ? t0 : min(t0 + j, tiles - 1);
+            const uint8_t* wm = SWIGLU && j == 1 ? w_b : w;
+            bulk7(st + (size_t)j * P * TB, wm + ((size_t)t * nb + (size_t)win * P) * TB, (uint32_t)(n * TB), &bar[win % D]);
         }
     };
     if (lane == 0 && active) {
@@ -418,6 +427,7 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
     }
     // per (tile, column, row): reduce8 of the 8 main lanes + reduce4 of the 4 min lanes (kdot.rs:75)
     const int base = rs * 4;
+    float vr[R][NC];
 #pragma unroll
     for (int j = 0; j < R; j++)
 #pragma unroll
@@ -427,13 +437,37 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
             for (int g = 0; g < 8; g++) l8[g] = __shfl_sync(0xffffffffu, acc[j][n][g & 1], base + (g >> 1));
 #pragma unroll
             for (int m = 0; m < 4; m++) m4[m] = __shfl_sync(0xffffffffu, accm[j][n], base + m);
+            float v = reduce8(l8);
+            if constexpr (G_::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
+            vr[j][n] = v;
             const int tile = t0 + j;
-            if (tg == 0 && tile < tiles) {
-                float v = reduce8(l8);
-                if constexpr (G_::MINS) v = __fadd_rn(v, __fadd_rn(__fadd_rn(m4[0], m4[2]), __fadd_rn(m4[1], m4[3])));
-                y[(size_t)n * rows + tile * 8 + rs] = v;
-            }
+            if (!SWIGLU && tg == 0 && tile < tiles) y[(size_t)n * rows + tile * 8 + rs] = v;
         }
+    if constexpr (SWIGLU) {
+        if (tg == 0)
+#pragma unroll
+            for (int n = 0; n < NC; n++) y_a[(size_t)n * rows + t0 * 8 + rs] = __fmul_rn(silu_f32(vr[0][n]), vr[1][n]);
+        __threadfence();  // the h rows before the block counter
+        __syncwarp();
+        const int blk = t0 / 32, nblk = rows / 256;
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&blk_cnt[blk], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == 31) {  // the block's last tile: quantise its 256 h values of every column
+            __threadfence();
+            float v[NC][8];  // every column's values first: one round trip to L2
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                const float4* hb = reinterpret_cast<const float4*>(y_a + (size_t)n * rows + (size_t)blk * 256 + lane * 8);
+                const float4 a = __ldcg(hb), b = __ldcg(hb + 1);
+                v[n][0] = a.x, v[n][1] = a.y, v[n][2] = a.z, v[n][3] = a.w;
+                v[n][4] = b.x, v[n][5] = b.y, v[n][6] = b.z, v[n][7] = b.w;
+            }
+#pragma unroll
+            for (int n = 0; n < NC; n++) q8k_quantize_to_image(v[n], img_out + ((size_t)n * nblk + blk) * Q8K_IMG_BYTES);
+            if (lane == 0) blk_cnt[blk] = 0u;  // ready for the next launch
+        }
+    }
 }
 
 // CTA = G x S warps: warp w serves tile group w % G (R tiles of 8 rows) and super-block phase w / G, i.e.
@@ -654,11 +688,11 @@ cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w
     return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
 }
 
-template <int TYPE, int NC, int G, int R, int D, int P>
+template <int TYPE, int NC, int G, int R, int D, int P, bool SWIGLU = false>
 cudaError_t launch7s(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
-                     const void* img, cudaStream_t s, bool pdl) {
+                     const void* img, cudaStream_t s, bool pdl, uint8_t* img_out = nullptr, unsigned* blk_cnt = nullptr) {
     using Geo = GeoS7<TYPE, NC, G, R, D, P>;
-    auto kern = kq_gemv7s_kernel<TYPE, NC, G, R, D, P>;
+    auto kern = kq_gemv7s_kernel<TYPE, NC, G, R, D, P, SWIGLU>;
     const size_t bytes = Geo::bytes(nb);
     static size_t attr_bytes = 0;  // per instantiation: the largest dynamic shared memory enabled so far
     if (bytes > 48 * 1024 && bytes > attr_bytes) {
@@ -667,7 +701,8 @@ cudaError_t launch7s(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* 
         attr_bytes = bytes;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((rows_a / 8 + G * R - 1) / (G * R) + (w_b ? (rows_b / 8 + G * R - 1) / (G * R) : 0));
+    cfg.gridDim = SWIGLU ? dim3((rows_a / 8 + G - 1) / G)
+                         : dim3((rows_a / 8 + G * R - 1) / (G * R) + (w_b ? (rows_b / 8 + G * R - 1) / (G * R) : 0));
     cfg.blockDim = dim3(32 * G);
     cfg.dynamicSmemBytes = bytes;
     cfg.stream = s;
@@ -676,7 +711,7 @@ cudaError_t launch7s(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
+    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img, img_out, blk_cnt);
 }
 
 int g_cfg7 = [] {
@@ -725,7 +760,38 @@ cudaError_t launch7_type(const uint8_t* w_a, int rows_a, float* y_a, const uint8
     }
 }
 
+template <int TYPE>
+cudaError_t launch7_swiglu_type(const uint8_t* w_g, const uint8_t* w_u, int rows, float* h, int nb, const void* img, int nc,
+                                uint8_t* img_out, unsigned* cnt, cudaStream_t s, bool pdl) {
+    switch (nc) {  // the pair's default geometry: 5 warps of one gate and one up tile, 2 stages of 2 super-blocks
+    case 1: return launch7s<TYPE, 1, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+    case 2: return launch7s<TYPE, 2, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+    case 3: return launch7s<TYPE, 3, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+    default: return launch7s<TYPE, 4, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gemv7_swiglu(int type, const uint8_t* w_gate, const uint8_t* w_up, int rows, int cols, const void* img,
+                                int ncols, float* h_out, uint8_t* img_out, unsigned* blk_cnt, cudaStream_t s, bool pdl) {
+    if (rows % 256 || cols % QK_K || !gemv7_supported(type)) return cudaErrorInvalidValue;
+    if (((uintptr_t)w_gate | (uintptr_t)w_up | (uintptr_t)img) & 15) return cudaErrorMisalignedAddress;
+    if (rows <= 0 || ncols <= 0) return cudaSuccess;
+    const int nb = cols / QK_K, nblk = rows / 256;
+    for (int c0 = 0; c0 < ncols; c0 += 4) {  // columns beyond 4 in groups of at most 4
+        const int nc = std::min(4, ncols - c0);
+        const uint8_t* im = (const uint8_t*)img + (size_t)c0 * nb * Q8K_IMG_BYTES;
+        float* hh = h_out + (size_t)c0 * rows;
+        uint8_t* io = img_out + (size_t)c0 * nblk * Q8K_IMG_BYTES;
+        cudaError_t e;
+        if (type == T_Q4_K_TILE) e = launch7_swiglu_type<T_Q4_K>(w_gate, w_up, rows, hh, nb, im, nc, io, blk_cnt, s, pdl);
+        else if (type == T_Q5_K_TILE) e = launch7_swiglu_type<T_Q5_K>(w_gate, w_up, rows, hh, nb, im, nc, io, blk_cnt, s, pdl);
+        else e = launch7_swiglu_type<T_Q6_K>(w_gate, w_up, rows, hh, nb, im, nc, io, blk_cnt, s, pdl);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 bool gemv7_supported(int type) { return type == T_Q4_K_TILE || type == T_Q5_K_TILE || type == T_Q6_K_TILE; }
 

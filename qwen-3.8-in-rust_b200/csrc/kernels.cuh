@@ -73,6 +73,11 @@ bool gemv7_supported(int type);
 void set_gemv7_config(int cfg);  // 0 = automatic by shape; 1..8 a fixed configuration (tests, sweeps)
 cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
                          int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
+// The MLP's gate and up tile matrices (rows x cols each, rows % 256 == 0) against the image columns, fused with
+// h = silu(gate) * up (written to h_out, [column][row]) and its quantisation into the Q8_K image img_out
+// ([column][rows / 256 blocks]); blk_cnt: rows / 256 zeroed counters, left zeroed.
+cudaError_t launch_gemv7_swiglu(int type, const uint8_t* w_gate, const uint8_t* w_up, int rows, int cols, const void* img,
+                                int ncols, float* h_out, uint8_t* img_out, unsigned* blk_cnt, cudaStream_t s, bool pdl);
 unsigned read_gemv7_error(bool clear);  // the error word of gemv7.cu's bounded waits (0 = none)
 int selftest_gemv7_timeout(unsigned long long wait_ns);  // failure-handling self-test of the stage wait (0 = as designed)
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.

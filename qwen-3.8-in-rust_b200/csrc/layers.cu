@@ -451,6 +451,35 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             }
         }
     }
+    if (!a.img_q8k && !a.img_q80) return;
+    // the out projection's input images of the t head rows (the quantise step of the layer, act.rs / q8k.rs)
+    const int n = a.n_v * dv, nw = blockDim.x / 32;
+    __threadfence();
+    __syncthreads();
+    if (a.img_q80) {  // this head's 32-value blocks, one warp each
+        for (int e = warp; e < a.t * (dv / 32); e += nw) {
+            const int r = e / (dv / 32), blk = p * (dv / 32) + e % (dv / 32);
+            uint8_t* row = a.img_q80 + (size_t)r * (n / 32) * Q80_IMG_BYTES;
+            q80_quantize_to_image(__ldcg(a.heads + (size_t)r * n + blk * 32 + lane), row + (size_t)blk * 32,
+                                  row + (size_t)(n / 32) * 32 + (size_t)blk * 8);
+        }
+    }
+    if (a.img_q8k) {
+        const int hpb = 256 / dv, blk = p / hpb;
+        __shared__ unsigned s_prev;
+        if (t == 0) s_prev = atomicAdd(&a.blk_cnt[blk], 1u);
+        __syncthreads();
+        if (s_prev == (unsigned)(hpb - 1)) {  // the block's last head: quantise its rows
+            __threadfence();
+            for (int r = warp; r < a.t; r += nw) {
+                const float4* hb = reinterpret_cast<const float4*>(a.heads + (size_t)r * n + (size_t)blk * 256 + lane * 8);
+                const float4 u0 = __ldcg(hb), u1 = __ldcg(hb + 1);
+                const float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                q8k_quantize_to_image(v, a.img_q8k + ((size_t)r * (n / 256) + blk) * Q8K_IMG_BYTES);
+            }
+            if (t == 0) a.blk_cnt[blk] = 0u;  // ready for the next call
+        }
+    }
 }
 
 // Per (row i, head): RMSNorm of q (heads 0..nh-1) or k (heads nh..nh+nkv-1) with the 8-lane order, then

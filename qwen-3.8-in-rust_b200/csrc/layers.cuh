@@ -27,6 +27,12 @@ struct DeltaArgs {
     const float* w_beta;
     const float* xn;
     int hid;
+    // optional: the head outputs quantised by this kernel for the out projection -- into the Q8_K image (a
+    // 256-value block spans 256 / dv heads: the block's last head to finish quantises it, blk_cnt holding one
+    // zeroed counter per block) and / or the Q8_0 image (32-value blocks inside each head)
+    uint8_t* img_q8k;
+    uint8_t* img_q80;
+    unsigned* blk_cnt;
 };
 
 struct QkArgs {
