@@ -727,7 +727,8 @@ cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, con
     if (cfg == 0) {  // by the rows of the launch (both matrices of a pair) and the column count, as measured
         const int rows = rows_a + (w_b ? rows_b : 0);
         if (rows >= 100000) cfg = NC == 1 ? 1 : 12;
-        else if (rows >= 16384) cfg = 11;
+        else if (rows >= 24576) cfg = 11;
+        else if (rows >= 16384) cfg = 5;
         else if (rows >= 8192) cfg = 3;
         else cfg = 13;
     }
