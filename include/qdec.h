@@ -102,7 +102,7 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
  *   impl 0 / 6: the kernel for ggml-layout Q4_K / Q5_K and split-layout Q6_K weights that reads the library's
  *     activation image (config 0 = automatic, 1..8 = lanes and rows per thread, depth, integer or FP32 scale
  *     multiply); impl 2: the kernel that reads block_q8_K activations in the reference layout instead;
- *   impl 7: the decode GEMV of K-quant tile matrices (config 0 = by shape, 1..14 = the streaming or windowed
+ *   impl 7: the decode GEMV of K-quant tile matrices (config 0 = by shape, 1..8 = the streaming or windowed
  *     kernel with a fixed number of warps, tiles per warp, super-block phases and stages in flight);
  *   impl 8: the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
  *     over 4 warps, 3 = the same with two tiles per CTA);

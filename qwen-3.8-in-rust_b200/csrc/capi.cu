@@ -254,8 +254,8 @@ int qdec_tune_gemv(int impl, int config) {
         set_gemm_tc_min_cols(config);
         return QDEC_OK;
     }
-    if (impl == 7) {  // the decode GEMV of tile matrices: 0 automatic by shape, 1..10 a fixed configuration
-        if (config < 0 || config > 14) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..14");
+    if (impl == 7) {  // the decode GEMV of tile matrices: 0 automatic by shape, 1..8 a fixed configuration
+        if (config < 0 || config > 8) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..8");
         set_gemv_impl(0);
         set_gemv7_config(config);
         return QDEC_OK;

@@ -726,27 +726,22 @@ cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, con
                         const void* img, cudaStream_t s, bool pdl) {
     if (cfg == 0) {  // by the rows of the launch (both matrices of a pair) and the column count, as measured
         const int rows = rows_a + (w_b ? rows_b : 0);
-        if (rows >= 100000) cfg = NC == 1 ? 1 : 12;
-        else if (rows >= 24576) cfg = 11;
-        else if (rows >= 16384) cfg = 5;
-        else if (rows >= 8192) cfg = 3;
-        else cfg = 13;
+        if (rows >= 100000) cfg = NC == 1 ? 1 : 5;
+        else if (rows >= 24576) cfg = 4;
+        else if (rows >= 16384) cfg = 3;
+        else if (rows >= 8192) cfg = rows / 80 <= num_sms() ? 6 : 2;  // 10-warp CTAs while they fit one wave
+        else cfg = 7;
     }
-    switch (cfg) {
+    switch (cfg) {  // streaming: <warps, tiles per warp, stages, super-blocks per stage>; windowed: <tile groups,
+                    // super-block phases, tiles per warp, windows, shifted image copy>
     case 1: return launch7s<TYPE, NC, 4, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 2: return launch7s<TYPE, NC, 4, 2, 3, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 3: return launch7s<TYPE, NC, 4, 1, 3, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 4: return launch7s<TYPE, NC, 4, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 5: return launch7s<TYPE, NC, 4, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 6: return launch7s<TYPE, NC, 2, 2, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 7: return launch7<TYPE, NC, 1, 4, 1, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 8: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 9: return launch7<TYPE, NC, 2, 4, 1, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 11: return launch7s<TYPE, NC, 5, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 12: return launch7s<TYPE, NC, 6, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 13: return launch7<TYPE, NC, 1, 4, 2, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 14: return launch7<TYPE, NC, 2, 4, 1, 3, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    default: return launch7<TYPE, NC, 1, 8, 1, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 2: return launch7s<TYPE, NC, 4, 1, 3, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3: return launch7s<TYPE, NC, 4, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4: return launch7s<TYPE, NC, 5, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 5: return launch7s<TYPE, NC, 6, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 6: return launch7s<TYPE, NC, 10, 1, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 7: return launch7<TYPE, NC, 1, 4, 2, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    default: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }
 
