@@ -147,6 +147,11 @@ int qdec_repack_tiles(int ggml_type, const void *src_dev, int rows, int cols, vo
 int qdec_matvec_noalloc(int ggml_type, const void *w_dev, int rows, int cols, const float *x_dev, int n_cols,
                         float *y_dev, void *stream);
 size_t qdec_matvec_noalloc_max_bytes(void);
+/* The scratch bytes qdec_matvec / qdec_matvec_noalloc need for n_cols columns of `cols` values against these
+ * weights (the path depends on the type and on w_dev's alignment, as listed above); (size_t)-1 for a type or
+ * width the kernels do not take.  A caller checks a noalloc call against qdec_matvec_noalloc_max_bytes() with
+ * it.  No device work. */
+size_t qdec_matvec_scratch_bytes(int ggml_type, const void *w_dev, int cols, int n_cols);
 
 /* out[i * cols + e] = dequantised element e of row ids[i] of `w_dev` (ids on the device, n_ids of them):
  * the embedding gather.  Replaces Model::embed_token_into (crates/core/src/model.rs:364-368) and

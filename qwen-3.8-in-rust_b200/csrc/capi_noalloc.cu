@@ -59,6 +59,11 @@ using namespace qdec;
 
 extern "C" size_t qdec_matvec_noalloc_max_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
 
+extern "C" size_t qdec_matvec_scratch_bytes(int ggml_type, const void *w_dev, int cols, int n_cols) {
+    if (!supported_type(ggml_type) || cols <= 0 || n_cols < 0 || cols % block_elems(ggml_type)) return (size_t)-1;
+    return matvec_scratch_bytes(ggml_type, w_dev, cols, n_cols);
+}
+
 extern "C" int qdec_matvec_noalloc(int ggml_type, const void* w_dev, int rows, int cols, const float* x_dev, int n_cols,
                                    float* y_dev, void* stream) {
     int rc = check_gemv_shape(ggml_type, rows, cols, n_cols);

@@ -77,6 +77,8 @@ def lib():
         L.qdec_act_row_bytes.argtypes = [I, I]
         L.qdec_matvec_noalloc_max_bytes.restype = S
         L.qdec_matvec_noalloc_max_bytes.argtypes = []
+        L.qdec_matvec_scratch_bytes.restype = S
+        L.qdec_matvec_scratch_bytes.argtypes = [I, P, I, I]
         PP = ctypes.POINTER(ctypes.c_void_p)
         U32P = ctypes.POINTER(ctypes.c_uint32)
         for name, args in {
@@ -164,6 +166,13 @@ def matvec_noalloc(t, w_ptr, rows, cols, x_ptr, ncols, y_ptr, stream=0):
 
 def matvec_noalloc_max_bytes():
     return lib().qdec_matvec_noalloc_max_bytes()
+
+
+def matvec_scratch_bytes(t, w_ptr, cols, ncols):
+    """Scratch bytes a matvec of ncols columns needs on these weights (qdec_matvec_scratch_bytes); None if the type
+    or width is not taken."""
+    v = lib().qdec_matvec_scratch_bytes(t, w_ptr, cols, ncols)
+    return None if v == (1 << 64) - 1 else v
 
 
 def image_row_bytes(t, cols):

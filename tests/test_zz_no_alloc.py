@@ -35,6 +35,17 @@ def test_oversize_request_is_rejected_before_any_device_work(t, w_ptr, per_value
         qdec.matvec_noalloc(t, w_ptr, 16, cols, 1, n, 1)
     assert e.value.code == qdec.EINVAL and "scratch" in str(e.value)
     assert f"need {n * per_col} bytes" in str(e.value)
+    # the query gives the same sizes (no device work), so a caller can check before calling
+    assert qdec.matvec_scratch_bytes(t, w_ptr, cols, n) == n * per_col
+    assert qdec.matvec_scratch_bytes(t, w_ptr, cols, n - 1) <= cap
+
+
+def test_scratch_query_rejects_what_the_kernels_do_not_take():
+    import qdec
+
+    assert qdec.matvec_scratch_bytes(12, 256, 100, 1) is None  # not a multiple of 256
+    assert qdec.matvec_scratch_bytes(7, 256, 256, 1) is None   # not a kernel type
+    assert qdec.matvec_scratch_bytes(0, 256, 256, 4) == 0       # F32 takes the columns as they are
 
 
 def _cuda():
