@@ -533,33 +533,28 @@ __global__ void qk_norm_rope_kernel(const QkArgs a) {
 constexpr int ATT_KCH = 32;      // dims staged per pass
 constexpr int ATT_SGRID = 32;    // CTAs per (kv head, pair group) over the positions
 // ATT_PAIRS: (query head, row) pairs per CTA -- 8 for long caches (a key is read once per 8 pairs), 2 for short
-// ones (4x the CTAs, so a short context still spreads over the SMs)
-template <int ATT_PAIRS>
-__global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a, int rows) {
-    __shared__ __align__(16) float kt[8][32][ATT_KCH + 4];
+// ones (4x the CTAs, so a short context still spreads over the SMs).  NW warps, 32 positions each, per chunk of
+// the cache.  (Every pair of a kv head in one 4-warp CTA, so each key is read once, measured slower at 8K
+// positions: 66 against 39 us per call, for want of warps.)
+template <int ATT_PAIRS, int NW>
+__global__ void __launch_bounds__(32 * NW) attn_scores_kernel(const AttnArgs a, int rows) {
+    __shared__ __align__(16) float kt[NW][32][ATT_KCH + 4];
     __shared__ __align__(16) float qs[ATT_PAIRS][256];
     const int hd = a.head_dim, group = a.n_head / a.n_kv, npairs = group * rows;
     const int kvh = blockIdx.y, pg = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *a.pos;
     const int np = min(ATT_PAIRS, npairs - pg * ATT_PAIRS);
-    int hh[ATT_PAIRS], ii[ATT_PAIRS];
-#pragma unroll
-    for (int j = 0; j < ATT_PAIRS; j++) {
-        const int pi = pg * ATT_PAIRS + min(j, np - 1);
-        hh[j] = kvh * group + pi % group;
-        ii[j] = pi / group;
-    }
     for (int e = threadIdx.x; e < np * hd; e += blockDim.x) {
         const int j = e / hd, d = e % hd;
         const int pi = pg * ATT_PAIRS + j, h = kvh * group + pi % group, i = pi / group;
         qs[j][d] = a.q[(size_t)i * a.n_head * hd + (size_t)h * hd + d];
     }
     __syncthreads();
-    const int len = pos + ii[np - 1] + 1;  // the longest row of the group (rows ascend with the pair index)
+    const int len = pos + (pg * ATT_PAIRS + np - 1) / group + 1;  // the group's longest row (rows ascend with the pair)
     const size_t rstride = (size_t)a.n_kv * hd;
-    for (int c = blockIdx.x; c * 256 < len; c += gridDim.x) {
-        const int p0 = c * 256 + warp * 32;
+    for (int c = blockIdx.x; c * (32 * NW) < len; c += gridDim.x) {
+        const int p0 = c * (32 * NW) + warp * 32;
         if (p0 >= len) continue;  // warp-uniform
         float acc[ATT_PAIRS];
 #pragma unroll
@@ -591,19 +586,25 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a, int 
         }
         const int t = p0 + lane;
 #pragma unroll
-        for (int j = 0; j < ATT_PAIRS; j++)
-            if (j < np && t < pos + ii[j] + 1)
-                a.scores[((size_t)ii[j] * a.n_head + hh[j]) * ((a.max_len + 3) & ~3) + t] = __fmul_rn(acc[j], a.scaling);
+        for (int j = 0; j < ATT_PAIRS; j++) {
+            const int pi = pg * ATT_PAIRS + j, i = pi / group, h = kvh * group + pi % group;
+            if (j < np && t < pos + i + 1)
+                a.scores[((size_t)i * a.n_head + h) * ((a.max_len + 3) & ~3) + t] = __fmul_rn(acc[j], a.scaling);
+        }
     }
 }
 
 // Softmax of each (head, row) score row in place (softmax.rs:22-50): m = max, e = exp(x - m), the 8-lane sum
-// (lane l adds e[l], e[l+8], ... left to right; reduce8; the tail), p = e / sum.  One CTA of 256 per row.
-__global__ void __launch_bounds__(256) attn_softmax_kernel(const AttnArgs a) {
+// (lane l adds e[l], e[l+8], ... left to right; reduce8; the tail), p = e / sum.  One CTA of 256 per row.  The
+// exps are kept in shared memory (`es`, when the launch gave it room for the row), so the 8 serial chains read
+// them at shared-memory latency rather than from L2.
+__global__ void __launch_bounds__(256) attn_softmax_kernel(const AttnArgs a, int staged) {
+    extern __shared__ __align__(16) float es_dyn[];
     __shared__ float red[16];
     const int h = blockIdx.x, i = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     const int len = *a.pos + i + 1;
     float* p = a.scores + ((size_t)i * a.n_head + h) * ((a.max_len + 3) & ~3);
+    float* e = staged ? es_dyn : p;
     float m = -INFINITY;
     for (int t = tid; t < len; t += 256) m = fmaxf(m, p[t]);
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -616,30 +617,31 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const AttnArgs a) {
     }
     __syncthreads();
     m = red[15];
-    for (int t = tid; t < len; t += 256) p[t] = exp_f32(__fsub_rn(p[t], m));
-    __syncthreads();  // global writes of this CTA are visible to its own threads after the barrier
+    for (int t = tid; t < len; t += 256) e[t] = exp_f32(__fsub_rn(p[t], m));
+    __syncthreads();  // this CTA's writes are visible to its own threads after the barrier
     const int n8 = len / 8 * 8;
     if (tid < 8) {
         float acc = 0.0f;
-        for (int t = tid; t < n8; t += 8) acc = __fadd_rn(acc, p[t]);
+        for (int t = tid; t < n8; t += 8) acc = __fadd_rn(acc, e[t]);
         red[tid] = acc;
     }
     __syncthreads();
     if (tid == 0) {
         float sum = reduce8(red);
-        for (int t = n8; t < len; t++) sum = __fadd_rn(sum, p[t]);
+        for (int t = n8; t < len; t++) sum = __fadd_rn(sum, e[t]);
         red[8] = sum;
     }
     __syncthreads();
     const float ssum = red[8];
-    for (int t = tid; t < len; t += 256) p[t] = __fdiv_rn(p[t], ssum);
+    for (int t = tid; t < len; t += 256) p[t] = __fdiv_rn(e[t], ssum);
 }
 
-// The value sum: one CTA per (32 output dims, kv head, group of 4 (query head, row) pairs reading that kv head),
-// warp j = pair j, lane = output dim: out[d] = sum_t p[t] * v_t[d] left to right over t, times sigmoid(gate)
-// (gqa_attention.rs:376-409).  The value rows (32 dims) and the pairs' probabilities stream through a 4-stage
-// ring of cp.async copies, 64 positions per stage, so a value row is read once for the 4 pairs.
-constexpr int ATT_VT = 64, ATT_VS = 4, ATT_VP = 4;
+// The value sum: one CTA per (32 output dims, kv head, group of ATT_VP (query head, row) pairs reading that kv
+// head), warp j = pair j, lane = output dim: out[d] = sum_t p[t] * v_t[d] left to right over t, times
+// sigmoid(gate) (gqa_attention.rs:376-409).  The value rows (32 dims) and the pairs' probabilities stream through
+// a 4-stage ring of cp.async copies, 64 positions per stage, so a value row is read once for the group's 4 pairs
+// (12 pairs per CTA measured slower at 8K positions: 110 against 95 us per call).
+constexpr int ATT_VT = 64, ATT_VS = 4;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
@@ -647,6 +649,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_stages() { asm volatile("cp.async.wait_group %0;" ::"n"(ATT_VS - 2) : "memory"); }
 
+template <int ATT_VP>
 __global__ void __launch_bounds__(32 * ATT_VP) attn_pv_kernel(const AttnArgs a, int rows) {
     __shared__ __align__(16) float vs[ATT_VS][ATT_VT][32];
     __shared__ __align__(16) float ps[ATT_VS][ATT_VP][ATT_VT];
@@ -852,16 +855,29 @@ cudaError_t launch_qk_norm_rope(const QkArgs& a, int t, cudaStream_t s) {
 cudaError_t launch_attention(const AttnArgs& a, int t, cudaStream_t s) {
     if (!a.scores || !attention_dims_supported(a.head_dim)) return cudaErrorInvalidValue;
     const int group = a.n_head / a.n_kv, npairs = group * t;
-    const int pairs = a.max_len > 2048 ? 8 : 2;
-    const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + pairs - 1) / pairs);
-    if (pairs == 8) attn_scores_kernel<8><<<sgrid, 256, 0, s>>>(a, t);
-    else attn_scores_kernel<2><<<sgrid, 256, 0, s>>>(a, t);
+    const bool lng = a.max_len > 2048;  // a long cache: read every key and value row once per call
+    if (lng) {
+        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + 7) / 8);
+        attn_scores_kernel<8, 8><<<sgrid, 256, 0, s>>>(a, t);
+    } else {
+        const dim3 sgrid(std::min((a.max_len + 255) / 256, ATT_SGRID), a.n_kv, (npairs + 1) / 2);
+        attn_scores_kernel<2, 8><<<sgrid, 256, 0, s>>>(a, t);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attn_softmax_kernel<<<dim3(a.n_head, t), 256, 0, s>>>(a);
+    // the exps of a score row in shared memory when it fits (up to 48K positions)
+    const size_t row_bytes = (size_t)((a.max_len + 3) & ~3) * sizeof(float);
+    const bool staged = row_bytes <= 192 * 1024;
+    static size_t sm_attr = 48 * 1024;  // raised once, before any graph capture reaches a longer cache
+    if (staged && row_bytes > sm_attr) {
+        e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_bytes);
+        if (e != cudaSuccess) return e;
+        sm_attr = row_bytes;
+    }
+    attn_softmax_kernel<<<dim3(a.n_head, t), 256, staged ? row_bytes : 0, s>>>(a, staged ? 1 : 0);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attn_pv_kernel<<<dim3(a.head_dim / 32, a.n_kv, (npairs + ATT_VP - 1) / ATT_VP), 32 * ATT_VP, 0, s>>>(a, t);
+    attn_pv_kernel<4><<<dim3(a.head_dim / 32, a.n_kv, (npairs + 3) / 4), 32 * 4, 0, s>>>(a, t);
     return cudaGetLastError();
 }
 

@@ -147,12 +147,14 @@ def test_forced_drafts_every_acceptance_count(model, omodel):
     assert want[: len(seq)] == seq
 
 
-def test_long_context_ids_and_logits_match_oracle(tiny, omodel):
+@pytest.mark.parametrize("max_pos", [1024, 4096])
+def test_long_context_ids_and_logits_match_oracle(tiny, omodel, max_pos):
     """A 700-token prompt: the attention runs over several 256-position score chunks and wraps the value
-    stream's stage ring; greedy ids, the last prompt row's logits and --spec 3 ids match the oracle."""
+    stream's stage ring; greedy ids, the last prompt row's logits and --spec 3 ids match the oracle.  With caches
+    longer than 2048 positions the attention takes its long-cache form (8 pairs per scores CTA)."""
     import qdec
 
-    m = qdec.Model(tiny, max_pos=1024)
+    m = qdec.Model(tiny, max_pos=max_pos)
     p = [int(v) for v in np.random.default_rng(SEED + 7).integers(0, 4096, 700)]
     want = omodel.state(1024).generate(p, 12, stop=False)
     st = m.new_state(max_rows=32)
