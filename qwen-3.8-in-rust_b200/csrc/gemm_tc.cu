@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tcgen05.cuh"
 
 namespace qdec {
 
@@ -54,7 +55,6 @@ constexpr int TC_B_BUF = 8 * TC_B_STEP;
 constexpr int TC_META = 20;  // floats per column and super-block: dx, 3 unused, then q8s[8] (Q4_K/Q5_K) or 2*bsums[16] (Q6_K)
 constexpr int TC_STAGES = 4;                       // raw super-blocks in flight (TMA tensor copies)
 constexpr int TC_IMG_STAGE = TC_N * Q8K_IMG_BYTES;  // the image blocks of one super-block's 16 columns
-constexpr unsigned long long TC_WAIT_NS = 1000000000ull;
 constexpr unsigned TC_ERR_WAIT = 0x7c01;
 
 template <int TYPE>
@@ -87,21 +87,6 @@ struct TcArgs {
     int ncols;
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ unsigned long long tc_clock_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// shared-memory matrix descriptor: canonical K-major layout without swizzle (8-row x 16-byte core matrices;
-// lbo = byte distance of the two core matrices along K, sbo = of consecutive 8-row groups), sm100 version bit
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
-}
-
 // instruction descriptor of kind::f16: f16 A and B (K-major), f32 D, M = 128, N = TC_N
 constexpr uint32_t TC_IDESC = (1u << 4) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 
@@ -111,9 +96,6 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t da, uint64_t db
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(da), "l"(db), "r"(TC_IDESC), "r"(accumulate));
 }
-
-__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // four packed bytes b0..b3 (each < 1024) as f16 pairs {1024 + b0, 1024 + b1}, {1024 + b2, 1024 + b3}
 __device__ __forceinline__ uint32_t f16_lo(uint32_t v) { return __byte_perm(v, 0x64646464u, 0x5140); }
@@ -147,13 +129,6 @@ __device__ __forceinline__ uint2 scaled4_signed(uint32_t q, __half2 sc) {
     const __half2 k = bits_h2(H2_1024);
     return make_uint2(h2_bits(__hmul2(__hsub2(bits_h2(f16_lo(q)), k), sc)),
                       h2_bits(__hmul2(__hsub2(bits_h2(f16_hi(q)), k), sc)));
-}
-
-// f32 of an unsigned byte / signed byte held in the low 8 bits (exact, no conversion unit)
-__device__ __forceinline__ float u8f(uint32_t b) { return __fsub_rn(__uint_as_float(0x4B000000u | b), 8388608.0f); }
-__device__ __forceinline__ float s8f(uint32_t b) { return __fsub_rn(__uint_as_float(0x4B000000u | ((b ^ 0x80u) & 0xFFu)), 8388736.0f); }
-__device__ __forceinline__ float s16f(uint32_t h) {
-    return __fsub_rn(__uint_as_float(0x4B000000u | ((h ^ 0x8000u) & 0xFFFFu)), 8421376.0f);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint8_t* p, uint2 a, uint2 b) {
@@ -221,26 +196,6 @@ __device__ __forceinline__ void dequant_item(const uint8_t* tile, int r, int tg,
             st_shared_v4(step, scaled4_signed(v[0], sc[0]), scaled4_signed(v[1], sc[1]));
             st_shared_v4(step + 2048, scaled4_signed(v[2], sc[2]), scaled4_signed(v[3], sc[3]));
         }
-    }
-}
-
-__device__ __forceinline__ void mbar_init1(uint64_t* bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(1u));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-// bounded wait for the completion of the phase with `parity`; false after about a second
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const unsigned long long t0 = tc_clock_ns();
-    for (uint32_t it = 0;; it++) {
-        uint32_t done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                     : "=r"(done)
-                     : "r"(smem_addr(bar)), "r"(parity)
-                     : "memory");
-        if (done) return true;
-        if ((it & 255) == 255 && tc_clock_ns() - t0 > TC_WAIT_NS) return false;
     }
 }
 
@@ -349,12 +304,6 @@ __device__ __forceinline__ void tmem_ld2(uint32_t addr, float& v0, float& v1) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
     v0 = __uint_as_float(r0), v1 = __uint_as_float(r1);
 }
-
-// f32 pairs: two of the reference's independent chains side by side, each step the scalar IEEE
-// round-to-nearest operation.
-__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
 
 // The epilogue's per-row values of a super-block (from the row's tile block in the raw stage): the f16 scales
 // as f32 and the Q4_K/Q5_K mins or the Q6_K chunk scales.
@@ -539,8 +488,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) kq_gemm_tc_kernel(const __grid_
                 for (int l = 0; l < 8; l++)
                     tc_mma(dbase + (uint32_t)(l * TC_N), smem_desc(abase + l * TC_A_PITCH, 2048, 128),
                            smem_desc(bbase + l * TC_B_STEP, TC_N * 16, 128), accumulate);
-                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(mma_bar))
-                             : "memory");
+                tc_commit(mma_bar);
                 committed = gs + 1;
             }
             __syncwarp();
@@ -602,30 +550,6 @@ int g_tc_min_cols = [] {
     const char* e = getenv("QDEC_GEMM_TC_MIN_COLS");
     return e ? atoi(e) : 8;
 }();
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
-// 2-D map of `outer` rows of `row_bytes` (u64 elements), box = 16 rows x `box_bytes`
-bool encode_rows(CUtensorMap* m, const void* base, size_t row_bytes, int outer, int box_bytes) {
-    auto enc = tensor_map_encoder();
-    if (!enc) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)outer};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 8), 16u};
-    const cuuint32_t estr[2] = {1u, 1u};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 template <int TYPE>
 cudaError_t launch_tc(TcArgs& a, int tiles, cudaStream_t s, bool pdl) {
