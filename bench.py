@@ -5,7 +5,8 @@ Default workload (`--workload spec`): `--spec 3` decoding of the 27B architectur
 the reference's type recipe), after a 128-token prompt prefilled as one batch.  One step = one speculative round
 (k = 3 MTP drafts, one verify pass over 4 rows, rollback, the MTP re-feed) replayed as one CUDA graph.  Metric:
 accepted tokens / second, whole job over all ranks (replicas, or one tensor-parallel model with --gpus N).  The
-JSON line also carries the plain-decode rate, the prefill rate, the K-quant GEMV table of the config-2 shapes
+JSON line also carries the plain-decode rate, the multi-sequence batched decode rate (2, 4 and 8 sequences per
+step through qdec_batch_step), the prefill rate, the K-quant GEMV table of the config-2 shapes
 (Q4_K / Q5_K / Q6_K / Q8_0 / Q4_0 at N = 1, 2, 4), an 8K-position KV run, the roofline of the dominant GEMV,
 parity against the CPU oracle and the CPU baseline (the AVX2 C restatement of the reference's decode on all host
 cores, on the same 128-token prompt).
@@ -488,7 +489,7 @@ def spec_prompt(vocab, seed):
 def dominant_gemv_timing(dev, launches=200, n=4):
     """The verify's dominant kernel timed alone on the launching stream with CUDA events: the fused Q4_K GEMV of
     ffn_gate and ffn_up (two 17408 x 5120 tile matrices against the same N = 4 image columns, one launch, as the
-    layer runs it), weight pairs rotating over 3 sets (300 MB > L2).  With n >= 8 columns the same call runs the
+    layer runs it), weight pairs rotating over 3 sets (300 MB > L2).  With n >= 16 columns the same call runs the
     prefill's tensor-core GEMM."""
     import torch
 
@@ -627,6 +628,35 @@ def plain_decode_timing(model, prompt, steps):
     s_tok = ms / 1e3 / steps
     return {"tokens": steps, "tok_s": round(1.0 / s_tok, 2), "s_per_token": round(s_tok, 6),
             "weight_gb_s": round(model.info.decode_bytes / s_tok / 1e9, 1)}
+
+
+def batch_decode_timing(model, prompt, steps, sizes=(2, 4, 8)):
+    """Multi-sequence batching (qdec_batch_step): B sequences decoded together, one greedy token each per step,
+    every weight read once per step for the B rows; aggregate tokens/s from CUDA events on the batch's stream
+    (the first state's).  Each sequence starts from its own prompt (the headline prompt rotated)."""
+    import torch
+
+    import qdec
+
+    res = {}
+    for b in sizes:
+        sts = [model.new_state(spec_k=0, max_rows=max(b, 4)) for _ in range(b)]
+        xs = [st.prefill(prompt[i:] + prompt[:i]) for i, st in enumerate(sts)]
+        stream = torch.cuda.ExternalStream(sts[0].stream)
+        for _ in range(3):
+            xs = qdec.batch_step(sts, xs)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            xs = qdec.batch_step(sts, xs)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        s_step = e0.elapsed_time(e1) / 1e3 / steps
+        for st in sts:
+            st.free()
+        res[str(b)] = {"tok_s": round(b / s_step, 2), "s_per_step": round(s_step, 6)}
+    return {"sequences": res, "api": "qdec_batch_step (greedy, one token per sequence per step)"}
 
 
 def long_kv_timing(path, dev_index, k, rounds, prompt_len=8064):
@@ -854,6 +884,7 @@ def run_spec_qdec(args, world, rank, local):
     ss.free()
     pre = prefill_timing(model, info, max_pos, SPEC_SEED + 7)
     plain_res = plain_decode_timing(model, prompt, min(args.steps, 64)) if not args.quick else None
+    batch_res = batch_decode_timing(model, prompt, min(args.steps, 32)) if not args.quick and world == 1 else None
     if world > 1:
         import torch.distributed as dist
 
@@ -913,6 +944,8 @@ def run_spec_qdec(args, world, rank, local):
     }
     if plain_res is not None:
         line["plain_decode"] = plain_res
+    if batch_res is not None:
+        line["batch_decode"] = batch_res
     if not args.quick:
         line["gemv"] = gemv_table(torch.device("cuda", local))
         line["long_kv"] = long_kv_timing(path, local, k, min(args.steps, 20))

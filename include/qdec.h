@@ -107,7 +107,7 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
  *   impl 8: the Q8_0 / Q4_0 tile kernel (config 0 = automatic, 1 = one warp per tile, 2 = the group range split
  *     over 4 warps, 3 = the same with two tiles per CTA);
  *   impl 9: the tensor-core prefill GEMM that K-quant tile matrices take for many columns (config = the smallest
- *     column count routed there, 8 by default, 0 = never; the 1..4 verify columns stay on the GEMV at any value
+ *     column count routed there, 16 by default, 0 = never; the 1..4 verify columns stay on the GEMV at any value
  *     >= 5).
  * No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
@@ -229,6 +229,16 @@ int qdec_prefill(qdec_state *s, const uint32_t *ids, int n, uint32_t *first_out)
 /* One token in, the greedy next token out; logits (vocab floats) copied to `logits_out` when non-null
  * (Model::forward_token, crates/core/src/model.rs:486). */
 int qdec_step(qdec_state *s, uint32_t id, uint32_t *next_out, float *logits_out);
+/* Multi-sequence batching on one GPU: one greedy step of each of `n` sequences in a single forward.  ids[i] is
+ * fed to states[i] and next_out[i] receives its next token, exactly what qdec_step(states[i], ids[i], ..)
+ * returns (each column of a batched matrix product is the single-row product bit for bit, the reference's
+ * blocked matmul_t semantics, crates/core/src/kernels/matvec.rs:401-539).  Every weight matrix is read once
+ * for the n rows; each row keeps its own state's conv window, DeltaNet state, KV cache and position.  The
+ * states belong to one model on one GPU (no tensor parallelism), are greedy (no sampler), appear once each,
+ * and states[0] was made with max_rows >= n (its row buffers carry the batch).  The reference decodes one
+ * sequence at a time; this is an extension of qdec_step, with its error behaviour (QDEC_EINVAL on a bad
+ * argument or a sequence at its max_pos, nothing advanced). */
+int qdec_batch_step(qdec_state *const *states, int n, const uint32_t *ids, uint32_t *next_out);
 /* Speculative prefill: prefill, x_T, the MTP over the prompt rows and the first k drafts; *x_out = x_T
  * (Model::spec_prefill, crates/core/src/spec.rs:229). */
 int qdec_spec_prefill(qdec_state *s, const uint32_t *ids, int n, uint32_t *x_out);

@@ -2,6 +2,7 @@
 // the engine, with every C++ exception turned into a status code and a message.
 #include <cstring>
 #include <memory>
+#include <vector>
 #include <new>
 #include <stdexcept>
 
@@ -212,6 +213,19 @@ int qdec_step(qdec_state* s, uint32_t id, uint32_t* next_out, float* logits_out)
     if (!s || !next_out) return qdec::fail(QDEC_EINVAL, "qdec_step: bad argument");
     return guard("qdec_step", [&] {
         *next_out = s->s->step(id, logits_out);
+        return QDEC_OK;
+    });
+}
+
+int qdec_batch_step(qdec_state* const* states, int n, const uint32_t* ids, uint32_t* next_out) {
+    if (!states || n <= 0 || !ids || !next_out) return qdec::fail(QDEC_EINVAL, "qdec_batch_step: bad argument");
+    std::vector<qdec::State*> ms((size_t)n);
+    for (int i = 0; i < n; i++) {
+        if (!states[i]) return qdec::fail(QDEC_EINVAL, "qdec_batch_step: state %d is null", i);
+        ms[(size_t)i] = states[i]->s.get();
+    }
+    return guard("qdec_batch_step", [&] {
+        qdec::State::batch_step(ms, ids, next_out);
         return QDEC_OK;
     });
 }

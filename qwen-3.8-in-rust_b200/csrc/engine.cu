@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <initializer_list>
 #include <cmath>
@@ -480,6 +481,8 @@ void* State::dalloc(size_t bytes) {
 }
 
 State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(spec_k), max_pos_(max_pos) {
+    static std::atomic<uint64_t> serials{0};
+    serial_ = ++serials;
     const ModelConfig& c = m.cfg;
     if (max_pos > m.max_pos) throw std::invalid_argument("max_pos exceeds the model's RoPE table");
     if (spec_k < 0 || 2 * spec_k + 2 > ROPE_SLACK) throw std::invalid_argument("spec_k out of range");
@@ -599,6 +602,8 @@ State::~State() {
     for (int k = 0; k < m_.tp.world; k++)
         if (k != m_.tp.rank && xpeer_[k]) cudaIpcCloseMemHandle(xpeer_[k]);
     if (round_exec_) cudaGraphExecDestroy(round_exec_);
+    if (step_exec_) cudaGraphExecDestroy(step_exec_);
+    if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
     if (h_io_) cudaFreeHost(h_io_);
     for (void* p : allocs_) cudaFree(p);
     for (float* p : capture_h_) cudaFree(p);
@@ -783,13 +788,22 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         gemv(L.q, normed_, t, qg_);
         gemv(L.k, normed_, t, kk_);
         gemv(L.v, normed_, t, vv_);
-        QkArgs qa{qg_, kk_, vv_, L.q_norm, L.k_norm, m_.rope_cos, m_.rope_sin, pos_dev, qr_, gate_, kv->k, kv->v,
-                  P.nq, P.nkv, hd, (int)c.rope_dim, eps};
-        count_launch(); ck(launch_qk_norm_rope(qa, t, stream), "qk_norm_rope");
-        AttnArgs aa{qr_, gate_, kv->k, kv->v, pos_dev, attn_, P.nq, P.nkv, hd,
-                    kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
-                    m_.attn_scaling, att_scores_};
-        count_launch(); ck(launch_attention(aa, t, stream), "attention");
+        // the rows' own positions and KV caches: all t rows this state's, or (batch_step) row i member i's
+        const size_t nqh = (size_t)P.nq * hd;  // floats per row of q, gate and the attention output
+        for (int i = 0; i < (batch_ ? t : 1); i++) {
+            State* o = batch_ ? (*batch_)[i] : this;
+            const int r0 = batch_ ? i : 0, tn = batch_ ? 1 : t;
+            KvState* kvo = batch_ ? &o->kv_[li] : kv;
+            const int* po = batch_ ? o->d_pos : pos_dev;
+            QkArgs qa{qg_ + (size_t)r0 * L.q.rows, kk_ + (size_t)r0 * L.k.rows, vv_ + (size_t)r0 * L.v.rows, L.q_norm, L.k_norm,
+                      m_.rope_cos, m_.rope_sin, po, qr_ + r0 * nqh, gate_ + r0 * nqh, kvo->k, kvo->v, P.nq, P.nkv, hd,
+                      (int)c.rope_dim, eps};
+            count_launch(); ck(launch_qk_norm_rope(qa, tn, stream), "qk_norm_rope");
+            AttnArgs aa{qr_ + r0 * nqh, gate_ + r0 * nqh, kvo->k, kvo->v, po, attn_ + r0 * nqh, P.nq, P.nkv, hd,
+                        batch_ ? o->max_pos_ : kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
+                        m_.attn_scaling, batch_ ? o->att_scores_ : att_scores_};
+            count_launch(); ck(launch_attention(aa, tn, stream), "attention");
+        }
         const float* attn_full = attn_;
         if (tp()) {
             const int seg[1][3] = {{0, P.qh_lo * hd * 4, P.nq * hd * 4}};
@@ -799,7 +813,6 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
         quant_for(L.o.type, attn_full, L.o.cols, t);
         gemv(L.o, attn_full, t, mix_out_);
     } else {
-        const DnState& d = dn_[li];
         const bool k8 = needs_q8k({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
         const bool k0 = needs_q80({L.qkv.type, L.gate_z.type, L.alpha.type, L.beta.type});
         resid_norm(li == 0 ? nullptr : mlp_in(), L.attn_norm, t, normed_, k8, k0);
@@ -821,19 +834,29 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
             gemv(L.beta, normed_, t, beta_);
         }
         const int channels = L.qkv.rows;  // this rank's q, k and v channels
-        count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, channels, qkv_, t, conved_, d.pend_x,
-                            commit_dn ? d_keep : nullptr, T_, stream), "conv");
-        const int dk = (int)c.dn_head_dim_k, dv = (int)c.dn_head_dim_v;
+        const int dk = (int)c.dn_head_dim_k, dv = (int)c.dn_head_dim_v, nvdv = P.nv * dv;
         // one GPU: the kernel also quantises its head outputs for ssm_out (over TP ranks the f32 heads are
         // exchanged first and the full rows quantised after)
         const int ot = L.ssm_out.type;
-        const bool q_fused = !tp() && (is_kquant(ot) || is_q80(ot)) && 256 % dv == 0 && (P.nv * dv) % 256 == 0;
-        DeltaArgs da{d.S, conved_, alpha_, beta_, z_, L.ssm_a, L.dt_bias, L.ssm_norm, heads_, d.pend_decay, d.pend_k, d.pend_delta,
-                     commit_dn ? d_keep : nullptr, t, T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps,
-                     ab_fused ? (const float*)L.alpha.p : nullptr, ab_fused ? (const float*)L.beta.p : nullptr,
-                     ab_fused ? normed_ : nullptr, H,
-                     q_fused && is_kquant(ot) ? q8k_ : nullptr, q_fused && is_q80(ot) ? q80_ : nullptr, dn_cnt_};
-        count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
+        const bool q_fused = !tp() && (is_kquant(ot) || is_q80(ot)) && 256 % dv == 0 && nvdv % 256 == 0;
+        // the rows' own conv windows and recurrent states: all t rows this state's, or (batch_step) row i
+        // member i's
+        for (int i = 0; i < (batch_ ? t : 1); i++) {
+            const State* o = batch_ ? (*batch_)[i] : this;
+            const int r0 = batch_ ? i : 0, tn = batch_ ? 1 : t;
+            const DnState& d = o->dn_[li];
+            const int* keep = commit_dn ? o->d_keep : nullptr;
+            count_launch(); ck(launch_conv_step(d.conv, L.conv_w, (int)c.dn_conv_kernel, channels, qkv_ + (size_t)r0 * channels, tn,
+                                conved_ + (size_t)r0 * channels, d.pend_x, keep, o->T_, stream), "conv");
+            DeltaArgs da{d.S, conved_ + (size_t)r0 * channels, alpha_ + (size_t)r0 * P.nv, beta_ + (size_t)r0 * P.nv,
+                         z_ + (size_t)r0 * L.gate_z.rows, L.ssm_a, L.dt_bias, L.ssm_norm, heads_ + (size_t)r0 * nvdv,
+                         d.pend_decay, d.pend_k, d.pend_delta, keep, tn, o->T_, P.nk, P.nv, dk, dv, P.nk * dk, channels, eps,
+                         ab_fused ? (const float*)L.alpha.p : nullptr, ab_fused ? (const float*)L.beta.p : nullptr,
+                         ab_fused ? normed_ + (size_t)r0 * H : nullptr, H,
+                         q_fused && is_kquant(ot) ? q8k_ + (size_t)r0 * (nvdv / 256) * Q8K_IMG_BYTES : nullptr,
+                         q_fused && is_q80(ot) ? q80_ + (size_t)r0 * (nvdv / 32) * Q80_IMG_BYTES : nullptr, dn_cnt_};
+            count_launch(); ck(launch_deltanet_heads(da, stream), "deltanet");
+        }
         const float* heads_full = heads_;
         if (tp()) {
             // local V heads g * nk + j are global heads g * n_k + kh_lo + j
@@ -959,11 +982,39 @@ uint32_t State::prefill(const uint32_t* ids, int n) {
     return (uint32_t)a;
 }
 
+// The kernels `enqueue` puts on the stream, captured into *exec on first use and replayed after (their launch
+// count is added on every replay).
+void State::graph_run(cudaGraphExec_t* exec, uint64_t* n_launches, const std::function<void()>& enqueue) {
+    if (!*exec) {
+        const uint64_t before = launches_;
+        cudaGraph_t g = nullptr;
+        ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "capture");
+        try {
+            enqueue();
+        } catch (...) {
+            cudaStreamEndCapture(stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        ck(cudaStreamEndCapture(stream, &g), "capture");
+        cudaError_t e = cudaGraphInstantiate(exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) *exec = nullptr;
+        ck(e, "graph");
+        *n_launches = launches_ - before;
+        launches_ = before;
+    }
+    ck(cudaGraphLaunch(*exec, stream), "graph launch");
+    launches_ += *n_launches;
+}
+
 uint32_t State::step(uint32_t id, float* logits) {
     if (pos_ + 1 > max_pos_) throw std::invalid_argument("step: the sequence would exceed max_pos");
     upload_ids(&id, 1);
     set_dev_int(d_pos, pos_, stream);
-    forward_rows(1, d_ids, true);
+    // one GPU: the step's kernels as one graph (debugging captures allocate per layer and run eagerly)
+    if (capture_ || tp()) forward_rows(1, d_ids, true);
+    else graph_run(&step_exec_, &step_launches_, [&] { forward_rows(1, d_ids, true); });
     set_dev_int(d_keep, 1, stream);
     pos_ += 1;
     set_dev_int(d_pos, pos_, stream);
@@ -974,6 +1025,51 @@ uint32_t State::step(uint32_t id, float* logits) {
     if (logits) ck(cudaMemcpyAsync(logits, logits_, (size_t)m_.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, stream), "logits");
     sync();
     return (uint32_t)a;
+}
+
+void State::batch_step(const std::vector<State*>& ms, const uint32_t* ids, uint32_t* out) {
+    const int B = (int)ms.size();
+    if (B < 1 || !ids || !out) throw std::invalid_argument("batch_step: no sequences");
+    State& L = *ms[0];
+    if (B > L.T_) throw std::invalid_argument("batch_step: more sequences than the first state's max_rows");
+    for (int i = 0; i < B; i++) {
+        const State* s = ms[i];
+        if (!s) throw std::invalid_argument("batch_step: a null state");
+        for (int j = 0; j < i; j++)
+            if (ms[j] == s) throw std::invalid_argument("batch_step: a state appears twice");
+        if (&s->m_ != &L.m_) throw std::invalid_argument("batch_step: the states belong to different models");
+        if (s->tp()) throw std::invalid_argument("batch_step: tensor-parallel states");
+        if (s->sampling()) throw std::invalid_argument("batch_step: a state with a sampler (batching is greedy)");
+        if (s->pos_ + 1 > s->max_pos_) throw std::invalid_argument("batch_step: a sequence would exceed its max_pos");
+    }
+    // the members' own queued work first: the batch runs on the first member's stream
+    for (int i = 1; i < B; i++) ms[i]->sync();
+    L.upload_ids(ids, B);
+    std::vector<uint64_t> key((size_t)B);
+    for (int i = 0; i < B; i++) key[(size_t)i] = ms[(size_t)i]->serial_;
+    if (key != L.batch_key_ && L.batch_exec_) {  // other members: the captured kernels hold the old ones' buffers
+        cudaGraphExecDestroy(L.batch_exec_);
+        L.batch_exec_ = nullptr;
+    }
+    L.batch_key_ = key;
+    L.batch_ = &ms;
+    try {
+        if (L.capture_) L.forward_rows(B, L.d_ids, true);
+        else L.graph_run(&L.batch_exec_, &L.batch_launches_, [&] { L.forward_rows(B, L.d_ids, true); });
+    } catch (...) {
+        L.batch_ = nullptr;
+        throw;
+    }
+    L.batch_ = nullptr;
+    for (State* s : ms) {  // as step(): the row is kept, the position advances
+        set_dev_int(s->d_keep, 1, L.stream);
+        s->pos_ += 1;
+        set_dev_int(s->d_pos, s->pos_, L.stream);
+    }
+    std::vector<int32_t> a(B);
+    ck(cudaMemcpyAsync(a.data(), L.d_argmax, (size_t)B * 4, cudaMemcpyDeviceToHost, L.stream), "argmax");
+    L.sync();
+    for (int i = 0; i < B; i++) out[i] = (uint32_t)a[i];
 }
 
 void State::logits_row(int row, float* out) const {

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
 #include <memory>
 #include <string>
 #include <vector>
@@ -118,6 +119,12 @@ class State {
     uint32_t spec_prefill(const uint32_t* ids, int n);
     // Model::spec_round (spec.rs:326-433) with greedy acceptance: emitted ids into `out` (m + 1 of them).
     int spec_round(uint32_t x_p, uint32_t* out);
+    // Plain greedy decode of several sequences in one forward, one row each (multi-sequence batching on one GPU):
+    // every weight matrix is read once for all the rows, while each row's conv window, DeltaNet state, KV cache
+    // and position are its own state's.  ids[i] is fed to members[i]; out[i] = its next id, as members[i]->step
+    // would give.  The first member's row buffers carry the batch (its max_rows >= members.size()); all members
+    // share the model, are greedy, and are on one GPU without tensor parallelism.
+    static void batch_step(const std::vector<State*>& members, const uint32_t* ids, uint32_t* out);
     // forced drafts for the next round (spec.rs:439-452, used by the identity tests)
     void set_drafts(const uint32_t* d, int k);
     // the sampler of this state (crates/core/src/sample.rs): temperature <= 0 is greedy; the RNG restarts from
@@ -159,6 +166,14 @@ class State {
     int k_, max_pos_, T_, mtp_cap_ = 0;
     int pos_ = 0, mtp_len_ = 0;
     bool capture_ = false;
+    const std::vector<State*>* batch_ = nullptr;  // during batch_step: the state that owns each row
+    // plain steps and batch steps as CUDA graphs (captured on first use; a batch graph holds its members' buffers,
+    // so it is keyed by their serial numbers and captured again when the members change)
+    uint64_t serial_ = 0;
+    cudaGraphExec_t step_exec_ = nullptr, batch_exec_ = nullptr;
+    uint64_t step_launches_ = 0, batch_launches_ = 0;
+    std::vector<uint64_t> batch_key_;
+    void graph_run(cudaGraphExec_t* exec, uint64_t* n_launches, const std::function<void()>& enqueue);
     bool drafts_ready_ = false;
     uint64_t launches_ = 0;  // kernels this state has launched
     void count_launch(uint64_t n = 1) { launches_ += n; }

@@ -1,5 +1,5 @@
 // Prompt prefill GEMM on the 5th-generation tensor cores (tcgen05): K-quant weights in the tile layout against
-// t >= 8 activation columns of the Q8_K device image, bit-exact with the reference's per-column dot
+// t >= 16 activation columns of the Q8_K device image, bit-exact with the reference's per-column dot
 // (crates/core/src/kernels/kdot.rs:37-141, reached from Model::prefill model.rs:443 through the blocked matmul
 // matvec.rs:446-467).  Decode (t <= 4 verify columns) stays on the CUDA-core GEMV.
 //
@@ -547,8 +547,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) kq_gemm_tc_kernel(const __grid_
 }
 
 int g_tc_min_cols = [] {
+    // below 16 columns the 4-column GEMV passes are faster (8 columns: 2 passes of a 17408 x 5120 Q4_K pair
+    // against one GEMM launch at half the time)
     const char* e = getenv("QDEC_GEMM_TC_MIN_COLS");
-    return e ? atoi(e) : 8;
+    return e ? atoi(e) : 16;
 }();
 
 template <int TYPE>

@@ -98,6 +98,7 @@ def lib():
             "qdec_state_pos": [P],
             "qdec_prefill": [P, U32P, I, U32P],
             "qdec_step": [P, ctypes.c_uint32, U32P, P],
+            "qdec_batch_step": [P, I, U32P, U32P],
             "qdec_spec_prefill": [P, U32P, I, U32P],
             "qdec_spec_round": [P, ctypes.c_uint32, U32P, ctypes.POINTER(I)],
             "qdec_set_drafts": [P, U32P, I],
@@ -200,11 +201,11 @@ def tune_gemv(impl=0, config=0):
     """Select a GEMV kernel / configuration (qdec_tune_gemv): impl 0/6 the image kernel of ggml-layout Q4_K/Q5_K
     and split Q6_K weights (config 0..8), impl 2 the reference-layout activation kernel, impl 7 the decode GEMV of
     K-quant tile matrices (0 by shape, 1..8), impl 8 the Q8_0/Q4_0 tile kernel (0..3), impl 9 the smallest column
-    count of the tensor-core prefill GEMM (default 8, 0 never). Results are identical for every value."""
+    count of the tensor-core prefill GEMM (default 16, 0 never). Results are identical for every value."""
     _check(lib().qdec_tune_gemv(impl, config))
 
 
-PREFILL_GEMM_MIN_COLS = 8
+PREFILL_GEMM_MIN_COLS = 16
 
 
 def selftest_wait(which, wait_ms=200):
@@ -441,6 +442,29 @@ def generate(state, prompt, n_tokens, stop=True):
     while len(out) < n_tokens and not (stop and state.model.is_stop(out[-1])):
         out.append(state.step(out[-1]))
     return out
+
+
+def batch_step(states, ids):
+    """One greedy step of several sequences in one forward (qdec_batch_step): ids[i] into states[i], their next
+    tokens out, identical to states[i].step(ids[i]); states[0] needs max_rows >= len(states)."""
+    n = len(states)
+    if n != len(ids):
+        raise ValueError("batch_step: one id per state")
+    hs = (ctypes.c_void_p * n)(*[s._h.value for s in states])
+    out = (ctypes.c_uint32 * n)()
+    _check(lib().qdec_batch_step(ctypes.cast(hs, ctypes.c_void_p), n, _u32(ids), out))
+    return list(out)
+
+
+def generate_batch(states, prompts, n_tokens):
+    """Plain greedy decoding of several sequences together: each state prefilled with its prompt, then
+    batch_step for the rest (the tokens of every sequence equal generate(state, prompt, n_tokens, stop=False))."""
+    outs = [[s.prefill(p)] for s, p in zip(states, prompts)]
+    while len(outs[0]) < n_tokens:
+        nxt = batch_step(states, [o[-1] for o in outs])
+        for o, t in zip(outs, nxt):
+            o.append(t)
+    return outs
 
 
 def generate_spec(state, prompt, n_tokens, stop=True):

@@ -215,3 +215,17 @@ def test_tp_rank_holds_its_share_not_the_whole_model(ck27):
         assert wb < 0.75 * total, f"rank {rank} holds {wb} of {total} bytes"
         assert wb <= grew <= wb + (512 << 20), f"rank {rank}: device memory grew by {grew}, weight bytes {wb}"
     assert sum(got) == 2 * replicated + sliced + vec_sliced + lm_from_embd
+
+
+def test_batch_step_27b(m27, o27):
+    """Four sequences decoded together at the 27B dimensions (the 4-column GEMVs and the fused gate/up/SwiGLU
+    over four sequences' rows; DeltaNet<128>, head_dim 256 attention and rope per sequence): each sequence's
+    greedy ids equal its own decoding and the oracle's."""
+    import qdec
+
+    prompts = [_prompt(n, SEED + 20 + n) for n in (5, 3, 2, 1)]
+    n = 4
+    got = qdec.generate_batch([m27.new_state(max_rows=8) for _ in prompts], prompts, n)
+    for p, g in zip(prompts, got):
+        assert qdec.generate(m27.new_state(max_rows=8), p, n, stop=False) == g
+        assert o27.state(MAX_POS).generate(p, n, stop=False) == g

@@ -224,3 +224,57 @@ def test_sampler_switch_to_greedy_mid_sequence(model):
     while len(plain) < 12:
         plain.append(b2.step(plain[-1]))
     assert cont[:12] == plain
+
+
+def _carried_all(st, n_layer):
+    out = {}
+    for layer in range(n_layer):
+        for what in range(4):
+            v = st.carried(layer, what)
+            if v is not None:
+                out[(layer, what)] = v
+    return out
+
+
+def test_batch_step_equals_single_sequences(model, omodel):
+    """Multi-sequence batching: three sequences of different prompt lengths decoded together (every weight
+    read once per step for the three rows) give each sequence's own greedy ids -- the oracle's -- and leave
+    every state's carried state (DeltaNet states, conv windows, K/V rows) bit for bit as single stepping does."""
+    import qdec
+
+    rng = np.random.default_rng(SEED + 7)
+    prompts = [[int(v) for v in rng.integers(0, 4096, n)] for n in (16, 9, 5)]
+    n = 12
+    batched = [model.new_state(max_rows=4) for _ in prompts]
+    got = qdec.generate_batch(batched, prompts, n)
+    singles = [model.new_state(max_rows=4) for _ in prompts]
+    for st, p, g in zip(singles, prompts, got):
+        assert qdec.generate(st, p, n, stop=False) == g
+        assert omodel.state(512).generate(p, n, stop=False) == g
+    for a, b in zip(batched, singles):
+        assert a.pos == b.pos
+        ca, cb = _carried_all(a, model.info.n_layer), _carried_all(b, model.info.n_layer)
+        assert ca.keys() == cb.keys()
+        for key in ca:
+            assert np.array_equal(ca[key].view(np.uint32), cb[key].view(np.uint32)), key
+    # a batched state continues on its own, and a single state joins a batch
+    assert batched[1].step(got[1][-1]) == singles[1].step(got[1][-1])
+
+
+def test_batch_step_rejects_bad_batches(model):
+    import qdec
+
+    a, b = model.new_state(max_rows=1), model.new_state(max_rows=4)
+    a.prefill([1, 2, 3])
+    b.prefill([4, 5])
+    with pytest.raises(qdec.QdecError):
+        qdec.batch_step([a, b], [7, 8])  # the first state's rows hold one sequence
+    with pytest.raises(qdec.QdecError):
+        qdec.batch_step([b, b], [7, 8])  # a state twice
+    c = model.new_state(max_rows=4)
+    c.set_sampler(temperature=0.8, seed=1)
+    with pytest.raises(qdec.QdecError):
+        qdec.batch_step([b, c], [7, 8])  # batching is greedy
+    assert (a.pos, b.pos) == (3, 2)  # nothing advanced
+    qdec.batch_step([b, a], [7, 8])  # the second state needs no spare rows
+    assert (a.pos, b.pos) == (4, 3)
