@@ -185,6 +185,8 @@ typedef struct qdec_model_info {
  * Replaces Model::load_with (crates/core/src/model.rs:184).  Malformed files give QDEC_EFORMAT with the
  * reference's GgufError / ConfigError message. */
 int qdec_open(const char *gguf_path, const qdec_opts *opts, qdec_model **out);
+/* Close a model.  With states of it still alive the model stays until the last of them is freed
+ * (qdec_state_new on the closed model then fails with QDEC_ESTATE). */
 int qdec_close(qdec_model *m);
 
 /* Tensor parallelism over the GPUs of one node, one process per GPU (rank tp_rank of tp_world, 1..8).  Each

@@ -2,6 +2,7 @@
 // the engine, with every C++ exception turned into a status code and a message.
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <vector>
 #include <new>
 #include <stdexcept>
@@ -14,6 +15,11 @@
 
 struct qdec_model {
     std::unique_ptr<qdec::Model> m;
+    // states made from this model and not yet freed; qdec_close with states alive defers the delete to the last
+    // qdec_state_free (a state reads its model until it is gone)
+    std::mutex mu;
+    int live = 0;
+    bool closed = false;
 };
 struct qdec_state {
     std::unique_ptr<qdec::State> s;
@@ -153,6 +159,14 @@ int qdec_tp_connect(qdec_state* s, const void* handles) {
 }
 
 int qdec_close(qdec_model* m) {
+    if (!m) return QDEC_OK;
+    {
+        std::lock_guard<std::mutex> g(m->mu);
+        if (m->live > 0) {
+            m->closed = true;
+            return QDEC_OK;
+        }
+    }
     delete m;
     return QDEC_OK;
 }
@@ -188,14 +202,28 @@ int qdec_state_new(qdec_model* m, int spec_k, int max_pos, int max_rows, qdec_st
         return qdec::fail(QDEC_EINVAL, "qdec_state_new: bad argument");
     *out = nullptr;
     return guard("qdec_state_new", [&] {
+        {
+            std::lock_guard<std::mutex> g(m->mu);
+            if (m->closed) throw std::logic_error("the model is closed");
+        }
         auto s = std::make_unique<qdec::State>(*m->m, spec_k, max_pos, max_rows);
         *out = new qdec_state{std::move(s), m};
+        std::lock_guard<std::mutex> g(m->mu);
+        m->live++;
         return QDEC_OK;
     });
 }
 
 int qdec_state_free(qdec_state* s) {
+    if (!s) return QDEC_OK;
+    qdec_model* m = s->owner;
     delete s;
+    bool last = false;
+    {
+        std::lock_guard<std::mutex> g(m->mu);
+        last = --m->live == 0 && m->closed;
+    }
+    if (last) delete m;
     return QDEC_OK;
 }
 

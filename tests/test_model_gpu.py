@@ -278,3 +278,16 @@ def test_batch_step_rejects_bad_batches(model):
     assert (a.pos, b.pos) == (3, 2)  # nothing advanced
     qdec.batch_step([b, a], [7, 8])  # the second state needs no spare rows
     assert (a.pos, b.pos) == (4, 3)
+
+
+def test_model_close_waits_for_its_states(tiny):
+    """qdec_close with a state still alive defers the release to the state's qdec_state_free: the state keeps
+    decoding after the close, and freeing it afterwards releases the model."""
+    import qdec
+
+    m = qdec.Model(tiny, max_pos=64)
+    st = m.new_state(max_rows=4)
+    a = st.prefill([5, 6, 7])
+    m.close()
+    assert isinstance(st.step(a), int)
+    st.free()
