@@ -251,15 +251,33 @@ __global__ void conv_step_kernel(float* __restrict__ state, const float* __restr
 template <int HK>
 __device__ __forceinline__ float chain_dot(const float (&S)[HK], const float* v, float acc) {
     const float4* v4 = reinterpret_cast<const float4*>(v);
-    float4 nx = v4[0];
+    float4 nx0 = v4[0], nx1 = v4[1];  // two quads ahead: a shared-memory load takes longer than four adds
 #pragma unroll
     for (int q = 0; q < HK / 4; q++) {
-        const float4 cur = nx;
-        if (q + 1 < HK / 4) nx = v4[q + 1];
+        const float4 cur = nx0;
+        nx0 = nx1;
+        if (q + 2 < HK / 4) nx1 = v4[q + 2];
         acc = __fadd_rn(acc, __fmul_rn(S[4 * q], cur.x));
         acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 1], cur.y));
         acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 2], cur.z));
         acc = __fadd_rn(acc, __fmul_rn(S[4 * q + 3], cur.w));
+    }
+    return acc;
+}
+// acc + v[0]^2 + v[1]^2 + .. + v[N-1]^2 left to right, v in shared memory (16-byte aligned), quads two ahead
+template <int N>
+__device__ __forceinline__ float chain_sq(const float* v, float acc) {
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    float4 nx0 = v4[0], nx1 = v4[1];
+#pragma unroll
+    for (int q = 0; q < N / 4; q++) {
+        const float4 cur = nx0;
+        nx0 = nx1;
+        if (q + 2 < N / 4) nx1 = v4[q + 2];
+        acc = __fadd_rn(acc, __fmul_rn(cur.x, cur.x));
+        acc = __fadd_rn(acc, __fmul_rn(cur.y, cur.y));
+        acc = __fadd_rn(acc, __fmul_rn(cur.z, cur.z));
+        acc = __fadd_rn(acc, __fmul_rn(cur.w, cur.w));
     }
     return acc;
 }
@@ -277,7 +295,9 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
     __shared__ __align__(16) float qs_all[CH][DK], ks_all[CH][DK];
     __shared__ float gate[CH][2], nrm[CH][2];  // (decay, beta), (1/|q|, 1/|k|)
     __shared__ float red[16], outs[128], part[128], dlt[128];
-    __shared__ float ab_part[2 * CH * 160], ab_val[2][CH];  // the in-kernel alpha / beta products
+    __shared__ __align__(16) float ab_part[2 * CH * 160];  // the in-kernel alpha / beta products
+    __shared__ float ab_val[2][CH];
+    __shared__ __align__(16) float vs_all[CH][128];  // the v rows of the chunk (dv <= 128)
     // Before griddepcontrol.wait: everything the conv kernel (launched right before) does not write -- the state
     // and the previous call's pending rows (this layer's own), the gates of the first rows (ssm_alpha/ssm_beta
     // two launches back, or their products from the normed rows, further back) and their z rows (attn_gate).
@@ -326,7 +346,23 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             const int which = t / nr0, r = t % nr0;
             const float* pp = ab_part + (which * CH + r) * 160;
             float acc = 0.0f;
-            for (int jp = 0; jp < nfull; jp++) acc = __fadd_rn(acc, pp[jp]);
+            int jp = 0;
+            if (nfull >= 8) {  // the partials in order, their shared-memory quads loaded two ahead
+                const float4* p4 = reinterpret_cast<const float4*>(pp);
+                const int nq = nfull / 4;
+                float4 nx0 = p4[0], nx1 = p4[1];
+                for (int q = 0; q < nq; q++) {
+                    const float4 cur = nx0;
+                    nx0 = nx1;
+                    if (q + 2 < nq) nx1 = p4[q + 2];
+                    acc = __fadd_rn(acc, cur.x);
+                    acc = __fadd_rn(acc, cur.y);
+                    acc = __fadd_rn(acc, cur.z);
+                    acc = __fadd_rn(acc, cur.w);
+                }
+                jp = nq * 4;
+            }
+            for (; jp < nfull; jp++) acc = __fadd_rn(acc, pp[jp]);
             ab_val[which][r] = __fadd_rn(acc, np > nfull ? pp[nfull] : 0.0f);
         }
         __syncthreads();
@@ -371,6 +407,10 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             qs_all[i][k] = row[kh * dk + k];
             ks_all[i][k] = row[a.kd + kh * dk + k];
         }
+        for (int e = t; e < nr * dv; e += blockDim.x) {  // the v rows, off the delta's path
+            const int i = e / dv, jj = e % dv;
+            vs_all[i][jj] = a.conved[(size_t)(c0 + i) * a.conv_dim + 2 * a.kd + p * dv + jj];
+        }
         __syncthreads();
         // l2norm (deltanet.rs:19-27, sums left to right): warp w normalises q of rows w, w + warps, .. on lane 0
         // and k on lane 16; the gates of later chunks on lane 8
@@ -383,9 +423,7 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
                 gate[i][1] = sigmoid_f32(a.beta[(size_t)r * a.n_v + p]);
             } else if (lane != 24) {
                 const float* vec = lane == 0 ? qs_all[i] : ks_all[i];
-                float ss = 0.0f;
-#pragma unroll
-                for (int k = 0; k < DK; k++) ss = __fadd_rn(ss, __fmul_rn(vec[k], vec[k]));
+                const float ss = chain_sq<DK>(vec, 0.0f);
                 nrm[i][lane == 0 ? 0 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
             }
         }
@@ -412,8 +450,7 @@ __global__ void __launch_bounds__(256) deltanet_halves_kernel(const DeltaArgs a)
             __syncthreads();
             if (h == 1) {
                 kv = chain_dot<HK>(S, ks, part[j]);
-                const float v = a.conved[(size_t)r * a.conv_dim + 2 * a.kd + p * dv + j];
-                dlt[j] = __fmul_rn(__fsub_rn(v, kv), beta);
+                dlt[j] = __fmul_rn(__fsub_rn(vs_all[i][j], kv), beta);
             }
             __syncthreads();
             const float delta = dlt[j];
