@@ -185,6 +185,10 @@ typedef struct qdec_model_info {
  * Replaces Model::load_with (crates/core/src/model.rs:184).  Malformed files give QDEC_EFORMAT with the
  * reference's GgufError / ConfigError message. */
 int qdec_open(const char *gguf_path, const qdec_opts *opts, qdec_model **out);
+/* 1 when the model's weights were read with O_DIRECT, bypassing the page cache (DirectFile,
+ * crates/core/src/os.rs:311): opted into with the environment variable QDEC_LOAD_DIRECT=1, on one GPU, where the
+ * file system allows O_DIRECT (not tmpfs); 0 when they were read through the page cache. */
+int qdec_model_loaded_direct(const qdec_model *m);
 /* Close a model.  With states of it still alive the model stays until the last of them is freed
  * (qdec_state_new on the closed model then fails with QDEC_ESTATE). */
 int qdec_close(qdec_model *m);

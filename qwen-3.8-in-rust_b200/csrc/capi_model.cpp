@@ -171,6 +171,8 @@ int qdec_close(qdec_model* m) {
     return QDEC_OK;
 }
 
+int qdec_model_loaded_direct(const qdec_model* m) { return m && m->m->loaded_direct ? 1 : 0; }
+
 int qdec_model_get_info(const qdec_model* m, qdec_model_info* info) {
     if (!m || !info) return qdec::fail(QDEC_EINVAL, "qdec_model_get_info: null argument");
     const qdec::ModelConfig& c = m->m->cfg;

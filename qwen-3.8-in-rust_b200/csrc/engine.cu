@@ -180,6 +180,13 @@ static int load_threads() {
     return n;
 }
 
+// QDEC_LOAD_DIRECT=1: the one-GPU load reads the file with O_DIRECT where its file system allows (buffered
+// otherwise; a tensor-parallel rank's per-tensor reads stay buffered).
+static bool load_direct() {
+    const char* e = getenv("QDEC_LOAD_DIRECT");
+    return e && atoi(e) > 0;
+}
+
 std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& opt) {
     const auto t0 = std::chrono::steady_clock::now();
     Gguf g(path);
@@ -216,13 +223,21 @@ std::unique_ptr<Model> Model::load(const std::string& path, const LoadOptions& o
         cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
         bool used[2] = {false, false};
         int b = 0;
+        // direct reads start at the block boundary at or before the data section: the `head` bytes before it
+        // are read and not uploaded (the staging buffers are page-aligned and CH is a multiple of the boundary)
+        const bool direct = load_direct() && g.open_direct();
+        const uint64_t head = direct ? g.data_offset() % Gguf::DIRECT_ALIGN : 0, base = g.data_offset() - head;
+        const uint64_t total = data_bytes + head;
+        m->loaded_direct = direct;
         try {
-            for (uint64_t off = 0; off < data_bytes; off += CH, b ^= 1) {
-                const uint64_t len = std::min<uint64_t>(CH, data_bytes - off);
+            for (uint64_t off = 0; off < total; off += CH, b ^= 1) {
+                const uint64_t len = std::min<uint64_t>(CH, total - off);
                 if (used[b]) ck(cudaEventSynchronize(done[b]), "staging wait");
                 uint8_t* hb = static_cast<uint8_t*>(host) + b * CH;
-                g.read_at_parallel(g.data_offset() + off, hb, len, load_threads());
-                ck(cudaMemcpyAsync(m->blob_ + off, hb, len, cudaMemcpyHostToDevice, s), "weights upload");
+                if (direct) g.read_direct_parallel(base + off, hb, len, load_threads());
+                else g.read_at_parallel(base + off, hb, len, load_threads());
+                const uint64_t skip = off == 0 ? head : 0;
+                ck(cudaMemcpyAsync(m->blob_ + off + skip - head, hb + skip, len - skip, cudaMemcpyHostToDevice, s), "weights upload");
                 ck(cudaEventRecord(done[b], s), "event");
                 used[b] = true;
             }

@@ -91,6 +91,7 @@ class Model {
     uint64_t decode_bytes = 0;   // weight bytes one plain token reads (model.rs:274)
     uint64_t mtp_bytes = 0;      // the MTP block's bytes (blk.{n_layer})
     double load_secs = 0;
+    bool loaded_direct = false;  // the weights were read with O_DIRECT (QDEC_LOAD_DIRECT)
     TpPlan tp;                   // this rank's shard (world 1: everything)
     bool is_stop(uint32_t id) const;
 

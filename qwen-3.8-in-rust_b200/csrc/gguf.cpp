@@ -232,6 +232,7 @@ Gguf::Gguf(const std::string &path) : path_(path) {
 }
 
 Gguf::~Gguf() {
+    if (fd_direct_ >= 0) ::close(fd_direct_);
     if (fd_ >= 0) ::close(fd_);
 }
 
@@ -310,6 +311,52 @@ void Gguf::read_at(uint64_t off, void *dst, uint64_t len) const {
         if (k <= 0) gerr("io error: short read of %s at %llu", path_.c_str(), (unsigned long long)(off + got));
         got += (uint64_t)k;
     }
+}
+
+bool Gguf::open_direct() {
+    if (fd_direct_ >= 0) return true;
+    fd_direct_ = ::open(path_.c_str(), O_RDONLY | O_CLOEXEC | O_DIRECT);
+    return fd_direct_ >= 0;
+}
+
+void Gguf::read_direct(uint64_t off, void *dst, uint64_t len) const {
+    const uint64_t want = (len + DIRECT_ALIGN - 1) & ~(DIRECT_ALIGN - 1);
+    uint8_t *d = static_cast<uint8_t *>(dst);
+    uint64_t got = 0;
+    while (got < want) {
+        const uint64_t chunk = std::min<uint64_t>(want - got, 1ull << 30);
+        const ssize_t k = pread(fd_direct_, d + got, chunk, (off_t)(off + got));
+        if (k < 0) gerr("io error: direct read of %s at %llu: %s", path_.c_str(), (unsigned long long)(off + got), strerror(errno));
+        if (k == 0) break;  // the end of the file
+        got += (uint64_t)k;
+        if ((uint64_t)k % DIRECT_ALIGN) break;  // a short read ends at the end of the file
+    }
+    if (got < len) gerr("io error: short direct read of %s at %llu", path_.c_str(), (unsigned long long)(off + got));
+}
+
+void Gguf::read_direct_parallel(uint64_t off, void *dst, uint64_t len, int threads) const {
+    if (fd_direct_ < 0) gerr("io error: %s is not open for direct reads", path_.c_str());
+    if (off % DIRECT_ALIGN || (uintptr_t)dst % DIRECT_ALIGN) gerr("io error: a direct read off its %llu-byte boundary",
+                                                                    (unsigned long long)DIRECT_ALIGN);
+    const uint64_t part_min = 16ull << 20;
+    const int n = (int)std::min<uint64_t>((uint64_t)std::max(threads, 1), std::max<uint64_t>(1, len / part_min));
+    const uint64_t per = ((len + n - 1) / n + DIRECT_ALIGN - 1) & ~(DIRECT_ALIGN - 1);
+    std::vector<std::thread> ts;
+    std::vector<std::string> errs(n);
+    for (int i = 0; i < n; i++) {
+        const uint64_t a = std::min<uint64_t>(len, (uint64_t)i * per), b = std::min<uint64_t>(len, a + per);
+        if (a >= b) break;
+        ts.emplace_back([this, off, dst, a, b, i, &errs] {
+            try {
+                read_direct(off + a, static_cast<uint8_t *>(dst) + a, b - a);
+            } catch (const std::exception &e) {
+                errs[i] = e.what();
+            }
+        });
+    }
+    for (std::thread &t : ts) t.join();
+    for (const std::string &e : errs)
+        if (!e.empty()) throw GgufError(e);
 }
 
 void Gguf::read_at_parallel(uint64_t off, void *dst, uint64_t len, int threads) const {

@@ -73,10 +73,18 @@ class Gguf {
     void read_at(uint64_t off, void *dst, uint64_t len) const;
     // the same bytes read by up to `threads` threads in contiguous parts
     void read_at_parallel(uint64_t off, void *dst, uint64_t len, int threads) const;
+    // Direct reads that bypass the page cache (O_DIRECT, os.rs:311 DirectFile): opens the file a second time and
+    // returns false where the file system refuses O_DIRECT (tmpfs, for one).  read_direct_parallel then reads
+    // [off, off + len) with off and dst on DIRECT_ALIGN boundaries, len rounded up to one (dst must have room for
+    // it); the file's end stops the read, so the rounding never reads past it.
+    static constexpr uint64_t DIRECT_ALIGN = 4096;
+    bool open_direct();
+    void read_direct_parallel(uint64_t off, void *dst, uint64_t len, int threads) const;
 
   private:
+    void read_direct(uint64_t off, void *dst, uint64_t len) const;
     std::string path_;
-    int fd_ = -1;
+    int fd_ = -1, fd_direct_ = -1;
     uint64_t file_size_ = 0, data_offset_ = 0;
     uint32_t alignment_ = 32;
     std::vector<std::pair<std::string, GValue>> kv_;

@@ -98,6 +98,7 @@ def lib():
             "qdec_state_pos": [P],
             "qdec_prefill": [P, U32P, I, U32P],
             "qdec_step": [P, ctypes.c_uint32, U32P, P],
+            "qdec_model_loaded_direct": [P],
             "qdec_batch_step": [P, I, U32P, U32P],
             "qdec_spec_prefill": [P, U32P, I, U32P],
             "qdec_spec_round": [P, ctypes.c_uint32, U32P, ctypes.POINTER(I)],
@@ -303,6 +304,11 @@ class Model:
 
     def is_stop(self, tok):
         return bool(lib().qdec_is_stop(self._h, tok))
+
+    @property
+    def loaded_direct(self):
+        """True when the weights were read with O_DIRECT (QDEC_LOAD_DIRECT=1 and a file system that allows it)."""
+        return bool(lib().qdec_model_loaded_direct(self._h))
 
     def new_state(self, spec_k=0, max_pos=None, max_rows=32):
         """Model::new_state / new_state_spec (model.rs:334, spec.rs:184)."""

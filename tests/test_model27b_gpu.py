@@ -229,3 +229,36 @@ def test_batch_step_27b(m27, o27):
     for p, g in zip(prompts, got):
         assert qdec.generate(m27.new_state(max_rows=8), p, n, stop=False) == g
         assert o27.state(MAX_POS).generate(p, n, stop=False) == g
+
+
+def test_direct_io_load_27b_dims(ck27, m27, tmp_path, monkeypatch):
+    """The O_DIRECT load over many 256 MiB staging chunks (the 4-layer 27B-dimension checkpoint copied to a disk
+    path): the same greedy ids as the buffered load."""
+    import shutil
+
+    import qdec
+
+    path = tmp_path / "ck27_direct.gguf"
+    shutil.copy(ck27, path)
+    try:
+        if not _odirect_ok(str(path)):
+            pytest.skip("the temporary directory's file system refuses O_DIRECT")
+        monkeypatch.setenv("QDEC_LOAD_DIRECT", "1")
+        m = qdec.Model(path, max_pos=MAX_POS)
+        try:
+            assert m.loaded_direct
+            p = _prompt(4, SEED + 31)
+            got = qdec.generate(m.new_state(max_rows=8), p, 3, stop=False)
+        finally:
+            m.close()
+        assert got == qdec.generate(m27.new_state(max_rows=8), p, 3, stop=False)
+    finally:
+        os.remove(path)
+
+
+def _odirect_ok(path):
+    try:
+        os.close(os.open(path, os.O_RDONLY | os.O_DIRECT))
+        return True
+    except OSError:
+        return False

@@ -291,3 +291,38 @@ def test_model_close_waits_for_its_states(tiny):
     m.close()
     assert isinstance(st.step(a), int)
     st.free()
+
+
+def _takes_odirect(path):
+    import os
+
+    try:
+        os.close(os.open(path, os.O_RDONLY | os.O_DIRECT))
+        return True
+    except OSError:
+        return False
+
+
+def test_direct_io_load_equals_buffered(tiny, tmp_path, monkeypatch):
+    """QDEC_LOAD_DIRECT=1 (O_DIRECT reads from the block boundary before the data section, the head bytes skipped
+    on upload, the last block cut by the end of the file) loads the same weights: greedy ids equal the buffered
+    load's; where the file system takes O_DIRECT the direct path was the one used."""
+    import shutil
+
+    import qdec
+
+    path = tmp_path / "tiny_direct.gguf"
+    shutil.copy(tiny, path)
+    p = prompt16()
+    monkeypatch.setenv("QDEC_LOAD_DIRECT", "1")
+    m = qdec.Model(path, max_pos=64)
+    direct = m.loaded_direct
+    got = qdec.generate(m.new_state(max_rows=4), p, 8, stop=False)
+    m.close()
+    monkeypatch.delenv("QDEC_LOAD_DIRECT")
+    mb = qdec.Model(path, max_pos=64)
+    assert not mb.loaded_direct
+    want = qdec.generate(mb.new_state(max_rows=4), p, 8, stop=False)
+    mb.close()
+    assert got == want
+    assert direct == _takes_odirect(str(path))
