@@ -1,6 +1,6 @@
-// Helpers of the tensor-core kernels (gemm_tc.cu, the prompt prefill GEMM): shared
-// memory and TMEM addressing, the shared-memory matrix descriptor, mbarriers with bounded waits, the tcgen05
-// fences, exact small-integer conversions, IEEE f32 pairs and the 2-D TMA tensor maps over tile-layout rows.
+// Helpers of the tensor-core kernel (gemm_tc.cu, the prompt prefill GEMM): shared-memory addressing, the
+// shared-memory matrix descriptor, mbarriers with bounded waits, the tcgen05 fences and commit, exact
+// small-integer conversions, IEEE f32 pairs and the 2-D TMA tensor maps over tile-layout rows.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -29,15 +29,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+__device__ __forceinline__ void mbar_init1(uint64_t* bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(1u));
 }
-__device__ __forceinline__ void mbar_init1(uint64_t* bar) { mbar_init(bar, 1u); }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 // bounded wait for the completion of the phase with `parity`; false after about a second
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -63,8 +59,6 @@ __device__ __forceinline__ float s8f(uint32_t b) { return __fsub_rn(__uint_as_fl
 __device__ __forceinline__ float s16f(uint32_t h) {
     return __fsub_rn(__uint_as_float(0x4B000000u | ((h ^ 0x8000u) & 0xFFFFu)), 8421376.0f);
 }
-// f32 of a signed 32-bit integer with |v| < 2^22 (exact: 1.5 * 2^23 + v is representable, the subtraction exact)
-__device__ __forceinline__ float s22f(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }
 
 // f32 pairs: two of the reference's independent chains side by side, each step the scalar IEEE
 // round-to-nearest operation.
