@@ -506,6 +506,8 @@ State::State(const Model& m, int spec_k, int max_pos, int max_rows) : m_(m), k_(
     T_ = std::max(max_rows, spec_k + 1);
     ck(cudaSetDevice(m.device), "cudaSetDevice");
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    ck(cudaMallocHost(&err_io_, 2 * sizeof(unsigned)), "pinned error words");
+    err_io_[0] = err_io_[1] = 0;
     const size_t H = c.hidden_size, FF = c.intermediate_size, T = T_;
     size_t maxw = std::max<size_t>(std::max<size_t>(2 * H, FF), std::max<size_t>(c.dn_v_dim, (size_t)c.n_head * c.head_dim_k));
     q8k_stride_ = maxw / 256 * Q8K_IMG_BYTES;  // the Q8_K device image
@@ -620,15 +622,21 @@ State::~State() {
     if (step_exec_) cudaGraphExecDestroy(step_exec_);
     if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
     if (h_io_) cudaFreeHost(h_io_);
+    if (err_io_) cudaFreeHost(err_io_);
     for (void* p : allocs_) cudaFree(p);
     for (float* p : capture_h_) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
 }
 
 void State::sync() {
+    // the error words travel with the stream's work: one synchronisation, no extra round trip per call
+    ck(enqueue_kernel_error_read(err_io_, stream), "error words");
     ck(cudaStreamSynchronize(stream), "decode step");
-    const unsigned err = read_kernel_error(true);
-    if (err) throw std::runtime_error("a device-side wait gave up (code " + std::to_string(err) + ")");
+    if (err_io_[0] || err_io_[1]) {
+        const unsigned err = err_io_[0] ? err_io_[0] : err_io_[1];
+        read_kernel_error(true);  // cleared for the calls after this one
+        throw std::runtime_error("a device-side wait gave up (code " + std::to_string(err) + ")");
+    }
     if (tp()) {
         unsigned xe = 0;
         ck(cudaMemcpy(&xe, xerr_, 4, cudaMemcpyDeviceToHost), "exchange status");
@@ -1016,6 +1024,7 @@ void State::graph_run(cudaGraphExec_t* exec, uint64_t* n_launches, const std::fu
         cudaGraphDestroy(g);
         if (e != cudaSuccess) *exec = nullptr;
         ck(e, "graph");
+        ck(cudaGraphUpload(*exec, stream), "graph upload");
         *n_launches = launches_ - before;
         launches_ = before;
     }
@@ -1349,6 +1358,7 @@ int State::spec_round(uint32_t x_p, uint32_t* out) {
             cudaError_t e = cudaGraphInstantiate(&round_exec_, g, 0);
             cudaGraphDestroy(g);
             ck(e, "round graph");
+            ck(cudaGraphUpload(round_exec_, stream), "round graph upload");
             round_launches_ = launches_ - before;
             launches_ = before;
         }

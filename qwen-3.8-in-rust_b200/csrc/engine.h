@@ -182,6 +182,7 @@ class State {
     cudaGraphExec_t round_exec_ = nullptr;
     uint64_t round_launches_ = 0;
     int32_t* h_io_ = nullptr;  // pinned: [0] x_p in; [16..] {keep, emitted ids} out
+    unsigned* err_io_ = nullptr;  // pinned: the kernels' two error words, read in stream order before each sync
     std::vector<void*> allocs_;
     void* dalloc(size_t bytes);
 

@@ -611,6 +611,10 @@ cudaError_t launch_gemm_tc(int type, const uint8_t* w_a, int rows_a, float* y_a,
     return cudaErrorInvalidValue;
 }
 
+cudaError_t enqueue_gemm_tc_error_read(unsigned* host_dst, cudaStream_t s) {
+    return cudaMemcpyFromSymbolAsync(host_dst, g_tc_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, s);
+}
+
 unsigned read_gemm_tc_error(bool clear) {
     unsigned v = 0;
     cudaMemcpyFromSymbol(&v, g_tc_error, sizeof v);

@@ -793,6 +793,10 @@ bool gemv7_supported(int type) { return type == T_Q4_K_TILE || type == T_Q5_K_TI
 
 void set_gemv7_config(int cfg) { g_cfg7 = cfg; }
 
+cudaError_t enqueue_gemv7_error_read(unsigned* host_dst, cudaStream_t s) {
+    return cudaMemcpyFromSymbolAsync(host_dst, g7_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, s);
+}
+
 unsigned read_gemv7_error(bool clear) {
     unsigned v = 0;
     cudaMemcpyFromSymbol(&v, g7_error, sizeof v);

@@ -512,6 +512,11 @@ cudaError_t launch_repack_q6k(const uint8_t* src, size_t nblocks, uint8_t* dst, 
     return cudaGetLastError();
 }
 
+cudaError_t enqueue_kernel_error_read(unsigned* host2, cudaStream_t s) {
+    const cudaError_t e = enqueue_gemm_tc_error_read(host2, s);
+    return e != cudaSuccess ? e : enqueue_gemv7_error_read(host2 + 1, s);
+}
+
 unsigned read_kernel_error(bool clear) {  // the error words of the kernels with bounded waits (0 = none)
     const unsigned t = read_gemm_tc_error(clear);
     const unsigned g7 = read_gemv7_error(clear);

@@ -82,10 +82,15 @@ unsigned read_gemv7_error(bool clear);  // the error word of gemv7.cu's bounded 
 int selftest_gemv7_timeout(unsigned long long wait_ns);  // failure-handling self-test of the stage wait (0 = as designed)
 // The device error word set by bounded waits that gave up (0 = none); optionally cleared.
 unsigned read_kernel_error(bool clear);
+// The same two error words (prefill GEMM, tile GEMV) copied into pinned host memory in stream order, so that the
+// stream's synchronisation also delivers them; read_kernel_error(true) clears them after one was set.
+cudaError_t enqueue_kernel_error_read(unsigned* host2, cudaStream_t s);
+cudaError_t enqueue_gemv7_error_read(unsigned* host_dst, cudaStream_t s);
+cudaError_t enqueue_gemm_tc_error_read(unsigned* host_dst, cudaStream_t s);
 // Prompt-prefill GEMM on the tensor cores (gemm_tc.cu): K-quant tile matrices (one, or two reading the same
 // image columns) against `ncols` Q8_K image columns, bit-exact with the GEMV.  launch_gemv_img and
 // launch_gemv_img_pair route there when gemm_tc_applies(type, ncols): tile types and ncols >= the minimum
-// column count (8 by default; 0 disables the path).
+// column count (16 by default; 0 disables the path).
 bool gemm_tc_applies(int type, int ncols);
 void set_gemm_tc_min_cols(int n);
 int gemm_tc_min_cols();
