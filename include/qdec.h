@@ -108,7 +108,9 @@ int qdec_gemv_image(int ggml_type, const void *w_dev, int rows, int cols, const 
  *     over 4 warps, 3 = the same with two tiles per CTA);
  *   impl 9: the tensor-core prefill GEMM that K-quant tile matrices take for many columns (config = the smallest
  *     column count routed there, 16 by default, 0 = never; the 1..4 verify columns stay on the GEMV at any value
- *     >= 5).
+ *     >= 5);
+ *   impl 10: the warp-MMA form of the Q4_K tile GEMV (integer lanes on mma.sync m16n8k32; config = the smallest
+ *     column group routed there, 1..4, 4 by default, 0 = never).
  * No counterpart in the reference. */
 int qdec_tune_gemv(int impl, int config);
 

@@ -254,13 +254,18 @@ int qdec_tune_gemv(int impl, int config) {
         set_gemm_tc_min_cols(config);
         return QDEC_OK;
     }
+    if (impl == 10) {  // the warp-MMA form of the Q4_K tile GEMV: the smallest column group routed to it (0 = never)
+        if (config < 0 || config > 4) return fail(QDEC_EINVAL, "warp-MMA minimum column count must be 0..4");
+        set_gemv7_mma_min_cols(config);
+        return QDEC_OK;
+    }
     if (impl == 7) {  // the decode GEMV of tile matrices: 0 automatic by shape, 1..8 a fixed configuration
         if (config < 0 || config > 8) return fail(QDEC_EINVAL, "tile gemv configuration must be 0..8");
         set_gemv_impl(0);
         set_gemv7_config(config);
         return QDEC_OK;
     }
-    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 7, 8 or 9");
+    if (impl != 0 && impl != 2 && impl != 6) return fail(QDEC_EINVAL, "gemv kernel must be 0, 2, 6, 7, 8, 9 or 10");
     if (impl == 0) set_gemv7_config(0);
     if (config < 0 || config > 8) return fail(QDEC_EINVAL, "gemv configuration must be 0..8");
     set_gemv_impl(impl);

@@ -470,6 +470,232 @@ kq_gemv7s_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
     }
 }
 
+// The same streaming form for Q4_K tile pairs with the integer lanes on the tensor cores: mma.sync m16n8k32 (s8)
+// per reference lane pair.  A warp's two tiles are the MMA's 16 rows (row g of tile 0, row g of tile 1); the K
+// dimension of one MMA is 4 chunks x 2 lanes (lanes 2u, 2u+1 of chunks 4q..4q+3), the activation codes are the B
+// operand masked per lane (B column 2n + s holds column n's codes at lane 2u+s's K words, zeros at the other lane's),
+// so D[row][2n+s] is exactly the reference's lane sum of lane 2u+s over those chunks; the chunk scale is folded
+// into A split in two byte parts (q * (sc >> 3), q * (sc & 7): every product of a 4-bit code fits a byte) and
+// sumi = 8 D0 + D1 in i32.  Thread (g = lane / 4, c = lane % 4) builds A words of chunk 4q + c for both its rows
+// and ends holding column c's lanes and mins of both rows: the f32 chains (kdot.rs:37-95) run in its registers in
+// super-block order, and the final reduce8 + reduce4 needs no shuffles.  The activation image is staged once per
+// CTA as [column][super-block][u][q][s][c] words with a column stride of 8 banks mod 32, so the B loads of a
+// warp hit 32 different banks.
+template <int NC>
+struct GeoM7 {
+    static constexpr int TB = G7<T_Q4_K>::TB;
+    __host__ __device__ static int col_words(int nb) { return nb * (Q8K_IMG_BYTES / 4) + ((8 - (nb * (Q8K_IMG_BYTES / 4)) % 32) + 32) % 32; }
+};
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One super-block of a warp's two Q4_K tiles (tile blocks tb0, tb1 in shared memory) against the B column of
+// thread (g, c): activation column g / 2 at lane parity g % 2, its image block at xb (zeros when !bval).  Leaves in
+// thread (g, c), for column c and row g of tile j, the eight exact lane sums and the row's d, dmin and min pairs
+// (get_scale_min_k4, quant.rs:45-51).  PERM: the block's code words are stored [u][q][s][c] (the streaming kernel's
+// staging) instead of the image's [lane][chunk].
+template <bool PERM>
+__device__ __forceinline__ void q4k_mma_sb(const uint8_t* tb0, const uint8_t* tb1, const uint32_t* xb, bool bval, int g, int c,
+                                           int (&sumi)[2][8], float (&dw)[2], float (&dminw)[2], uint32_t (&mp)[2][4]) {
+    const uint8_t* tb[2] = {tb0, tb1};
+    uint32_t shi[2][2], slo[2][2];  // the scale parts of chunks c and 4 + c
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const uint4 hd = *reinterpret_cast<const uint4*>(tb[j] + 1024 + g * 16);
+        const uint32_t sw0 = hd.y & 0x3F3F3F3Fu, sw1 = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+        const uint32_t s0 = (sw0 >> (8 * c)) & 0xFFu, s1 = (sw1 >> (8 * c)) & 0xFFu;
+        shi[j][0] = s0 >> 3, slo[j][0] = s0 & 7u, shi[j][1] = s1 >> 3, slo[j][1] = s1 & 7u;
+        const uint32_t mlo = hd.z & 0x3F3F3F3Fu, mhi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+        mp[j][0] = mlo, mp[j][1] = mlo >> 16, mp[j][2] = mhi, mp[j][3] = mhi >> 16;
+        dw[j] = f16_bits_to_f32((uint16_t)(hd.x & 0xffff));
+        dminw[j] = f16_bits_to_f32((uint16_t)(hd.x >> 16));
+    }
+    const int s = g & 1, sh = 4 * (c & 1);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {  // lanes 2u, 2u + 1
+        int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            // chunk 4q + c = pair 2q + c/2, nibble c % 2: the 8 bytes of lanes 2u, 2u + 1 of both rows
+            const uint2 w0 = *reinterpret_cast<const uint2*>(tb0 + q * 512 + (g * 4 + u) * 16 + (c >> 1) * 8);
+            const uint2 w1 = *reinterpret_cast<const uint2*>(tb1 + q * 512 + (g * 4 + u) * 16 + (c >> 1) * 8);
+            const uint32_t n00 = (w0.x >> sh) & 0x0F0F0F0Fu, n01 = (w0.y >> sh) & 0x0F0F0F0Fu;
+            const uint32_t n10 = (w1.x >> sh) & 0x0F0F0F0Fu, n11 = (w1.y >> sh) & 0x0F0F0F0Fu;
+            // A: a0 row g (tile 0) K word c (lane 2u), a1 row g + 8 (tile 1), a2 / a3 K word c + 4 (lane 2u + 1)
+            const uint32_t ah[4] = {n00 * shi[0][q], n10 * shi[1][q], n01 * shi[0][q], n11 * shi[1][q]};
+            const uint32_t al[4] = {n00 * slo[0][q], n10 * slo[1][q], n01 * slo[0][q], n11 * slo[1][q]};
+            // B: lane 2u + s of chunk 4q + c, in the K half of that lane
+            const uint32_t xw = bval ? xb[PERM ? (u * 2 + q) * 8 + s * 4 + c : (2 * u + s) * 8 + 4 * q + c] : 0u;
+            const uint32_t b0 = s ? 0u : xw, b1 = s ? xw : 0u;
+            mma_s8_16832(d0, ah, b0, b1);
+            mma_s8_16832(d1, al, b0, b1);
+        }
+        // d[0], d[1]: row g of tile 0, column c, lanes 2u, 2u + 1; d[2], d[3]: tile 1
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) sumi[j][2 * u + e] = 8 * d0[2 * j + e] + d1[2 * j + e];
+    }
+}
+
+// (-dx * dmin) * (mn[2k] q8s[2k] + mn[2k+1] q8s[2k+1]) of min group k (exact integer, then the reference's products)
+__device__ __forceinline__ float q4k_min_term(float dx, float dminw, uint32_t q8w, uint32_t mpair) {
+    const float prod = __fsub_rn(__int_as_float(dp2a_lo_s(q8w, mpair, (int)G7_MAGIC_I)), G7_MAGIC_F);
+    return __fmul_rn(__fmul_rn(-dx, dminw), prod);
+}
+
+template <int NC, int G, int D, int P, bool SWIGLU = false>
+__global__ void __launch_bounds__(32 * G)
+kq_gemv7m_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
+                 int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img, uint8_t* __restrict__ img_out,
+                 unsigned* __restrict__ blk_cnt) {
+    constexpr int TYPE = T_Q4_K, R = 2;
+    using Geo = GeoS7<TYPE, NC, G, R, D, P>;
+    constexpr int TB = G7<TYPE>::TB;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int g = lane >> 2, c = lane & 3;  // MMA group (row g of each tile; B column g) and thread in group
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem) + wid * D;
+    uint8_t* ring = smem + Geo::BAR + (size_t)wid * D * Geo::STAGE;
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Geo::BAR + Geo::RING);
+    const int cw = GeoM7<NC>::col_words(nb);
+    constexpr int TPW = SWIGLU ? 1 : R;
+    const int ctas_a = (rows_a / 8 + G * TPW - 1) / (G * TPW);
+    const bool second = !SWIGLU && (int)blockIdx.x >= ctas_a;
+    const uint8_t* w = second ? w_b : w_a;
+    const int rows = second ? rows_b : rows_a;
+    float* y = second ? y_b : y_a;
+    const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
+    const int tiles = rows / 8;
+    const int t0 = (bid * G + wid) * TPW;
+    const bool active = t0 < tiles;
+    const int nwin = (nb + P - 1) / P;
+
+    auto issue = [&](int win) {
+        uint8_t* st = ring + (size_t)(win % D) * Geo::STAGE;
+        const int n = min(P, nb - win * P);
+        mbar_expect7(&bar[win % D], (uint32_t)(R * n * TB) + (win == 0 && wid == 0 ? g7_test_extra_tx : 0u));
+        for (int j = 0; j < R; j++) {
+            const int t = SWIGLU ? t0 : min(t0 + j, tiles - 1);
+            const uint8_t* wm = SWIGLU && j == 1 ? w_b : w;
+            bulk7(st + (size_t)j * P * TB, wm + ((size_t)t * nb + (size_t)win * P) * TB, (uint32_t)(n * TB), &bar[win % D]);
+        }
+    };
+    if (lane == 0 && active) {
+        for (int d = 0; d < D; d++) mbar_init7(&bar[d]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    if (lane == 0 && active)
+        for (int d = 0; d < D && d < nwin; d++) issue(d);  // weights are never written after load: before the wait
+    gd_wait();  // the activation image is the previous kernel's output
+    gd_launch();
+    {  // stage the image: code quad Q = 2 L + q (lane L = 2u + s, chunks 4q..4q+3) goes to quad (2u + q) * 2 + s
+        const uint4* src = reinterpret_cast<const uint4*>(img);
+        const int nq = NC * nb * (Q8K_IMG_BYTES / 16);
+        for (int i = tid; i < nq; i += 32 * G) {
+            const int blk = i / (Q8K_IMG_BYTES / 16), Q = i % (Q8K_IMG_BYTES / 16);
+            const int L = Q >> 1, q = Q & 1;
+            const int qd = Q < 16 ? ((L >> 1) * 2 + q) * 2 + (L & 1) : Q;
+            const int n = blk / nb, sb = blk % nb;
+            reinterpret_cast<uint4*>(xs + (size_t)n * cw + (size_t)sb * (Q8K_IMG_BYTES / 4))[qd] = src[i];
+        }
+    }
+    __syncthreads();
+    if (!active) return;
+    float acc[R][8], accm[R][4];  // column c of rows g (tile 0) and g (tile 1): the 8 lanes and the 4 mins groups
+#pragma unroll
+    for (int j = 0; j < R; j++) {
+#pragma unroll
+        for (int l = 0; l < 8; l++) acc[j][l] = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 4; m++) accm[j][m] = 0.0f;
+    }
+    const int bn = g >> 1;  // this thread's B column: activation column bn (lane parity g % 2)
+    const bool bval = bn < NC, cval = c < NC;
+    bool ok = true;
+    int win = 0;
+    for (; win < nwin; win++) {
+        const int slot = win % D;
+        if (!__all_sync(0xffffffffu, mbar_wait7(&bar[slot], (uint32_t)((win / D) & 1)))) {
+            ok = false;
+            break;
+        }
+        const uint8_t* st = ring + (size_t)slot * Geo::STAGE;
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int sb = win * P + p;
+            if (P > 1 && sb >= nb) break;
+            int sumi[R][8];
+            float dw[R], dminw[R];
+            uint32_t mp[R][4];
+            const uint32_t* xb = xs + (size_t)(bval ? bn : 0) * cw + (size_t)sb * (Q8K_IMG_BYTES / 4);
+            q4k_mma_sb<true>(st + (size_t)p * TB, st + (size_t)(P + p) * TB, xb, bval, g, c, sumi, dw, dminw, mp);
+            // column c's scale and chunk sums
+            const uint32_t* xc = xs + (size_t)(cval ? c : 0) * cw + (size_t)sb * (Q8K_IMG_BYTES / 4);
+            const float dx = cval ? __uint_as_float(xc[Q8K_IMG_D / 4]) : 0.0f;
+            const uint4 q8 = cval ? *reinterpret_cast<const uint4*>(xc + Q8K_IMG_Q8S / 4) : make_uint4(0, 0, 0, 0);
+            const uint32_t q8w[4] = {q8.x, q8.y, q8.z, q8.w};
+#pragma unroll
+            for (int j = 0; j < R; j++) {
+                const float dd = __fmul_rn(dx, dw[j]);  // d = dx * d_w (kdot.rs:50)
+#pragma unroll
+                for (int l = 0; l < 8; l++) acc[j][l] = __fadd_rn(acc[j][l], __fmul_rn(dd, __int2float_rn(sumi[j][l])));
+#pragma unroll
+                for (int k = 0; k < 4; k++) accm[j][k] = __fadd_rn(accm[j][k], q4k_min_term(dx, dminw[j], q8w[k], mp[j][k]));
+            }
+        }
+        __syncwarp();  // every lane is done with this slot
+        if (lane == 0 && win + D < nwin) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the async refill
+            issue(win + D);
+        }
+    }
+    if (!ok) {
+        if (lane == 0) {
+            atomicCAS(&g7_error, 0u, 0x700u | (unsigned)TYPE);
+            for (int k = win; k < nwin && k < win + D; k++) mbar_wait7(&bar[k % D], (uint32_t)((k / D) & 1));
+        }
+        return;
+    }
+    // per (tile, column c, row g): reduce8 of the 8 lanes + reduce4 of the 4 mins groups (kdot.rs:75)
+    float vr[R];
+#pragma unroll
+    for (int j = 0; j < R; j++) {
+        const float v = reduce8(acc[j]);
+        vr[j] = __fadd_rn(v, __fadd_rn(__fadd_rn(accm[j][0], accm[j][2]), __fadd_rn(accm[j][1], accm[j][3])));
+        const int tile = t0 + j;
+        if (!SWIGLU && cval && tile < tiles) y[(size_t)c * rows + tile * 8 + g] = vr[j];
+    }
+    if constexpr (SWIGLU) {
+        if (cval) y_a[(size_t)c * rows + t0 * 8 + g] = __fmul_rn(silu_f32(vr[0]), vr[1]);
+        __threadfence();  // the h rows before the block counter
+        __syncwarp();
+        const int blk = t0 / 32, nblk = rows / 256;
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&blk_cnt[blk], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == 31) {  // the block's last tile: quantise its 256 h values of every column
+            __threadfence();
+            float v[NC][8];
+#pragma unroll
+            for (int n = 0; n < NC; n++) {
+                const float4* hb = reinterpret_cast<const float4*>(y_a + (size_t)n * rows + (size_t)blk * 256 + lane * 8);
+                const float4 a = __ldcg(hb), b = __ldcg(hb + 1);
+                v[n][0] = a.x, v[n][1] = a.y, v[n][2] = a.z, v[n][3] = a.w;
+                v[n][4] = b.x, v[n][5] = b.y, v[n][6] = b.z, v[n][7] = b.w;
+            }
+#pragma unroll
+            for (int n = 0; n < NC; n++) q8k_quantize_to_image(v[n], img_out + ((size_t)n * nblk + blk) * Q8K_IMG_BYTES);
+            if (lane == 0) blk_cnt[blk] = 0u;  // ready for the next launch
+        }
+    }
+}
+
 // CTA = G x S warps: warp w serves tile group w % G (R tiles of 8 rows) and super-block phase w / G, i.e.
 // super-blocks w/G, w/G + S, ... of its tiles.  Thread 0 keeps D windows of S super-blocks in flight.
 template <int TYPE, int NC, int G, int S, int R, int D, bool X2>
@@ -664,6 +890,195 @@ kq_gemv7_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__
     }
 }
 
+// The windowed form with the integer lanes on the tensor cores (Q4_K): warp w of the CTA serves the two tiles of
+// tile group w % G (the MMA's 16 rows) and super-block phase w / G; per super-block each thread writes its
+// column's 8 lane terms d * sumi and 4 min terms for its row of both tiles, and the owners add them in
+// super-block order as in kq_gemv7_kernel.  A window's image blocks of column n start at n * XC + {0, 16, 64, 80}
+// bytes (XC a multiple of 128), so the B loads of a warp (8 (lane parity) + 4 n' + c banks) hit 32 different banks;
+// the term rows of a column are padded to 104 floats so the 16-byte term stores of a quarter warp do not collide.
+template <int NC, int G, int S, int D>
+struct GeoMW7 {
+    static constexpr int TB = G7<T_Q4_K>::TB, R = 2;
+    static constexpr int WST = G * R * S * TB;
+    static constexpr int XC = (S * Q8K_IMG_BYTES + 127) / 128 * 128;
+    __host__ __device__ static constexpr int xoff(int n) { return n * XC + (n & 1) * 16 + (n >> 1) * 64; }
+    static constexpr int XW = xoff(NC - 1) + S * Q8K_IMG_BYTES;
+    static constexpr int STAGE = (WST + XW + 127) / 128 * 128;
+    static constexpr int CW = 8 * 12 + 8;  // one (tile, column)'s 8 rows of 12 terms, padded
+    static constexpr int PER_SB = R * NC * CW;
+    static constexpr size_t BAR = 128;
+    static constexpr size_t ST0 = BAR;
+    static constexpr size_t TERMS = ST0 + (size_t)D * STAGE;
+    static constexpr size_t FIN = TERMS + (size_t)2 * G * S * PER_SB * 4;
+    static constexpr size_t BYTES = FIN + (size_t)G * R * NC * 8 * 12 * 4;
+    static_assert(S > 1 && D <= 16 && NC <= 4, "geometry");
+};
+
+template <int NC, int G, int S, int D>
+__global__ void __launch_bounds__(32 * G * S)
+kq_gemv7mw_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict__ y_a, const uint8_t* __restrict__ w_b,
+                  int rows_b, float* __restrict__ y_b, int nb, const uint8_t* __restrict__ img) {
+    constexpr int TYPE = T_Q4_K, R = 2, LPC = 12;
+    using Geo = GeoMW7<NC, G, S, D>;
+    constexpr int TB = Geo::TB, PER_SB = Geo::PER_SB, CW = Geo::CW;
+    constexpr int CHAINS = G * R * NC * 8 * LPC;
+    constexpr int NT = 32 * G * S;
+    constexpr int CPT = (CHAINS + NT - 1) / NT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_abort;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    uint8_t* stages = smem + Geo::ST0;
+    float* terms = reinterpret_cast<float*>(smem + Geo::TERMS);
+    float* fin = reinterpret_cast<float*>(smem + Geo::FIN);
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, gi = wid % G, si = wid / G;
+    const int g = lane >> 2, c = lane & 3;
+    const int ctas_a = (rows_a / 8 + G * R - 1) / (G * R);
+    const bool second = (int)blockIdx.x >= ctas_a;
+    const uint8_t* w = second ? w_b : w_a;
+    const int rows = second ? rows_b : rows_a;
+    float* y = second ? y_b : y_a;
+    const int bid = second ? (int)blockIdx.x - ctas_a : (int)blockIdx.x;
+    const int tiles = rows / 8;
+    const int nwin = (nb + S - 1) / S;
+
+    auto win_sbs = [&](int win) { return min(S, nb - win * S); };
+    auto issue_w = [&](int win) {
+        uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE;
+        const int n = win_sbs(win);
+        mbar_expect7(&bar[win % D], (uint32_t)(n * (G * R * TB + NC * Q8K_IMG_BYTES)) + (win == 0 ? g7_test_extra_tx : 0u));
+        for (int k = 0; k < G * R; k++) {
+            const int t = min(bid * G * R + k, tiles - 1);
+            bulk7(st + (size_t)k * S * TB, w + ((size_t)t * nb + (size_t)win * S) * TB, (uint32_t)(n * TB), &bar[win % D]);
+        }
+    };
+    auto issue_x = [&](int win) {
+        uint8_t* st = stages + (size_t)(win % D) * Geo::STAGE + Geo::WST;
+        const int n = win_sbs(win);
+        for (int col = 0; col < NC; col++)
+            bulk7(st + Geo::xoff(col), img + ((size_t)col * nb + (size_t)win * S) * Q8K_IMG_BYTES, (uint32_t)(n * Q8K_IMG_BYTES),
+                  &bar[win % D]);
+    };
+    if (tid == 0) {
+        s_abort = 0;
+        for (int d = 0; d < D; d++) mbar_init7(&bar[d]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int d = 0; d < D && d < nwin; d++) issue_w(d);  // weights are never written after load: before the wait
+    }
+    gd_wait();  // the activation image is the previous kernel's output
+    gd_launch();
+    if (tid == 0)
+        for (int d = 0; d < D && d < nwin; d++) issue_x(d);
+    __syncthreads();
+
+    float cacc[CPT];
+#pragma unroll
+    for (int k = 0; k < CPT; k++) cacc[k] = 0.0f;
+    const int bn = g >> 1;
+    const bool bval = bn < NC, cval = c < NC;
+
+    for (int win = 0; win < nwin; win++) {
+        const int slot = win % D;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait7(&bar[slot], (uint32_t)((win / D) & 1)));
+        if (!ok && lane == 0) s_abort = 1;
+        const int sb = win * S + si;
+        if (ok && sb < nb) {
+            const uint8_t* st = stages + (size_t)slot * Geo::STAGE;
+            const uint8_t* xw = st + Geo::WST + (size_t)si * Q8K_IMG_BYTES;
+            int sumi[R][8];
+            float dw[R], dminw[R];
+            uint32_t mp[R][4];
+            q4k_mma_sb<false>(st + ((size_t)(gi * R) * S + si) * TB, st + ((size_t)(gi * R + 1) * S + si) * TB,
+                              reinterpret_cast<const uint32_t*>(xw + Geo::xoff(bval ? bn : 0)), bval, g, c, sumi, dw, dminw, mp);
+            if (cval) {
+                const uint8_t* xc = xw + Geo::xoff(c);
+                const float dx = *reinterpret_cast<const float*>(xc + Q8K_IMG_D);
+                const uint4 q8 = *reinterpret_cast<const uint4*>(xc + Q8K_IMG_Q8S);
+                const uint32_t q8w[4] = {q8.x, q8.y, q8.z, q8.w};
+                float* tb = terms + (size_t)(((win & 1) * S + si) * G + gi) * PER_SB;
+#pragma unroll
+                for (int j = 0; j < R; j++) {
+                    const float dd = __fmul_rn(dx, dw[j]);  // d = dx * d_w (kdot.rs:50)
+                    float t[12];
+#pragma unroll
+                    for (int l = 0; l < 8; l++) t[l] = __fmul_rn(dd, __int2float_rn(sumi[j][l]));
+#pragma unroll
+                    for (int k = 0; k < 4; k++) t[8 + k] = q4k_min_term(dx, dminw[j], q8w[k], mp[j][k]);
+                    float4* tp = reinterpret_cast<float4*>(tb + (j * NC + c) * CW + g * 12);
+                    tp[0] = make_float4(t[0], t[1], t[2], t[3]);
+                    tp[1] = make_float4(t[4], t[5], t[6], t[7]);
+                    tp[2] = make_float4(t[8], t[9], t[10], t[11]);
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with this slot (and has written its terms)
+        if (s_abort) {
+            if (tid == 0) {
+                atomicCAS(&g7_error, 0u, 0x700u | (unsigned)TYPE);
+                for (int k = win; k < nwin && k < win + D; k++) mbar_wait7(&bar[k % D], (uint32_t)((k / D) & 1));
+            }
+            return;
+        }
+        if (tid == 0 && win + D < nwin) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the async refill
+            issue_w(win + D);
+            issue_x(win + D);
+        }
+        const int nsb = win_sbs(win);  // the owners add this window's terms in super-block order
+#pragma unroll
+        for (int k = 0; k < CPT; k++) {
+            const int ci = tid + k * NT;
+            if (ci < CHAINS) {
+                const int gg = ci / (R * NC * 8 * LPC), r = ci % (R * NC * 8 * LPC);
+                const int row = r / LPC, jn = row / 8;  // row = (j * NC + n) * 8 + row in tile
+                const float* tw = terms + (size_t)((win & 1) * S * G + gg) * PER_SB + jn * CW + (row % 8) * 12 + r % LPC;
+                float a = cacc[k];
+#pragma unroll
+                for (int p = 0; p < S; p++)
+                    if (p < nsb) a = __fadd_rn(a, tw[(size_t)p * G * PER_SB]);
+                cacc[k] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < CPT; k++) {
+        const int ci = tid + k * NT;
+        if (ci < CHAINS) fin[ci] = cacc[k];  // fin[gg][(j * NC + n) * 8 + row][12]
+    }
+    __syncthreads();
+    // per (tile, column, row): reduce8 of the 8 main lanes + reduce4 of the 4 min lanes (kdot.rs:75)
+    for (int o = tid; o < G * R * NC * 8; o += NT) {
+        const int r = o % 8, n = (o / 8) % NC, j = (o / (8 * NC)) % R, gg = o / (8 * NC * R);
+        const float* f = fin + (size_t)o * 12;
+        const float v = __fadd_rn(reduce8(f), __fadd_rn(__fadd_rn(f[8], f[10]), __fadd_rn(f[9], f[11])));
+        const int tile = (bid * G + gg) * R + j;
+        if (tile < tiles) y[(size_t)n * rows + tile * 8 + r] = v;
+    }
+}
+
+template <int NC, int G, int S, int D>
+cudaError_t launch7mw(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                      const void* img, cudaStream_t s, bool pdl) {
+    using Geo = GeoMW7<NC, G, S, D>;
+    auto kern = kq_gemv7mw_kernel<NC, G, S, D>;
+    static bool attr_done = false;  // per instantiation
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Geo::BYTES);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows_a / 8 + G * 2 - 1) / (G * 2) + (w_b ? (rows_b / 8 + G * 2 - 1) / (G * 2) : 0));
+    cfg.blockDim = dim3(32 * G * S);
+    cfg.dynamicSmemBytes = Geo::BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img);
+}
+
 template <int TYPE, int NC, int G, int S, int R, int D, bool X2 = false>
 cudaError_t launch7(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
                     const void* img, cudaStream_t s, bool pdl) {
@@ -714,6 +1129,35 @@ cudaError_t launch7s(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* 
     return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img, img_out, blk_cnt);
 }
 
+template <int NC, int G, int D, int P, bool SWIGLU = false>
+cudaError_t launch7m(const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b, int nb,
+                     const void* img, cudaStream_t s, bool pdl, uint8_t* img_out = nullptr, unsigned* blk_cnt = nullptr) {
+    static_assert(NC <= 4, "the MMA's 8 B columns hold 4 activation columns x 2 lanes");
+    using Geo = GeoS7<T_Q4_K, NC, G, 2, D, P>;
+    auto kern = kq_gemv7m_kernel<NC, G, D, P, SWIGLU>;
+    const size_t bytes = Geo::BAR + Geo::RING + (size_t)NC * GeoM7<NC>::col_words(nb) * 4;
+    static size_t attr_bytes = 0;
+    if (bytes > 48 * 1024 && bytes > attr_bytes) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        attr_bytes = bytes;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = SWIGLU ? dim3((rows_a / 8 + G - 1) / G)
+                         : dim3((rows_a / 8 + G * 2 - 1) / (G * 2) + (w_b ? (rows_b / 8 + G * 2 - 1) / (G * 2) : 0));
+    cfg.blockDim = dim3(32 * G);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, w_a, rows_a, y_a, w_b, rows_b, y_b, nb, (const uint8_t*)img, img_out, blk_cnt);
+}
+
+int g_mma7_min_cols = 4;  // the smallest column group that takes the warp-MMA form for Q4_K (0 = never)
+
 int g_cfg7 = [] {
     const char* e = getenv("QDEC_GEMV7_CFG");
     return e ? atoi(e) : 0;
@@ -736,11 +1180,19 @@ cudaError_t launch7_cfg(int cfg, const uint8_t* w_a, int rows_a, float* y_a, con
                     // super-block phases, tiles per warp, windows, shifted image copy>
     case 1: return launch7s<TYPE, NC, 4, 1, 4, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 2: return launch7s<TYPE, NC, 4, 1, 3, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 3: return launch7s<TYPE, NC, 4, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 4: return launch7s<TYPE, NC, 5, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 5: return launch7s<TYPE, NC, 6, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 3:
+        if (TYPE == T_Q4_K && g_mma7_min_cols > 0 && NC >= g_mma7_min_cols) return launch7m<NC, 4, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+        return launch7s<TYPE, NC, 4, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 4:
+        if (TYPE == T_Q4_K && g_mma7_min_cols > 0 && NC >= g_mma7_min_cols) return launch7m<NC, 5, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+        return launch7s<TYPE, NC, 5, 2, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 5:
+        if (TYPE == T_Q4_K && g_mma7_min_cols > 0 && NC >= g_mma7_min_cols) return launch7m<NC, 6, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+        return launch7s<TYPE, NC, 6, 2, 2, 1>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     case 6: return launch7s<TYPE, NC, 10, 1, 2, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
-    case 7: return launch7<TYPE, NC, 1, 4, 2, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+    case 7:
+        if (TYPE == T_Q4_K && g_mma7_min_cols > 0 && NC >= g_mma7_min_cols) return launch7mw<NC, 1, 4, 2>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
+        return launch7<TYPE, NC, 1, 4, 2, 2, true>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     default: return launch7<TYPE, NC, 1, 4, 2, 3>(w_a, rows_a, y_a, w_b, rows_b, y_b, nb, img, s, pdl);
     }
 }
@@ -759,6 +1211,12 @@ cudaError_t launch7_type(const uint8_t* w_a, int rows_a, float* y_a, const uint8
 template <int TYPE>
 cudaError_t launch7_swiglu_type(const uint8_t* w_g, const uint8_t* w_u, int rows, float* h, int nb, const void* img, int nc,
                                 uint8_t* img_out, unsigned* cnt, cudaStream_t s, bool pdl) {
+    if (TYPE == T_Q4_K && g_mma7_min_cols > 0 && nc >= g_mma7_min_cols) switch (nc) {
+        case 1: return launch7m<1, 5, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+        case 2: return launch7m<2, 5, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+        case 3: return launch7m<3, 5, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+        default: return launch7m<4, 5, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
+        }
     switch (nc) {  // the pair's default geometry: 5 warps of one gate and one up tile, 2 stages of 2 super-blocks
     case 1: return launch7s<TYPE, 1, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
     case 2: return launch7s<TYPE, 2, 5, 2, 2, 2, true>(w_g, rows, h, w_u, rows, nullptr, nb, img, s, pdl, img_out, cnt);
@@ -792,6 +1250,7 @@ cudaError_t launch_gemv7_swiglu(int type, const uint8_t* w_gate, const uint8_t* 
 bool gemv7_supported(int type) { return type == T_Q4_K_TILE || type == T_Q5_K_TILE || type == T_Q6_K_TILE; }
 
 void set_gemv7_config(int cfg) { g_cfg7 = cfg; }
+void set_gemv7_mma_min_cols(int n) { g_mma7_min_cols = n; }
 
 cudaError_t enqueue_gemv7_error_read(unsigned* host_dst, cudaStream_t s) {
     return cudaMemcpyFromSymbolAsync(host_dst, g7_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, s);

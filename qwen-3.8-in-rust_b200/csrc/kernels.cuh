@@ -71,6 +71,7 @@ cudaError_t launch_gemv_q80_img(int type, const uint8_t* w, int rows, int cols, 
 // Bit-exact with crates/core/src/kernels/kdot.rs.  rows % 8 == 0, cols % 256 == 0.
 bool gemv7_supported(int type);
 void set_gemv7_config(int cfg);  // 0 = automatic by shape; 1..8 a fixed configuration (tests, sweeps)
+void set_gemv7_mma_min_cols(int n);  // Q4_K column groups of at least n take the warp-MMA form (0 = never)
 cudaError_t launch_gemv7(int type, const uint8_t* w_a, int rows_a, float* y_a, const uint8_t* w_b, int rows_b, float* y_b,
                          int cols, const void* img, int ncols, cudaStream_t s, bool pdl);
 // The MLP's gate and up tile matrices (rows x cols each, rows % 256 == 0) against the image columns, fused with

@@ -202,11 +202,13 @@ def tune_gemv(impl=0, config=0):
     """Select a GEMV kernel / configuration (qdec_tune_gemv): impl 0/6 the image kernel of ggml-layout Q4_K/Q5_K
     and split Q6_K weights (config 0..8), impl 2 the reference-layout activation kernel, impl 7 the decode GEMV of
     K-quant tile matrices (0 by shape, 1..8), impl 8 the Q8_0/Q4_0 tile kernel (0..3), impl 9 the smallest column
-    count of the tensor-core prefill GEMM (default 16, 0 never). Results are identical for every value."""
+    count of the tensor-core prefill GEMM (default 16, 0 never), impl 10 the smallest column group of the warp-MMA
+    Q4_K GEMV (1..4, default 4, 0 never). Results are identical for every value."""
     _check(lib().qdec_tune_gemv(impl, config))
 
 
 PREFILL_GEMM_MIN_COLS = 16
+GEMV_MMA_MIN_COLS = 4
 
 
 def selftest_wait(which, wait_ms=200):

@@ -396,3 +396,36 @@ def test_gemv7_integer_extremes_bit_exact(q, orc, t, neg, cfg):
     finally:
         q.tune_gemv(0, 0)
     assert bits_equal(got, want), (t, neg, cfg)
+
+
+@pytest.mark.parametrize("cfg", [0, 3, 4, 5, 7])
+def test_gemv7_warp_mma_bit_exact(q, orc, cfg):
+    """The warp-MMA forms of the Q4_K tile GEMV (integer lanes on mma.sync m16n8k32, gemv7.cu): streaming (configs
+    3-5) and windowed (7; 0 picks by shape) with every column count 1..5 routed there, against the oracle's bits:
+    an odd tile count (the last warp's second tile is past the end), 21 super-blocks (not a multiple of any
+    window or stage), tiny, huge and zero columns, and the integer extremes of the codes and scales."""
+    rows, cols = 8 * 37, 5376
+    w = random_blocks(12, rows, cols, seed=300 + cfg)
+    x = np.random.default_rng(400 + cfg).standard_normal((5, cols)).astype(np.float32)
+    x[1] *= 1e-30
+    x[3] *= 1e20
+    x[4, ::3] = 0.0
+    want = orc.matmul(12, w, rows, cols, x)
+    dst = _repack(q, 12, w, rows, cols)
+    we = _extreme_blocks(12, 64, 2048, seed=5)
+    xe = np.stack([np.full(2048, 3.0, np.float32), np.full(2048, -3.0, np.float32),
+                   np.where(np.arange(2048) % 2 == 0, 2.0, -2.0).astype(np.float32),
+                   np.random.default_rng(6).standard_normal(2048).astype(np.float32)])
+    want_e = orc.matmul(12, we, 64, 2048, xe)
+    dst_e = _repack(q, 12, we, 64, 2048)
+    q.tune_gemv(7, cfg)
+    q.tune_gemv(10, 1)
+    try:
+        for n in (1, 2, 3, 4, 5):
+            got = run_gemv_raw(q, q.TILE[12], dst, rows, cols, x[:n])
+            assert bits_equal(got, want[:n]), (cfg, n)
+        got_e = run_gemv_raw(q, q.TILE[12], dst_e, 64, 2048, xe)
+        assert bits_equal(got_e, want_e), (cfg, "extremes")
+    finally:
+        q.tune_gemv(10, q.GEMV_MMA_MIN_COLS)
+        q.tune_gemv(0, 0)

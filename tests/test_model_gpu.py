@@ -54,19 +54,27 @@ def test_greedy_ids_match_oracle(model, omodel):
     assert got == want
 
 
-def test_hidden_states_and_logits_bit_exact(model, omodel):
-    """Every layer's residual row and the logits of every prompt position, bit for bit."""
+@pytest.mark.parametrize("mma_min", [4, 1])
+def test_hidden_states_and_logits_bit_exact(model, omodel, mma_min):
+    """Every layer's residual row and the logits of every prompt position, bit for bit; with mma_min = 1 the
+    one-column steps take the warp-MMA Q4_K GEMV (the gate/up pair with its SwiGLU epilogue included)."""
+    import qdec
+
     p = prompt16()
     st = model.new_state(max_rows=1)
     st.set_capture(True)
     os_ = omodel.state(512)
-    for tok in p[:6]:
-        st.step(tok)
-        lg, cap = os_.forward_token(tok, capture=True)
-        for layer in range(model.info.n_layer + 1):
-            h = st.hidden(layer)
-            assert np.array_equal(h.view(np.uint32), cap[layer].view(np.uint32)), f"layer {layer} at position {os_.pos - 1}"
-        assert np.array_equal(st.logits(0).view(np.uint32), lg.view(np.uint32))
+    qdec.tune_gemv(10, mma_min)
+    try:
+        for tok in p[:6]:
+            st.step(tok)
+            lg, cap = os_.forward_token(tok, capture=True)
+            for layer in range(model.info.n_layer + 1):
+                h = st.hidden(layer)
+                assert np.array_equal(h.view(np.uint32), cap[layer].view(np.uint32)), f"layer {layer} at position {os_.pos - 1}"
+            assert np.array_equal(st.logits(0).view(np.uint32), lg.view(np.uint32))
+    finally:
+        qdec.tune_gemv(10, qdec.GEMV_MMA_MIN_COLS)
 
 
 def test_batched_prefill_equals_token_steps(model):
