@@ -929,7 +929,7 @@ def run_spec_qdec(args, world, rank, local):
         "e2e": {"value": round(emitted_all / wall, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * (k + 2)},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "kq_gemv7s_kernel: ffn_gate + ffn_up Q4_K 2 x 17408x5120, N=4 (one launch)",
+        "roofline": {"bound": "hbm", "kernel": "kq_gemv7m_kernel (integer lanes on mma.sync): ffn_gate + ffn_up Q4_K 2 x 17408x5120, N=4 (one launch)",
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "alg_bytes_per_launch": alg,
                      "launch_us": round(kern_ms * 1e3, 2),
@@ -984,6 +984,8 @@ def main():
     ap.add_argument("--profile-gemv", action="store_true",
                     help="run the dominant GEMV (ffn_gate + ffn_up, Q4_K 2 x 17408x5120, N=4, one launch) 4 times and exit: "
                          "the ncu capture target")
+    ap.add_argument("--no-gemv-mma", action="store_true",
+                    help="with --profile-gemv: the CUDA-core (dp4a) form of the 4-column Q4_K GEMV instead of the warp-MMA form")
     ap.add_argument("--profile-prefill-gemm", action="store_true",
                     help="run the prefill's tensor-core GEMM (Q4_K 17408x5120, 32 columns) 4 times, print its event time "
                          "and exit: the ncu capture target")
@@ -991,7 +993,11 @@ def main():
     if args.profile_gemv or args.profile_prefill_gemm:
         import torch
 
+        import qdec
+
         torch.cuda.set_device(0)
+        if args.no_gemv_mma:
+            qdec.tune_gemv(10, 0)
         n = 32 if args.profile_prefill_gemm else 4
         _, ms = dominant_gemv_timing(torch.device("cuda", 0), launches=4, n=n)
         print(json.dumps({"kernel": f"Q4_K 2 x 17408x5120 (gate + up) x {n} columns", "us_per_launch": round(ms * 1e3, 2)}))

@@ -495,7 +495,8 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4]
 
 // One super-block of a warp's two Q4_K tiles (tile blocks tb0, tb1 in shared memory) against the B column of
 // thread (g, c): activation column g / 2 at lane parity g % 2, its image block at xb (zeros when !bval).  Leaves in
-// thread (g, c), for column c and row g of tile j, the eight exact lane sums and the row's d, dmin and min pairs
+// thread (g, c), for column c and row g of tile j, the eight exact lane sums (biased: the bits of 1.5 * 2^23 + sumi
+// as a float) and the row's d, dmin and min pairs
 // (get_scale_min_k4, quant.rs:45-51).  PERM: the block's code words are stored [u][q][s][c] (the streaming kernel's
 // staging) instead of the image's [lane][chunk].
 template <bool PERM>
@@ -517,7 +518,9 @@ __device__ __forceinline__ void q4k_mma_sb(const uint8_t* tb0, const uint8_t* tb
     const int s = g & 1, sh = 4 * (c & 1);
 #pragma unroll
     for (int u = 0; u < 4; u++) {  // lanes 2u, 2u + 1
-        int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+        // the low part accumulates onto 1.5 * 2^23's bits, so 8 D0 + D1 read as a float is 1.5 * 2^23 + sumi
+        // (|sumi| < 2^22): the lane as f32 with one subtraction
+        int d0[4] = {0, 0, 0, 0}, d1[4] = {(int)G7_MAGIC_I, (int)G7_MAGIC_I, (int)G7_MAGIC_I, (int)G7_MAGIC_I};
 #pragma unroll
         for (int q = 0; q < 2; q++) {
             // chunk 4q + c = pair 2q + c/2, nibble c % 2: the 8 bytes of lanes 2u, 2u + 1 of both rows
@@ -644,7 +647,7 @@ kq_gemv7m_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict_
             for (int j = 0; j < R; j++) {
                 const float dd = __fmul_rn(dx, dw[j]);  // d = dx * d_w (kdot.rs:50)
 #pragma unroll
-                for (int l = 0; l < 8; l++) acc[j][l] = __fadd_rn(acc[j][l], __fmul_rn(dd, __int2float_rn(sumi[j][l])));
+                for (int l = 0; l < 8; l++) acc[j][l] = __fadd_rn(acc[j][l], __fmul_rn(dd, __fsub_rn(__int_as_float(sumi[j][l]), G7_MAGIC_F)));
 #pragma unroll
                 for (int k = 0; k < 4; k++) accm[j][k] = __fadd_rn(accm[j][k], q4k_min_term(dx, dminw[j], q8w[k], mp[j][k]));
             }
@@ -1000,7 +1003,7 @@ kq_gemv7mw_kernel(const uint8_t* __restrict__ w_a, int rows_a, float* __restrict
                     const float dd = __fmul_rn(dx, dw[j]);  // d = dx * d_w (kdot.rs:50)
                     float t[12];
 #pragma unroll
-                    for (int l = 0; l < 8; l++) t[l] = __fmul_rn(dd, __int2float_rn(sumi[j][l]));
+                    for (int l = 0; l < 8; l++) t[l] = __fmul_rn(dd, __fsub_rn(__int_as_float(sumi[j][l]), G7_MAGIC_F));
 #pragma unroll
                     for (int k = 0; k < 4; k++) t[8 + k] = q4k_min_term(dx, dminw[j], q8w[k], mp[j][k]);
                     float4* tp = reinterpret_cast<float4*>(tb + (j * NC + c) * CW + g * 12);
