@@ -16,6 +16,11 @@
 // may exceed that) are converted with a rounding I2F, as the reference's `as f32`.  All integer steps are exact,
 // so the f32 operations are the reference's, in its order.
 //
+// Four Q4_K columns take the warp-MMA forms instead (kq_gemv7m_kernel, kq_gemv7mw_kernel): the same lanes as
+// exact i32 accumulators of mma.sync.m16n8k32 (s8), with the chunk scale split into two byte parts on the weight
+// operand and the activation operand masked per lane, so the per-column integer work -- most of the dp4a form's
+// instructions at four columns -- runs on the tensor pipe; the f32 chains are unchanged.
+//
 // Work split.  Four threads share a weight row (thread tg holds lanes 2tg, 2tg+1 and min lane tg), eight rows
 // make a tile (one tile block per super-block: 8 x the block bytes, contiguous, in the order the threads read
 // it), a warp owns R tiles.  A CTA is G x S warps: G groups of R tiles each, and S warps per group splitting the
