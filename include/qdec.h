@@ -116,8 +116,9 @@ int qdec_tune_gemv(int impl, int config);
 
 /* Failure-handling self-test of one bounded device wait on the current device, in this process, without a peer
  * or a fault: `which` = 0 runs a tensor-parallel exchange step whose peer lines never arrive (they carry the
- * previous step's tag), 1 a decode GEMV whose first stage waits for bytes nothing sends.  Each wait must give up
- * after wait_ms (1..10000), record its error word and let the kernel return with the context usable; the same work
+ * previous step's tag), 1 a decode GEMV whose first stage waits for bytes nothing sends (four runs: the streaming
+ * and the windowed kernel, each in its dp4a and its warp-MMA form).  Each wait must give up after wait_ms
+ * (1..10000), record its error word and let the kernel return with the context usable; the same work
  * is then run normally and must give the right result.  QDEC_OK when all of that held, QDEC_ECUDA (with the step
  * that misbehaved in qdec_last_error()) otherwise.  The engine's own waits give up the same way and surface as
  * QDEC_ETIMEOUT.  No counterpart in the reference (its CPU code has no device waits). */

@@ -1278,28 +1278,33 @@ unsigned read_gemv7_error(bool clear) {
 // wait_ns, record its error word and leave the context usable; the same GEMV run normally afterwards must give the
 // right result (zero weights: zeros).  Returns 0, or a code naming the half that misbehaved.
 int selftest_gemv7_timeout(unsigned long long wait_ns) {
-    const int rows = 64, cols = 256;
+    const int rows = 64, cols = 256, maxc = 4;
     uint8_t *w = nullptr, *img = nullptr;
     float* y = nullptr;
     cudaStream_t st = nullptr;
     int rc = 0;
-    if (cudaMalloc(&w, (size_t)rows / 8 * 1152) || cudaMalloc(&img, Q8K_IMG_BYTES) || cudaMalloc(&y, rows * 4) ||
+    if (cudaMalloc(&w, (size_t)rows / 8 * 1152) || cudaMalloc(&img, maxc * Q8K_IMG_BYTES) || cudaMalloc(&y, maxc * rows * 4) ||
         cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking))
         rc = 1;
     if (!rc) {
         cudaMemset(w, 0, (size_t)rows / 8 * 1152);
-        cudaMemset(img, 0, Q8K_IMG_BYTES);
-        cudaMemset(y, 0xff, rows * 4);
+        cudaMemset(img, 0, maxc * Q8K_IMG_BYTES);
+        cudaMemset(y, 0xff, maxc * rows * 4);
         read_gemv7_error(true);
     }
-    const int saved_cfg = g_cfg7;
-    for (int cfg : {1, 8}) {  // the streaming kernel's first weight stage, the windowed kernel's first window
+    const int saved_cfg = g_cfg7, saved_mma = g_mma7_min_cols;
+    // the streaming kernel's first weight stage and the windowed kernel's first window, each in the dp4a form (one
+    // column) and the warp-MMA form (four columns)
+    const int cases[4][2] = {{1, 1}, {8, 1}, {4, 4}, {7, 4}};
+    for (const auto& cs : cases) {
         if (rc) break;
-        g_cfg7 = cfg;
+        g_cfg7 = cs[0];
+        g_mma7_min_cols = 4;
+        const int nc = cs[1];
         const unsigned extra = 16;
         cudaMemcpyToSymbol(g7_test_extra_tx, &extra, sizeof extra);
         cudaMemcpyToSymbol(g7_wait_ns, &wait_ns, sizeof wait_ns);
-        if (launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
+        if (launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, nc, st, false) != cudaSuccess ||
             cudaStreamSynchronize(st) != cudaSuccess)
             rc = 2;  // the timed-out run must still complete as a kernel
         else if ((read_gemv7_error(true) & 0xff00u) != 0x700u)
@@ -1309,18 +1314,20 @@ int selftest_gemv7_timeout(unsigned long long wait_ns) {
         cudaMemcpyToSymbol(g7_test_extra_tx, &zero, sizeof zero);
         cudaMemcpyToSymbol(g7_wait_ns, &dflt, sizeof dflt);
         if (!rc) {
-            float h[64];
-            if (cudaMemset(y, 0xff, rows * 4) != cudaSuccess ||
-                launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, 1, st, false) != cudaSuccess ||
-                cudaStreamSynchronize(st) != cudaSuccess || cudaMemcpy(h, y, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
+            float h[maxc * 64];
+            if (cudaMemset(y, 0xff, maxc * rows * 4) != cudaSuccess ||
+                launch_gemv7(T_Q4_K_TILE, w, rows, y, nullptr, 0, nullptr, cols, img, nc, st, false) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess ||
+                cudaMemcpy(h, y, (size_t)nc * rows * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
                 rc = 4;
             else if (read_gemv7_error(true) != 0)
                 rc = 5;
             else
-                for (int i = 0; i < rows && !rc; i++)
+                for (int i = 0; i < nc * rows && !rc; i++)
                     if (h[i] != 0.0f) rc = 6;  // the normal run after the timeout gives the right result
         }
     }
+    g_mma7_min_cols = saved_mma;
     g_cfg7 = saved_cfg;
     if (st) cudaStreamDestroy(st);
     cudaFree(w);
