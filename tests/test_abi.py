@@ -53,3 +53,19 @@ def test_act_row_bytes(q):
     assert q.act_row_bytes(q.Q8_0, 6144) == 192 * 34
     assert q.act_row_bytes(q.F32, 48) == 192
     assert q.act_row_bytes(q.Q4_K, 100) == 0
+
+
+def test_tune_gemv_ranges_checked_without_gpu(q):
+    """qdec_tune_gemv validates every knob on the host: the tile GEMV configuration (0..8), the prefill GEMM's
+    column threshold (>= 0) and the warp-MMA GEMV's column threshold (0..4); an unknown kernel is refused."""
+    for impl, cfg in ((7, 9), (7, -1), (9, -1), (10, 5), (10, -1), (3, 0), (11, 0)):
+        with pytest.raises(q.QdecError) as e:
+            q.tune_gemv(impl, cfg)
+        assert e.value.code == q.EINVAL
+    try:
+        for n in (0, 1, 4):
+            q.tune_gemv(10, n)
+        q.tune_gemv(7, 0)
+    finally:
+        q.tune_gemv(10, q.GEMV_MMA_MIN_COLS)
+        q.tune_gemv(0, 0)
