@@ -825,7 +825,7 @@ void State::layer_forward(const LayerW& L, int li, int t, KvState* kv, const int
             AttnArgs aa{qr_ + r0 * nqh, gate_ + r0 * nqh, kvo->k, kvo->v, po, attn_ + r0 * nqh, P.nq, P.nkv, hd,
                         batch_ ? o->max_pos_ : kv == &mtp_kv_ ? mtp_cap_ : max_pos_,
                         m_.attn_scaling, batch_ ? o->att_scores_ : att_scores_};
-            count_launch(); ck(launch_attention(aa, tn, stream), "attention");
+            count_launch(3); ck(launch_attention(aa, tn, stream), "attention");  // scores, softmax, values
         }
         const float* attn_full = attn_;
         if (tp()) {
